@@ -1,0 +1,274 @@
+// Python bindings of the wavelet_b200 CUDA extension.  Thin torch::Tensor
+// wrappers that check dtypes/shapes/strides and forward raw pointers plus the
+// current CUDA stream to the kernel launchers.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm.h"
+#include "kernels.h"
+
+namespace wb {
+int* error_word(int device);
+int read_error_word(int device);
+void clear_error_word(int device);
+}  // namespace wb
+
+namespace {
+
+#define WB_CHECK(cond, msg) TORCH_CHECK(cond, "wavelet_b200: ", msg)
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline void check_cuda(const at::Tensor& t, const char* name) {
+  WB_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+}
+inline void check_bf16(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  WB_CHECK(t.scalar_type() == at::kBFloat16, std::string(name) + " must be bfloat16");
+}
+inline void check_f32(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  WB_CHECK(t.scalar_type() == at::kFloat, std::string(name) + " must be float32");
+}
+
+// Leading dimension of a 2-D view whose inner stride is 1.
+inline int64_t ld_of(const at::Tensor& t, const char* name) {
+  WB_CHECK(t.dim() == 2, std::string(name) + " must be 2-D");
+  WB_CHECK(t.stride(1) == 1 || t.size(1) == 1, std::string(name) + " inner stride must be 1");
+  return t.size(0) == 1 ? std::max<int64_t>(t.stride(0), t.size(1)) : t.stride(0);
+}
+
+// C[M,N] (op)= alpha * A(m,k) B(n,k) (+bias).
+//   a: [M,K] (a_mn=false) or [K,M] (a_mn=true);  b: [N,K] or [K,N].
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& c,
+          int64_t epi, double alpha, const c10::optional<at::Tensor>& bias) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_cuda(c, "c");
+  const c10::cuda::CUDAGuard guard(a.device());
+  wb::GemmArgs g;
+  g.A = a.data_ptr();
+  g.lda = ld_of(a, "a");
+  g.a_mn = a_mn;
+  g.B = b.data_ptr();
+  g.ldb = ld_of(b, "b");
+  g.b_mn = b_mn;
+  g.M = a_mn ? a.size(1) : a.size(0);
+  const int64_t ka = a_mn ? a.size(0) : a.size(1);
+  g.N = b_mn ? b.size(1) : b.size(0);
+  const int64_t kb = b_mn ? b.size(0) : b.size(1);
+  WB_CHECK(ka == kb, "gemm: K mismatch");
+  g.K = ka;
+  WB_CHECK(c.dim() == 2 && c.size(0) == g.M && c.size(1) == g.N, "gemm: bad output shape");
+  g.C = c.data_ptr();
+  g.ldc = ld_of(c, "c");
+  g.epi = static_cast<int>(epi);
+  if (g.epi == wb::kEpiBF16)
+    check_bf16(c, "c");
+  else
+    check_f32(c, "c");
+  g.alpha = static_cast<float>(alpha);
+  if (bias.has_value() && bias->defined()) {
+    check_bf16(*bias, "bias");
+    WB_CHECK(bias->numel() == g.N && bias->is_contiguous(), "gemm: bias must be [N]");
+    WB_CHECK(g.epi == wb::kEpiBF16, "gemm: bias only with the bf16 epilogue");
+    g.bias = bias->data_ptr();
+  }
+  wb::gemm_bf16(g, cur_stream());
+}
+
+void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
+                 const c10::optional<at::Tensor>& h_out, const at::Tensor& w, at::Tensor& y,
+                 const c10::optional<at::Tensor>& rstd, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  WB_CHECK(x.is_contiguous() && y.is_contiguous(), "rmsnorm: x, y must be contiguous");
+  const int H = w.numel();
+  const int rows = x.numel() / H;
+  const c10::cuda::CUDAGuard guard(x.device());
+  wb::rmsnorm_fwd(x.data_ptr(), res ? res->data_ptr() : nullptr,
+                  h_out ? h_out->data_ptr() : nullptr, w.data_ptr(), y.data_ptr(),
+                  rstd ? rstd->data_ptr<float>() : nullptr, rows, H, (float)eps, cur_stream());
+}
+
+void rmsnorm_bwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                 const at::Tensor& dy, const c10::optional<at::Tensor>& dres, at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dw) {
+  check_bf16(x, "x");
+  check_bf16(dy, "dy");
+  check_bf16(dx, "dx");
+  check_f32(rstd, "rstd");
+  WB_CHECK(x.is_contiguous() && dy.is_contiguous() && dx.is_contiguous(),
+           "rmsnorm_bwd: tensors must be contiguous");
+  const int H = w.numel();
+  const int rows = x.numel() / H;
+  if (dw) check_f32(*dw, "dw");
+  const c10::cuda::CUDAGuard guard(x.device());
+  wb::rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(),
+                  dres ? dres->data_ptr() : nullptr, dx.data_ptr(),
+                  dw ? dw->data_ptr<float>() : nullptr, rows, H, cur_stream());
+}
+
+void qk_norm_rope_fwd(at::Tensor& qkv, int64_t n_q, int64_t n_k, const at::Tensor& pos,
+                      const at::Tensor& inv_freq, const c10::optional<at::Tensor>& q_w,
+                      const c10::optional<at::Tensor>& k_w, const c10::optional<at::Tensor>& rstd,
+                      double eps) {
+  check_bf16(qkv, "qkv");
+  WB_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "qk_norm_rope: qkv must be [T, W] row-major");
+  WB_CHECK(pos.scalar_type() == at::kInt, "qk_norm_rope: pos must be int32");
+  check_f32(inv_freq, "inv_freq");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  wb::qk_norm_rope_fwd(qkv.data_ptr(), qkv.stride(0), n_q, n_k, pos.data_ptr<int>(),
+                       inv_freq.data_ptr<float>(), q_w ? q_w->data_ptr() : nullptr,
+                       k_w ? k_w->data_ptr() : nullptr, rstd ? rstd->data_ptr<float>() : nullptr,
+                       qkv.size(0), (float)eps, cur_stream());
+}
+
+void qk_norm_rope_bwd(at::Tensor& dqkv, const at::Tensor& qkv_pre, int64_t n_q, int64_t n_k,
+                      const at::Tensor& pos, const at::Tensor& inv_freq,
+                      const c10::optional<at::Tensor>& q_w, const c10::optional<at::Tensor>& k_w,
+                      const c10::optional<at::Tensor>& rstd,
+                      const c10::optional<at::Tensor>& dq_w,
+                      const c10::optional<at::Tensor>& dk_w) {
+  check_bf16(dqkv, "dqkv");
+  const c10::cuda::CUDAGuard guard(dqkv.device());
+  wb::qk_norm_rope_bwd(dqkv.data_ptr(), dqkv.stride(0), qkv_pre.data_ptr(), qkv_pre.stride(0), n_q,
+                       n_k, pos.data_ptr<int>(), inv_freq.data_ptr<float>(),
+                       q_w ? q_w->data_ptr() : nullptr, k_w ? k_w->data_ptr() : nullptr,
+                       rstd ? rstd->data_ptr<float>() : nullptr,
+                       dq_w ? dq_w->data_ptr<float>() : nullptr,
+                       dk_w ? dk_w->data_ptr<float>() : nullptr, dqkv.size(0), cur_stream());
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
+  check_bf16(gu, "gu");
+  check_bf16(h, "h");
+  WB_CHECK(gu.is_contiguous() && h.is_contiguous(), "swiglu: tensors must be contiguous");
+  const int64_t I = h.size(-1);
+  const c10::cuda::CUDAGuard guard(gu.device());
+  wb::swiglu_fwd(gu.data_ptr(), h.data_ptr(), h.numel() / I, I, cur_stream());
+}
+
+void swiglu_bwd(const at::Tensor& gu, const at::Tensor& dh, at::Tensor& dgu) {
+  check_bf16(gu, "gu");
+  check_bf16(dh, "dh");
+  check_bf16(dgu, "dgu");
+  WB_CHECK(gu.is_contiguous() && dh.is_contiguous() && dgu.is_contiguous(),
+           "swiglu_bwd: tensors must be contiguous");
+  const int64_t I = dh.size(-1);
+  const c10::cuda::CUDAGuard guard(gu.device());
+  wb::swiglu_bwd(gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), dh.numel() / I, I, cur_stream());
+}
+
+void embedding_fwd(const at::Tensor& table, const at::Tensor& ids, at::Tensor& out) {
+  check_bf16(table, "table");
+  WB_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embedding: ids must be int64");
+  const c10::cuda::CUDAGuard guard(table.device());
+  wb::embedding_fwd(table.data_ptr(), ids.data_ptr<int64_t>(), out.data_ptr(), ids.numel(),
+                    table.size(1), table.size(0), cur_stream());
+}
+
+void embedding_bwd(const at::Tensor& dy, const at::Tensor& ids, at::Tensor& dtable) {
+  check_bf16(dy, "dy");
+  check_f32(dtable, "dtable");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  wb::embedding_bwd(dy.data_ptr(), ids.data_ptr<int64_t>(), dtable.data_ptr<float>(), ids.numel(),
+                    dtable.size(1), dtable.size(0), cur_stream());
+}
+
+void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& p16, double lr, double b1, double b2, double eps,
+                double wd, int64_t step, const c10::optional<at::Tensor>& gscale_dev,
+                double gscale_host) {
+  check_f32(p, "p");
+  check_f32(g, "g");
+  check_f32(m, "m");
+  check_f32(v, "v");
+  WB_CHECK(p.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(),
+           "adamw: buffers must be contiguous");
+  WB_CHECK(g.numel() == p.numel() && m.numel() == p.numel() && v.numel() == p.numel(),
+           "adamw: size mismatch");
+  if (p16) {
+    check_bf16(*p16, "p16");
+    WB_CHECK(p16->numel() == p.numel() && p16->is_contiguous(), "adamw: bad p16");
+  }
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  const c10::cuda::CUDAGuard guard(p.device());
+  wb::adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
+                 v.data_ptr<float>(), p16 ? p16->data_ptr() : nullptr, p.numel(), (float)lr,
+                 (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
+                 gscale_dev ? gscale_dev->data_ptr<float>() : nullptr, (float)gscale_host,
+                 cur_stream());
+}
+
+void sumsq(const at::Tensor& x, at::Tensor& out) {
+  check_f32(x, "x");
+  check_f32(out, "out");
+  WB_CHECK(x.is_contiguous(), "sumsq: x must be contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  wb::sumsq(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), cur_stream());
+}
+
+void clip_factor(const at::Tensor& sumsq_v, double max_norm, at::Tensor& out) {
+  const c10::cuda::CUDAGuard guard(sumsq_v.device());
+  wb::clip_factor(sumsq_v.data_ptr<float>(), (float)max_norm, out.data_ptr<float>(), cur_stream());
+}
+
+void softmax_stats(const at::Tensor& z, const c10::optional<at::Tensor>& target, double inv_tau,
+                   at::Tensor& lse, const c10::optional<at::Tensor>& lp,
+                   const c10::optional<at::Tensor>& ent) {
+  check_bf16(z, "z");
+  WB_CHECK(z.dim() == 2 && z.stride(1) == 1, "softmax_stats: z must be [rows, V] row-major");
+  check_f32(lse, "lse");
+  const c10::cuda::CUDAGuard guard(z.device());
+  wb::softmax_stats(z.data_ptr(), z.stride(0), z.size(0), z.size(1),
+                    target ? target->data_ptr<int64_t>() : nullptr, (float)inv_tau,
+                    lse.data_ptr<float>(), lp ? lp->data_ptr<float>() : nullptr,
+                    ent ? ent->data_ptr<float>() : nullptr, cur_stream());
+}
+
+void softmax_grad(at::Tensor& z, const c10::optional<at::Tensor>& target, double inv_tau,
+                  const at::Tensor& lse, const c10::optional<at::Tensor>& ent,
+                  const c10::optional<at::Tensor>& dlp, const c10::optional<at::Tensor>& dent) {
+  check_bf16(z, "z");
+  WB_CHECK(z.dim() == 2 && z.stride(1) == 1, "softmax_grad: z must be [rows, V] row-major");
+  const c10::cuda::CUDAGuard guard(z.device());
+  wb::softmax_grad(z.data_ptr(), z.stride(0), z.size(0), z.size(1),
+                   target ? target->data_ptr<int64_t>() : nullptr, (float)inv_tau,
+                   lse.data_ptr<float>(), ent ? ent->data_ptr<float>() : nullptr,
+                   dlp ? dlp->data_ptr<float>() : nullptr, dent ? dent->data_ptr<float>() : nullptr,
+                   cur_stream());
+}
+
+int64_t read_error(int64_t device) { return wb::read_error_word((int)device); }
+void clear_error(int64_t device) { wb::clear_error_word((int)device); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "wavelet_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"),
+        py::arg("b_mn"), py::arg("c"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
+        py::arg("bias") = py::none());
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("sumsq", &sumsq);
+  m.def("clip_factor", &clip_factor);
+  m.def("softmax_stats", &softmax_stats);
+  m.def("softmax_grad", &softmax_grad);
+  m.def("read_error", &read_error);
+  m.def("clear_error", &clear_error);
+  m.attr("EPI_BF16") = (int)wb::kEpiBF16;
+  m.attr("EPI_F32") = (int)wb::kEpiF32;
+  m.attr("EPI_F32_ACC") = (int)wb::kEpiF32Acc;
+}

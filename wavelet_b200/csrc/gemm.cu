@@ -1,0 +1,381 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M, N] (op)= alpha * sum_k A(m, k) * B(n, k)  (+ bias[n])
+//
+// A and B are each either K-major (row m / n holds K contiguous elements) or
+// MN-major (row k holds M / N contiguous elements), so one kernel serves the
+// three GEMMs of a linear layer without any transpose:
+//   forward  Y  = X  W^T : A = X  (K-major),  B = W  (K-major)
+//   dgrad    dX = dY W   : A = dY (K-major),  B = W  (MN-major)
+//   wgrad    dW = dY^T X : A = dY (MN-major), B = X  (MN-major)
+// (the three linear GEMMs of the reference run as cuBLAS calls inside
+// torch.nn.Linear, trainer/model.py; this replaces them on the GPU path).
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: streams 128x64 A and 256x64 B tiles into a
+//               4-stage shared-memory ring (128-byte swizzle, no multicast).
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256,
+//               K=16) into one of two TMEM accumulators (2 x 256 columns).
+//   warps 2..5  epilogue: tcgen05.ld the finished accumulator (warp w reads
+//               TMEM lanes 32*(w%4)..+31 = tile rows), apply the epilogue and
+//               store to global memory while the MMA warp fills the other
+//               accumulator.
+// Every wait is bounded (common.cuh); on timeout the CTA drains its in-flight
+// TMA and MMA work, frees TMEM, reports through the error word and exits.
+#include "common.cuh"
+#include "gemm.h"
+#include "tma.h"
+
+namespace wb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;        // 16 KB
+constexpr int B_BYTES = BN * BK * 2;        // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int MN_BOX = 64;                  // MN-major TMA box width (128 bytes)
+constexpr int MN_BOX_BYTES = MN_BOX * BK * 2;  // 8 KB
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+
+struct __align__(8) Smem {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(Smem) + 64; }
+
+struct Params {
+  void* C;
+  const __nv_bfloat16* bias;
+  int64_t ldc;
+  float alpha;
+  int M, N, K;
+  int num_m, num_n, num_k;
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
+  const int in_group = GROUP_M * num_n;
+  const int gid = t / in_group;
+  const int first_m = gid * GROUP_M;
+  const int gsm = min(num_m - first_m, GROUP_M);
+  const int r = t - gid * in_group;
+  m = first_m + r % gsm;
+  n = r / gsm;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col0,
+                                               const uint32_t (&v)[32]) {
+  if (row >= p.M) return;
+  const bool full = (col0 + 32 <= p.N);
+  if constexpr (EPI == kEpiBF16) {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)row * p.ldc + col0;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * p.alpha;
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) f[j] += __bfloat162float(p.bias[col0 + j]);
+    }
+    if (full && ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
+      uint4* dst = reinterpret_cast<uint4*>(c);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16(f[8 * q + 0], f[8 * q + 1]);
+        w.y = pack_bf16(f[8 * q + 2], f[8 * q + 3]);
+        w.z = pack_bf16(f[8 * q + 4], f[8 * q + 5]);
+        w.w = pack_bf16(f[8 * q + 6], f[8 * q + 7]);
+        dst[q] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) c[j] = __float2bfloat16(f[j]);
+    }
+  } else {
+    float* c = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col0;
+    if (full && ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
+      float4* dst = reinterpret_cast<float4*>(c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = make_float4(__uint_as_float(v[4 * q + 0]) * p.alpha,
+                               __uint_as_float(v[4 * q + 1]) * p.alpha,
+                               __uint_as_float(v[4 * q + 2]) * p.alpha,
+                               __uint_as_float(v[4 * q + 3]) * p.alpha);
+        if constexpr (EPI == kEpiF32Acc) {
+          float4 o = dst[q];
+          w.x += o.x;
+          w.y += o.y;
+          w.z += o.z;
+          w.w += o.w;
+        }
+        dst[q] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j < p.N) {
+          float w = __uint_as_float(v[j]) * p.alpha;
+          if constexpr (EPI == kEpiF32Acc) w += c[j];
+          c[j] = w;
+        }
+      }
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  Smem* s = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
+  volatile int* abort = &s->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s->full[i], 1);
+      mbar_init(&s->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s->tmem_full[i], 1);
+      mbar_init(&s->tmem_empty[i], 128);
+    }
+    mbar_init(&s->drain, 1);
+    s->abort = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[STAGES];
+      uint32_t issued_phase[STAGES];
+      for (int i = 0; i < STAGES; ++i) issued[i] = 0, issued_phase[i] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p.num_m, p.num_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < p.num_k; ++kb) {
+          if (!mbar_wait(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = tiles + stage * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_BYTES;
+          mbar_arrive_expect_tx(&s->full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / MN_BOX; ++j)
+              tma_load_2d(&tmA, &s->full[stage], a_dst + j * MN_BOX_BYTES, m0 + j * MN_BOX, k0);
+          } else {
+            tma_load_2d(&tmA, &s->full[stage], a_dst, k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / MN_BOX; ++j)
+              tma_load_2d(&tmB, &s->full[stage], b_dst + j * MN_BOX_BYTES, n0 + j * MN_BOX, k0);
+          } else {
+            tma_load_2d(&tmB, &s->full[stage], b_dst, k0, n0);
+          }
+          issued[stage] = 1;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if (!ok || *abort) {
+        // Drain: every TMA we issued must land before the CTA may exit.
+        for (int i = 0; i < STAGES; ++i) {
+          if (!issued[i]) continue;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&s->full[i], issued_phase[i])) {
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+              atomicOr(p.err, kErrTimeoutDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool any = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&s->tmem_empty[acc], acc_phase ^ 1, abort, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_k; ++kb) {
+          if (!mbar_wait(&s->full[stage], phase, abort, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad, bd;
+            if constexpr (A_MN)
+              ad = smem_desc_sw128(a_addr + k * 16 * 128, MN_BOX_BYTES, 1024);
+            else
+              ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            if constexpr (B_MN)
+              bd = smem_desc_sw128(b_addr + k * 16 * 128, MN_BOX_BYTES, 1024);
+            else
+              bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s->empty[stage]);
+          any = true;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        umma_commit(&s->tmem_full[acc]);
+        if (++acc == 2) acc = 0, acc_phase ^= 1;
+      }
+      if (any) {
+        // All MMAs must retire before TMEM is released.
+        umma_commit(&s->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&s->drain, 0)) {
+          if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            atomicOr(p.err, kErrTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      if (!mbar_wait(&s->tmem_full[acc], acc_phase, abort, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, p.num_m, p.num_n, tm, tn);
+      const int row = tm * BM + q * 32 + lane;
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (tn * BN + c >= p.N) break;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_addr + c, v);
+        tmem_wait_ld();
+        epilogue_chunk<EPI>(p, row, tn * BN + c, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&s->tmem_empty[acc]);
+      if (++acc == 2) acc = 0, acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch(const GemmArgs& g, cudaStream_t stream) {
+  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
+    attr_set[dev & 63] = true;
+  }
+  // A(m,k): K-major -> rows of K; MN-major -> rows of M.
+  CUtensorMap ta = A_MN ? make_tmap_2d(g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.M, g.K, g.lda,
+                                       MN_BOX, BK, CU_TENSOR_MAP_SWIZZLE_128B)
+                        : make_tmap_2d(g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, g.M, g.lda,
+                                       BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = B_MN ? make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, g.K, g.ldb,
+                                       MN_BOX, BK, CU_TENSOR_MAP_SWIZZLE_128B)
+                        : make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, g.N, g.ldb,
+                                       BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  Params p;
+  p.C = g.C;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(g.bias);
+  p.ldc = g.ldc;
+  p.alpha = g.alpha;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.num_m = (g.M + BM - 1) / BM;
+  p.num_n = (g.N + BN - 1) / BN;
+  p.num_k = (g.K + BK - 1) / BK;
+  p.err = error_word(dev);
+  const int tiles = p.num_m * p.num_n;
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  kern<<<grid, NUM_THREADS, smem_bytes(), stream>>>(ta, tb, p);
+}
+
+}  // namespace gemm
+
+void gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
+  using namespace gemm;
+  if (g.M <= 0 || g.N <= 0) return;
+  if (g.K <= 0) throw std::runtime_error("wavelet_b200 gemm: K must be positive");
+#define WB_GEMM_DISPATCH(AM, BMJ)                                               \
+  if (g.a_mn == AM && g.b_mn == BMJ) {                                          \
+    if (g.epi == kEpiBF16) return launch<AM, BMJ, kEpiBF16>(g, stream);         \
+    if (g.epi == kEpiF32) return launch<AM, BMJ, kEpiF32>(g, stream);           \
+    if (g.epi == kEpiF32Acc) return launch<AM, BMJ, kEpiF32Acc>(g, stream);     \
+  }
+  WB_GEMM_DISPATCH(false, false)
+  WB_GEMM_DISPATCH(false, true)
+  WB_GEMM_DISPATCH(true, false)
+  WB_GEMM_DISPATCH(true, true)
+#undef WB_GEMM_DISPATCH
+  throw std::runtime_error("wavelet_b200 gemm: unsupported epilogue");
+}
+
+}  // namespace wb

@@ -1,0 +1,33 @@
+// Host API of the tcgen05 GEMM family (gemm.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wb {
+
+enum GemmEpilogue : int {
+  kEpiBF16 = 0,    // C(bf16) = alpha * acc (+ bias)
+  kEpiF32 = 1,     // C(fp32) = alpha * acc
+  kEpiF32Acc = 2,  // C(fp32) += alpha * acc
+};
+
+struct GemmArgs {
+  // A(m, k): K-major -> A[m * lda + k];  MN-major -> A[k * lda + m]
+  const void* A = nullptr;
+  int64_t lda = 0;
+  bool a_mn = false;
+  // B(n, k): K-major -> B[n * ldb + k];  MN-major -> B[k * ldb + n]
+  const void* B = nullptr;
+  int64_t ldb = 0;
+  bool b_mn = false;
+  void* C = nullptr;  // row-major [M, ldc]
+  int64_t ldc = 0;
+  const void* bias = nullptr;  // bf16 [N] (kEpiBF16 only)
+  float alpha = 1.0f;
+  int epi = kEpiBF16;
+  int M = 0, N = 0, K = 0;
+};
+
+void gemm_bf16(const GemmArgs& g, cudaStream_t stream);
+
+}  // namespace wb

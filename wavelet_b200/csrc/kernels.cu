@@ -1,0 +1,723 @@
+// Bandwidth-bound sm_100a kernels of the trainer and generator:
+//   RMSNorm forward/backward (optionally fused with the residual add),
+//   per-head QK-RMSNorm + rotary embedding forward/backward (in place on the
+//   packed qkv activation), SwiGLU forward/backward, embedding gather and
+//   scatter-add backward, fused flat AdamW with bf16 shadow write, squared
+//   norm / finite reduction, and the row-wise softmax statistics used by the
+//   chunked LM-head log-prob / entropy / cross-entropy path.
+//
+// The reference implements these with Liger/Triton or HF eager torch ops
+// (trainer/model.py Liger patches; kernels/swiglu.py:12-83 for SwiGLU;
+// trainer/losses.py:600-1004 for the chunked log-prob head; trainer/optim.py
+// for AdamW).  All math is fp32 in registers; tensors are bf16 unless noted.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <stdexcept>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wb {
+
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float r = (l < nw) ? red[l] : 0.f;
+  r = warp_sum(r);
+  return r;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// ------------------------------------------------------------------ RMSNorm
+// One warp per row; 8 bf16 (16 bytes) per lane per step.
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ res,
+                                   __nv_bfloat16* __restrict__ h_out,
+                                   const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out,
+                                   int rows, int H, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * H);
+  const uint4* rr = res ? reinterpret_cast<const uint4*>(res + (int64_t)row * H) : nullptr;
+  uint4* hr = h_out ? reinterpret_cast<uint4*>(h_out + (int64_t)row * H) : nullptr;
+  const int nv = H >> 3;
+  float ss = 0.f;
+  for (int i = lane; i < nv; i += 32) {
+    uint4 a = xr[i];
+    if (rr) {
+      uint4 b = rr[i];
+      uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        pa[j] = pack_bf16(bf16_lo(pa[j]) + bf16_lo(pb[j]), bf16_hi(pa[j]) + bf16_hi(pb[j]));
+      if (hr) hr[i] = a;
+    }
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float u = bf16_lo(pa[j]), v = bf16_hi(pa[j]);
+      ss += u * u + v * v;
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / H + eps);
+  if (lane == 0 && rstd_out) rstd_out[row] = rstd;
+  const uint4* src = rr ? reinterpret_cast<const uint4*>(h_out ? h_out + (int64_t)row * H : nullptr)
+                        : xr;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)row * H);
+  for (int i = lane; i < nv; i += 32) {
+    uint4 a;
+    if (rr && !h_out) {
+      uint4 p = xr[i], q = rr[i];
+      uint32_t* pa = reinterpret_cast<uint32_t*>(&p);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        pa[j] = pack_bf16(bf16_lo(pa[j]) + bf16_lo(pb[j]), bf16_hi(pa[j]) + bf16_hi(pb[j]));
+      a = p;
+    } else {
+      a = src[i];
+    }
+    uint4 ww = wr[i];
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&ww);
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      po[j] = pack_bf16(bf16_lo(pa[j]) * rstd * bf16_lo(pw[j]),
+                        bf16_hi(pa[j]) * rstd * bf16_hi(pw[j]));
+    yr[i] = o;
+  }
+}
+
+// dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres);  dw += sum_rows dy*xhat.
+// Each CTA owns a contiguous run of rows and accumulates dw in shared memory.
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w,
+                                   const float* __restrict__ rstd,
+                                   const __nv_bfloat16* __restrict__ dy,
+                                   const __nv_bfloat16* __restrict__ dres,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
+                                   int rows, int H, int rows_per_cta) {
+  extern __shared__ float sdw[];
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x >> 5;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(rows, r0 + rows_per_cta);
+  const int nv = H >> 3;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  for (int row = r0 + wid; row < r1; row += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * H);
+    const uint4* dyr = reinterpret_cast<const uint4*>(dy + (int64_t)row * H);
+    const float rs = rstd[row];
+    float dot = 0.f;
+    for (int i = lane; i < nv; i += 32) {
+      uint4 a = xr[i], g = dyr[i], ww = wr[i];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(&ww);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dot += bf16_lo(pa[j]) * bf16_lo(pg[j]) * bf16_lo(pw[j]);
+        dot += bf16_hi(pa[j]) * bf16_hi(pg[j]) * bf16_hi(pw[j]);
+      }
+    }
+    dot = warp_sum(dot) * rs;  // sum(xhat * w * dy)
+    const float mean = dot / H;
+    uint4* dxr = reinterpret_cast<uint4*>(dx + (int64_t)row * H);
+    const uint4* drr = dres ? reinterpret_cast<const uint4*>(dres + (int64_t)row * H) : nullptr;
+    for (int i = lane; i < nv; i += 32) {
+      uint4 a = xr[i], g = dyr[i], ww = wr[i];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+      const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(&ww);
+      uint4 rres;
+      if (drr) rres = drr[i];
+      const uint32_t* pr = reinterpret_cast<const uint32_t*>(&rres);
+      uint4 o;
+      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float xh0 = bf16_lo(pa[j]) * rs, xh1 = bf16_hi(pa[j]) * rs;
+        float g0 = bf16_lo(pg[j]), g1 = bf16_hi(pg[j]);
+        float d0 = rs * (bf16_lo(pw[j]) * g0 - xh0 * mean);
+        float d1 = rs * (bf16_hi(pw[j]) * g1 - xh1 * mean);
+        if (drr) {
+          d0 += bf16_lo(pr[j]);
+          d1 += bf16_hi(pr[j]);
+        }
+        po[j] = pack_bf16(d0, d1);
+        const int c = i * 8 + 2 * j;
+        atomicAdd(&sdw[c], g0 * xh0);
+        atomicAdd(&sdw[c + 1], g1 * xh1);
+      }
+      dxr[i] = o;
+    }
+  }
+  __syncthreads();
+  if (dw)
+    for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+// ------------------------------------------------------------ QK-norm + RoPE
+// One warp per (token, head) of a 128-wide head; lane l holds elements
+// [4l, 4l+4); rotate-half partners live 16 lanes apart.
+__global__ void qk_norm_rope_fwd_kernel(__nv_bfloat16* __restrict__ qkv, int64_t row_stride,
+                                        int n_q, int n_k, const int* __restrict__ pos,
+                                        const float* __restrict__ inv_freq,
+                                        const __nv_bfloat16* __restrict__ q_w,
+                                        const __nv_bfloat16* __restrict__ k_w,
+                                        float* __restrict__ rstd_out, int tokens, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = n_q + n_k;
+  if (gw >= tokens * heads) return;
+  const int t = gw / heads, h = gw - t * heads;
+  __nv_bfloat16* base = qkv + (int64_t)t * row_stride + (int64_t)h * 128;
+  uint2 raw = reinterpret_cast<uint2*>(base)[lane];
+  float v[4] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y)};
+  const __nv_bfloat16* nw = (h < n_q) ? q_w : k_w;
+  if (nw) {
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / 128.f + eps);
+    if (lane == 0 && rstd_out) rstd_out[gw] = rs;
+    uint2 wraw = reinterpret_cast<const uint2*>(nw)[lane];
+    v[0] = __bfloat162float(__float2bfloat16(v[0] * rs * bf16_lo(wraw.x)));
+    v[1] = __bfloat162float(__float2bfloat16(v[1] * rs * bf16_hi(wraw.x)));
+    v[2] = __bfloat162float(__float2bfloat16(v[2] * rs * bf16_lo(wraw.y)));
+    v[3] = __bfloat162float(__float2bfloat16(v[3] * rs * bf16_hi(wraw.y)));
+  }
+  const float p = static_cast<float>(pos[t]);
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float other = __shfl_xor_sync(0xffffffffu, v[j], 16);
+    const int d = (lane & 15) * 4 + j;  // frequency index in [0, 64)
+    float s, c;
+    sincosf(p * inv_freq[d], &s, &c);
+    // first half: x1*cos - x2*sin ; second half: x2*cos + x1*sin
+    o[j] = (lane < 16) ? (v[j] * c - other * s) : (v[j] * c + other * s);
+  }
+  raw.x = pack_bf16(o[0], o[1]);
+  raw.y = pack_bf16(o[2], o[3]);
+  reinterpret_cast<uint2*>(base)[lane] = raw;
+}
+
+// Backward of qk_norm_rope_fwd: `dqkv` holds dL/d(rotated output) on entry and
+// dL/d(pre-norm input) on exit.  `qkv_pre` is the saved pre-norm activation.
+__global__ void qk_norm_rope_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, int64_t drow_stride,
+                                        const __nv_bfloat16* __restrict__ qkv_pre,
+                                        int64_t row_stride, int n_q, int n_k,
+                                        const int* __restrict__ pos,
+                                        const float* __restrict__ inv_freq,
+                                        const __nv_bfloat16* __restrict__ q_w,
+                                        const __nv_bfloat16* __restrict__ k_w,
+                                        const float* __restrict__ rstd, float* __restrict__ dq_w,
+                                        float* __restrict__ dk_w, int tokens) {
+  __shared__ float sdq[128], sdk[128];
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) sdq[i] = 0.f, sdk[i] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = n_q + n_k;
+  if (gw < tokens * heads) {
+    const int t = gw / heads, h = gw - t * heads;
+    __nv_bfloat16* dbase = dqkv + (int64_t)t * drow_stride + (int64_t)h * 128;
+    uint2 draw = reinterpret_cast<uint2*>(dbase)[lane];
+    float g[4] = {bf16_lo(draw.x), bf16_hi(draw.x), bf16_lo(draw.y), bf16_hi(draw.y)};
+    const float p = static_cast<float>(pos[t]);
+    float gr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float other = __shfl_xor_sync(0xffffffffu, g[j], 16);
+      const int d = (lane & 15) * 4 + j;
+      float s, c;
+      sincosf(p * inv_freq[d], &s, &c);
+      // transpose of the rotation
+      gr[j] = (lane < 16) ? (g[j] * c + other * s) : (g[j] * c - other * s);
+    }
+    const __nv_bfloat16* nw = (h < n_q) ? q_w : k_w;
+    if (nw) {
+      const __nv_bfloat16* xb = qkv_pre + (int64_t)t * row_stride + (int64_t)h * 128;
+      uint2 xraw = reinterpret_cast<const uint2*>(xb)[lane];
+      uint2 wraw = reinterpret_cast<const uint2*>(nw)[lane];
+      float x[4] = {bf16_lo(xraw.x), bf16_hi(xraw.x), bf16_lo(xraw.y), bf16_hi(xraw.y)};
+      float wv[4] = {bf16_lo(wraw.x), bf16_hi(wraw.x), bf16_lo(wraw.y), bf16_hi(wraw.y)};
+      const float rs = rstd[gw];
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dot += x[j] * rs * wv[j] * gr[j];
+      dot = warp_sum(dot) / 128.f;
+      float* sacc = (h < n_q) ? sdq : sdk;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float xh = x[j] * rs;
+        atomicAdd(&sacc[lane * 4 + j], gr[j] * xh);
+        gr[j] = rs * (wv[j] * gr[j] - xh * dot);
+      }
+    }
+    draw.x = pack_bf16(gr[0], gr[1]);
+    draw.y = pack_bf16(gr[2], gr[3]);
+    reinterpret_cast<uint2*>(dbase)[lane] = draw;
+  }
+  __syncthreads();
+  if (dq_w && q_w)
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) atomicAdd(&dq_w[i], sdq[i]);
+  if (dk_w && k_w)
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) atomicAdd(&dk_w[i], sdk[i]);
+}
+
+// ------------------------------------------------------------------ SwiGLU
+// gu row = [gate (I) | up (I)];  h = silu(gate) * up.
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                  __nv_bfloat16* __restrict__ h, int64_t rows, int I) {
+  const int nv = I >> 3;
+  const int64_t total = rows * nv;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / nv;
+    const int c = static_cast<int>(idx - r * nv);
+    const uint4* gr = reinterpret_cast<const uint4*>(gu + r * 2 * I);
+    uint4 g = gr[c], u = gr[nv + c];
+    const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+    const uint32_t* pu = reinterpret_cast<const uint32_t*>(&u);
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      po[j] = pack_bf16(silu_f(bf16_lo(pg[j])) * bf16_lo(pu[j]),
+                        silu_f(bf16_hi(pg[j])) * bf16_hi(pu[j]));
+    reinterpret_cast<uint4*>(h + r * I)[c] = o;
+  }
+}
+
+// dgu = [dh*u*s*(1+g*(1-s)) | dh*silu(g)],  s = sigmoid(g).
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                  const __nv_bfloat16* __restrict__ dh,
+                                  __nv_bfloat16* __restrict__ dgu, int64_t rows, int I) {
+  const int nv = I >> 3;
+  const int64_t total = rows * nv;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / nv;
+    const int c = static_cast<int>(idx - r * nv);
+    const uint4* gr = reinterpret_cast<const uint4*>(gu + r * 2 * I);
+    uint4 g = gr[c], u = gr[nv + c];
+    uint4 d = reinterpret_cast<const uint4*>(dh + r * I)[c];
+    const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+    const uint32_t* pu = reinterpret_cast<const uint32_t*>(&u);
+    const uint32_t* pd = reinterpret_cast<const uint32_t*>(&d);
+    uint4 og, ou;
+    uint32_t* pog = reinterpret_cast<uint32_t*>(&og);
+    uint32_t* pou = reinterpret_cast<uint32_t*>(&ou);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float gg[2] = {bf16_lo(pg[j]), bf16_hi(pg[j])};
+      float uu[2] = {bf16_lo(pu[j]), bf16_hi(pu[j])};
+      float dd[2] = {bf16_lo(pd[j]), bf16_hi(pd[j])};
+      float rg[2], ru[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float s = 1.f / (1.f + __expf(-gg[e]));
+        rg[e] = dd[e] * uu[e] * s * (1.f + gg[e] * (1.f - s));
+        ru[e] = dd[e] * gg[e] * s;
+      }
+      pog[j] = pack_bf16(rg[0], rg[1]);
+      pou[j] = pack_bf16(ru[0], ru[1]);
+    }
+    uint4* dr = reinterpret_cast<uint4*>(dgu + r * 2 * I);
+    dr[c] = og;
+    dr[nv + c] = ou;
+  }
+}
+
+// ------------------------------------------------------------------ embedding
+__global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ table,
+                                     const int64_t* __restrict__ ids,
+                                     __nv_bfloat16* __restrict__ out, int64_t T, int H,
+                                     int64_t V) {
+  const int nv = H >> 3;
+  const int64_t total = T * nv;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = idx / nv;
+    const int c = static_cast<int>(idx - t * nv);
+    int64_t id = ids[t];
+    id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+    reinterpret_cast<uint4*>(out + t * H)[c] = reinterpret_cast<const uint4*>(table + id * H)[c];
+  }
+}
+
+__global__ void embedding_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                     const int64_t* __restrict__ ids, float* __restrict__ dtable,
+                                     int64_t T, int H, int64_t V) {
+  const int nv = H >> 2;
+  const int64_t total = T * nv;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = idx / nv;
+    const int c = static_cast<int>(idx - t * nv);
+    int64_t id = ids[t];
+    if (id < 0 || id >= V) continue;
+    const uint2 g = reinterpret_cast<const uint2*>(dy + t * H)[c];
+    float4 v = make_float4(bf16_lo(g.x), bf16_hi(g.x), bf16_lo(g.y), bf16_hi(g.y));
+    atomicAdd(reinterpret_cast<float4*>(dtable + id * H) + c, v);
+  }
+}
+
+// ------------------------------------------------------------------ AdamW
+// Decoupled weight decay (torch.optim.AdamW semantics) over flat fp32 buffers
+// with the gradient scaled by `gscale` (token normalisation x clip factor read
+// from device memory so the step needs no host sync), writing the bf16 shadow.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v,
+                             __nv_bfloat16* __restrict__ p16, int64_t n, float lr, float b1,
+                             float b2, float eps, float wd, float bc1, float bc2,
+                             const float* __restrict__ gscale_dev, float gscale_host) {
+  const float gs = gscale_host * (gscale_dev ? *gscale_dev : 1.f);
+  const float step = lr / bc1;
+  const float rbc2 = rsqrtf(bc2);
+  const int64_t n4 = n >> 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    float4 gg = reinterpret_cast<const float4*>(g)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* ap = &pp.x;
+    float* ag = &gg.x;
+    float* am = &mm.x;
+    float* av = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gj = ag[j] * gs;
+      am[j] = b1 * am[j] + (1.f - b1) * gj;
+      av[j] = b2 * av[j] + (1.f - b2) * gj * gj;
+      ap[j] = ap[j] * (1.f - lr * wd);
+      ap[j] -= step * am[j] / (sqrtf(av[j]) * rbc2 + eps);
+    }
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (p16) {
+      uint2 o;
+      o.x = pack_bf16(pp.x, pp.y);
+      o.y = pack_bf16(pp.z, pp.w);
+      reinterpret_cast<uint2*>(p16)[i] = o;
+    }
+  }
+  // scalar tail
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float gj = g[i] * gs;
+    m[i] = b1 * m[i] + (1.f - b1) * gj;
+    v[i] = b2 * v[i] + (1.f - b2) * gj * gj;
+    p[i] = p[i] * (1.f - lr * wd) - step * m[i] / (sqrtf(v[i]) * rbc2 + eps);
+    if (p16) p16[i] = __float2bfloat16(p[i]);
+  }
+}
+
+// Sum of squares of a flat fp32 buffer into out[0] (atomic), non-finite count
+// into out[1].
+__global__ void sumsq_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+  __shared__ float red[32];
+  float s = 0.f, bad = 0.f;
+  const int64_t n4 = n >> 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = reinterpret_cast<const float4*>(x)[i];
+    s += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    bad += (isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w)) ? 0.f : 1.f;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    s += x[i] * x[i];
+    bad += isfinite(x[i]) ? 0.f : 1.f;
+  }
+  s = block_sum(s, red);
+  __syncthreads();
+  bad = block_sum(bad, red);
+  if (threadIdx.x == 0) {
+    atomicAdd(&out[0], s);
+    atomicAdd(&out[1], bad);
+  }
+}
+
+// clip factor = min(1, max_norm / (sqrt(sumsq) + 1e-6)); written to out.
+__global__ void clip_factor_kernel(const float* __restrict__ sumsq, float max_norm,
+                                   float* __restrict__ out) {
+  const float norm = sqrtf(sumsq[0]);
+  float f = 1.f;
+  if (max_norm > 0.f) f = fminf(1.f, max_norm / (norm + 1e-6f));
+  out[0] = f;
+  out[1] = norm;
+}
+
+// ------------------------------------------------------ softmax row statistics
+// For each row of z (bf16 logits, temperature tau): lse of z/tau, the target
+// log-prob z_t/tau - lse and the entropy lse - sum p * z/tau.  One CTA per row,
+// single pass with per-thread online (max, sum, weighted-sum) merged at the end.
+__global__ void softmax_stats_kernel(const __nv_bfloat16* __restrict__ z, int64_t ldz, int V,
+                                     const int64_t* __restrict__ target, float inv_tau,
+                                     float* __restrict__ lse_out, float* __restrict__ lp_out,
+                                     float* __restrict__ ent_out) {
+  __shared__ float sm[32], ss[32], sw[32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* zr = z + row * ldz;
+  float m = -INFINITY, s = 0.f, w = 0.f;
+  const int nv = V >> 3;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    uint4 a = reinterpret_cast<const uint4*>(zr)[i];
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+    float vals[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) vals[2 * j] = bf16_lo(pa[j]) * inv_tau, vals[2 * j + 1] = bf16_hi(pa[j]) * inv_tau;
+    float lm = vals[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, vals[j]);
+    if (lm > m) {
+      const float sc = __expf(m - lm);
+      s *= sc;
+      w *= sc;
+      m = lm;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float e = __expf(vals[j] - m);
+      s += e;
+      w += e * vals[j];
+    }
+  }
+  for (int i = (nv << 3) + threadIdx.x; i < V; i += blockDim.x) {
+    const float val = __bfloat162float(zr[i]) * inv_tau;
+    if (val > m) {
+      const float sc = __expf(m - val);
+      s *= sc;
+      w *= sc;
+      m = val;
+    }
+    const float e = __expf(val - m);
+    s += e;
+    w += e * val;
+  }
+  // warp merge
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float w2 = __shfl_xor_sync(0xffffffffu, w, o);
+    const float mm = fmaxf(m, m2);
+    const float a = (m == -INFINITY) ? 0.f : __expf(m - mm);
+    const float b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
+    s = s * a + s2 * b;
+    w = w * a + w2 * b;
+    m = mm;
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sm[wid] = m, ss[wid] = s, sw[wid] = w;
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+    w = lane < nw ? sw[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float w2 = __shfl_xor_sync(0xffffffffu, w, o);
+      const float mm = fmaxf(m, m2);
+      const float a = (m == -INFINITY) ? 0.f : __expf(m - mm);
+      const float b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
+      s = s * a + s2 * b;
+      w = w * a + w2 * b;
+      m = mm;
+    }
+    if (lane == 0) {
+      const float lse = m + __logf(s);
+      lse_out[row] = lse;
+      if (ent_out) ent_out[row] = lse - w / s;
+      if (lp_out) {
+        int64_t t = target ? target[row] : -1;
+        lp_out[row] = (t >= 0 && t < V) ? __bfloat162float(zr[t]) * inv_tau - lse : 0.f;
+      }
+    }
+  }
+}
+
+// In-place: z <- dL/dz = inv_tau * [dlp * (1[j=t] - p_j) - dent * p_j * (log p_j + H)].
+__global__ void softmax_grad_kernel(__nv_bfloat16* __restrict__ z, int64_t ldz, int V,
+                                    const int64_t* __restrict__ target, float inv_tau,
+                                    const float* __restrict__ lse, const float* __restrict__ ent,
+                                    const float* __restrict__ dlp, const float* __restrict__ dent) {
+  const int64_t row = blockIdx.x;
+  __nv_bfloat16* zr = z + row * ldz;
+  const float L = lse[row];
+  const float gl = dlp ? dlp[row] : 0.f;
+  const float ge = dent ? dent[row] : 0.f;
+  const float Hh = (ent && dent) ? ent[row] : 0.f;
+  const int64_t t = target ? target[row] : -1;
+  const int nv = V >> 3;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    uint4 a = reinterpret_cast<uint4*>(zr)[i];
+    uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float r[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = i * 8 + 2 * j + e;
+        const float zz = (e ? bf16_hi(pa[j]) : bf16_lo(pa[j])) * inv_tau;
+        const float logp = zz - L;
+        const float pj = __expf(logp);
+        float gv = -gl * pj - ge * pj * (logp + Hh);
+        if (col == t) gv += gl;
+        r[e] = gv * inv_tau;
+      }
+      pa[j] = pack_bf16(r[0], r[1]);
+    }
+    reinterpret_cast<uint4*>(zr)[i] = a;
+  }
+  for (int col = (nv << 3) + threadIdx.x; col < V; col += blockDim.x) {
+    const float zz = __bfloat162float(zr[col]) * inv_tau;
+    const float logp = zz - L;
+    const float pj = __expf(logp);
+    float gv = -gl * pj - ge * pj * (logp + Hh);
+    if (col == t) gv += gl;
+    zr[col] = __float2bfloat16(gv * inv_tau);
+  }
+}
+
+inline int grid_for(int64_t work, int threads, int cap = 148 * 16) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+void rmsnorm_fwd(const void* x, const void* res, void* h_out, const void* w, void* y,
+                 float* rstd, int rows, int H, float eps, cudaStream_t st) {
+  if (H % 8) throw std::runtime_error("rmsnorm: hidden size must be a multiple of 8");
+  const int threads = 256, warps = threads / 32;
+  rmsnorm_fwd_kernel<<<(rows + warps - 1) / warps, threads, 0, st>>>(
+      (const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (__nv_bfloat16*)h_out,
+      (const __nv_bfloat16*)w, (__nv_bfloat16*)y, rstd, rows, H, eps);
+}
+
+void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres,
+                 void* dx, float* dw, int rows, int H, cudaStream_t st) {
+  if (H % 8) throw std::runtime_error("rmsnorm: hidden size must be a multiple of 8");
+  const int threads = 256;
+  const int ctas = 148 * 2;
+  const int rows_per_cta = (rows + ctas - 1) / ctas;
+  const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
+  rmsnorm_bwd_kernel<<<grid, threads, H * sizeof(float), st>>>(
+      (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dy,
+      (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, rows, H, rows_per_cta);
+}
+
+void qk_norm_rope_fwd(void* qkv, int64_t row_stride, int n_q, int n_k, const int* pos,
+                      const float* inv_freq, const void* q_w, const void* k_w, float* rstd,
+                      int tokens, float eps, cudaStream_t st) {
+  const int threads = 256, warps = 8;
+  const int64_t work = (int64_t)tokens * (n_q + n_k);
+  qk_norm_rope_fwd_kernel<<<(int)((work + warps - 1) / warps), threads, 0, st>>>(
+      (__nv_bfloat16*)qkv, row_stride, n_q, n_k, pos, inv_freq, (const __nv_bfloat16*)q_w,
+      (const __nv_bfloat16*)k_w, rstd, tokens, eps);
+}
+
+void qk_norm_rope_bwd(void* dqkv, int64_t drow_stride, const void* qkv_pre, int64_t row_stride,
+                      int n_q, int n_k, const int* pos, const float* inv_freq, const void* q_w,
+                      const void* k_w, const float* rstd, float* dq_w, float* dk_w, int tokens,
+                      cudaStream_t st) {
+  const int threads = 256, warps = 8;
+  const int64_t work = (int64_t)tokens * (n_q + n_k);
+  qk_norm_rope_bwd_kernel<<<(int)((work + warps - 1) / warps), threads, 0, st>>>(
+      (__nv_bfloat16*)dqkv, drow_stride, (const __nv_bfloat16*)qkv_pre, row_stride, n_q, n_k, pos,
+      inv_freq, (const __nv_bfloat16*)q_w, (const __nv_bfloat16*)k_w, rstd, dq_w, dk_w, tokens);
+}
+
+void swiglu_fwd(const void* gu, void* h, int64_t rows, int I, cudaStream_t st) {
+  if (I % 8) throw std::runtime_error("swiglu: intermediate size must be a multiple of 8");
+  swiglu_fwd_kernel<<<grid_for(rows * (I / 8), 256), 256, 0, st>>>((const __nv_bfloat16*)gu,
+                                                                  (__nv_bfloat16*)h, rows, I);
+}
+
+void swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t rows, int I, cudaStream_t st) {
+  if (I % 8) throw std::runtime_error("swiglu: intermediate size must be a multiple of 8");
+  swiglu_bwd_kernel<<<grid_for(rows * (I / 8), 256), 256, 0, st>>>(
+      (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dh, (__nv_bfloat16*)dgu, rows, I);
+}
+
+void embedding_fwd(const void* table, const int64_t* ids, void* out, int64_t T, int H, int64_t V,
+                   cudaStream_t st) {
+  embedding_fwd_kernel<<<grid_for(T * (H / 8), 256), 256, 0, st>>>(
+      (const __nv_bfloat16*)table, ids, (__nv_bfloat16*)out, T, H, V);
+}
+
+void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T, int H, int64_t V,
+                   cudaStream_t st) {
+  embedding_bwd_kernel<<<grid_for(T * (H / 4), 256), 256, 0, st>>>((const __nv_bfloat16*)dy, ids,
+                                                                  dtable, T, H, V);
+}
+
+void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,
+                float b1, float b2, float eps, float wd, float bc1, float bc2,
+                const float* gscale_dev, float gscale_host, cudaStream_t st) {
+  if (n <= 0) return;
+  adamw_kernel<<<grid_for((n + 3) / 4, 256, 148 * 8), 256, 0, st>>>(
+      p, g, m, v, (__nv_bfloat16*)p16, n, lr, b1, b2, eps, wd, bc1, bc2, gscale_dev, gscale_host);
+}
+
+void sumsq(const float* x, int64_t n, float* out, cudaStream_t st) {
+  if (n <= 0) return;
+  sumsq_kernel<<<grid_for((n + 3) / 4, 256, 148 * 4), 256, 0, st>>>(x, n, out);
+}
+
+void clip_factor(const float* sumsq_v, float max_norm, float* out, cudaStream_t st) {
+  clip_factor_kernel<<<1, 1, 0, st>>>(sumsq_v, max_norm, out);
+}
+
+void softmax_stats(const void* z, int64_t ldz, int rows, int V, const int64_t* target,
+                   float inv_tau, float* lse, float* lp, float* ent, cudaStream_t st) {
+  if (rows <= 0) return;
+  if ((ldz % 8) || (reinterpret_cast<uintptr_t>(z) & 15))
+    throw std::runtime_error("softmax_stats: rows must be 16-byte aligned");
+  softmax_stats_kernel<<<rows, 512, 0, st>>>((const __nv_bfloat16*)z, ldz, V, target, inv_tau,
+                                             lse, lp, ent);
+}
+
+void softmax_grad(void* z, int64_t ldz, int rows, int V, const int64_t* target, float inv_tau,
+                  const float* lse, const float* ent, const float* dlp, const float* dent,
+                  cudaStream_t st) {
+  if (rows <= 0) return;
+  if ((ldz % 8) || (reinterpret_cast<uintptr_t>(z) & 15))
+    throw std::runtime_error("softmax_grad: rows must be 16-byte aligned");
+  softmax_grad_kernel<<<rows, 512, 0, st>>>((__nv_bfloat16*)z, ldz, V, target, inv_tau, lse, ent,
+                                            dlp, dent);
+}
+
+}  // namespace wb
