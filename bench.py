@@ -1,0 +1,248 @@
+#!/usr/bin/env python
+"""Headline benchmark: SFT tokens/s on the Qwen2.5-7B-shaped dense model.
+
+Contract (one JSON line from rank 0):
+  python bench.py --gpus N --steps K --warmup W            (N=1)
+  torchrun --nproc-per-node N bench.py --gpus N ...        (N>1, one rank per GPU)
+  python bench.py --impl reference ...                     (reference arm)
+
+Workload (BASELINE config "Qwen2.5-7B-shaped dense SFT"): 28 layers, hidden
+3584, 28/4 heads x 128, SwiGLU 18944, vocab 152064 untied, RoPE 1e6, random
+N(0, 0.02) init, bf16 compute / fp32 master + AdamW, sequences of 4096 uniform
+random tokens with the loss masked on a random 10-40% prompt prefix.  Weak
+scaling: every GPU runs 8 micro-batches of 1 x 4096 per optimizer step, so the
+global batch is 8 x N sequences (64 at N = 8).  Data parallelism over N ranks
+with sharded fp32 optimizer state and resident bf16 weights.
+
+Timing: W untimed warm-up steps, then K steps bracketed by barrier +
+cuda.synchronize and CUDA events on the launching stream; the max over ranks is
+reported.  The weights (15 GB) exceed the 126 MB L2, so no flush is needed.
+A second timed run goes through the public ``SFTStepper.train_step`` API with
+the micro-batches copied from pinned host memory each step and the loss read
+back to the host (the "e2e" number).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+BASELINE_TOKS = None  # BASELINE.md publishes no number for this config
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="native", choices=["native", "reference"])
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--seq-len", type=int, default=4096)
+    p.add_argument("--micro-batches", type=int, default=8, help="micro-batches of 1 sequence per GPU per step")
+    p.add_argument("--layers", type=int, default=None, help="(debug only) override layer count; invalidates the number")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def reference_arm(args):
+    reason = (
+        "reference build unavailable: its build backend (hatchling) is not installed and there is no "
+        "offline wheel for it, so `pip install --no-index --find-links /opt/wheelhouse` of the reference fails; "
+        "it also pins torch>=2.13 and vllm>=0.28 (image has torch 2.11, vllm 0.22)"
+    )
+    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if os.path.isdir(os.path.join(ref_dir, "wavelet")):
+        reason = "reference installed but the reference arm runner is not implemented"
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+    return 0
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sms.sort()
+        med = sms[len(sms) // 2] if sms else None
+        return {"sm_mhz": med, "sm_max_mhz": max(maxes) if maxes else None, "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from wavelet_b200.models.config import resolve_arch
+    from wavelet_b200.models.qwen import build_model
+    from wavelet_b200.ops import _ext
+    from wavelet_b200.parallel.dist import destroy_distributed, init_distributed
+    from wavelet_b200.parallel.zero import AdamWHyper
+    from wavelet_b200.data.fake import synthetic_sft_microbatches
+    from wavelet_b200.trainer.engine import Engine
+    from wavelet_b200.trainer.sft_step import SFTStepper
+
+    world = init_distributed(timeout_s=900)
+    rank, N = world.rank, world.world_size
+    assert N == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={N}"
+    dev = world.device
+    _ext.load()
+
+    overrides = {"num_layers": args.layers} if args.layers else None
+    cfg = resolve_arch(args.model, overrides)
+    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234)
+    hyper = AdamWHyper(lr=1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, max_grad_norm=1.0)
+    engine = Engine(model, hyper, dp_group=None, dp_world=N)
+    stepper = SFTStepper(engine, dev)
+
+    S, mb = args.seq_len, args.micro_batches
+    host_batches = synthetic_sft_microbatches(mb, S, cfg.vocab_size, seed=100 + rank)
+    host_batches = [b.pin_memory() for b in host_batches]
+    dev_batches = [b.to(dev) for b in host_batches]
+    torch.cuda.synchronize()
+
+    def step_device():
+        return stepper.train_step(dev_batches, hyper.lr, device_resident=True)
+
+    for _ in range(args.warmup):
+        step_device()
+
+    sampler = ClockSampler(dev.index if dev.index is not None else 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    if N > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with _ext.count_launches() as counter:
+        start.record()
+        for _ in range(args.steps):
+            out = step_device()
+        end.record()
+    torch.cuda.synchronize()
+    if N > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_local = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+    if N > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    launches = counter.count
+    tokens_per_step = N * mb * S
+    value = tokens_per_step / (ms / 1000.0)
+
+    e2e = None
+    if not args.no_e2e:
+        stepper.h2d_bytes = stepper.d2h_bytes = 0
+        if N > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e_s = torch.cuda.Event(enable_timing=True)
+        e_e = torch.cuda.Event(enable_timing=True)
+        e_s.record()
+        for _ in range(args.steps):
+            stepper.train_step(host_batches, hyper.lr)
+        e_e.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e_s.elapsed_time(e_e) / args.steps], device=dev, dtype=torch.float64)
+        if N > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {
+            "value": tokens_per_step / (float(te.item()) / 1000.0),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": stepper.h2d_bytes // args.steps,
+            "d2h_bytes_per_step": stepper.d2h_bytes // args.steps,
+            "ms_per_step": float(te.item()),
+        }
+
+    mfu_flops = 6 * cfg.num_params(active_only=True) + 12 * cfg.num_layers * cfg.hidden_size * S
+    if rank == 0:
+        rec = {
+            "metric": "SFT tok/s (Qwen2.5-7B-shape dense SFT, bf16)",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": N,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None,
+            "dtype": "bf16",
+            "data": "synthetic (uniform random tokens, random-init weights)",
+            "config": {
+                "model": "Qwen2.5-7B-shape" + (f" ({args.layers} layers: INVALID debug run)" if args.layers else ""),
+                "global_batch": N * mb,
+                "seq_len": S,
+                "micro_batch": 1,
+                "grad_accum": mb,
+                "parallelism": f"dp{N}",
+                "optimizer": "AdamW (fp32 master, sharded)",
+                "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",
+            },
+            "mfu": value * mfu_flops / (N * 2.25e15),
+            "loss": out["loss"],
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "e2e": e2e,
+        }
+        print(json.dumps(rec), flush=True)
+    destroy_distributed()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

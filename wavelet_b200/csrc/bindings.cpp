@@ -42,7 +42,8 @@ inline int64_t ld_of(const at::Tensor& t, const char* name) {
 // C[M,N] (op)= alpha * A(m,k) B(n,k) (+bias).
 //   a: [M,K] (a_mn=false) or [K,M] (a_mn=true);  b: [N,K] or [K,N].
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& c,
-          int64_t epi, double alpha, const c10::optional<at::Tensor>& bias) {
+          int64_t epi, double alpha, const c10::optional<at::Tensor>& bias,
+          const c10::optional<at::Tensor>& res) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_cuda(c, "c");
@@ -74,6 +75,14 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
     WB_CHECK(bias->numel() == g.N && bias->is_contiguous(), "gemm: bias must be [N]");
     WB_CHECK(g.epi == wb::kEpiBF16, "gemm: bias only with the bf16 epilogue");
     g.bias = bias->data_ptr();
+  }
+  if (res.has_value() && res->defined()) {
+    check_bf16(*res, "res");
+    WB_CHECK(res->dim() == 2 && res->size(0) == g.M && res->size(1) == g.N,
+             "gemm: residual must be [M, N]");
+    WB_CHECK(g.epi == wb::kEpiBF16, "gemm: residual only with the bf16 epilogue");
+    g.res = res->data_ptr();
+    g.ldr = ld_of(*res, "res");
   }
   wb::gemm_bf16(g, cur_stream());
 }
@@ -252,7 +261,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "wavelet_b200 sm_100a kernels";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"),
         py::arg("b_mn"), py::arg("c"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
-        py::arg("bias") = py::none());
+        py::arg("bias") = py::none(), py::arg("res") = py::none());
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

@@ -57,6 +57,8 @@ constexpr size_t smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(Smem
 struct Params {
   void* C;
   const __nv_bfloat16* bias;
+  const __nv_bfloat16* res;  // optional residual added in the bf16 epilogue
+  int64_t ldr;
   int64_t ldc;
   float alpha;
   int M, N, K;
@@ -88,6 +90,27 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (col0 + j < p.N) f[j] += __bfloat162float(p.bias[col0 + j]);
+    }
+    if (p.res) {
+      const __nv_bfloat16* r = p.res + (int64_t)row * p.ldr + col0;
+      if (full && ((p.ldr & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.res) & 15) == 0)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = reinterpret_cast<const uint4*>(r)[q];
+          f[8 * q + 0] += bf16_lo(w.x);
+          f[8 * q + 1] += bf16_hi(w.x);
+          f[8 * q + 2] += bf16_lo(w.y);
+          f[8 * q + 3] += bf16_hi(w.y);
+          f[8 * q + 4] += bf16_lo(w.z);
+          f[8 * q + 5] += bf16_hi(w.z);
+          f[8 * q + 6] += bf16_lo(w.w);
+          f[8 * q + 7] += bf16_hi(w.w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N) f[j] += __bfloat162float(r[j]);
+      }
     }
     if (full && ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0)) {
       uint4* dst = reinterpret_cast<uint4*>(c);
@@ -344,6 +367,8 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   Params p;
   p.C = g.C;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(g.bias);
+  p.res = reinterpret_cast<const __nv_bfloat16*>(g.res);
+  p.ldr = g.ldr;
   p.ldc = g.ldc;
   p.alpha = g.alpha;
   p.M = g.M;

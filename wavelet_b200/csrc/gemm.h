@@ -23,6 +23,8 @@ struct GemmArgs {
   void* C = nullptr;  // row-major [M, ldc]
   int64_t ldc = 0;
   const void* bias = nullptr;  // bf16 [N] (kEpiBF16 only)
+  const void* res = nullptr;   // bf16 [M, ldr] residual added to C (kEpiBF16 only)
+  int64_t ldr = 0;
   float alpha = 1.0f;
   int epi = kEpiBF16;
   int M = 0, N = 0, K = 0;

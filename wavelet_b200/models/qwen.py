@@ -1,0 +1,192 @@
+"""Qwen2 / Qwen3 / Qwen3-MoE causal LM on flat parameters.
+
+GPU path: embedding -> N x ``DecoderLayerFn`` (fused kernels, recompute) ->
+final RMSNorm -> chunked LM head (``ops.lm_head``).  CPU path: the same math
+with plain PyTorch float32 ops and autograd (used by the CPU/gloo plumbing
+configuration and as the numerics oracle).
+
+Parity: the reference trains Hugging Face ``Qwen2ForCausalLM`` /
+``Qwen3ForCausalLM`` / ``Qwen3MoeForCausalLM`` loaded in trainer/model.py:536;
+parameter names map 1:1 to the HF names (``models.hf_io``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..ops import reference as ref
+from .config import ArchConfig
+from .layers import BatchCtx, DecoderLayerFn, EmbeddingFn, FinalNormFn
+from .params import FlatParams, ParamSpec
+
+
+def param_specs(cfg: ArchConfig) -> list[ParamSpec]:
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    std = cfg.init_std
+    s: list[ParamSpec] = [ParamSpec("embed", (cfg.vocab_size, H), std=std)]
+    for i in range(cfg.num_layers):
+        p = f"l{i}."
+        s.append(ParamSpec(p + "in_norm", (H,), "ones", False))
+        s.append(ParamSpec(p + "qkv_w", (cfg.qkv_dim, H), std=std))
+        if cfg.qkv_bias:
+            s.append(ParamSpec(p + "qkv_b", (cfg.qkv_dim,), "zeros", False))
+        if cfg.qk_norm:
+            s.append(ParamSpec(p + "q_norm", (hd,), "ones", False))
+            s.append(ParamSpec(p + "k_norm", (hd,), "ones", False))
+        s.append(ParamSpec(p + "o_w", (H, cfg.q_dim), std=std))
+        s.append(ParamSpec(p + "post_norm", (H,), "ones", False))
+        if cfg.layer_is_moe(i):
+            E, Ie = cfg.num_experts, cfg.moe_intermediate_size
+            s.append(ParamSpec(p + "router_w", (E, H), std=std))
+            s.append(ParamSpec(p + "exp_gu_w", (E, 2 * Ie, H), std=std))
+            s.append(ParamSpec(p + "exp_down_w", (E, H, Ie), std=std))
+        else:
+            s.append(ParamSpec(p + "gu_w", (2 * I, H), std=std))
+            s.append(ParamSpec(p + "down_w", (H, I), std=std))
+    s.append(ParamSpec("norm", (H,), "ones", False))
+    if not cfg.tie_embeddings:
+        s.append(ParamSpec("lm_head", (cfg.vocab_size, H), std=std))
+    return s
+
+
+@dataclass
+class _Layer:
+    cfg: ArchConfig
+    P: dict
+    G: dict
+    batch: BatchCtx | None = None
+    moe: Any = None
+
+
+class CausalLM:
+    """A decoder-only LM whose parameters live in a ``FlatParams`` store."""
+
+    def __init__(self, cfg: ArchConfig, flat: FlatParams):
+        self.cfg = cfg
+        self.flat = flat
+        self.device = flat.device
+        self.inv_freq = ref.rope_inv_freq(cfg.head_dim, cfg.rope_theta, device=self.device)
+        self.layers: list[_Layer] = []
+        for i in range(cfg.num_layers):
+            pre = f"l{i}."
+            names = [n for n in flat.names() if n.startswith(pre)]
+            P = {n[len(pre):]: flat.view(n) for n in names}
+            G = {n[len(pre):]: flat.grad_view(n) for n in names} if flat.grad is not None else {}
+            layer = _Layer(cfg, P, G)
+            if cfg.layer_is_moe(i):
+                from .moe import MoEBlock
+
+                layer.moe = MoEBlock(cfg, i)
+            self.layers.append(layer)
+        self.anchor = torch.empty(0, device=self.device, requires_grad=True)
+        self.ep_group = None
+
+    # ----------------------------------------------------------- weights
+    def weight(self, name: str) -> torch.Tensor:
+        return self.flat.view(name)
+
+    def grad(self, name: str) -> torch.Tensor | None:
+        return self.flat.grad_view(name)
+
+    @property
+    def head_name(self) -> str:
+        return "embed" if self.cfg.tie_embeddings else "lm_head"
+
+    def head_weight(self) -> torch.Tensor:
+        return self.flat.view(self.head_name)
+
+    def head_grad(self) -> torch.Tensor | None:
+        return self.flat.grad_view(self.head_name)
+
+    # ----------------------------------------------------------- batches
+    def batch_ctx(self, position_ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> BatchCtx:
+        return BatchCtx(
+            pos=position_ids.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous(),
+            cu_seqlens=cu_seqlens.to(device=self.device, dtype=torch.int32).contiguous(),
+            max_seqlen=int(max_seqlen),
+            inv_freq=self.inv_freq,
+        )
+
+    # ----------------------------------------------------------- forward
+    def hidden(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
+        """Final normalised hidden states [T, H] (autograd-connected)."""
+        if not input_ids.is_cuda:
+            return self._hidden_cpu(input_ids.reshape(-1), batch)
+        ids = input_ids.reshape(-1).contiguous()
+        x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"))
+        for layer in self.layers:
+            layer.batch = batch
+            if layer.moe is not None:
+                layer.moe.ep_group = self.ep_group
+            x = DecoderLayerFn.apply(x, self.anchor, layer)
+        return FinalNormFn.apply(x, self.weight("norm"), self.grad("norm"), self.cfg.rms_eps)
+
+    # CPU float32 reference path (autograd through views of flat.compute)
+    def _hidden_cpu(self, ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
+        cfg = self.cfg
+        flat = self.flat
+        if not flat.compute.requires_grad:
+            flat.compute.requires_grad_(True)
+
+        def W(n):
+            off, k = flat.offsets[n]
+            shape = next(s.shape for s in flat.specs if s.name == n)
+            return flat.compute[off : off + k].view(shape)
+
+        T = ids.shape[0]
+        nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        x = W("embed")[ids]
+        for i in range(cfg.num_layers):
+            p = f"l{i}."
+            h = ref.rmsnorm(x, W(p + "in_norm"), cfg.rms_eps)
+            qkv = F.linear(h, W(p + "qkv_w"), W(p + "qkv_b") if cfg.qkv_bias else None)
+            q = qkv[:, : nq * hd].view(T, nq, hd)
+            k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
+            v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
+            if cfg.qk_norm:
+                q = ref.rmsnorm(q, W(p + "q_norm"), cfg.rms_eps)
+                k = ref.rmsnorm(k, W(p + "k_norm"), cfg.rms_eps)
+            q = ref.apply_rope(q, batch.pos, batch.inv_freq)
+            k = ref.apply_rope(k, batch.pos, batch.inv_freq)
+            att = ref.attention(q, k, v, batch.cu_seqlens, True)
+            x = x + F.linear(att.reshape(T, nq * hd), W(p + "o_w"))
+            h2 = ref.rmsnorm(x, W(p + "post_norm"), cfg.rms_eps)
+            if cfg.layer_is_moe(i):
+                from .moe import moe_reference
+
+                x = x + moe_reference(h2, W(p + "router_w"), W(p + "exp_gu_w"), W(p + "exp_down_w"), cfg)[0]
+            else:
+                x = x + F.linear(ref.swiglu(F.linear(h2, W(p + "gu_w"))), W(p + "down_w"))
+        return ref.rmsnorm(x, W("norm"), cfg.rms_eps)
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        W = self.head_weight()
+        if h.is_cuda:
+            return ops.gemm(h.contiguous(), W)
+        off, k = self.flat.offsets[self.head_name]
+        Wv = self.flat.compute[off : off + k].view(W.shape)
+        return h @ Wv.t()
+
+    def collect_cpu_grads(self) -> None:
+        """CPU path: move autograd grads of the flat buffer into flat.grad."""
+        g = self.flat.compute.grad
+        if g is not None and self.flat.grad is not None:
+            self.flat.grad.add_(g.float())
+            self.flat.compute.grad = None
+
+
+def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
+                with_grad=True, with_optimizer=True) -> CausalLM:
+    device = torch.device(device)
+    if dtype is None:
+        dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    flat = FlatParams(param_specs(cfg), device, dtype, dp_rank, dp_world, with_grad, with_optimizer)
+    if init:
+        flat.init_(seed)
+    return CausalLM(cfg, flat)

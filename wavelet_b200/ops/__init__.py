@@ -1,0 +1,227 @@
+"""Fused operators of wavelet_b200.
+
+Every op has two implementations selected by the device of its inputs:
+
+* CUDA tensors run the hand-written sm_100a kernels of the in-tree ``wb_C``
+  extension (``wavelet_b200/csrc``).  There is no silent fallback: if the
+  extension cannot be loaded on a GPU machine the op raises.
+* CPU tensors run the float32 PyTorch formulation in ``ops.reference`` (the
+  CPU/gloo plumbing configuration and the numerics oracle).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ._ext import load as _load_ext
+
+EPI_BF16 = 0
+EPI_F32 = 1
+EPI_F32_ACC = 2
+
+
+def ext():
+    """The loaded CUDA extension (raises if it cannot be built/loaded)."""
+    return _load_ext()
+
+
+# --------------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False,
+         out: Optional[torch.Tensor] = None, epi: int = EPI_BF16, alpha: float = 1.0,
+         bias: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """C[M, N] = alpha * A(m, k) B(n, k) (+ bias + res) on the tcgen05 GEMM.
+
+    ``a`` is [M, K] (K-major) or [K, M] with ``a_mn``; ``b`` is [N, K] or [K, N]
+    with ``b_mn``.  ``epi`` selects bf16 store, fp32 store or fp32 accumulate.
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        dtype = torch.bfloat16 if epi == EPI_BF16 else torch.float32
+        out = torch.empty(M, N, device=a.device, dtype=dtype)
+    if not a.is_cuda:
+        A = a.t() if a_mn else a
+        B = b if b_mn else b.t()
+        r = alpha * (A.float() @ B.float())
+        if bias is not None:
+            r = r + bias.float()
+        if res is not None:
+            r = r + res.float()
+        if epi == EPI_F32_ACC:
+            out.add_(r)
+        else:
+            out.copy_(r)
+        return out
+    ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
+    return out
+
+
+class LinearFn(torch.autograd.Function):
+    """y = x W^T (+ b); the weight gradient is accumulated in fp32 directly
+    into ``main_grad`` by the GEMM epilogue (no bf16 dW is materialised)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, main_grad, bias_grad):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        y = gemm(x2, w, bias=b)
+        ctx.save_for_backward(x2, w)
+        ctx.main_grad = main_grad
+        ctx.bias_grad = bias_grad
+        ctx.has_bias = b is not None
+        ctx.shp = shp
+        return y.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = dy.reshape(-1, w.shape[0]).contiguous()
+        dx = gemm(dy2, w, b_mn=True)
+        dw = None
+        if ctx.main_grad is not None:
+            gemm(dy2, x2, a_mn=True, b_mn=True, out=ctx.main_grad, epi=EPI_F32_ACC)
+        elif ctx.needs_input_grad[1]:
+            dw = gemm(dy2, x2, a_mn=True, b_mn=True, epi=EPI_F32).to(w.dtype)
+        db = None
+        if ctx.has_bias:
+            s = dy2.float().sum(0)
+            if ctx.bias_grad is not None:
+                ctx.bias_grad.add_(s)
+            else:
+                db = s.to(w.dtype)
+        return dx.view(ctx.shp), dw, db, None, None
+
+
+def linear(x, w, b=None, main_grad=None, bias_grad=None):
+    if not x.is_cuda:
+        return torch.nn.functional.linear(x, w, b)
+    return LinearFn.apply(x, w, b, main_grad, bias_grad)
+
+
+# ------------------------------------------------------------------ RMSNorm
+def rmsnorm_fwd(x, w, eps, res=None, want_h=False):
+    """Returns (y, rstd, h) with h = x + res when ``res`` is given."""
+    x = x.contiguous()
+    if not x.is_cuda:
+        h = x + res if res is not None else x
+        hf = h.float()
+        rstd = torch.rsqrt(hf.pow(2).mean(-1) + eps)
+        y = (hf * rstd[..., None] * w.float()).to(x.dtype)
+        return y, rstd, h
+    y = torch.empty_like(x)
+    rows = x.numel() // x.shape[-1]
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    h = torch.empty_like(x) if (res is not None and want_h) else None
+    ext().rmsnorm_fwd(x, res, h, w, y, rstd, eps)
+    return y, rstd, h
+
+
+def rmsnorm_bwd(x, w, rstd, dy, dres=None, dw=None):
+    dx = torch.empty_like(x)
+    ext().rmsnorm_bwd(x, w, rstd, dy.contiguous(), dres, dx, dw)
+    return dx
+
+
+class RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps, w_grad):
+        y, rstd, _ = rmsnorm_fwd(x, w, eps)
+        ctx.save_for_backward(x, w, rstd)
+        ctx.w_grad = w_grad
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        if ctx.w_grad is not None:
+            dx = rmsnorm_bwd(x, w, rstd, dy, dw=ctx.w_grad)
+            return dx, None, None, None
+        dw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+        dx = rmsnorm_bwd(x, w, rstd, dy, dw=dw)
+        return dx, dw.to(w.dtype), None, None
+
+
+def rmsnorm(x, w, eps=1e-6, w_grad=None):
+    if not x.is_cuda:
+        return ref.rmsnorm(x, w, eps)
+    return RMSNormFn.apply(x, w, eps, w_grad)
+
+
+# ----------------------------------------------------------------- SwiGLU
+def swiglu_fwd(gu):
+    if not gu.is_cuda:
+        return ref.swiglu(gu)
+    I = gu.shape[-1] // 2
+    h = torch.empty(*gu.shape[:-1], I, device=gu.device, dtype=gu.dtype)
+    ext().swiglu_fwd(gu.contiguous(), h)
+    return h
+
+
+def swiglu_bwd(gu, dh):
+    dgu = torch.empty_like(gu)
+    ext().swiglu_bwd(gu.contiguous(), dh.contiguous(), dgu)
+    return dgu
+
+
+# ----------------------------------------------------------- QK-norm + RoPE
+def qk_norm_rope_(qkv, n_q, n_k, pos, inv_freq, q_w=None, k_w=None, eps=1e-6):
+    """In place on the q and k heads of a packed [T, (n_q+2 n_k) * 128] qkv row."""
+    if not qkv.is_cuda:
+        T = qkv.shape[0]
+        heads = qkv[:, : (n_q + n_k) * 128].view(T, n_q + n_k, 128)
+        x = heads
+        if q_w is not None:
+            q = ref.rmsnorm(x[:, :n_q], q_w, eps)
+            k = ref.rmsnorm(x[:, n_q:], k_w, eps)
+            x = torch.cat([q, k], 1)
+        heads.copy_(ref.apply_rope(x, pos, inv_freq))
+        return None
+    rstd = torch.empty(qkv.shape[0] * (n_q + n_k), device=qkv.device, dtype=torch.float32) if q_w is not None else None
+    ext().qk_norm_rope_fwd(qkv, n_q, n_k, pos, inv_freq, q_w, k_w, rstd, eps)
+    return rstd
+
+
+# ---------------------------------------------------------------- embedding
+def embedding_fwd(table, ids):
+    if not table.is_cuda:
+        return table[ids]
+    out = torch.empty(ids.numel(), table.shape[1], device=table.device, dtype=table.dtype)
+    ext().embedding_fwd(table, ids.reshape(-1).contiguous(), out)
+    return out
+
+
+def embedding_bwd_(dy, ids, dtable):
+    ext().embedding_bwd(dy.contiguous(), ids.reshape(-1).contiguous(), dtable)
+
+
+# -------------------------------------------------------------- attention
+from .attention import attention_bwd, attention_fwd  # noqa: E402
+
+# ----------------------------------------------------------------- AdamW
+def adamw_flat_(p, g, m, v, p16, *, lr, betas, eps, weight_decay, step, gscale=None, gscale_host=1.0):
+    """One fused AdamW step over flat fp32 buffers, writing the bf16 shadow."""
+    if not p.is_cuda:
+        b1, b2 = betas
+        gg = g * gscale_host * (gscale if gscale is not None else 1.0)
+        m.mul_(b1).add_(gg, alpha=1 - b1)
+        v.mul_(b2).addcmul_(gg, gg, value=1 - b2)
+        p.mul_(1 - lr * weight_decay)
+        bc1 = 1 - b1**step
+        bc2 = 1 - b2**step
+        p.addcdiv_(m, (v.sqrt() / math.sqrt(bc2)).add_(eps), value=-lr / bc1)
+        if p16 is not None:
+            p16.copy_(p)
+        return
+    ext().adamw_step(p, g, m, v, p16, lr, betas[0], betas[1], eps, weight_decay, step, gscale, gscale_host)
+
+
+def sumsq_(x, out):
+    if not x.is_cuda:
+        out[0] += x.double().pow(2).sum().float()
+        out[1] += (~torch.isfinite(x)).sum().float()
+        return
+    ext().sumsq(x, out)

@@ -123,3 +123,48 @@ def available() -> bool:
         return True
     except Exception:  # pragma: no cover - depends on the toolchain
         return False
+
+
+# --------------------------------------------------------------------------
+# Launch accounting: while a ``count_launches()`` block is active, every call
+# into the extension is counted (each binding launches one kernel, except
+# ``adamw_step``/``gemm`` which also launch exactly one).  bench.py reports the
+# count of kernels this repository launched inside its timed region.
+_NON_KERNEL = {"read_error", "clear_error"}
+
+
+class _CountingProxy:
+    def __init__(self, mod: ModuleType):
+        self._mod = mod
+        self.count = 0
+
+    def __getattr__(self, name):
+        attr = getattr(self._mod, name)
+        if callable(attr) and name not in _NON_KERNEL:
+            def wrapped(*a, **k):
+                self.count += 1
+                return attr(*a, **k)
+
+            return wrapped
+        return attr
+
+
+class count_launches:
+    """Context manager counting extension kernel launches."""
+
+    def __enter__(self):
+        global _module
+        base = load()
+        self._base = base
+        self.proxy = _CountingProxy(base)
+        _module = self.proxy  # type: ignore[assignment]
+        return self
+
+    @property
+    def count(self) -> int:
+        return self.proxy.count
+
+    def __exit__(self, *exc):
+        global _module
+        _module = self._base
+        return False

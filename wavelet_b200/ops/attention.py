@@ -1,0 +1,87 @@
+"""Packed variable-length causal attention (training forward/backward).
+
+Layout: q [T, Hq, 128], k/v [T, Hk, 128] bf16 with sequences packed along T
+and delimited by ``cu_seqlens`` (int32 [n+1]); GQA with Hq % Hk == 0.  This is
+the varlen attention the reference reaches through FA2/FA3/SDPA with packed
+``position_ids`` (trainer/rl.py:189-229, trainer/model.py:315-360).
+
+CUDA tensors use the extension's sm_100a attention kernels when they are
+compiled in (``wb_C.attn_fwd``/``attn_bwd``); until then the PyTorch-bundled
+flash-attention kernels are used and ``native_attention()`` reports False.
+CPU tensors use the float32 reference in ``ops.reference``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import reference as ref
+from ._ext import load as _load_ext
+
+
+def native_attention() -> bool:
+    try:
+        return hasattr(_load_ext(), "attn_fwd")
+    except Exception:
+        return False
+
+
+def attention_fwd(q, k, v, cu_seqlens, max_seqlen: int, causal: bool = True, scale: float | None = None):
+    """Returns (out [T, Hq, D], lse [Hq, T] fp32)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not q.is_cuda:
+        out = ref.attention(q, k, v, cu_seqlens, causal, scale)
+        return out, None
+    m = _load_ext()
+    if hasattr(m, "attn_fwd"):
+        out = torch.empty_like(q)
+        lse = torch.empty(q.shape[1], q.shape[0], device=q.device, dtype=torch.float32)
+        m.attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), bool(causal), float(scale), out, lse)
+        return out, lse
+    out, lse, _rng, _unused, _dbg = torch.ops.aten._flash_attention_forward(
+        q, k, v, cu_seqlens, cu_seqlens, int(max_seqlen), int(max_seqlen), 0.0, bool(causal), False, scale=scale
+    )
+    return out, lse
+
+
+def attention_bwd(do, q, k, v, out, lse, cu_seqlens, max_seqlen: int, causal: bool = True, scale: float | None = None):
+    """Returns (dq, dk, dv)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    m = _load_ext()
+    if hasattr(m, "attn_bwd"):
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        m.attn_bwd(do.contiguous(), q, k, v, out, lse, cu_seqlens, int(max_seqlen), bool(causal), float(scale), dq, dk, dv)
+        return dq, dk, dv
+    rng = torch.zeros(2, dtype=torch.int64, device=q.device)
+    unused = torch.empty(0, device=q.device)
+    dq, dk, dv = torch.ops.aten._flash_attention_backward(
+        do.contiguous(), q, k, v, out, lse, cu_seqlens, cu_seqlens, int(max_seqlen), int(max_seqlen), 0.0,
+        bool(causal), rng, unused, scale=scale
+    )
+    return dq, dk, dv
+
+
+class AttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, causal, scale):
+        out, lse = attention_fwd(q, k, v, cu_seqlens, max_seqlen, causal, scale)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens)
+        ctx.cfg = (max_seqlen, causal, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, out, lse, cu = ctx.saved_tensors
+        max_seqlen, causal, scale = ctx.cfg
+        dq, dk, dv = attention_bwd(do, q, k, v, out, lse, cu, max_seqlen, causal, scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def attention(q, k, v, cu_seqlens, max_seqlen, causal=True, scale=None):
+    if not q.is_cuda:
+        return ref.attention(q, k, v, cu_seqlens, causal, scale)
+    return AttentionFn.apply(q, k, v, cu_seqlens, max_seqlen, causal, scale)

@@ -1,0 +1,89 @@
+"""Training engine: micro-steps and optimizer steps on a ``CausalLM``.
+
+The engine owns no data logic; trainers (SFT, RL) feed it device tensors in
+the packed layout (``input_ids`` [T], ``position_ids`` [T], ``cu_seqlens``)
+and per-token loss weights.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from ..models.qwen import CausalLM
+from ..ops import lm_head
+from ..parallel.zero import AdamWHyper, ShardedAdamW
+
+
+@dataclass
+class PackedBatch:
+    input_ids: torch.Tensor  # int64 [T]
+    position_ids: torch.Tensor  # int32 [T]
+    cu_seqlens: torch.Tensor  # int32 [n+1]
+    max_seqlen: int
+    targets: torch.Tensor  # int64 [T], -100 = ignore
+    loss_mask: torch.Tensor  # float [T]
+
+    def to(self, device, non_blocking=True) -> "PackedBatch":
+        return PackedBatch(
+            self.input_ids.to(device, non_blocking=non_blocking),
+            self.position_ids.to(device, non_blocking=non_blocking),
+            self.cu_seqlens.to(device, non_blocking=non_blocking),
+            self.max_seqlen,
+            self.targets.to(device, non_blocking=non_blocking),
+            self.loss_mask.to(device, non_blocking=non_blocking),
+        )
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.numel())
+
+    def pin_memory(self) -> "PackedBatch":
+        return PackedBatch(
+            self.input_ids.pin_memory(), self.position_ids.pin_memory(), self.cu_seqlens.pin_memory(),
+            self.max_seqlen, self.targets.pin_memory(), self.loss_mask.pin_memory(),
+        )
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.input_ids, self.position_ids, self.cu_seqlens, self.targets, self.loss_mask))
+
+
+class Engine:
+    def __init__(self, model: CausalLM, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
+                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK):
+        self.model = model
+        self.opt = ShardedAdamW(model.flat, hyper, dp_group, dp_world)
+        self.dp_group = dp_group
+        self.dp_world = dp_world
+        self.chunk = lm_head_chunk
+
+    # --------------------------------------------------------------- SFT
+    def sft_micro_step(self, b: PackedBatch, token_scale: float) -> torch.Tensor:
+        """Forward + backward of the token-normalised CE on one micro-batch.
+
+        ``token_scale`` = 1 / (loss tokens of the whole step over all ranks),
+        so that summing gradients across micro-batches and ranks yields the
+        global token mean (parity: trainer/trainer.py:1317-1372).
+        Returns the (scaled) loss contribution as a device scalar.
+        """
+        m = self.model
+        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen)
+        h = m.hidden(b.input_ids, ctx)
+        weights = b.loss_mask.float() * token_scale
+        loss, dh = lm_head.sft_loss_and_grad(h.detach(), m.head_weight(), b.targets, weights, m.head_grad(), self.chunk)
+        h.backward(dh)
+        if not b.input_ids.is_cuda:
+            m.collect_cpu_grads()
+        return loss
+
+    def optimizer_step(self, lr: float) -> dict[str, float]:
+        return self.opt.step(lr)
+
+    def global_token_count(self, local: float, device) -> float:
+        if self.dp_world > 1 and dist.is_initialized():
+            t = torch.tensor([local], device=device, dtype=torch.float64)
+            dist.all_reduce(t, group=self.dp_group)
+            return float(t.item())
+        return float(local)
