@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "attention.h"
 #include "gemm.h"
 #include "kernels.h"
 
@@ -252,6 +253,74 @@ void softmax_grad(at::Tensor& z, const c10::optional<at::Tensor>& target, double
                    cur_stream());
 }
 
+// q/k/v: [T, H, 128] views whose head and dim strides are (128, 1).
+static int64_t head_row_stride(const at::Tensor& t, const char* name) {
+  check_bf16(t, name);
+  WB_CHECK(t.dim() == 3 && t.size(2) == 128, std::string(name) + " must be [T, H, 128]");
+  WB_CHECK(t.stride(2) == 1 && t.stride(1) == 128, std::string(name) + " must have head stride 128, dim stride 1");
+  return t.stride(0);
+}
+
+static wb::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                              const at::Tensor& cu, int64_t max_seqlen, bool causal, double scale) {
+  WB_CHECK(causal, "attention: only causal attention is implemented");
+  WB_CHECK(cu.scalar_type() == at::kInt && cu.is_cuda() && cu.is_contiguous(), "attention: cu_seqlens must be int32 CUDA");
+  wb::AttnArgs a;
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.q_row = head_row_stride(q, "q");
+  a.k_row = head_row_stride(k, "k");
+  a.v_row = head_row_stride(v, "v");
+  a.T = q.size(0);
+  a.Hq = q.size(1);
+  a.Hk = k.size(1);
+  WB_CHECK(k.size(0) == a.T && v.size(0) == a.T && v.size(1) == a.Hk, "attention: k/v shape mismatch");
+  a.cu_seqlens = cu.data_ptr<int>();
+  a.nseq = cu.numel() - 1;
+  a.max_seqlen = max_seqlen;
+  a.scale = static_cast<float>(scale);
+  return a;
+}
+
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
+              int64_t max_seqlen, bool causal, double scale, at::Tensor& out, at::Tensor& lse) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  wb::AttnArgs a = attn_args(q, k, v, cu, max_seqlen, causal, scale);
+  check_bf16(out, "out");
+  WB_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "attention: out must be contiguous [T, Hq, 128]");
+  check_f32(lse, "lse");
+  WB_CHECK(lse.is_contiguous() && lse.size(0) == a.Hq && lse.size(1) == a.T, "attention: lse must be [Hq, T]");
+  a.o = out.data_ptr();
+  a.o_row = out.stride(0);
+  a.lse = lse.data_ptr<float>();
+  if (a.T == 0 || a.nseq == 0) return;
+  wb::attn_fwd(a, cur_stream());
+}
+
+void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+              const at::Tensor& out, const at::Tensor& lse, const at::Tensor& cu, int64_t max_seqlen, bool causal,
+              double scale, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  wb::AttnBwdArgs b;
+  b.f = attn_args(q, k, v, cu, max_seqlen, causal, scale);
+  check_bf16(dout, "dout");
+  WB_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes(), "attention: dout must be contiguous [T, Hq, 128]");
+  WB_CHECK(out.sizes() == q.sizes() && out.stride(2) == 1 && out.stride(1) == 128, "attention: bad out");
+  b.f.o = const_cast<void*>(out.data_ptr());
+  b.f.o_row = out.stride(0);
+  b.f.lse = const_cast<float*>(lse.data_ptr<float>());
+  for (auto* t : {&dq, &dk, &dv}) WB_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16, "attention: grads must be contiguous bf16");
+  b.dout = dout.data_ptr();
+  b.dq = dq.data_ptr();
+  b.dk = dk.data_ptr();
+  b.dv = dv.data_ptr();
+  at::Tensor delta = at::empty({b.f.Hq, b.f.T}, q.options().dtype(at::kFloat));
+  b.delta = delta.data_ptr<float>();
+  if (b.f.T == 0 || b.f.nseq == 0) return;
+  wb::attn_bwd(b, cur_stream());
+}
+
 int64_t read_error(int64_t device) { return wb::read_error_word((int)device); }
 void clear_error(int64_t device) { wb::clear_error_word((int)device); }
 
@@ -275,6 +344,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_factor", &clip_factor);
   m.def("softmax_stats", &softmax_stats);
   m.def("softmax_grad", &softmax_grad);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.attr("EPI_BF16") = (int)wb::kEpiBF16;

@@ -1,0 +1,299 @@
+"""SFT data pipeline: sources, normalisation, tokenisation with role loss
+masks, packing and a resumable per-rank iterator.
+
+Sources (``data.source``):
+* ``local`` — ``.jsonl`` / ``.json`` / ``.parquet`` files (one or many);
+* ``hf`` — ``datasets.load_dataset`` (offline cache only on this machine);
+* ``fake`` — synthetic token ids (``fake_vocab_size``, ``fake_length``,
+  ``fake_input_ids``), no tokenizer needed.
+
+Records are prompt/completion pairs or chat ``messages``; the loss mask is set
+per message role by ``data.loss_mask`` (assistant only by default).  Packing:
+``pad`` (one example per row, right padding) or ``cat`` (examples concatenated
+into ``seq_len`` windows with sequence boundaries kept in ``cu_seqlens`` so
+attention never crosses examples).
+
+Parity: data/sft.py:25-994 of the reference (sources, mixing, chat templates,
+role loss masks, pad/cat packing, stateful resume).
+"""
+
+from __future__ import annotations
+
+import json
+import random
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Iterator
+
+import torch
+
+from ..trainer.engine import PackedBatch
+
+
+@dataclass
+class Sample:
+    input_ids: list[int]
+    loss_mask: list[int]
+    source: str = "local"
+
+
+# ------------------------------------------------------------------- sources
+def _paths(v) -> list[Path]:
+    return [Path(p) for p in (v if isinstance(v, list) else [v])]
+
+
+def load_payloads(path: Path) -> list[dict[str, Any]]:
+    if path.suffix == ".jsonl":
+        return [json.loads(l) for l in path.read_text(encoding="utf-8").splitlines() if l.strip()]
+    if path.suffix == ".json":
+        data = json.loads(path.read_text(encoding="utf-8"))
+        return data if isinstance(data, list) else [data]
+    if path.suffix == ".parquet":
+        import pyarrow.parquet as pq
+
+        return pq.read_table(path).to_pylist()
+    raise ValueError(f"unsupported data file {path} (use .jsonl, .json or .parquet)")
+
+
+def _mix(groups: list[list[dict]], probs: list[float] | None, strategy: str, seed: int) -> list[dict]:
+    if len(groups) == 1:
+        return groups[0]
+    if probs is None:
+        return [r for g in groups for r in g]
+    if len(probs) != len(groups):
+        raise ValueError("probabilities must match the number of dataset groups")
+    rng = random.Random(seed)
+    iters = [list(g) for g in groups]
+    pos = [0] * len(groups)
+    out = []
+    exhausted = set()
+    while True:
+        i = rng.choices(range(len(groups)), weights=probs)[0]
+        if pos[i] >= len(iters[i]):
+            exhausted.add(i)
+            if strategy == "first_exhausted" or len(exhausted) == len(groups):
+                break
+            pos[i] = 0
+        out.append(iters[i][pos[i]])
+        pos[i] += 1
+    return out
+
+
+def load_records(cfg) -> list[dict[str, Any]]:
+    if cfg.source == "local":
+        groups = [load_payloads(p) for p in _paths(cfg.path)]
+    elif cfg.source == "hf":
+        from datasets import load_dataset  # offline cache only
+
+        pairs = list(zip(cfg.hf_subsets or [None] * len(cfg.hf_splits or ["train"]), cfg.hf_splits or ["train"] * len(cfg.hf_subsets or [None])))
+        groups = [[dict(r) for r in load_dataset(cfg.hf_name, s, split=sp)] for s, sp in pairs]
+    else:
+        return []
+    for g, name in zip(groups, [str(p) for p in _paths(cfg.path)] if cfg.source == "local" else [cfg.hf_name] * len(groups)):
+        for r in g:
+            r.setdefault("__source", Path(name).stem if cfg.source == "local" else name)
+    rows = _mix(groups, cfg.probabilities, cfg.stopping_strategy, cfg.seed)
+    if cfg.max_examples is not None:
+        rows = rows[: cfg.max_examples]
+    return rows
+
+
+# ------------------------------------------------------------- normalisation
+def normalize_messages(row: dict[str, Any], cfg) -> list[dict[str, Any]]:
+    if cfg.messages_column in row and row[cfg.messages_column]:
+        msgs = row[cfg.messages_column]
+        if isinstance(msgs, str):
+            msgs = json.loads(msgs)
+        msgs = [dict(m) for m in msgs]
+    else:
+        prompt = row.get(cfg.prompt_column)
+        completion = row.get(cfg.completion_column)
+        if prompt is None or completion is None:
+            raise ValueError(f"record has neither '{cfg.messages_column}' nor '{cfg.prompt_column}'/'{cfg.completion_column}'")
+        msgs = []
+        msgs += prompt if isinstance(prompt, list) else [{"role": "user", "content": str(prompt)}]
+        msgs += completion if isinstance(completion, list) else [{"role": "assistant", "content": str(completion)}]
+    if cfg.merge_messages_thinking:
+        for m in msgs:
+            th = m.pop("reasoning_content", None) or m.pop("thinking", None)
+            if th and m.get("role") == "assistant":
+                m["content"] = f"<think>\n{th}\n</think>\n\n{m.get('content') or ''}"
+    if cfg.system_prompt and not (msgs and msgs[0].get("role") == "system"):
+        msgs = [{"role": "system", "content": cfg.system_prompt}] + msgs
+    return msgs
+
+
+def _role_trainable(role: str, lm) -> bool:
+    return bool(getattr(lm, role, False)) if role in ("system", "user", "assistant", "tool") else False
+
+
+def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
+    """Tokenise message by message so every token knows its role.
+
+    With a template-capable tokenizer the rendered prefix of messages[:i+1]
+    is diffed against messages[:i] (exact under incremental templates); the
+    char tokenizer renders each message independently.
+    """
+    ids: list[int] = []
+    mask: list[int] = []
+    if hasattr(tok, "render_message"):
+        for m in msgs:
+            t = tok.encode(tok.render_message(m["role"], str(m.get("content") or "")))
+            ids += t
+            mask += [1 if _role_trainable(m["role"], cfg.loss_mask) else 0] * len(t)
+        ids.append(tok.eos_token_id)
+        mask.append(1 if _role_trainable(msgs[-1]["role"], cfg.loss_mask) else 0)
+        return Sample(ids, mask)
+    prev: list[int] = []
+    for i, m in enumerate(msgs):
+        cur = tok.apply_chat_template(msgs[: i + 1], tokenize=True, add_generation_prompt=False)
+        if hasattr(cur, "input_ids"):
+            cur = cur["input_ids"]
+        cur = list(cur)
+        if cur[: len(prev)] != prev:  # non-incremental template: fall back to suffix tokens
+            common = 0
+            while common < min(len(cur), len(prev)) and cur[common] == prev[common]:
+                common += 1
+            ids = ids[:common]
+            mask = mask[:common]
+            prev = prev[:common]
+        new = cur[len(prev):]
+        ids += new
+        mask += [1 if _role_trainable(m["role"], cfg.loss_mask) else 0] * len(new)
+        prev = cur
+    return Sample(ids, mask)
+
+
+# ----------------------------------------------------------------- datasets
+@dataclass
+class SFTDataState:
+    epoch: int = 0
+    cursor: int = 0
+    num_samples: dict[str, int] = field(default_factory=dict)
+    num_tokens: dict[str, int] = field(default_factory=dict)
+
+
+class SFTDataset:
+    """Per-rank iterator of packed micro-batches with a resumable cursor."""
+
+    def __init__(self, cfg, tokenizer=None, dp_rank: int = 0, dp_world: int = 1, seed: int = 0):
+        self.cfg = cfg
+        self.tok = tokenizer
+        self.dp_rank = dp_rank
+        self.dp_world = dp_world
+        self.seed = seed + cfg.seed
+        self.state = SFTDataState()
+        self._samples: list[Sample] | None = None
+
+    # samples --------------------------------------------------------------
+    def _fake_samples(self) -> list[Sample]:
+        c = self.cfg
+        n = c.max_examples or max(c.batch_size * 4, 8)
+        g = torch.Generator().manual_seed(self.seed)
+        out = []
+        lo, hi = getattr(c, "fake_prompt_fraction", (0.0, 0.0))
+        for i in range(n):
+            L = c.seq_len if c.fake_length == "fixed" else int(torch.randint(max(8, c.seq_len // 4), c.seq_len + 1, (1,), generator=g))
+            if c.fake_input_ids == "increasing":
+                ids = [(3 + i + j) % c.fake_vocab_size for j in range(L)]
+            else:
+                ids = torch.randint(3, c.fake_vocab_size, (L,), generator=g).tolist()
+            f = lo + (hi - lo) * float(torch.rand((), generator=g)) if hi > 0 else 0.0
+            mask = [0] * int(f * L) + [1] * (L - int(f * L))
+            out.append(Sample(ids, mask, "fake"))
+        return out
+
+    def samples(self) -> list[Sample]:
+        if self._samples is None:
+            if self.cfg.source == "fake":
+                self._samples = self._fake_samples()
+            else:
+                if self.tok is None:
+                    raise ValueError("a tokenizer is required for non-fake SFT data")
+                self._samples = []
+                for r in load_records(self.cfg):
+                    s = tokenize_messages(normalize_messages(r, self.cfg), self.tok, self.cfg)
+                    s.source = r.get("__source", "local")
+                    if s.input_ids:
+                        self._samples.append(s)
+        return self._samples
+
+    def _order(self, epoch: int) -> list[int]:
+        idx = list(range(len(self.samples())))
+        if self.cfg.shuffle:
+            random.Random(self.seed * 7919 + epoch).shuffle(idx)
+        return idx
+
+    def _next_sample(self) -> Sample:
+        order = self._order(self.state.epoch)
+        if not order:
+            raise ValueError("empty SFT dataset")
+        while True:
+            if self.state.cursor >= len(order):
+                self.state.epoch += 1
+                self.state.cursor = 0
+                order = self._order(self.state.epoch)
+            i = order[self.state.cursor]
+            self.state.cursor += 1
+            if (self.state.cursor - 1) % self.dp_world == self.dp_rank:
+                s = self.samples()[i]
+                self.state.num_samples[s.source] = self.state.num_samples.get(s.source, 0) + 1
+                self.state.num_tokens[s.source] = self.state.num_tokens.get(s.source, 0) + len(s.input_ids)
+                return s
+
+    # batches ---------------------------------------------------------------
+    def next_micro_batch(self) -> PackedBatch:
+        c = self.cfg
+        S = c.seq_len
+        mode = getattr(c, "pack_function", "pad")
+        seqs, masks = [], []
+        if mode == "cat":
+            budget = S * c.micro_batch_size
+            used = 0
+            while used < budget:
+                s = self._pending if getattr(self, "_pending", None) else self._next_sample()
+                self._pending = None
+                take = min(len(s.input_ids), budget - used)
+                if take < len(s.input_ids) and used > 0:
+                    self._pending = s  # start the next window with it
+                    break
+                seqs.append(torch.tensor(s.input_ids[:take]))
+                masks.append(torch.tensor(s.loss_mask[:take], dtype=torch.float32))
+                used += take
+        else:
+            for _ in range(c.micro_batch_size):
+                s = self._next_sample()
+                seqs.append(torch.tensor(s.input_ids[:S]))
+                masks.append(torch.tensor(s.loss_mask[:S], dtype=torch.float32))
+        return pack(seqs, masks)
+
+    def state_dict(self) -> dict[str, Any]:
+        return {"epoch": self.state.epoch, "cursor": self.state.cursor, "num_samples": dict(self.state.num_samples),
+                "num_tokens": dict(self.state.num_tokens)}
+
+    def load_state_dict(self, sd: dict[str, Any]) -> None:
+        self.state = SFTDataState(int(sd["epoch"]), int(sd["cursor"]), dict(sd.get("num_samples", {})),
+                                  dict(sd.get("num_tokens", {})))
+
+
+def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor]) -> PackedBatch:
+    """Concatenate sequences; target of position t is token t+1 of the same
+    sequence (last position of each sequence is ignored)."""
+    ids = torch.cat(seqs).long()
+    lens = [len(s) for s in seqs]
+    cu = torch.zeros(len(seqs) + 1, dtype=torch.int32)
+    cu[1:] = torch.tensor(lens, dtype=torch.int32).cumsum(0)
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens])
+    tg, mk = [], []
+    for s, m in zip(seqs, masks):
+        t = torch.full_like(s, -100, dtype=torch.long)
+        t[:-1] = s[1:]
+        # the loss mask marks trainable *target* tokens
+        mm = torch.zeros(len(s), dtype=torch.float32)
+        mm[:-1] = m[1:].float()
+        tg.append(t)
+        mk.append(mm)
+    tgt = torch.cat(tg)
+    mask = torch.cat(mk)
+    tgt = torch.where(mask > 0, tgt, torch.full_like(tgt, -100))
+    return PackedBatch(ids, pos, cu, max(lens), tgt, mask)

@@ -1,0 +1,57 @@
+"""Tokenizers.
+
+* ``CharTokenizer`` — a dependency-free byte/character tokenizer with a tiny
+  chat template, used by the debug model and CPU tests (the reference's debug
+  character tokenizer, trainer/debug.py:26-115).
+* ``load_tokenizer`` — a Hugging Face tokenizer from a local directory
+  (``transformers.AutoTokenizer``, no network), or the char tokenizer for
+  presets / the debug model.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+from typing import Any
+
+
+class CharTokenizer:
+    """UTF-8 byte tokenizer: ids 0..2 are <pad>, <bos>, <eos>; bytes map to 3..258."""
+
+    pad_token_id = 0
+    bos_token_id = 1
+    eos_token_id = 2
+    vocab_size = 259
+    ROLE_TAGS = {"system": "<|system|>", "user": "<|user|>", "assistant": "<|assistant|>", "tool": "<|tool|>"}
+
+    def encode(self, text: str, add_special_tokens: bool = False) -> list[int]:
+        ids = [b + 3 for b in text.encode("utf-8")]
+        return ([self.bos_token_id] + ids) if add_special_tokens else ids
+
+    def decode(self, ids: list[int], skip_special_tokens: bool = True) -> str:
+        out = bytes(i - 3 for i in ids if 3 <= i < 259)
+        return out.decode("utf-8", errors="replace")
+
+    def __call__(self, text: str, add_special_tokens: bool = False, **_: Any) -> dict[str, list[int]]:
+        return {"input_ids": self.encode(text, add_special_tokens)}
+
+    def render_message(self, role: str, content: str) -> str:
+        return f"{self.ROLE_TAGS.get(role, '<|' + role + '|>')}{content}\n"
+
+    def apply_chat_template(self, messages: list[dict[str, Any]], tokenize: bool = False,
+                            add_generation_prompt: bool = False, **_: Any):
+        text = "".join(self.render_message(m["role"], str(m.get("content") or "")) for m in messages)
+        if add_generation_prompt:
+            text += self.ROLE_TAGS["assistant"]
+        return self.encode(text) if tokenize else text
+
+
+def load_tokenizer(name_or_path: str | Path, trust_remote_code: bool = False):
+    p = Path(str(name_or_path))
+    if p.is_dir() and ((p / "tokenizer.json").exists() or (p / "tokenizer_config.json").exists()):
+        from transformers import AutoTokenizer
+
+        tok = AutoTokenizer.from_pretrained(str(p), trust_remote_code=trust_remote_code, local_files_only=True)
+        if tok.pad_token_id is None:
+            tok.pad_token = tok.eos_token
+        return tok
+    return CharTokenizer()

@@ -36,7 +36,7 @@ def attention_fwd(q, k, v, cu_seqlens, max_seqlen: int, causal: bool = True, sca
         return out, None
     m = _load_ext()
     if hasattr(m, "attn_fwd"):
-        out = torch.empty_like(q)
+        out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
         lse = torch.empty(q.shape[1], q.shape[0], device=q.device, dtype=torch.float32)
         m.attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), bool(causal), float(scale), out, lse)
         return out, lse
@@ -51,9 +51,9 @@ def attention_bwd(do, q, k, v, out, lse, cu_seqlens, max_seqlen: int, causal: bo
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     m = _load_ext()
     if hasattr(m, "attn_bwd"):
-        dq = torch.empty_like(q)
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
+        dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+        dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+        dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
         m.attn_bwd(do.contiguous(), q, k, v, out, lse, cu_seqlens, int(max_seqlen), bool(causal), float(scale), dq, dk, dv)
         return dq, dk, dv
     rng = torch.zeros(2, dtype=torch.int64, device=q.device)

@@ -59,6 +59,7 @@ class ShardedAdamW:
             return self.g_shard
         return self.flat.grad
 
+    @torch.no_grad()
     def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
         flat = self.flat
         lr = self.h.lr if lr is None else lr
@@ -75,17 +76,18 @@ class ShardedAdamW:
         if self.h.max_grad_norm and self.h.max_grad_norm > 0:
             factor = min(1.0, self.h.max_grad_norm / (norm + 1e-6))
         self.step_count += 1
-        p16 = flat.compute[flat.shard_slice]
+        compute = flat.compute.detach()
+        p16 = compute[flat.shard_slice]
         ops.adamw_flat_(
             flat.master, g, flat.exp_avg, flat.exp_avg_sq, p16 if flat.compute.dtype == torch.bfloat16 else None,
             lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
             step=self.step_count, gscale_host=factor,
         )
-        if flat.compute.dtype != torch.bfloat16:
-            with torch.no_grad():
-                p16.copy_(flat.master)
+        if compute.dtype != torch.bfloat16:
+            p16.copy_(flat.master)
         if self.world > 1:
-            dist.all_gather_into_tensor(flat.compute, p16.clone() if not p16.is_contiguous() else p16, group=self.group)
+            src = p16 if compute.is_cuda else p16.clone()
+            dist.all_gather_into_tensor(compute, src, group=self.group)
         flat.zero_grad()
         return {"grad_norm": norm, "clip_factor": factor}
 
@@ -98,13 +100,14 @@ class ShardedAdamW:
             "exp_avg_sq": self.flat.exp_avg_sq,
         }
 
+    @torch.no_grad()
     def load_state_dict(self, sd: dict) -> None:
         self.step_count = int(sd["step"])
         self.flat.master.copy_(sd["master"])
         self.flat.exp_avg.copy_(sd["exp_avg"])
         self.flat.exp_avg_sq.copy_(sd["exp_avg_sq"])
-        p16 = self.flat.compute[self.flat.shard_slice]
-        with torch.no_grad():
-            p16.copy_(self.flat.master.to(p16.dtype))
+        compute = self.flat.compute.detach()
+        p16 = compute[self.flat.shard_slice]
+        p16.copy_(self.flat.master.to(p16.dtype))
         if self.world > 1:
-            dist.all_gather_into_tensor(self.flat.compute, p16.clone(), group=self.group)
+            dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)

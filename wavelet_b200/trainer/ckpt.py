@@ -1,0 +1,166 @@
+"""Checkpoints: asynchronous, sharded, resumable.
+
+Layout of ``<output_dir>/checkpoint-<step>/`` (``STABLE`` is written last, after
+every rank finished, so a crash never leaves a checkpoint that looks valid):
+
+    meta.json                       step, world size, model arch, flat layout hash
+    trainer/model.safetensors       full bf16 compute weights (rank 0)
+    trainer/optim-rank<r>.pt        fp32 master / exp_avg / exp_avg_sq shard of rank r
+    trainer/scheduler.json          optimizer step counter and LR state
+    dataloader/rank<r>.json         data cursor of rank r
+    STABLE
+
+Saving copies device state into (optionally pinned) host buffers on the
+caller's stream, then writes files on a background thread so the next
+training step overlaps the I/O (``ckpt.mode: async`` /
+``async_with_pinned_mem``).  A gloo group coordinates ranks so the NCCL
+stream is never blocked by file I/O.  Resuming on a different world size
+re-shards the optimizer state from the saved shards (the flat layout is
+identical for every world size up to padding).
+
+Parity: trainer/ckpt.py:55-436 of the reference (DCP async_save on a gloo
+group, STABLE markers, keep_last / keep_interval, skip flags).
+"""
+
+from __future__ import annotations
+
+import json
+import shutil
+import threading
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from ..utils import pathing
+
+
+def _save_safetensors(tensors: dict[str, torch.Tensor], path: Path) -> None:
+    from safetensors.torch import save_file
+
+    save_file({k: v.contiguous() for k, v in tensors.items()}, str(path))
+
+
+class CheckpointManager:
+    def __init__(self, output_dir: Path, *, mode: str = "async", keep_last: int = 2, keep_interval: int | None = None,
+                 rank: int = 0, world: int = 1):
+        self.output_dir = Path(output_dir)
+        self.mode = mode
+        self.keep_last = keep_last
+        self.keep_interval = keep_interval
+        self.rank = rank
+        self.world = world
+        self._thread: threading.Thread | None = None
+        self._error: BaseException | None = None
+        self._gloo = None
+        if world > 1 and dist.is_initialized():
+            self._gloo = dist.new_group(backend="gloo")
+        self._pinned: dict[str, torch.Tensor] = {}
+
+    # ---------------------------------------------------------------- save
+    def _host(self, name: str, t: torch.Tensor) -> torch.Tensor:
+        if t.device.type == "cpu":
+            return t.detach().clone()
+        if self.mode == "async_with_pinned_mem":
+            buf = self._pinned.get(name)
+            if buf is None or buf.shape != t.shape or buf.dtype != t.dtype:
+                buf = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                self._pinned[name] = buf
+            buf.copy_(t.detach(), non_blocking=True)
+            return buf
+        return t.detach().to("cpu")
+
+    def save(self, step: int, *, model, optimizer, data_state: dict | None, meta: dict[str, Any],
+             scheduler_state: dict | None = None, block: bool = False) -> Path:
+        self.wait()
+        d = pathing.checkpoint_dir(self.output_dir, step)
+        flat = model.flat
+        weights = None
+        if self.rank == 0:
+            weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
+        opt = {k: (self._host("o:" + k, v) if torch.is_tensor(v) else v) for k, v in optimizer.state_dict().items()}
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+
+        def work():
+            try:
+                (d / "trainer").mkdir(parents=True, exist_ok=True)
+                (d / "dataloader").mkdir(parents=True, exist_ok=True)
+                if weights is not None:
+                    _save_safetensors(weights, d / "trainer" / "model.safetensors")
+                    (d / "meta.json").write_text(json.dumps({"step": step, "world_size": self.world, **meta}, indent=2))
+                    (d / "trainer" / "scheduler.json").write_text(json.dumps(scheduler_state or {}, indent=2))
+                torch.save({**opt, "shard_rank": self.rank, "shard_world": self.world}, d / "trainer" / f"optim-rank{self.rank}.pt")
+                if data_state is not None:
+                    (d / "dataloader" / f"rank{self.rank}.json").write_text(json.dumps(data_state))
+            except BaseException as e:  # surfaced by wait()
+                self._error = e
+
+        if self.mode == "disabled" or block:
+            work()
+            self._finalize(d, step)
+        else:
+            self._thread = threading.Thread(target=lambda: (work(), self._finalize(d, step)), daemon=True)
+            self._thread.start()
+        return d
+
+    def _finalize(self, d: Path, step: int) -> None:
+        ok = torch.tensor([0 if self._error is None else 1])
+        if self._gloo is not None:
+            dist.all_reduce(ok, group=self._gloo)
+        if int(ok.item()) == 0 and self.rank == 0:
+            (d / pathing.STABLE).write_text(str(step))
+            self._cleanup()
+
+    def wait(self) -> None:
+        if self._thread is not None:
+            self._thread.join()
+            self._thread = None
+        if self._error is not None:
+            e, self._error = self._error, None
+            raise RuntimeError(f"checkpoint save failed: {e}") from e
+
+    def _cleanup(self) -> None:
+        steps = pathing.list_checkpoint_steps(self.output_dir)
+        keep = set(steps[-self.keep_last:])
+        if self.keep_interval:
+            keep |= {s for s in steps if s % self.keep_interval == 0}
+        for s in steps:
+            if s not in keep:
+                shutil.rmtree(pathing.checkpoint_dir(self.output_dir, s), ignore_errors=True)
+
+    # ---------------------------------------------------------------- load
+    def load(self, d: Path, *, model, optimizer=None, skip_optimizer=False) -> dict[str, Any]:
+        from safetensors.torch import load_file
+
+        meta = json.loads((d / "meta.json").read_text())
+        w = load_file(str(d / "trainer" / "model.safetensors"))
+        model.flat.load_state({k: v.to(model.flat.device) for k, v in w.items()})
+        if optimizer is not None and not skip_optimizer:
+            saved_world = int(meta.get("world_size", 1))
+            flat = model.flat
+            if saved_world == self.world:
+                sd = torch.load(d / "trainer" / f"optim-rank{self.rank}.pt", map_location=flat.device, weights_only=False)
+            else:
+                # re-shard: concatenate every saved shard then take ours
+                parts = [torch.load(d / "trainer" / f"optim-rank{r}.pt", map_location="cpu", weights_only=False) for r in range(saved_world)]
+                sd = {"step": parts[0]["step"]}
+                for k in ("master", "exp_avg", "exp_avg_sq"):
+                    full = torch.cat([p[k] for p in parts])
+                    full = torch.nn.functional.pad(full, (0, max(0, flat.numel - full.numel())))[: flat.numel]
+                    sd[k] = full[flat.shard_slice].to(flat.device)
+                if "momentum" in parts[0]:
+                    full = torch.cat([p["momentum"] for p in parts])
+                    full = torch.nn.functional.pad(full, (0, max(0, flat.numel - full.numel())))[: flat.numel]
+                    sd["momentum"] = full[flat.shard_slice].to(flat.device)
+            optimizer.load_state_dict(sd)
+        data_state = None
+        p = d / "dataloader" / f"rank{self.rank}.json"
+        if p.exists():
+            data_state = json.loads(p.read_text())
+        sched = {}
+        sp = d / "trainer" / "scheduler.json"
+        if sp.exists():
+            sched = json.loads(sp.read_text())
+        return {"meta": meta, "data_state": data_state, "scheduler": sched}

@@ -1,0 +1,212 @@
+"""``wavelet sft``: supervised fine-tuning.
+
+    python -m wavelet_b200 sft @ cfg.yaml [--section.key value ...]
+    torchrun --nproc-per-node N -m wavelet_b200 sft @ cfg.yaml
+
+Setup order: seed -> distributed -> model -> data -> optimizer -> run state
+(monitor, checkpoints, resume).  Each optimizer step runs
+``batch_size / (micro_batch_size * dp)`` micro-batches per rank, normalises
+the loss by the global count of trainable tokens, clips, steps the sharded
+optimizer and logs ``loss``, ``optim/grad_norm``, ``optim/lr`` and the
+``perf/*`` metrics.
+
+Parity: trainer/trainer.py:1162-1683 of the reference (SFTTrainer and main).
+"""
+
+from __future__ import annotations
+
+import gc
+import logging
+import os
+import sys
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+
+from ..configs.config import SFTConfig
+from ..models.config import resolve_arch
+from ..models.qwen import build_model
+from ..monitor import RunMonitor, setup_logger
+from ..parallel.dist import Groups, ParallelDims, destroy_distributed, init_distributed
+from ..utils import pathing
+from ..utils.config import config_to_plain, dump_yaml, load_config
+from .ckpt import CheckpointManager
+from .engine import Engine
+from .optim import FlatOptimizer, lr_at
+from .perf import PerfTracker
+
+log = logging.getLogger("wavelet")
+
+
+class SFTTrainer:
+    def __init__(self, config: SFTConfig):
+        self.config = config
+        self.step = 0
+        self.world = None
+        self.model = None
+        self.engine = None
+        self.optimizer = None
+        self.dataset = None
+        self.monitor = None
+        self.ckpt = None
+        self.perf = None
+
+    # ------------------------------------------------------------------ setup
+    def setup(self) -> "SFTTrainer":
+        c = self.config
+        torch.manual_seed(c.seed)
+        backend = c.fsdp.backend
+        self.world = init_distributed(backend, timeout_s=c.dist_timeout_seconds)
+        w = self.world
+        dims = ParallelDims(dp_replicate=c.fsdp.dp_replicate, dp_shard=c.fsdp.dp_shard, cp=c.fsdp.cp, tp=c.fsdp.tp,
+                            ep=c.fsdp.ep, world_size=w.world_size)
+        if dims.tp > 1 or dims.cp > 1:
+            raise NotImplementedError("tensor / context parallel SFT are not wired into the SFT trainer yet")
+        self.groups = Groups(dims, w.rank)
+        dp_rank, dp_world = self.groups.dp_rank, dims.dp
+        dev = w.device
+        arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
+        dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
+        self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed,
+                                 init=c.model.random_init or not _has_weights(c.model.name))
+        if not c.model.random_init and _has_weights(c.model.name):
+            from ..models.hf_io import load_hf_weights
+
+            load_hf_weights(self.model, Path(c.model.name))
+        self.optimizer = FlatOptimizer(self.model.flat, c.optim, c.max_grad_norm, self.groups.dp, dp_world)
+        self.engine = Engine(self.model, self.optimizer.adamw.h, self.groups.dp, dp_world)
+        self.engine.opt = self.optimizer  # type: ignore[assignment]
+        from ..data.sft import SFTDataset
+        from ..data.tokenizer import load_tokenizer
+
+        tok = None if c.data.source == "fake" else load_tokenizer(c.model.name)
+        self.dataset = SFTDataset(c.data, tok, dp_rank, dp_world, seed=c.seed)
+        gm = c.data.micro_batch_size * dp_world
+        if c.data.batch_size % gm:
+            raise ValueError(
+                f"SFT data.batch_size is the global optimizer batch and must be divisible by "
+                f"micro_batch_size * dp ({c.data.micro_batch_size} * {dp_world})"
+            )
+        self.accum = c.data.batch_size // gm
+        self.total_steps = c.max_steps or max(1, c.epochs * len(self.dataset.samples()) // c.data.batch_size)
+        out = Path(c.output_dir)
+        resume = None
+        if c.ckpt is not None:
+            resume = pathing.resolve_resume_dir(c.checkpoint_output_dir, c.ckpt.resume_step, c.ckpt.resume_dir)
+        if w.rank == 0:
+            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume is not None)
+            attempt = pathing.create_launch_attempt(out)
+            dump_yaml(attempt.config_dir / "sft.yaml", config_to_plain(c))
+        if w.distributed:
+            torch.distributed.barrier()
+        setup_logger("sft", out, c.log.level, c.log.json_console, c.log.json_file)
+        self.monitor = RunMonitor.from_config(out, c.monitor, checkpoint_dir=c.checkpoint_output_dir)
+        self.ckpt = None
+        if c.ckpt is not None and c.ckpt.mode != "disabled":
+            self.ckpt = CheckpointManager(c.checkpoint_output_dir, mode=c.ckpt.mode, keep_last=c.ckpt.keep_last,
+                                          keep_interval=c.ckpt.keep_interval, rank=w.rank, world=w.world_size)
+        if resume is not None:
+            mgr = self.ckpt or CheckpointManager(c.checkpoint_output_dir, mode="disabled", rank=w.rank, world=w.world_size)
+            st = mgr.load(resume, model=self.model, optimizer=self.optimizer, skip_optimizer=c.ckpt.skip_optimizer)
+            if not c.ckpt.skip_progress:
+                self.step = int(st["meta"]["step"])
+            if st["data_state"] is not None and not c.ckpt.skip_dataloader:
+                self.dataset.load_state_dict(st["data_state"])
+        self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
+        self.perf = PerfTracker(arch, w.device, lora_rank=None)
+        if c.gc is not None:
+            gc.disable()
+        return self
+
+    # ------------------------------------------------------------------ loop
+    def train_step(self) -> dict[str, Any]:
+        c = self.config
+        t0 = time.perf_counter()
+        batches = [self.dataset.next_micro_batch() for _ in range(self.accum)]
+        local = float(sum(float(b.loss_mask.sum()) for b in batches))
+        total = self.engine.global_token_count(local, self.world.device)
+        scale = 1.0 / max(total, 1.0)
+        dev = self.world.device
+        loss = torch.zeros((), device=dev)
+        tokens = 0
+        for b in batches:
+            if c.data.pin_memory and dev.type == "cuda":
+                b = b.pin_memory()
+            b = b.to(dev)
+            tokens += b.num_tokens
+            loss += self.engine.sft_micro_step(b, scale)
+        lr = lr_at(self.step, c.optim.lr, self.total_steps, c.scheduler)
+        stats = self.optimizer.step(lr)
+        if self.world.distributed:
+            torch.distributed.all_reduce(loss, group=self.groups.dp)
+        loss_v = float(loss.item())
+        if not (loss_v == loss_v) or loss_v in (float("inf"), float("-inf")):
+            raise FloatingPointError(f"non-finite SFT loss at step {self.step}")
+        self.step += 1
+        dt = time.perf_counter() - t0
+        m = {"loss": loss_v, "optim/grad_norm": stats["grad_norm"], "optim/lr": lr, "train/loss_tokens": total}
+        m.update(self.perf.step_metrics(tokens * (self.world.world_size // max(1, self.config.fsdp.tp)), dt))
+        return m
+
+    def train(self) -> int:
+        c = self.config
+        status = "failed"
+        try:
+            while self.step < self.total_steps:
+                metrics = self.train_step()
+                if self.step % c.log.log_every == 0:
+                    self.monitor.log(metrics, self.step)
+                    log.info("step %d loss %.4f grad_norm %.3f tok/s %.0f", self.step, metrics["loss"],
+                             metrics["optim/grad_norm"], metrics.get("perf/tokens_per_second", 0))
+                if self.ckpt is not None and c.ckpt.interval and self.step % c.ckpt.interval == 0:
+                    self.save_checkpoint()
+                if c.gc is not None and self.step % c.gc.interval == 0:
+                    gc.collect(1)
+            if self.ckpt is not None:
+                self.save_checkpoint(block=True)
+            status = "completed"
+            return 0
+        finally:
+            if self.ckpt is not None:
+                try:
+                    self.ckpt.wait()
+                except Exception:
+                    status = "failed"
+            self.monitor.finish(status=status, step=self.step)
+
+    def save_checkpoint(self, block: bool = False) -> None:
+        c = self.config
+        self.ckpt.save(
+            self.step, model=self.model, optimizer=self.optimizer, data_state=self.dataset.state_dict(),
+            meta={"arch": self.model.cfg.to_dict(), "numel": self.model.flat.numel},
+            scheduler_state={"step": self.step}, block=block,
+        )
+        self.monitor.log_event("checkpoint_saved", step=self.step)
+
+
+def _has_weights(name: str) -> bool:
+    p = Path(name)
+    return p.is_dir() and any(p.glob("*.safetensors"))
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    cfg = load_config(SFTConfig, argv)
+    if cfg.dry_run:
+        print(cfg.model_dump_json(indent=2))
+        return 0
+    if cfg.slurm is not None:
+        from ..deployment.slurm import launch_slurm
+
+        return launch_slurm(cfg, "sft", argv)
+    trainer = SFTTrainer(cfg).setup()
+    try:
+        return trainer.train()
+    finally:
+        destroy_distributed()
+
+
+if __name__ == "__main__":
+    sys.exit(main())
