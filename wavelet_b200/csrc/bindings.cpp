@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include "attention.h"
+#include "decode.h"
 #include "gemm.h"
 #include "kernels.h"
 
@@ -321,6 +322,67 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, 
   wb::attn_bwd(b, cur_stream());
 }
 
+void kv_append(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at::Tensor& v_cache,
+               const at::Tensor& slot) {
+  // k, v: [T, Hk, 128] views; caches [num_blocks, block_size, Hk, 128]; slot int32 [T]
+  check_bf16(k, "k");
+  check_bf16(v, "v");
+  WB_CHECK(k.stride(2) == 1 && k.stride(1) == 128 && v.stride(2) == 1 && v.stride(1) == 128, "kv_append: bad k/v layout");
+  WB_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "kv_append: caches must be contiguous");
+  WB_CHECK(slot.scalar_type() == at::kInt && slot.is_contiguous(), "kv_append: slot must be int32");
+  const c10::cuda::CUDAGuard guard(k.device());
+  wb::kv_append(k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                slot.data_ptr<int>(), k.size(0), k.size(1), k_cache.size(1), cur_stream());
+}
+
+void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      const at::Tensor& block_tables, const at::Tensor& ctx_lens, at::Tensor& out, int64_t splits,
+                      double scale) {
+  check_bf16(q, "q");
+  WB_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == 128 && q.size(2) == 128, "decode_attention: q must be [B, Hq, 128]");
+  WB_CHECK(out.dim() == 3 && out.stride(2) == 1 && out.stride(1) == 128, "decode_attention: bad out");
+  WB_CHECK(block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(), "decode_attention: block_tables int32");
+  WB_CHECK(ctx_lens.scalar_type() == at::kInt, "decode_attention: ctx_lens int32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  wb::DecodeArgs a;
+  a.q = q.data_ptr();
+  a.q_row = q.stride(0);
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.block_tables = block_tables.data_ptr<int>();
+  a.max_blocks = block_tables.size(1);
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.out_row = out.stride(0);
+  a.nseq = q.size(0);
+  a.Hq = q.size(1);
+  a.Hk = k_cache.size(2);
+  a.block_size = k_cache.size(1);
+  a.splits = std::max<int64_t>(1, splits);
+  a.scale = (float)scale;
+  at::Tensor po, pml;
+  if (a.splits > 1) {
+    po = at::empty({a.nseq, a.Hq, a.splits, 128}, q.options().dtype(at::kFloat));
+    pml = at::empty({a.nseq, a.Hq, a.splits, 2}, q.options().dtype(at::kFloat));
+    a.part_o = po.data_ptr<float>();
+    a.part_ml = pml.data_ptr<float>();
+  }
+  wb::decode_attention(a, cur_stream());
+}
+
+void sample_tokens(const at::Tensor& z, const at::Tensor& inv_tau, const c10::optional<at::Tensor>& thresh,
+                   double min_p, int64_t seed, const c10::optional<at::Tensor>& row_ids, at::Tensor& out_tok,
+                   at::Tensor& out_lp) {
+  check_bf16(z, "z");
+  WB_CHECK(z.dim() == 2 && z.stride(1) == 1, "sample_tokens: z must be [B, V] row-major");
+  check_f32(inv_tau, "inv_tau");
+  const c10::cuda::CUDAGuard guard(z.device());
+  wb::sample_tokens(z.data_ptr(), z.stride(0), z.size(0), z.size(1), inv_tau.data_ptr<float>(),
+                    thresh ? thresh->data_ptr<float>() : nullptr, (float)min_p, (uint64_t)seed,
+                    row_ids ? row_ids->data_ptr<int64_t>() : nullptr, out_tok.data_ptr<int64_t>(),
+                    out_lp.data_ptr<float>(), cur_stream());
+}
+
 int64_t read_error(int64_t device) { return wb::read_error_word((int)device); }
 void clear_error(int64_t device) { wb::clear_error_word((int)device); }
 
@@ -346,6 +408,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softmax_grad", &softmax_grad);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  m.def("kv_append", &kv_append);
+  m.def("decode_attention", &decode_attention);
+  m.def("sample_tokens", &sample_tokens);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.attr("EPI_BF16") = (int)wb::kEpiBF16;

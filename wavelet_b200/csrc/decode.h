@@ -1,0 +1,31 @@
+// Host API of the generator kernels (decode.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wb {
+
+struct DecodeArgs {
+  const void* q = nullptr;  // [nseq, Hq, 128] rows of q_row elements
+  int64_t q_row = 0;
+  const void* k_cache = nullptr;  // [num_blocks, block_size, Hk, 128]
+  const void* v_cache = nullptr;
+  const int* block_tables = nullptr;  // [nseq, max_blocks]
+  int max_blocks = 0;
+  const int* ctx_lens = nullptr;  // [nseq]
+  void* out = nullptr;            // [nseq, Hq, 128] rows of out_row elements
+  int64_t out_row = 0;
+  float* part_o = nullptr;   // [nseq, Hq, splits, 128] when splits > 1
+  float* part_ml = nullptr;  // [nseq, Hq, splits, 2]
+  int nseq = 0, Hq = 0, Hk = 0, block_size = 0, splits = 1;
+  float scale = 0.f;
+};
+
+void kv_append(const void* k, int64_t k_row, const void* v, int64_t v_row, void* k_cache, void* v_cache,
+               const int* slot, int T, int Hk, int block_size, cudaStream_t st);
+void decode_attention(const DecodeArgs& a, cudaStream_t st);
+void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv_tau, const float* thresh,
+                   float min_p, uint64_t seed, const int64_t* row_ids, int64_t* out_tok, float* out_lp,
+                   cudaStream_t st);
+
+}  // namespace wb

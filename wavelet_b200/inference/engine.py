@@ -1,0 +1,394 @@
+"""Native batched generator (replaces the reference's vLLM engine).
+
+* Paged KV cache: per layer ``k``/``v`` tensors [num_blocks, block_size, Hk,
+  128] bf16; a block manager hands out blocks, with reference counts so the
+  ``n`` samples of one prompt share the prompt's full blocks (the partial last
+  block is copied per sample).
+* Continuous batching: sequences are admitted while blocks are free, prefilled
+  as one packed batch (tcgen05 attention forward over ``cu_seqlens``), then
+  advanced together one token per decode step until they hit a stop token or
+  ``max_tokens``; finished sequences free their blocks and new ones join.
+* Decode step: embedding -> per layer (RMSNorm, QKV GEMM, QK-norm + RoPE,
+  KV append, paged decode attention, O GEMM + residual, RMSNorm, gate/up
+  GEMM, SwiGLU, down GEMM + residual) -> final norm -> LM head GEMM -> fused
+  sampling (Gumbel-max at temperature, processed log-prob of the sampled
+  token, optional top-k / min-p / top-p support).
+* Outputs match what the trainer needs: exact token ids, the processed
+  log-probs at the sampling temperature, and the sampling support set when
+  top-k / top-p / min-p truncate it (vLLM ``processed_logprobs`` and
+  ``return_sampling_mask`` in the reference, inference/engine.py:775-944).
+
+The engine shares the model's flat parameter store, so an in-process trainer
+updates the policy in place (zero-copy policy transfer).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from .. import ops
+from ..models.qwen import CausalLM
+from ..ops import reference as ref
+from ..ops.attention import attention_fwd
+
+
+@dataclass
+class SamplingParams:
+    temperature: float = 1.0
+    top_p: float = 1.0
+    top_k: int = -1
+    min_p: float = 0.0
+    max_tokens: int = 256
+    min_tokens: int = 0
+    n: int = 1
+    stop_token_ids: list[int] = field(default_factory=list)
+    seed: int | None = None
+    return_sampling_mask: bool = False
+
+    @property
+    def truncated(self) -> bool:
+        return self.top_p < 1.0 or self.top_k > 0 or self.min_p > 0.0
+
+
+@dataclass
+class Completion:
+    prompt_index: int
+    sample_index: int
+    prompt_ids: list[int]
+    token_ids: list[int]
+    logprobs: list[float]
+    finish_reason: str
+    sampling_mask: list[list[int]] | None = None
+
+
+@dataclass
+class _Seq:
+    pid: int
+    sidx: int
+    prompt: list[int]
+    params: SamplingParams
+    blocks: list[int]
+    length: int  # tokens in cache
+    out: list[int] = field(default_factory=list)
+    lps: list[float] = field(default_factory=list)
+    masks: list[list[int]] | None = None
+    done: str | None = None
+    row_id: int = 0
+
+
+class BlockManager:
+    def __init__(self, num_blocks: int):
+        self.free = list(range(num_blocks - 1, -1, -1))
+        self.ref = [0] * num_blocks
+
+    def alloc(self) -> int:
+        if not self.free:
+            raise MemoryError("KV cache out of blocks")
+        b = self.free.pop()
+        self.ref[b] = 1
+        return b
+
+    def share(self, b: int) -> int:
+        self.ref[b] += 1
+        return b
+
+    def release(self, blocks: list[int]) -> None:
+        for b in blocks:
+            self.ref[b] -= 1
+            if self.ref[b] == 0:
+                self.free.append(b)
+
+    @property
+    def num_free(self) -> int:
+        return len(self.free)
+
+
+class Generator:
+    def __init__(self, model: CausalLM, *, max_num_seqs: int = 512, max_model_len: int = 4096,
+                 kv_cache_bytes: int | None = None, gpu_memory_utilization: float | None = None,
+                 block_size: int = 64, decode_splits: int | None = None):
+        self.m = model
+        cfg = model.cfg
+        self.cfg = cfg
+        self.dev = model.device
+        self.block_size = block_size
+        self.max_num_seqs = max_num_seqs
+        self.max_model_len = max_model_len
+        per_block = 2 * cfg.num_layers * block_size * cfg.num_kv_heads * cfg.head_dim * 2
+        if kv_cache_bytes is None:
+            if self.dev.type == "cuda":
+                free, total = torch.cuda.mem_get_info(self.dev)
+                frac = gpu_memory_utilization if gpu_memory_utilization is not None else 0.35
+                kv_cache_bytes = int(min(free * 0.9, total * frac))
+            else:
+                kv_cache_bytes = 64 * per_block
+        self.num_blocks = max(4, kv_cache_bytes // per_block)
+        shape = (self.num_blocks, block_size, cfg.num_kv_heads, cfg.head_dim)
+        dt = model.flat.compute_dtype
+        self.k_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
+        self.v_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
+        self.bm = BlockManager(self.num_blocks)
+        self.max_blocks_per_seq = (max_model_len + block_size - 1) // block_size
+        self.decode_splits = decode_splits
+        self.stats: dict[str, float] = {}
+        self._moe = [layer.moe for layer in model.layers]
+
+    # ------------------------------------------------------------ utilities
+    def kv_usage(self) -> float:
+        return 1.0 - self.bm.num_free / self.num_blocks
+
+    def _slots(self, seqs: list[_Seq], positions: list[list[int]]) -> torch.Tensor:
+        out = []
+        for s, ps in zip(seqs, positions):
+            for p in ps:
+                out.append(s.blocks[p // self.block_size] * self.block_size + p % self.block_size)
+        return torch.tensor(out, dtype=torch.int32, device=self.dev)
+
+    def _ensure_blocks(self, s: _Seq, upto: int) -> None:
+        while len(s.blocks) * self.block_size < upto:
+            s.blocks.append(self.bm.alloc())
+
+    # -------------------------------------------------------------- forward
+    def _layers_forward(self, x, pos, slots, attn_fn):
+        cfg = self.cfg
+        nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        T = x.shape[0]
+        for li, layer in enumerate(self.m.layers):
+            P = layer.P
+            h, _, _ = ops.rmsnorm_fwd(x, P["in_norm"], cfg.rms_eps)
+            qkv = ops.gemm(h, P["qkv_w"], bias=P.get("qkv_b"))
+            ops.qk_norm_rope_(qkv, nq, nk, pos, self.m.inv_freq, P.get("q_norm"), P.get("k_norm"), cfg.rms_eps)
+            q = qkv[:, : nq * hd].view(T, nq, hd)
+            k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
+            v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
+            if x.is_cuda:
+                ops.ext().kv_append(k, v, self.k_cache[li], self.v_cache[li], slots)
+            else:
+                sl = slots.long()
+                self.k_cache[li].view(-1, nk, hd)[sl] = k
+                self.v_cache[li].view(-1, nk, hd)[sl] = v
+            att = attn_fn(li, q, k, v)
+            x = ops.gemm(att.reshape(T, nq * hd), P["o_w"], res=x)
+            if layer.moe is not None:
+                h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
+                x = layer.moe.infer(h2, x, P)
+            else:
+                h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
+                a = ops.swiglu_fwd(ops.gemm(h2, P["gu_w"]))
+                x = ops.gemm(a, P["down_w"], res=x)
+        hf, _, _ = ops.rmsnorm_fwd(x, self.m.weight("norm"), cfg.rms_eps)
+        return hf
+
+    @torch.no_grad()
+    def _prefill(self, seqs: list[_Seq]) -> torch.Tensor:
+        """Packed prefill of the prompts; returns final hidden of each last prompt token."""
+        ids = torch.tensor([t for s in seqs for t in s.prompt], device=self.dev, dtype=torch.long)
+        lens = [len(s.prompt) for s in seqs]
+        cu = torch.zeros(len(seqs) + 1, dtype=torch.int32)
+        cu[1:] = torch.tensor(lens).cumsum(0)
+        pos = torch.cat([torch.arange(L, dtype=torch.int32) for L in lens]).to(self.dev)
+        slots = self._slots(seqs, [list(range(L)) for L in lens])
+        cu_d = cu.to(self.dev)
+        maxlen = max(lens)
+        x = ops.embedding_fwd(self.m.weight("embed"), ids)
+
+        def attn(li, q, k, v):
+            o, _ = attention_fwd(q, k, v, cu_d, maxlen, True)
+            return o
+
+        hf = self._layers_forward(x, pos, slots, attn)
+        last = (cu[1:] - 1).to(self.dev).long()
+        return hf[last]
+
+    @torch.no_grad()
+    def _decode(self, seqs: list[_Seq]) -> torch.Tensor:
+        B = len(seqs)
+        ids = torch.tensor([s.out[-1] if s.out else s.prompt[-1] for s in seqs], device=self.dev, dtype=torch.long)
+        pos_l = [s.length for s in seqs]
+        for s in seqs:
+            self._ensure_blocks(s, s.length + 1)
+        slots = self._slots(seqs, [[p] for p in pos_l])
+        pos = torch.tensor(pos_l, dtype=torch.int32, device=self.dev)
+        ctx = torch.tensor([p + 1 for p in pos_l], dtype=torch.int32, device=self.dev)
+        bt = torch.zeros(B, self.max_blocks_per_seq, dtype=torch.int32)
+        for i, s in enumerate(seqs):
+            bt[i, : len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
+        bt = bt.to(self.dev)
+        max_ctx = max(pos_l) + 1
+        splits = self.decode_splits or max(1, min(16, (max_ctx // self.block_size) // 4))
+        x = ops.embedding_fwd(self.m.weight("embed"), ids)
+        scale = 1.0 / math.sqrt(self.cfg.head_dim)
+
+        def attn(li, q, k, v):
+            if not q.is_cuda:
+                return self._decode_attn_ref(li, q, bt, ctx, scale)
+            out = torch.empty(q.shape, device=self.dev, dtype=q.dtype)
+            ops.ext().decode_attention(q, self.k_cache[li], self.v_cache[li], bt, ctx, out, splits, scale)
+            return out
+
+        return self._layers_forward(x, pos, slots, attn)
+
+    def _decode_attn_ref(self, li, q, bt, ctx, scale):
+        """Dense attention over the gathered paged KV (CPU path and oracle)."""
+        B, Hq, D = q.shape
+        Hk = self.cfg.num_kv_heads
+        out = torch.empty_like(q)
+        for i in range(B):
+            L = int(ctx[i])
+            nb = (L + self.block_size - 1) // self.block_size
+            blocks = bt[i, :nb].long()
+            kk = self.k_cache[li][blocks].reshape(-1, Hk, D)[:L].float()
+            vv = self.v_cache[li][blocks].reshape(-1, Hk, D)[:L].float()
+            kk = kk.repeat_interleave(Hq // Hk, 1)
+            vv = vv.repeat_interleave(Hq // Hk, 1)
+            sc = torch.einsum("hd,lhd->hl", q[i].float(), kk) * scale
+            out[i] = torch.einsum("hl,lhd->hd", sc.softmax(-1), vv).to(q.dtype)
+        return out
+
+    def _sample(self, hf: torch.Tensor, seqs: list[_Seq], step_seed: int):
+        z = self.m.logits(hf)  # [B, V] bf16
+        B = z.shape[0]
+        inv_tau = torch.tensor([(1.0 / s.params.temperature) if s.params.temperature > 0 else 0.0 for s in seqs],
+                               device=self.dev, dtype=torch.float32)
+        thresh = None
+        need_k = [s.params.top_k for s in seqs if s.params.top_k > 0]
+        if need_k:
+            kmax = max(need_k)
+            top = torch.topk(z.float(), kmax, dim=-1).values
+            th = torch.full((B,), float("-inf"), device=self.dev)
+            for i, s in enumerate(seqs):
+                if s.params.top_k > 0:
+                    th[i] = top[i, s.params.top_k - 1]
+            thresh = th
+        top_p_rows = [i for i, s in enumerate(seqs) if s.params.top_p < 1.0]
+        if top_p_rows:
+            # nucleus: threshold = smallest logit inside the top-p mass (sorted once per row)
+            zz = z[top_p_rows].float() * inv_tau[top_p_rows, None].clamp_min(1e-6)
+            srt, _ = torch.sort(zz, dim=-1, descending=True)
+            pr = torch.softmax(srt, -1).cumsum(-1)
+            th_p = torch.full((B,), float("-inf"), device=self.dev)
+            for j, i in enumerate(top_p_rows):
+                k = int((pr[j] < seqs[i].params.top_p).sum().item()) + 1
+                th_p[i] = srt[j, min(k, srt.shape[1]) - 1] / max(1e-6, float(inv_tau[i]))
+            thresh = th_p if thresh is None else torch.maximum(thresh, th_p)
+        min_p = max((s.params.min_p for s in seqs), default=0.0)
+        tok = torch.empty(B, dtype=torch.long, device=self.dev)
+        lp = torch.empty(B, dtype=torch.float32, device=self.dev)
+        if z.is_cuda:
+            row_ids = torch.tensor([s.row_id for s in seqs], dtype=torch.long, device=self.dev)
+            ops.ext().sample_tokens(z, inv_tau, thresh, float(min_p), int(step_seed), row_ids, tok, lp)
+        else:
+            zt = z.float() * inv_tau[:, None]
+            if thresh is not None:
+                zt = zt.masked_fill(z.float() < thresh[:, None], float("-inf"))
+            g = torch.Generator().manual_seed(int(step_seed))
+            probs = torch.softmax(zt, -1)
+            tok = torch.multinomial(probs, 1, generator=g)[:, 0]
+            lp = torch.log_softmax(zt, -1).gather(1, tok[:, None])[:, 0]
+        masks = None
+        if any(s.params.truncated and s.params.return_sampling_mask for s in seqs):
+            keep = torch.ones_like(z, dtype=torch.bool)
+            if thresh is not None:
+                keep &= z.float() >= thresh[:, None]
+            if min_p > 0:
+                zt = z.float() * inv_tau[:, None]
+                keep &= zt >= (zt.max(-1, keepdim=True).values + math.log(min_p))
+            masks = [keep[i].nonzero().flatten().tolist() if seqs[i].params.return_sampling_mask else None for i in range(B)]
+        return tok, lp, masks
+
+    # -------------------------------------------------------------- driver
+    def generate(self, prompts: list[list[int]], params: SamplingParams) -> list[Completion]:
+        """Generate ``params.n`` completions for every prompt."""
+        t0 = time.perf_counter()
+        base_seed = params.seed if params.seed is not None else int(time.time_ns() & 0x7FFFFFFF)
+        pending: list[tuple[int, list[int]]] = list(enumerate(prompts))
+        active: list[_Seq] = []
+        finished: list[_Seq] = []
+        gen_tokens = 0
+        step = 0
+        row_counter = 0
+        while pending or active:
+            # admit whole prompt groups while capacity allows
+            admit: list[_Seq] = []
+            while pending and len(active) + len(admit) + params.n <= self.max_num_seqs:
+                pid, pr = pending[0]
+                need = (len(pr) + params.max_tokens + self.block_size - 1) // self.block_size
+                if need * params.n > self.bm.num_free and (active or admit):
+                    break
+                pending.pop(0)
+                if len(pr) + params.max_tokens > self.max_model_len:
+                    raise ValueError(f"prompt {pid} of {len(pr)} tokens + max_tokens exceeds max_model_len={self.max_model_len}")
+                first = _Seq(pid, 0, list(pr), params, [], 0, row_id=row_counter)
+                row_counter += 1
+                self._ensure_blocks(first, len(pr))
+                admit.append(first)
+            if admit:
+                hf = self._prefill(admit)
+                for s in admit:
+                    s.length = len(s.prompt)
+                groups = []
+                for s in admit:
+                    grp = [s]
+                    full = len(s.prompt) // self.block_size
+                    for j in range(1, params.n):
+                        c = _Seq(s.pid, j, s.prompt, params, [self.bm.share(b) for b in s.blocks[:full]], s.length,
+                                 row_id=row_counter)
+                        row_counter += 1
+                        if full < len(s.blocks):  # copy the partial block
+                            nb = self.bm.alloc()
+                            for li in range(self.cfg.num_layers):
+                                self.k_cache[li][nb].copy_(self.k_cache[li][s.blocks[full]])
+                                self.v_cache[li][nb].copy_(self.v_cache[li][s.blocks[full]])
+                            c.blocks.append(nb)
+                        grp.append(c)
+                    groups.append(grp)
+                hf_rep = torch.cat([hf[i : i + 1].expand(len(g), -1) for i, g in enumerate(groups)])
+                new = [c for g in groups for c in g]
+                tok, lp, masks = self._sample(hf_rep, new, base_seed * 1000003 + step)
+                self._append(new, tok, lp, masks)
+                active += new
+                gen_tokens += len(new)
+            elif active:
+                hf = self._decode(active)
+                for s in active:
+                    s.length += 1
+                tok, lp, masks = self._sample(hf, active, base_seed * 1000003 + step)
+                self._append(active, tok, lp, masks)
+                gen_tokens += len(active)
+            step += 1
+            still = []
+            for s in active:
+                if s.done:
+                    self.bm.release(s.blocks)
+                    s.blocks = []
+                    finished.append(s)
+                else:
+                    still.append(s)
+            active = still
+        dt = time.perf_counter() - t0
+        self.stats = {"generated_tokens": float(gen_tokens), "seconds": dt, "tokens_per_second": gen_tokens / max(dt, 1e-9),
+                      "decode_steps": float(step)}
+        finished.sort(key=lambda s: (s.pid, s.sidx))
+        return [Completion(s.pid, s.sidx, s.prompt, s.out, s.lps, s.done or "length", s.masks) for s in finished]
+
+    def _append(self, seqs: list[_Seq], tok: torch.Tensor, lp: torch.Tensor, masks) -> None:
+        tl = tok.tolist()
+        ll = lp.tolist()
+        for i, s in enumerate(seqs):
+            t = int(tl[i])
+            s.out.append(t)
+            s.lps.append(float(ll[i]))
+            if masks is not None and masks[i] is not None:
+                if s.masks is None:
+                    s.masks = []
+                s.masks.append(masks[i])
+            n = len(s.out)
+            if n >= s.params.max_tokens:
+                s.done = "length"
+            elif n >= s.params.min_tokens and t in s.params.stop_token_ids:
+                s.done = "stop"

@@ -41,7 +41,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     M = a.shape[1] if a_mn else a.shape[0]
     N = b.shape[1] if b_mn else b.shape[0]
     if out is None:
-        dtype = torch.bfloat16 if epi == EPI_BF16 else torch.float32
+        if epi == EPI_BF16:
+            dtype = torch.bfloat16 if a.is_cuda else a.dtype
+        else:
+            dtype = torch.float32
         out = torch.empty(M, N, device=a.device, dtype=dtype)
     if not a.is_cuda:
         A = a.t() if a_mn else a
@@ -172,7 +175,8 @@ def qk_norm_rope_(qkv, n_q, n_k, pos, inv_freq, q_w=None, k_w=None, eps=1e-6):
     """In place on the q and k heads of a packed [T, (n_q+2 n_k) * 128] qkv row."""
     if not qkv.is_cuda:
         T = qkv.shape[0]
-        heads = qkv[:, : (n_q + n_k) * 128].view(T, n_q + n_k, 128)
+        hd = 2 * inv_freq.numel()
+        heads = qkv[:, : (n_q + n_k) * hd].view(T, n_q + n_k, hd)
         x = heads
         if q_w is not None:
             q = ref.rmsnorm(x[:, :n_q], q_w, eps)

@@ -1,0 +1,253 @@
+"""RL losses on the packed token layout.
+
+Every tensor is 1-D over the packed tokens of a micro-batch ([T]); ``seg``
+gives each token's sequence index (from ``cu_seqlens``).  The reference
+loops over sequence spans in Python (trainer/losses.py:323-591); here every
+reduction is a vectorised segment sum, with identical semantics:
+
+* per-token component losses (``dppo``, ``ipo``, ``icepop``, ``custom`` RL
+  loss; ``ce``; ``ref_kl``) from trainer / inference / teacher log-probs and
+  advantages (trainer/losses.py:100-272);
+* token normalisation (sum / global token count) or sequence normalisation
+  (each sequence's mean, summed, / global sequence count) for the RL part;
+  CE and ref-KL are token-normalised;
+* metrics are per-sequence masked means averaged over sequences, plus
+  mean / median / std / min / max across sequences.
+"""
+
+from __future__ import annotations
+
+import importlib
+from dataclasses import dataclass, field
+from typing import Callable
+
+import torch
+from torch import Tensor
+
+
+@dataclass
+class LossInputs:
+    trainer_logprobs: Tensor
+    inference_logprobs: Tensor
+    teacher_logprobs: Tensor | None
+    advantages: Tensor
+    loss_mask: Tensor  # bool
+    loss_weights: Tensor | None = None
+
+
+@dataclass
+class LossOutput:
+    loss: Tensor  # per-token loss vector [T] (summed by compute_loss)
+    metrics: dict[str, tuple[Tensor, Tensor]] = field(default_factory=dict)  # name -> (values, mask)
+
+
+def _trust_region(inp: LossInputs, cfg, invalid, masked_high, masked_low, teacher_logprobs) -> LossOutput:
+    lp, adv, mask = inp.trainer_logprobs, inp.advantages, inp.loss_mask
+    keep = mask & ~invalid
+    log_ratio = lp - inp.inference_logprobs
+    ratio = torch.exp(torch.where(keep, log_ratio, torch.zeros_like(log_ratio)))
+    with torch.no_grad():
+        mismatch = torch.exp(log_ratio) - log_ratio - 1
+    sadv = cfg.adv_tau * adv
+    tkl = None
+    if teacher_logprobs is not None:
+        tkl = teacher_logprobs - lp
+        sadv = sadv + cfg.teacher_tau * tkl.detach()
+    pg = torch.where(keep, sadv, torch.zeros_like(sadv)) * ratio
+    kl = torch.where(mask, log_ratio, torch.zeros_like(log_ratio)).square()
+    per = -pg + cfg.kl_tau * kl
+    if inp.loss_weights is not None:
+        per = per * inp.loss_weights
+    per = torch.where(mask, per, torch.zeros_like(per))
+    m = {
+        "mismatch_kl": (mismatch, mask),
+        "masked_mismatch_kl": (mismatch, mask & invalid),
+        "unmasked_mismatch_kl": (mismatch, keep),
+        "is_masked": (invalid.float(), mask),
+        "is_masked_low": (masked_low.float(), mask),
+        "is_masked_high": (masked_high.float(), mask),
+        "policy_loss": (-pg.detach(), mask),
+        "kl_loss": (kl.detach(), mask),
+        "advantage_mean": (adv, mask),
+    }
+    if tkl is not None:
+        m["teacher_kl"] = (tkl.detach(), mask)
+    return LossOutput(per, m)
+
+
+def dppo_loss(inp: LossInputs, cfg) -> LossOutput:
+    """DPPO: mask tokens whose probability moved past the advantage-signed band."""
+    d = torch.exp(inp.trainer_logprobs) - torch.exp(inp.inference_logprobs)
+    hi = d > cfg.dppo_mask_high
+    lo = d < -cfg.dppo_mask_low
+    pos = inp.advantages > 0
+    return _trust_region(inp, cfg, torch.where(pos, hi, lo), pos & hi, (inp.advantages < 0) & lo, inp.teacher_logprobs)
+
+
+def ipo_loss(inp: LossInputs, cfg) -> LossOutput:
+    """IPO: symmetric probability trust region of width ipo_epsilon."""
+    d = torch.exp(inp.trainer_logprobs) - torch.exp(inp.inference_logprobs)
+    return _trust_region(inp, cfg, d.abs() > cfg.ipo_epsilon, d > cfg.ipo_epsilon, d < -cfg.ipo_epsilon, None)
+
+
+def icepop_loss(inp: LossInputs, cfg) -> LossOutput:
+    """IcePop: importance-ratio PG, tokens outside [ratio_low, ratio_high] dropped."""
+    log_ratio = inp.trainer_logprobs - inp.inference_logprobs
+    lo = torch.log(torch.tensor(cfg.ratio_low, device=log_ratio.device))
+    hi = torch.log(torch.tensor(cfg.ratio_high, device=log_ratio.device))
+    rej = (log_ratio.detach() < lo) | (log_ratio.detach() > hi)
+    keep = inp.loss_mask & ~rej
+    ratio = torch.exp(torch.where(keep, log_ratio, torch.zeros_like(log_ratio)))
+    per = -keep.to(inp.advantages.dtype) * cfg.adv_tau * inp.advantages * ratio
+    if inp.loss_weights is not None:
+        per = per * inp.loss_weights
+    mismatch = (torch.exp(log_ratio) - log_ratio - 1).detach()
+    return LossOutput(per, {
+        "masked_mismatch_kl": (mismatch, inp.loss_mask & rej),
+        "unmasked_mismatch_kl": (mismatch, keep),
+        "is_masked": (rej.float(), inp.loss_mask),
+    })
+
+
+def ce_loss(inp: LossInputs) -> LossOutput:
+    per = -inp.trainer_logprobs
+    if inp.loss_weights is not None:
+        per = per * inp.loss_weights
+    per = torch.where(inp.loss_mask, per, torch.zeros_like(per))
+    return LossOutput(per, {"ce/nll": (-inp.trainer_logprobs.detach(), inp.loss_mask)})
+
+
+def ref_kl_loss(inp: LossInputs) -> LossOutput:
+    """Reverse-KL to a teacher with a one-sided probability trust region."""
+    if inp.teacher_logprobs is None:
+        raise ValueError("ref_kl loss requires teacher_logprobs for every weighted token.")
+    log_ratio = inp.trainer_logprobs - inp.inference_logprobs
+    with torch.no_grad():
+        mismatch = torch.exp(log_ratio) - log_ratio - 1
+    delta = torch.exp(inp.trainer_logprobs) - torch.exp(inp.inference_logprobs)
+    invalid = delta < -0.2
+    keep = inp.loss_mask & ~invalid
+    ratio = torch.exp(torch.where(keep, log_ratio, torch.zeros_like(log_ratio)))
+    tkl = inp.teacher_logprobs - inp.trainer_logprobs
+    pol = -(torch.where(keep, tkl.detach(), torch.zeros_like(tkl)) * ratio)
+    reg = torch.where(inp.loss_mask, log_ratio, torch.zeros_like(log_ratio)).square()
+    per = pol + 1e-3 * reg
+    if inp.loss_weights is not None:
+        per = per * inp.loss_weights
+    per = torch.where(inp.loss_mask, per, torch.zeros_like(per))
+    return LossOutput(per, {
+        "ref_kl/masked_mismatch_kl": (mismatch, inp.loss_mask & invalid),
+        "ref_kl/unmasked_mismatch_kl": (mismatch, keep),
+        "ref_kl/is_masked": (invalid.float(), inp.loss_mask),
+        "ref_kl": (tkl.detach(), inp.loss_mask),
+    })
+
+
+LossFn = Callable[[LossInputs], LossOutput]
+
+
+def setup_rl_loss_fn(cfg) -> LossFn:
+    if cfg.type == "custom":
+        mod, _, attr = cfg.import_path.rpartition(".")
+        if not mod:
+            raise ValueError("Custom loss import_path must include a module and attribute name.")
+        fn = getattr(importlib.import_module(mod), attr)
+        if not callable(fn):
+            raise TypeError(f"Custom loss object {cfg.import_path!r} is not callable.")
+        kwargs = dict(cfg.kwargs)
+
+        def custom(inp: LossInputs) -> LossOutput:
+            out = fn(inp, **kwargs)
+            if not isinstance(out, LossOutput):
+                raise TypeError("Custom RL loss must return LossOutput.")
+            return out
+
+        return custom
+    return {"ipo": lambda i: ipo_loss(i, cfg), "icepop": lambda i: icepop_loss(i, cfg)}.get(
+        cfg.type, lambda i: dppo_loss(i, cfg))
+
+
+# ------------------------------------------------------------- segmentation
+def segment_ids(cu_seqlens: Tensor, T: int) -> Tensor:
+    lens = (cu_seqlens[1:] - cu_seqlens[:-1]).long()
+    return torch.repeat_interleave(torch.arange(len(lens), device=cu_seqlens.device), lens, output_size=T)
+
+
+def seg_sum(x: Tensor, seg: Tensor, n: int) -> Tensor:
+    return torch.zeros(n, device=x.device, dtype=x.dtype).index_add_(0, seg, x)
+
+
+def _seq_means(values: Tensor, mask: Tensor, seg: Tensor, n: int, active: Tensor) -> Tensor:
+    """Per-sequence masked means, only for sequences in ``active``."""
+    num = seg_sum(torch.where(mask, values.float(), torch.zeros_like(values, dtype=torch.float32)), seg, n)
+    den = seg_sum(mask.float(), seg, n).clamp_min(1.0)
+    return (num / den)[active]
+
+
+def component_unit_counts(loss_mask: Tensor, seg: Tensor, n: int, rl_weights=None, ce_weights=None,
+                          ref_kl_weights=None, rl_normalization="token") -> dict[str, float]:
+    rl_mask = loss_mask if rl_weights is None else loss_mask & (rl_weights != 0)
+    if rl_normalization == "sequence":
+        rl = float((seg_sum(rl_mask.float(), seg, n) > 0).sum())
+    else:
+        rl = float(rl_mask.sum())
+    ce = float((loss_mask & (ce_weights != 0)).sum()) if ce_weights is not None else 0.0
+    rk = float((loss_mask & (ref_kl_weights != 0)).sum()) if ref_kl_weights is not None else 0.0
+    return {"rl": rl, "ce": ce, "ref_kl": rk}
+
+
+def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_logprobs: Tensor | None,
+                 advantages: Tensor, loss_mask: Tensor, cfg, *, cu_seqlens: Tensor,
+                 rl_weights: Tensor | None = None, ce_weights: Tensor | None = None,
+                 ref_kl_weights: Tensor | None = None, component_scales: dict[str, float] | None = None,
+                 rl_loss_fn: LossFn | None = None) -> tuple[Tensor, dict[str, float]]:
+    """Scalar loss (already divided by the component scales) and metrics.
+
+    ``component_scales`` are the global normalisers (token / sequence counts
+    summed over data-parallel ranks and micro-batches); when absent the local
+    counts are used (trainer/losses.py:520-591).
+    """
+    T = trainer_logprobs.shape[0]
+    seg = segment_ids(cu_seqlens, T)
+    n = cu_seqlens.numel() - 1
+    loss_mask = loss_mask.bool()
+    fn = rl_loss_fn or setup_rl_loss_fn(cfg)
+    counts = component_unit_counts(loss_mask, seg, n, rl_weights, ce_weights, ref_kl_weights, cfg.normalization)
+    scales = {k: max(float(v), 1.0) for k, v in counts.items()}
+    scales.update({k: max(float(v), 1.0) for k, v in (component_scales or {}).items()})
+    total = trainer_logprobs.sum() * 0.0
+    metrics_in: dict[str, tuple[Tensor, Tensor]] = {}
+
+    rl_mask = loss_mask if rl_weights is None else loss_mask & (rl_weights != 0)
+    if bool(rl_mask.any()):
+        out = fn(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, rl_mask, rl_weights))
+        per = out.loss
+        if cfg.normalization == "sequence":
+            per_seq = seg_sum(per, seg, n)
+            cnt = seg_sum(rl_mask.float(), seg, n).clamp_min(1.0)
+            total = total + (per_seq / cnt).sum() / scales["rl"]
+        else:
+            total = total + per.sum() / scales["rl"]
+        metrics_in.update(out.metrics)
+    for name, w, f in (("ce", ce_weights, ce_loss), ("ref_kl", ref_kl_weights, ref_kl_loss)):
+        if w is None:
+            continue
+        cm = loss_mask & (w != 0)
+        if bool(cm.any()):
+            out = f(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, cm, w))
+            total = total + out.loss.sum() / scales[name]
+            metrics_in.update(out.metrics)
+
+    metrics: dict[str, float] = {}
+    active = seg_sum(loss_mask.float(), seg, n) > 0
+    for k, (vals, m) in metrics_in.items():
+        per_seq = _seq_means(vals.detach(), m, seg, n, active)
+        if per_seq.numel() == 0:
+            continue
+        metrics[k] = float(per_seq.mean())
+        metrics[f"{k}/mean"] = float(per_seq.mean())
+        metrics[f"{k}/median"] = float(per_seq.median())
+        metrics[f"{k}/std"] = float(per_seq.std(unbiased=False)) if per_seq.numel() > 1 else 0.0
+        metrics[f"{k}/min"] = float(per_seq.min())
+        metrics[f"{k}/max"] = float(per_seq.max())
+    return total, metrics
