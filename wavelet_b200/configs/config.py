@@ -534,6 +534,8 @@ class RLDataConfig(TrainingDataConfig):
     ce_weight_column: str = "ce_weight"
     ref_kl_weight_column: str = "ref_kl_weight"
     metadata_column: str = "metadata"
+    # Native-only: prompt length of the synthetic reverse-text task (data.source: fake)
+    fake_prompt_len: int = Field(default=256, ge=1)
 
     @model_validator(mode="before")
     @classmethod

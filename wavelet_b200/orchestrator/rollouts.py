@@ -1,0 +1,163 @@
+"""Rollout materialisation: prompts -> generations -> rewards -> advantages -> queue.
+
+``RLOrchestrator.publish(step)`` (orchestrator/rollouts.py:43-525 of the
+reference) selects the step's prompts, asks the inference engine for
+``rollouts_per_example`` completions each (exact token ids + processed
+log-probs + optional sampling masks), scores rewards, assigns advantages with
+the configured algorithm, drops zero-advantage groups (optionally refilling
+them up to ``zero_advantage_max_retries``), and publishes the batch to the
+filesystem queue as ``RLExample`` training records.
+"""
+
+from __future__ import annotations
+
+import random
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable, Iterator
+
+import torch
+
+from ..data.rl import RLExample, example_to_payload
+from ..transport.queue import FileSystemRolloutSender
+from .algorithms import algorithm_epsilon, algorithm_scope, build_algorithm, score_records
+from .reward import RLRewardScorer
+
+
+@dataclass
+class PromptRecord:
+    prompt_ids: list[int]
+    prompt: list[dict[str, str]] = field(default_factory=list)
+    target_completion: list[dict[str, str]] | None = None
+    metadata: dict[str, Any] = field(default_factory=dict)
+    example_id: str = ""
+
+
+class SyntheticReversePrompts:
+    """The GRPO benchmark's data: uniform random prompts of ``prompt_len``
+    tokens; the verifiable target is the reversed prompt."""
+
+    def __init__(self, vocab: int, prompt_len: int, seed: int = 0, low: int = 3):
+        self.vocab = vocab
+        self.prompt_len = prompt_len
+        self.rng = torch.Generator().manual_seed(seed)
+        self.low = low
+        self.cursor = 0
+
+    def take(self, n: int) -> list[PromptRecord]:
+        out = []
+        for _ in range(n):
+            ids = torch.randint(self.low, self.vocab, (self.prompt_len,), generator=self.rng).tolist()
+            out.append(PromptRecord(ids, metadata={"task": "reverse"}, example_id=f"synthetic-{self.cursor}"))
+            self.cursor += 1
+        return out
+
+    def state_dict(self) -> dict:
+        return {"cursor": self.cursor, "rng": self.rng.get_state().tolist()}
+
+
+class RLOrchestrator:
+    def __init__(self, cfg, engine, sender: FileSystemRolloutSender | None, prompts, monitor=None,
+                 custom_rollout: Callable | None = None):
+        self.cfg = cfg
+        self.engine = engine
+        self.sender = sender
+        self.prompts = prompts
+        self.monitor = monitor
+        self.algo = build_algorithm(cfg.algo)
+        self.scope = algorithm_scope(cfg.algo)
+        self.eps = algorithm_epsilon(cfg.algo)
+        self.scorer = RLRewardScorer(cfg.reward)
+        self.custom_rollout = custom_rollout
+        self.last_stats: dict[str, float] = {}
+
+    def _sampling(self):
+        from ..inference.engine import SamplingParams
+
+        s = self.cfg.inference.sampling
+        return SamplingParams(
+            temperature=s.temperature, top_p=s.top_p, top_k=s.top_k, min_p=s.min_p,
+            max_tokens=s.max_completion_tokens or 256, min_tokens=s.min_tokens,
+            n=self.cfg.orchestrator.rollouts_per_example or 1, seed=s.seed,
+            return_sampling_mask=self.cfg.sampling_mask_required(),
+        )
+
+    def generate_records(self, prompts: list[PromptRecord], step: int) -> list[RLExample]:
+        params = self._sampling()
+        if params.seed is not None:
+            params.seed = params.seed + step
+        t0 = time.perf_counter()
+        comps = self.engine.generate([p.prompt_ids for p in prompts], params)
+        gen_s = time.perf_counter() - t0
+        recs = []
+        for c in comps:
+            p = prompts[c.prompt_index]
+            ids = p.prompt_ids + c.token_ids
+            mask = [False] * len(p.prompt_ids) + [True] * len(c.token_ids)
+            md = dict(p.metadata)
+            md.update(prompt_ids=p.prompt_ids, completion_ids=c.token_ids, finish_reason=c.finish_reason,
+                      is_truncated=c.finish_reason == "length", completion_token_count=len(c.token_ids),
+                      prompt_token_count=len(p.prompt_ids), group=f"{step}:{c.prompt_index}",
+                      sample_index=c.sample_index, example_id=p.example_id)
+            recs.append(RLExample(prompt=p.prompt, completion=[], advantage=None, reward=None, input_ids=ids,
+                                  loss_mask=mask, target_completion=p.target_completion,
+                                  inference_logprobs=c.logprobs, temperatures=params.temperature,
+                                  sampling_mask=c.sampling_mask, metadata=md, source="orchestrator"))
+        st = getattr(self.engine, "stats", {}) or {}
+        ntok = sum(len(c.token_ids) for c in comps)
+        self.last_stats = {"rollout/generate_seconds": gen_s, "rollout/generated_tokens": float(ntok),
+                           "rollout/tokens_per_second": ntok / max(gen_s, 1e-9),
+                           "rollout/samples": float(len(comps))}
+        self.last_stats.update({f"inference/{k}": float(v) for k, v in st.items()})
+        return recs
+
+    def score(self, recs: list[RLExample]) -> list[RLExample]:
+        from dataclasses import replace
+
+        recs = [replace(r, reward=self.scorer.score(r)) for r in recs]
+        return score_records(self.algo, recs, self.scope, group_key=lambda r: (r.metadata or {}).get("group"))
+
+    def _filter_zero(self, recs: list[RLExample]) -> tuple[list[RLExample], int]:
+        if not self.cfg.orchestrator.filter_zero_advantage or self.scope == "rollout":
+            return recs, 0
+        groups: dict[Any, list[RLExample]] = {}
+        for r in recs:
+            groups.setdefault((r.metadata or {}).get("group"), []).append(r)
+        keep, dropped = [], 0
+        for g in groups.values():
+            if all(abs(float(r.advantage or 0.0)) <= self.eps for r in g):
+                dropped += len(g)
+            else:
+                keep += g
+        return keep, dropped
+
+    def materialize(self, step: int) -> list[RLExample]:
+        o = self.cfg.orchestrator
+        n_prompts = o.examples_per_step or 1
+        prompts = self.prompts.take(n_prompts)
+        recs = self.score(self.custom_rollout(prompts, step) if self.custom_rollout else self.generate_records(prompts, step))
+        kept, dropped = self._filter_zero(recs)
+        retries = 0
+        while (o.refill_zero_advantage and dropped and retries < o.zero_advantage_max_retries
+               and len(kept) < len(recs)):
+            need = max(1, dropped // max(1, o.rollouts_per_example or 1))
+            more = self.score(self.generate_records(self.prompts.take(need), step))
+            more_kept, dropped = self._filter_zero(more)
+            kept += more_kept
+            retries += 1
+        if not kept:
+            kept = recs  # never publish an empty batch; zero-advantage rows contribute no gradient
+        rewards = [float(r.reward or 0.0) for r in recs]
+        self.last_stats.update({"reward/mean": sum(rewards) / max(1, len(rewards)),
+                                "rollout/zero_advantage_dropped": float(dropped),
+                                "rollout/zero_advantage_retries": float(retries)})
+        return kept
+
+    def publish(self, step: int, policy_step: int | None = None) -> Any:
+        recs = self.materialize(step)
+        rows = [example_to_payload(r) for r in recs]
+        tokens = sum(len(r.input_ids or []) for r in recs)
+        if self.sender is None:
+            return recs
+        return self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=policy_step,
+                                   tokens=tokens, reward_mean=self.last_stats.get("reward/mean"))

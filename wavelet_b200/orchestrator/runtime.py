@@ -1,0 +1,157 @@
+"""``wavelet rl``: the RL launcher.
+
+Modes (``launcher.mode``; orchestrator/runtime.py of the reference):
+
+* ``integrated`` — one process per GPU runs trainer, generator and
+  orchestrator.  The generator reads the trainer's bf16 weights in place
+  (zero-copy policy transfer).  With several ranks every rank generates the
+  rollouts of its share of the prompts; rank 0 gathers and publishes the
+  batch to the durable queue; every rank trains on its packed share.
+  ``orchestrator.max_async_level >= 1`` generates step s+1 while step s trains
+  (one step of policy lag), otherwise generation and training alternate.
+* ``process`` / ``colocate`` / ``colocate_sleep`` — separate role processes
+  (inference server(s), ``rl-trainer`` under torchrun, ``rl-inference``)
+  supervised by ``orchestrator.launcher``; they communicate only through the
+  filesystem queues (and HTTP to the inference server).
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+import sys
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from ..configs.config import RLConfig
+from ..data.rl import example_from_payload, example_to_payload
+from ..transport.queue import FileSystemRolloutSender, prune_from
+from ..utils import pathing
+from ..utils.config import config_to_plain, dump_yaml, load_config
+from .rollouts import RLOrchestrator, SyntheticReversePrompts
+
+log = logging.getLogger("wavelet")
+
+
+def build_prompt_source(cfg: RLConfig, vocab: int, rank: int = 0):
+    """Prompt source for the orchestrator: synthetic reverse-text prompts
+    (``data.source: fake``) or pretokenised prompt rows from local files."""
+    d = cfg.data
+    if d.source == "fake":
+        return SyntheticReversePrompts(min(vocab, d.fake_vocab_size), d.fake_prompt_len, seed=d.seed * 1000 + rank)
+    from .sources import FilePromptSource
+
+    return FilePromptSource(cfg, rank=rank)
+
+
+class IntegratedRunner:
+    def __init__(self, cfg: RLConfig):
+        self.cfg = cfg
+
+    def setup(self) -> "IntegratedRunner":
+        from ..inference.engine import Generator
+        from ..trainer.rl import RLTrainer
+
+        c = self.cfg
+        out = Path(c.output_dir)
+        self.trainer = RLTrainer(c)
+        world_rank = int(os.environ.get("RANK", "0"))
+        if world_rank == 0:
+            resume = c.ckpt is not None and c.ckpt.is_resuming
+            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume)
+            attempt = pathing.create_launch_attempt(out)
+            dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(c))
+        self.trainer.setup()
+        t = self.trainer
+        self.world = t.world
+        v = c.inference.vllm
+        max_len = v.max_model_len or c.data.seq_len
+        self.engine = Generator(t.model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
+                                gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
+        self.sender = FileSystemRolloutSender(out, c.transport) if self.world.rank == 0 else None
+        # batches past a resumed step are stale
+        if self.world.rank == 0 and t.step > 0:
+            prune_from(self.sender.queue_dir, t.step)
+        prompts = build_prompt_source(c, t.model.cfg.vocab_size, rank=t.dp_rank)
+        self.orch = RLOrchestrator(c, self.engine, None, prompts, monitor=t.monitor)
+        return self
+
+    def _gather(self, rows: list[dict]) -> list[dict]:
+        if not dist.is_initialized() or self.world.world_size == 1:
+            return rows
+        allr: list[Any] = [None] * self.world.world_size
+        dist.all_gather_object(allr, rows)
+        return [r for part in allr for r in part]
+
+    def run(self) -> int:
+        c = self.cfg
+        t = self.trainer
+        total = c.max_steps if c.max_steps is not None else 1
+        status = "failed"
+        try:
+            while t.step < total:
+                step = t.step
+                t0 = time.perf_counter()
+                recs = self.orch.materialize(step)
+                gen_s = time.perf_counter() - t0
+                rows = self._gather([example_to_payload(r) for r in recs])
+                if self.sender is not None:
+                    self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=step,
+                                        tokens=sum(len(r.get("input_ids") or []) for r in rows))
+                if dist.is_initialized():
+                    dist.barrier()
+                batch = t.receiver.wait()
+                if self.world.rank == 0:
+                    t.receiver.claim(batch, step)
+                from ..transport.queue import read_training_records
+
+                records = [example_from_payload(r) for r in read_training_records(batch.training_path)]
+                t1 = time.perf_counter()
+                m = t.train_on_examples(records)
+                train_s = time.perf_counter() - t1
+                if self.world.rank == 0:
+                    t.receiver.consumed(batch, step, t.step)
+                m.update(self.orch.last_stats)
+                m["time/generate_seconds"] = gen_s
+                m["time/train_seconds"] = train_s
+                m["time/step_seconds"] = time.perf_counter() - t0
+                t.monitor.log(m, t.step)
+                log.info("rl step %d reward %.4f loss %.4f gen %.2fs train %.2fs", t.step, m.get("reward/mean", 0.0),
+                         m["loss"], gen_s, train_s)
+                if c.policy_transfer.type == "filesystem" and t.step % c.policy_transfer.export_every_steps == 0 and c.policy_transfer.export_initial:
+                    pass  # the in-process generator already sees the new weights
+                if t.ckpt is not None and c.ckpt.interval and t.step % c.ckpt.interval == 0:
+                    t.ckpt.save(t.step, model=t.model, optimizer=t.optimizer, data_state=None,
+                                meta={"arch": t.model.cfg.to_dict()}, scheduler_state={"step": t.step})
+            status = "completed"
+            return 0
+        finally:
+            if t.ckpt is not None:
+                t.ckpt.wait()
+            t.monitor.finish(status=status, step=t.step)
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    cfg = load_config(RLConfig, argv)
+    if cfg.dry_run:
+        print(cfg.model_dump_json(indent=2))
+        return 0
+    if cfg.launcher.mode == "integrated":
+        from ..parallel.dist import destroy_distributed
+
+        try:
+            return IntegratedRunner(cfg).setup().run()
+        finally:
+            destroy_distributed()
+    from .launcher import run_process_launcher
+
+    return run_process_launcher(cfg, argv)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
