@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(&s->s_full[st], (j >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      if (!mbar_wait_warp(&s->s_full[st], (j >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       float sv[128];
 #pragma unroll
@@ -253,10 +253,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       // P buffer and O must be idle: wait for PV_{j-1}
       if (j > 0) {
-        if (!mbar_wait(&s->pv_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+        if (!mbar_wait_warp(&s->pv_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
         tc_fence_after();
       }
-      if (rescale) {
+      // tcgen05.ld/st are warp-collective: rescale the whole warp's rows
+      // together when any row needs it (alpha = 1 for the others).
+      if (__any_sync(0xffffffffu, rescale)) {
         l_run *= alpha;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_arrive(&s->p_full);
     }
     if (ok && n_kv > 0) {
-      if (mbar_wait(&s->pv_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
+      if (mbar_wait_warp(&s->pv_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
         tc_fence_after();
         const bool valid = qi < L;
         const float inv_l = 1.f / l_run;
@@ -534,7 +536,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float* lse_row = p.lse + (int64_t)h * p.T + s0 + q0;
       const float* dlt_row = p.delta + (int64_t)h * p.T + s0 + q0;
       const int qlim = L - q0;  // columns c < qlim are real queries
-      if (!mbar_wait(&s->s_full, it & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      if (!mbar_wait_warp(&s->s_full, it & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       float pt[128];
       ld_row128(tS + lane_off, pt, p.scale_log2);
@@ -546,7 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         pt[c] = valid ? exp2f(pt[c] - __ldg(lse_row + c) * LOG2E) : 0.f;
       }
       if (it > 0) {
-        if (!mbar_wait(&s->mma_done, (it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+        if (!mbar_wait_warp(&s->mma_done, (it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       }
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -582,7 +584,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&s->p_full);
     }
-    if (ok && n_it > 0 && mbar_wait(&s->mma_done, (n_it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
+    if (ok && n_it > 0 && mbar_wait_warp(&s->mma_done, (n_it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
       const bool valid = kj < L;
       store_row128(tdV + lane_off, p.dv + ((int64_t)(s0 + kj) * p.Hk + g) * HD, 1.f, valid);
@@ -722,7 +724,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float dlt = vq ? p.delta[(int64_t)h * p.T + s0 + qi] : 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s->s_full, j & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      if (!mbar_wait_warp(&s->s_full, j & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       float pr[128];
       ld_row128(tS + lane_off, pr, p.scale_log2);
@@ -741,7 +743,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) pr[c * 32 + e] *= (__uint_as_float(v[e]) - dlt);
       }
-      if (j > 0 && !mbar_wait(&s->mma_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      if (j > 0 && !mbar_wait_warp(&s->mma_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         uint4 w;
@@ -755,7 +757,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&s->p_full);
     }
-    if (ok && n_kv > 0 && mbar_wait(&s->mma_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
+    if (ok && n_kv > 0 && mbar_wait_warp(&s->mma_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
       store_row128(tdQ + lane_off, p.dq + ((int64_t)(s0 + qi) * p.Hq + h) * HD, p.scale, vq);
     }

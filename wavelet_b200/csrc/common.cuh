@@ -100,6 +100,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-collective form: every lane of the warp calls it and every lane gets
+// the same answer, so a timeout observed by one lane can never split the warp
+// before a `.sync.aligned` tcgen05 instruction.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               int* err_word, int err_code) {
+  const bool ok = mbar_wait(bar, parity, abort, err_word, err_code);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
                                             int c0, int c1) {

@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      if (!mbar_wait(&s->tmem_full[acc], acc_phase, abort, p.err, kErrTimeoutEpilogue)) break;
+      if (!mbar_wait_warp(&s->tmem_full[acc], acc_phase, abort, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       int tm, tn;
       tile_coords(t, p.num_m, p.num_n, tm, tn);
