@@ -852,4 +852,57 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   attn_bwd_dq_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
 }
 
+// Same launch sequence as attn_bwd, with the Delta scratch (b.delta) and the
+// error word supplied by the caller instead of looked up / allocated here.
+// Used by the allocation-free entry point (attention_noalloc.cu).
+int attn_bwd_explicit(const AttnBwdArgs& b, int* err, cudaStream_t stream) {
+  using namespace attn;
+  const AttnArgs& a = b.f;
+  if (a.head_dim != 128) return 1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 2;
+  static bool attr[64] = {false};
+  if (!attr[dev & 63]) {
+    if (cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dkv_smem_bytes()) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq_smem_bytes()) !=
+            cudaSuccess)
+      return 3;
+    attr[dev & 63] = true;
+  }
+  {
+    const int warps = 8;
+    const int64_t work = (int64_t)a.T * a.Hq;
+    attn_delta_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row, reinterpret_cast<const __nv_bfloat16*>(b.dout),
+        b.delta, a.T, a.Hq);
+  }
+  CUtensorMap mq, mk, mv, mdo;
+  try {
+    mq = head_map(a.q, a.q_row, a.Hq, a.T);
+    mk = head_map(a.k, a.k_row, a.Hk, a.T);
+    mv = head_map(a.v, a.v_row, a.Hk, a.T);
+    mdo = head_map(b.dout, (int64_t)a.Hq * 128, a.Hq, a.T);
+  } catch (const std::exception&) {
+    return 4;
+  }
+  BwdParams p;
+  p.lse = a.lse;
+  p.delta = b.delta;
+  p.cu = a.cu_seqlens;
+  p.dq = reinterpret_cast<__nv_bfloat16*>(b.dq);
+  p.dk = reinterpret_cast<__nv_bfloat16*>(b.dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(b.dv);
+  p.Hq = a.Hq;
+  p.Hk = a.Hk;
+  p.T = a.T;
+  p.scale = a.scale;
+  p.scale_log2 = a.scale * LOG2E;
+  p.err = err;
+  const int nt = (a.max_seqlen + TILE - 1) / TILE;
+  attn_bwd_dkv_kernel<<<dim3(nt, a.Hk, a.nseq), NUM_THREADS, dkv_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
+  attn_bwd_dq_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 5;
+}
+
 }  // namespace wb

@@ -29,5 +29,8 @@ struct AttnBwdArgs {
 
 void attn_fwd(const AttnArgs& a, cudaStream_t stream);
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t stream);
+// attn_bwd with caller-provided Delta scratch (a.delta) and error word;
+// returns 0 on success (no exceptions, no allocation).
+int attn_bwd_explicit(const AttnBwdArgs& a, int* err, cudaStream_t stream);
 
 }  // namespace wb
