@@ -89,6 +89,43 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
   wb::gemm_bf16(g, cur_stream());
 }
 
+// Grouped (MoE expert) GEMM.  mode 1: C = A B_g^T with g = tile_group[m_tile];
+// mode 2: C[g*M:(g+1)*M] (op)= A_g^T B_g over token segments (k_start, k_len).
+void gemm_grouped(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& c, int64_t mode,
+                  int64_t M, int64_t N, int64_t K, const c10::optional<at::Tensor>& tile_group,
+                  int64_t b_group_stride, int64_t b_outer, const c10::optional<at::Tensor>& k_start,
+                  const c10::optional<at::Tensor>& k_len, int64_t groups, int64_t epi, double alpha) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_cuda(c, "c");
+  const c10::cuda::CUDAGuard guard(a.device());
+  wb::GemmArgs g;
+  g.A = a.data_ptr();
+  g.lda = ld_of(a, "a");
+  g.a_mn = a_mn;
+  g.B = b.data_ptr();
+  g.ldb = ld_of(b, "b");
+  g.b_mn = b_mn;
+  g.C = c.data_ptr();
+  g.ldc = ld_of(c, "c");
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = static_cast<int>(epi);
+  g.alpha = static_cast<float>(alpha);
+  g.group_mode = static_cast<int>(mode);
+  if (tile_group) {
+    WB_CHECK(tile_group->scalar_type() == at::kInt && tile_group->is_cuda(), "gemm_grouped: tile_group int32 CUDA");
+    g.tile_group = tile_group->data_ptr<int>();
+  }
+  g.b_group_stride = b_group_stride;
+  g.b_outer = b_outer;
+  if (k_start) g.k_start = k_start->data_ptr<int>();
+  if (k_len) g.k_len = k_len->data_ptr<int>();
+  g.groups = static_cast<int>(groups);
+  wb::gemm_bf16(g, cur_stream());
+}
+
 void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
                  const c10::optional<at::Tensor>& h_out, const at::Tensor& w, at::Tensor& y,
                  const c10::optional<at::Tensor>& rstd, double eps) {
@@ -393,6 +430,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"),
         py::arg("b_mn"), py::arg("c"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
         py::arg("bias") = py::none(), py::arg("res") = py::none());
+  m.def("gemm_grouped", &gemm_grouped);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

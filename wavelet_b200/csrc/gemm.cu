@@ -64,6 +64,20 @@ struct Params {
   int M, N, K;
   int num_m, num_n, num_k;
   int* err;
+  // grouped modes (GROUP template parameter)
+  const int* tile_group;   // M-grouped: expert of every 128-row M tile
+  int64_t b_group_stride;  // M-grouped: B outer-coordinate offset per group
+  const int* k_start;      // K-grouped: first K row of every group (multiple of BK)
+  const int* k_len;        // K-grouped: K rows of every group
+  int groups;
+};
+
+// Tile decode shared by the three warp roles (they must agree exactly).
+struct TileInfo {
+  int tm, tn;
+  int kb_begin, num_k;
+  int64_t b_off;
+  int64_t c_row_off;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
@@ -76,10 +90,32 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m,
   n = r / gsm;
 }
 
+template <int GROUP>
+__device__ __forceinline__ TileInfo tile_info(int t, const Params& p) {
+  TileInfo ti;
+  if constexpr (GROUP == 2) {
+    const int per = p.num_m * p.num_n;
+    const int g = t / per;
+    tile_coords(t - g * per, p.num_m, p.num_n, ti.tm, ti.tn);
+    ti.kb_begin = p.k_start[g] / BK;
+    ti.num_k = (p.k_len[g] + BK - 1) / BK;
+    ti.b_off = 0;
+    ti.c_row_off = (int64_t)g * p.M;
+  } else {
+    tile_coords(t, p.num_m, p.num_n, ti.tm, ti.tn);
+    ti.kb_begin = 0;
+    ti.num_k = p.num_k;
+    ti.b_off = (GROUP == 1) ? (int64_t)p.tile_group[ti.tm] * p.b_group_stride : 0;
+    ti.c_row_off = 0;
+  }
+  return ti;
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col0,
-                                               const uint32_t (&v)[32]) {
+                                               const uint32_t (&v)[32], int64_t row_off) {
   if (row >= p.M) return;
+  row += static_cast<int>(row_off);
   const bool full = (col0 + 32 <= p.N);
   if constexpr (EPI == kEpiBF16) {
     __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)row * p.ldc + col0;
@@ -160,7 +196,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int GROUP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 Params p) {
@@ -172,7 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.num_m * p.num_n;
+  const int num_tiles = p.num_m * p.num_n * (GROUP == 2 ? p.groups : 1);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -208,10 +244,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int i = 0; i < STAGES; ++i) issued[i] = 0, issued_phase[i] = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, p.num_m, p.num_n, tm, tn);
-        const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < p.num_k; ++kb) {
+        const TileInfo ti = tile_info<GROUP>(t, p);
+        const int m0 = ti.tm * BM, n0 = ti.tn * BN;
+        for (int kb = 0; kb < ti.num_k; ++kb) {
           if (!mbar_wait(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -219,7 +254,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* a_dst = tiles + stage * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
           mbar_arrive_expect_tx(&s->full[stage], STAGE_BYTES);
-          const int k0 = kb * BK;
+          const int k0 = (ti.kb_begin + kb) * BK;
           if constexpr (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / MN_BOX; ++j)
@@ -230,9 +265,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if constexpr (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / MN_BOX; ++j)
-              tma_load_2d(&tmB, &s->full[stage], b_dst + j * MN_BOX_BYTES, n0 + j * MN_BOX, k0);
+              tma_load_2d(&tmB, &s->full[stage], b_dst + j * MN_BOX_BYTES, n0 + j * MN_BOX,
+                          k0 + (int)ti.b_off);
           } else {
-            tma_load_2d(&tmB, &s->full[stage], b_dst, k0, n0);
+            tma_load_2d(&tmB, &s->full[stage], b_dst, k0, n0 + (int)ti.b_off);
           }
           issued[stage] = 1;
           issued_phase[stage] = phase;
@@ -264,13 +300,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       bool any = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<GROUP>(t, p);
+        if (ti.num_k == 0) continue;  // empty group: no MMA, no epilogue
         if (!mbar_wait(&s->tmem_empty[acc], acc_phase ^ 1, abort, p.err, kErrTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_k; ++kb) {
+        for (int kb = 0; kb < ti.num_k; ++kb) {
           if (!mbar_wait(&s->full[stage], phase, abort, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -317,10 +355,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const TileInfo ti = tile_info<GROUP>(t, p);
+      if (ti.num_k == 0) continue;
       if (!mbar_wait_warp(&s->tmem_full[acc], acc_phase, abort, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      int tm, tn;
-      tile_coords(t, p.num_m, p.num_n, tm, tn);
+      const int tm = ti.tm, tn = ti.tn;
       const int row = tm * BM + q * 32 + lane;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -329,7 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_addr + c, v);
         tmem_wait_ld();
-        epilogue_chunk<EPI>(p, row, tn * BN + c, v);
+        epilogue_chunk<EPI>(p, row, tn * BN + c, v, ti.c_row_off);
       }
       tc_fence_before();
       mbar_arrive(&s->tmem_empty[acc]);
@@ -345,9 +384,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int GROUP = 0>
 static void launch(const GemmArgs& g, cudaStream_t stream) {
-  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
+  auto kern = gemm_kernel<A_MN, B_MN, EPI, GROUP>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -360,9 +399,12 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
                                        MN_BOX, BK, CU_TENSOR_MAP_SWIZZLE_128B)
                         : make_tmap_2d(g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, g.M, g.lda,
                                        BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = B_MN ? make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, g.K, g.ldb,
+  // B outer extent: N (K-major) or K (MN-major) rows, times the group count
+  // in M-grouped mode where every group has its own weight block.
+  const uint64_t b_outer = g.b_outer > 0 ? (uint64_t)g.b_outer : (uint64_t)(B_MN ? g.K : g.N);
+  CUtensorMap tb = B_MN ? make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, b_outer, g.ldb,
                                        MN_BOX, BK, CU_TENSOR_MAP_SWIZZLE_128B)
-                        : make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, g.N, g.ldb,
+                        : make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, b_outer, g.ldb,
                                        BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   Params p;
   p.C = g.C;
@@ -378,7 +420,12 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   p.num_n = (g.N + BN - 1) / BN;
   p.num_k = (g.K + BK - 1) / BK;
   p.err = error_word(dev);
-  const int tiles = p.num_m * p.num_n;
+  p.tile_group = g.tile_group;
+  p.b_group_stride = g.b_group_stride;
+  p.k_start = g.k_start;
+  p.k_len = g.k_len;
+  p.groups = g.groups;
+  const int tiles = p.num_m * p.num_n * (GROUP == 2 ? g.groups : 1);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
   kern<<<grid, NUM_THREADS, smem_bytes(), stream>>>(ta, tb, p);
 }
@@ -388,6 +435,21 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
 void gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
   using namespace gemm;
   if (g.M <= 0 || g.N <= 0) return;
+  if (g.group_mode == 1) {
+    // expert forward / dgrad: rows of A are expert segments padded to 128
+    if (!g.tile_group) throw std::runtime_error("wavelet_b200 grouped gemm: tile_group required");
+    if (g.epi != kEpiBF16 || g.a_mn) throw std::runtime_error("wavelet_b200 grouped gemm: M-grouped mode is K-major A, bf16 out");
+    if (g.b_mn) return launch<false, true, kEpiBF16, 1>(g, stream);
+    return launch<false, false, kEpiBF16, 1>(g, stream);
+  }
+  if (g.group_mode == 2) {
+    // expert wgrad: K = token segments; A and B MN-major; C = [groups * M, N]
+    if (!g.k_start || !g.k_len || g.groups <= 0) throw std::runtime_error("wavelet_b200 grouped gemm: k_start/k_len required");
+    if (!g.a_mn || !g.b_mn) throw std::runtime_error("wavelet_b200 grouped gemm: K-grouped mode needs MN-major A and B");
+    if (g.epi == kEpiF32Acc) return launch<true, true, kEpiF32Acc, 2>(g, stream);
+    if (g.epi == kEpiF32) return launch<true, true, kEpiF32, 2>(g, stream);
+    throw std::runtime_error("wavelet_b200 grouped gemm: K-grouped mode writes fp32");
+  }
   if (g.K <= 0) throw std::runtime_error("wavelet_b200 gemm: K must be positive");
 #define WB_GEMM_DISPATCH(AM, BMJ)                                               \
   if (g.a_mn == AM && g.b_mn == BMJ) {                                          \

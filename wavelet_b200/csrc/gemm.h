@@ -28,6 +28,19 @@ struct GemmArgs {
   float alpha = 1.0f;
   int epi = kEpiBF16;
   int M = 0, N = 0, K = 0;
+  // Grouped (MoE expert) modes.  0: dense.
+  // 1 (M-grouped): A rows are expert segments padded to 128; tile_group[m_tile]
+  //   gives the expert; B holds every expert's weights stacked along its outer
+  //   dimension (b_outer rows in total) and expert g starts at g * b_group_stride.
+  // 2 (K-grouped): C[g] (rows g*M .. g*M+M-1) = A_g^T B_g where A_g / B_g are the
+  //   token rows [k_start[g], k_start[g] + k_len[g]) of MN-major A and B.
+  int group_mode = 0;
+  const int* tile_group = nullptr;
+  int64_t b_group_stride = 0;
+  int64_t b_outer = 0;
+  const int* k_start = nullptr;
+  const int* k_len = nullptr;
+  int groups = 0;
 };
 
 void gemm_bf16(const GemmArgs& g, cudaStream_t stream);
