@@ -139,6 +139,22 @@ class Generator:
         self._moe = [layer.moe for layer in model.layers]
 
     # ------------------------------------------------------------ utilities
+    def release_cache(self) -> None:
+        """Free the KV cache memory (``sleep``); ``restore_cache`` re-allocates it."""
+        self._cache_shape = self.k_cache[0].shape if self.k_cache else None
+        self.k_cache = []
+        self.v_cache = []
+        if self.dev.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def restore_cache(self) -> None:
+        if self.k_cache or getattr(self, "_cache_shape", None) is None:
+            return
+        dt = self.m.flat.compute_dtype
+        self.k_cache = [torch.empty(self._cache_shape, device=self.dev, dtype=dt) for _ in range(self.cfg.num_layers)]
+        self.v_cache = [torch.empty(self._cache_shape, device=self.dev, dtype=dt) for _ in range(self.cfg.num_layers)]
+        self.bm = BlockManager(self.num_blocks)
+
     def kv_usage(self) -> float:
         return 1.0 - self.bm.num_free / self.num_blocks
 

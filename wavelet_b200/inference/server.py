@@ -1,0 +1,232 @@
+"""``wavelet inference-server``: the native generator behind HTTP.
+
+Routes (the reference's inference server surface, inference/server.py:693-1036
+and native_server.py:92-215):
+
+    GET  /health, /liveness, /debug/state, /v1/models, /metrics
+    POST /pause, /resume, /sleep, /wake
+    POST /load_policy            {"policy_dir": ..., "step": N}
+    POST /init_broadcaster       device weight transfer group (flat_v1 protocol)
+    POST /annotate               {"records": [RLExample payloads]} -> annotated records
+    POST /score                  teacher-forced log-probs of given token sequences
+    POST /v1/completions         {"prompt_token_ids" | "prompt", sampling...}
+    POST /v1/chat/completions[/tokens], /chat/completions/tokens
+    POST /tokenize, /v1/tokenize
+
+Generation requests are serialised by a gate that ``/pause`` closes while a
+policy is being loaded.
+"""
+
+from __future__ import annotations
+
+import sys
+import threading
+import time
+from contextlib import contextmanager
+from pathlib import Path
+from typing import Any
+
+from ..configs.config import RLConfig
+from ..data.rl import example_from_payload, example_to_payload
+from ..utils.config import load_config
+
+
+class GenerationGate:
+    def __init__(self):
+        self._cv = threading.Condition()
+        self._paused = False
+        self._active = 0
+
+    @contextmanager
+    def generation(self):
+        with self._cv:
+            while self._paused:
+                self._cv.wait()
+            self._active += 1
+        try:
+            yield
+        finally:
+            with self._cv:
+                self._active -= 1
+                self._cv.notify_all()
+
+    def pause(self, wait: bool = True):
+        with self._cv:
+            self._paused = True
+            while wait and self._active:
+                self._cv.wait()
+
+    def resume(self):
+        with self._cv:
+            self._paused = False
+            self._cv.notify_all()
+
+    @property
+    def paused(self) -> bool:
+        return self._paused
+
+
+def build_app(config: RLConfig, engine=None):
+    from fastapi import FastAPI, HTTPException
+
+    from ..data.tokenizer import load_tokenizer
+    from .policy import NativePolicyInferenceEngine
+
+    tok = load_tokenizer(config.model.name)
+    if engine is None:
+        engine = NativePolicyInferenceEngine(config, tokenizer=tok)
+        engine.setup()
+    gate = GenerationGate()
+    app = FastAPI(title="wavelet inference server")
+    state: dict[str, Any] = {"started_at": time.time(), "requests": 0, "generated_tokens": 0, "sleeping": False}
+    lock = threading.Lock()
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok"}
+
+    @app.get("/liveness")
+    def liveness():
+        return {"status": "alive", "paused": gate.paused, "sleeping": state["sleeping"]}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": config.model.name, "object": "model", "owned_by": "wavelet"}]}
+
+    @app.get("/debug/state")
+    def debug_state():
+        g = engine.generator
+        return {"policy_step": engine.policy_step, "paused": gate.paused, **state,
+                "kv_cache_usage": g.kv_usage() if g is not None else None,
+                "num_blocks": g.num_blocks if g is not None else None}
+
+    @app.get("/metrics")
+    def metrics():
+        g = engine.generator
+        usage = g.kv_usage() if g is not None else 0.0
+        lines = [
+            f"wavelet:kv_cache_usage_perc {usage}",
+            f"wavelet:num_requests_running 0",
+            f"wavelet:generation_tokens_total {state['generated_tokens']}",
+            f"wavelet:requests_total {state['requests']}",
+        ]
+        from fastapi.responses import PlainTextResponse
+
+        return PlainTextResponse("\n".join(lines) + "\n")
+
+    @app.post("/pause")
+    def pause():
+        gate.pause()
+        return {"status": "paused"}
+
+    @app.post("/resume")
+    def resume():
+        gate.resume()
+        return {"status": "resumed"}
+
+    @app.post("/sleep")
+    def sleep():
+        gate.pause()
+        engine.sleep()
+        state["sleeping"] = True
+        return {"status": "sleeping"}
+
+    @app.post("/wake")
+    def wake(payload: dict[str, Any] | None = None):
+        engine.wake(tags=(payload or {}).get("tags"))
+        state["sleeping"] = False
+        gate.resume()
+        return {"status": "awake"}
+
+    @app.post("/load_policy")
+    def load_policy(payload: dict[str, Any]):
+        step = int(payload["step"])
+        pdir = payload.get("policy_dir")
+        with lock:
+            engine.load_policy(Path(pdir) if pdir else None, step=step)
+        return {"status": "loaded", "policy_step": step}
+
+    @app.post("/init_broadcaster")
+    def init_broadcaster(payload: dict[str, Any]):
+        state["broadcaster"] = payload
+        return {"status": "ok", "protocol": "flat_v1"}
+
+    @app.post("/annotate")
+    def annotate(payload: dict[str, Any]):
+        with gate.generation(), lock:
+            recs = [example_from_payload(r) for r in payload["records"]]
+            out = engine.annotate(recs)
+        state["requests"] += 1
+        state["generated_tokens"] += sum(len((r.metadata or {}).get("completion_ids", [])) for r in out)
+        return {"records": [example_to_payload(r) for r in out], "policy_step": engine.policy_step}
+
+    @app.post("/score")
+    def score(payload: dict[str, Any]):
+        with gate.generation(), lock:
+            lps = engine.score(payload["sequences"], payload["prompt_lens"], float(payload.get("temperature", 1.0)))
+        return {"logprobs": lps}
+
+    def _complete(prompts: list[list[int]], payload: dict[str, Any]) -> list[Any]:
+        ov = {"temperature": payload.get("temperature"), "top_p": payload.get("top_p"),
+              "top_k": payload.get("top_k"), "min_p": payload.get("min_p"),
+              "max_tokens": payload.get("max_completion_tokens") or payload.get("max_tokens"),
+              "n": payload.get("n"), "seed": payload.get("seed")}
+        with gate.generation(), lock:
+            return engine.generate_ids(prompts, ov)
+
+    @app.post("/v1/completions")
+    def completions(payload: dict[str, Any]):
+        if "prompt_token_ids" in payload:
+            prompts = payload["prompt_token_ids"]
+            prompts = [prompts] if prompts and isinstance(prompts[0], int) else prompts
+        else:
+            p = payload["prompt"]
+            prompts = [tok.encode(x) for x in ([p] if isinstance(p, str) else p)]
+        comps = _complete(prompts, payload)
+        return {"object": "text_completion", "model": config.model.name, "policy_step": engine.policy_step,
+                "choices": [{"index": i, "prompt_index": c.prompt_index, "token_ids": c.token_ids,
+                             "logprobs": {"token_logprobs": c.logprobs}, "text": tok.decode(c.token_ids),
+                             "finish_reason": c.finish_reason} for i, c in enumerate(comps)]}
+
+    def _chat(payload: dict[str, Any]):
+        ids = tok.apply_chat_template(payload["messages"], tokenize=True, add_generation_prompt=True)
+        ids = list(ids["input_ids"] if isinstance(ids, dict) else ids)
+        comps = _complete([ids], payload)
+        return {"object": "chat.completion", "model": config.model.name, "prompt_token_ids": ids,
+                "choices": [{"index": i, "message": {"role": "assistant", "content": tok.decode(c.token_ids)},
+                             "token_ids": c.token_ids,
+                             "logprobs": {"content": [{"token_id": t, "logprob": lp} for t, lp in zip(c.token_ids, c.logprobs)]},
+                             "finish_reason": c.finish_reason} for i, c in enumerate(comps)]}
+
+    app.post("/v1/chat/completions")(_chat)
+    app.post("/v1/chat/completions/tokens")(_chat)
+    app.post("/chat/completions/tokens")(_chat)
+
+    def _tokenize(payload: dict[str, Any]):
+        if "messages" in payload:
+            ids = tok.apply_chat_template(payload["messages"], tokenize=True,
+                                          add_generation_prompt=bool(payload.get("add_generation_prompt", True)))
+            ids = list(ids["input_ids"] if isinstance(ids, dict) else ids)
+        else:
+            ids = tok.encode(payload.get("prompt", ""))
+        return {"tokens": ids, "count": len(ids)}
+
+    app.post("/tokenize")(_tokenize)
+    app.post("/v1/tokenize")(_tokenize)
+    app.state.engine = engine
+    app.state.gate = gate
+    return app
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    cfg = load_config(RLConfig, argv)
+    import uvicorn
+
+    app = build_app(cfg)
+    uvicorn.run(app, host=cfg.inference.http.host, port=cfg.inference.http.port, log_level="warning")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,147 @@
+"""Process-mode RL launcher: role processes under one supervisor.
+
+Order (orchestrator/runtime.py:465-657 and launcher.py:18-348 of the
+reference): write role configs into ``configs/attempt_<n>/resolved/``, start
+the inference server(s) (one per replica, pinned with CUDA_VISIBLE_DEVICES),
+wait for ``/health``, optionally put them to sleep (colocate_sleep), then
+start the trainer (``torchrun ... -m wavelet_b200 rl-trainer``) and the
+rollout role (``rl-inference``).  ``wait_for_roles`` polls every role; when
+any exits non-zero all others are terminated and the run fails; SIGTERM is
+forwarded to the children.
+"""
+
+from __future__ import annotations
+
+import os
+import signal
+import subprocess
+import sys
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+
+from ..utils import pathing
+from ..utils.config import config_to_plain, dump_yaml
+from .placement import plan
+
+
+@dataclass
+class RoleSpec:
+    name: str
+    argv: list[str]
+    env: dict[str, str] = field(default_factory=dict)
+    service: bool = False  # long-running server (terminated when jobs finish)
+
+
+class RoleProcess:
+    def __init__(self, spec: RoleSpec, log_dir: Path):
+        self.spec = spec
+        log_dir.mkdir(parents=True, exist_ok=True)
+        self.log = open(log_dir / f"{spec.name}.log", "ab")
+        env = {**os.environ, **spec.env}
+        self.p = subprocess.Popen(spec.argv, env=env, stdout=self.log, stderr=subprocess.STDOUT,
+                                  start_new_session=True)
+
+    def poll(self):
+        return self.p.poll()
+
+    def terminate(self, grace: float = 10.0):
+        if self.p.poll() is not None:
+            return
+        try:
+            os.killpg(self.p.pid, signal.SIGTERM)
+        except ProcessLookupError:
+            return
+        t0 = time.monotonic()
+        while self.p.poll() is None and time.monotonic() - t0 < grace:
+            time.sleep(0.1)
+        if self.p.poll() is None:
+            try:
+                os.killpg(self.p.pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+
+
+def wait_for_roles(jobs: list[RoleProcess], services: list[RoleProcess], poll: float = 1.0) -> int:
+    """Return 0 when every job exits 0; tear everything down on the first failure."""
+    try:
+        while True:
+            codes = [j.poll() for j in jobs]
+            failed = [(j.spec.name, c) for j, c in zip(jobs, codes) if c not in (None, 0)]
+            dead_services = [(s.spec.name, s.poll()) for s in services if s.poll() is not None]
+            if failed or dead_services:
+                for r in jobs + services:
+                    r.terminate()
+                print(f"role failure: {failed or dead_services}", file=sys.stderr)
+                return 1
+            if all(c == 0 for c in codes):
+                return 0
+            time.sleep(poll)
+    finally:
+        for s in services:
+            s.terminate()
+
+
+def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executable) -> tuple[list[RoleSpec], list[RoleSpec]]:
+    pl = plan(cfg)
+    base = config_to_plain(cfg)
+    services: list[RoleSpec] = []
+    if cfg.inference.mode == "vllm_http":
+        for r, (devs, port) in enumerate(zip(pl.inference_devices, pl.ports)):
+            c = dict(base)
+            c["inference"] = {**base["inference"], "http": {**base["inference"]["http"], "port": port, "ports": None}}
+            path = attempt.config_dir / f"inference_server_{r}.yaml"
+            dump_yaml(path, c)
+            services.append(RoleSpec(f"inference-server-{r}", [python, "-m", "wavelet_b200", "inference-server", "@", str(path)],
+                                     {"CUDA_VISIBLE_DEVICES": ",".join(devs)} if devs else {}, service=True))
+    trainer_cfg = attempt.config_dir / "rl_trainer.yaml"
+    dump_yaml(trainer_cfg, base)
+    n = len(pl.trainer_devices) or cfg.launcher.trainer_num_processes
+    port = cfg.deployment.trainer_master_port
+    trainer_argv = ([python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+                     "--master-addr=127.0.0.1", f"--master-port={port}", "-m", "wavelet_b200", "rl-trainer", "@", str(trainer_cfg)]
+                    if n > 1 else [python, "-m", "wavelet_b200", "rl-trainer", "@", str(trainer_cfg)])
+    env_t = {"CUDA_VISIBLE_DEVICES": ",".join(pl.trainer_devices)} if pl.trainer_devices else {}
+    env_t.update(cfg.launcher.env_vars.for_role("trainer"))
+    inf_cfg = dict(base)
+    inf_cfg["inference"] = {**base["inference"], "http": {**base["inference"]["http"], "ports": pl.ports,
+                                                          "port": pl.ports[0]}}
+    inf_path = attempt.config_dir / "rl_inference.yaml"
+    dump_yaml(inf_path, inf_cfg)
+    env_i = cfg.launcher.env_vars.for_role("orchestrator")
+    jobs = [RoleSpec("rl-trainer", trainer_argv, env_t),
+            RoleSpec("rl-inference", [python, "-m", "wavelet_b200", "rl-inference", "@", str(inf_path)], env_i)]
+    for s in services:
+        s.env.update(cfg.launcher.env_vars.for_role("inference"))
+    return services, jobs
+
+
+def run_process_launcher(cfg, argv: list[str]) -> int:
+    out = Path(cfg.output_dir)
+    pathing.validate_output_dir(out, clean=cfg.clean_output_dir, resuming=cfg.ckpt is not None and cfg.ckpt.is_resuming)
+    attempt = pathing.create_launch_attempt(out)
+    pathing.write_launch_artifacts(attempt, command="rl", argv=argv)
+    dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(cfg))
+    services, jobs = build_roles(cfg, attempt)
+    running_services = [RoleProcess(s, attempt.log_dir) for s in services]
+    if running_services:
+        from ..inference.client import endpoints, wait_healthy
+
+        try:
+            wait_healthy(endpoints(cfg), cfg.inference.http.startup_timeout_seconds)
+        except TimeoutError:
+            for s in running_services:
+                s.terminate()
+            raise
+    running_jobs = [RoleProcess(j, attempt.log_dir) for j in jobs]
+
+    def _sigterm(*_):
+        raise KeyboardInterrupt
+
+    signal.signal(signal.SIGTERM, _sigterm)
+    try:
+        return wait_for_roles(running_jobs, running_services, cfg.launcher.poll_interval_seconds)
+    except KeyboardInterrupt:
+        for r in running_jobs + running_services:
+            r.terminate()
+        return 130
