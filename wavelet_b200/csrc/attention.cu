@@ -770,12 +770,521 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+
+// ------------------------------------------------------------ dK/dV, v2
+// CTA per (kv tile of 128 keys, q head, seq): every q head of a GQA group
+// works in parallel and writes fp32 partial dK/dV; a reduction kernel sums
+// the group (or, with one q head per kv head, the CTA writes bf16 directly).
+// Queries come in tiles of 64 through a 2-stage TMA ring, and S^T / dP^T are
+// double-buffered in TMEM so the MMAs of tile i+1 overlap the softmax of i.
+//   S^T = K Q^T, dP^T = V dO^T         (M=128 keys, N=64 queries, K=128)
+//   P^T = exp2(S^T*sl2 - lse2[q]),  dS^T = P^T (dP^T - delta[q])
+//   dV += P^T dO, dK += dS^T Q         (M=128 keys, N=128 dims, K=64 queries)
+constexpr int QT = 64;
+constexpr int QSLAB = QT * 64 * 2;          // [64 rows x 64 cols] bf16 = 8 KB
+constexpr int QTILE_BYTES = 2 * QSLAB;      // [64 x 128] = 16 KB
+constexpr int PT_BYTES = TILE * QT * 2;     // [128 keys x 64 q] = 16 KB
+constexpr uint32_t IDESC_S64 = idesc_bf16_f32(128, 64, 0, 0);
+
+__device__ __forceinline__ uint64_t kmajor64_desc(uint32_t tile, int kk) {
+  return smem_desc_sw128(tile + (kk >> 2) * QSLAB + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t mnmajor64_desc(uint32_t tile, int kk) {
+  return smem_desc_sw128(tile + kk * 16 * 128, QSLAB, 1024);
+}
+__device__ __forceinline__ uint64_t pt_desc(uint32_t tile, int kk) {
+  return smem_desc_sw128(tile + kk * 32, 16, 1024);
+}
+
+struct Bwd2Params {
+  BwdParams b;
+  float* part_dk;  // [T, Hq, 128] fp32 (rep > 1)
+  float* part_dv;
+};
+
+struct __align__(8) Bwd2Smem {
+  uint64_t a_full;
+  uint64_t b_full[2];
+  uint64_t b_empty[2];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t mma_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t dkv2_smem_bytes() {
+  return 1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PT_BYTES + sizeof(Bwd2Smem) + 64;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_dkv2_kernel(const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO64,
+                         Bwd2Params p2) {
+  const BwdParams& p = p2.b;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = base;
+  uint8_t* sV = base + TILE_BYTES;
+  uint8_t* sQ[2] = {base + 2 * TILE_BYTES, base + 2 * TILE_BYTES + QTILE_BYTES};
+  uint8_t* sDO[2] = {base + 2 * TILE_BYTES + 2 * QTILE_BYTES, base + 2 * TILE_BYTES + 3 * QTILE_BYTES};
+  uint8_t* sPt = base + 2 * TILE_BYTES + 4 * QTILE_BYTES;
+  uint8_t* sdSt = sPt + PT_BYTES;
+  Bwd2Smem* s = reinterpret_cast<Bwd2Smem*>(sdSt + PT_BYTES);
+  volatile int* abort = &s->abort;
+
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int rep = p.Hq / p.Hk;
+  const int g = h / rep;
+  const int s0 = p.cu[seq];
+  const int L = p.cu[seq + 1] - s0;
+  const int n_kt = (L + TILE - 1) / TILE;
+  const int jt = n_kt - 1 - static_cast<int>(blockIdx.x);  // heaviest (earliest) tiles launch first
+  if (jt < 0) return;
+  const int k0 = jt * TILE;
+  const int i0 = k0 / QT;                  // first q tile that sees these keys (causal)
+  const int n_it = (L + QT - 1) / QT - i0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s->a_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s->b_full[i], 1);
+      mbar_init(&s->b_empty[i], 1);
+      mbar_init(&s->s_full[i], 1);
+    }
+    mbar_init(&s->p_full, 128);
+    mbar_init(&s->mma_done, 1);
+    mbar_init(&s->drain, 1);
+    s->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  const uint32_t tS[2] = {tmem, tmem + 64};
+  const uint32_t tdP[2] = {tmem + 128, tmem + 192};
+  const uint32_t tdV = tmem + 256, tdK = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s->a_full, 2 * TILE_BYTES);
+      tma_load_2d(&tmK, &s->a_full, sK, g * HD, s0 + k0);
+      tma_load_2d(&tmK, &s->a_full, sK + SLAB_BYTES, g * HD + 64, s0 + k0);
+      tma_load_2d(&tmV, &s->a_full, sV, g * HD, s0 + k0);
+      tma_load_2d(&tmV, &s->a_full, sV + SLAB_BYTES, g * HD + 64, s0 + k0);
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it & 1;
+        if (it >= 2 && !mbar_wait(&s->b_empty[st], ((it - 2) >> 1) & 1, abort, p.err, kErrTimeoutProducer)) break;
+        const int qrow = s0 + (i0 + it) * QT;
+        mbar_arrive_expect_tx(&s->b_full[st], 2 * QTILE_BYTES);
+        tma_load_2d(&tmQ64, &s->b_full[st], sQ[st], h * HD, qrow);
+        tma_load_2d(&tmQ64, &s->b_full[st], sQ[st] + QSLAB, h * HD + 64, qrow);
+        tma_load_2d(&tmDO64, &s->b_full[st], sDO[st], h * HD, qrow);
+        tma_load_2d(&tmDO64, &s->b_full[st], sDO[st] + QSLAB, h * HD + 64, qrow);
+        issued = it + 1;
+      }
+      if (*abort) {
+        for (int it = max(0, issued - 2); it < issued; ++it) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&s->b_full[it & 1], (it >> 1) & 1))
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+        }
+        const uint64_t t1 = globaltimer_ns();
+        while (!mbar_try_wait(&s->a_full, 0))
+          if (globaltimer_ns() - t1 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&s->a_full, 0, abort, p.err, kErrTimeoutMma);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      const uint32_t aPt = smem_u32(sPt), adSt = smem_u32(sdSt);
+      bool any = false;
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        if (!mbar_wait(&s->b_full[st], (it >> 1) & 1, abort, p.err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ[st]), aDO = smem_u32(sDO[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(tS[st], kmajor_desc(aK, kk), kmajor64_desc(aQ, kk), IDESC_S64, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(tdP[st], kmajor_desc(aV, kk), kmajor64_desc(aDO, kk), IDESC_S64, kk > 0);
+        umma_commit(&s->s_full[st]);
+        any = true;
+        return true;
+      };
+      if (ok && n_it > 0) ok = issue_s(0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
+        if (!mbar_wait(&s->p_full, it & 1, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ[it & 1]), aDO = smem_u32(sDO[it & 1]);
+#pragma unroll
+        for (int kk = 0; kk < QT / 16; ++kk)
+          umma_f16_ss(tdV, pt_desc(aPt, kk), mnmajor64_desc(aDO, kk), IDESC_KMN, (it > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < QT / 16; ++kk)
+          umma_f16_ss(tdK, pt_desc(adSt, kk), mnmajor64_desc(aQ, kk), IDESC_KMN, (it > 0 || kk > 0));
+        umma_commit(&s->b_empty[it & 1]);
+        umma_commit(&s->mma_done);
+      }
+      if (any) {
+        umma_commit(&s->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&s->drain, 0))
+          if (globaltimer_ns() - t0 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // key row
+    const int kj = k0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int st = it & 1;
+      const int q0 = (i0 + it) * QT;
+      const float* lse_row = p.lse + (int64_t)h * p.T + s0 + q0;
+      const float* dlt_row = p.delta + (int64_t)h * p.T + s0 + q0;
+      const int qlim = L - q0;
+      if (!mbar_wait_warp(&s->s_full[st], (it >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      float pt[64], dp[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS[st] + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pt[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
+        tmem_ld_32x32b_x32(tdP[st] + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dp[c * 32 + e] = __uint_as_float(v[e]);
+      }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int qi = q0 + c;
+        const bool valid = (kj <= qi) && (c < qlim) && (kj < L);
+        const float pv = valid ? exp2f(pt[c] - __ldg(lse_row + c) * LOG2E) : 0.f;
+        pt[c] = pv;
+        dp[c] = pv * (dp[c] - (valid ? __ldg(dlt_row + c) : 0.f));
+      }
+      if (it > 0 && !mbar_wait_warp(&s->mma_done, (it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        w.x = pack_bf16(pt[c * 8 + 0], pt[c * 8 + 1]);
+        w.y = pack_bf16(pt[c * 8 + 2], pt[c * 8 + 3]);
+        w.z = pack_bf16(pt[c * 8 + 4], pt[c * 8 + 5]);
+        w.w = pack_bf16(pt[c * 8 + 6], pt[c * 8 + 7]);
+        st_tile_chunk(sPt, r, c, w);
+        uint4 d;
+        d.x = pack_bf16(dp[c * 8 + 0], dp[c * 8 + 1]);
+        d.y = pack_bf16(dp[c * 8 + 2], dp[c * 8 + 3]);
+        d.z = pack_bf16(dp[c * 8 + 4], dp[c * 8 + 5]);
+        d.w = pack_bf16(dp[c * 8 + 6], dp[c * 8 + 7]);
+        st_tile_chunk(sdSt, r, c, d);
+      }
+      fence_proxy_async_shared();
+      tc_fence_before();
+      mbar_arrive(&s->p_full);
+    }
+    if (ok && n_it > 0 && mbar_wait_warp(&s->mma_done, (n_it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      const bool valid = kj < L;
+      if (rep == 1) {
+        store_row128(tdV + lane_off, p.dv + ((int64_t)(s0 + kj) * p.Hk + g) * HD, 1.f, valid);
+        store_row128(tdK + lane_off, p.dk + ((int64_t)(s0 + kj) * p.Hk + g) * HD, p.scale, valid);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32], w[32];
+          tmem_ld_32x32b_x32(tdV + lane_off + c * 32, v);
+          tmem_ld_32x32b_x32(tdK + lane_off + c * 32, w);
+          tmem_wait_ld();
+          if (valid) {
+            float4* dv4 = reinterpret_cast<float4*>(p2.part_dv + ((int64_t)(s0 + kj) * p.Hq + h) * HD + c * 32);
+            float4* dk4 = reinterpret_cast<float4*>(p2.part_dk + ((int64_t)(s0 + kj) * p.Hq + h) * HD + c * 32);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              dv4[u] = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]), __uint_as_float(v[4 * u + 2]),
+                                   __uint_as_float(v[4 * u + 3]));
+              dk4[u] = make_float4(__uint_as_float(w[4 * u]), __uint_as_float(w[4 * u + 1]), __uint_as_float(w[4 * u + 2]),
+                                   __uint_as_float(w[4 * u + 3]));
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dk/dv[t, g] = sum over the group's q heads of the fp32 partials (dK also
+// times the softmax scale).  One warp per (token, kv head); 4 dims per lane.
+__global__ void attn_dkv_reduce_kernel(const float* __restrict__ part_dk, const float* __restrict__ part_dv,
+                                       __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int T, int Hq,
+                                       int Hk, float scale) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= T * Hk) return;
+  const int t = w / Hk, g = w - t * Hk;
+  const int rep = Hq / Hk;
+  float4 ak = make_float4(0.f, 0.f, 0.f, 0.f), av = ak;
+  for (int r = 0; r < rep; ++r) {
+    const int64_t off = ((int64_t)t * Hq + g * rep + r) * HD;
+    const float4 k4 = reinterpret_cast<const float4*>(part_dk + off)[lane];
+    const float4 v4 = reinterpret_cast<const float4*>(part_dv + off)[lane];
+    ak.x += k4.x; ak.y += k4.y; ak.z += k4.z; ak.w += k4.w;
+    av.x += v4.x; av.y += v4.y; av.z += v4.z; av.w += v4.w;
+  }
+  const int64_t o = ((int64_t)t * Hk + g) * HD;
+  uint2 kk, vv;
+  kk.x = pack_bf16(ak.x * scale, ak.y * scale);
+  kk.y = pack_bf16(ak.z * scale, ak.w * scale);
+  vv.x = pack_bf16(av.x, av.y);
+  vv.y = pack_bf16(av.z, av.w);
+  reinterpret_cast<uint2*>(dk + o)[lane] = kk;
+  reinterpret_cast<uint2*>(dv + o)[lane] = vv;
+}
+
+
+// ---------------------------------------------------------------- dQ, v2
+// CTA per (128-query tile, q head, seq); keys in tiles of 64 through a
+// 3-stage TMA ring; S / dP double-buffered in TMEM so the next tile's MMAs
+// overlap this tile's softmax.
+//   S = Q K^T, dP = dO V^T   (M=128 q, N=64 keys, K=128)
+//   dS = P (dP - delta)      (thread = query row)
+//   dQ += dS K               (M=128 q, N=128 dims, K=64 keys)
+constexpr int KT = 64;
+constexpr int KV_STAGES = 3;
+constexpr int DS_BYTES = TILE * KT * 2;  // [128 q x 64 keys] = 16 KB
+
+constexpr size_t dq2_smem_bytes() {
+  return 1024 + 2 * TILE_BYTES + KV_STAGES * 2 * QTILE_BYTES + DS_BYTES + sizeof(Bwd2Smem) + 64 + 64;
+}
+
+struct __align__(8) Dq2Smem {
+  uint64_t a_full;
+  uint64_t kv_full[KV_STAGES];
+  uint64_t kv_empty[KV_STAGES];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t ds_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_dq2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK64,
+                        const __grid_constant__ CUtensorMap tmV64, const __grid_constant__ CUtensorMap tmDO,
+                        BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;
+  uint8_t* sDO = base + TILE_BYTES;
+  uint8_t* sKV = base + 2 * TILE_BYTES;  // stage st: K at +st*2*QTILE, V at +QTILE
+  uint8_t* sdS = sKV + KV_STAGES * 2 * QTILE_BYTES;
+  Dq2Smem* s = reinterpret_cast<Dq2Smem*>(sdS + DS_BYTES);
+  volatile int* abort = &s->abort;
+
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int g = h / (p.Hq / p.Hk);
+  const int s0 = p.cu[seq];
+  const int L = p.cu[seq + 1] - s0;
+  const int n_qt = (L + TILE - 1) / TILE;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
+  if (qt < 0) return;
+  const int q0 = qt * TILE;
+  const int n_kv = (min(L, q0 + TILE) + KT - 1) / KT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s->a_full, 1);
+    for (int i = 0; i < KV_STAGES; ++i) {
+      mbar_init(&s->kv_full[i], 1);
+      mbar_init(&s->kv_empty[i], 1);
+    }
+    mbar_init(&s->s_full[0], 1);
+    mbar_init(&s->s_full[1], 1);
+    mbar_init(&s->p_full, 128);
+    mbar_init(&s->ds_done, 1);
+    mbar_init(&s->drain, 1);
+    s->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  const uint32_t tS[2] = {tmem, tmem + 64};
+  const uint32_t tdP[2] = {tmem + 128, tmem + 192};
+  const uint32_t tdQ = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s->a_full, 2 * TILE_BYTES);
+      tma_load_2d(&tmQ, &s->a_full, sQ, h * HD, s0 + q0);
+      tma_load_2d(&tmQ, &s->a_full, sQ + SLAB_BYTES, h * HD + 64, s0 + q0);
+      tma_load_2d(&tmDO, &s->a_full, sDO, h * HD, s0 + q0);
+      tma_load_2d(&tmDO, &s->a_full, sDO + SLAB_BYTES, h * HD + 64, s0 + q0);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % KV_STAGES;
+        if (j >= KV_STAGES && !mbar_wait(&s->kv_empty[st], ((j - KV_STAGES) / KV_STAGES) & 1, abort, p.err, kErrTimeoutProducer)) break;
+        uint8_t* kd = sKV + st * 2 * QTILE_BYTES;
+        uint8_t* vd = kd + QTILE_BYTES;
+        const int krow = s0 + j * KT;
+        mbar_arrive_expect_tx(&s->kv_full[st], 2 * QTILE_BYTES);
+        tma_load_2d(&tmK64, &s->kv_full[st], kd, g * HD, krow);
+        tma_load_2d(&tmK64, &s->kv_full[st], kd + QSLAB, g * HD + 64, krow);
+        tma_load_2d(&tmV64, &s->kv_full[st], vd, g * HD, krow);
+        tma_load_2d(&tmV64, &s->kv_full[st], vd + QSLAB, g * HD + 64, krow);
+        issued = j + 1;
+      }
+      if (*abort) {
+        for (int j = max(0, issued - KV_STAGES); j < issued; ++j) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&s->kv_full[j % KV_STAGES], (j / KV_STAGES) & 1))
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+        }
+        const uint64_t t1 = globaltimer_ns();
+        while (!mbar_try_wait(&s->a_full, 0))
+          if (globaltimer_ns() - t1 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&s->a_full, 0, abort, p.err, kErrTimeoutMma);
+      const uint32_t aQ = smem_u32(sQ), aDO = smem_u32(sDO), adS = smem_u32(sdS);
+      bool any = false;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&s->kv_full[st], (j / KV_STAGES) & 1, abort, p.err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sKV + st * 2 * QTILE_BYTES), aV = aK + QTILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(tS[j & 1], kmajor_desc(aQ, kk), kmajor64_desc(aK, kk), IDESC_S64, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16_ss(tdP[j & 1], kmajor_desc(aDO, kk), kmajor64_desc(aV, kk), IDESC_S64, kk > 0);
+        umma_commit(&s->s_full[j & 1]);
+        any = true;
+        return true;
+      };
+      if (ok && n_kv > 0) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
+        if (!mbar_wait(&s->p_full, j & 1, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const int st = j % KV_STAGES;
+        const uint32_t aK = smem_u32(sKV + st * 2 * QTILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)
+          umma_f16_ss(tdQ, pt_desc(adS, kk), mnmajor64_desc(aK, kk), IDESC_KMN, (j > 0 || kk > 0));
+        umma_commit(&s->kv_empty[st]);
+        umma_commit(&s->ds_done);
+      }
+      if (any) {
+        umma_commit(&s->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&s->drain, 0))
+          if (globaltimer_ns() - t0 > kWaitBudgetNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const bool vq = qi < L;
+    const float lse2 = vq ? p.lse[(int64_t)h * p.T + s0 + qi] * LOG2E : INFINITY;
+    const float dlt = vq ? p.delta[(int64_t)h * p.T + s0 + qi] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait_warp(&s->s_full[j & 1], (j >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      float pr[64], dp[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS[j & 1] + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pr[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
+        tmem_ld_32x32b_x32(tdP[j & 1] + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dp[c * 32 + e] = __uint_as_float(v[e]);
+      }
+      const int kb = j * KT;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int kj = kb + c;
+        const bool valid = (kj <= qi) && (kj < L) && vq;
+        const float pv = valid ? exp2f(pr[c] - lse2) : 0.f;
+        pr[c] = pv * (dp[c] - dlt);
+      }
+      if (j > 0 && !mbar_wait_warp(&s->ds_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        w.x = pack_bf16(pr[c * 8 + 0], pr[c * 8 + 1]);
+        w.y = pack_bf16(pr[c * 8 + 2], pr[c * 8 + 3]);
+        w.z = pack_bf16(pr[c * 8 + 4], pr[c * 8 + 5]);
+        w.w = pack_bf16(pr[c * 8 + 6], pr[c * 8 + 7]);
+        st_tile_chunk(sdS, r, c, w);
+      }
+      fence_proxy_async_shared();
+      tc_fence_before();
+      mbar_arrive(&s->p_full);
+    }
+    if (ok && n_kv > 0 && mbar_wait_warp(&s->ds_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      store_row128(tdQ + lane_off, p.dq + ((int64_t)(s0 + qi) * p.Hq + h) * HD, p.scale, vq);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace attn
 
 static CUtensorMap head_map(const void* base, int64_t row_stride, int heads, int T) {
   // 2-D view: T rows x (heads*128) columns, pitch row_stride elements, box 64 x 128.
   return make_tmap_2d(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)heads * 128, (uint64_t)T,
                       (uint64_t)row_stride, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+static CUtensorMap head_map64(const void* base, int64_t row_stride, int heads, int T) {
+  return make_tmap_2d(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)heads * 128, (uint64_t)T,
+                      (uint64_t)row_stride, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
@@ -815,12 +1324,15 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   using namespace attn;
   const AttnArgs& a = b.f;
   if (a.head_dim != 128) throw std::runtime_error("wavelet_b200 attention: head_dim must be 128");
+  const int rep = a.Hq / a.Hk;
+  if (rep > 1 && (!b.part_dk || !b.part_dv))
+    throw std::runtime_error("wavelet_b200 attention: GQA backward needs fp32 partial buffers");
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr[64] = {false};
   if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dkv_smem_bytes());
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq_smem_bytes());
+    cudaFuncSetAttribute(attn_bwd_dkv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dkv2_smem_bytes());
+    cudaFuncSetAttribute(attn_bwd_dq2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq2_smem_bytes());
     attr[dev & 63] = true;
   }
   {
@@ -834,7 +1346,10 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   CUtensorMap mk = head_map(a.k, a.k_row, a.Hk, a.T);
   CUtensorMap mv = head_map(a.v, a.v_row, a.Hk, a.T);
   CUtensorMap mdo = head_map(b.dout, (int64_t)a.Hq * 128, a.Hq, a.T);
-  BwdParams p;
+  CUtensorMap mq64 = head_map64(a.q, a.q_row, a.Hq, a.T);
+  CUtensorMap mdo64 = head_map64(b.dout, (int64_t)a.Hq * 128, a.Hq, a.T);
+  Bwd2Params p2;
+  BwdParams& p = p2.b;
   p.lse = a.lse;
   p.delta = b.delta;
   p.cu = a.cu_seqlens;
@@ -847,9 +1362,19 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   p.scale = a.scale;
   p.scale_log2 = a.scale * LOG2E;
   p.err = error_word(dev);
+  p2.part_dk = b.part_dk;
+  p2.part_dv = b.part_dv;
   const int nt = (a.max_seqlen + TILE - 1) / TILE;
-  attn_bwd_dkv_kernel<<<dim3(nt, a.Hk, a.nseq), NUM_THREADS, dkv_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
-  attn_bwd_dq_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
+  attn_bwd_dkv2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
+  CUtensorMap mk64 = head_map64(a.k, a.k_row, a.Hk, a.T);
+  CUtensorMap mv64 = head_map64(a.v, a.v_row, a.Hk, a.T);
+  attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p);
+  if (rep > 1) {
+    const int warps = 8;
+    const int64_t work = (int64_t)a.T * a.Hk;
+    attn_dkv_reduce_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
+        b.part_dk, b.part_dv, p.dk, p.dv, a.T, a.Hq, a.Hk, a.scale);
+  }
 }
 
 // Same launch sequence as attn_bwd, with the Delta scratch (b.delta) and the

@@ -25,6 +25,8 @@ struct AttnBwdArgs {
   void* dk = nullptr;          // [T, Hk, 128] contiguous
   void* dv = nullptr;          // [T, Hk, 128] contiguous
   float* delta = nullptr;      // [Hq, T] scratch
+  float* part_dk = nullptr;    // [T, Hq, 128] fp32 scratch (GQA: per-q-head partials)
+  float* part_dv = nullptr;
 };
 
 void attn_fwd(const AttnArgs& a, cudaStream_t stream);

@@ -355,6 +355,13 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, 
   b.dv = dv.data_ptr();
   at::Tensor delta = at::empty({b.f.Hq, b.f.T}, q.options().dtype(at::kFloat));
   b.delta = delta.data_ptr<float>();
+  at::Tensor pdk, pdv;
+  if (b.f.Hq != b.f.Hk) {
+    pdk = at::empty({b.f.T, b.f.Hq, 128}, q.options().dtype(at::kFloat));
+    pdv = at::empty({b.f.T, b.f.Hq, 128}, q.options().dtype(at::kFloat));
+    b.part_dk = pdk.data_ptr<float>();
+    b.part_dv = pdv.data_ptr<float>();
+  }
   if (b.f.T == 0 || b.f.nseq == 0) return;
   wb::attn_bwd(b, cur_stream());
 }
