@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--micro-batches", type=int, default=8, help="micro-batches of 1 sequence per GPU per step")
     p.add_argument("--layers", type=int, default=None, help="(debug only) override layer count; invalidates the number")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
+                   help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
     return p.parse_args()
 
 
@@ -128,6 +130,7 @@ def main():
     from wavelet_b200.models.qwen import build_model
     from wavelet_b200.ops import _ext
     from wavelet_b200.parallel.dist import destroy_distributed, init_distributed
+    from wavelet_b200.parallel.fabric import maybe_fabric
     from wavelet_b200.parallel.zero import AdamWHyper
     from wavelet_b200.data.fake import synthetic_sft_microbatches
     from wavelet_b200.trainer.engine import Engine
@@ -141,9 +144,10 @@ def main():
 
     overrides = {"num_layers": args.layers} if args.layers else None
     cfg = resolve_arch(args.model, overrides)
-    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234)
+    fabric = maybe_fabric(N, rank, dev) if args.comm == "fabric" else None
+    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234, fabric=fabric)
     hyper = AdamWHyper(lr=1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, max_grad_norm=1.0)
-    engine = Engine(model, hyper, dp_group=None, dp_world=N)
+    engine = Engine(model, hyper, dp_group=None, dp_world=N, fabric=fabric)
     stepper = SFTStepper(engine, dev)
 
     S, mb = args.seq_len, args.micro_batches
@@ -231,6 +235,8 @@ def main():
                 "grad_accum": mb,
                 "parallelism": f"dp{N}",
                 "optimizer": "AdamW (fp32 master, sharded)",
+                "optimizer_comm": ("fused peer-memory RS+AdamW+AG kernels" if fabric is not None
+                                   else ("NCCL reduce-scatter/all-gather" if N > 1 else "none (1 GPU)")),
                 "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",
             },
             "mfu": value * mfu_flops / (N * 2.25e15),
@@ -240,6 +246,8 @@ def main():
             "e2e": e2e,
         }
         print(json.dumps(rec), flush=True)
+    if fabric is not None:
+        fabric.close()
     destroy_distributed()
     return 0
 

@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include "attention.h"
+#include "comm.h"
 #include "decode.h"
 #include "gemm.h"
 #include "kernels.h"
@@ -89,6 +90,68 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
   wb::gemm_bf16(g, cur_stream());
 }
 
+// Extended GEMM: optional second operand pair (LoRA-fused linear) and/or an
+// NF4 B operand (QLoRA base weight).  b is ignored when q is given.
+void gemm_ex(const at::Tensor& a, bool a_mn, const c10::optional<at::Tensor>& b, bool b_mn, at::Tensor& c,
+             int64_t N, int64_t epi, double alpha, const c10::optional<at::Tensor>& bias,
+             const c10::optional<at::Tensor>& res, const c10::optional<at::Tensor>& a2,
+             const c10::optional<at::Tensor>& b2, const c10::optional<at::Tensor>& q,
+             const c10::optional<at::Tensor>& q_absmax, int64_t q_rows, int64_t q_cols,
+             const std::vector<double>& lut) {
+  check_bf16(a, "a");
+  check_cuda(c, "c");
+  const c10::cuda::CUDAGuard guard(a.device());
+  wb::GemmArgs g;
+  g.A = a.data_ptr();
+  g.lda = ld_of(a, "a");
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.M = a_mn ? a.size(1) : a.size(0);
+  g.K = a_mn ? a.size(0) : a.size(1);
+  g.N = N;
+  if (q) {
+    WB_CHECK(q->scalar_type() == at::kByte && q->is_cuda() && q->is_contiguous(), "gemm_ex: q must be contiguous uint8 CUDA");
+    WB_CHECK(q_absmax && q_absmax->scalar_type() == at::kFloat && q_absmax->is_contiguous(), "gemm_ex: q_absmax fp32");
+    WB_CHECK(lut.size() == 16, "gemm_ex: lut must have 16 entries");
+    WB_CHECK(q->numel() == q_rows * q_cols / 2 && q_absmax->numel() == q_rows * q_cols / 64, "gemm_ex: NF4 sizes");
+    WB_CHECK((reinterpret_cast<uintptr_t>(q->data_ptr()) & 15) == 0, "gemm_ex: q must be 16-byte aligned");
+    g.q = q->data_ptr<uint8_t>();
+    g.q_absmax = q_absmax->data_ptr<float>();
+    g.q_rows = q_rows;
+    g.q_cols = q_cols;
+    for (int i = 0; i < 16; ++i) g.q_lut[i] = static_cast<float>(lut[i]);
+  } else {
+    WB_CHECK(b.has_value(), "gemm_ex: b or q required");
+    check_bf16(*b, "b");
+    g.B = b->data_ptr();
+    g.ldb = ld_of(*b, "b");
+  }
+  if (a2) {
+    WB_CHECK(b2.has_value(), "gemm_ex: a2 needs b2");
+    check_bf16(*a2, "a2");
+    check_bf16(*b2, "b2");
+    g.A2 = a2->data_ptr();
+    g.lda2 = ld_of(*a2, "a2");
+    g.B2 = b2->data_ptr();
+    g.ldb2 = ld_of(*b2, "b2");
+    g.K2 = a_mn ? a2->size(0) : a2->size(1);
+  }
+  g.C = c.data_ptr();
+  g.ldc = ld_of(c, "c");
+  g.epi = static_cast<int>(epi);
+  g.alpha = static_cast<float>(alpha);
+  if (bias) {
+    check_bf16(*bias, "bias");
+    g.bias = bias->data_ptr();
+  }
+  if (res) {
+    check_bf16(*res, "res");
+    g.res = res->data_ptr();
+    g.ldr = ld_of(*res, "res");
+  }
+  wb::gemm_bf16(g, cur_stream());
+}
+
 // Grouped (MoE expert) GEMM.  mode 1: C = A B_g^T with g = tile_group[m_tile];
 // mode 2: C[g*M:(g+1)*M] (op)= A_g^T B_g over token segments (k_start, k_len).
 void gemm_grouped(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& c, int64_t mode,
@@ -124,6 +187,85 @@ void gemm_grouped(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn
   if (k_len) g.k_len = k_len->data_ptr<int>();
   g.groups = static_cast<int>(groups);
   wb::gemm_bf16(g, cur_stream());
+}
+
+// ------------------------------------------------------------ peer fabric
+int64_t fabric_malloc_(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  return reinterpret_cast<int64_t>(wb::fabric_malloc(static_cast<size_t>(nbytes)));
+}
+void fabric_free_(int64_t p) { wb::fabric_free(reinterpret_cast<void*>(p)); }
+py::bytes fabric_export_(int64_t p) {
+  unsigned char h[64];
+  wb::fabric_export(reinterpret_cast<void*>(p), h);
+  return py::bytes(reinterpret_cast<const char*>(h), 64);
+}
+int64_t fabric_import_(const std::string& h, int64_t device) {
+  WB_CHECK(h.size() == 64, "fabric_import: handle must be 64 bytes");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  return reinterpret_cast<int64_t>(wb::fabric_import(reinterpret_cast<const unsigned char*>(h.data())));
+}
+void fabric_close_(int64_t p) { wb::fabric_close(reinterpret_cast<void*>(p)); }
+
+// A tensor view of fabric memory (the fabric owns the allocation).
+at::Tensor from_ptr(int64_t p, int64_t numel, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return at::from_blob(reinterpret_cast<void*>(p), {numel}, [](void*) {}, opts);
+}
+
+inline wb::PeerPtrs peers_of(const std::vector<int64_t>& v, int world) {
+  WB_CHECK(world >= 1 && world <= wb::kMaxPeers && (int)v.size() >= world, "bad peer pointer list");
+  wb::PeerPtrs pp{};
+  for (int i = 0; i < world; ++i) pp.p[i] = reinterpret_cast<void*>(v[i]);
+  return pp;
+}
+
+void peer_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t world, int64_t epoch, int64_t slot_base,
+                  double budget_s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  wb::peer_barrier(peers_of(pads, (int)world), (int)rank, (int)world, static_cast<uint32_t>(epoch), (int)slot_base,
+                   static_cast<uint64_t>(budget_s * 1e9), wb::error_word(dev), cur_stream());
+}
+
+void rs_sum_sumsq(const std::vector<int64_t>& grads, int64_t world, int64_t lo, int64_t n, double scale,
+                  at::Tensor& out, at::Tensor& stats) {
+  check_f32(out, "out");
+  check_f32(stats, "stats");
+  WB_CHECK(out.numel() >= n, "rs_sum_sumsq: out too small");
+  wb::rs_sum_sumsq(peers_of(grads, (int)world), (int)world, lo, n, (float)scale, out.data_ptr<float>(),
+                   stats.data_ptr<float>(), cur_stream());
+}
+
+void norm_exchange(const std::vector<int64_t>& pads, int64_t rank, int64_t world, int64_t epoch,
+                   const at::Tensor& stats, double max_norm, at::Tensor& tot, double budget_s) {
+  check_f32(stats, "stats");
+  check_f32(tot, "tot");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  wb::norm_exchange(peers_of(pads, (int)world), (int)rank, (int)world, static_cast<uint32_t>(epoch),
+                    stats.data_ptr<float>(), (float)max_norm, tot.data_ptr<float>(),
+                    static_cast<uint64_t>(budget_s * 1e9), wb::error_word(dev), cur_stream());
+}
+
+void adamw_allgather(const std::vector<int64_t>& compute, int64_t world, int64_t lo, at::Tensor& master,
+                     const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2, double eps,
+                     double wd, int64_t step, const at::Tensor& tot) {
+  check_f32(master, "master");
+  check_f32(g, "g");
+  check_f32(m, "m");
+  check_f32(v, "v");
+  check_f32(tot, "tot");
+  const float bc1 = 1.f - std::pow((float)b1, (float)step);
+  const float bc2 = 1.f - std::pow((float)b2, (float)step);
+  wb::adamw_allgather(peers_of(compute, (int)world), (int)world, lo, master.data_ptr<float>(), g.data_ptr<float>(),
+                      m.data_ptr<float>(), v.data_ptr<float>(), master.numel(), (float)lr, (float)b1, (float)b2,
+                      (float)eps, (float)wd, bc1, bc2, tot.data_ptr<float>(), cur_stream());
+}
+
+void allgather_bf16(const std::vector<int64_t>& dst, int64_t world, int64_t lo, const at::Tensor& src) {
+  check_bf16(src, "src");
+  wb::allgather_bf16(peers_of(dst, (int)world), (int)world, lo, src.data_ptr(), src.numel(), cur_stream());
 }
 
 void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
@@ -438,6 +580,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b_mn"), py::arg("c"), py::arg("epi") = 0, py::arg("alpha") = 1.0,
         py::arg("bias") = py::none(), py::arg("res") = py::none());
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_ex", &gemm_ex);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
@@ -456,6 +599,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append", &kv_append);
   m.def("decode_attention", &decode_attention);
   m.def("sample_tokens", &sample_tokens);
+  m.def("fabric_malloc", &fabric_malloc_);
+  m.def("fabric_free", &fabric_free_);
+  m.def("fabric_export", &fabric_export_);
+  m.def("fabric_import", &fabric_import_);
+  m.def("fabric_close", &fabric_close_);
+  m.def("from_ptr", &from_ptr);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("rs_sum_sumsq", &rs_sum_sumsq);
+  m.def("norm_exchange", &norm_exchange);
+  m.def("adamw_allgather", &adamw_allgather);
+  m.def("allgather_bf16", &allgather_bf16);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.attr("EPI_BF16") = (int)wb::kEpiBF16;

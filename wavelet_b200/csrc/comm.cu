@@ -1,0 +1,329 @@
+// Peer-memory fabric (CUDA IPC) and the fused reduce-scatter -> AdamW ->
+// all-gather optimizer step over NVLink.  Layout and protocol: comm.h.
+//
+// Roofline of the fused step on W ranks with a flat fp32 gradient of P
+// elements: each rank pulls (W-1)/W * 4P bytes of gradient over NVLink and
+// pushes (W-1)/W * 2P bytes of bf16 parameters, i.e. the same bytes as NCCL's
+// reduce-scatter + all-gather, but the sum, the norm, the clip, the AdamW
+// update and the bf16 cast ride along with the transfer instead of running
+// as separate passes over HBM.
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "comm.h"
+#include "common.cuh"
+
+namespace wb {
+namespace comm {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(float* p, float v) {
+  asm volatile("st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float ld_relaxed_sys(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until *p has reached `epoch` (wrap-safe); false when the budget ran out.
+__device__ bool wait_epoch(const uint32_t* p, uint32_t epoch, uint64_t budget_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (static_cast<int32_t>(ld_acquire_sys(p) - epoch) < 0) {
+    if (globaltimer_ns() - t0 > budget_ns) return false;
+    __nanosleep(100);
+  }
+  return true;
+}
+
+// One thread signals every peer, then waits for every peer.  A single thread
+// keeps the acquire/release reasoning local; the kernel is latency-bound
+// anyway (a few microseconds over NVSwitch).
+__global__ void barrier_kernel(PeerPtrs pads, int rank, int world, uint32_t epoch, int slot_base,
+                               uint64_t budget_ns, int* err) {
+  if (threadIdx.x != 0) return;
+  // Cumulative fence: everything this GPU wrote before this kernel (earlier
+  // kernels on the stream) is ordered before the signal stores.
+  __threadfence_system();
+  for (int t = 0; t < world; ++t) st_release_sys(static_cast<uint32_t*>(pads.p[t]) + slot_base + rank, epoch);
+  const uint32_t* mine = static_cast<const uint32_t*>(pads.p[rank]) + slot_base;
+  for (int t = 0; t < world; ++t) {
+    if (!wait_epoch(mine + t, epoch, budget_ns)) {
+      atomicOr(err, kErrTimeoutPeer);
+      return;
+    }
+  }
+  __threadfence_system();
+}
+
+__global__ void norm_exchange_kernel(PeerPtrs pads, int rank, int world, uint32_t epoch, const float* stats,
+                                     float max_norm, float* tot, uint64_t budget_ns, int* err) {
+  if (threadIdx.x != 0) return;
+  const float ss = stats[0], bad = stats[1];
+  __threadfence_system();
+  for (int t = 0; t < world; ++t) {
+    uint32_t* pad = static_cast<uint32_t*>(pads.p[t]);
+    float* vals = reinterpret_cast<float*>(pad + kPadNormVals) + 2 * rank;
+    st_relaxed_sys(vals, ss);
+    st_relaxed_sys(vals + 1, bad);
+    st_release_sys(pad + kPadNormFlag + rank, epoch);  // release: orders the two value stores
+  }
+  const uint32_t* mine = static_cast<const uint32_t*>(pads.p[rank]);
+  const float* mvals = reinterpret_cast<const float*>(mine + kPadNormVals);
+  float s = 0.f, b = 0.f;
+  bool ok = true;
+  for (int t = 0; t < world; ++t) {  // fixed order: identical totals on every rank
+    if (!wait_epoch(mine + kPadNormFlag + t, epoch, budget_ns)) {
+      atomicOr(err, kErrTimeoutPeer);
+      ok = false;
+      break;
+    }
+    s += ld_relaxed_sys(mvals + 2 * t);
+    b += ld_relaxed_sys(mvals + 2 * t + 1);
+  }
+  if (!ok) b = 1.f;  // a missing peer: treat as non-finite so no rank updates from a partial norm
+  float factor = 1.f;
+  if (max_norm > 0.f) factor = fminf(1.f, max_norm / (sqrtf(s) + 1e-6f));
+  tot[0] = s;
+  tot[1] = b;
+  tot[2] = factor;
+}
+
+__device__ __forceinline__ void add4(float4& a, const float4& b) {
+  a.x += b.x;
+  a.y += b.y;
+  a.z += b.z;
+  a.w += b.w;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  }
+  return v;
+}
+
+// Each thread owns 8 consecutive floats (two 16-byte loads per rank, all
+// ranks' loads issued before the adds so W*2 requests are in flight).
+template <int W>
+__global__ void __launch_bounds__(512) rs_kernel(PeerPtrs grads, int64_t lo, int64_t n8, float scale, float* out,
+                                                 float* stats) {
+  __shared__ float red[32];
+  float ss = 0.f, bad = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 x0[W], x1[W];
+#pragma unroll
+    for (int r = 0; r < W; ++r) {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(grads.p[r]) + lo) + 2 * i;
+      x0[r] = src[0];
+      x1[r] = src[1];
+    }
+    float4 a0 = x0[0], a1 = x1[0];
+#pragma unroll
+    for (int r = 1; r < W; ++r) {
+      add4(a0, x0[r]);
+      add4(a1, x1[r]);
+    }
+    float* e0 = &a0.x;
+    float* e1 = &a1.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      e0[j] *= scale;
+      e1[j] *= scale;
+      ss += e0[j] * e0[j] + e1[j] * e1[j];
+      bad += (isfinite(e0[j]) ? 0.f : 1.f) + (isfinite(e1[j]) ? 0.f : 1.f);
+    }
+    float4* dst = reinterpret_cast<float4*>(out) + 2 * i;
+    dst[0] = a0;
+    dst[1] = a1;
+  }
+  ss = block_sum(ss, red);
+  bad = block_sum(bad, red);
+  if (threadIdx.x == 0) {
+    atomicAdd(stats, ss);
+    atomicAdd(stats + 1, bad);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int W>
+__global__ void __launch_bounds__(256) adamw_ag_kernel(PeerPtrs compute, int64_t lo, float* __restrict__ master,
+                                                       const float* __restrict__ g, float* __restrict__ m,
+                                                       float* __restrict__ v, int64_t n8, float lr, float b1, float b2,
+                                                       float eps, float wd, float bc1, float bc2, const float* tot) {
+  const bool skip = tot[1] > 0.f;
+  const float gs = tot[2];
+  const float step = lr / bc1;
+  const float rbc2 = rsqrtf(bc2);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 p[2], gg[2], mm[2], vv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      p[h] = reinterpret_cast<const float4*>(master)[2 * i + h];
+      gg[h] = reinterpret_cast<const float4*>(g)[2 * i + h];
+      mm[h] = reinterpret_cast<const float4*>(m)[2 * i + h];
+      vv[h] = reinterpret_cast<const float4*>(v)[2 * i + h];
+    }
+    if (!skip) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float* ap = &p[h].x;
+        float* ag = &gg[h].x;
+        float* am = &mm[h].x;
+        float* av = &vv[h].x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gj = ag[j] * gs;
+          am[j] = b1 * am[j] + (1.f - b1) * gj;
+          av[j] = b2 * av[j] + (1.f - b2) * gj * gj;
+          ap[j] = ap[j] * (1.f - lr * wd);
+          ap[j] -= step * am[j] / (sqrtf(av[j]) * rbc2 + eps);
+        }
+        reinterpret_cast<float4*>(master)[2 * i + h] = p[h];
+        reinterpret_cast<float4*>(m)[2 * i + h] = mm[h];
+        reinterpret_cast<float4*>(v)[2 * i + h] = vv[h];
+      }
+    }
+    uint4 w;
+    w.x = pack2(p[0].x, p[0].y);
+    w.y = pack2(p[0].z, p[0].w);
+    w.z = pack2(p[1].x, p[1].y);
+    w.w = pack2(p[1].z, p[1].w);
+#pragma unroll
+    for (int r = 0; r < W; ++r)
+      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(compute.p[r]) + lo)[i] = w;
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(256) ag_kernel(PeerPtrs dst, int64_t lo, const uint4* __restrict__ src, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 w = src[i];
+#pragma unroll
+    for (int r = 0; r < W; ++r) reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst.p[r]) + lo)[i] = w;
+  }
+}
+
+inline int grid_for(int64_t work, int threads, int cap) {
+  int64_t b = (work + threads - 1) / threads;
+  if (b < 1) b = 1;
+  return static_cast<int>(b < cap ? b : cap);
+}
+
+}  // namespace comm
+
+static void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string("wavelet_b200 fabric: ") + what + ": " + cudaGetErrorString(e));
+}
+
+void* fabric_malloc(size_t bytes) {
+  void* p = nullptr;
+  check(cudaMalloc(&p, bytes), "cudaMalloc");
+  check(cudaMemset(p, 0, bytes), "cudaMemset");
+  return p;
+}
+
+void fabric_free(void* p) {
+  if (p) cudaFree(p);
+}
+
+void fabric_export(void* p, unsigned char out[64]) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  check(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  std::memcpy(out, &h, 64);
+}
+
+void* fabric_import(const unsigned char in[64]) {
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, in, 64);
+  void* p = nullptr;
+  check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return p;
+}
+
+void fabric_close(void* p) {
+  if (p) cudaIpcCloseMemHandle(p);
+}
+
+static void check_world(int world) {
+  if (world < 1 || world > kMaxPeers) throw std::runtime_error("wavelet_b200 fabric: world size must be 1..8");
+}
+
+void peer_barrier(const PeerPtrs& pads, int rank, int world, uint32_t epoch, int slot_base, uint64_t budget_ns,
+                  int* err, cudaStream_t st) {
+  check_world(world);
+  comm::barrier_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, slot_base, budget_ns, err);
+}
+
+void norm_exchange(const PeerPtrs& pads, int rank, int world, uint32_t epoch, const float* stats, float max_norm,
+                   float* tot, uint64_t budget_ns, int* err, cudaStream_t st) {
+  check_world(world);
+  comm::norm_exchange_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, stats, max_norm, tot, budget_ns, err);
+}
+
+#define WB_WORLD_SWITCH(W, ...)                          \
+  switch (W) {                                           \
+    case 1: { constexpr int kW = 1; __VA_ARGS__; } break; \
+    case 2: { constexpr int kW = 2; __VA_ARGS__; } break; \
+    case 3: { constexpr int kW = 3; __VA_ARGS__; } break; \
+    case 4: { constexpr int kW = 4; __VA_ARGS__; } break; \
+    case 5: { constexpr int kW = 5; __VA_ARGS__; } break; \
+    case 6: { constexpr int kW = 6; __VA_ARGS__; } break; \
+    case 7: { constexpr int kW = 7; __VA_ARGS__; } break; \
+    case 8: { constexpr int kW = 8; __VA_ARGS__; } break; \
+    default: throw std::runtime_error("wavelet_b200 fabric: world size must be 1..8"); \
+  }
+
+void rs_sum_sumsq(const PeerPtrs& grads, int world, int64_t lo, int64_t n, float scale, float* out, float* stats,
+                  cudaStream_t st) {
+  if (n <= 0) return;
+  if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
+  const int64_t n8 = n / 8;
+  const int grid = comm::grid_for(n8, 512, 148 * 4);
+  WB_WORLD_SWITCH(world, comm::rs_kernel<kW><<<grid, 512, 0, st>>>(grads, lo, n8, scale, out, stats));
+}
+
+void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* master, const float* g, float* m, float* v,
+                     int64_t n, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                     const float* tot, cudaStream_t st) {
+  if (n <= 0) return;
+  if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
+  const int64_t n8 = n / 8;
+  const int grid = comm::grid_for(n8, 256, 148 * 8);
+  WB_WORLD_SWITCH(world, comm::adamw_ag_kernel<kW><<<grid, 256, 0, st>>>(compute, lo, master, g, m, v, n8, lr, b1, b2,
+                                                                            eps, wd, bc1, bc2, tot));
+}
+
+void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src, int64_t n, cudaStream_t st) {
+  if (n <= 0) return;
+  if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
+  const int64_t n8 = n / 8;
+  const int grid = comm::grid_for(n8, 256, 148 * 8);
+  WB_WORLD_SWITCH(world, comm::ag_kernel<kW><<<grid, 256, 0, st>>>(dst, lo, static_cast<const uint4*>(src), n8));
+}
+
+}  // namespace wb

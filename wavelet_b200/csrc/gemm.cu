@@ -22,6 +22,18 @@
 //               accumulator.
 // Every wait is bounded (common.cuh); on timeout the CTA drains its in-flight
 // TMA and MMA work, frees TMEM, reports through the error word and exits.
+//
+// Two extensions serve LoRA / QLoRA (reference kernels/lora.py and the
+// bitsandbytes dequant + matmul it calls):
+//   * a second operand pair (A2, B2, K2): after the K/64 k-blocks of A B^T
+//     the producer streams K2/64 k-blocks of A2 B2^T into the same TMEM
+//     accumulator, so the low-rank update costs one or two extra k-blocks of
+//     the base GEMM instead of a separate GEMM plus an add;
+//   * an NF4 B operand (BQ): warps 6..13 load 4-bit codes and per-64 absmax
+//     scales, dequantise through a 16-entry table in shared memory and store
+//     bf16 straight into the 128-byte-swizzled stage layout that TMA would
+//     have produced (fence.proxy.async before arriving on the stage barrier),
+//     so a frozen base weight is read at 0.5 byte per element.
 #include "common.cuh"
 #include "gemm.h"
 #include "tma.h"
@@ -39,6 +51,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int MN_BOX = 64;                  // MN-major TMA box width (128 bytes)
 constexpr int MN_BOX_BYTES = MN_BOX * BK * 2;  // 8 KB
 constexpr int NUM_THREADS = 192;
+constexpr int NUM_DQ_THREADS = 256;  // NF4 dequant producers (warps 6..13)
+constexpr int NUM_THREADS_Q = NUM_THREADS + NUM_DQ_THREADS;
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 
@@ -50,6 +64,7 @@ struct __align__(8) Smem {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  float lut[16];
 };
 
 constexpr size_t smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(Smem) + 64; }
@@ -70,6 +85,11 @@ struct Params {
   const int* k_start;      // K-grouped: first K row of every group (multiple of BK)
   const int* k_len;        // K-grouped: K rows of every group
   int groups;
+  int num_k2;              // k-blocks of the second operand pair (dense mode)
+  const uint8_t* q;        // NF4 B operand
+  const float* q_absmax;
+  int64_t q_cols;
+  float lut[16];
 };
 
 // Tile decode shared by the three warp roles (they must agree exactly).
@@ -196,9 +216,28 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI, int GROUP>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// 32 bytes of codes (64 elements) -> 8 chunks of 8 bf16 at swizzled offsets.
+__device__ __forceinline__ void dequant_segment(uint8_t* row_base, int swz, uint4 w0, uint4 w1, float am,
+                                                const float* lut) {
+  const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t b = words[c];  // 4 bytes = 8 codes, little-endian byte order
+    uint4 o;
+    uint32_t* op = &o.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t byte = (b >> (8 * j)) & 0xffu;
+      op[j] = pack_bf16(lut[byte >> 4] * am, lut[byte & 15u] * am);
+    }
+    *reinterpret_cast<uint4*>(row_base + ((c ^ swz) << 4)) = o;
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI, int GROUP, bool BQ>
+__global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                 Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -209,10 +248,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = p.num_m * p.num_n * (GROUP == 2 ? p.groups : 1);
+  const int num_k2 = (GROUP == 0) ? p.num_k2 : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&s->full[i], 1);
+      mbar_init(&s->full[i], BQ ? 1 + NUM_DQ_THREADS : 1);
       mbar_init(&s->empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -224,6 +264,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_mbar_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
+    if (BQ)
+      for (int i = 0; i < 16; ++i) s->lut[i] = p.lut[i];
   }
   if (warp == 1) {
     tmem_alloc(&s->tmem_base, TMEM_COLS);
@@ -246,29 +288,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const TileInfo ti = tile_info<GROUP>(t, p);
         const int m0 = ti.tm * BM, n0 = ti.tn * BN;
-        for (int kb = 0; kb < ti.num_k; ++kb) {
+        const int nk = ti.num_k + (ti.num_k > 0 ? num_k2 : 0);
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
           uint8_t* a_dst = tiles + stage * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
-          mbar_arrive_expect_tx(&s->full[stage], STAGE_BYTES);
-          const int k0 = (ti.kb_begin + kb) * BK;
+          const bool second = kb >= ti.num_k;
+          const bool load_b = second || !BQ;
+          mbar_arrive_expect_tx(&s->full[stage], load_b ? STAGE_BYTES : A_BYTES);
+          const int k0 = second ? (kb - ti.num_k) * BK : (ti.kb_begin + kb) * BK;
+          const int boff = second ? 0 : (int)ti.b_off;
+          const CUtensorMap* mA = second ? &tmA2 : &tmA;
+          const CUtensorMap* mB = second ? &tmB2 : &tmB;
           if constexpr (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / MN_BOX; ++j)
-              tma_load_2d(&tmA, &s->full[stage], a_dst + j * MN_BOX_BYTES, m0 + j * MN_BOX, k0);
+              tma_load_2d(mA, &s->full[stage], a_dst + j * MN_BOX_BYTES, m0 + j * MN_BOX, k0);
           } else {
-            tma_load_2d(&tmA, &s->full[stage], a_dst, k0, m0);
+            tma_load_2d(mA, &s->full[stage], a_dst, k0, m0);
           }
-          if constexpr (B_MN) {
+          if (load_b) {
+            if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / MN_BOX; ++j)
-              tma_load_2d(&tmB, &s->full[stage], b_dst + j * MN_BOX_BYTES, n0 + j * MN_BOX,
-                          k0 + (int)ti.b_off);
-          } else {
-            tma_load_2d(&tmB, &s->full[stage], b_dst, k0, n0 + (int)ti.b_off);
+              for (int j = 0; j < BN / MN_BOX; ++j)
+                tma_load_2d(mB, &s->full[stage], b_dst + j * MN_BOX_BYTES, n0 + j * MN_BOX, k0 + boff);
+            } else {
+              tma_load_2d(mB, &s->full[stage], b_dst, k0, n0 + boff);
+            }
           }
           issued[stage] = 1;
           issued_phase[stage] = phase;
@@ -308,7 +357,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < ti.num_k; ++kb) {
+        const int nk = ti.num_k + num_k2;
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&s->full[stage], phase, abort, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -349,6 +399,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+  } else if (BQ && warp >= NUM_THREADS / 32) {
+    // ------------------------------------------------------------ NF4 dequant producers
+    const int d = threadIdx.x - NUM_THREADS;  // 0..255: one 64-element segment per stage
+    const int64_t qb = p.q_cols / 2;          // bytes per W row
+    const int64_t qa = p.q_cols / 64;         // absmax entries per W row
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = tile_info<GROUP>(t, p);
+      const int n0 = ti.tn * BN;
+      const int nk = ti.num_k + (ti.num_k > 0 ? num_k2 : 0);
+      for (int kb = 0; kb < nk; ++kb) {
+        if (!mbar_wait_warp(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        if (kb < ti.num_k) {
+          uint8_t* b_dst = tiles + stage * STAGE_BYTES + A_BYTES;
+          const int k0 = kb * BK;
+          uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+          float am = 0.f;
+          uint8_t* row_base;
+          int swz;
+          if constexpr (!B_MN) {
+            // B(n, k) = W[n][k]: segment = row n0 + d, columns k0 .. k0+63
+            const int n = n0 + d;
+            if (n < p.N) {
+              const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)n * qb + k0 / 2);
+              w0 = __ldg(src);
+              w1 = __ldg(src + 1);
+              am = __ldg(p.q_absmax + (int64_t)n * qa + kb);
+            }
+            row_base = b_dst + d * 128;
+            swz = d & 7;
+          } else {
+            // B(n, k) = W[k][n]: segment = W row k0 + r, columns n0 + 64 j .. +63
+            const int r = d & 63, j = d >> 6;
+            const int kr = k0 + r, nb = n0 + j * 64;
+            if (kr < p.K && nb < p.N) {
+              const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)kr * qb + nb / 2);
+              w0 = __ldg(src);
+              w1 = __ldg(src + 1);
+              am = __ldg(p.q_absmax + (int64_t)kr * qa + nb / 64);
+            }
+            row_base = b_dst + j * MN_BOX_BYTES + r * 128;
+            swz = r & 7;
+          }
+          dequant_segment(row_base, swz, w0, w1, am, s->lut);
+          fence_proxy_async_shared();
+        }
+        mbar_arrive(&s->full[stage]);
+        if (++stage == STAGES) stage = 0, phase ^= 1;
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -384,9 +489,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI, int GROUP = 0>
+template <bool A_MN, bool B_MN, int EPI, int GROUP = 0, bool BQ = false>
 static void launch(const GemmArgs& g, cudaStream_t stream) {
-  auto kern = gemm_kernel<A_MN, B_MN, EPI, GROUP>;
+  auto kern = gemm_kernel<A_MN, B_MN, EPI, GROUP, BQ>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -402,10 +507,25 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   // B outer extent: N (K-major) or K (MN-major) rows, times the group count
   // in M-grouped mode where every group has its own weight block.
   const uint64_t b_outer = g.b_outer > 0 ? (uint64_t)g.b_outer : (uint64_t)(B_MN ? g.K : g.N);
-  CUtensorMap tb = B_MN ? make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, b_outer, g.ldb,
-                                       MN_BOX, BK, CU_TENSOR_MAP_SWIZZLE_128B)
-                        : make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, b_outer, g.ldb,
-                                       BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb;
+  if (BQ)
+    tb = ta;  // unused: B comes from the NF4 dequant warps
+  else
+    tb = B_MN ? make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, b_outer, g.ldb, MN_BOX, BK,
+                             CU_TENSOR_MAP_SWIZZLE_128B)
+              : make_tmap_2d(g.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K, b_outer, g.ldb, BK, BN,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap ta2 = ta, tb2 = tb;
+  if (g.K2 > 0) {
+    ta2 = A_MN ? make_tmap_2d(g.A2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.M, g.K2, g.lda2, MN_BOX, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B)
+               : make_tmap_2d(g.A2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K2, g.M, g.lda2, BK, BM,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    tb2 = B_MN ? make_tmap_2d(g.B2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, g.K2, g.ldb2, MN_BOX, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B)
+               : make_tmap_2d(g.B2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.K2, g.N, g.ldb2, BK, BN,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   Params p;
   p.C = g.C;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(g.bias);
@@ -425,9 +545,14 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   p.k_start = g.k_start;
   p.k_len = g.k_len;
   p.groups = g.groups;
+  p.num_k2 = g.K2 > 0 ? (g.K2 + BK - 1) / BK : 0;
+  p.q = g.q;
+  p.q_absmax = g.q_absmax;
+  p.q_cols = g.q_cols;
+  for (int i = 0; i < 16; ++i) p.lut[i] = g.q_lut[i];
   const int tiles = p.num_m * p.num_n * (GROUP == 2 ? g.groups : 1);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, NUM_THREADS, smem_bytes(), stream>>>(ta, tb, p);
+  kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem_bytes(), stream>>>(ta, tb, ta2, tb2, p);
 }
 
 }  // namespace gemm
@@ -451,6 +576,17 @@ void gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
     throw std::runtime_error("wavelet_b200 grouped gemm: K-grouped mode writes fp32");
   }
   if (g.K <= 0) throw std::runtime_error("wavelet_b200 gemm: K must be positive");
+  if (g.K2 > 0 && (!g.A2 || !g.B2)) throw std::runtime_error("wavelet_b200 gemm: K2 > 0 needs A2 and B2");
+  if (g.K2 % 64) throw std::runtime_error("wavelet_b200 gemm: K2 must be a multiple of 64 (pad the adapter rank)");
+  if (g.q) {
+    // NF4 base weight: forward (B K-major) or dgrad (B MN-major), bf16 out
+    if (g.a_mn || g.epi != kEpiBF16) throw std::runtime_error("wavelet_b200 nf4 gemm: K-major A and bf16 output only");
+    if (g.q_cols % 64) throw std::runtime_error("wavelet_b200 nf4 gemm: weight columns must be a multiple of 64");
+    if (g.b_mn ? (g.K != g.q_rows || g.N != g.q_cols) : (g.N != g.q_rows || g.K != g.q_cols))
+      throw std::runtime_error("wavelet_b200 nf4 gemm: weight shape does not match M/N/K");
+    if (g.b_mn) return launch<false, true, kEpiBF16, 0, true>(g, stream);
+    return launch<false, false, kEpiBF16, 0, true>(g, stream);
+  }
 #define WB_GEMM_DISPATCH(AM, BMJ)                                               \
   if (g.a_mn == AM && g.b_mn == BMJ) {                                          \
     if (g.epi == kEpiBF16) return launch<AM, BMJ, kEpiBF16>(g, stream);         \

@@ -41,6 +41,24 @@ struct GemmArgs {
   const int* k_start = nullptr;
   const int* k_len = nullptr;
   int groups = 0;
+  // Second operand pair (dense mode): C (op)= alpha * (A B^T + A2 B2^T), with
+  // A2 / B2 of the same majorness as A / B and inner dimension K2.  This is
+  // the LoRA-fused linear: A2 = s * X A_lora^T, B2 = B_lora (forward), or
+  // A2 = s * dY B_lora, B2 = A_lora (dgrad).
+  const void* A2 = nullptr;
+  int64_t lda2 = 0;
+  const void* B2 = nullptr;
+  int64_t ldb2 = 0;
+  int K2 = 0;
+  // NF4 B operand (dense mode, K-major A, bf16 out): B is dequantised on the
+  // fly from 4-bit codes.  The weight W is [q_rows, q_cols] row-major with
+  // two codes per byte (element 2i in the high nibble) and one fp32 absmax
+  // per 64 consecutive elements of a row.  b_mn=false: B(n,k) = W[n][k];
+  // b_mn=true: B(n,k) = W[k][n].  q_cols must be a multiple of 64.
+  const uint8_t* q = nullptr;
+  const float* q_absmax = nullptr;
+  int64_t q_rows = 0, q_cols = 0;
+  float q_lut[16] = {0};
 };
 
 void gemm_bf16(const GemmArgs& g, cudaStream_t stream);

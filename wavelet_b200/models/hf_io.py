@@ -107,7 +107,15 @@ def load_hf_weights(model, path: Path) -> None:
     hf: dict[str, torch.Tensor] = {}
     for fp in files:
         hf.update(load_file(str(fp)))
-    model.flat.load_state(internal_from_hf(model.cfg, hf))
+    tensors = internal_from_hf(model.cfg, hf)
+    model.flat.load_state(tensors)
+    if getattr(model, "quant", None):
+        from ..ops.nf4 import quantize
+
+        for name, q in model.quant.items():  # QLoRA: quantise the loaded projections in place
+            nq = quantize(tensors[name].to(device=q.device, dtype=model.flat.compute_dtype))
+            q.codes.copy_(nq.codes)
+            q.absmax.copy_(nq.absmax)
 
 
 def save_hf(model, out_dir: Path, dtype: torch.dtype = torch.bfloat16, max_shard_bytes: int = 5 * 2**30) -> list[Path]:

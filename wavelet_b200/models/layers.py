@@ -40,20 +40,47 @@ class BatchCtx:
     inv_freq: torch.Tensor  # fp32 [head_dim/2]
 
 
-def _dense_mlp_fwd(x2, P, c, save):
+def _lin(x, w, ad, bias=None, res=None):
+    """y = x W^T (+ bias + res) (+ s (x A^T) B^T with an adapter) -> (y, u)."""
+    if ad is None:
+        return ops.gemm(x, w, bias=bias, res=res), None
+    u = ops.gemm(x, ad.A, alpha=ad.scale)
+    return ops.gemm(x, w, bias=bias, res=res, a2=u, b2=ad.B), u
+
+
+def _lin_bwd(dy, x, u, w, gw, ad):
+    """dx of ``_lin``; accumulates dW into ``gw`` (None: frozen) and the
+    adapter gradients (block-diagonal dB, dA) when ``ad`` is given."""
+    if gw is not None:
+        ops.gemm(dy, x, a_mn=True, b_mn=True, out=gw, epi=ops.EPI_F32_ACC)
+    if ad is None:
+        return ops.gemm(dy, w, b_mn=True)
+    if ad.GB is not None:
+        ad.add_b_grad(ops.gemm(dy, u, a_mn=True, b_mn=True, epi=ops.EPI_F32))
+    g = ops.gemm(dy, ad.B, b_mn=True, alpha=ad.scale)
+    if ad.GA is not None:
+        ops.gemm(g, x, a_mn=True, b_mn=True, out=ad.GA, epi=ops.EPI_F32_ACC)
+    return ops.gemm(dy, w, b_mn=True, a2=g, b2=ad.A)
+
+
+def _dense_mlp_fwd(x2, P, c, save, lora):
     h2, rstd2, _ = ops.rmsnorm_fwd(x2, P["post_norm"], c.rms_eps)
-    gu = ops.gemm(h2, P["gu_w"])
+    gu, u_gu = _lin(h2, P["gu_w"], lora.get("gu"))
     a = ops.swiglu_fwd(gu)
-    out = ops.gemm(a, P["down_w"], res=x2)
-    return out, (dict(h2=h2, rstd2=rstd2, gu=gu, a=a) if save else None)
+    out, u_dn = _lin(a, P["down_w"], lora.get("down"), res=x2)
+    return out, (dict(h2=h2, rstd2=rstd2, gu=gu, a=a, u_gu=u_gu, u_dn=u_dn) if save else None)
 
 
-def layer_fwd(x: torch.Tensor, P: dict[str, torch.Tensor], cfg: ArchConfig, b: BatchCtx, save: bool,
-              moe: Any = None):
+_NO_LORA: dict = {}
+
+
+def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool,
+              moe: Any = None, lora: dict | None = None):
+    lora = lora or _NO_LORA
     T = x.shape[0]
     nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
     h1, rstd1, _ = ops.rmsnorm_fwd(x, P["in_norm"], cfg.rms_eps)
-    qkv = ops.gemm(h1, P["qkv_w"], bias=P.get("qkv_b"))
+    qkv, u_qkv = _lin(h1, P["qkv_w"], lora.get("qkv"), bias=P.get("qkv_b"))
     qkv_pre = qkv.clone() if (save and cfg.qk_norm) else None
     rstd_qk = ops.qk_norm_rope_(qkv, nq, nk, b.pos, b.inv_freq, P.get("q_norm"), P.get("k_norm"), cfg.rms_eps)
     q = qkv[:, : nq * hd].view(T, nq, hd)
@@ -61,39 +88,38 @@ def layer_fwd(x: torch.Tensor, P: dict[str, torch.Tensor], cfg: ArchConfig, b: B
     v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
     att, lse = attention_fwd(q, k, v, b.cu_seqlens, b.max_seqlen, True)
     att2 = att.view(T, nq * hd)
-    x2 = ops.gemm(att2, P["o_w"], res=x)
+    x2, u_o = _lin(att2, P["o_w"], lora.get("o"), res=x)
     if moe is None:
-        out, mc = _dense_mlp_fwd(x2, P, cfg, save)
+        out, mc = _dense_mlp_fwd(x2, P, cfg, save, lora)
     else:
         out, mc = moe.forward(x2, P, save)
     cache = None
     if save:
-        cache = dict(h1=h1, rstd1=rstd1, qkv=qkv, qkv_pre=qkv_pre, rstd_qk=rstd_qk, att=att, lse=lse, x2=x2, mlp=mc)
+        cache = dict(h1=h1, rstd1=rstd1, qkv=qkv, qkv_pre=qkv_pre, rstd_qk=rstd_qk, att=att, lse=lse, x2=x2, mlp=mc,
+                     u_qkv=u_qkv, u_o=u_o)
     return out, cache
 
 
-def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict[str, torch.Tensor],
-              G: dict[str, torch.Tensor], cfg: ArchConfig, b: BatchCtx, moe: Any = None):
+def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cfg: ArchConfig, b: BatchCtx,
+              moe: Any = None, lora: dict | None = None):
+    lora = lora or _NO_LORA
     T = x.shape[0]
     nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
     dout = dout.contiguous()
     mc = c["mlp"]
     if moe is None:
         # out = x2 + a Wd^T
-        da = ops.gemm(dout, P["down_w"], b_mn=True)
-        ops.gemm(dout, mc["a"], a_mn=True, b_mn=True, out=G["down_w"], epi=ops.EPI_F32_ACC)
+        da = _lin_bwd(dout, mc["a"], mc["u_dn"], P["down_w"], G.get("down_w"), lora.get("down"))
         dgu = ops.swiglu_bwd(mc["gu"], da)
         del da
-        ops.gemm(dgu, mc["h2"], a_mn=True, b_mn=True, out=G["gu_w"], epi=ops.EPI_F32_ACC)
-        dh2 = ops.gemm(dgu, P["gu_w"], b_mn=True)
+        dh2 = _lin_bwd(dgu, mc["h2"], mc["u_gu"], P["gu_w"], G.get("gu_w"), lora.get("gu"))
         del dgu
-        dx2 = ops.rmsnorm_bwd(c["x2"], P["post_norm"], mc["rstd2"], dh2, dres=dout, dw=G["post_norm"])
+        dx2 = ops.rmsnorm_bwd(c["x2"], P["post_norm"], mc["rstd2"], dh2, dres=dout, dw=G.get("post_norm"))
         del dh2
     else:
         dx2 = moe.backward(dout, c["x2"], mc, P, G)
     # x2 = x + att Wo^T
-    datt = ops.gemm(dx2, P["o_w"], b_mn=True)
-    ops.gemm(dx2, c["att"].view(T, nq * hd), a_mn=True, b_mn=True, out=G["o_w"], epi=ops.EPI_F32_ACC)
+    datt = _lin_bwd(dx2, c["att"].view(T, nq * hd), c["u_o"], P["o_w"], G.get("o_w"), lora.get("o"))
     qkv = c["qkv"]
     q = qkv[:, : nq * hd].view(T, nq, hd)
     k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
@@ -107,12 +133,11 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict[str, torch.T
         dqkv, qkv_pre, nq, nk, b.pos, b.inv_freq, P.get("q_norm"), P.get("k_norm"), c["rstd_qk"],
         G.get("q_norm"), G.get("k_norm"),
     )
-    if "qkv_b" in P:
+    if G.get("qkv_b") is not None:
         G["qkv_b"].add_(dqkv.float().sum(0))
-    ops.gemm(dqkv, c["h1"], a_mn=True, b_mn=True, out=G["qkv_w"], epi=ops.EPI_F32_ACC)
-    dh1 = ops.gemm(dqkv, P["qkv_w"], b_mn=True)
+    dh1 = _lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv"))
     del dqkv
-    dx = ops.rmsnorm_bwd(x, P["in_norm"], c["rstd1"], dh1, dres=dx2, dw=G["in_norm"])
+    dx = ops.rmsnorm_bwd(x, P["in_norm"], c["rstd1"], dh1, dres=dx2, dw=G.get("in_norm"))
     return dx
 
 
@@ -122,7 +147,7 @@ class DecoderLayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, layer):
         with torch.no_grad():
-            out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe)
+            out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe, lora=layer.lora)
         ctx.save_for_backward(x)
         ctx.layer = layer
         return out
@@ -132,8 +157,8 @@ class DecoderLayerFn(torch.autograd.Function):
         (x,) = ctx.saved_tensors
         layer = ctx.layer
         with torch.no_grad():
-            _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe)
-            dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe)
+            _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora)
+            dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe, lora=layer.lora)
         return dx, None, None
 
 

@@ -170,12 +170,14 @@ class MoEBlock:
         da = torch.empty(rt.R, Ie, device=dout.device, dtype=dout.dtype)
         m.gemm_grouped(dy, False, P["exp_down_w"].view(E * H, Ie), True, da, 1, rt.R, Ie, H, rt.tile_group, H, E * H,
                        None, None, E, ops.EPI_BF16, 1.0)
-        m.gemm_grouped(dy, True, c["a"], True, G["exp_down_w"].view(E * H, Ie), 2, H, Ie, rt.R, None, 0, 0,
-                       rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
+        if G.get("exp_down_w") is not None:
+            m.gemm_grouped(dy, True, c["a"], True, G["exp_down_w"].view(E * H, Ie), 2, H, Ie, rt.R, None, 0, 0,
+                           rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
         dgu = ops.swiglu_bwd(c["gu"], da)
         del da
-        m.gemm_grouped(dgu, True, c["xs"], True, G["exp_gu_w"].view(E * 2 * Ie, H), 2, 2 * Ie, H, rt.R, None, 0, 0,
-                       rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
+        if G.get("exp_gu_w") is not None:
+            m.gemm_grouped(dgu, True, c["xs"], True, G["exp_gu_w"].view(E * 2 * Ie, H), 2, 2 * Ie, H, rt.R, None, 0,
+                           0, rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
         dxs = torch.empty(rt.R, H, device=dout.device, dtype=dout.dtype)
         m.gemm_grouped(dgu, False, P["exp_gu_w"].view(E * 2 * Ie, H), True, dxs, 1, rt.R, H, 2 * Ie, rt.tile_group,
                        2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
@@ -194,9 +196,10 @@ class MoEBlock:
             dprobs += self.aux_loss_scale * cfg.num_experts * c["f"][None, :] / T
         dlogits = probs * (dprobs - (dprobs * probs).sum(-1, keepdim=True))
         dl16 = dlogits.to(dout.dtype).contiguous()
-        ops.gemm(dl16, c["h2"], a_mn=True, b_mn=True, out=G["router_w"], epi=ops.EPI_F32_ACC)
+        if G.get("router_w") is not None:
+            ops.gemm(dl16, c["h2"], a_mn=True, b_mn=True, out=G["router_w"], epi=ops.EPI_F32_ACC)
         dh2 += ops.gemm(dl16, P["router_w"], b_mn=True).float()
-        return ops.rmsnorm_bwd(x2, P["post_norm"], c["rstd2"], dh2.to(dout.dtype), dres=dout, dw=G["post_norm"])
+        return ops.rmsnorm_bwd(x2, P["post_norm"], c["rstd2"], dh2.to(dout.dtype), dres=dout, dw=G.get("post_norm"))
 
     # ------------------------------------------------------------ generator
     @torch.no_grad()

@@ -48,6 +48,7 @@ class FlatParams:
         dp_world: int = 1,
         with_grad: bool = True,
         with_optimizer: bool = True,
+        alloc=None,
     ):
         self.specs: list[ParamSpec] = list(specs)
         self.device = torch.device(device)
@@ -63,8 +64,14 @@ class FlatParams:
         unit = ALIGN * dp_world
         self.numel = (off + unit - 1) // unit * unit
         self.shard_numel = self.numel // dp_world
-        self.compute = torch.zeros(self.numel, device=self.device, dtype=compute_dtype)
-        self.grad = torch.zeros(self.numel, device=self.device, dtype=torch.float32) if with_grad else None
+        # ``alloc(numel, dtype)`` places the replicated buffers in peer-visible
+        # memory (parallel.fabric) for the fused collective kernels.
+        if alloc is not None:
+            self.compute = alloc(self.numel, compute_dtype)
+            self.grad = alloc(self.numel, torch.float32) if with_grad else None
+        else:
+            self.compute = torch.zeros(self.numel, device=self.device, dtype=compute_dtype)
+            self.grad = torch.zeros(self.numel, device=self.device, dtype=torch.float32) if with_grad else None
         self.master = None
         self.exp_avg = None
         self.exp_avg_sq = None
@@ -105,7 +112,7 @@ class FlatParams:
         return slice(self.dp_rank * self.shard_numel, (self.dp_rank + 1) * self.shard_numel)
 
     # ------------------------------------------------------------- init
-    def init_(self, seed: int = 0, std_override: float | None = None) -> None:
+    def init_(self, seed: int = 0, std_override: float | None = None, seed_index: dict | None = None) -> None:
         """Random init N(0, std) for matrices, ones for norms, zeros for biases.
 
         Every rank produces identical weights (same generator seed per tensor).
@@ -118,7 +125,7 @@ class FlatParams:
             elif s.init == "zeros":
                 v.zero_()
             else:
-                g.manual_seed(seed * 1_000_003 + i)
+                g.manual_seed(seed * 1_000_003 + (seed_index[s.name] if seed_index else i))
                 std = std_override if std_override is not None else s.std
                 # generate in fp32 then cast (bf16 normal_ draws differ by dtype)
                 tmp = torch.empty(v.shape, device=self.device, dtype=torch.float32)

@@ -55,6 +55,9 @@ def param_specs(cfg: ArchConfig) -> list[ParamSpec]:
     return s
 
 
+QUANTIZABLE = ("qkv_w", "o_w", "gu_w", "down_w")  # dense 2-D projections (NF4 for QLoRA)
+
+
 @dataclass
 class _Layer:
     cfg: ArchConfig
@@ -62,14 +65,17 @@ class _Layer:
     G: dict
     batch: BatchCtx | None = None
     moe: Any = None
+    lora: dict | None = None
 
 
 class CausalLM:
     """A decoder-only LM whose parameters live in a ``FlatParams`` store."""
 
-    def __init__(self, cfg: ArchConfig, flat: FlatParams):
+    def __init__(self, cfg: ArchConfig, flat: FlatParams, quant: dict | None = None):
         self.cfg = cfg
         self.flat = flat
+        self.quant = quant or {}  # name -> NF4Weight (frozen QLoRA base projections)
+        self.lora = None
         self.device = flat.device
         self.inv_freq = ref.rope_inv_freq(cfg.head_dim, cfg.rope_theta, device=self.device)
         self.layers: list[_Layer] = []
@@ -77,6 +83,7 @@ class CausalLM:
             pre = f"l{i}."
             names = [n for n in flat.names() if n.startswith(pre)]
             P = {n[len(pre):]: flat.view(n) for n in names}
+            P.update({n[len(pre):]: q for n, q in self.quant.items() if n.startswith(pre)})
             G = {n[len(pre):]: flat.grad_view(n) for n in names} if flat.grad is not None else {}
             layer = _Layer(cfg, P, G)
             if cfg.layer_is_moe(i):
@@ -86,6 +93,17 @@ class CausalLM:
             self.layers.append(layer)
         self.anchor = torch.empty(0, device=self.device, requires_grad=True)
         self.ep_group = None
+
+    # ----------------------------------------------------------- adapters
+    def attach_lora(self, adapters) -> None:
+        """Train LoRA adapters on a frozen base (the base store has no grads)."""
+        self.lora = adapters
+        for i, layer in enumerate(self.layers):
+            layer.lora = adapters.layer_views(i)
+
+    @property
+    def trainable(self) -> FlatParams:
+        return self.lora.flat if self.lora is not None else self.flat
 
     # ----------------------------------------------------------- weights
     def weight(self, name: str) -> torch.Tensor:
@@ -131,13 +149,37 @@ class CausalLM:
     def _hidden_cpu(self, ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
         cfg = self.cfg
         flat = self.flat
-        if not flat.compute.requires_grad:
+        if self.lora is None and not flat.compute.requires_grad:
             flat.compute.requires_grad_(True)
 
         def W(n):
+            if n in self.quant:
+                return self.quant[n].dequantize(flat.compute.dtype)
             off, k = flat.offsets[n]
             shape = next(s.shape for s in flat.specs if s.name == n)
             return flat.compute[off : off + k].view(shape)
+
+        lf = self.lora.flat if self.lora is not None else None
+        if lf is not None and not lf.compute.requires_grad:
+            lf.compute.requires_grad_(True)
+
+        def lin(x, i, wname, target, bias=None):
+            y = F.linear(x, W(f"l{i}.{wname}"), bias)
+            if lf is None or f"l{i}.{target}.A" not in lf.offsets:
+                return y
+            lay = self.lora.layouts[target]
+            r, sc = self.lora.rank, self.lora.scale
+            oa, na = lf.offsets[f"l{i}.{target}.A"]
+            ob, nb = lf.offsets[f"l{i}.{target}.B"]
+            A = lf.compute[oa : oa + na].view(lay.kp, lay.in_dim)
+            B = lf.compute[ob : ob + nb].view(lay.out_dim, lay.kp)
+            parts = []
+            for _, _, lo, hi, c0 in lay.parts:
+                parts.append((lo, hi, sc * (x @ A[c0 : c0 + r].t()) @ B[lo:hi, c0 : c0 + r].t()))
+            delta = torch.zeros_like(y)
+            for lo, hi, d in parts:
+                delta = delta.index_add(1, torch.arange(lo, hi), d)
+            return y + delta
 
         T = ids.shape[0]
         nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -145,7 +187,7 @@ class CausalLM:
         for i in range(cfg.num_layers):
             p = f"l{i}."
             h = ref.rmsnorm(x, W(p + "in_norm"), cfg.rms_eps)
-            qkv = F.linear(h, W(p + "qkv_w"), W(p + "qkv_b") if cfg.qkv_bias else None)
+            qkv = lin(h, i, "qkv_w", "qkv", W(p + "qkv_b") if cfg.qkv_bias else None)
             q = qkv[:, : nq * hd].view(T, nq, hd)
             k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
             v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
@@ -155,14 +197,14 @@ class CausalLM:
             q = ref.apply_rope(q, batch.pos, batch.inv_freq)
             k = ref.apply_rope(k, batch.pos, batch.inv_freq)
             att = ref.attention(q, k, v, batch.cu_seqlens, True)
-            x = x + F.linear(att.reshape(T, nq * hd), W(p + "o_w"))
+            x = x + lin(att.reshape(T, nq * hd), i, "o_w", "o")
             h2 = ref.rmsnorm(x, W(p + "post_norm"), cfg.rms_eps)
             if cfg.layer_is_moe(i):
                 from .moe import moe_reference
 
                 x = x + moe_reference(h2, W(p + "router_w"), W(p + "exp_gu_w"), W(p + "exp_down_w"), cfg)[0]
             else:
-                x = x + F.linear(ref.swiglu(F.linear(h2, W(p + "gu_w"))), W(p + "down_w"))
+                x = x + lin(ref.swiglu(lin(h2, i, "gu_w", "gu")), i, "down_w", "down")
         return ref.rmsnorm(x, W("norm"), cfg.rms_eps)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
@@ -175,18 +217,55 @@ class CausalLM:
 
     def collect_cpu_grads(self) -> None:
         """CPU path: move autograd grads of the flat buffer into flat.grad."""
-        g = self.flat.compute.grad
-        if g is not None and self.flat.grad is not None:
-            self.flat.grad.add_(g.float())
-            self.flat.compute.grad = None
+        for f in (self.flat, self.lora.flat if self.lora is not None else None):
+            if f is None:
+                continue
+            g = f.compute.grad
+            if g is not None and f.grad is not None:
+                f.grad.add_(g.float())
+            f.compute.grad = None
 
 
 def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
-                with_grad=True, with_optimizer=True) -> CausalLM:
+                with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
+                lora_seed: int = 0) -> CausalLM:
+    """Build (and random-init) a model.
+
+    ``lora``: an object with ``rank``, ``alpha``, ``target_modules``, ``dropout``
+    (the ``lora`` config section) -> frozen base + trainable adapters.
+    ``load_in_4bit``: NF4-quantise the dense projections after init (QLoRA).
+    """
     device = torch.device(device)
     if dtype is None:
         dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
-    flat = FlatParams(param_specs(cfg), device, dtype, dp_rank, dp_world, with_grad, with_optimizer)
+    specs = param_specs(cfg)
+    qnames = {s.name for s in specs if load_in_4bit and s.name.split(".", 1)[-1] in QUANTIZABLE}
+    frozen = lora is not None
+    seed_index = {s.name: i for i, s in enumerate(specs)}
+    flat = FlatParams([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,
+                      with_grad and not frozen, with_optimizer and not frozen,
+                      alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
+    quant = {}
     if init:
-        flat.init_(seed)
-    return CausalLM(cfg, flat)
+        flat.init_(seed, seed_index=seed_index)
+    if qnames:
+        from ..ops.nf4 import quantize
+
+        g = torch.Generator(device=device)
+        for s in specs:
+            if s.name not in qnames:
+                continue
+            tmp = torch.zeros(s.shape, device=device, dtype=torch.float32)
+            if init:
+                g.manual_seed(seed * 1_000_003 + seed_index[s.name])
+                tmp.normal_(0.0, s.std, generator=g)
+            quant[s.name] = quantize(tmp.to(dtype))
+            del tmp
+    model = CausalLM(cfg, flat, quant)
+    if frozen:
+        from .lora import LoRAAdapters
+
+        ad = LoRAAdapters(cfg, lora.rank, lora.alpha, list(lora.target_modules), device, dtype, dp_rank, dp_world,
+                          dropout=getattr(lora, "dropout", 0.0), seed=lora_seed, fabric=fabric)
+        model.attach_lora(ad)
+    return model

@@ -30,16 +30,26 @@ def ext():
 
 
 # --------------------------------------------------------------------- GEMM
-def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False,
+def gemm(a: torch.Tensor, b, *, a_mn: bool = False, b_mn: bool = False,
          out: Optional[torch.Tensor] = None, epi: int = EPI_BF16, alpha: float = 1.0,
-         bias: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """C[M, N] = alpha * A(m, k) B(n, k) (+ bias + res) on the tcgen05 GEMM.
+         bias: Optional[torch.Tensor] = None, res: Optional[torch.Tensor] = None,
+         a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """C[M, N] = alpha * (A(m, k) B(n, k) + A2(m, j) B2(n, j)) (+ bias + res) on the tcgen05 GEMM.
 
     ``a`` is [M, K] (K-major) or [K, M] with ``a_mn``; ``b`` is [N, K] or [K, N]
-    with ``b_mn``.  ``epi`` selects bf16 store, fp32 store or fp32 accumulate.
+    with ``b_mn``, or an ``NF4Weight`` (dequantised inside the kernel).
+    ``a2``/``b2`` (same majorness as ``a``/``b``) add a second product into the
+    same accumulator (the LoRA-fused linear).  ``epi`` selects bf16 store,
+    fp32 store or fp32 accumulate.
     """
+    from .nf4 import NF4Weight, nf4_table
+
+    quant = isinstance(b, NF4Weight)
     M = a.shape[1] if a_mn else a.shape[0]
-    N = b.shape[1] if b_mn else b.shape[0]
+    if quant:
+        N = b.cols if b_mn else b.rows
+    else:
+        N = b.shape[1] if b_mn else b.shape[0]
     if out is None:
         if epi == EPI_BF16:
             dtype = torch.bfloat16 if a.is_cuda else a.dtype
@@ -48,8 +58,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         out = torch.empty(M, N, device=a.device, dtype=dtype)
     if not a.is_cuda:
         A = a.t() if a_mn else a
-        B = b if b_mn else b.t()
-        r = alpha * (A.float() @ B.float())
+        Bm = b.dequantize(torch.float32) if quant else b
+        B = Bm if b_mn else Bm.t()
+        r = A.float() @ B.float()
+        if a2 is not None:
+            A2 = a2.t() if a_mn else a2
+            B2 = b2 if b_mn else b2.t()
+            r = r + A2.float() @ B2.float()
+        r = alpha * r
         if bias is not None:
             r = r + bias.float()
         if res is not None:
@@ -59,7 +75,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
         else:
             out.copy_(r)
         return out
-    ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
+    if not quant and a2 is None:
+        ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
+        return out
+    if quant:
+        ext().gemm_ex(a, a_mn, None, b_mn, out, N, epi, alpha, bias, res, a2, b2, b.codes, b.absmax, b.rows,
+                      b.cols, list(nf4_table()))
+    else:
+        ext().gemm_ex(a, a_mn, b, b_mn, out, N, epi, alpha, bias, res, a2, b2, None, None, 0, 0, [0.0] * 16)
     return out
 
 

@@ -1,0 +1,96 @@
+"""4-bit NormalFloat (NF4) weights for QLoRA.
+
+NF4 (Dettmers et al., "QLoRA", 2023, section 3) maps each block of 64
+consecutive weights to 4-bit codes of a 16-value table built from quantiles
+of the standard normal distribution, scaled by the block's absolute maximum.
+The table is asymmetric so that zero is exactly representable: 8 positive
+quantiles at probabilities linspace(delta, 1/2, 9)[:-1], 7 negative ones at
+linspace(delta, 1/2, 8)[:-1], plus 0, normalised to [-1, 1], with
+delta = 1 - (1/(2*15) + 1/(2*16)) / 2.  It is computed here from that
+construction (``statistics.NormalDist``) rather than copied.
+
+Storage (``NF4Weight``): the row-major [rows, cols] matrix as uint8 codes,
+two per byte (element 2i in the high nibble, 2i+1 in the low nibble), and
+one fp32 absmax per 64 elements of a row (cols % 64 == 0).  The reference
+loads its base model through bitsandbytes ``load_in_4bit`` (NF4, blocksize
+64; trainer/model.py:446-468) and dequantises per call inside its LoRA
+kernels (kernels/utils.py:8-86); here the tcgen05 GEMM dequantises inside
+the kernel (csrc/gemm.cu, NF4 B operand).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from functools import lru_cache
+from statistics import NormalDist
+
+import torch
+
+BLOCK = 64
+
+
+@lru_cache(maxsize=1)
+def nf4_table() -> tuple[float, ...]:
+    nd = NormalDist()
+    delta = 1.0 - 0.5 * (1.0 / (2 * 15) + 1.0 / (2 * 16))
+    pos = [nd.inv_cdf(delta + (0.5 - delta) * i / 8) for i in range(8)]
+    neg = [-nd.inv_cdf(delta + (0.5 - delta) * i / 7) for i in range(7)]
+    vals = sorted(pos + neg + [0.0])
+    top = max(abs(v) for v in vals)
+    return tuple(v / top for v in vals)
+
+
+@dataclass
+class NF4Weight:
+    codes: torch.Tensor  # uint8 [rows * cols / 2]
+    absmax: torch.Tensor  # fp32 [rows * cols / 64]
+    rows: int
+    cols: int
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.rows, self.cols)
+
+    @property
+    def device(self) -> torch.device:
+        return self.codes.device
+
+    def nbytes(self) -> int:
+        return self.codes.numel() + 4 * self.absmax.numel()
+
+    def dequantize(self, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        return dequantize(self, dtype)
+
+
+def _lut(device) -> torch.Tensor:
+    return torch.tensor(nf4_table(), dtype=torch.float32, device=device)
+
+
+@torch.no_grad()
+def quantize(w: torch.Tensor, chunk_rows: int = 4096) -> NF4Weight:
+    """Blockwise NF4 quantisation of a [rows, cols] matrix (nearest code)."""
+    if w.dim() != 2 or w.shape[1] % BLOCK:
+        raise ValueError(f"NF4 needs a 2-D weight with cols % {BLOCK} == 0, got {tuple(w.shape)}")
+    rows, cols = w.shape
+    lut = _lut(w.device)
+    mids = (lut[1:] + lut[:-1]) / 2
+    codes = torch.empty(rows * cols // 2, dtype=torch.uint8, device=w.device)
+    absmax = torch.empty(rows * cols // BLOCK, dtype=torch.float32, device=w.device)
+    for r0 in range(0, rows, chunk_rows):
+        r1 = min(rows, r0 + chunk_rows)
+        blk = w[r0:r1].float().reshape(-1, BLOCK)
+        am = blk.abs().amax(1)
+        xn = blk / am.clamp_min(1e-30)[:, None]
+        q = torch.bucketize(xn, mids).to(torch.uint8).reshape(-1)
+        codes[r0 * cols // 2 : r1 * cols // 2] = (q[0::2] << 4) | q[1::2]
+        absmax[r0 * cols // BLOCK : r1 * cols // BLOCK] = am
+    return NF4Weight(codes, absmax, rows, cols)
+
+
+@torch.no_grad()
+def dequantize(q: NF4Weight, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    lut = _lut(q.codes.device)
+    hi = (q.codes >> 4).long()
+    lo = (q.codes & 15).long()
+    vals = torch.stack([lut[hi], lut[lo]], 1).reshape(-1, BLOCK) * q.absmax[:, None]
+    return vals.reshape(q.rows, q.cols).to(dtype)

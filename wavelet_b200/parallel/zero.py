@@ -10,7 +10,12 @@ Per optimizer step, on every data-parallel rank:
    shard into the resident compute buffer;
 4. all-gather the bf16 compute buffer.
 
-With world size 1 steps 1 and 4 disappear.  Parity: the reference's FSDP
+With world size 1 steps 1 and 4 disappear.  ``FusedShardedAdamW`` runs the
+same step as three kernels over peer memory (parallel.fabric): a
+reduce-scatter that pulls every rank's gradient slice over NVLink and sums,
+scales and squares it in one pass; a norm exchange; and an AdamW kernel that
+stores the updated bf16 shard straight into every rank's compute buffer (the
+all-gather rides on the update's stores).  Parity: the reference's FSDP
 reduce-scatter + ``torch.optim.AdamW`` (fused) + ``clip_grad_norm_`` path
 (trainer/optim.py:393-512, trainer/trainer.py:1034-1101).
 """
@@ -111,3 +116,64 @@ class ShardedAdamW:
         p16.copy_(self.flat.master.to(p16.dtype))
         if self.world > 1:
             dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
+
+
+class FusedShardedAdamW(ShardedAdamW):
+    """ZeRO step as fused peer-memory kernels (one node, world <= 8).
+
+    Per step: barrier (every rank's gradients complete) -> reduce-scatter +
+    squared norm -> norm exchange + clip factor -> AdamW + bf16 all-gather ->
+    barrier (every rank's parameters complete).  No host synchronisation
+    inside; the finite check reads the totals after the step, and a
+    non-finite step leaves the parameters unchanged on every rank.
+    """
+
+    def __init__(self, flat: FlatParams, hyper: AdamWHyper, fabric):
+        super().__init__(flat, hyper, dp_group=fabric.group, dp_world=fabric.world)
+        self.fabric = fabric
+        if self.g_shard is None:
+            self.g_shard = torch.empty(flat.shard_numel, device=flat.device, dtype=torch.float32)
+        self.tot = torch.zeros(3, device=flat.device, dtype=torch.float32)
+        self.grad_ptrs = fabric.ptrs_of(flat.grad)
+        self.compute_ptrs = fabric.ptrs_of(flat.compute)
+
+    @torch.no_grad()
+    def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
+        from .fabric import SLOT_NORM
+
+        flat, fab, m = self.flat, self.fabric, ops.ext()
+        lr = self.h.lr if lr is None else lr
+        lo = flat.dp_rank * flat.shard_numel
+        fab.barrier()
+        self.stats.zero_()
+        m.rs_sum_sumsq(self.grad_ptrs, self.world, lo, flat.shard_numel, 1.0, self.g_shard, self.stats)
+        e = fab.next_epoch(SLOT_NORM)
+        max_norm = float(self.h.max_grad_norm or 0.0)
+        m.norm_exchange(fab.pads.ptrs, fab.rank, self.world, e, self.stats, max_norm, self.tot, fab.budget_s)
+        self.step_count += 1
+        b1, b2 = self.h.betas
+        m.adamw_allgather(self.compute_ptrs, self.world, lo, flat.master, self.g_shard, flat.exp_avg,
+                          flat.exp_avg_sq, lr, b1, b2, self.h.eps, self.h.weight_decay, self.step_count, self.tot)
+        fab.barrier()
+        flat.zero_grad()
+        norm_sq, bad, factor = self.tot.tolist()
+        fab.check()
+        if bad > 0:
+            self.step_count -= 1
+            if check_finite:
+                raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements); step skipped")
+        return {"grad_norm": norm_sq**0.5, "clip_factor": factor}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict) -> None:
+        self.step_count = int(sd["step"])
+        self.flat.master.copy_(sd["master"])
+        self.flat.exp_avg.copy_(sd["exp_avg"])
+        self.flat.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        shard = self.flat.master.to(torch.bfloat16)
+        lo = self.flat.dp_rank * self.flat.shard_numel
+        self.fabric.barrier()
+        ops.ext().allgather_bf16(self.compute_ptrs, self.world, lo, shard)
+        self.fabric.barrier()
+        torch.cuda.synchronize(self.flat.device)
+        self.fabric.check()

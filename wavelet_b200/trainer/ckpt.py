@@ -75,7 +75,7 @@ class CheckpointManager:
              scheduler_state: dict | None = None, block: bool = False) -> Path:
         self.wait()
         d = pathing.checkpoint_dir(self.output_dir, step)
-        flat = model.flat
+        flat = getattr(model, "trainable", model.flat)  # LoRA: only the adapters are saved
         weights = None
         if self.rank == 0:
             weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
@@ -136,10 +136,10 @@ class CheckpointManager:
 
         meta = json.loads((d / "meta.json").read_text())
         w = load_file(str(d / "trainer" / "model.safetensors"))
-        model.flat.load_state({k: v.to(model.flat.device) for k, v in w.items()})
+        flat = getattr(model, "trainable", model.flat)
+        flat.load_state({k: v.to(flat.device) for k, v in w.items()})
         if optimizer is not None and not skip_optimizer:
             saved_world = int(meta.get("world_size", 1))
-            flat = model.flat
             if saved_world == self.world:
                 sd = torch.load(d / "trainer" / f"optim-rank{self.rank}.pt", map_location=flat.device, weights_only=False)
             else:

@@ -14,7 +14,7 @@ import torch.distributed as dist
 
 from ..models.qwen import CausalLM
 from ..ops import lm_head
-from ..parallel.zero import AdamWHyper, ShardedAdamW
+from ..parallel.zero import AdamWHyper, FusedShardedAdamW, ShardedAdamW
 
 
 @dataclass
@@ -52,9 +52,15 @@ class PackedBatch:
 
 class Engine:
     def __init__(self, model: CausalLM, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK):
+                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK, fabric=None):
         self.model = model
-        self.opt = ShardedAdamW(model.flat, hyper, dp_group, dp_world)
+        # the optimizer owns the trainable store: the full model, or only the
+        # LoRA adapters when the base is frozen
+        if fabric is not None:
+            self.opt = FusedShardedAdamW(model.trainable, hyper, fabric)
+        else:
+            self.opt = ShardedAdamW(model.trainable, hyper, dp_group, dp_world)
+        self.fabric = fabric
         self.dp_group = dp_group
         self.dp_world = dp_world
         self.chunk = lm_head_chunk

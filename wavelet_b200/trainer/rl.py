@@ -59,7 +59,8 @@ class RLTrainer:
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if w.device.type == "cuda" else torch.float32
         if model is None:
-            model = build_model(arch, w.device, dtype, dp_rank=self.dp_rank, dp_world=self.dp_world, seed=c.seed)
+            model = build_model(arch, w.device, dtype, dp_rank=self.dp_rank, dp_world=self.dp_world, seed=c.seed,
+                                lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed)
             p = Path(c.model.name)
             if not c.model.random_init and p.is_dir() and any(p.glob("*.safetensors")):
                 from ..models.hf_io import load_hf_weights
@@ -68,7 +69,7 @@ class RLTrainer:
         self.model = model
         if self.groups.ep is not None:
             model.ep_group = self.groups.ep
-        self.optimizer = FlatOptimizer(model.flat, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world)
+        self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world)
         self.loss_fn = setup_rl_loss_fn(c.loss)
         out = Path(c.output_dir)
         self.output_dir = out

@@ -70,12 +70,13 @@ class SFTTrainer:
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
         self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed,
-                                 init=c.model.random_init or not _has_weights(c.model.name))
+                                 init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
+                                 load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed)
         if not c.model.random_init and _has_weights(c.model.name):
             from ..models.hf_io import load_hf_weights
 
             load_hf_weights(self.model, Path(c.model.name))
-        self.optimizer = FlatOptimizer(self.model.flat, c.optim, c.max_grad_norm, self.groups.dp, dp_world)
+        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, self.groups.dp, dp_world)
         self.engine = Engine(self.model, self.optimizer.adamw.h, self.groups.dp, dp_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
@@ -115,7 +116,8 @@ class SFTTrainer:
             if st["data_state"] is not None and not c.ckpt.skip_dataloader:
                 self.dataset.load_state_dict(st["data_state"])
         self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
-        self.perf = PerfTracker(arch, w.device, lora_rank=None)
+        lora_params = self.model.lora.num_trainable() if self.model.lora is not None else None
+        self.perf = PerfTracker(arch, w.device, lora_rank=c.lora.rank if c.lora else None, lora_params=lora_params)
         if c.gc is not None:
             gc.disable()
         return self
