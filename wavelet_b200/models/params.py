@@ -89,7 +89,9 @@ class FlatParams:
         if v is None:
             off, n = self.offsets[name]
             shape = next(s.shape for s in self.specs if s.name == name)
-            v = self.compute[off : off + n].view(shape)
+            # views for kernels and I/O never take part in autograd (the CPU
+            # reference path slices ``compute`` itself when it needs gradients)
+            v = self.compute.detach()[off : off + n].view(shape)
             self._views[name] = v
         return v
 
