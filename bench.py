@@ -42,10 +42,13 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--model", default="qwen2.5-7b")
-    p.add_argument("--seq-len", type=int, default=4096)
-    p.add_argument("--micro-batches", type=int, default=8, help="micro-batches of 1 sequence per GPU per step")
+    p.add_argument("--seq-len", type=int, default=None, help="default 4096 (sft) / 2048 (qlora)")
+    p.add_argument("--micro-batches", type=int, default=None,
+                   help="micro-batches of 1 sequence per GPU per step (default 8 for sft; 32/N for qlora)")
     p.add_argument("--layers", type=int, default=None, help="(debug only) override layer count; invalidates the number")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", default="sft", choices=["sft", "qlora"],
+                   help="sft: dense full fine-tune (headline); qlora: NF4 base + LoRA r16 on all projections")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
                    help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
     return p.parse_args()
@@ -145,12 +148,22 @@ def main():
     overrides = {"num_layers": args.layers} if args.layers else None
     cfg = resolve_arch(args.model, overrides)
     fabric = maybe_fabric(N, rank, dev) if args.comm == "fabric" else None
-    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234, fabric=fabric)
-    hyper = AdamWHyper(lr=1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, max_grad_norm=1.0)
+    qlora = args.workload == "qlora"
+    lora = None
+    if qlora:
+        from types import SimpleNamespace
+
+        lora = SimpleNamespace(rank=16, alpha=32.0, dropout=0.0, target_modules=[
+            "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"])
+    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234, fabric=fabric,
+                        lora=lora, load_in_4bit=qlora)
+    hyper = AdamWHyper(lr=2e-4 if qlora else 1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
+                       max_grad_norm=1.0)
     engine = Engine(model, hyper, dp_group=None, dp_world=N, fabric=fabric)
     stepper = SFTStepper(engine, dev)
 
-    S, mb = args.seq_len, args.micro_batches
+    S = args.seq_len or (2048 if qlora else 4096)
+    mb = args.micro_batches or (max(1, 32 // N) if qlora else 8)
     host_batches = synthetic_sft_microbatches(mb, S, cfg.vocab_size, seed=100 + rank)
     host_batches = [b.pin_memory() for b in host_batches]
     dev_batches = [b.to(dev) for b in host_batches]
@@ -212,10 +225,13 @@ def main():
             "ms_per_step": float(te.item()),
         }
 
-    mfu_flops = 6 * cfg.num_params(active_only=True) + 12 * cfg.num_layers * cfg.hidden_size * S
+    from wavelet_b200.trainer.perf import flops_per_token
+
+    mfu_flops = flops_per_token(cfg, S, model.lora.num_trainable() if model.lora is not None else None)
     if rank == 0:
         rec = {
-            "metric": "SFT tok/s (Qwen2.5-7B-shape dense SFT, bf16)",
+            "metric": ("QLoRA SFT tok/s (Qwen2.5-7B-shape, NF4 base, LoRA r16 all projections)" if qlora
+                       else "SFT tok/s (Qwen2.5-7B-shape dense SFT, bf16)"),
             "value": value,
             "unit": "tokens/s",
             "n_gpus": N,
@@ -223,7 +239,7 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if qlora else "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None,
             "dtype": "bf16",
             "data": "synthetic (uniform random tokens, random-init weights)",
@@ -234,7 +250,9 @@ def main():
                 "micro_batch": 1,
                 "grad_accum": mb,
                 "parallelism": f"dp{N}",
-                "optimizer": "AdamW (fp32 master, sharded)",
+                **({"base": "NF4 blocksize 64 (fp32 absmax), frozen", "lora": "r=16 alpha=32 on q/k/v/o/gate/up/down"}
+                   if qlora else {}),
+                "optimizer": "AdamW (fp32 master, sharded)" + (" on LoRA adapters" if qlora else ""),
                 "optimizer_comm": ("fused peer-memory RS+AdamW+AG kernels" if fabric is not None
                                    else ("NCCL reduce-scatter/all-gather" if N > 1 else "none (1 GPU)")),
                 "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",

@@ -60,3 +60,18 @@ def test_nf4_gemm(cuda_ext, M, N, K):
     assert cuda_ext.read_error(0) == 0
 
 
+
+
+def test_nf4_dequant_kernel_and_large_m_path(cuda_ext):
+    from wavelet_b200.ops.nf4 import dequant_cache
+
+    torch.manual_seed(2)
+    w = torch.randn(384, 512, device="cuda") * 0.03
+    q = quantize(w)
+    ref = dequantize(q, torch.float32).to(torch.bfloat16)
+    got = dequant_cache().get(q)
+    assert torch.equal(got, ref)
+    x = torch.randn(1024, 512, device="cuda", dtype=torch.bfloat16)  # M > FUSED_MAX_M: cached dense path
+    _close(ops.gemm(x, q), x.float() @ ref.float().t())
+    dy = torch.randn(1024, 384, device="cuda", dtype=torch.bfloat16)
+    _close(ops.gemm(dy, q, b_mn=True), dy.float() @ ref.float())

@@ -268,6 +268,18 @@ void allgather_bf16(const std::vector<int64_t>& dst, int64_t world, int64_t lo, 
   wb::allgather_bf16(peers_of(dst, (int)world), (int)world, lo, src.data_ptr(), src.numel(), cur_stream());
 }
 
+void nf4_dequant(const at::Tensor& codes, const at::Tensor& absmax, at::Tensor& out, const std::vector<double>& lut) {
+  WB_CHECK(codes.scalar_type() == at::kByte && codes.is_cuda() && codes.is_contiguous(), "nf4_dequant: codes");
+  check_f32(absmax, "absmax");
+  check_bf16(out, "out");
+  WB_CHECK(out.is_contiguous() && out.numel() == codes.numel() * 2 && absmax.numel() * 64 == out.numel(),
+           "nf4_dequant: sizes");
+  WB_CHECK(lut.size() == 16, "nf4_dequant: lut must have 16 entries");
+  float l[16];
+  for (int i = 0; i < 16; ++i) l[i] = static_cast<float>(lut[i]);
+  wb::nf4_dequant(codes.data_ptr(), absmax.data_ptr<float>(), out.data_ptr(), out.numel(), l, cur_stream());
+}
+
 void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
                  const c10::optional<at::Tensor>& h_out, const at::Tensor& w, at::Tensor& y,
                  const c10::optional<at::Tensor>& rstd, double eps) {
@@ -581,6 +593,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias") = py::none(), py::arg("res") = py::none());
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_ex", &gemm_ex);
+  m.def("nf4_dequant", &nf4_dequant);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

@@ -234,6 +234,43 @@ __device__ __forceinline__ void dequant_segment(uint8_t* row_base, int swz, uint
   }
 }
 
+struct NF4Seg {
+  uint4 w0, w1;
+  float am;
+};
+
+// Codes + absmax of dequant thread d's segment for flat iteration `it` of
+// this CTA (dense mode: every tile has nk = num_k + num_k2 iterations; the
+// second-operand iterations and out-of-range rows load nothing).
+template <bool B_MN>
+__device__ __forceinline__ void nf4_fetch(const Params& p, int it, int nk, int num_tiles, int d, NF4Seg& sg) {
+  sg.w0 = make_uint4(0, 0, 0, 0);
+  sg.w1 = sg.w0;
+  sg.am = 0.f;
+  const int j = it / nk, kb = it - j * nk;
+  const int t = blockIdx.x + j * gridDim.x;
+  if (t >= num_tiles || kb >= p.num_k) return;
+  int tm, tn;
+  tile_coords(t, p.num_m, p.num_n, tm, tn);
+  const int n0 = tn * BN, k0 = kb * BK;
+  const int64_t qb = p.q_cols / 2, qa = p.q_cols / 64;
+  if constexpr (!B_MN) {
+    const int n = n0 + d;  // B(n, k) = W[n][k]
+    if (n >= p.N) return;
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)n * qb + k0 / 2);
+    sg.w0 = __ldg(src);
+    sg.w1 = __ldg(src + 1);
+    sg.am = __ldg(p.q_absmax + (int64_t)n * qa + kb);
+  } else {
+    const int kr = k0 + (d & 63), nb = n0 + (d >> 6) * 64;  // B(n, k) = W[k][n]
+    if (kr >= p.K || nb >= p.N) return;
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)kr * qb + nb / 2);
+    sg.w0 = __ldg(src);
+    sg.w1 = __ldg(src + 1);
+    sg.am = __ldg(p.q_absmax + (int64_t)kr * qa + nb / 64);
+  }
+}
+
 template <bool A_MN, bool B_MN, int EPI, int GROUP, bool BQ>
 __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -401,58 +438,41 @@ __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
     }
   } else if (BQ && warp >= NUM_THREADS / 32) {
     // ------------------------------------------------------------ NF4 dequant producers
+    // Flat iteration space it -> (tile j of this CTA, k-block kb); the codes of
+    // iteration it+4 are loaded into registers while iteration it is
+    // converted, so four stages of global-load latency are in flight.
     const int d = threadIdx.x - NUM_THREADS;  // 0..255: one 64-element segment per stage
-    const int64_t qb = p.q_cols / 2;          // bytes per W row
-    const int64_t qa = p.q_cols / 64;         // absmax entries per W row
+    const int nk = p.num_k + num_k2;
+    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int total = my_tiles * nk;
+    uint8_t* row_off;
+    int swz;
+    if constexpr (!B_MN) {
+      row_off = tiles + A_BYTES + d * 128;
+      swz = d & 7;
+    } else {
+      row_off = tiles + A_BYTES + (d >> 6) * MN_BOX_BYTES + (d & 63) * 128;
+      swz = d & 7;
+    }
+    NF4Seg s0, s1, s2, s3;
+    nf4_fetch<B_MN>(p, 0, nk, num_tiles, d, s0);
+    nf4_fetch<B_MN>(p, 1, nk, num_tiles, d, s1);
+    nf4_fetch<B_MN>(p, 2, nk, num_tiles, d, s2);
+    nf4_fetch<B_MN>(p, 3, nk, num_tiles, d, s3);
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = tile_info<GROUP>(t, p);
-      const int n0 = ti.tn * BN;
-      const int nk = ti.num_k + (ti.num_k > 0 ? num_k2 : 0);
-      for (int kb = 0; kb < nk; ++kb) {
-        if (!mbar_wait_warp(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        if (kb < ti.num_k) {
-          uint8_t* b_dst = tiles + stage * STAGE_BYTES + A_BYTES;
-          const int k0 = kb * BK;
-          uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-          float am = 0.f;
-          uint8_t* row_base;
-          int swz;
-          if constexpr (!B_MN) {
-            // B(n, k) = W[n][k]: segment = row n0 + d, columns k0 .. k0+63
-            const int n = n0 + d;
-            if (n < p.N) {
-              const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)n * qb + k0 / 2);
-              w0 = __ldg(src);
-              w1 = __ldg(src + 1);
-              am = __ldg(p.q_absmax + (int64_t)n * qa + kb);
-            }
-            row_base = b_dst + d * 128;
-            swz = d & 7;
-          } else {
-            // B(n, k) = W[k][n]: segment = W row k0 + r, columns n0 + 64 j .. +63
-            const int r = d & 63, j = d >> 6;
-            const int kr = k0 + r, nb = n0 + j * 64;
-            if (kr < p.K && nb < p.N) {
-              const uint4* src = reinterpret_cast<const uint4*>(p.q + (int64_t)kr * qb + nb / 2);
-              w0 = __ldg(src);
-              w1 = __ldg(src + 1);
-              am = __ldg(p.q_absmax + (int64_t)kr * qa + nb / 64);
-            }
-            row_base = b_dst + j * MN_BOX_BYTES + r * 128;
-            swz = r & 7;
-          }
-          dequant_segment(row_base, swz, w0, w1, am, s->lut);
-          fence_proxy_async_shared();
-        }
-        mbar_arrive(&s->full[stage]);
-        if (++stage == STAGES) stage = 0, phase ^= 1;
+    for (int it = 0; it < total; ++it) {
+      if (!mbar_wait_warp(&s->empty[stage], phase ^ 1, abort, p.err, kErrTimeoutProducer)) break;
+      if (it % nk < p.num_k) {
+        dequant_segment(row_off + stage * STAGE_BYTES, swz, s0.w0, s0.w1, s0.am, s->lut);
+        fence_proxy_async_shared();
       }
+      mbar_arrive(&s->full[stage]);
+      if (++stage == STAGES) stage = 0, phase ^= 1;
+      s0 = s1;
+      s1 = s2;
+      s2 = s3;
+      nf4_fetch<B_MN>(p, it + 4, nk, num_tiles, d, s3);
     }
   } else {
     // ------------------------------------------------------------ epilogue

@@ -609,6 +609,41 @@ __global__ void softmax_grad_kernel(__nv_bfloat16* __restrict__ z, int64_t ldz, 
   }
 }
 
+// NF4 -> bf16 dequantisation (QLoRA base weights at training batch sizes:
+// dequantise once, then the dense tcgen05 GEMM).  One thread = one block of
+// 64 elements: 32 bytes of codes (element 2i in the high nibble) + one fp32
+// absmax -> 128 bytes of bf16.  Memory-bound: 2.56 bytes moved per element.
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint4* __restrict__ codes,
+                                                          const float* __restrict__ absmax,
+                                                          uint4* __restrict__ out, int64_t nblk, float4 l0,
+                                                          float4 l1, float4 l2, float4 l3) {
+  __shared__ float lut[16];
+  if (threadIdx.x < 16) {
+    const float t[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
+                         l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+    lut[threadIdx.x] = t[threadIdx.x];
+  }
+  __syncthreads();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nblk; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 w0 = __ldcs(codes + 2 * i);
+    const uint4 w1 = __ldcs(codes + 2 * i + 1);
+    const float am = __ldcs(absmax + i);
+    const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    uint4* dst = out + 8 * i;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 o;
+      uint32_t* op = &o.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t byte = (words[c] >> (8 * j)) & 0xffu;
+        op[j] = pack_bf16(lut[byte >> 4] * am, lut[byte & 15u] * am);
+      }
+      dst[c] = o;
+    }
+  }
+}
+
 inline int grid_for(int64_t work, int threads, int cap = 148 * 16) {
   int64_t g = (work + threads - 1) / threads;
   if (g > cap) g = cap;
@@ -682,6 +717,17 @@ void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T,
                    cudaStream_t st) {
   embedding_bwd_kernel<<<grid_for(T * (H / 4), 256), 256, 0, st>>>((const __nv_bfloat16*)dy, ids,
                                                                   dtable, T, H, V);
+}
+
+void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,
+                 cudaStream_t st) {
+  if (numel <= 0) return;
+  if (numel % 64) throw std::runtime_error("nf4_dequant: numel must be a multiple of 64");
+  const int64_t nblk = numel / 64;
+  nf4_dequant_kernel<<<grid_for(nblk, 256, 148 * 8), 256, 0, st>>>(
+      (const uint4*)codes, absmax, (uint4*)out, nblk, make_float4(lut[0], lut[1], lut[2], lut[3]),
+      make_float4(lut[4], lut[5], lut[6], lut[7]), make_float4(lut[8], lut[9], lut[10], lut[11]),
+      make_float4(lut[12], lut[13], lut[14], lut[15]));
 }
 
 void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,

@@ -22,6 +22,8 @@ void embedding_fwd(const void* table, const int64_t* ids, void* out, int64_t T, 
                    cudaStream_t st);
 void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T, int H, int64_t V,
                    cudaStream_t st);
+void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,
+                 cudaStream_t st);
 void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,
                 float b1, float b2, float eps, float wd, float bc1, float bc2,
                 const float* gscale_dev, float gscale_host, cudaStream_t st);

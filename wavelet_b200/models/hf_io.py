@@ -116,6 +116,7 @@ def load_hf_weights(model, path: Path) -> None:
             nq = quantize(tensors[name].to(device=q.device, dtype=model.flat.compute_dtype))
             q.codes.copy_(nq.codes)
             q.absmax.copy_(nq.absmax)
+            q.version += 1
 
 
 def save_hf(model, out_dir: Path, dtype: torch.dtype = torch.bfloat16, max_shard_bytes: int = 5 * 2**30) -> list[Path]:

@@ -42,7 +42,7 @@ def gemm(a: torch.Tensor, b, *, a_mn: bool = False, b_mn: bool = False,
     same accumulator (the LoRA-fused linear).  ``epi`` selects bf16 store,
     fp32 store or fp32 accumulate.
     """
-    from .nf4 import NF4Weight, nf4_table
+    from .nf4 import FUSED_MAX_M, NF4Weight, dequant_cache, nf4_table
 
     quant = isinstance(b, NF4Weight)
     M = a.shape[1] if a_mn else a.shape[0]
@@ -78,6 +78,13 @@ def gemm(a: torch.Tensor, b, *, a_mn: bool = False, b_mn: bool = False,
     if not quant and a2 is None:
         ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
         return out
+    if quant and M > FUSED_MAX_M:
+        # training-size M: dequantise once (cached), then the dense GEMM
+        b = dequant_cache().get(b)
+        quant = False
+        if a2 is None:
+            ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
+            return out
     if quant:
         ext().gemm_ex(a, a_mn, None, b_mn, out, N, epi, alpha, bias, res, a2, b2, b.codes, b.absmax, b.rows,
                       b.cols, list(nf4_table()))

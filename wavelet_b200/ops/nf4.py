@@ -46,6 +46,7 @@ class NF4Weight:
     absmax: torch.Tensor  # fp32 [rows * cols / 64]
     rows: int
     cols: int
+    version: int = 0  # bumped whenever codes/absmax change (invalidates dequant caches)
 
     @property
     def shape(self) -> tuple[int, int]:
@@ -85,6 +86,59 @@ def quantize(w: torch.Tensor, chunk_rows: int = 4096) -> NF4Weight:
         codes[r0 * cols // 2 : r1 * cols // 2] = (q[0::2] << 4) | q[1::2]
         absmax[r0 * cols // BLOCK : r1 * cols // BLOCK] = am
     return NF4Weight(codes, absmax, rows, cols)
+
+
+# GEMMs with more rows than this dequantise the weight once (memory-bound
+# kernel, cached) and run the dense GEMM; smaller ones (generation) dequantise
+# inside the GEMM so the weight is read at 0.5 byte per element.  With M rows
+# the in-kernel path repeats the dequantisation for every 128-row M tile.
+FUSED_MAX_M = 256
+
+
+class DequantCache:
+    """Small LRU of dequantised bf16 weights.  A decoder layer's backward
+    recomputes its forward and then runs the dgrad GEMMs in reverse order, so
+    four entries (qkv, o, gate/up, down) let the dgrads reuse the recompute's
+    dequantisation."""
+
+    def __init__(self, capacity: int = 4):
+        self.capacity = capacity
+        self.entries: list[tuple[tuple[int, int], torch.Tensor]] = []
+        self.pool: list[torch.Tensor] = []
+
+    def get(self, q: NF4Weight) -> torch.Tensor:
+        key = (id(q), q.version)
+        n = q.rows * q.cols
+        for i, (k, t) in enumerate(self.entries):
+            if k == key:
+                self.entries.append(self.entries.pop(i))
+                return t[:n].view(q.rows, q.cols)
+        buf = None
+        while len(self.entries) >= self.capacity:
+            self.pool.append(self.entries.pop(0)[1])
+        for i, t in enumerate(self.pool):
+            if t.numel() >= n and t.device == q.device:
+                buf = self.pool.pop(i)
+                break
+        if buf is None:
+            buf = torch.empty(n, device=q.device, dtype=torch.bfloat16)
+        out = buf[:n]
+        from . import ext
+
+        ext().nf4_dequant(q.codes, q.absmax, out, list(nf4_table()))
+        self.entries.append((key, buf))
+        return out.view(q.rows, q.cols)
+
+    def clear(self) -> None:
+        self.entries.clear()
+        self.pool.clear()
+
+
+_cache = DequantCache()
+
+
+def dequant_cache() -> DequantCache:
+    return _cache
 
 
 @torch.no_grad()
