@@ -267,6 +267,19 @@ class SFTDataset:
                 masks.append(torch.tensor(s.loss_mask[:S], dtype=torch.float32))
         return pack(seqs, masks)
 
+    def eval_batches(self, max_batches: int | None = None):
+        """One ordered pass over this rank's share of the samples (validation)."""
+        c = self.cfg
+        mine = [s for i, s in enumerate(self.samples()) if i % self.dp_world == self.dp_rank]
+        n = 0
+        for i in range(0, len(mine), c.micro_batch_size):
+            if max_batches is not None and n >= max_batches:
+                return
+            grp = mine[i : i + c.micro_batch_size]
+            yield pack([torch.tensor(s.input_ids[: c.seq_len]) for s in grp],
+                       [torch.tensor(s.loss_mask[: c.seq_len], dtype=torch.float32) for s in grp])
+            n += 1
+
     def state_dict(self) -> dict[str, Any]:
         return {"epoch": self.state.epoch, "cursor": self.state.cursor, "num_samples": dict(self.state.num_samples),
                 "num_tokens": dict(self.state.num_tokens)}

@@ -209,6 +209,8 @@ class RunMonitor:
                 self._wandb.log({k: v for k, v in row.items() if k != "timestamp" and k not in bad})
             except Exception:
                 pass
+        if ranks is not None:
+            self._last_ranks = ranks
         self._heartbeat("running", step, row, ranks)
 
     def log_event(self, name: str, *, step: int | None = None, payload: dict[str, Any] | None = None) -> None:
@@ -230,7 +232,7 @@ class RunMonitor:
         if not self._active():
             return
         self.log_event("run_finished", step=step, payload={"status": status})
-        self._heartbeat(status, step)
+        self._heartbeat(status, step, ranks=getattr(self, "_last_ranks", None))
         if self._wandb is not None:
             try:
                 self._wandb.finish()

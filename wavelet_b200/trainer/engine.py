@@ -84,6 +84,17 @@ class Engine:
             m.collect_cpu_grads()
         return loss
 
+    @torch.no_grad()
+    def sft_eval(self, b: PackedBatch) -> tuple[torch.Tensor, float]:
+        """Forward-only masked CE sum and loss-token count of one micro-batch."""
+        m = self.model
+        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen)
+        h = m.hidden(b.input_ids, ctx)
+        valid = (b.targets >= 0).float() * b.loss_mask.float()
+        lp, _ = lm_head.logprob_entropy(h.detach(), m.head_weight(), b.targets.clamp_min(0), 1.0,
+                                        chunk=self.chunk, want_entropy=False)
+        return -(lp * valid).sum(), float(valid.sum())
+
     def optimizer_step(self, lr: float) -> dict[str, float]:
         return self.opt.step(lr)
 

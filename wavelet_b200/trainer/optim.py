@@ -76,7 +76,7 @@ def newton_schulz5(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.
 class FlatOptimizer:
     """Common driver: reduce-scatter, norm/clip, per-type update, all-gather."""
 
-    def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1):
+    def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1, fabric=None):
         self.flat = flat
         self.cfg = cfg
         self.type = cfg.type
@@ -87,7 +87,12 @@ class FlatOptimizer:
             weight_decay=0.0 if cfg.type in ("adam", "adam_8bit") else cfg.weight_decay,
             max_grad_norm=max_grad_norm,
         )
-        self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world)
+        if fabric is not None and cfg.type in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
+            from ..parallel.zero import FusedShardedAdamW
+
+            self.adamw = FusedShardedAdamW(flat, hyper, fabric)  # fused peer-memory RS + AdamW + AG
+        else:
+            self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world)
         self.momentum_buf = None
 
     @property

@@ -28,6 +28,9 @@ import torch
 from ..configs.config import SFTConfig
 from ..models.config import resolve_arch
 from ..models.qwen import build_model
+from .gc_control import StepGarbageCollector
+from .profiling import CudaMemoryProfiler, StepProfiler
+from .telemetry import Telemetry, node_metrics, rank_rows
 from ..monitor import RunMonitor, setup_logger
 from ..parallel.dist import Groups, ParallelDims, destroy_distributed, init_distributed
 from ..utils import pathing
@@ -69,14 +72,20 @@ class SFTTrainer:
         dev = w.device
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
-        self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed,
+        self.fabric = None
+        if dev.type == "cuda" and dims.dp == w.world_size and c.fsdp.backend != "gloo":
+            from ..parallel.fabric import maybe_fabric
+
+            self.fabric = maybe_fabric(dp_world, dp_rank, dev)
+        self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed, fabric=self.fabric,
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed)
         if not c.model.random_init and _has_weights(c.model.name):
             from ..models.hf_io import load_hf_weights
 
             load_hf_weights(self.model, Path(c.model.name))
-        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, self.groups.dp, dp_world)
+        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, self.groups.dp, dp_world,
+                                       fabric=self.fabric)
         self.engine = Engine(self.model, self.optimizer.adamw.h, self.groups.dp, dp_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
@@ -84,6 +93,7 @@ class SFTTrainer:
 
         tok = None if c.data.source == "fake" else load_tokenizer(c.model.name)
         self.dataset = SFTDataset(c.data, tok, dp_rank, dp_world, seed=c.seed)
+        self.val_dataset = SFTDataset(c.val.data, tok, dp_rank, dp_world, seed=c.seed) if c.val is not None else None
         gm = c.data.micro_batch_size * dp_world
         if c.data.batch_size % gm:
             raise ValueError(
@@ -118,9 +128,34 @@ class SFTTrainer:
         self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
         lora_params = self.model.lora.num_trainable() if self.model.lora is not None else None
         self.perf = PerfTracker(arch, w.device, lora_rank=c.lora.rank if c.lora else None, lora_params=lora_params)
-        if c.gc is not None:
-            gc.disable()
+        self.telemetry = Telemetry(w, replication=max(1, dims.tp * dims.cp))
+        self.gc = StepGarbageCollector(c.gc.interval) if c.gc is not None else None
+        self.profiler = None
+        if c.profiler is not None:
+            path = c.profiler.trace_path or out / "traces" / f"rank{w.rank}.json"
+            self.profiler = StepProfiler(path, start_step=c.profiler.start_step, end_step=c.profiler.end_step,
+                                         record_shapes=c.profiler.record_shapes,
+                                         profile_memory=c.profiler.profile_memory)
+        self.mem_profiler = None
+        if c.memory_profiler is not None and dev.type == "cuda":
+            self.mem_profiler = CudaMemoryProfiler(c.memory_profiler.output_dir or out / "memory", rank=w.rank,
+                                                   interval=c.memory_profiler.interval,
+                                                   max_entries=c.memory_profiler.max_entries)
         return self
+
+    # ------------------------------------------------------------ validation
+    def validate(self) -> dict[str, float]:
+        """Token-mean masked CE over one pass of the validation set (all ranks)."""
+        dev = self.world.device
+        tot = torch.zeros(2, dtype=torch.float64, device=dev)
+        for b in self.val_dataset.eval_batches():
+            loss, n = self.engine.sft_eval(b.to(dev))
+            tot[0] += loss.double()
+            tot[1] += n
+        if self.world.distributed:
+            torch.distributed.all_reduce(tot, group=self.groups.dp)
+        loss_v, n_v = tot.tolist()
+        return {"val/loss": loss_v / max(n_v, 1.0), "val/tokens": n_v}
 
     # ------------------------------------------------------------------ loop
     def train_step(self) -> dict[str, Any]:
@@ -150,22 +185,35 @@ class SFTTrainer:
         dt = time.perf_counter() - t0
         m = {"loss": loss_v, "optim/grad_norm": stats["grad_norm"], "optim/lr": lr, "train/loss_tokens": total}
         m.update(self.perf.step_metrics(tokens * (self.world.world_size // max(1, self.config.fsdp.tp)), dt))
+        m["_tokens"], m["_seconds"] = float(tokens), dt
         return m
 
     def train(self) -> int:
         c = self.config
         status = "failed"
         try:
+            if self.val_dataset is not None and c.val.eval_on_start:
+                self.monitor.log(self.validate(), self.step)
             while self.step < self.total_steps:
+                if self.profiler is not None:
+                    self.profiler.before_step(self.step + 1)
                 metrics = self.train_step()
+                ranks = self.telemetry.sample(metrics.pop("_tokens"), metrics.pop("_seconds"))
+                metrics.update(node_metrics(ranks))
+                if self.profiler is not None:
+                    self.profiler.after_step(self.step)
+                if self.mem_profiler is not None:
+                    self.mem_profiler.step(self.step)
+                if self.val_dataset is not None and self.step % c.val.interval == 0:
+                    metrics.update(self.validate())
                 if self.step % c.log.log_every == 0:
-                    self.monitor.log(metrics, self.step)
+                    self.monitor.log(metrics, self.step, ranks=rank_rows(ranks))
                     log.info("step %d loss %.4f grad_norm %.3f tok/s %.0f", self.step, metrics["loss"],
                              metrics["optim/grad_norm"], metrics.get("perf/tokens_per_second", 0))
                 if self.ckpt is not None and c.ckpt.interval and self.step % c.ckpt.interval == 0:
                     self.save_checkpoint()
-                if c.gc is not None and self.step % c.gc.interval == 0:
-                    gc.collect(1)
+                if self.gc is not None:
+                    self.gc.run(self.step)
             if self.ckpt is not None:
                 self.save_checkpoint(block=True)
             status = "completed"
@@ -177,6 +225,9 @@ class SFTTrainer:
                 except Exception:
                     status = "failed"
             self.monitor.finish(status=status, step=self.step)
+            for closer in (self.profiler, self.mem_profiler, self.gc):
+                if closer is not None:
+                    closer.close()
 
     def save_checkpoint(self, block: bool = False) -> None:
         c = self.config
@@ -207,6 +258,8 @@ def main(argv: list[str] | None = None) -> int:
     try:
         return trainer.train()
     finally:
+        if trainer.fabric is not None:
+            trainer.fabric.close()
         destroy_distributed()
 
 
