@@ -1,0 +1,104 @@
+"""CLI tools, dashboard API, SLURM rendering and trace conversion on CPU."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_dashboard_api_over_synthetic_run(tmp_path):
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.dashboard.server import RunRegistry, build_app, default_static_dir
+    from wavelet_b200.dashboard.synth import write_synthetic_run
+
+    write_synthetic_run(tmp_path / "runA", steps=30, ranks=4)
+    app = build_app(RunRegistry([tmp_path]), default_static_dir())
+    c = TestClient(app)
+    assert c.get("/api/health").json()["ok"]
+    runs = c.get("/api/runs").json()["runs"]
+    assert runs[0]["run_id"] == "runA" and runs[0]["status"] == "completed"
+    keys = c.get("/api/runs/runA/metrics/keys").json()
+    assert "loss" in keys["trainer"] and "reward/mean" in keys["orchestrator"]
+    s = c.get("/api/runs/runA/series", params={"keys": "loss", "points": 10}).json()
+    assert 0 < len(s["steps"]) <= 12 and len(s["series"]["loss"]) == len(s["steps"])
+    assert max(s["series"]["loss"]) == max(json.loads(l)["loss"] for l in (tmp_path / "runA/metrics.jsonl").read_text().splitlines())
+    assert c.get("/api/runs/runA/series", params={"keys": "nope"}).status_code == 400
+    assert len(c.get("/api/runs/runA/nodes").json()["ranks"]) == 4
+    q = c.get("/api/runs/runA/queue").json()
+    assert q["published"] == 30 and q["consumed"] == 30
+    rows = c.get("/api/runs/runA/rollouts/rows", params={"step": 3}).json()
+    assert rows["total"] == 4
+    assert c.get("/api/runs/runA/evals").json()["metrics"]
+    assert "trainer.log" in c.get("/api/runs/runA/logs").json()["logs"]
+    assert "step 30" in c.get("/api/runs/runA/logs/trainer.log").text
+    assert c.get("/api/runs/runA/logs/..%2F..%2Fetc%2Fpasswd").status_code == 404
+    assert c.get("/").status_code == 200
+    # incremental tail: a new row appears without reopening
+    with open(tmp_path / "runA/metrics.jsonl", "a") as f:
+        f.write(json.dumps({"step": 31, "loss": 0.1}) + "\n")
+    s2 = c.get("/api/runs/runA/series", params={"keys": "loss", "after": 30}).json()
+    assert s2["steps"] == [31.0]
+
+
+def test_trace_conversion(tmp_path):
+    from wavelet_b200.orchestrator.trace import TraceWriter
+    from wavelet_b200.tools.convert_traces import main
+
+    tw = TraceWriter(tmp_path / "run", "orchestrator")
+    tw.event("batch_published", step=3, policy_step=2, path="x")
+    tw.event("rollout", step=3, rollout_id="3:0", reward=1.0)
+    assert main([str(tmp_path / "run"), "--output-dir", str(tmp_path / "ds")]) == 0
+    import pyarrow.parquet as pq
+
+    t = pq.read_table(tmp_path / "ds" / "default" / "train-00000-of-00001.parquet").to_pylist()
+    assert [r["event"] for r in t] == ["batch_published", "rollout"]
+    assert json.loads(t[1]["payload"])["reward"] == 1.0 and t[0]["policy_step"] == 2
+
+
+def test_slurm_render_and_nodelist(tmp_path):
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.deployment.slurm import expand_nodelist, render_sbatch, worker_commands
+
+    assert expand_nodelist("gpu[01-03,07],login1") == ["gpu01", "gpu02", "gpu03", "gpu07", "login1"]
+    cfg = RLConfig.model_validate({"output_dir": str(tmp_path), "slurm": {"partition": "p", "time_limit": "1:00:00"},
+                                   "deployment": {"type": "multi_node", "num_train_nodes": 1,
+                                                  "num_inference_nodes": 1, "gpus_per_node": 8},
+                                   "launcher": {"mode": "process"}})
+    script = render_sbatch(cfg, "rl", ["@", "x.yaml"])
+    assert "#SBATCH --nodes=2" in script and "#SBATCH --partition=p" in script and "slurm-worker rl" in script
+    t = worker_commands(cfg, "rl", ["@", "x.yaml"], 0, ["n0", "n1"])
+    assert "--nproc-per-node=8" in t[0] and "rl-inference" in t[1]
+    i = worker_commands(cfg, "rl", ["@", "x.yaml"], 1, ["n0", "n1"])
+    assert "inference-server" in i[0]
+
+
+@pytest.mark.integration
+def test_convert_checkpoint_and_benchmark_compare(tmp_path):
+    import os
+
+    out = tmp_path / "out"
+    cfg = tmp_path / "sft.yaml"
+    cfg.write_text((ROOT / "examples" / "tiny_cpu" / "sft.yaml").read_text().replace("outputs/tiny_cpu_sft", str(out))
+                   .replace("max_steps: 10", "max_steps: 3") + "ckpt:\n  mode: async\n  interval: 3\n")
+    env = {**os.environ, "WAVELET_FORCE_CPU": "1"}
+    r = subprocess.run([sys.executable, "-m", "wavelet_b200", "sft", "@", str(cfg)], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    r = subprocess.run([sys.executable, "-m", "wavelet_b200", "convert-checkpoint", str(out / "checkpoint-3"),
+                        str(tmp_path / "hf"), "--dtype", "float32"], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert (tmp_path / "hf" / "config.json").exists() and list((tmp_path / "hf").glob("*.safetensors"))
+    from wavelet_b200.tools.benchmark import aggregate, compare
+
+    res = aggregate(out, warmup_steps=1)
+    assert res["steps"] == 2 and res["tokens_per_second"]["median"] > 0
+    worse = json.loads(json.dumps(res))
+    worse["tokens_per_second"]["median"] *= 0.5
+    lines, bad = compare(worse, res, 0.05)
+    assert bad and "REGRESSION" in "\n".join(lines)

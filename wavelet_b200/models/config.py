@@ -80,6 +80,14 @@ class ArchConfig:
         total += emb + H + (0 if self.tie_embeddings else emb)
         return total
 
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "ArchConfig":
+        d = dict(d)
+        if "mlp_only_layers" in d:
+            d["mlp_only_layers"] = tuple(d["mlp_only_layers"])
+        known = set(cls.__dataclass_fields__)
+        return cls(**{k: v for k, v in d.items() if k in known})
+
     def to_dict(self) -> dict[str, Any]:
         d = asdict(self)
         d["mlp_only_layers"] = list(self.mlp_only_layers)

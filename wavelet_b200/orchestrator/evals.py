@@ -1,0 +1,96 @@
+"""Evaluation runs over configured environments (``eval.env``).
+
+Built-in environments (no network, no external verifier package):
+
+* ``reverse`` — synthetic reverse-the-prompt task (``args``: ``prompt_len``,
+  ``vocab``, ``seed``), reward = fraction of generated tokens matching the
+  reversed prompt;
+* ``file:<path>`` — prompt rows from a local JSONL/Parquet file scored by the
+  configured reward (``reference_match`` / ``math_format`` against ``answer``).
+
+For every example ``rollouts_per_example`` samples are drawn; the metrics are
+the mean reward, pass@1 and pass@k (unbiased estimator of Chen et al. 2021,
+"Evaluating Large Language Models Trained on Code") with success = reward >=
+``args.success_threshold`` (default 1.0).  Results go to
+``eval_metrics.jsonl`` and ``evals/<env>/step-<n>.jsonl`` (reference
+orchestrator/eval_utils.py and entrypoints/rl_evals.py).
+"""
+
+from __future__ import annotations
+
+import json
+import math
+from dataclasses import replace
+from pathlib import Path
+from types import SimpleNamespace
+from typing import Any
+
+from ..monitor import append_jsonl, utc_now
+from .reward import RLRewardScorer
+from .rollouts import RLOrchestrator, SyntheticReversePrompts
+
+
+def pass_at_k(n: int, c: int, k: int) -> float:
+    if n - c < k:
+        return 1.0
+    return 1.0 - math.prod(1.0 - k / i for i in range(n - c + 1, n + 1))
+
+
+def _env_prompts(cfg, env):
+    a = env.args or {}
+    if env.id.startswith("file:"):
+        from .sources import FilePromptSource
+
+        data = cfg.data.model_copy(update={"path": Path(env.id[5:]), "shuffle": False})
+        return FilePromptSource(SimpleNamespace(data=data, model=cfg.model))
+    if env.resolved_name in ("reverse", "reverse_match", "synthetic-reverse"):
+        vocab = int(a.get("vocab", cfg.data.fake_vocab_size))
+        return SyntheticReversePrompts(vocab, int(a.get("prompt_len", cfg.data.fake_prompt_len)), seed=int(a.get("seed", 12345)))
+    raise ValueError(f"unknown eval environment {env.id!r} (built-ins: reverse, file:<path>)")
+
+
+def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]:
+    n_ex = env.num_examples if env.num_examples > 0 else 32
+    k = env.rollouts_per_example
+    reward_cfg = cfg.reward
+    if env.resolved_name in ("reverse", "reverse_match", "synthetic-reverse"):
+        reward_cfg = cfg.reward.model_copy(update={"mode": "reverse_match"})
+    ecfg = cfg.model_copy(update={"reward": reward_cfg,
+                                  "orchestrator": cfg.orchestrator.model_copy(update={"rollouts_per_example": k})})
+    s = env.sampling
+    if s.max_completion_tokens or s.temperature is not None:
+        samp = cfg.inference.sampling.model_copy(update={
+            kk: v for kk, v in (("max_completion_tokens", s.max_completion_tokens), ("temperature", s.temperature),
+                                ("top_p", s.top_p), ("top_k", s.top_k)) if v is not None})
+        ecfg = ecfg.model_copy(update={"inference": cfg.inference.model_copy(update={"sampling": samp})})
+    orch = RLOrchestrator(ecfg, engine, None, _env_prompts(cfg, env))
+    prompts = orch.prompts.take(n_ex)
+    recs = orch.generate_records(prompts, step)
+    scorer = RLRewardScorer(reward_cfg)
+    recs = [replace(r, reward=scorer.score(r)) for r in recs]
+    thr = float((env.args or {}).get("success_threshold", 1.0))
+    by_ex: dict[str, list[float]] = {}
+    for r in recs:
+        by_ex.setdefault(str((r.metadata or {}).get("example_id")), []).append(float(r.reward or 0.0))
+    rewards = [x for v in by_ex.values() for x in v]
+    m = {f"eval/{env.resolved_name}/reward_mean": sum(rewards) / max(1, len(rewards)),
+         f"eval/{env.resolved_name}/pass@1": sum(pass_at_k(len(v), sum(x >= thr for x in v), 1) for v in by_ex.values()) / max(1, len(by_ex)),
+         f"eval/{env.resolved_name}/pass@{k}": sum(pass_at_k(len(v), sum(x >= thr for x in v), k) for v in by_ex.values()) / max(1, len(by_ex)),
+         f"eval/{env.resolved_name}/num_examples": float(len(by_ex))}
+    d = out_dir / "evals" / env.resolved_name
+    d.mkdir(parents=True, exist_ok=True)
+    with (d / f"step-{step}.jsonl").open("w") as f:
+        for r in recs:
+            md = r.metadata or {}
+            f.write(json.dumps({"example_id": md.get("example_id"), "reward": r.reward,
+                                "completion_ids": md.get("completion_ids")}) + "\n")
+    return m
+
+
+def run_evals(cfg, engine, step: int = 0, envs=None) -> dict[str, Any]:
+    out = Path(cfg.output_dir)
+    metrics: dict[str, Any] = {}
+    for env in envs if envs is not None else cfg.eval.env:
+        metrics.update(run_eval_env(cfg, engine, env, step, out))
+    append_jsonl(out / "eval_metrics.jsonl", {"step": step, "timestamp": utc_now(), **metrics})
+    return metrics

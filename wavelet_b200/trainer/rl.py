@@ -218,13 +218,20 @@ class RLTrainer:
                     self.exporter.export(self.model, self.step)
                 if self.ckpt is not None and c.ckpt.interval and self.step % c.ckpt.interval == 0:
                     self.ckpt.save(self.step, model=self.model, optimizer=self.optimizer, data_state=None,
-                                   meta={"arch": self.model.cfg.to_dict()}, scheduler_state={"step": self.step})
+                                   meta={"arch": self.model.cfg.to_dict(), **_lora_meta(self.config, self.model)}, scheduler_state={"step": self.step})
             status = "completed"
             return 0
         finally:
             if self.ckpt is not None:
                 self.ckpt.wait()
             self.monitor.finish(status=status, step=self.step)
+
+
+def _lora_meta(cfg, model) -> dict:
+    if model.lora is None:
+        return {"model_name": cfg.model.name}
+    return {"model_name": cfg.model.name, "lora_rank": model.lora.rank, "lora_alpha": model.lora.alpha,
+            "lora_target_modules": model.lora.target_modules}
 
 
 def main(argv: list[str] | None = None) -> int:

@@ -233,7 +233,7 @@ class SFTTrainer:
         c = self.config
         self.ckpt.save(
             self.step, model=self.model, optimizer=self.optimizer, data_state=self.dataset.state_dict(),
-            meta={"arch": self.model.cfg.to_dict(), "numel": self.model.flat.numel},
+            meta={"arch": self.model.cfg.to_dict(), "numel": self.model.flat.numel, **_lora_meta(self.config, self.model)},
             scheduler_state={"step": self.step}, block=block,
         )
         self.monitor.log_event("checkpoint_saved", step=self.step)
@@ -242,6 +242,13 @@ class SFTTrainer:
 def _has_weights(name: str) -> bool:
     p = Path(name)
     return p.is_dir() and any(p.glob("*.safetensors"))
+
+
+def _lora_meta(cfg, model) -> dict:
+    if model.lora is None:
+        return {"model_name": cfg.model.name}
+    return {"model_name": cfg.model.name, "lora_rank": model.lora.rank, "lora_alpha": model.lora.alpha,
+            "lora_target_modules": model.lora.target_modules}
 
 
 def main(argv: list[str] | None = None) -> int:
