@@ -102,3 +102,31 @@ def test_convert_checkpoint_and_benchmark_compare(tmp_path):
     worse["tokens_per_second"]["median"] *= 0.5
     lines, bad = compare(worse, res, 0.05)
     assert bad and "REGRESSION" in "\n".join(lines)
+
+
+def test_debug_preflight_and_trainer_inspect(tmp_path, capsys):
+    from wavelet_b200.debug import build_preflight_report, inspect_rollout_batch, main
+    from wavelet_b200.configs.config import RLConfig
+
+    ok = build_preflight_report(RLConfig.model_validate({"output_dir": str(tmp_path / "o"), "model": {"name": "tiny"},
+                                                         "data": {"source": "fake"}}))
+    assert ok["ok"], ok["checks"]
+    bad = build_preflight_report(RLConfig.model_validate({
+        "output_dir": str(tmp_path / "o"), "model": {"name": "tiny"}, "algo": {"type": "grpo"}, "data": {"source": "fake"},
+        "orchestrator": {"rollouts_per_example": 1}}))
+    assert not bad["ok"] and any(c["name"] == "grpo_group" for c in bad["checks"])
+    assert main(["preflight", "--json", "--output-dir", str(tmp_path / "o"), "--model.name", "tiny",
+                 "--data.source", "fake"]) == 0
+    nf = build_preflight_report(RLConfig.model_validate({"output_dir": str(tmp_path / "o"), "data": {"source": "local"},
+                                                         "model": {"name": "tiny"}}))
+    assert any(c["name"] == "data_paths" and c["status"] == "error" for c in nf["checks"])
+    # a rollout batch with a misaligned mask is flagged
+    d = tmp_path / "step-000000"
+    d.mkdir()
+    rows = [{"prompt": [], "completion": [], "advantage": 0.5, "reward": 1.0, "input_ids": [1, 2, 3],
+             "loss_mask": [False, True, True], "inference_logprobs": [-0.1, -0.2]},
+            {"prompt": [], "completion": [], "advantage": 0.5, "reward": 1.0, "input_ids": [1, 2, 3],
+             "loss_mask": [False, True]}]
+    (d / "rollouts.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+    rep = inspect_rollout_batch(d)
+    assert rep["rows"] == 2 and not rep["ok"] and rep["issues"][0]["row"] == 1

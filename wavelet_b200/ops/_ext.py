@@ -69,6 +69,12 @@ def _stamp_path() -> Path:
     return BUILD_DIR / f"{NAME}.hash"
 
 
+def is_built() -> bool:
+    """True when the in-tree library exists and matches the current sources."""
+    st = _stamp_path()
+    return _so_path() is not None and st.exists() and st.read_text().strip() == source_hash()
+
+
 def build(verbose: bool = False) -> ModuleType:
     """Compile the extension for sm_100a (works without a GPU) and load it."""
     from torch.utils import cpp_extension
