@@ -102,10 +102,19 @@ class Routing:
 
 
 class MoEBlock:
-    def __init__(self, cfg, layer_idx: int):
+    """Sparse MLP of one decoder layer (GPU path and the CPU fallbacks of the
+    same ops).  With ``ep_size > 1`` this rank holds experts
+    [ep_rank * E/ep, (ep_rank + 1) * E/ep) and token copies travel to their
+    expert's rank and back (dispatch / combine); gradients take the same
+    route in reverse.  ``ep_group`` is set by the model before each forward."""
+
+    def __init__(self, cfg, layer_idx: int, ep_size: int = 1, ep_rank: int = 0):
         self.cfg = cfg
         self.layer = layer_idx
         self.ep_group = None
+        self.ep_size = ep_size
+        self.ep_rank = ep_rank
+        self.E_loc = cfg.num_experts // ep_size
         self.aux_loss_scale = 0.0
         self.last_aux = None
         self.last_counts = None
@@ -120,20 +129,75 @@ class MoEBlock:
         w = topv / s if cfg.norm_topk_prob else topv
         return probs, topv, topi, s, w
 
-    def _experts(self, h2, P, rt: Routing):
+    def _experts(self, x, P, rt: Routing):
+        """Expert FFNs of this rank over the rows ``x[rt.tok]`` laid out by ``rt``."""
         cfg = self.cfg
-        E, H, Ie = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
-        xs = torch.zeros(rt.R, H, device=h2.device, dtype=h2.dtype)
-        xs.index_copy_(0, rt.pos, h2.index_select(0, rt.tok))
-        m = ops.ext()
-        gu = torch.empty(rt.R, 2 * Ie, device=h2.device, dtype=h2.dtype)
-        m.gemm_grouped(xs, False, P["exp_gu_w"].view(E * 2 * Ie, H), False, gu, 1, rt.R, 2 * Ie, H, rt.tile_group,
-                       2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
+        E, H, Ie = self.E_loc, cfg.hidden_size, cfg.moe_intermediate_size
+        xs = torch.zeros(rt.R, H, device=x.device, dtype=x.dtype)
+        xs.index_copy_(0, rt.pos, x.index_select(0, rt.tok))
+        gu = torch.empty(rt.R, 2 * Ie, device=x.device, dtype=x.dtype)
+        ops.gemm_grouped(xs, False, P["exp_gu_w"].view(E * 2 * Ie, H), False, gu, 1, rt.R, 2 * Ie, H, rt.tile_group,
+                         2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
         a = ops.swiglu_fwd(gu)
-        y = torch.empty(rt.R, H, device=h2.device, dtype=h2.dtype)
-        m.gemm_grouped(a, False, P["exp_down_w"].view(E * H, Ie), False, y, 1, rt.R, H, Ie, rt.tile_group, H, E * H,
-                       None, None, E, ops.EPI_BF16, 1.0)
+        y = torch.empty(rt.R, H, device=x.device, dtype=x.dtype)
+        ops.gemm_grouped(a, False, P["exp_down_w"].view(E * H, Ie), False, y, 1, rt.R, H, Ie, rt.tile_group, H, E * H,
+                         None, None, E, ops.EPI_BF16, 1.0)
         return xs, gu, a, y
+
+    def _experts_bwd(self, dy, c, P, G):
+        """Backward of ``_experts`` from the padded-row gradient ``dy`` [R, H];
+        accumulates the expert weight gradients, returns d(xs) [R, H]."""
+        cfg = self.cfg
+        E, H, Ie = self.E_loc, cfg.hidden_size, cfg.moe_intermediate_size
+        rt: Routing = c["rt"]
+        da = torch.empty(rt.R, Ie, device=dy.device, dtype=dy.dtype)
+        ops.gemm_grouped(dy, False, P["exp_down_w"].view(E * H, Ie), True, da, 1, rt.R, Ie, H, rt.tile_group, H, E * H,
+                         None, None, E, ops.EPI_BF16, 1.0)
+        if G.get("exp_down_w") is not None:
+            ops.gemm_grouped(dy, True, c["a"], True, G["exp_down_w"].view(E * H, Ie), 2, H, Ie, rt.R, None, 0, 0,
+                             rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
+        dgu = ops.swiglu_bwd(c["gu"], da)
+        del da
+        if G.get("exp_gu_w") is not None:
+            ops.gemm_grouped(dgu, True, c["xs"], True, G["exp_gu_w"].view(E * 2 * Ie, H), 2, 2 * Ie, H, rt.R, None, 0,
+                             0, rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
+        dxs = torch.empty(rt.R, H, device=dy.device, dtype=dy.dtype)
+        ops.gemm_grouped(dgu, False, P["exp_gu_w"].view(E * 2 * Ie, H), True, dxs, 1, rt.R, H, 2 * Ie, rt.tile_group,
+                         2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
+        return dxs
+
+    # ------------------------------------------------------- dispatch / combine
+    def _a2a(self, out, inp, out_splits, in_splits):
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.ep_group)
+        return out
+
+    def _dispatch(self, h2, topi):
+        """Send every (token, slot) copy to its expert's rank.  Returns the
+        plan (orders and split sizes) and the received rows, which arrive
+        grouped by source rank, then by local expert."""
+        T, k = topi.shape
+        ep, El = self.ep_size, self.E_loc
+        e = topi.reshape(-1)
+        order = torch.argsort(e, stable=True)  # by destination rank, then local expert
+        cnt = torch.bincount(e, minlength=self.cfg.num_experts)
+        recv = torch.empty_like(cnt)
+        self._a2a(recv, cnt, None, None)  # recv[src * El + el]: copies from src for my expert el
+        send_h = cnt.view(ep, El).sum(1).tolist()
+        recv_mat = recv.view(ep, El)
+        recv_h = recv_mat.sum(1).tolist()  # host sync: the split sizes size the transfers
+        tok = torch.arange(T, device=h2.device).repeat_interleave(k)[order]
+        x_recv = h2.new_empty(sum(recv_h), h2.shape[1])
+        self._a2a(x_recv, h2.index_select(0, tok), recv_h, send_h)
+        el = torch.repeat_interleave(torch.arange(El, device=h2.device).repeat(ep), recv_mat.reshape(-1))
+        return dict(order=order, tok=tok, send=send_h, recv=recv_h, counts=cnt), x_recv, el
+
+    def _combine(self, y_recv, plan, T, k):
+        """Return expert outputs to their tokens' ranks, in (token, slot) order."""
+        y_send = y_recv.new_empty(T * k, y_recv.shape[1])
+        self._a2a(y_send, y_recv, plan["send"], plan["recv"])
+        y_copy = torch.empty_like(y_send)
+        y_copy[plan["order"]] = y_send
+        return y_copy
 
     # ------------------------------------------------------------ forward
     def forward(self, x2, P, save: bool):
@@ -142,48 +206,58 @@ class MoEBlock:
         k = cfg.num_experts_per_tok
         h2, rstd2, _ = ops.rmsnorm_fwd(x2, P["post_norm"], cfg.rms_eps)
         probs, topv, topi, s, w = self._route(h2, P)
-        rt = Routing(topi, cfg.num_experts)
-        xs, gu, a, y = self._experts(h2, P, rt)
-        contrib = y.index_select(0, rt.pos).float() * w.reshape(-1, 1)
+        if self.ep_size > 1:
+            plan, x_recv, el = self._dispatch(h2, topi)
+            rt = Routing(el.view(-1, 1), self.E_loc)
+            xs, gu, a, y = self._experts(x_recv, P, rt)
+            y_copy = self._combine(y.index_select(0, rt.pos), plan, T, k)
+            counts = plan["counts"]
+        else:
+            plan = None
+            rt = Routing(topi, cfg.num_experts)
+            xs, gu, a, y = self._experts(h2, P, rt)
+            y_copy = y.index_select(0, rt.pos)
+            counts = rt.counts
+        contrib = y_copy.float() * w.reshape(-1, 1)
         out = (x2.float() + contrib.view(T, k, -1).sum(1)).to(x2.dtype)
-        f = rt.counts.float() / (T * k)
+        f = counts.float() / (T * k)
         self.last_aux = float(cfg.num_experts * (f * probs.mean(0)).sum())
-        self.last_counts = rt.counts
+        self.last_counts = counts
         cache = None
         if save:
-            cache = dict(h2=h2, rstd2=rstd2, probs=probs, topv=topv, topi=topi, s=s, w=w, rt=rt, xs=xs, gu=gu, a=a, y=y, f=f)
+            cache = dict(h2=h2, rstd2=rstd2, probs=probs, topv=topv, topi=topi, s=s, w=w, rt=rt, xs=xs, gu=gu, a=a,
+                         y_copy=y_copy, f=f, plan=plan)
         return out, cache
 
     # ------------------------------------------------------------ backward
     def backward(self, dout, x2, c, P, G):
         cfg = self.cfg
-        E, H, Ie, k = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts_per_tok
+        H, k = cfg.hidden_size, cfg.num_experts_per_tok
         T = x2.shape[0]
         rt: Routing = c["rt"]
-        m = ops.ext()
-        dout_rows = dout.index_select(0, rt.tok)  # [T*k, H]
+        tok_copy = torch.arange(T, device=dout.device).repeat_interleave(k)
+        dout_rows = dout.index_select(0, tok_copy).float()  # [T*k, H] in (token, slot) order
         w = c["w"].reshape(-1, 1)
-        dy = torch.zeros(rt.R, H, device=dout.device, dtype=dout.dtype)
-        dy.index_copy_(0, rt.pos, (dout_rows.float() * w).to(dout.dtype))
-        dw = (dout_rows.float() * c["y"].index_select(0, rt.pos).float()).sum(-1).view(T, k)
-        # down projection
-        da = torch.empty(rt.R, Ie, device=dout.device, dtype=dout.dtype)
-        m.gemm_grouped(dy, False, P["exp_down_w"].view(E * H, Ie), True, da, 1, rt.R, Ie, H, rt.tile_group, H, E * H,
-                       None, None, E, ops.EPI_BF16, 1.0)
-        if G.get("exp_down_w") is not None:
-            m.gemm_grouped(dy, True, c["a"], True, G["exp_down_w"].view(E * H, Ie), 2, H, Ie, rt.R, None, 0, 0,
-                           rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
-        dgu = ops.swiglu_bwd(c["gu"], da)
-        del da
-        if G.get("exp_gu_w") is not None:
-            m.gemm_grouped(dgu, True, c["xs"], True, G["exp_gu_w"].view(E * 2 * Ie, H), 2, 2 * Ie, H, rt.R, None, 0,
-                           0, rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
-        dxs = torch.empty(rt.R, H, device=dout.device, dtype=dout.dtype)
-        m.gemm_grouped(dgu, False, P["exp_gu_w"].view(E * 2 * Ie, H), True, dxs, 1, rt.R, H, 2 * Ie, rt.tile_group,
-                       2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
-        del dgu
+        dw = (dout_rows * c["y_copy"].float()).sum(-1).view(T, k)
+        dy_copy = (dout_rows * w).to(dout.dtype)
+        plan = c["plan"]
+        if plan is not None:
+            dy_recv = dout.new_empty(sum(plan["recv"]), H)
+            self._a2a(dy_recv, dy_copy[plan["order"]], plan["recv"], plan["send"])
+            dy = torch.zeros(rt.R, H, device=dout.device, dtype=dout.dtype)
+            dy.index_copy_(0, rt.pos, dy_recv)
+        else:
+            dy = torch.zeros(rt.R, H, device=dout.device, dtype=dout.dtype)
+            dy.index_copy_(0, rt.pos, dy_copy)
+        dxs = self._experts_bwd(dy, c, P, G)
         dh2 = torch.zeros(T, H, device=dout.device, dtype=torch.float32)
-        dh2.index_add_(0, rt.tok, dxs.index_select(0, rt.pos).float())
+        if plan is not None:
+            dx_send = dout.new_empty(T * k, H)
+            self._a2a(dx_send, dxs.index_select(0, rt.pos), plan["send"], plan["recv"])
+            dh2.index_add_(0, plan["tok"], dx_send.float())
+        else:
+            dh2.index_add_(0, rt.tok, dxs.index_select(0, rt.pos).float())
+        del dxs
         # router: top-k weights (optionally renormalised) and the aux loss
         if cfg.norm_topk_prob:
             wv = c["w"]
@@ -207,11 +281,18 @@ class MoEBlock:
         cfg = self.cfg
         T = h2.shape[0]
         k = cfg.num_experts_per_tok
-        if not h2.is_cuda:
+        if not h2.is_cuda and self.ep_size == 1:
             out, _, _ = moe_reference(h2, P["router_w"], P["exp_gu_w"], P["exp_down_w"], cfg)
             return x + out
         probs, topv, topi, s, w = self._route(h2, P)
-        rt = Routing(topi, cfg.num_experts)
-        _, _, _, y = self._experts(h2, P, rt)
-        contrib = y.index_select(0, rt.pos).float() * w.reshape(-1, 1)
+        if self.ep_size > 1:
+            plan, x_recv, el = self._dispatch(h2, topi)
+            rt = Routing(el.view(-1, 1), self.E_loc)
+            _, _, _, y = self._experts(x_recv, P, rt)
+            y_copy = self._combine(y.index_select(0, rt.pos), plan, T, k)
+        else:
+            rt = Routing(topi, cfg.num_experts)
+            _, _, _, y = self._experts(h2, P, rt)
+            y_copy = y.index_select(0, rt.pos)
+        contrib = y_copy.float() * w.reshape(-1, 1)
         return (x.float() + contrib.view(T, k, -1).sum(1)).to(x.dtype)

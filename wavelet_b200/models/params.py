@@ -114,7 +114,8 @@ class FlatParams:
         return slice(self.dp_rank * self.shard_numel, (self.dp_rank + 1) * self.shard_numel)
 
     # ------------------------------------------------------------- init
-    def init_(self, seed: int = 0, std_override: float | None = None, seed_index: dict | None = None) -> None:
+    def init_(self, seed: int = 0, std_override: float | None = None, seed_index: dict | None = None,
+              row_slices: dict | None = None) -> None:
         """Random init N(0, std) for matrices, ones for norms, zeros for biases.
 
         Every rank produces identical weights (same generator seed per tensor).
@@ -130,8 +131,17 @@ class FlatParams:
                 g.manual_seed(seed * 1_000_003 + (seed_index[s.name] if seed_index else i))
                 std = std_override if std_override is not None else s.std
                 # generate in fp32 then cast (bf16 normal_ draws differ by dtype)
-                tmp = torch.empty(v.shape, device=self.device, dtype=torch.float32)
-                tmp.normal_(0.0, std, generator=g)
+                if row_slices and s.name in row_slices:
+                    # a shard of a larger tensor (expert parallelism): draw the full
+                    # tensor with its own seed and keep our rows, so every layout
+                    # of the model holds identical weights
+                    full_shape, lo, hi = row_slices[s.name]
+                    tmp = torch.empty(full_shape, device=self.device, dtype=torch.float32)
+                    tmp.normal_(0.0, std, generator=g)
+                    tmp = tmp[lo:hi]
+                else:
+                    tmp = torch.empty(v.shape, device=self.device, dtype=torch.float32)
+                    tmp.normal_(0.0, std, generator=g)
                 v.copy_(tmp)
         self.sync_master_from_compute()
 

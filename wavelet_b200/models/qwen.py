@@ -56,6 +56,11 @@ def param_specs(cfg: ArchConfig) -> list[ParamSpec]:
 
 
 QUANTIZABLE = ("qkv_w", "o_w", "gu_w", "down_w")  # dense 2-D projections (NF4 for QLoRA)
+EXPERT_PARAMS = ("exp_gu_w", "exp_down_w")  # sharded by expert under expert parallelism
+
+
+def is_expert_param(name: str) -> bool:
+    return name.split(".", 1)[-1] in EXPERT_PARAMS
 
 
 @dataclass
@@ -71,9 +76,14 @@ class _Layer:
 class CausalLM:
     """A decoder-only LM whose parameters live in a ``FlatParams`` store."""
 
-    def __init__(self, cfg: ArchConfig, flat: FlatParams, quant: dict | None = None):
+    def __init__(self, cfg: ArchConfig, flat: FlatParams, quant: dict | None = None,
+                 expert_flat: FlatParams | None = None, ep: tuple[int, int] = (1, 0)):
         self.cfg = cfg
         self.flat = flat
+        # expert parallelism: this rank's experts [ep_rank*E/ep, (ep_rank+1)*E/ep) live in expert_flat
+        self.expert_flat = expert_flat
+        self.ep_size, self.ep_rank = ep
+        self.ep_dp_rank = 0
         self.quant = quant or {}  # name -> NF4Weight (frozen QLoRA base projections)
         self.lora = None
         self.device = flat.device
@@ -85,11 +95,16 @@ class CausalLM:
             P = {n[len(pre):]: flat.view(n) for n in names}
             P.update({n[len(pre):]: q for n, q in self.quant.items() if n.startswith(pre)})
             G = {n[len(pre):]: flat.grad_view(n) for n in names} if flat.grad is not None else {}
+            if expert_flat is not None:
+                en = [n for n in expert_flat.names() if n.startswith(pre)]
+                P.update({n[len(pre):]: expert_flat.view(n) for n in en})
+                if expert_flat.grad is not None:
+                    G.update({n[len(pre):]: expert_flat.grad_view(n) for n in en})
             layer = _Layer(cfg, P, G)
             if cfg.layer_is_moe(i):
                 from .moe import MoEBlock
 
-                layer.moe = MoEBlock(cfg, i)
+                layer.moe = MoEBlock(cfg, i, ep_size=self.ep_size, ep_rank=self.ep_rank)
             self.layers.append(layer)
         self.anchor = torch.empty(0, device=self.device, requires_grad=True)
         self.ep_group = None
@@ -135,6 +150,8 @@ class CausalLM:
     def hidden(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
         """Final normalised hidden states [T, H] (autograd-connected)."""
         if not input_ids.is_cuda:
+            if self.expert_flat is not None:
+                raise NotImplementedError("the CPU reference path runs without expert parallelism")
             return self._hidden_cpu(input_ids.reshape(-1), batch)
         ids = input_ids.reshape(-1).contiguous()
         x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"))
@@ -228,12 +245,14 @@ class CausalLM:
 
 def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
                 with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
-                lora_seed: int = 0) -> CausalLM:
+                lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None) -> CausalLM:
     """Build (and random-init) a model.
 
     ``lora``: an object with ``rank``, ``alpha``, ``target_modules``, ``dropout``
     (the ``lora`` config section) -> frozen base + trainable adapters.
     ``load_in_4bit``: NF4-quantise the dense projections after init (QLoRA).
+    ``ep``: (ep size, ep rank, expert-dp rank, expert-dp size) for expert
+    parallelism; the expert tensors of this rank go to ``model.expert_flat``.
     """
     device = torch.device(device)
     if dtype is None:
@@ -242,6 +261,24 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     qnames = {s.name for s in specs if load_in_4bit and s.name.split(".", 1)[-1] in QUANTIZABLE}
     frozen = lora is not None
     seed_index = {s.name: i for i, s in enumerate(specs)}
+    ep_size, ep_rank, ep_dp_rank, ep_dp_world = ep or (1, 0, 0, 1)
+    expert_flat = None
+    if ep_size > 1:
+        if cfg.num_experts % ep_size:
+            raise ValueError(f"num_experts {cfg.num_experts} is not divisible by ep {ep_size}")
+        if frozen:
+            raise NotImplementedError("LoRA with expert parallelism is not supported")
+        el = cfg.num_experts // ep_size
+        lo, hi = ep_rank * el, (ep_rank + 1) * el
+        espec, rows = [], {}
+        for s_ in specs:
+            if is_expert_param(s_.name):
+                espec.append(ParamSpec(s_.name, (el,) + tuple(s_.shape[1:]), s_.init, s_.weight_decay, s_.std))
+                rows[s_.name] = (tuple(s_.shape), lo, hi)
+        specs = [s_ for s_ in specs if not is_expert_param(s_.name)]
+        expert_flat = FlatParams(espec, device, dtype, ep_dp_rank, ep_dp_world, with_grad, with_optimizer)
+        if init:
+            expert_flat.init_(seed, seed_index=seed_index, row_slices=rows)
     flat = FlatParams([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,
                       with_grad and not frozen, with_optimizer and not frozen,
                       alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
@@ -261,7 +298,8 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                 tmp.normal_(0.0, s.std, generator=g)
             quant[s.name] = quantize(tmp.to(dtype))
             del tmp
-    model = CausalLM(cfg, flat, quant)
+    model = CausalLM(cfg, flat, quant, expert_flat, (ep_size, ep_rank))
+    model.ep_dp_rank = ep_dp_rank
     if frozen:
         from .lora import LoRAAdapters
 

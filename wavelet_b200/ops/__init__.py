@@ -93,6 +93,34 @@ def gemm(a: torch.Tensor, b, *, a_mn: bool = False, b_mn: bool = False,
     return out
 
 
+def gemm_grouped(a, a_mn, b, b_mn, c, mode, M, N, K, tile_group=None, b_group_stride=0, b_outer=0, k_start=None,
+                 k_len=None, groups=0, epi=EPI_BF16, alpha=1.0):
+    """Grouped (MoE expert) GEMM; see ``csrc/gemm.h``.  CPU: a per-group loop."""
+    if a.is_cuda:
+        ext().gemm_grouped(a, a_mn, b, b_mn, c, mode, M, N, K, tile_group, b_group_stride, b_outer, k_start, k_len,
+                           groups, epi, alpha)
+        return c
+    if mode == 1:  # rows of A in 128-row tiles, tile t uses weight block tile_group[t]
+        for t, g in enumerate(tile_group.tolist()):
+            r0, r1 = t * 128, min(M, (t + 1) * 128)
+            Bg = b[g * b_group_stride : g * b_group_stride + (K if b_mn else N)]
+            B = Bg if b_mn else Bg.t()
+            r = alpha * (a[r0:r1].float() @ B.float())
+            c[r0:r1] = r.to(c.dtype) if epi == EPI_BF16 else (c[r0:r1] + r if epi == EPI_F32_ACC else r)
+        return c
+    for g in range(groups):  # mode 2: C[g] (op)= A_g^T B_g over token rows
+        k0, kl = int(k_start[g]), int(k_len[g])
+        if kl == 0:
+            continue
+        r = alpha * (a[k0 : k0 + kl].float().t() @ b[k0 : k0 + kl].float())
+        blk = c[g * M : (g + 1) * M]
+        if epi == EPI_F32_ACC:
+            blk.add_(r)
+        else:
+            blk.copy_(r)
+    return c
+
+
 class LinearFn(torch.autograd.Function):
     """y = x W^T (+ b); the weight gradient is accumulated in fp32 directly
     into ``main_grad`` by the GEMM epilogue (no bf16 dW is materialised)."""
@@ -154,6 +182,16 @@ def rmsnorm_fwd(x, w, eps, res=None, want_h=False):
 
 
 def rmsnorm_bwd(x, w, rstd, dy, dres=None, dw=None):
+    if not x.is_cuda:
+        xf, wf, dyf = x.float(), w.float(), dy.float()
+        xh = xf * rstd[..., None]
+        g = dyf * wf
+        dx = rstd[..., None] * (g - xh * (g * xh).mean(-1, keepdim=True))
+        if dres is not None:
+            dx = dx + dres.float()
+        if dw is not None:
+            dw.add_((dyf * xh).reshape(-1, x.shape[-1]).sum(0).to(dw.dtype))
+        return dx.to(x.dtype)
     dx = torch.empty_like(x)
     ext().rmsnorm_bwd(x, w, rstd, dy.contiguous(), dres, dx, dw)
     return dx
@@ -195,6 +233,12 @@ def swiglu_fwd(gu):
 
 
 def swiglu_bwd(gu, dh):
+    if not gu.is_cuda:
+        I = gu.shape[-1] // 2
+        g, u = gu[..., :I].float(), gu[..., I:].float()
+        sg = torch.sigmoid(g)
+        d = dh.float()
+        return torch.cat([d * u * sg * (1 + g * (1 - sg)), d * g * sg], -1).to(gu.dtype)
     dgu = torch.empty_like(gu)
     ext().swiglu_bwd(gu.contiguous(), dh.contiguous(), dgu)
     return dgu

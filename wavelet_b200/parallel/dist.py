@@ -131,6 +131,9 @@ class Groups:
         self.tp = None
         self.cp = None
         self.ep = None
+        self.ep_dp = None  # ranks holding the same expert shard (dp_mod_ep)
+        self.ep_dp_rank = 0
+        self.ep_dp_size = dims.world_size // max(1, dims.ep)
         self.dp_rank = 0
         self.dp_size = dims.dp
         self.tp_rank = 0
@@ -161,6 +164,12 @@ class Groups:
                 if rank in ranks:
                     self.ep = g
                     self.ep_rank = ranks.index(rank)
+            for j in range(dims.ep):
+                ranks = list(range(j, W, dims.ep))
+                g = dist.new_group(ranks) if len(ranks) > 1 else None
+                if rank in ranks:
+                    self.ep_dp = g
+                    self.ep_dp_rank = ranks.index(rank)
 
 
 def all_ranks_true(flag: bool, device: torch.device, group=None) -> bool:

@@ -64,27 +64,25 @@ class ShardedAdamW:
             return self.g_shard
         return self.flat.grad
 
+    # Two phases so several stores (dense + expert shards) can share one clip:
+    # ``prepare`` reduces the gradients and returns this rank's (sumsq,
+    # non-finite) of its shard; ``apply`` runs the update with a clip factor.
     @torch.no_grad()
-    def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
-        flat = self.flat
-        lr = self.h.lr if lr is None else lr
-        g = self.reduce_grads()
+    def prepare(self) -> torch.Tensor:
+        self._g = self.reduce_grads()
         self.stats.zero_()
-        ops.sumsq_(g, self.stats)
-        if self.world > 1:
-            dist.all_reduce(self.stats, group=self.group)
-        norm_sq, bad = self.stats.tolist()
-        if check_finite and bad > 0:
-            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
-        norm = norm_sq**0.5
-        factor = 1.0
-        if self.h.max_grad_norm and self.h.max_grad_norm > 0:
-            factor = min(1.0, self.h.max_grad_norm / (norm + 1e-6))
+        ops.sumsq_(self._g, self.stats)
+        return self.stats
+
+    @torch.no_grad()
+    def apply(self, lr: float, factor: float) -> None:
+        flat = self.flat
         self.step_count += 1
         compute = flat.compute.detach()
         p16 = compute[flat.shard_slice]
         ops.adamw_flat_(
-            flat.master, g, flat.exp_avg, flat.exp_avg_sq, p16 if flat.compute.dtype == torch.bfloat16 else None,
+            flat.master, self._g, flat.exp_avg, flat.exp_avg_sq,
+            p16 if flat.compute.dtype == torch.bfloat16 else None,
             lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
             step=self.step_count, gscale_host=factor,
         )
@@ -94,6 +92,26 @@ class ShardedAdamW:
             src = p16 if compute.is_cuda else p16.clone()
             dist.all_gather_into_tensor(compute, src, group=self.group)
         flat.zero_grad()
+        self._g = None
+
+    def clip_factor(self, norm: float) -> float:
+        if self.h.max_grad_norm and self.h.max_grad_norm > 0:
+            return min(1.0, self.h.max_grad_norm / (norm + 1e-6))
+        return 1.0
+
+    @torch.no_grad()
+    def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
+        lr = self.h.lr if lr is None else lr
+        stats = self.prepare()
+        if self.world > 1:
+            dist.all_reduce(stats, group=self.group)
+        norm_sq, bad = stats.tolist()
+        if check_finite and bad > 0:
+            self.flat.zero_grad()
+            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
+        norm = norm_sq**0.5
+        factor = self.clip_factor(norm)
+        self.apply(lr, factor)
         return {"grad_norm": norm, "clip_factor": factor}
 
     # ---------------------------------------------------------------- state
@@ -177,3 +195,50 @@ class FusedShardedAdamW(ShardedAdamW):
         self.fabric.barrier()
         torch.cuda.synchronize(self.flat.device)
         self.fabric.check()
+
+
+class CompositeAdamW:
+    """One optimizer step over several flat stores with a single global clip.
+
+    Used with expert parallelism: the dense store is sharded over the whole
+    data-parallel group and the expert store over the ranks that hold the same
+    experts.  Every (store, rank) shard is disjoint, so the global squared
+    norm is one all-reduce over ``norm_group`` of the per-rank shard sums.
+    """
+
+    def __init__(self, parts: list[ShardedAdamW], norm_group=None, distributed: bool = False):
+        self.parts = parts
+        self.norm_group = norm_group
+        self.distributed = distributed
+        self.h = parts[0].h
+
+    @property
+    def step_count(self) -> int:
+        return self.parts[0].step_count
+
+    @torch.no_grad()
+    def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
+        lr = self.h.lr if lr is None else lr
+        total = None
+        for p in self.parts:
+            st = p.prepare()
+            total = st.clone() if total is None else total + st
+        if self.distributed:
+            dist.all_reduce(total, group=self.norm_group)
+        norm_sq, bad = total.tolist()
+        if check_finite and bad > 0:
+            for p in self.parts:
+                p.flat.zero_grad()
+            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
+        norm = norm_sq**0.5
+        factor = self.parts[0].clip_factor(norm)
+        for p in self.parts:
+            p.apply(lr, factor)
+        return {"grad_norm": norm, "clip_factor": factor}
+
+    def state_dict(self) -> dict:
+        return {f"part{i}": p.state_dict() for i, p in enumerate(self.parts)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        for i, p in enumerate(self.parts):
+            p.load_state_dict(sd[f"part{i}"])

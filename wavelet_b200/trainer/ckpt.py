@@ -79,6 +79,11 @@ class CheckpointManager:
         weights = None
         if self.rank == 0:
             weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
+        experts = None
+        ef = getattr(model, "expert_flat", None)
+        if ef is not None and getattr(model, "ep_dp_rank", 0) == 0:  # one copy per expert shard
+            experts = {n: self._host("e:" + n, ef.view(n)) for n in ef.names()}
+        ep_rank = getattr(model, "ep_rank", 0)
         opt = {k: (self._host("o:" + k, v) if torch.is_tensor(v) else v) for k, v in optimizer.state_dict().items()}
         if torch.cuda.is_available():
             torch.cuda.synchronize()
@@ -91,6 +96,8 @@ class CheckpointManager:
                     _save_safetensors(weights, d / "trainer" / "model.safetensors")
                     (d / "meta.json").write_text(json.dumps({"step": step, "world_size": self.world, **meta}, indent=2))
                     (d / "trainer" / "scheduler.json").write_text(json.dumps(scheduler_state or {}, indent=2))
+                if experts is not None:
+                    _save_safetensors(experts, d / "trainer" / f"experts-ep{ep_rank}.safetensors")
                 torch.save({**opt, "shard_rank": self.rank, "shard_world": self.world}, d / "trainer" / f"optim-rank{self.rank}.pt")
                 if data_state is not None:
                     (d / "dataloader" / f"rank{self.rank}.json").write_text(json.dumps(data_state))
@@ -138,6 +145,10 @@ class CheckpointManager:
         w = load_file(str(d / "trainer" / "model.safetensors"))
         flat = getattr(model, "trainable", model.flat)
         flat.load_state({k: v.to(flat.device) for k, v in w.items()})
+        ef = getattr(model, "expert_flat", None)
+        if ef is not None:
+            we = load_file(str(d / "trainer" / f"experts-ep{model.ep_rank}.safetensors"))
+            ef.load_state({k: v.to(ef.device) for k, v in we.items()})
         if optimizer is not None and not skip_optimizer:
             saved_world = int(meta.get("world_size", 1))
             if saved_world == self.world:

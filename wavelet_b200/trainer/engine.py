@@ -14,7 +14,7 @@ import torch.distributed as dist
 
 from ..models.qwen import CausalLM
 from ..ops import lm_head
-from ..parallel.zero import AdamWHyper, FusedShardedAdamW, ShardedAdamW
+from ..parallel.zero import AdamWHyper, CompositeAdamW, FusedShardedAdamW, ShardedAdamW
 
 
 @dataclass
@@ -52,11 +52,17 @@ class PackedBatch:
 
 class Engine:
     def __init__(self, model: CausalLM, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK, fabric=None):
+                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK, fabric=None, ep_dp_group=None, ep_dp_world: int = 1):
         self.model = model
         # the optimizer owns the trainable store: the full model, or only the
-        # LoRA adapters when the base is frozen
-        if fabric is not None:
+        # LoRA adapters when the base is frozen; with expert parallelism the
+        # expert store is a second part sharded over the expert-replica group
+        if model.expert_flat is not None:
+            self.opt = CompositeAdamW(
+                [ShardedAdamW(model.flat, hyper, dp_group, dp_world),
+                 ShardedAdamW(model.expert_flat, hyper, ep_dp_group, ep_dp_world)],
+                norm_group=None, distributed=dist.is_initialized() and dp_world > 1)
+        elif fabric is not None:
             self.opt = FusedShardedAdamW(model.trainable, hyper, fabric)
         else:
             self.opt = ShardedAdamW(model.trainable, hyper, dp_group, dp_world)

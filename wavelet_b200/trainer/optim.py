@@ -76,7 +76,8 @@ def newton_schulz5(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.
 class FlatOptimizer:
     """Common driver: reduce-scatter, norm/clip, per-type update, all-gather."""
 
-    def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1, fabric=None):
+    def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1, fabric=None,
+                 expert_flat: FlatParams | None = None, ep_dp_group=None, ep_dp_world: int = 1):
         self.flat = flat
         self.cfg = cfg
         self.type = cfg.type
@@ -87,7 +88,16 @@ class FlatOptimizer:
             weight_decay=0.0 if cfg.type in ("adam", "adam_8bit") else cfg.weight_decay,
             max_grad_norm=max_grad_norm,
         )
-        if fabric is not None and cfg.type in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
+        if expert_flat is not None:
+            # expert parallelism: dense + expert stores, one global clip
+            if cfg.type not in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
+                raise NotImplementedError("expert parallelism supports the AdamW family only")
+            from ..parallel.zero import CompositeAdamW
+
+            self.adamw = CompositeAdamW([ShardedAdamW(flat, hyper, dp_group, dp_world),
+                                         ShardedAdamW(expert_flat, hyper, ep_dp_group, ep_dp_world)],
+                                        distributed=dist.is_initialized() and dp_world > 1)
+        elif fabric is not None and cfg.type in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
             from ..parallel.zero import FusedShardedAdamW
 
             self.adamw = FusedShardedAdamW(flat, hyper, fabric)  # fused peer-memory RS + AdamW + AG
@@ -181,7 +191,7 @@ class FlatOptimizer:
             flat.master[rest] -= lr * (m[rest] / (1 - b1**t)) / den
 
     def state_dict(self) -> dict:
-        sd = self.adamw.state_dict()
+        sd = dict(self.adamw.state_dict())
         sd["type"] = self.type
         if self.momentum_buf is not None:
             sd["momentum"] = self.momentum_buf

@@ -60,7 +60,9 @@ class RLTrainer:
         dtype = torch.bfloat16 if w.device.type == "cuda" else torch.float32
         if model is None:
             model = build_model(arch, w.device, dtype, dp_rank=self.dp_rank, dp_world=self.dp_world, seed=c.seed,
-                                lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed)
+                                lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
+                                ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
+                                if dims.ep > 1 else None)
             p = Path(c.model.name)
             if not c.model.random_init and p.is_dir() and any(p.glob("*.safetensors")):
                 from ..models.hf_io import load_hf_weights
@@ -69,7 +71,9 @@ class RLTrainer:
         self.model = model
         if self.groups.ep is not None:
             model.ep_group = self.groups.ep
-        self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world)
+        self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world,
+                                       expert_flat=model.expert_flat, ep_dp_group=self.groups.ep_dp,
+                                       ep_dp_world=self.groups.ep_dp_size)
         self.loss_fn = setup_rl_loss_fn(c.loss)
         out = Path(c.output_dir)
         self.output_dir = out

@@ -73,19 +73,24 @@ class SFTTrainer:
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
         self.fabric = None
-        if dev.type == "cuda" and dims.dp == w.world_size and c.fsdp.backend != "gloo":
+        if dev.type == "cuda" and dims.dp == w.world_size and dims.ep == 1 and c.fsdp.backend != "gloo":
             from ..parallel.fabric import maybe_fabric
 
             self.fabric = maybe_fabric(dp_world, dp_rank, dev)
         self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed, fabric=self.fabric,
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
-                                 load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed)
+                                 load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
+                                 ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
+                                 if dims.ep > 1 else None)
+        if self.groups.ep is not None:
+            self.model.ep_group = self.groups.ep
         if not c.model.random_init and _has_weights(c.model.name):
             from ..models.hf_io import load_hf_weights
 
             load_hf_weights(self.model, Path(c.model.name))
         self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, self.groups.dp, dp_world,
-                                       fabric=self.fabric)
+                                       fabric=self.fabric, expert_flat=self.model.expert_flat,
+                                       ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size)
         self.engine = Engine(self.model, self.optimizer.adamw.h, self.groups.dp, dp_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
