@@ -522,7 +522,7 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, 
 
 void kv_append(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at::Tensor& v_cache,
                const at::Tensor& slot) {
-  // k, v: [T, Hk, 128] views; caches [num_blocks, block_size, Hk, 128]; slot int32 [T]
+  // k, v: [T, Hk, 128] views; caches [num_blocks, Hk, block_size, 128]; slot int32 [T]
   check_bf16(k, "k");
   check_bf16(v, "v");
   WB_CHECK(k.stride(2) == 1 && k.stride(1) == 128 && v.stride(2) == 1 && v.stride(1) == 128, "kv_append: bad k/v layout");
@@ -530,7 +530,7 @@ void kv_append(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at
   WB_CHECK(slot.scalar_type() == at::kInt && slot.is_contiguous(), "kv_append: slot must be int32");
   const c10::cuda::CUDAGuard guard(k.device());
   wb::kv_append(k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-                slot.data_ptr<int>(), k.size(0), k.size(1), k_cache.size(1), cur_stream());
+                slot.data_ptr<int>(), k.size(0), k.size(1), k_cache.size(2), cur_stream());
 }
 
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
@@ -554,8 +554,9 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   a.out_row = out.stride(0);
   a.nseq = q.size(0);
   a.Hq = q.size(1);
-  a.Hk = k_cache.size(2);
-  a.block_size = k_cache.size(1);
+  a.Hk = k_cache.size(1);  // [num_blocks, Hk, block_size, 128]
+  a.block_size = k_cache.size(2);
+  a.cache_rows = k_cache.size(0) * k_cache.size(2);
   a.splits = std::max<int64_t>(1, splits);
   a.scale = (float)scale;
   at::Tensor po, pml;
@@ -570,7 +571,7 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
 
 void sample_tokens(const at::Tensor& z, const at::Tensor& inv_tau, const c10::optional<at::Tensor>& thresh,
                    double min_p, int64_t seed, const c10::optional<at::Tensor>& row_ids, at::Tensor& out_tok,
-                   at::Tensor& out_lp) {
+                   at::Tensor& out_lp, const c10::optional<at::Tensor>& seed_dev) {
   check_bf16(z, "z");
   WB_CHECK(z.dim() == 2 && z.stride(1) == 1, "sample_tokens: z must be [B, V] row-major");
   check_f32(inv_tau, "inv_tau");
@@ -578,7 +579,22 @@ void sample_tokens(const at::Tensor& z, const at::Tensor& inv_tau, const c10::op
   wb::sample_tokens(z.data_ptr(), z.stride(0), z.size(0), z.size(1), inv_tau.data_ptr<float>(),
                     thresh ? thresh->data_ptr<float>() : nullptr, (float)min_p, (uint64_t)seed,
                     row_ids ? row_ids->data_ptr<int64_t>() : nullptr, out_tok.data_ptr<int64_t>(),
-                    out_lp.data_ptr<float>(), cur_stream());
+                    out_lp.data_ptr<float>(), cur_stream(), seed_dev ? seed_dev->data_ptr<int64_t>() : nullptr);
+}
+
+void decode_advance(const at::Tensor& tok, const at::Tensor& lp, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx,
+                    at::Tensor& slots, const at::Tensor& bt, int64_t block_size, at::Tensor& win_tok,
+                    at::Tensor& win_lp, at::Tensor& step, at::Tensor& seed) {
+  WB_CHECK(tok.scalar_type() == at::kLong && ids.scalar_type() == at::kLong && seed.scalar_type() == at::kLong,
+           "decode_advance: tok/ids/seed int64");
+  WB_CHECK(pos.scalar_type() == at::kInt && ctx.scalar_type() == at::kInt && slots.scalar_type() == at::kInt &&
+               bt.scalar_type() == at::kInt && step.scalar_type() == at::kInt, "decode_advance: int32 state");
+  WB_CHECK(bt.dim() == 2 && bt.size(0) >= tok.size(0) && win_tok.size(0) >= tok.size(0), "decode_advance: shapes");
+  const c10::cuda::CUDAGuard guard(tok.device());
+  wb::decode_advance(tok.data_ptr<int64_t>(), lp.data_ptr<float>(), ids.data_ptr<int64_t>(), pos.data_ptr<int32_t>(),
+                     ctx.data_ptr<int32_t>(), slots.data_ptr<int32_t>(), bt.data_ptr<int32_t>(), (int)bt.size(1),
+                     (int)block_size, win_tok.data_ptr<int64_t>(), win_lp.data_ptr<float>(), (int)win_tok.size(1),
+                     step.data_ptr<int32_t>(), seed.data_ptr<int64_t>(), (int)tok.size(0), cur_stream());
 }
 
 int64_t read_error(int64_t device) { return wb::read_error_word((int)device); }
@@ -611,7 +627,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd);
   m.def("kv_append", &kv_append);
   m.def("decode_attention", &decode_attention);
-  m.def("sample_tokens", &sample_tokens);
+  m.def("sample_tokens", &sample_tokens, py::arg("z"), py::arg("inv_tau"), py::arg("thresh"), py::arg("min_p"),
+        py::arg("seed"), py::arg("row_ids"), py::arg("out_tok"), py::arg("out_lp"), py::arg("seed_dev") = py::none());
+  m.def("decode_advance", &decode_advance);
   m.def("fabric_malloc", &fabric_malloc_);
   m.def("fabric_free", &fabric_free_);
   m.def("fabric_export", &fabric_export_);

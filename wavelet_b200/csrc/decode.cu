@@ -2,8 +2,10 @@
 // attention (GQA), and fused temperature sampling with the processed
 // log-prob of the sampled token.
 //
-// KV cache layout per layer: k_cache / v_cache [num_blocks, block_size, Hk, 128]
-// bf16; block_tables [num_seqs, max_blocks] int32; context_lens [num_seqs].
+// KV cache layout per layer: k_cache / v_cache [num_blocks, Hk, block_size, 128]
+// bf16 (head-major pages: the tokens of one head in one block are a
+// contiguous run); block_tables [num_seqs, max_blocks] int32; context_lens
+// [num_seqs].
 // These replace vLLM's paged attention / sampler used by the reference's
 // rollout engine (inference/engine.py:776-818).
 #include <cuda_bf16.h>
@@ -14,6 +16,7 @@
 
 #include "common.cuh"
 #include "decode.h"
+#include "tma.h"
 
 namespace wb {
 namespace {
@@ -32,7 +35,8 @@ __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k, int64_t k_
   const int t = w / Hk, h = w - t * Hk;
   const int s = slot[t];
   if (s < 0) return;
-  const int64_t dst = ((int64_t)s * Hk + h) * HD;  // slot = block * block_size + offset
+  const int blk = s / block_size, off = s - blk * block_size;  // slot = block * block_size + offset
+  const int64_t dst = (((int64_t)blk * Hk + h) * block_size + off) * HD;
   reinterpret_cast<uint2*>(k_cache + dst)[lane] = reinterpret_cast<const uint2*>(k + (int64_t)t * k_row + h * HD)[lane];
   reinterpret_cast<uint2*>(v_cache + dst)[lane] = reinterpret_cast<const uint2*>(v + (int64_t)t * v_row + h * HD)[lane];
 }
@@ -91,7 +95,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
     const int vec_per_row = HD / 8;
     for (int i = tid; i < ntok * vec_per_row; i += DEC_THREADS) {
       const int j = i / vec_per_row, c = i - j * vec_per_row;
-      const int64_t src = (((int64_t)blk * block_size + j) * Hk + g) * HD + c * 8;
+      const int64_t src = (((int64_t)blk * Hk + g) * block_size + j) * HD + c * 8;
       reinterpret_cast<uint4*>(sK)[j * vec_per_row + c] = *reinterpret_cast<const uint4*>(k_cache + src);
       reinterpret_cast<uint4*>(sV)[j * vec_per_row + c] = *reinterpret_cast<const uint4*>(v_cache + src);
     }
@@ -181,6 +185,252 @@ __global__ void __launch_bounds__(DEC_THREADS)
   }
 }
 
+// ------------------------------------------------------------ decode attention (TMA ring)
+// Memory-bound by design: every (sequence, kv head) reads its K/V history
+// once.  CTA per (sequence, kv head, split), 4 warps, a ring of 4 stages of 32
+// tokens (K and V, 16 KB) in shared memory filled by TMA (two 64-column
+// halves per tile, 128-byte swizzle, no multicast; pages are head-major so a
+// stage is one contiguous 8 KB run per tensor).  Warp w owns ring slot w: it
+// processes stages w, w+4, ... of the split with its own online-softmax state
+// and refills its slot as soon as it has read it, so while one warp computes,
+// the other slots' loads are in flight.  The four warp states merge at the
+// end; splits > 1 write partials for decode_combine.
+constexpr int D2_WARPS = 4;
+constexpr int D2_TOK = 32;
+constexpr int D2_HALF = D2_TOK * 64 * 2;  // 32 rows x 64 bf16 = 4 KB
+constexpr int D2_STAGE = 4 * D2_HALF;     // K lo, K hi, V lo, V hi
+constexpr int D2_MAXREP = 8;
+
+constexpr size_t d2_smem_bytes(int rep) {
+  return 1024 + (size_t)D2_WARPS * D2_STAGE + (size_t)rep * HD * 4 + D2_WARPS * 8 + 16;
+}
+
+// Both products run
+// on the tensor cores with mma.sync m16n8k16 (bf16 in, fp32 accumulate):
+//   S[16 x 32]  = Q[16 x 128] K^T   (rows = the rep q heads of this kv head,
+//                                    padded to 16; 4 n-tiles x 8 k-steps)
+//   O[16 x 128] += P[16 x 32] V     (16 n-tiles x 2 k-steps; P comes straight
+//                                    from the S accumulators as A fragments)
+// K fragments come from ldmatrix on the swizzled tile, V fragments from
+// ldmatrix.trans.  tcgen05 needs M >= 64 while a GQA decode step has only
+// rep (4..8) query rows per kv head, so the warp-level MMA is the right unit
+// here; it needs about a tenth of the issue slots of a CUDA-core dot-product
+// loop (measured: the scalar version was issue-bound at ~1.5 TB/s).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// byte offset of (row, 16-byte chunk c in 0..15) in a [32 x 128] bf16 tile
+// stored as two 128-byte-swizzled 64-column halves
+__device__ __forceinline__ uint32_t tile_off(int row, int c) {
+  return (uint32_t)((c >> 3) * D2_HALF + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(D2_WARPS * 32)
+    decode_attn3_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                        const __nv_bfloat16* __restrict__ q, int64_t q_row, const int* __restrict__ block_tables,
+                        int max_blocks, const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
+                        int64_t out_row, float* __restrict__ part_o, float* __restrict__ part_ml, int Hq, int Hk,
+                        int block_size, int splits, float scale_log2, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + D2_WARPS * D2_STAGE);
+  volatile int* abort = reinterpret_cast<volatile int*>(full + D2_WARPS);
+  const int rep = Hq / Hk;
+  const int seq = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int L = ctx_lens[seq];
+  const int n_st = (L + D2_TOK - 1) / D2_TOK;
+  const int per = (n_st + splits - 1) / splits;
+  const int s0 = sp * per, s1 = min(n_st, s0 + per);
+  const int* bt = block_tables + (int64_t)seq * max_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < D2_WARPS; ++i) mbar_init(&full[i], 1);
+    *abort = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+  }
+  __syncthreads();
+  uint8_t* slot = ring + warp * D2_STAGE;
+  auto issue = [&](int st) {
+    const int tok0 = st * D2_TOK;
+    const int row = (bt[tok0 / block_size] * Hk + g) * block_size + tok0 % block_size;
+    mbar_arrive_expect_tx(&full[warp], D2_STAGE);
+    tma_load_2d(&tmK, &full[warp], slot, 0, row);
+    tma_load_2d(&tmK, &full[warp], slot + D2_HALF, 64, row);
+    tma_load_2d(&tmV, &full[warp], slot + 2 * D2_HALF, 0, row);
+    tma_load_2d(&tmV, &full[warp], slot + 3 * D2_HALF, 64, row);
+  };
+  bool pending = s0 + warp < s1;
+  if (lane == 0 && pending) issue(s0 + warp);
+
+  // Q A-fragments for the 8 k-steps: rows gid (< rep) real, rows gid + 8 zero
+  uint32_t qa[8][2];
+  {
+    const bool real = gid < rep;
+    const __nv_bfloat16* qr = q + (int64_t)seq * q_row + (g * rep + (real ? gid : 0)) * HD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + tig * 2) : 0u;
+      qa[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + 8 + tig * 2) : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_row = -INFINITY, l_part = 0.f;
+  uint32_t phase = 0;
+  const uint32_t kbase = smem_u32(slot), vbase = kbase + 2 * D2_HALF;
+  const int mi = lane >> 3, r8 = lane & 7;
+  for (int st = s0 + warp; st < s1; st += D2_WARPS) {
+    if (!mbar_wait_warp(&full[warp], phase, abort, err, kErrTimeoutProducer)) break;
+    pending = false;
+    phase ^= 1;
+    // ---- S = Q K^T (4 n-tiles of 8 tokens)
+    float sacc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ks += 2) {
+        // matrices: (ks lo, ks hi, ks+1 lo, ks+1 hi) of tokens 8j..8j+7
+        const int tok = 8 * j + r8;
+        const int c = 2 * (ks + (mi >> 1)) + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + tile_off(tok, c), b0, b1, b2, b3);
+        const uint32_t a0[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        const uint32_t a1[4] = {qa[ks + 1][0], 0u, qa[ks + 1][1], 0u};
+        mma_bf16_16816(sacc[j], a0, b0, b1);
+        mma_bf16_16816(sacc[j], a1, b2, b3);
+      }
+    }
+    // ---- online softmax on rows gid (the 4 threads of a group share a row)
+    const int tbase = st * D2_TOK;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tbase + 8 * j + tig * 2 + e;
+        const float v = (t < L) ? sacc[j][e] * scale_log2 : -INFINITY;
+        sacc[j][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m_row, mx);
+    const float alpha = (m_row == -INFINITY) ? 0.f : exp2f(m_row - mn);
+    m_row = mn;
+    float ps = 0.f;
+    uint32_t pa[4][2];  // P as bf16 pairs per n-tile (rows gid)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float p0 = exp2f(sacc[j][0] - mn), p1 = exp2f(sacc[j][1] - mn);
+      ps += p0 + p1;
+      pa[j][0] = pack_bf16x2(p0, p1);
+    }
+    l_part = l_part * alpha + ps;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= alpha;
+      o[n][1] *= alpha;
+    }
+    // ---- O += P V (2 k-steps of 16 tokens, 16 n-tiles of 8 dims)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const uint32_t a[4] = {pa[2 * ks][0], 0u, pa[2 * ks + 1][0], 0u};
+#pragma unroll
+      for (int n = 0; n < 16; n += 2) {
+        // matrices: (n: tokens lo, tokens hi), (n+1: tokens lo, tokens hi)
+        const int tok = 16 * ks + 8 * (mi & 1) + r8;
+        const int c = n + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + tile_off(tok, c), b0, b1, b2, b3);
+        mma_bf16_16816(o[n], a, b0, b1);
+        mma_bf16_16816(o[n + 1], a, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (st + D2_WARPS < s1) {
+      if (lane == 0) {
+        fence_proxy_async_shared();  // generic reads of the slot before the async-proxy refill
+        issue(st + D2_WARPS);
+      }
+      pending = true;
+    }
+  }
+  if (pending && lane == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&full[warp], phase))
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) { atomicOr(err, kErrTimeoutDrain); break; }
+  }
+  float l_row = l_part + __shfl_xor_sync(0xffffffffu, l_part, 1);
+  l_row += __shfl_xor_sync(0xffffffffu, l_row, 2);
+  __syncthreads();
+  float* sm = reinterpret_cast<float*>(ring);  // [warps][8] m
+  float* sl = sm + D2_WARPS * 8;               // [warps][8] l
+  float* so = sl + D2_WARPS * 8;               // [warps][8][128]
+  if (gid < rep) {
+    if (tig == 0) {
+      sm[warp * 8 + gid] = m_row;
+      sl[warp * 8 + gid] = l_row;
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+      *reinterpret_cast<float2*>(so + (warp * 8 + gid) * HD + 8 * n + tig * 2) = make_float2(o[n][0], o[n][1]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rep * HD; i += blockDim.x) {
+    const int r = i / HD, d = i - r * HD;
+    float mm = -INFINITY;
+    for (int w = 0; w < D2_WARPS; ++w) mm = fmaxf(mm, sm[w * 8 + r]);
+    float ll = 0.f, acc = 0.f;
+    for (int w = 0; w < D2_WARPS; ++w) {
+      const float mw = sm[w * 8 + r];
+      if (mw == -INFINITY) continue;
+      const float a = exp2f(mw - mm);
+      ll += sl[w * 8 + r] * a;
+      acc += so[(w * 8 + r) * HD + d] * a;
+    }
+    const int h = g * rep + r;
+    if (splits == 1) {
+      out[(int64_t)seq * out_row + h * HD + d] = __float2bfloat16(ll > 0.f ? acc / ll : 0.f);
+    } else {
+      part_o[(((int64_t)seq * Hq + h) * splits + sp) * HD + d] = acc;
+      if (d == 0) {
+        part_ml[(((int64_t)seq * Hq + h) * splits + sp) * 2 + 0] = mm;
+        part_ml[(((int64_t)seq * Hq + h) * splits + sp) * 2 + 1] = ll;
+      }
+    }
+  }
+}
+
 // Merge split partials: one warp per (seq, q head), lane covers 4 dims.
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                       __nv_bfloat16* __restrict__ out, int64_t out_row, int nseq, int Hq,
@@ -231,8 +481,10 @@ __device__ __forceinline__ float uniform01(uint64_t seed, uint64_t row, uint64_t
 __global__ void sample_kernel(const __nv_bfloat16* __restrict__ z, int64_t ldz, int V,
                               const float* __restrict__ inv_tau, const float* __restrict__ thresh,
                               float min_p, uint64_t seed, const int64_t* __restrict__ row_ids,
-                              int64_t* __restrict__ out_tok, float* __restrict__ out_lp) {
+                              int64_t* __restrict__ out_tok, float* __restrict__ out_lp,
+                              const int64_t* __restrict__ seed_dev) {
   const int row = blockIdx.x;
+  if (seed_dev) seed = (uint64_t)*seed_dev;  // device-resident seed (CUDA-graph replays)
   const float it = inv_tau[row];
   const bool greedy = !(it > 0.f) || isinf(it);
   const float scale = greedy ? 1.f : it;
@@ -339,10 +591,31 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st) {
   if (a.block_size > PAGE_MAX) throw std::runtime_error("decode_attention: block_size must be <= 64");
   if (a.nseq <= 0) return;
   dim3 grid(a.nseq, a.Hk, a.splits);
+  const int rep = a.Hq / a.Hk;
+  if (rep <= D2_MAXREP && a.block_size % D2_TOK == 0 && a.cache_rows > 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr[64] = {false};
+    const size_t smem = d2_smem_bytes(D2_MAXREP);
+    if (!attr[dev & 63]) {
+      cudaFuncSetAttribute(decode_attn3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr[dev & 63] = true;
+    }
+    const uint64_t rows = (uint64_t)a.cache_rows * a.Hk;  // [num_blocks * Hk * block_size, 128]
+    CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, rows, HD, 64, D2_TOK,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, rows, HD, 64, D2_TOK,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    decode_attn3_kernel<<<grid, D2_WARPS * 32, smem, st>>>(
+        tk, tv, (const __nv_bfloat16*)a.q, a.q_row, a.block_tables, a.max_blocks, a.ctx_lens, (__nv_bfloat16*)a.out,
+        a.out_row, a.part_o, a.part_ml, a.Hq, a.Hk, a.block_size, a.splits, a.scale * 1.4426950408889634f,
+        error_word(dev));
+  } else {
   decode_attn_kernel<<<grid, DEC_THREADS, 0, st>>>(
       (const __nv_bfloat16*)a.q, a.q_row, (const __nv_bfloat16*)a.k_cache, (const __nv_bfloat16*)a.v_cache,
       a.block_tables, a.max_blocks, a.ctx_lens, (__nv_bfloat16*)a.out, a.out_row, a.part_o, a.part_ml, a.Hq, a.Hk,
       a.block_size, a.splits, a.scale * 1.4426950408889634f);
+  }
   if (a.splits > 1) {
     const int warps = 8;
     decode_combine_kernel<<<(a.nseq * a.Hq + warps - 1) / warps, warps * 32, 0, st>>>(
@@ -352,10 +625,51 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st) {
 
 void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv_tau, const float* thresh,
                    float min_p, uint64_t seed, const int64_t* row_ids, int64_t* out_tok, float* out_lp,
-                   cudaStream_t st) {
+                   cudaStream_t st, const int64_t* seed_dev) {
   if (rows <= 0) return;
   sample_kernel<<<rows, 1024, 0, st>>>((const __nv_bfloat16*)z, ldz, V, inv_tau, thresh, min_p, seed, row_ids, out_tok,
-                                       out_lp);
+                                       out_lp, seed_dev);
+}
+
+// One decode step's bookkeeping on the device (so a step needs no host work):
+// record the sampled token / log-prob in column step[0] of the window
+// buffers, make it the next input, advance position and context length, look
+// up the next KV slot in the block table, then bump the step index and the
+// sampling seed.  One CTA (rows <= 1024).
+__global__ void decode_advance_kernel(const int64_t* __restrict__ tok, const float* __restrict__ lp,
+                                      int64_t* __restrict__ ids, int32_t* __restrict__ pos, int32_t* __restrict__ ctx,
+                                      int32_t* __restrict__ slots, const int32_t* __restrict__ bt, int max_blocks,
+                                      int block_size, int64_t* __restrict__ win_tok, float* __restrict__ win_lp,
+                                      int win_ld, int32_t* __restrict__ step, int64_t* __restrict__ seed, int rows) {
+  const int s = *step;
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    const int64_t t = tok[i];
+    if (s < win_ld) {
+      win_tok[(int64_t)i * win_ld + s] = t;
+      win_lp[(int64_t)i * win_ld + s] = lp[i];
+    }
+    ids[i] = t;
+    const int p = pos[i] + 1;
+    pos[i] = p;
+    ctx[i] = p + 1;
+    const int b = min(p / block_size, max_blocks - 1);
+    slots[i] = bt[(int64_t)i * max_blocks + b] * block_size + p % block_size;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *step = s + 1;
+    *seed = *seed + 1;
+  }
+}
+
+void decode_advance(const int64_t* tok, const float* lp, int64_t* ids, int32_t* pos, int32_t* ctx, int32_t* slots,
+                    const int32_t* bt, int max_blocks, int block_size, int64_t* win_tok, float* win_lp, int win_ld,
+                    int32_t* step, int64_t* seed, int rows, cudaStream_t st) {
+  if (rows <= 0) return;
+  if (rows > 1024) throw std::runtime_error("decode_advance: at most 1024 rows");
+  decode_advance_kernel<<<1, 1024, 0, st>>>(tok, lp, ids, pos, ctx, slots, bt, max_blocks, block_size, win_tok, win_lp,
+                                            win_ld, step, seed, rows);
 }
 
 }  // namespace wb

@@ -18,6 +18,7 @@ struct DecodeArgs {
   float* part_o = nullptr;   // [nseq, Hq, splits, 128] when splits > 1
   float* part_ml = nullptr;  // [nseq, Hq, splits, 2]
   int nseq = 0, Hq = 0, Hk = 0, block_size = 0, splits = 1;
+  int64_t cache_rows = 0;  // num_blocks * block_size (TMA view of the cache)
   float scale = 0.f;
 };
 
@@ -26,6 +27,9 @@ void kv_append(const void* k, int64_t k_row, const void* v, int64_t v_row, void*
 void decode_attention(const DecodeArgs& a, cudaStream_t st);
 void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv_tau, const float* thresh,
                    float min_p, uint64_t seed, const int64_t* row_ids, int64_t* out_tok, float* out_lp,
-                   cudaStream_t st);
+                   cudaStream_t st, const int64_t* seed_dev = nullptr);
+void decode_advance(const int64_t* tok, const float* lp, int64_t* ids, int32_t* pos, int32_t* ctx, int32_t* slots,
+                    const int32_t* bt, int max_blocks, int block_size, int64_t* win_tok, float* win_lp, int win_ld,
+                    int32_t* step, int64_t* seed, int rows, cudaStream_t st);
 
 }  // namespace wb

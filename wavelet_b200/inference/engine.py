@@ -1,7 +1,7 @@
 """Native batched generator (replaces the reference's vLLM engine).
 
-* Paged KV cache: per layer ``k``/``v`` tensors [num_blocks, block_size, Hk,
-  128] bf16; a block manager hands out blocks, with reference counts so the
+* Paged KV cache: per layer ``k``/``v`` tensors [num_blocks, Hk, block_size,
+  128] bf16 (head-major pages); a block manager hands out blocks, with reference counts so the
   ``n`` samples of one prompt share the prompt's full blocks (the partial last
   block is copied per sample).
 * Continuous batching: sequences are admitted while blocks are free, prefilled
@@ -13,6 +13,14 @@
   GEMM, SwiGLU, down GEMM + residual) -> final norm -> LM head GEMM -> fused
   sampling (Gumbel-max at temperature, processed log-prob of the sampled
   token, optional top-k / min-p / top-p support).
+* Fast decode (dense models, untruncated sampling): the decode state
+  (last token, position, context length, KV slot, block table, sampling
+  seed) lives on the device; the host allocates KV blocks once per window of
+  up to 16 steps and replays one CUDA graph per step (captured per
+  batch-size bucket and split count).  A ``decode_advance`` kernel records
+  the sampled token and advances the state, so a window costs one host sync.
+  Stop tokens are found when the window's tokens come back; tokens sampled
+  after a stop are dropped.
 * Outputs match what the trainer needs: exact token ids, the processed
   log-probs at the sampling temperature, and the sampling support set when
   top-k / top-p / min-p truncate it (vLLM ``processed_logprobs`` and
@@ -29,9 +37,11 @@ import time
 from dataclasses import dataclass, field
 from typing import Any
 
+import numpy as np
 import torch
 
 from .. import ops
+from ..models.layers import _lin
 from ..models.qwen import CausalLM
 from ..ops import reference as ref
 from ..ops.attention import attention_fwd
@@ -111,7 +121,8 @@ class BlockManager:
 class Generator:
     def __init__(self, model: CausalLM, *, max_num_seqs: int = 512, max_model_len: int = 4096,
                  kv_cache_bytes: int | None = None, gpu_memory_utilization: float | None = None,
-                 block_size: int = 64, decode_splits: int | None = None):
+                 block_size: int = 64, decode_splits: int | None = None, cuda_graphs: bool = True,
+                 window: int = 16):
         self.m = model
         cfg = model.cfg
         self.cfg = cfg
@@ -128,15 +139,23 @@ class Generator:
             else:
                 kv_cache_bytes = 64 * per_block
         self.num_blocks = max(4, kv_cache_bytes // per_block)
-        shape = (self.num_blocks, block_size, cfg.num_kv_heads, cfg.head_dim)
+        # head-major pages: one head's tokens of a block are contiguous (decode
+        # attention streams 8 KB runs per head instead of 256-byte pieces)
+        shape = (self.num_blocks, cfg.num_kv_heads, block_size, cfg.head_dim)
         dt = model.flat.compute_dtype
         self.k_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
         self.v_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
         self.bm = BlockManager(self.num_blocks)
-        self.max_blocks_per_seq = (max_model_len + block_size - 1) // block_size
+        self.sink_block = self.bm.alloc()  # KV writes of padded graph rows land here
+        self.max_blocks_per_seq = (max_model_len + block_size - 1) // block_size + 1
         self.decode_splits = decode_splits
         self.stats: dict[str, float] = {}
         self._moe = [layer.moe for layer in model.layers]
+        self.window = window
+        self.use_graphs = (cuda_graphs and self.dev.type == "cuda" and not any(self._moe) and not model.quant)
+        self._bufs: dict[int, dict[str, torch.Tensor]] = {}
+        self._graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
+        self._graph_pool = None
 
     # ------------------------------------------------------------ utilities
     def release_cache(self) -> None:
@@ -176,8 +195,9 @@ class Generator:
         T = x.shape[0]
         for li, layer in enumerate(self.m.layers):
             P = layer.P
+            lora = layer.lora or {}
             h, _, _ = ops.rmsnorm_fwd(x, P["in_norm"], cfg.rms_eps)
-            qkv = ops.gemm(h, P["qkv_w"], bias=P.get("qkv_b"))
+            qkv, _ = _lin(h, P["qkv_w"], lora.get("qkv"), bias=P.get("qkv_b"))
             ops.qk_norm_rope_(qkv, nq, nk, pos, self.m.inv_freq, P.get("q_norm"), P.get("k_norm"), cfg.rms_eps)
             q = qkv[:, : nq * hd].view(T, nq, hd)
             k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
@@ -186,17 +206,18 @@ class Generator:
                 ops.ext().kv_append(k, v, self.k_cache[li], self.v_cache[li], slots)
             else:
                 sl = slots.long()
-                self.k_cache[li].view(-1, nk, hd)[sl] = k
-                self.v_cache[li].view(-1, nk, hd)[sl] = v
+                blk, off = sl // self.block_size, sl % self.block_size
+                self.k_cache[li][blk, :, off] = k
+                self.v_cache[li][blk, :, off] = v
             att = attn_fn(li, q, k, v)
-            x = ops.gemm(att.reshape(T, nq * hd), P["o_w"], res=x)
+            x, _ = _lin(att.reshape(T, nq * hd), P["o_w"], lora.get("o"), res=x)
             if layer.moe is not None:
                 h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
                 x = layer.moe.infer(h2, x, P)
             else:
                 h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
-                a = ops.swiglu_fwd(ops.gemm(h2, P["gu_w"]))
-                x = ops.gemm(a, P["down_w"], res=x)
+                a = ops.swiglu_fwd(_lin(h2, P["gu_w"], lora.get("gu"))[0])
+                x, _ = _lin(a, P["down_w"], lora.get("down"), res=x)
         hf, _, _ = ops.rmsnorm_fwd(x, self.m.weight("norm"), cfg.rms_eps)
         return hf
 
@@ -236,7 +257,7 @@ class Generator:
             bt[i, : len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
         bt = bt.to(self.dev)
         max_ctx = max(pos_l) + 1
-        splits = self.decode_splits or max(1, min(16, (max_ctx // self.block_size) // 4))
+        splits = self.decode_splits or self._splits(B, max_ctx)
         x = ops.embedding_fwd(self.m.weight("embed"), ids)
         scale = 1.0 / math.sqrt(self.cfg.head_dim)
 
@@ -258,8 +279,8 @@ class Generator:
             L = int(ctx[i])
             nb = (L + self.block_size - 1) // self.block_size
             blocks = bt[i, :nb].long()
-            kk = self.k_cache[li][blocks].reshape(-1, Hk, D)[:L].float()
-            vv = self.v_cache[li][blocks].reshape(-1, Hk, D)[:L].float()
+            kk = self.k_cache[li][blocks].transpose(1, 2).reshape(-1, Hk, D)[:L].float()
+            vv = self.v_cache[li][blocks].transpose(1, 2).reshape(-1, Hk, D)[:L].float()
             kk = kk.repeat_interleave(Hq // Hk, 1)
             vv = vv.repeat_interleave(Hq // Hk, 1)
             sc = torch.einsum("hd,lhd->hl", q[i].float(), kk) * scale
@@ -369,6 +390,10 @@ class Generator:
                 self._append(new, tok, lp, masks)
                 active += new
                 gen_tokens += len(new)
+            elif active and self._fast_ok(active):
+                n = self._decode_window(active, base_seed * 1000003 + step)
+                gen_tokens += n
+                step += self._last_window - 1
             elif active:
                 hf = self._decode(active)
                 for s in active:
@@ -391,6 +416,138 @@ class Generator:
                       "decode_steps": float(step)}
         finished.sort(key=lambda s: (s.pid, s.sidx))
         return [Completion(s.pid, s.sidx, s.prompt, s.out, s.lps, s.done or "length", s.masks) for s in finished]
+
+    def _splits(self, B: int, max_ctx: int) -> int:
+        """Split the context only when (sequences x kv heads) CTAs cannot fill
+        the GPU (~3 resident per SM); each split keeps >= 2 stages of 32 tokens.
+        Powers of two keep the number of captured graphs small."""
+        ctas = B * self.cfg.num_kv_heads
+        want = max(1, -(-3 * 148 // max(1, ctas)))
+        cap = max(1, max_ctx // 64)
+        sp = max(1, min(16, want, cap))
+        return 1 << (sp.bit_length() - 1)
+
+    # ------------------------------------------------------- fast decode
+    def _fast_ok(self, seqs: list[_Seq]) -> bool:
+        if self.dev.type != "cuda" or len(seqs) > 1024:
+            return False
+        return all(not s.params.truncated and not s.params.return_sampling_mask for s in seqs)
+
+    @staticmethod
+    def _bucket(B: int) -> int:
+        return max(32, (B + 31) // 32 * 32) if B <= 256 else (B + 127) // 128 * 128
+
+    def _buffers(self, Bb: int) -> dict[str, torch.Tensor]:
+        b = self._bufs.get(Bb)
+        if b is None:
+            d, W = self.dev, self.window
+            b = dict(ids=torch.zeros(Bb, dtype=torch.long, device=d), pos=torch.zeros(Bb, dtype=torch.int32, device=d),
+                     ctx=torch.ones(Bb, dtype=torch.int32, device=d), slots=torch.zeros(Bb, dtype=torch.int32, device=d),
+                     bt=torch.zeros(Bb, self.max_blocks_per_seq, dtype=torch.int32, device=d),
+                     inv_tau=torch.ones(Bb, dtype=torch.float32, device=d),
+                     row_ids=torch.zeros(Bb, dtype=torch.long, device=d),
+                     seed=torch.zeros(1, dtype=torch.long, device=d), step=torch.zeros(1, dtype=torch.int32, device=d),
+                     win_tok=torch.zeros(Bb, W, dtype=torch.long, device=d),
+                     win_lp=torch.zeros(Bb, W, dtype=torch.float32, device=d),
+                     tok=torch.zeros(Bb, dtype=torch.long, device=d), lp=torch.zeros(Bb, dtype=torch.float32, device=d))
+            self._bufs[Bb] = b
+        return b
+
+    def _step_on(self, b: dict[str, torch.Tensor], splits: int) -> None:
+        """One decode step entirely on device buffers (graph-capturable)."""
+        scale = 1.0 / math.sqrt(self.cfg.head_dim)
+        x = ops.embedding_fwd(self.m.weight("embed"), b["ids"])
+
+        def attn(li, q, k, v):
+            out = torch.empty(q.shape, device=self.dev, dtype=q.dtype)
+            ops.ext().decode_attention(q, self.k_cache[li], self.v_cache[li], b["bt"], b["ctx"], out, splits, scale)
+            return out
+
+        hf = self._layers_forward(x, b["pos"], b["slots"], attn)
+        z = self.m.logits(hf)
+        ext = ops.ext()
+        ext.sample_tokens(z, b["inv_tau"], None, 0.0, 0, b["row_ids"], b["tok"], b["lp"], b["seed"])
+        ext.decode_advance(b["tok"], b["lp"], b["ids"], b["pos"], b["ctx"], b["slots"], b["bt"], self.block_size,
+                           b["win_tok"], b["win_lp"], b["step"], b["seed"])
+
+    def _run_step(self, Bb: int, splits: int) -> None:
+        b = self._buffers(Bb)
+        if not self.use_graphs:
+            self._step_on(b, splits)
+            return
+        key = (Bb, splits)
+        g = self._graphs.get(key)
+        if g is None:
+            # capture on a snapshot of the state, then restore it: warm-up and
+            # capture both execute the step once
+            saved = {k: v.clone() for k, v in b.items()}
+            s = torch.cuda.Stream(self.dev)
+            s.wait_stream(torch.cuda.current_stream(self.dev))
+            with torch.cuda.stream(s):
+                self._step_on(b, splits)
+            torch.cuda.current_stream(self.dev).wait_stream(s)
+            for k, v in saved.items():
+                b[k].copy_(v)
+            g = torch.cuda.CUDAGraph()
+            if self._graph_pool is None:
+                self._graph_pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(g, pool=self._graph_pool):
+                self._step_on(b, splits)
+            for k, v in saved.items():
+                b[k].copy_(v)
+            self._graphs[key] = g
+        g.replay()
+
+    @torch.no_grad()
+    def _decode_window(self, seqs: list[_Seq], seed: int) -> int:
+        B = len(seqs)
+        n = min(self.window, max(1, min(s.params.max_tokens - len(s.out) for s in seqs)))
+        self._last_window = n
+        for s in seqs:
+            self._ensure_blocks(s, s.length + n + 1)
+        Bb = self._bucket(B)
+        b = self._buffers(Bb)
+        bs = self.block_size
+        bt = np.full((Bb, self.max_blocks_per_seq), self.sink_block, dtype=np.int32)
+        pos = np.zeros(Bb, dtype=np.int32)
+        ids = np.zeros(Bb, dtype=np.int64)
+        inv = np.ones(Bb, dtype=np.float32)
+        rid = np.zeros(Bb, dtype=np.int64)
+        for i, s in enumerate(seqs):
+            bt[i, : len(s.blocks)] = s.blocks
+            pos[i] = s.length
+            ids[i] = s.out[-1] if s.out else s.prompt[-1]
+            t = s.params.temperature
+            inv[i] = (1.0 / t) if t > 0 else 0.0
+            rid[i] = s.row_id
+        slots = bt[np.arange(Bb), np.minimum(pos // bs, self.max_blocks_per_seq - 1)] * bs + pos % bs
+        host = {"bt": bt, "pos": pos, "ctx": pos + 1, "slots": slots.astype(np.int32), "ids": ids, "inv_tau": inv,
+                "row_ids": rid}
+        for k, v in host.items():
+            b[k].copy_(torch.from_numpy(v), non_blocking=False)
+        b["step"].zero_()
+        b["seed"].fill_(seed)
+        max_ctx = int(pos[:B].max()) + n + 1
+        splits = self.decode_splits or self._splits(B, max_ctx)
+        for _ in range(n):
+            self._run_step(Bb, splits)
+        toks = b["win_tok"][:B, :n].cpu().tolist()
+        lps = b["win_lp"][:B, :n].cpu().tolist()
+        produced = 0
+        for i, s in enumerate(seqs):
+            for j in range(n):
+                s.out.append(int(toks[i][j]))
+                s.lps.append(float(lps[i][j]))
+                s.length += 1
+                produced += 1
+                k = len(s.out)
+                if k >= s.params.max_tokens:
+                    s.done = "length"
+                elif k >= s.params.min_tokens and s.out[-1] in s.params.stop_token_ids:
+                    s.done = "stop"
+                if s.done:
+                    break
+        return produced
 
     def _append(self, seqs: list[_Seq], tok: torch.Tensor, lp: torch.Tensor, masks) -> None:
         tl = tok.tolist()
