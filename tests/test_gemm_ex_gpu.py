@@ -75,3 +75,25 @@ def test_nf4_dequant_kernel_and_large_m_path(cuda_ext):
     _close(ops.gemm(x, q), x.float() @ ref.float().t())
     dy = torch.randn(1024, 384, device="cuda", dtype=torch.bfloat16)
     _close(ops.gemm(dy, q, b_mn=True), dy.float() @ ref.float())
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 2560, 9728), (64, 4096, 4096), (300, 1024, 3584)])
+def test_splitk_skinny_gemm(cuda_ext, M, N, K):
+    from wavelet_b200.ops import _splitk
+
+    torch.manual_seed(3)
+    bf = torch.bfloat16
+    x = torch.randn(M, K, device="cuda", dtype=bf)
+    w = (torch.randn(N, K, device="cuda") / 32).to(bf)
+    bias = torch.randn(N, device="cuda", dtype=bf)
+    res = torch.randn(M, N, device="cuda", dtype=bf)
+    out = torch.empty(M, N, device="cuda", dtype=bf)
+    assert _splitk(M, N, K, False, 0, out) > 1
+    y = ops.gemm(x, w, bias=bias, res=res, alpha=0.5)
+    _close(y, 0.5 * (x.float() @ w.float().t()) + bias.float() + res.float())
+    dy = torch.randn(M, N, device="cuda", dtype=bf)
+    w2 = (torch.randn(N, K, device="cuda") / 32).to(bf)
+    dx = ops.gemm(dy, w2, b_mn=True)  # dgrad form (N=K output), split when skinny
+    _close(dx, dy.float() @ w2.float())
+    torch.cuda.synchronize()
+    assert cuda_ext.read_error(0) == 0

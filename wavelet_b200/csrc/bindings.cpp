@@ -268,6 +268,18 @@ void allgather_bf16(const std::vector<int64_t>& dst, int64_t world, int64_t lo, 
   wb::allgather_bf16(peers_of(dst, (int)world), (int)world, lo, src.data_ptr(), src.numel(), cur_stream());
 }
 
+void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+                   const c10::optional<at::Tensor>& res, double alpha) {
+  check_f32(ws, "ws");
+  check_bf16(out, "out");
+  const int64_t M = out.size(0), N = out.size(1);
+  WB_CHECK(ws.is_contiguous() && ws.numel() == S * M * N, "splitk_reduce: workspace must be [S*M, N]");
+  const c10::cuda::CUDAGuard guard(out.device());
+  wb::splitk_reduce(ws.data_ptr<float>(), (int)S, M, (int)N, out.data_ptr(), ld_of(out, "out"),
+                    bias ? bias->data_ptr() : nullptr, res ? res->data_ptr() : nullptr, res ? ld_of(*res, "res") : 0,
+                    (float)alpha, cur_stream());
+}
+
 void nf4_dequant(const at::Tensor& codes, const at::Tensor& absmax, at::Tensor& out, const std::vector<double>& lut) {
   WB_CHECK(codes.scalar_type() == at::kByte && codes.is_cuda() && codes.is_contiguous(), "nf4_dequant: codes");
   check_f32(absmax, "absmax");
@@ -610,6 +622,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_ex", &gemm_ex);
   m.def("nf4_dequant", &nf4_dequant);
+  m.def("splitk_reduce", &splitk_reduce);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

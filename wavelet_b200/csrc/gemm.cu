@@ -588,12 +588,18 @@ void gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
     return launch<false, false, kEpiBF16, 1>(g, stream);
   }
   if (g.group_mode == 2) {
-    // expert wgrad: K = token segments; A and B MN-major; C = [groups * M, N]
+    // K-grouped: C[g] = A_g^T B_g over K ranges [k_start[g], +k_len[g]); C = [groups * M, N] fp32.
+    // MN-major A and B: expert wgrad over token segments.  K-major A (B either way):
+    // split-K partials of a skinny forward / dgrad GEMM (reduced by splitk_reduce).
     if (!g.k_start || !g.k_len || g.groups <= 0) throw std::runtime_error("wavelet_b200 grouped gemm: k_start/k_len required");
-    if (!g.a_mn || !g.b_mn) throw std::runtime_error("wavelet_b200 grouped gemm: K-grouped mode needs MN-major A and B");
-    if (g.epi == kEpiF32Acc) return launch<true, true, kEpiF32Acc, 2>(g, stream);
-    if (g.epi == kEpiF32) return launch<true, true, kEpiF32, 2>(g, stream);
-    throw std::runtime_error("wavelet_b200 grouped gemm: K-grouped mode writes fp32");
+    if (g.a_mn && g.b_mn) {
+      if (g.epi == kEpiF32Acc) return launch<true, true, kEpiF32Acc, 2>(g, stream);
+      if (g.epi == kEpiF32) return launch<true, true, kEpiF32, 2>(g, stream);
+    } else if (!g.a_mn && g.epi == kEpiF32) {
+      if (g.b_mn) return launch<false, true, kEpiF32, 2>(g, stream);
+      return launch<false, false, kEpiF32, 2>(g, stream);
+    }
+    throw std::runtime_error("wavelet_b200 grouped gemm: unsupported K-grouped layout / epilogue");
   }
   if (g.K <= 0) throw std::runtime_error("wavelet_b200 gemm: K must be positive");
   if (g.K2 > 0 && (!g.A2 || !g.B2)) throw std::runtime_error("wavelet_b200 gemm: K2 > 0 needs A2 and B2");

@@ -644,6 +644,42 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint4* __restric
   }
 }
 
+// Split-K reduction: out[m, n] = bf16(alpha * sum_s ws[s, m, n] + bias[n] + res[m, n]).
+// 4 columns per thread (N % 4 == 0).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int S, int64_t M, int N,
+                                                            __nv_bfloat16* __restrict__ out, int64_t ldc,
+                                                            const __nv_bfloat16* __restrict__ bias,
+                                                            const __nv_bfloat16* __restrict__ res, int64_t ldr,
+                                                            float alpha) {
+  const int64_t n4 = N / 4;
+  const int64_t total = M * n4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n4;
+    const int c = (int)(i - m * n4) * 4;
+    float4 acc = reinterpret_cast<const float4*>(ws + m * N + c)[0];
+    for (int s = 1; s < S; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(ws + ((int64_t)s * M + m) * N + c)[0];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    float r[4] = {acc.x * alpha, acc.y * alpha, acc.z * alpha, acc.w * alpha};
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] += __bfloat162float(bias[c + j]);
+    }
+    if (res) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] += __bfloat162float(res[m * ldr + c + j]);
+    }
+    uint2 o;
+    o.x = pack_bf16(r[0], r[1]);
+    o.y = pack_bf16(r[2], r[3]);
+    *reinterpret_cast<uint2*>(out + m * ldc + c) = o;
+  }
+}
+
 inline int grid_for(int64_t work, int threads, int cap = 148 * 16) {
   int64_t g = (work + threads - 1) / threads;
   if (g > cap) g = cap;
@@ -717,6 +753,14 @@ void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T,
                    cudaStream_t st) {
   embedding_bwd_kernel<<<grid_for(T * (H / 4), 256), 256, 0, st>>>((const __nv_bfloat16*)dy, ids,
                                                                   dtable, T, H, V);
+}
+
+void splitk_reduce(const float* ws, int S, int64_t M, int N, void* out, int64_t ldc, const void* bias, const void* res,
+                   int64_t ldr, float alpha, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return;
+  if (N % 4 || ldc % 4 || (res && ldr % 4)) throw std::runtime_error("splitk_reduce: N and strides must be multiples of 4");
+  splitk_reduce_kernel<<<grid_for(M * (N / 4), 256, 148 * 8), 256, 0, st>>>(
+      ws, S, M, N, (__nv_bfloat16*)out, ldc, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)res, ldr, alpha);
 }
 
 void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,

@@ -22,6 +22,8 @@ void embedding_fwd(const void* table, const int64_t* ids, void* out, int64_t T, 
                    cudaStream_t st);
 void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T, int H, int64_t V,
                    cudaStream_t st);
+void splitk_reduce(const float* ws, int S, int64_t M, int N, void* out, int64_t ldc, const void* bias, const void* res,
+                   int64_t ldr, float alpha, cudaStream_t st);
 void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,
                  cudaStream_t st);
 void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,

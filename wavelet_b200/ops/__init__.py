@@ -76,6 +76,9 @@ def gemm(a: torch.Tensor, b, *, a_mn: bool = False, b_mn: bool = False,
             out.copy_(r)
         return out
     if not quant and a2 is None:
+        S = _splitk(M, N, a.shape[0] if a_mn else a.shape[1], a_mn, epi, out)
+        if S > 1:
+            return _gemm_splitk(a, b, b_mn, out, S, alpha, bias, res)
         ext().gemm(a, a_mn, b, b_mn, out, epi, alpha, bias, res)
         return out
     if quant and M > FUSED_MAX_M:
@@ -119,6 +122,42 @@ def gemm_grouped(a, a_mn, b, b_mn, c, mode, M, N, K, tile_group=None, b_group_st
         else:
             blk.copy_(r)
     return c
+
+
+_SMS = 148
+_KRANGES: dict = {}
+
+
+def _splitk(M: int, N: int, K: int, a_mn: bool, epi: int, out) -> int:
+    """Split K when a bf16-output GEMM has too few 128x256 tiles to fill the
+    SMs (skinny generation GEMMs); every split keeps >= 8 k-blocks."""
+    if a_mn or epi != EPI_BF16 or M > 2048 or N % 4 or (out.stride(0) % 4):
+        return 1
+    tiles = -(-M // 128) * -(-N // 256)
+    if tiles * 2 > _SMS:
+        return 1
+    s = min(8, _SMS // tiles, K // 512)  # tiles * s <= one wave of CTAs
+    return s if s > 1 else 1
+
+
+def _gemm_splitk(a, b, b_mn, out, S, alpha, bias, res):
+    M, K = a.shape
+    N = out.shape[1]
+    kb = -(-K // 64)
+    per = -(-kb // S)
+    S = -(-kb // per)  # every range non-empty (an empty one would leave its partial unwritten)
+    key = (a.device, K, S)
+    kr = _KRANGES.get(key)
+    if kr is None:
+        starts = [min(K, i * per * 64) for i in range(S)]
+        lens = [max(0, min(K, (i + 1) * per * 64) - starts[i]) for i in range(S)]
+        kr = (torch.tensor(starts, dtype=torch.int32, device=a.device),
+              torch.tensor(lens, dtype=torch.int32, device=a.device))
+        _KRANGES[key] = kr
+    ws = torch.empty(S * M, N, device=a.device, dtype=torch.float32)
+    ext().gemm_grouped(a, False, b, b_mn, ws, 2, M, N, K, None, 0, 0, kr[0], kr[1], S, EPI_F32, 1.0)
+    ext().splitk_reduce(ws, S, out, bias, res, alpha)
+    return out
 
 
 class LinearFn(torch.autograd.Function):
