@@ -47,8 +47,9 @@ def parse():
                    help="micro-batches of 1 sequence per GPU per step (default 8 for sft; 32/N for qlora)")
     p.add_argument("--layers", type=int, default=None, help="(debug only) override layer count; invalidates the number")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", default="sft", choices=["sft", "qlora"],
-                   help="sft: dense full fine-tune (headline); qlora: NF4 base + LoRA r16 on all projections")
+    p.add_argument("--workload", default="sft", choices=["sft", "qlora", "grpo-4b"],
+                   help="sft: dense full fine-tune (headline); qlora: NF4 base + LoRA r16 on all projections; "
+                        "grpo-4b: Qwen3-4B-shape GRPO step (native generator + trainer, integrated)")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
                    help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
     return p.parse_args()
@@ -120,10 +121,99 @@ class ClockSampler:
         return {"sm_mhz": med, "sm_max_mhz": max(maxes) if maxes else None, "reasons": sorted(reasons), "samples": len(sms)}
 
 
+def rl_main(args):
+    """GRPO step on the Qwen3-4B shape through the integrated RL runner
+    (``wavelet rl`` with launcher.mode=integrated): every rank generates
+    64/N prompts x 8 samples (256-token prompts, 1024 new tokens), scores and
+    publishes them, then trains on the packed batch.  Reports rollout tokens/s
+    (generated tokens over device-timed generation, summed over ranks) and
+    the device-timed step time (max over ranks)."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.ops import _ext
+    from wavelet_b200.orchestrator.runtime import IntegratedRunner
+    from wavelet_b200.parallel.dist import destroy_distributed
+    from wavelet_b200.utils.config import load_yaml
+
+    root = os.path.dirname(os.path.abspath(__file__))
+    d = load_yaml(os.path.join(root, "examples", "grpo_4b", "rl.yaml"))
+    N = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    d["orchestrator"]["examples_per_step"] = max(1, 64 // N)
+    d["output_dir"] = os.path.join(tempfile.gettempdir(), f"wavelet_b200_bench_rl_{os.environ.get('MASTER_PORT', 'x')}")
+    d["clean_output_dir"] = True
+    d["max_steps"] = args.warmup + args.steps
+    cfg = RLConfig.model_validate(d)
+    runner = IntegratedRunner(cfg).setup()
+    _ext.load()
+    dev = runner.world.device
+    for _ in range(args.warmup):
+        runner.run_step()
+    sampler = ClockSampler(dev.index if dev.index is not None else 0) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    if N > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    gen_ms = step_ms = 0.0
+    gen_tok = 0.0
+    train_tok = 0.0
+    with _ext.count_launches() as counter:
+        for _ in range(args.steps):
+            m = runner.run_step()
+            gen_ms += m["time/generate_ms_device"]
+            step_ms += m["time/step_ms_device"]
+            gen_tok += m.get("rollout/generated_tokens", 0.0)
+            train_tok += m.get("train/tokens", 0.0)
+    torch.cuda.synchronize()
+    if N > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    t = torch.tensor([gen_ms, step_ms, gen_tok, train_tok], device=dev, dtype=torch.float64)
+    if N > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm)
+        gen_ms, step_ms, gen_tok, train_tok = mx[0].item(), mx[1].item(), sm[2].item(), sm[3].item()
+    else:
+        gen_ms, step_ms, gen_tok, train_tok = t.tolist()
+    K = args.steps
+    value = gen_tok / (gen_ms / 1000.0)
+    if rank == 0:
+        rec = {
+            "metric": "RL rollout tok/s (Qwen3-4B-shape GRPO, native generator)",
+            "value": value, "unit": "tokens/s", "n_gpus": N, "steps": K, "warmup": args.warmup,
+            "ms_per_step": step_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (uniform random 256-token prompts, reversed-prompt reward, random-init weights)",
+            "config": {"model": "Qwen3-4B-shape", "prompts_per_step": 64, "samples_per_prompt": 8,
+                       "prompt_len": 256, "max_new_tokens": 1024, "temperature": 1.0,
+                       "parallelism": f"integrated dp{N} (each rank generates and trains)",
+                       "l2": "inputs larger than L2 (8 GB of weights, tens of GB of KV per step)"},
+            "rl_step_ms": step_ms / K, "generate_ms_per_step": gen_ms / K,
+            "train_tokens_per_step": train_tok / K, "generated_tokens_per_step": gen_tok / K,
+            "gpu_launches": counter.count, "clocks": clocks,
+            "e2e": {"value": value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(train_tok / K * 32), "d2h_bytes_per_step": int(gen_tok / K * 12),
+                    "note": "the RL step is end to end by construction: rollouts return to the host (token ids and "
+                            "log-probs), pass through the filesystem queue and are copied back for training"},
+        }
+        print(json.dumps(rec), flush=True)
+    destroy_distributed()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "grpo-4b":
+        return rl_main(args)
 
     import torch
     import torch.distributed as dist

@@ -68,7 +68,8 @@ def test_scheduler_publishes_with_policy_lag(tmp_path, cpu_env, monkeypatch):
     from wavelet_b200.orchestrator.scheduler import RolloutScheduler
     from wavelet_b200.transport.queue import STABLE, read_training_records, stable_steps, step_dir
 
-    cfg = _cfg(tmp_path, orchestrator={"examples_per_step": 2, "rollouts_per_example": 2, "max_async_level": 1})
+    cfg = _cfg(tmp_path, orchestrator={"examples_per_step": 2, "rollouts_per_example": 2, "max_async_level": 1,
+                                       "filter_zero_advantage": False})
     out = tmp_path / "out"
     # a policy snapshot for step 0 (device-kind marker is enough for the in-process engine)
     pd = step_dir(out / "policies", 0)

@@ -349,13 +349,18 @@ class Generator:
         gen_tokens = 0
         step = 0
         row_counter = 0
+        n_windows = n_eager = n_prefill = 0
+        captures0 = len(self._graphs)
         while pending or active:
             # admit whole prompt groups while capacity allows
             admit: list[_Seq] = []
             while pending and len(active) + len(admit) + params.n <= self.max_num_seqs:
                 pid, pr = pending[0]
-                need = (len(pr) + params.max_tokens + self.block_size - 1) // self.block_size
-                if need * params.n > self.bm.num_free and (active or admit):
+                # the group shares the prompt's full blocks; each sample owns the rest
+                shared = len(pr) // self.block_size
+                total = (len(pr) + params.max_tokens + self.block_size - 1) // self.block_size
+                need = shared + params.n * (total - shared)
+                if need > self.bm.num_free and (active or admit):
                     break
                 pending.pop(0)
                 if len(pr) + params.max_tokens > self.max_model_len:
@@ -365,6 +370,7 @@ class Generator:
                 self._ensure_blocks(first, len(pr))
                 admit.append(first)
             if admit:
+                n_prefill += 1
                 hf = self._prefill(admit)
                 for s in admit:
                     s.length = len(s.prompt)
@@ -394,7 +400,9 @@ class Generator:
                 n = self._decode_window(active, base_seed * 1000003 + step)
                 gen_tokens += n
                 step += self._last_window - 1
+                n_windows += 1
             elif active:
+                n_eager += 1
                 hf = self._decode(active)
                 for s in active:
                     s.length += 1
@@ -413,7 +421,8 @@ class Generator:
             active = still
         dt = time.perf_counter() - t0
         self.stats = {"generated_tokens": float(gen_tokens), "seconds": dt, "tokens_per_second": gen_tokens / max(dt, 1e-9),
-                      "decode_steps": float(step)}
+                      "decode_steps": float(step), "decode_windows": float(n_windows), "eager_steps": float(n_eager),
+                      "prefills": float(n_prefill), "graph_captures": float(len(self._graphs) - captures0)}
         finished.sort(key=lambda s: (s.pid, s.sidx))
         return [Completion(s.pid, s.sidx, s.prompt, s.out, s.lps, s.done or "length", s.masks) for s in finished]
 
@@ -431,7 +440,8 @@ class Generator:
     def _fast_ok(self, seqs: list[_Seq]) -> bool:
         if self.dev.type != "cuda" or len(seqs) > 1024:
             return False
-        return all(not s.params.truncated and not s.params.return_sampling_mask for s in seqs)
+        # untruncated sampling has the whole vocabulary as its support: no mask to record
+        return all(not s.params.truncated for s in seqs)
 
     @staticmethod
     def _bucket(B: int) -> int:
@@ -503,8 +513,8 @@ class Generator:
         B = len(seqs)
         n = min(self.window, max(1, min(s.params.max_tokens - len(s.out) for s in seqs)))
         self._last_window = n
-        for s in seqs:
-            self._ensure_blocks(s, s.length + n + 1)
+        for s in seqs:  # KV slots for positions length .. length + n - 1
+            self._ensure_blocks(s, s.length + n)
         Bb = self._bucket(B)
         b = self._buffers(Bb)
         bs = self.block_size

@@ -87,6 +87,49 @@ class IntegratedRunner:
         dist.all_gather_object(allr, rows)
         return [r for part in allr for r in part]
 
+    def run_step(self) -> dict[str, Any]:
+        """One RL step: generate + score this rank's prompts, publish the batch
+        (rank 0), train on it, return the step metrics."""
+        c = self.cfg
+        t = self.trainer
+        step = t.step
+        cuda = self.world.device.type == "cuda"
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if cuda else None
+        if ev:
+            ev[0].record()
+        t0 = time.perf_counter()
+        recs = self.orch.materialize(step)
+        gen_s = time.perf_counter() - t0
+        if ev:
+            ev[1].record()
+        rows = self._gather([example_to_payload(r) for r in recs])
+        if self.sender is not None:
+            self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=step,
+                                tokens=sum(len(r.get("input_ids") or []) for r in rows))
+        if dist.is_initialized():
+            dist.barrier()
+        batch = t.receiver.wait()
+        if self.world.rank == 0:
+            t.receiver.claim(batch, step)
+        from ..transport.queue import read_training_records
+
+        records = [example_from_payload(r) for r in read_training_records(batch.training_path)]
+        t1 = time.perf_counter()
+        m = t.train_on_examples(records)
+        train_s = time.perf_counter() - t1
+        if self.world.rank == 0:
+            t.receiver.consumed(batch, step, t.step)
+        m.update(self.orch.last_stats)
+        m["time/generate_seconds"] = gen_s
+        m["time/train_seconds"] = train_s
+        m["time/step_seconds"] = time.perf_counter() - t0
+        if ev:
+            ev[2].record()
+            ev[2].synchronize()
+            m["time/generate_ms_device"] = ev[0].elapsed_time(ev[1])
+            m["time/step_ms_device"] = ev[0].elapsed_time(ev[2])
+        return m
+
     def run(self) -> int:
         c = self.cfg
         t = self.trainer
@@ -94,36 +137,10 @@ class IntegratedRunner:
         status = "failed"
         try:
             while t.step < total:
-                step = t.step
-                t0 = time.perf_counter()
-                recs = self.orch.materialize(step)
-                gen_s = time.perf_counter() - t0
-                rows = self._gather([example_to_payload(r) for r in recs])
-                if self.sender is not None:
-                    self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=step,
-                                        tokens=sum(len(r.get("input_ids") or []) for r in rows))
-                if dist.is_initialized():
-                    dist.barrier()
-                batch = t.receiver.wait()
-                if self.world.rank == 0:
-                    t.receiver.claim(batch, step)
-                from ..transport.queue import read_training_records
-
-                records = [example_from_payload(r) for r in read_training_records(batch.training_path)]
-                t1 = time.perf_counter()
-                m = t.train_on_examples(records)
-                train_s = time.perf_counter() - t1
-                if self.world.rank == 0:
-                    t.receiver.consumed(batch, step, t.step)
-                m.update(self.orch.last_stats)
-                m["time/generate_seconds"] = gen_s
-                m["time/train_seconds"] = train_s
-                m["time/step_seconds"] = time.perf_counter() - t0
+                m = self.run_step()
                 t.monitor.log(m, t.step)
                 log.info("rl step %d reward %.4f loss %.4f gen %.2fs train %.2fs", t.step, m.get("reward/mean", 0.0),
-                         m["loss"], gen_s, train_s)
-                if c.policy_transfer.type == "filesystem" and t.step % c.policy_transfer.export_every_steps == 0 and c.policy_transfer.export_initial:
-                    pass  # the in-process generator already sees the new weights
+                         m["loss"], m["time/generate_seconds"], m["time/train_seconds"])
                 if t.ckpt is not None and c.ckpt.interval and t.step % c.ckpt.interval == 0:
                     t.ckpt.save(t.step, model=t.model, optimizer=t.optimizer, data_state=None,
                                 meta={"arch": t.model.cfg.to_dict()}, scheduler_state={"step": t.step})

@@ -158,7 +158,8 @@ class RLTrainer:
         if self.dp_world > 1:
             dist.all_reduce(lt, group=self.groups.dp)
         metrics.update({"loss": float(lt), "optim/grad_norm": st["grad_norm"], "optim/lr": lr,
-                        "train/rl_units": scales["rl"], "train/num_samples": float(len(examples))})
+                        "train/rl_units": scales["rl"], "train/num_samples": float(len(examples)),
+                        "train/tokens": float(tokens)})
         metrics.update(self.perf.step_metrics(tokens * self.dp_world, time.perf_counter() - t0, c.data.seq_len))
         return metrics
 
