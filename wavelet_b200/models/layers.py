@@ -141,6 +141,41 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
     return dx
 
 
+class ActivationOffload:
+    """Keeps every decoder layer's saved input in pinned host memory between
+    forward and backward (``model.smart_gc``; reference kernels/smart_gc.py
+    offloads checkpoint inputs over 2 MB to pinned CPU).  The device-to-host
+    copy runs on a side stream ordered after the producing kernels; the
+    backward copies the input back before recomputing the layer.  Only the
+    per-layer inputs are kept (the layer itself is recomputed), so device
+    activation memory no longer grows with depth."""
+
+    def __init__(self, min_bytes: int = 2 << 20):
+        self.min_bytes = min_bytes
+        self.stream = None
+
+    def save(self, x: torch.Tensor):
+        if not x.is_cuda or x.numel() * x.element_size() < self.min_bytes:
+            return x, None
+        if self.stream is None:
+            self.stream = torch.cuda.Stream(x.device)
+        host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        self.stream.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(self.stream):
+            host.copy_(x, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        x.record_stream(self.stream)  # keep x alive until the copy has read it
+        return host, ev
+
+    @staticmethod
+    def restore(saved, ev, device) -> torch.Tensor:
+        if ev is None:
+            return saved
+        ev.synchronize()
+        return saved.to(device, non_blocking=True)
+
+
 class DecoderLayerFn(torch.autograd.Function):
     """Activation-checkpointed decoder layer: saves x, recomputes in backward."""
 
@@ -148,13 +183,24 @@ class DecoderLayerFn(torch.autograd.Function):
     def forward(ctx, x, anchor, layer):
         with torch.no_grad():
             out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe, lora=layer.lora)
-        ctx.save_for_backward(x)
+        off = getattr(layer, "offload", None)
+        if off is not None:
+            ctx.host, ctx.ev = off.save(x)
+            ctx.device = x.device
+            ctx.save_for_backward()
+        else:
+            ctx.host = None
+            ctx.save_for_backward(x)
         ctx.layer = layer
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        (x,) = ctx.saved_tensors
+        if ctx.host is not None:
+            x = ActivationOffload.restore(ctx.host, ctx.ev, ctx.device)
+            ctx.host = None
+        else:
+            (x,) = ctx.saved_tensors
         layer = ctx.layer
         with torch.no_grad():
             _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora)

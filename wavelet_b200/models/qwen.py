@@ -71,6 +71,7 @@ class _Layer:
     batch: BatchCtx | None = None
     moe: Any = None
     lora: dict | None = None
+    offload: Any = None  # ActivationOffload when activations live in host memory
 
 
 class CausalLM:
@@ -115,6 +116,13 @@ class CausalLM:
         self.lora = adapters
         for i, layer in enumerate(self.layers):
             layer.lora = adapters.layer_views(i)
+
+    def enable_activation_offload(self, on: bool = True) -> None:
+        from .layers import ActivationOffload
+
+        off = ActivationOffload() if on else None
+        for layer in self.layers:
+            layer.offload = off
 
     @property
     def trainable(self) -> FlatParams:

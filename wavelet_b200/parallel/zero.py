@@ -45,13 +45,26 @@ class AdamWHyper:
 
 
 class ShardedAdamW:
-    def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1):
+    def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
+                 offload: bool = False, offload_chunk: int = 1 << 26):
         self.flat = flat
         self.h = hyper
         self.group = dp_group
         self.world = dp_world
         self.step_count = 0
         dev = flat.device
+        # optim.cpu_offload: fp32 master / moments live in pinned host memory and
+        # stream through the GPU AdamW kernel in chunks (reference
+        # trainer/optim.py:191-390 offloads optimizer state to pinned CPU)
+        self.offload = offload and dev.type == "cuda"
+        self.offload_chunk = offload_chunk
+        if self.offload:
+            for name in ("master", "exp_avg", "exp_avg_sq"):
+                t = getattr(flat, name)
+                setattr(flat, name, t.cpu().pin_memory())
+                del t
+            self._stage = [torch.empty(min(offload_chunk, flat.shard_numel), device=dev, dtype=torch.float32)
+                           for _ in range(3)]
         self.g_shard = (
             torch.empty(flat.shard_numel, device=dev, dtype=torch.float32) if dp_world > 1 else None
         )
@@ -80,12 +93,15 @@ class ShardedAdamW:
         self.step_count += 1
         compute = flat.compute.detach()
         p16 = compute[flat.shard_slice]
-        ops.adamw_flat_(
-            flat.master, self._g, flat.exp_avg, flat.exp_avg_sq,
-            p16 if flat.compute.dtype == torch.bfloat16 else None,
-            lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
-            step=self.step_count, gscale_host=factor,
-        )
+        if self.offload:
+            self._apply_offloaded(p16, lr, factor)
+        else:
+            ops.adamw_flat_(
+                flat.master, self._g, flat.exp_avg, flat.exp_avg_sq,
+                p16 if flat.compute.dtype == torch.bfloat16 else None,
+                lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
+                step=self.step_count, gscale_host=factor,
+            )
         if compute.dtype != torch.bfloat16:
             p16.copy_(flat.master)
         if self.world > 1:
@@ -93,6 +109,28 @@ class ShardedAdamW:
             dist.all_gather_into_tensor(compute, src, group=self.group)
         flat.zero_grad()
         self._g = None
+
+    def _apply_offloaded(self, p16, lr: float, factor: float) -> None:
+        """Chunk by chunk: host -> device, fused AdamW (writes the bf16 shard),
+        device -> host; all on the current stream, so each chunk's staging
+        buffers are reused only after its copy-back has been issued in order."""
+        flat = self.flat
+        n = flat.shard_numel
+        sp, sm, sv = self._stage
+        for lo in range(0, n, self.offload_chunk):
+            hi = min(n, lo + self.offload_chunk)
+            k = hi - lo
+            sp[:k].copy_(flat.master[lo:hi], non_blocking=True)
+            sm[:k].copy_(flat.exp_avg[lo:hi], non_blocking=True)
+            sv[:k].copy_(flat.exp_avg_sq[lo:hi], non_blocking=True)
+            ops.adamw_flat_(sp[:k], self._g[lo:hi], sm[:k], sv[:k],
+                            p16[lo:hi] if flat.compute.dtype == torch.bfloat16 else None,
+                            lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
+                            step=self.step_count, gscale_host=factor)
+            flat.master[lo:hi].copy_(sp[:k], non_blocking=True)
+            flat.exp_avg[lo:hi].copy_(sm[:k], non_blocking=True)
+            flat.exp_avg_sq[lo:hi].copy_(sv[:k], non_blocking=True)
+        torch.cuda.current_stream(flat.device).synchronize()  # host copies complete before the next step reads them
 
     def clip_factor(self, norm: float) -> float:
         if self.h.max_grad_norm and self.h.max_grad_norm > 0:

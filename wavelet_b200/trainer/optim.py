@@ -102,7 +102,8 @@ class FlatOptimizer:
 
             self.adamw = FusedShardedAdamW(flat, hyper, fabric)  # fused peer-memory RS + AdamW + AG
         else:
-            self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world)
+            self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world,
+                                      offload=bool(getattr(cfg, "cpu_offload", False)))
         self.momentum_buf = None
 
     @property

@@ -69,6 +69,8 @@ class RLTrainer:
 
                 load_hf_weights(model, p)
         self.model = model
+        if c.model.smart_gc:
+            model.enable_activation_offload()
         if self.groups.ep is not None:
             model.ep_group = self.groups.ep
         self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world,

@@ -84,6 +84,8 @@ class SFTTrainer:
                                  if dims.ep > 1 else None)
         if self.groups.ep is not None:
             self.model.ep_group = self.groups.ep
+        if c.model.smart_gc:
+            self.model.enable_activation_offload()
         if not c.model.random_init and _has_weights(c.model.name):
             from ..models.hf_io import load_hf_weights
 
