@@ -1,0 +1,75 @@
+"""Tensor parallelism on 2 GPUs (NCCL all-reduce of the row-parallel partial
+sums, tcgen05 kernels on the local head / column slices) against the
+single-GPU model."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+
+    import torch.distributed as dist
+
+    from wavelet_b200.data.fake import synthetic_sft_microbatches
+    from wavelet_b200.models.config import PRESETS
+    from wavelet_b200.models.qwen import build_model, tp_slicers
+    from wavelet_b200.parallel.zero import AdamWHyper
+    from wavelet_b200.trainer.engine import Engine
+
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        cfg = PRESETS["tiny-gpu"]
+        tp = build_model(cfg, dev, torch.bfloat16, seed=13, tp=(world, rank))
+        tp.tp_group = dist.group.WORLD
+        full = build_model(cfg, dev, torch.bfloat16, seed=13)
+        (b,) = synthetic_sft_microbatches(1, 256, cfg.vocab_size, seed=7, seqs_per_micro=2)
+        b = b.to(dev)
+        lt = Engine(tp, AdamWHyper()).sft_micro_step(b, 1e-3)
+        tp.finalize_grads()
+        lf = Engine(full, AdamWHyper()).sft_micro_step(b, 1e-3)
+        torch.cuda.synchronize()
+        assert abs(lt.item() - lf.item()) < 1e-2 * abs(lf.item()) + 1e-4, (lt.item(), lf.item())
+        sl = tp_slicers(cfg, world, rank)
+        for n in tp.flat.names():
+            key = n.split(".", 1)[-1]
+            r = full.flat.grad_view(n)
+            r = sl[key][1](r) if key in sl else r
+            a = tp.flat.grad_view(n)
+            cos = torch.nn.functional.cosine_similarity(a.flatten().float(), r.flatten().float(), dim=0).item()
+            rel = ((a.float() - r.float()).norm() / (r.float().norm() + 1e-12)).item()
+            assert cos > 0.99 and rel < 0.1, (n, cos, rel)
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        import traceback
+
+        q.put((rank, traceback.format_exc()[-1500:]))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_model_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "ok", 1: "ok"}, res

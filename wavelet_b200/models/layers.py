@@ -63,11 +63,26 @@ def _lin_bwd(dy, x, u, w, gw, ad):
     return ops.gemm(dy, w, b_mn=True, a2=g, b2=ad.A)
 
 
-def _dense_mlp_fwd(x2, P, c, save, lora):
+def _tp_reduce(t, tp):
+    """Sum the row-parallel partial products of the TP ranks (in place)."""
+    if tp is not None:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, group=tp.group)
+    return t
+
+
+def _res(x, tp):
+    # under TP the residual joins the partial sums on one rank only
+    return x if tp is None or tp.rank == 0 else None
+
+
+def _dense_mlp_fwd(x2, P, c, save, lora, tp=None):
     h2, rstd2, _ = ops.rmsnorm_fwd(x2, P["post_norm"], c.rms_eps)
     gu, u_gu = _lin(h2, P["gu_w"], lora.get("gu"))
     a = ops.swiglu_fwd(gu)
-    out, u_dn = _lin(a, P["down_w"], lora.get("down"), res=x2)
+    out, u_dn = _lin(a, P["down_w"], lora.get("down"), res=_res(x2, tp))
+    _tp_reduce(out, tp)
     return out, (dict(h2=h2, rstd2=rstd2, gu=gu, a=a, u_gu=u_gu, u_dn=u_dn) if save else None)
 
 
@@ -75,7 +90,7 @@ _NO_LORA: dict = {}
 
 
 def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool,
-              moe: Any = None, lora: dict | None = None):
+              moe: Any = None, lora: dict | None = None, tp: Any = None):
     lora = lora or _NO_LORA
     T = x.shape[0]
     nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -88,9 +103,10 @@ def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool
     v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
     att, lse = attention_fwd(q, k, v, b.cu_seqlens, b.max_seqlen, True)
     att2 = att.view(T, nq * hd)
-    x2, u_o = _lin(att2, P["o_w"], lora.get("o"), res=x)
+    x2, u_o = _lin(att2, P["o_w"], lora.get("o"), res=_res(x, tp))
+    _tp_reduce(x2, tp)
     if moe is None:
-        out, mc = _dense_mlp_fwd(x2, P, cfg, save, lora)
+        out, mc = _dense_mlp_fwd(x2, P, cfg, save, lora, tp)
     else:
         out, mc = moe.forward(x2, P, save)
     cache = None
@@ -101,7 +117,7 @@ def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool
 
 
 def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cfg: ArchConfig, b: BatchCtx,
-              moe: Any = None, lora: dict | None = None):
+              moe: Any = None, lora: dict | None = None, tp: Any = None):
     lora = lora or _NO_LORA
     T = x.shape[0]
     nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -112,7 +128,7 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
         da = _lin_bwd(dout, mc["a"], mc["u_dn"], P["down_w"], G.get("down_w"), lora.get("down"))
         dgu = ops.swiglu_bwd(mc["gu"], da)
         del da
-        dh2 = _lin_bwd(dgu, mc["h2"], mc["u_gu"], P["gu_w"], G.get("gu_w"), lora.get("gu"))
+        dh2 = _tp_reduce(_lin_bwd(dgu, mc["h2"], mc["u_gu"], P["gu_w"], G.get("gu_w"), lora.get("gu")), tp)
         del dgu
         dx2 = ops.rmsnorm_bwd(c["x2"], P["post_norm"], mc["rstd2"], dh2, dres=dout, dw=G.get("post_norm"))
         del dh2
@@ -129,13 +145,11 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
     dqkv = torch.cat([dq.reshape(T, -1), dk.reshape(T, -1), dv.reshape(T, -1)], 1)
     del dq, dk, dv
     qkv_pre = c["qkv_pre"] if c["qkv_pre"] is not None else qkv
-    ops.ext().qk_norm_rope_bwd(
-        dqkv, qkv_pre, nq, nk, b.pos, b.inv_freq, P.get("q_norm"), P.get("k_norm"), c["rstd_qk"],
-        G.get("q_norm"), G.get("k_norm"),
-    )
+    ops.qk_norm_rope_bwd_(dqkv, qkv_pre, nq, nk, b.pos, b.inv_freq, P.get("q_norm"), P.get("k_norm"), c["rstd_qk"],
+                          G.get("q_norm"), G.get("k_norm"), cfg.rms_eps)
     if G.get("qkv_b") is not None:
         G["qkv_b"].add_(dqkv.float().sum(0))
-    dh1 = _lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv"))
+    dh1 = _tp_reduce(_lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv")), tp)
     del dqkv
     dx = ops.rmsnorm_bwd(x, P["in_norm"], c["rstd1"], dh1, dres=dx2, dw=G.get("in_norm"))
     return dx
@@ -182,7 +196,8 @@ class DecoderLayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, layer):
         with torch.no_grad():
-            out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe, lora=layer.lora)
+            out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe, lora=layer.lora,
+                               tp=layer.tp)
         off = getattr(layer, "offload", None)
         if off is not None:
             ctx.host, ctx.ev = off.save(x)
@@ -203,8 +218,10 @@ class DecoderLayerFn(torch.autograd.Function):
             (x,) = ctx.saved_tensors
         layer = ctx.layer
         with torch.no_grad():
-            _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora)
-            dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe, lora=layer.lora)
+            _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora,
+                                 tp=layer.tp)
+            dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe, lora=layer.lora,
+                           tp=layer.tp)
         return dx, None, None
 
 

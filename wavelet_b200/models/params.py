@@ -132,13 +132,15 @@ class FlatParams:
                 std = std_override if std_override is not None else s.std
                 # generate in fp32 then cast (bf16 normal_ draws differ by dtype)
                 if row_slices and s.name in row_slices:
-                    # a shard of a larger tensor (expert parallelism): draw the full
-                    # tensor with its own seed and keep our rows, so every layout
-                    # of the model holds identical weights
-                    full_shape, lo, hi = row_slices[s.name]
-                    tmp = torch.empty(full_shape, device=self.device, dtype=torch.float32)
+                    # a shard of a larger tensor (expert / tensor parallelism): draw
+                    # the full tensor with its own seed and keep our part, so every
+                    # layout of the model holds identical weights.  The entry is
+                    # (full shape, lo, hi) for a row range or (full shape, fn) with
+                    # fn(full) -> local.
+                    ent = row_slices[s.name]
+                    tmp = torch.empty(ent[0], device=self.device, dtype=torch.float32)
                     tmp.normal_(0.0, std, generator=g)
-                    tmp = tmp[lo:hi]
+                    tmp = ent[1](tmp) if callable(ent[1]) else tmp[ent[1]:ent[2]]
                 else:
                     tmp = torch.empty(v.shape, device=self.device, dtype=torch.float32)
                     tmp.normal_(0.0, std, generator=g)

@@ -56,6 +56,48 @@ def param_specs(cfg: ArchConfig) -> list[ParamSpec]:
 
 
 QUANTIZABLE = ("qkv_w", "o_w", "gu_w", "down_w")  # dense 2-D projections (NF4 for QLoRA)
+
+
+def tp_local_cfg(cfg: ArchConfig, tp: int) -> ArchConfig:
+    """The per-rank layer shape under tensor parallelism: heads and the MLP
+    width are split, the hidden size is not."""
+    if tp == 1:
+        return cfg
+    if cfg.num_heads % tp or cfg.num_kv_heads % tp or cfg.intermediate_size % tp:
+        raise ValueError(f"tp={tp} must divide the heads ({cfg.num_heads}/{cfg.num_kv_heads}) and the MLP width")
+    if cfg.is_moe:
+        raise NotImplementedError("tensor parallelism with MoE layers is not supported (use expert parallelism)")
+    from dataclasses import replace
+
+    return replace(cfg, num_heads=cfg.num_heads // tp, num_kv_heads=cfg.num_kv_heads // tp,
+                   intermediate_size=cfg.intermediate_size // tp)
+
+
+def tp_slicers(cfg: ArchConfig, tp: int, r: int) -> dict[str, tuple]:
+    """name suffix -> (full shape, fn(full) -> this rank's part).  Column-parallel
+    qkv (by heads) and gate/up (by rows), row-parallel o and down (by columns):
+    the Megatron split of a decoder layer."""
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    q, kv = cfg.q_dim, cfg.kv_dim
+    ql, kvl, il = q // tp, kv // tp, I // tp
+
+    def qkv_rows(full):
+        return torch.cat([full[r * ql:(r + 1) * ql], full[q + r * kvl:q + (r + 1) * kvl],
+                          full[q + kv + r * kvl:q + kv + (r + 1) * kvl]], 0)
+
+    def gu_rows(full):
+        return torch.cat([full[r * il:(r + 1) * il], full[I + r * il:I + (r + 1) * il]], 0)
+
+    return {"qkv_w": ((cfg.qkv_dim, H), qkv_rows), "qkv_b": ((cfg.qkv_dim,), qkv_rows),
+            "o_w": ((H, q), lambda f: f[:, r * ql:(r + 1) * ql]), "gu_w": ((2 * I, H), gu_rows),
+            "down_w": ((H, I), lambda f: f[:, r * il:(r + 1) * il])}
+
+
+@dataclass
+class TPContext:
+    group: Any
+    rank: int
+    size: int
 EXPERT_PARAMS = ("exp_gu_w", "exp_down_w")  # sharded by expert under expert parallelism
 
 
@@ -72,20 +114,25 @@ class _Layer:
     moe: Any = None
     lora: dict | None = None
     offload: Any = None  # ActivationOffload when activations live in host memory
+    tp: Any = None  # TPContext under tensor parallelism
 
 
 class CausalLM:
     """A decoder-only LM whose parameters live in a ``FlatParams`` store."""
 
     def __init__(self, cfg: ArchConfig, flat: FlatParams, quant: dict | None = None,
-                 expert_flat: FlatParams | None = None, ep: tuple[int, int] = (1, 0)):
+                 expert_flat: FlatParams | None = None, ep: tuple[int, int] = (1, 0), tp: tuple[int, int] = (1, 0)):
         self.cfg = cfg
+        self.tp_size, self.tp_rank = tp
+        self.tp_group = None  # set by the trainer (NCCL / gloo group of the TP peers)
+        self.layer_cfg = tp_local_cfg(cfg, self.tp_size)
         self.flat = flat
         # expert parallelism: this rank's experts [ep_rank*E/ep, (ep_rank+1)*E/ep) live in expert_flat
         self.expert_flat = expert_flat
         self.ep_size, self.ep_rank = ep
         self.ep_dp_rank = 0
         self.quant = quant or {}  # name -> NF4Weight (frozen QLoRA base projections)
+        self.fused_cpu = False  # run the kernel-path layer functions with their CPU fallbacks
         self.lora = None
         self.device = flat.device
         self.inv_freq = ref.rope_inv_freq(cfg.head_dim, cfg.rope_theta, device=self.device)
@@ -101,7 +148,7 @@ class CausalLM:
                 P.update({n[len(pre):]: expert_flat.view(n) for n in en})
                 if expert_flat.grad is not None:
                     G.update({n[len(pre):]: expert_flat.grad_view(n) for n in en})
-            layer = _Layer(cfg, P, G)
+            layer = _Layer(self.layer_cfg, P, G)
             if cfg.layer_is_moe(i):
                 from .moe import MoEBlock
 
@@ -116,6 +163,18 @@ class CausalLM:
         self.lora = adapters
         for i, layer in enumerate(self.layers):
             layer.lora = adapters.layer_views(i)
+
+    def finalize_grads(self) -> None:
+        """Cross-TP sums of gradients that each TP rank only partially owns:
+        the QK-norm weights are shared by all heads, which are split."""
+        if self.tp_size > 1 and self.flat.grad is not None:
+            import torch.distributed as dist
+
+            for layer in self.layers:
+                for n in ("q_norm", "k_norm"):
+                    g = layer.G.get(n)
+                    if g is not None:
+                        dist.all_reduce(g, group=self.tp_group)
 
     def enable_activation_offload(self, on: bool = True) -> None:
         from .layers import ActivationOffload
@@ -157,14 +216,16 @@ class CausalLM:
     # ----------------------------------------------------------- forward
     def hidden(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
         """Final normalised hidden states [T, H] (autograd-connected)."""
-        if not input_ids.is_cuda:
+        if not input_ids.is_cuda and not self.fused_cpu and self.tp_size == 1:
             if self.expert_flat is not None:
                 raise NotImplementedError("the CPU reference path runs without expert parallelism")
             return self._hidden_cpu(input_ids.reshape(-1), batch)
         ids = input_ids.reshape(-1).contiguous()
         x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"))
+        tpc = TPContext(self.tp_group, self.tp_rank, self.tp_size) if self.tp_size > 1 else None
         for layer in self.layers:
             layer.batch = batch
+            layer.tp = tpc
             if layer.moe is not None:
                 layer.moe.ep_group = self.ep_group
             x = DecoderLayerFn.apply(x, self.anchor, layer)
@@ -253,7 +314,8 @@ class CausalLM:
 
 def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
                 with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
-                lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None) -> CausalLM:
+                lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None,
+                tp: tuple[int, int] | None = None) -> CausalLM:
     """Build (and random-init) a model.
 
     ``lora``: an object with ``rank``, ``alpha``, ``target_modules``, ``dropout``
@@ -265,10 +327,18 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     device = torch.device(device)
     if dtype is None:
         dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
-    specs = param_specs(cfg)
+    tp_size, tp_rank = tp or (1, 0)
+    full_specs = param_specs(cfg)
+    specs = param_specs(tp_local_cfg(cfg, tp_size)) if tp_size > 1 else full_specs
+    if tp_size > 1 and (lora is not None or load_in_4bit or (ep or (1,))[0] > 1):
+        raise NotImplementedError("tensor parallelism does not combine with LoRA, NF4 or expert parallelism here")
     qnames = {s.name for s in specs if load_in_4bit and s.name.split(".", 1)[-1] in QUANTIZABLE}
     frozen = lora is not None
-    seed_index = {s.name: i for i, s in enumerate(specs)}
+    seed_index = {s.name: i for i, s in enumerate(full_specs)}
+    tp_rows = {}
+    if tp_size > 1:
+        sl = tp_slicers(cfg, tp_size, tp_rank)
+        tp_rows = {s.name: sl[s.name.split(".", 1)[-1]] for s in specs if s.name.split(".", 1)[-1] in sl}
     ep_size, ep_rank, ep_dp_rank, ep_dp_world = ep or (1, 0, 0, 1)
     expert_flat = None
     if ep_size > 1:
@@ -292,7 +362,7 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                       alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
     quant = {}
     if init:
-        flat.init_(seed, seed_index=seed_index)
+        flat.init_(seed, seed_index=seed_index, row_slices=tp_rows or None)
     if qnames:
         from ..ops.nf4 import quantize
 
@@ -306,7 +376,7 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                 tmp.normal_(0.0, s.std, generator=g)
             quant[s.name] = quantize(tmp.to(dtype))
             del tmp
-    model = CausalLM(cfg, flat, quant, expert_flat, (ep_size, ep_rank))
+    model = CausalLM(cfg, flat, quant, expert_flat, (ep_size, ep_rank), tp=(tp_size, tp_rank))
     model.ep_dp_rank = ep_dp_rank
     if frozen:
         from .lora import LoRAAdapters

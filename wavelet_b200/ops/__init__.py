@@ -312,7 +312,39 @@ def embedding_fwd(table, ids):
 
 
 def embedding_bwd_(dy, ids, dtable):
+    if not dy.is_cuda:
+        dtable.index_add_(0, ids.reshape(-1), dy.to(dtable.dtype))
+        return
     ext().embedding_bwd(dy.contiguous(), ids.reshape(-1).contiguous(), dtable)
+
+
+def qk_norm_rope_bwd_(dqkv, qkv_pre, n_q, n_k, pos, inv_freq, q_w, k_w, rstd, dq_w, dk_w, eps=1e-6):
+    """In place: d(qkv) through RoPE (and the per-head QK RMSNorm); weight
+    gradients accumulate into ``dq_w`` / ``dk_w``.  CPU: autograd through the
+    reference forward."""
+    if dqkv.is_cuda:
+        ext().qk_norm_rope_bwd(dqkv, qkv_pre, n_q, n_k, pos, inv_freq, q_w, k_w, rstd, dq_w, dk_w)
+        return
+    T = qkv_pre.shape[0]
+    hd = 2 * inv_freq.numel()
+    with torch.enable_grad():
+        x = qkv_pre[:, : (n_q + n_k) * hd].view(T, n_q + n_k, hd).detach().float().requires_grad_(True)
+        leaves = [x]
+        y = x
+        if q_w is not None:
+            qw = q_w.detach().float().requires_grad_(True)
+            kw = k_w.detach().float().requires_grad_(True)
+            leaves += [qw, kw]
+            y = torch.cat([ref.rmsnorm(x[:, :n_q], qw, eps), ref.rmsnorm(x[:, n_q:], kw, eps)], 1)
+        y = ref.apply_rope(y, pos, inv_freq)
+        dy = dqkv[:, : (n_q + n_k) * hd].view(T, n_q + n_k, hd).float()
+        grads = torch.autograd.grad(y, leaves, dy)
+    dqkv[:, : (n_q + n_k) * hd].copy_(grads[0].reshape(T, -1).to(dqkv.dtype))
+    if q_w is not None:
+        if dq_w is not None:
+            dq_w.add_(grads[1].to(dq_w.dtype))
+        if dk_w is not None:
+            dk_w.add_(grads[2].to(dk_w.dtype))
 
 
 # -------------------------------------------------------------- attention

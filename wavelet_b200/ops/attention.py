@@ -35,33 +35,26 @@ def attention_fwd(q, k, v, cu_seqlens, max_seqlen: int, causal: bool = True, sca
         out = ref.attention(q, k, v, cu_seqlens, causal, scale)
         return out, None
     m = _load_ext()
-    if hasattr(m, "attn_fwd"):
-        out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-        lse = torch.empty(q.shape[1], q.shape[0], device=q.device, dtype=torch.float32)
-        m.attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), bool(causal), float(scale), out, lse)
-        return out, lse
-    out, lse, _rng, _unused, _dbg = torch.ops.aten._flash_attention_forward(
-        q, k, v, cu_seqlens, cu_seqlens, int(max_seqlen), int(max_seqlen), 0.0, bool(causal), False, scale=scale
-    )
+    out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    lse = torch.empty(q.shape[1], q.shape[0], device=q.device, dtype=torch.float32)
+    m.attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), bool(causal), float(scale), out, lse)
     return out, lse
 
 
 def attention_bwd(do, q, k, v, out, lse, cu_seqlens, max_seqlen: int, causal: bool = True, scale: float | None = None):
     """Returns (dq, dk, dv)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not q.is_cuda:  # CPU: autograd through the reference attention
+        with torch.enable_grad():
+            qq, kk, vv = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+            o = ref.attention(qq, kk, vv, cu_seqlens, causal, scale)
+            dq, dk, dv = torch.autograd.grad(o, (qq, kk, vv), do.float())
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
     m = _load_ext()
-    if hasattr(m, "attn_bwd"):
-        dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-        dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
-        dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
-        m.attn_bwd(do.contiguous(), q, k, v, out, lse, cu_seqlens, int(max_seqlen), bool(causal), float(scale), dq, dk, dv)
-        return dq, dk, dv
-    rng = torch.zeros(2, dtype=torch.int64, device=q.device)
-    unused = torch.empty(0, device=q.device)
-    dq, dk, dv = torch.ops.aten._flash_attention_backward(
-        do.contiguous(), q, k, v, out, lse, cu_seqlens, cu_seqlens, int(max_seqlen), int(max_seqlen), 0.0,
-        bool(causal), rng, unused, scale=scale
-    )
+    dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+    dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
+    m.attn_bwd(do.contiguous(), q, k, v, out, lse, cu_seqlens, int(max_seqlen), bool(causal), float(scale), dq, dk, dv)
     return dq, dk, dv
 
 

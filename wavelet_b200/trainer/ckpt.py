@@ -77,7 +77,9 @@ class CheckpointManager:
         d = pathing.checkpoint_dir(self.output_dir, step)
         flat = getattr(model, "trainable", model.flat)  # LoRA: only the adapters are saved
         weights = None
-        if self.rank == 0:
+        tp_size = getattr(model, "tp_size", 1)
+        wname = "model.safetensors" if tp_size == 1 else f"model-tp{model.tp_rank}.safetensors"
+        if (self.rank == 0) if tp_size == 1 else (flat.dp_rank == 0):  # one copy of every TP shard
             weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
         experts = None
         ef = getattr(model, "expert_flat", None)
@@ -93,8 +95,10 @@ class CheckpointManager:
                 (d / "trainer").mkdir(parents=True, exist_ok=True)
                 (d / "dataloader").mkdir(parents=True, exist_ok=True)
                 if weights is not None:
-                    _save_safetensors(weights, d / "trainer" / "model.safetensors")
-                    (d / "meta.json").write_text(json.dumps({"step": step, "world_size": self.world, **meta}, indent=2))
+                    _save_safetensors(weights, d / "trainer" / wname)
+                if self.rank == 0:
+                    (d / "meta.json").write_text(json.dumps({"step": step, "world_size": self.world,
+                                                             "tp": tp_size, **meta}, indent=2))
                     (d / "trainer" / "scheduler.json").write_text(json.dumps(scheduler_state or {}, indent=2))
                 if experts is not None:
                     _save_safetensors(experts, d / "trainer" / f"experts-ep{ep_rank}.safetensors")
@@ -142,7 +146,11 @@ class CheckpointManager:
         from safetensors.torch import load_file
 
         meta = json.loads((d / "meta.json").read_text())
-        w = load_file(str(d / "trainer" / "model.safetensors"))
+        tp_size = getattr(model, "tp_size", 1)
+        if int(meta.get("tp", 1)) != tp_size:
+            raise ValueError(f"checkpoint was written with tp={meta.get('tp', 1)}, resuming with tp={tp_size}")
+        w = load_file(str(d / "trainer" / ("model.safetensors" if tp_size == 1 else
+                                           f"model-tp{model.tp_rank}.safetensors")))
         flat = getattr(model, "trainable", model.flat)
         flat.load_state({k: v.to(flat.device) for k, v in w.items()})
         ef = getattr(model, "expert_flat", None)

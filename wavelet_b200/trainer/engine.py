@@ -102,6 +102,7 @@ class Engine:
         return -(lp * valid).sum(), float(valid.sum())
 
     def optimizer_step(self, lr: float) -> dict[str, float]:
+        self.model.finalize_grads()
         return self.opt.step(lr)
 
     def global_token_count(self, local: float, device) -> float:

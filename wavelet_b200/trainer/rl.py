@@ -62,7 +62,9 @@ class RLTrainer:
             model = build_model(arch, w.device, dtype, dp_rank=self.dp_rank, dp_world=self.dp_world, seed=c.seed,
                                 lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                 ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
-                                if dims.ep > 1 else None)
+                                if dims.ep > 1 else None,
+                                tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
+            model.tp_group = self.groups.tp
             p = Path(c.model.name)
             if not c.model.random_init and p.is_dir() and any(p.glob("*.safetensors")):
                 from ..models.hf_io import load_hf_weights
@@ -153,6 +155,7 @@ class RLTrainer:
             for k, v in met.items():
                 agg.setdefault(k, []).append(v)
         lr = lr_at(self.step, c.optim.lr, max(1, c.max_steps or 1), c.scheduler)
+        m.finalize_grads()
         st = self.optimizer.step(lr)
         self.step += 1
         metrics = {k: sum(v) / len(v) for k, v in agg.items() if v}

@@ -65,8 +65,8 @@ class SFTTrainer:
         w = self.world
         dims = ParallelDims(dp_replicate=c.fsdp.dp_replicate, dp_shard=c.fsdp.dp_shard, cp=c.fsdp.cp, tp=c.fsdp.tp,
                             ep=c.fsdp.ep, world_size=w.world_size)
-        if dims.tp > 1 or dims.cp > 1:
-            raise NotImplementedError("tensor / context parallel SFT are not wired into the SFT trainer yet")
+        if dims.cp > 1:
+            raise NotImplementedError("context parallel SFT is not wired into the SFT trainer yet")
         self.groups = Groups(dims, w.rank)
         dp_rank, dp_world = self.groups.dp_rank, dims.dp
         dev = w.device
@@ -81,7 +81,9 @@ class SFTTrainer:
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                  ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
-                                 if dims.ep > 1 else None)
+                                 if dims.ep > 1 else None,
+                                 tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
+        self.model.tp_group = self.groups.tp
         if self.groups.ep is not None:
             self.model.ep_group = self.groups.ep
         if c.model.smart_gc:
@@ -182,6 +184,7 @@ class SFTTrainer:
             tokens += b.num_tokens
             loss += self.engine.sft_micro_step(b, scale)
         lr = lr_at(self.step, c.optim.lr, self.total_steps, c.scheduler)
+        self.model.finalize_grads()
         stats = self.optimizer.step(lr)
         if self.world.distributed:
             torch.distributed.all_reduce(loss, group=self.groups.dp)
