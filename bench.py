@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--workload", default="sft", choices=["sft", "qlora", "grpo-4b"],
                    help="sft: dense full fine-tune (headline); qlora: NF4 base + LoRA r16 on all projections; "
                         "grpo-4b: Qwen3-4B-shape GRPO step (native generator + trainer, integrated)")
+    p.add_argument("--activation-checkpointing", default="none", choices=["none", "full"],
+                   help="none: keep every layer's activations (no recompute); full: recompute each layer in backward")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
                    help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
     return p.parse_args()
@@ -249,6 +251,7 @@ def main():
                         lora=lora, load_in_4bit=qlora)
     hyper = AdamWHyper(lr=2e-4 if qlora else 1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
                        max_grad_norm=1.0)
+    model.set_activation_checkpointing(1 if args.activation_checkpointing == "full" else None)
     engine = Engine(model, hyper, dp_group=None, dp_world=N, fabric=fabric)
     stepper = SFTStepper(engine, dev)
 
@@ -343,6 +346,7 @@ def main():
                 **({"base": "NF4 blocksize 64 (fp32 absmax), frozen", "lora": "r=16 alpha=32 on q/k/v/o/gate/up/down"}
                    if qlora else {}),
                 "optimizer": "AdamW (fp32 master, sharded)" + (" on LoRA adapters" if qlora else ""),
+                "activation_checkpointing": args.activation_checkpointing,
                 "optimizer_comm": ("fused peer-memory RS+AdamW+AG kernels" if fabric is not None
                                    else ("NCCL reduce-scatter/all-gather" if N > 1 else "none (1 GPU)")),
                 "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",

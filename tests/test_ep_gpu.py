@@ -11,7 +11,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, fabric=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import datetime
 
@@ -31,6 +31,12 @@ def _worker(rank, world, port, q):
         cfg = PRESETS["tiny-moe-gpu"]
         ep = build_model(cfg, dev, torch.bfloat16, seed=11, ep=(world, rank, 0, 1))
         ep.ep_group = dist.group.WORLD
+        fab = None
+        if fabric:
+            from wavelet_b200.parallel.fabric import Fabric
+
+            fab = Fabric(rank, world, dev)
+            ep.attach_ep_fabric(fab, capacity_rows=256)  # small: exercises the collective growth
         full = build_model(cfg, dev, torch.bfloat16, seed=11)
         (b,) = synthetic_sft_microbatches(1, 256, cfg.vocab_size, seed=50 + rank, seqs_per_micro=2)
         b = b.to(dev)
@@ -51,6 +57,10 @@ def _worker(rank, world, port, q):
             g = full.flat.grad_view(n).clone()
             dist.all_reduce(g)  # expert gradient over both ranks' tokens
             close(ep.expert_flat.grad_view(n), g[rank * El : (rank + 1) * El], n)
+        torch.cuda.synchronize()
+        if fab is not None:
+            fab.check()
+            fab.close()
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except Exception as e:  # reported to the parent
@@ -60,7 +70,8 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep2_model_matches_single_gpu():
+@pytest.mark.parametrize("fabric", [False, True])
+def test_ep2_model_matches_single_gpu(fabric):
     import torch.multiprocessing as mp
 
     s = socket.socket()
@@ -69,7 +80,7 @@ def test_ep2_model_matches_single_gpu():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, fabric)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

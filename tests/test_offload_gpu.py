@@ -41,3 +41,17 @@ def test_optimizer_offload_matches(cuda_ext):
     torch.cuda.synchronize()
     assert torch.equal(ms[0].flat.compute, ms[1].flat.compute)
     assert torch.equal(ms[0].flat.master.cpu(), ms[1].flat.master)
+
+
+def test_kept_activations_match_recompute(cuda_ext):
+    cfg = PRESETS["tiny-gpu"]
+    (b,) = synthetic_sft_microbatches(1, 512, cfg.vocab_size, seed=5, seqs_per_micro=2)
+    b = b.to("cuda")
+    grads = []
+    for every in (1, None, 2):
+        m = build_model(cfg, "cuda", torch.bfloat16, seed=6)
+        m.set_activation_checkpointing(every)
+        Engine(m, AdamWHyper()).sft_micro_step(b, 1e-3)
+        torch.cuda.synchronize()
+        grads.append(m.flat.grad.clone())
+    assert torch.equal(grads[0], grads[1]) and torch.equal(grads[0], grads[2])

@@ -263,6 +263,31 @@ void adamw_allgather(const std::vector<int64_t>& compute, int64_t world, int64_t
                       (float)eps, (float)wd, bc1, bc2, tot.data_ptr<float>(), cur_stream());
 }
 
+void rows_scatter(const at::Tensor& x, const at::Tensor& src_row, const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                  const c10::optional<at::Tensor>& scale, const std::vector<int64_t>& dst, int64_t world, int64_t ldd) {
+  check_bf16(x, "x");
+  WB_CHECK(src_row.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong && dst_rank.scalar_type() == at::kInt,
+           "rows_scatter: index dtypes");
+  if (scale) check_f32(*scale, "scale");
+  wb::rows_scatter(x.data_ptr(), ld_of(x, "x"), src_row.data_ptr<int64_t>(), dst_rank.data_ptr<int>(),
+                   dst_row.data_ptr<int64_t>(), scale ? scale->data_ptr<float>() : nullptr, peers_of(dst, (int)world),
+                   ldd, (int)src_row.numel(), (int)x.size(1), cur_stream());
+}
+
+void rows_gather_sum(const std::vector<int64_t>& src, int64_t world, int64_t lds, const at::Tensor& src_rank,
+                     const at::Tensor& src_row, const c10::optional<at::Tensor>& w, int64_t k,
+                     const c10::optional<at::Tensor>& res, at::Tensor& out) {
+  WB_CHECK(src_row.scalar_type() == at::kLong && src_rank.scalar_type() == at::kInt, "rows_gather_sum: index dtypes");
+  if (w) check_f32(*w, "w");
+  const bool f32 = out.scalar_type() == at::kFloat;
+  WB_CHECK(f32 || out.scalar_type() == at::kBFloat16, "rows_gather_sum: out bf16 or fp32");
+  if (res) check_bf16(*res, "res");
+  wb::rows_gather_sum(peers_of(src, (int)world), lds, src_rank.data_ptr<int>(), src_row.data_ptr<int64_t>(),
+                      w ? w->data_ptr<float>() : nullptr, (int)k, res ? res->data_ptr() : nullptr,
+                      res ? ld_of(*res, "res") : 0, out.data_ptr(), ld_of(out, "out"), f32, (int)out.size(0),
+                      (int)out.size(1), cur_stream());
+}
+
 void allgather_bf16(const std::vector<int64_t>& dst, int64_t world, int64_t lo, const at::Tensor& src) {
   check_bf16(src, "src");
   wb::allgather_bf16(peers_of(dst, (int)world), (int)world, lo, src.data_ptr(), src.numel(), cur_stream());
@@ -654,6 +679,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_exchange", &norm_exchange);
   m.def("adamw_allgather", &adamw_allgather);
   m.def("allgather_bf16", &allgather_bf16);
+  m.def("rows_scatter", &rows_scatter);
+  m.def("rows_gather_sum", &rows_gather_sum);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);
   m.attr("EPI_BF16") = (int)wb::kEpiBF16;

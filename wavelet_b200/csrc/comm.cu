@@ -227,6 +227,93 @@ __global__ void __launch_bounds__(256) ag_kernel(PeerPtrs dst, int64_t lo, const
   }
 }
 
+// ---------------------------------------------------------------- expert-parallel rows
+// Dispatch: row i of the send list goes to rank dst_rank[i], row dst_row[i] of
+// that rank's receive buffer: out = bf16(scale[i] * x[src_row[i]]).  One warp
+// per row, 16-byte stores straight into peer memory over NVLink (the gather,
+// the routing-weight scale and the transfer are one pass).
+__global__ void __launch_bounds__(256) rows_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                           const int64_t* __restrict__ src_row,
+                                                           const int* __restrict__ dst_rank,
+                                                           const int64_t* __restrict__ dst_row,
+                                                           const float* __restrict__ scale, PeerPtrs dst, int64_t ldd,
+                                                           int n, int H) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + src_row[w] * ldx);
+  uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst.p[dst_rank[w]]) + dst_row[w] * ldd);
+  const float sc = scale ? scale[w] : 1.f;
+  for (int c = lane; c < H / 8; c += 32) {
+    uint4 v = src[c];
+    if (scale) {
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        h[j] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+      }
+    }
+    out[c] = v;
+  }
+}
+
+// Combine: out[t] = res[t] + sum_j w[t*k+j] * src[src_rank[t*k+j]][src_row[t*k+j]]
+// (fp32 accumulation in a fixed slot order; out bf16 or fp32).  One warp per
+// token, plain 16-byte loads from peer memory.
+template <bool F32OUT>
+__global__ void __launch_bounds__(256) rows_gather_sum_kernel(PeerPtrs src, int64_t lds,
+                                                              const int* __restrict__ src_rank,
+                                                              const int64_t* __restrict__ src_row,
+                                                              const float* __restrict__ wt, int k,
+                                                              const __nv_bfloat16* __restrict__ res, int64_t ldr,
+                                                              void* __restrict__ out, int64_t ldo, int T, int H) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  for (int c = lane; c < H / 8; c += 32) {
+    float acc[8];
+    if (res) {
+      const uint4 r = reinterpret_cast<const uint4*>(res + (int64_t)t * ldr)[c];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] = f.x;
+        acc[2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    }
+    for (int s = 0; s < k; ++s) {
+      const int64_t i = (int64_t)t * k + s;
+      const float wv = wt ? wt[i] : 1.f;
+      const uint4 v = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src.p[src_rank[i]]) +
+                                                     src_row[i] * lds)[c];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += wv * f.x;
+        acc[2 * j + 1] += wv * f.y;
+      }
+    }
+    if constexpr (F32OUT) {
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + (int64_t)t * ldo) + 2 * c;
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 o;
+      o.x = pack2(acc[0], acc[1]);
+      o.y = pack2(acc[2], acc[3]);
+      o.z = pack2(acc[4], acc[5]);
+      o.w = pack2(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + (int64_t)t * ldo)[c] = o;
+    }
+  }
+}
+
 inline int grid_for(int64_t work, int threads, int cap) {
   int64_t b = (work + threads - 1) / threads;
   if (b < 1) b = 1;
@@ -324,6 +411,29 @@ void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src,
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 256, 148 * 8);
   WB_WORLD_SWITCH(world, comm::ag_kernel<kW><<<grid, 256, 0, st>>>(dst, lo, static_cast<const uint4*>(src), n8));
+}
+
+void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,
+                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, cudaStream_t st) {
+  if (n <= 0) return;
+  if (H % 8 || ldx % 8 || ldd % 8) throw std::runtime_error("wavelet_b200 rows_scatter: H and strides must be multiples of 8");
+  comm::rows_scatter_kernel<<<(n + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, src_row, dst_rank,
+                                                         dst_row, scale, dst, ldd, n, H);
+}
+
+void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, const int64_t* src_row, const float* w,
+                     int k, const void* res, int64_t ldr, void* out, int64_t ldo, bool f32_out, int T, int H,
+                     cudaStream_t st) {
+  if (T <= 0) return;
+  if (H % 8 || lds % 8 || ldo % 8 || (res && ldr % 8))
+    throw std::runtime_error("wavelet_b200 rows_gather_sum: H and strides must be multiples of 8");
+  const int grid = (T + 7) / 8;
+  if (f32_out)
+    comm::rows_gather_sum_kernel<true><<<grid, 256, 0, st>>>(src, lds, src_rank, src_row, w, k,
+                                                             static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H);
+  else
+    comm::rows_gather_sum_kernel<false><<<grid, 256, 0, st>>>(src, lds, src_rank, src_row, w, k,
+                                                              static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H);
 }
 
 }  // namespace wb

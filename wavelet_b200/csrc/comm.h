@@ -65,4 +65,12 @@ void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* mast
 void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src, int64_t n,
                     cudaStream_t st);
 
+// Expert-parallel row exchange over peer memory (comm.cu): dispatch rows to
+// their expert's rank / combine the k expert outputs of every token.
+void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,
+                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, cudaStream_t st);
+void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, const int64_t* src_row, const float* w,
+                     int k, const void* res, int64_t ldr, void* out, int64_t ldo, bool f32_out, int T, int H,
+                     cudaStream_t st);
+
 }  // namespace wb

@@ -191,14 +191,20 @@ class ActivationOffload:
 
 
 class DecoderLayerFn(torch.autograd.Function):
-    """Activation-checkpointed decoder layer: saves x, recomputes in backward."""
+    """One decoder layer as one autograd node.  With ``layer.recompute``
+    (activation checkpointing, the default) only the input is saved and the
+    backward recomputes the layer; otherwise the forward keeps the layer's
+    activations and the backward uses them directly (one GEMM pass fewer,
+    about 0.66 GB per layer per 4096 tokens at the 7B shape)."""
 
     @staticmethod
     def forward(ctx, x, anchor, layer):
+        keep = not getattr(layer, "recompute", True)
         with torch.no_grad():
-            out, _ = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=False, moe=layer.moe, lora=layer.lora,
-                               tp=layer.tp)
-        off = getattr(layer, "offload", None)
+            out, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=keep, moe=layer.moe, lora=layer.lora,
+                                   tp=layer.tp)
+        ctx.cache = cache  # kept activations: the backward skips the recompute
+        off = getattr(layer, "offload", None) if not keep else None
         if off is not None:
             ctx.host, ctx.ev = off.save(x)
             ctx.device = x.device
@@ -218,8 +224,10 @@ class DecoderLayerFn(torch.autograd.Function):
             (x,) = ctx.saved_tensors
         layer = ctx.layer
         with torch.no_grad():
-            _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora,
-                                 tp=layer.tp)
+            cache, ctx.cache = ctx.cache, None
+            if cache is None:
+                _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora,
+                                     tp=layer.tp)
             dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe, lora=layer.lora,
                            tp=layer.tp)
         return dx, None, None

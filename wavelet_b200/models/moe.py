@@ -112,6 +112,7 @@ class MoEBlock:
         self.cfg = cfg
         self.layer = layer_idx
         self.ep_group = None
+        self.ep_fabric = None  # parallel.ep_fabric.FabricEP: dispatch / combine over peer memory
         self.ep_size = ep_size
         self.ep_rank = ep_rank
         self.E_loc = cfg.num_experts // ep_size
@@ -144,7 +145,7 @@ class MoEBlock:
                          None, None, E, ops.EPI_BF16, 1.0)
         return xs, gu, a, y
 
-    def _experts_bwd(self, dy, c, P, G):
+    def _experts_bwd(self, dy, c, P, G, out=None):
         """Backward of ``_experts`` from the padded-row gradient ``dy`` [R, H];
         accumulates the expert weight gradients, returns d(xs) [R, H]."""
         cfg = self.cfg
@@ -161,7 +162,7 @@ class MoEBlock:
         if G.get("exp_gu_w") is not None:
             ops.gemm_grouped(dgu, True, c["xs"], True, G["exp_gu_w"].view(E * 2 * Ie, H), 2, 2 * Ie, H, rt.R, None, 0,
                              0, rt.k_start, rt.k_len, E, ops.EPI_F32_ACC, 1.0)
-        dxs = torch.empty(rt.R, H, device=dy.device, dtype=dy.dtype)
+        dxs = out if out is not None else torch.empty(rt.R, H, device=dy.device, dtype=dy.dtype)
         ops.gemm_grouped(dgu, False, P["exp_gu_w"].view(E * 2 * Ie, H), True, dxs, 1, rt.R, H, 2 * Ie, rt.tile_group,
                          2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
         return dxs
@@ -206,6 +207,8 @@ class MoEBlock:
         k = cfg.num_experts_per_tok
         h2, rstd2, _ = ops.rmsnorm_fwd(x2, P["post_norm"], cfg.rms_eps)
         probs, topv, topi, s, w = self._route(h2, P)
+        if self.ep_fabric is not None and self.ep_size > 1:
+            return self._forward_fabric(x2, P, save, h2, rstd2, probs, topv, topi, s, w)
         if self.ep_size > 1:
             plan, x_recv, el = self._dispatch(h2, topi)
             rt = Routing(el.view(-1, 1), self.E_loc)
@@ -229,12 +232,52 @@ class MoEBlock:
                          y_copy=y_copy, f=f, plan=plan)
         return out, cache
 
+    # ------------------------------------------- expert parallel over peer memory
+    def _fabric_experts(self, xs, P, fp, y_out):
+        cfg = self.cfg
+        E, H, Ie = self.E_loc, cfg.hidden_size, cfg.moe_intermediate_size
+        gu = torch.empty(fp.R, 2 * Ie, device=xs.device, dtype=xs.dtype)
+        ops.gemm_grouped(xs, False, P["exp_gu_w"].view(E * 2 * Ie, H), False, gu, 1, fp.R, 2 * Ie, H, fp.tile_group,
+                         2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
+        a = ops.swiglu_fwd(gu)
+        ops.gemm_grouped(a, False, P["exp_down_w"].view(E * H, Ie), False, y_out, 1, fp.R, H, Ie, fp.tile_group, H,
+                         E * H, None, None, E, ops.EPI_BF16, 1.0)
+        return gu, a
+
+    def _forward_fabric(self, x2, P, save, h2, rstd2, probs, topv, topi, s, w):
+        cfg = self.cfg
+        T, k = x2.shape[0], cfg.num_experts_per_tok
+        fe = self.ep_fabric
+        fp = fe.plan(topi)
+        xs = fe.dispatch("xs", h2, fp)  # rows land directly in the owner's padded expert layout
+        gu, a = self._fabric_experts(xs, P, fp, fe.view("y", fp.R))
+        out = torch.empty_like(x2)
+        fe.combine("y", fp, k, w, x2, out)  # out = x2 + sum_k w_k y_k, read from the owners
+        f = fp.counts.float() / (T * k)
+        self.last_aux = float(cfg.num_experts * (f * probs.mean(0)).sum())
+        self.last_counts = fp.counts
+        cache = None
+        if save:
+            y_copy = fe.gather_copies("y", fp, T, k)
+            cache = dict(h2=h2, rstd2=rstd2, probs=probs, topv=topv, topi=topi, s=s, w=w, rt=fp, xs=xs.clone(),
+                         gu=gu, a=a, y_copy=y_copy, f=f, plan=None, fplan=fp)
+        return out, cache
+
     # ------------------------------------------------------------ backward
     def backward(self, dout, x2, c, P, G):
         cfg = self.cfg
         H, k = cfg.hidden_size, cfg.num_experts_per_tok
         T = x2.shape[0]
         rt: Routing = c["rt"]
+        if c.get("fplan") is not None:
+            fe, fp = self.ep_fabric, c["fplan"]
+            dy = fe.dispatch("dy", dout.contiguous(), fp, scale=c["w"].reshape(-1).float().contiguous())
+            self._experts_bwd(dy, c, P, G, out=fe.view("dxs", fp.R))
+            dh2 = torch.empty(T, H, device=dout.device, dtype=torch.float32)
+            fe.combine("dxs", fp, k, None, None, dh2)
+            tok_copy = torch.arange(T, device=dout.device).repeat_interleave(k)
+            dw = (dout.index_select(0, tok_copy).float() * c["y_copy"].float()).sum(-1).view(T, k)
+            return self._router_bwd(dout, x2, c, P, G, dw, dh2)
         tok_copy = torch.arange(T, device=dout.device).repeat_interleave(k)
         dout_rows = dout.index_select(0, tok_copy).float()  # [T*k, H] in (token, slot) order
         w = c["w"].reshape(-1, 1)
@@ -258,6 +301,11 @@ class MoEBlock:
         else:
             dh2.index_add_(0, rt.tok, dxs.index_select(0, rt.pos).float())
         del dxs
+        return self._router_bwd(dout, x2, c, P, G, dw, dh2)
+
+    def _router_bwd(self, dout, x2, c, P, G, dw, dh2):
+        cfg = self.cfg
+        T = x2.shape[0]
         # router: top-k weights (optionally renormalised) and the aux loss
         if cfg.norm_topk_prob:
             wv = c["w"]
@@ -285,6 +333,13 @@ class MoEBlock:
             out, _, _ = moe_reference(h2, P["router_w"], P["exp_gu_w"], P["exp_down_w"], cfg)
             return x + out
         probs, topv, topi, s, w = self._route(h2, P)
+        if self.ep_fabric is not None and self.ep_size > 1:
+            fe = self.ep_fabric
+            fp = fe.plan(topi)
+            xs = fe.dispatch("xs", h2, fp)
+            self._fabric_experts(xs, P, fp, fe.view("y", fp.R))
+            out = torch.empty_like(x)
+            return fe.combine("y", fp, k, w, x, out)
         if self.ep_size > 1:
             plan, x_recv, el = self._dispatch(h2, topi)
             rt = Routing(el.view(-1, 1), self.E_loc)

@@ -114,6 +114,7 @@ class _Layer:
     moe: Any = None
     lora: dict | None = None
     offload: Any = None  # ActivationOffload when activations live in host memory
+    recompute: bool = True  # activation checkpointing of this layer
     tp: Any = None  # TPContext under tensor parallelism
 
 
@@ -175,6 +176,23 @@ class CausalLM:
                     g = layer.G.get(n)
                     if g is not None:
                         dist.all_reduce(g, group=self.tp_group)
+
+    def attach_ep_fabric(self, fabric, capacity_rows: int = 1 << 16):
+        """Expert dispatch / combine over peer memory (parallel.ep_fabric) for
+        every MoE layer; ``fabric`` spans the expert-parallel group."""
+        from ..parallel.ep_fabric import FabricEP
+
+        fe = FabricEP(fabric, self.ep_group, self.cfg.num_experts, self.cfg.hidden_size, capacity_rows)
+        for layer in self.layers:
+            if layer.moe is not None:
+                layer.moe.ep_fabric = fe
+        return fe
+
+    def set_activation_checkpointing(self, every: int | None) -> None:
+        """Recompute every ``every``-th layer in backward (1: all, the
+        reference's full mode with freq 1); None keeps all activations."""
+        for i, layer in enumerate(self.layers):
+            layer.recompute = every is not None and (i % every == 0)
 
     def enable_activation_offload(self, on: bool = True) -> None:
         from .layers import ActivationOffload

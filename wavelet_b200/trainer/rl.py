@@ -71,6 +71,8 @@ class RLTrainer:
 
                 load_hf_weights(model, p)
         self.model = model
+        ac = c.model.activation_checkpointing
+        model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
             model.enable_activation_offload()
         if self.groups.ep is not None:

@@ -86,6 +86,8 @@ class SFTTrainer:
         self.model.tp_group = self.groups.tp
         if self.groups.ep is not None:
             self.model.ep_group = self.groups.ep
+        ac = c.model.activation_checkpointing
+        self.model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
             self.model.enable_activation_offload()
         if not c.model.random_init and _has_weights(c.model.name):
