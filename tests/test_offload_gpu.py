@@ -1,5 +1,6 @@
 """Activation offloading (layer inputs in pinned host memory) and optimizer
-state offloading (chunked host <-> device AdamW) give bit-identical results."""
+state offloading (chunked host <-> device AdamW) give the results of the
+device-resident runs."""
 
 import pytest
 import torch
@@ -24,7 +25,9 @@ def test_activation_offload_matches(cuda_ext):
         Engine(m, AdamWHyper()).sft_micro_step(b, 1e-3)
         torch.cuda.synchronize()
         grads.append(m.flat.grad.clone())
-    assert torch.equal(grads[0], grads[1])
+    # the restored layer inputs are bit-exact; the norm-weight and embedding
+    # gradients accumulate with float atomics, so only their summation order varies
+    torch.testing.assert_close(grads[0], grads[1], rtol=1e-4, atol=1e-6)
 
 
 def test_optimizer_offload_matches(cuda_ext):

@@ -1,6 +1,6 @@
-"""Tensor parallelism on 2 GPUs (NCCL all-reduce of the row-parallel partial
-sums, tcgen05 kernels on the local head / column slices) against the
-single-GPU model."""
+"""Tensor parallelism on 2 GPUs (row-parallel partial sums reduced by NCCL
+all-reduce, or by the fused GEMM -> all-reduce over peer memory; tcgen05
+kernels on the local head / column slices) against the single-GPU model."""
 
 import os
 import socket
@@ -11,7 +11,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, fused):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import datetime
 
@@ -31,6 +31,12 @@ def _worker(rank, world, port, q):
         cfg = PRESETS["tiny-gpu"]
         tp = build_model(cfg, dev, torch.bfloat16, seed=13, tp=(world, rank))
         tp.tp_group = dist.group.WORLD
+        fab = None
+        if fused:
+            from wavelet_b200.parallel.fabric import Fabric
+
+            fab = Fabric(rank, world, dev)
+            tp.attach_tp_fabric(fab, capacity=4096)  # small: exercises the collective growth
         full = build_model(cfg, dev, torch.bfloat16, seed=13)
         (b,) = synthetic_sft_microbatches(1, 256, cfg.vocab_size, seed=7, seqs_per_micro=2)
         b = b.to(dev)
@@ -48,6 +54,9 @@ def _worker(rank, world, port, q):
             cos = torch.nn.functional.cosine_similarity(a.flatten().float(), r.flatten().float(), dim=0).item()
             rel = ((a.float() - r.float()).norm() / (r.float().norm() + 1e-12)).item()
             assert cos > 0.99 and rel < 0.1, (n, cos, rel)
+        if fab is not None:
+            fab.check()
+            fab.close()
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except Exception:
@@ -57,7 +66,8 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_model_matches_single_gpu():
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fabric"])
+def test_tp2_model_matches_single_gpu(fused):
     import torch.multiprocessing as mp
 
     s = socket.socket()
@@ -66,7 +76,7 @@ def test_tp2_model_matches_single_gpu():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)

@@ -278,6 +278,12 @@ class FSDPConfig(ConfigModel):
     ep: int = Field(default=1, ge=1)
     cpu_offload: bool = False
     reshard_after_forward: bool = True
+    # how expert-parallel token copies move on one CUDA node: fused row kernels
+    # over peer memory ("fabric") or variable-split NCCL all-to-alls ("nccl")
+    ep_dispatch: Literal["fabric", "nccl"] = "fabric"
+    # how tensor-parallel partial sums are reduced on one CUDA node: GEMMs whose
+    # epilogue stores into the peers' buffers ("fabric") or NCCL all-reduce
+    tp_reduce: Literal["fabric", "nccl"] = "fabric"
 
     @model_validator(mode="after")
     def _checks(self):

@@ -263,6 +263,68 @@ void adamw_allgather(const std::vector<int64_t>& compute, int64_t world, int64_t
                       (float)eps, (float)wd, bc1, bc2, tot.data_ptr<float>(), cur_stream());
 }
 
+void gather_from_peers(const std::vector<int64_t>& src, int64_t world, int64_t off, int64_t n, at::Tensor& dst) {
+  check_bf16(dst, "dst");
+  WB_CHECK(dst.is_contiguous() && dst.numel() >= n * world, "gather_from_peers: dst too small");
+  wb::gather_from_peers(peers_of(src, (int)world), (int)world, off, n, dst.data_ptr(), cur_stream());
+}
+
+// Fused GEMM -> all-reduce / reduce-scatter, GEMM half: the tcgen05 GEMM of
+// a (K-major [M, K]) and b (B(n, k) K-major [N, K] or MN-major [K, N]), with
+// an optional second operand pair (LoRA), writes its bf16 partial product
+// into every peer's receive buffer at element `off` (kEpiPeerBF16).
+void gemm_peer(const at::Tensor& a, const at::Tensor& b, bool b_mn, int64_t N, double alpha,
+               const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2,
+               const std::vector<int64_t>& peers, int64_t rank, int64_t off, int64_t ldc, int64_t rs_rows) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  WB_CHECK(!peers.empty() && peers.size() <= 8, "gemm_peer: 1..8 peer buffers");
+  const c10::cuda::CUDAGuard guard(a.device());
+  wb::GemmArgs g;
+  g.A = a.data_ptr();
+  g.lda = ld_of(a, "a");
+  g.B = b.data_ptr();
+  g.ldb = ld_of(b, "b");
+  g.b_mn = b_mn;
+  g.M = a.size(0);
+  g.K = a.size(1);
+  g.N = N;
+  if (a2) {
+    WB_CHECK(b2.has_value(), "gemm_peer: a2 needs b2");
+    check_bf16(*a2, "a2");
+    check_bf16(*b2, "b2");
+    g.A2 = a2->data_ptr();
+    g.lda2 = ld_of(*a2, "a2");
+    g.B2 = b2->data_ptr();
+    g.ldb2 = ld_of(*b2, "b2");
+    g.K2 = a2->size(1);
+  }
+  g.epi = wb::kEpiPeerBF16;
+  g.alpha = static_cast<float>(alpha);
+  g.peer_world = static_cast<int>(peers.size());
+  for (size_t r = 0; r < peers.size(); ++r) g.peer[r] = reinterpret_cast<void*>(peers[r]);
+  g.peer_rank = static_cast<int>(rank);
+  g.peer_off = off;
+  g.ldc = ldc;
+  g.C = g.peer[rank];
+  g.peer_rs_rows = rs_rows;
+  wb::gemm_bf16(g, cur_stream());
+}
+
+void slots_sum(const at::Tensor& slots, int64_t world, int64_t stride, int64_t n,
+               const c10::optional<at::Tensor>& res, at::Tensor& out) {
+  check_bf16(slots, "slots");
+  check_bf16(out, "out");
+  WB_CHECK(slots.is_contiguous() && out.is_contiguous() && slots.numel() >= (world - 1) * stride + n &&
+               out.numel() >= n, "slots_sum: sizes");
+  if (res) {
+    check_bf16(*res, "res");
+    WB_CHECK(res->is_contiguous() && res->numel() >= n, "slots_sum: res");
+  }
+  wb::slots_sum(slots.data_ptr(), (int)world, stride, n, res ? res->data_ptr() : nullptr, out.data_ptr(),
+                cur_stream());
+}
+
 void rows_scatter(const at::Tensor& x, const at::Tensor& src_row, const at::Tensor& dst_rank, const at::Tensor& dst_row,
                   const c10::optional<at::Tensor>& scale, const std::vector<int64_t>& dst, int64_t world, int64_t ldd) {
   check_bf16(x, "x");
@@ -680,6 +742,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_allgather", &adamw_allgather);
   m.def("allgather_bf16", &allgather_bf16);
   m.def("rows_scatter", &rows_scatter);
+  m.def("gather_from_peers", &gather_from_peers);
+  m.def("gemm_peer", &gemm_peer);
+  m.def("slots_sum", &slots_sum);
   m.def("rows_gather_sum", &rows_gather_sum);
   m.def("read_error", &read_error);
   m.def("clear_error", &clear_error);

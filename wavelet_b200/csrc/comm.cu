@@ -314,6 +314,47 @@ __global__ void __launch_bounds__(256) rows_gather_sum_kernel(PeerPtrs src, int6
   }
 }
 
+// Pull-gather: dst[r * n + i] = src[r][off + i] for every rank r (16-byte
+// loads from peer memory; n and off multiples of 8 bf16).  Used to re-form a
+// full weight tensor from its expert-parallel shards in place.
+__global__ void __launch_bounds__(256) gather_from_peers_kernel(PeerPtrs src, int world, int64_t off, int64_t n8,
+                                                                uint4* __restrict__ dst) {
+  const int64_t total = n8 * world;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / n8);
+    const int64_t j = i - (int64_t)r * n8;
+    dst[i] = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src.p[r]) + off)[j];
+  }
+}
+
+// out[i] = res[i] + sum_r slots[r * stride + i] in rank order (fp32 sum, bf16
+// out): the local half of the fused GEMM -> all-reduce, run after the
+// barrier that orders every peer's epilogue stores into `slots`.  Every rank
+// sums the same values in the same order, so all replicas agree bit for bit.
+__global__ void __launch_bounds__(256) slots_sum_kernel(const __nv_bfloat16* __restrict__ slots, int world,
+                                                        int64_t stride, int64_t n8,
+                                                        const __nv_bfloat16* __restrict__ res,
+                                                        __nv_bfloat16* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float f[8];
+    if (res) {
+      const uint4 w = reinterpret_cast<const uint4*>(res)[i];
+      f[0] = bf16_lo(w.x), f[1] = bf16_hi(w.x), f[2] = bf16_lo(w.y), f[3] = bf16_hi(w.y);
+      f[4] = bf16_lo(w.z), f[5] = bf16_hi(w.z), f[6] = bf16_lo(w.w), f[7] = bf16_hi(w.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = 0.f;
+    }
+    for (int r = 0; r < world; ++r) {
+      const uint4 w = reinterpret_cast<const uint4*>(slots + r * stride)[i];
+      f[0] += bf16_lo(w.x), f[1] += bf16_hi(w.x), f[2] += bf16_lo(w.y), f[3] += bf16_hi(w.y);
+      f[4] += bf16_lo(w.z), f[5] += bf16_hi(w.z), f[6] += bf16_lo(w.w), f[7] += bf16_hi(w.w);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]),
+                                                  pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+  }
+}
+
 inline int grid_for(int64_t work, int threads, int cap) {
   int64_t b = (work + threads - 1) / threads;
   if (b < 1) b = 1;
@@ -411,6 +452,22 @@ void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src,
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 256, 148 * 8);
   WB_WORLD_SWITCH(world, comm::ag_kernel<kW><<<grid, 256, 0, st>>>(dst, lo, static_cast<const uint4*>(src), n8));
+}
+
+void gather_from_peers(const PeerPtrs& src, int world, int64_t off, int64_t n, void* dst, cudaStream_t st) {
+  if (n <= 0) return;
+  if (n % 8 || off % 8) throw std::runtime_error("wavelet_b200 gather_from_peers: n and offset must be multiples of 8");
+  comm::gather_from_peers_kernel<<<comm::grid_for(n / 8 * world, 256, 148 * 8), 256, 0, st>>>(
+      src, world, off, n / 8, static_cast<uint4*>(dst));
+}
+
+void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const void* res, void* out,
+               cudaStream_t st) {
+  if (n <= 0) return;
+  if (n % 8 || stride % 8) throw std::runtime_error("wavelet_b200 slots_sum: n and slot stride must be multiples of 8");
+  comm::slots_sum_kernel<<<comm::grid_for(n / 8, 256, 148 * 8), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(slots), world, stride, n / 8, static_cast<const __nv_bfloat16*>(res),
+      static_cast<__nv_bfloat16*>(out));
 }
 
 void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,

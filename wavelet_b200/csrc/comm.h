@@ -65,6 +65,15 @@ void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* mast
 void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src, int64_t n,
                     cudaStream_t st);
 
+// dst[r * n + i] = src[r][off + i] (bf16) for every rank r: re-forms a full
+// tensor from its per-rank shards (expert-parallel policy refresh).
+void gather_from_peers(const PeerPtrs& src, int world, int64_t off, int64_t n, void* dst, cudaStream_t st);
+
+// out[i] = res[i] (optional) + sum_r slots[r * stride + i], r in rank order:
+// the local reduction after a kEpiPeerBF16 GEMM filled `slots` (one slot per
+// source rank).  n and stride multiples of 8.
+void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const void* res, void* out, cudaStream_t st);
+
 // Expert-parallel row exchange over peer memory (comm.cu): dispatch rows to
 // their expert's rank / combine the k expert outputs of every token.
 void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,

@@ -90,6 +90,9 @@ struct Params {
   const float* q_absmax;
   int64_t q_cols;
   float lut[16];
+  void* peer[8];  // kEpiPeerBF16 receive buffers (GemmArgs::peer)
+  int peer_world, peer_rank;
+  int64_t peer_off, peer_rs_rows;
 };
 
 // Tile decode shared by the three warp roles (they must agree exactly).
@@ -183,6 +186,34 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (col0 + j < p.N) c[j] = __float2bfloat16(f[j]);
+    }
+  } else if constexpr (EPI == kEpiPeerBF16) {
+    // partial product -> peer receive buffers over NVLink (plain 16-byte stores)
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      w[j] = pack_bf16(__uint_as_float(v[2 * j]) * p.alpha, __uint_as_float(v[2 * j + 1]) * p.alpha);
+    int64_t drow = row;
+    int first = p.peer_rank + 1, count = p.peer_world;
+    if (p.peer_rs_rows > 0) {
+      first = static_cast<int>(row / p.peer_rs_rows);
+      drow = row - (int64_t)first * p.peer_rs_rows;
+      count = 1;
+    }
+    const bool vec = full && ((p.ldc & 7) == 0) && ((p.peer_off & 7) == 0);
+    for (int i = 0; i < count; ++i) {
+      int r = first + i;
+      if (r >= p.peer_world) r -= p.peer_world;
+      __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.peer[r]) + p.peer_off + drow * p.ldc + col0;
+      if (vec) {
+        uint4* dst = reinterpret_cast<uint4*>(c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N) c[j] = __float2bfloat16(__uint_as_float(v[j]) * p.alpha);
+      }
     }
   } else {
     float* c = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col0;
@@ -570,6 +601,11 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   p.q_absmax = g.q_absmax;
   p.q_cols = g.q_cols;
   for (int i = 0; i < 16; ++i) p.lut[i] = g.q_lut[i];
+  for (int i = 0; i < 8; ++i) p.peer[i] = g.peer[i];
+  p.peer_world = g.peer_world;
+  p.peer_rank = g.peer_rank;
+  p.peer_off = g.peer_off;
+  p.peer_rs_rows = g.peer_rs_rows;
   const int tiles = p.num_m * p.num_n * (GROUP == 2 ? g.groups : 1);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
   kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem_bytes(), stream>>>(ta, tb, ta2, tb2, p);
@@ -612,6 +648,17 @@ void gemm_bf16(const GemmArgs& g, cudaStream_t stream) {
       throw std::runtime_error("wavelet_b200 nf4 gemm: weight shape does not match M/N/K");
     if (g.b_mn) return launch<false, true, kEpiBF16, 0, true>(g, stream);
     return launch<false, false, kEpiBF16, 0, true>(g, stream);
+  }
+  if (g.epi == kEpiPeerBF16) {
+    // fused GEMM -> all-reduce / reduce-scatter: forward (B K-major) or dgrad (B MN-major)
+    if (g.a_mn || g.peer_world < 1 || g.peer_world > 8 || g.peer_rank < 0 || g.peer_rank >= g.peer_world)
+      throw std::runtime_error("wavelet_b200 peer gemm: K-major A and 1..8 ranks");
+    for (int r = 0; r < g.peer_world; ++r)
+      if (!g.peer[r]) throw std::runtime_error("wavelet_b200 peer gemm: missing peer buffer");
+    if (g.peer_rs_rows > 0 && (int64_t)g.peer_world * g.peer_rs_rows < g.M)
+      throw std::runtime_error("wavelet_b200 peer gemm: reduce-scatter rows do not cover M");
+    if (g.b_mn) return launch<false, true, kEpiPeerBF16>(g, stream);
+    return launch<false, false, kEpiPeerBF16>(g, stream);
   }
 #define WB_GEMM_DISPATCH(AM, BMJ)                                               \
   if (g.a_mn == AM && g.b_mn == BMJ) {                                          \

@@ -9,6 +9,9 @@ enum GemmEpilogue : int {
   kEpiBF16 = 0,    // C(bf16) = alpha * acc (+ bias)
   kEpiF32 = 1,     // C(fp32) = alpha * acc
   kEpiF32Acc = 2,  // C(fp32) += alpha * acc
+  // C(bf16) = alpha * acc stored straight into peer memory: the GEMM half of a
+  // fused GEMM -> all-reduce / reduce-scatter (see peer_* below).
+  kEpiPeerBF16 = 3,
 };
 
 struct GemmArgs {
@@ -59,6 +62,17 @@ struct GemmArgs {
   const float* q_absmax = nullptr;
   int64_t q_rows = 0, q_cols = 0;
   float q_lut[16] = {0};
+  // kEpiPeerBF16 (dense mode): peer[r] is rank r's receive buffer (fabric
+  // memory, mapped on this rank) and this rank's partial product lands at
+  // element peer_off + row * ldc + col of it.  peer_rs_rows == 0: every rank
+  // gets every row (all-reduce); > 0: row m goes only to rank m / peer_rs_rows,
+  // at row m % peer_rs_rows (reduce-scatter).  Stores start at the next rank
+  // (rank-rotated) so the ranks do not all write the same peer at once.
+  void* peer[8] = {nullptr};
+  int peer_world = 0;
+  int peer_rank = 0;
+  int64_t peer_off = 0;
+  int64_t peer_rs_rows = 0;
 };
 
 void gemm_bf16(const GemmArgs& g, cudaStream_t stream);

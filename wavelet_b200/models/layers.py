@@ -48,19 +48,37 @@ def _lin(x, w, ad, bias=None, res=None):
     return ops.gemm(x, w, bias=bias, res=res, a2=u, b2=ad.B), u
 
 
-def _lin_bwd(dy, x, u, w, gw, ad):
+def _fused_tp(tp, w, ad) -> bool:
+    # the fused GEMM -> all-reduce covers plain bf16 weights (no adapter / NF4)
+    return tp is not None and tp.fabric is not None and ad is None and isinstance(w, torch.Tensor)
+
+
+def _lin_rowpar(x, w, ad, res, tp):
+    """Row-parallel linear summed over the TP ranks (+ res): one fused
+    GEMM -> all-reduce over peer memory when the TP group has a fabric, else
+    the GEMM (residual on TP rank 0 only) and an NCCL all-reduce."""
+    if _fused_tp(tp, w, ad):
+        return tp.fabric.gemm_allreduce(x, w, res=res), None
+    y, u = _lin(x, w, ad, res=_res(res, tp))
+    return _tp_reduce(y, tp), u
+
+
+def _lin_bwd(dy, x, u, w, gw, ad, tp=None):
     """dx of ``_lin``; accumulates dW into ``gw`` (None: frozen) and the
-    adapter gradients (block-diagonal dB, dA) when ``ad`` is given."""
+    adapter gradients (block-diagonal dB, dA) when ``ad`` is given.  With
+    ``tp`` (column-parallel weight) dx is summed over the TP ranks."""
     if gw is not None:
         ops.gemm(dy, x, a_mn=True, b_mn=True, out=gw, epi=ops.EPI_F32_ACC)
+    if _fused_tp(tp, w, ad):
+        return tp.fabric.gemm_allreduce(dy, w, b_mn=True)
     if ad is None:
-        return ops.gemm(dy, w, b_mn=True)
+        return _tp_reduce(ops.gemm(dy, w, b_mn=True), tp)
     if ad.GB is not None:
         ad.add_b_grad(ops.gemm(dy, u, a_mn=True, b_mn=True, epi=ops.EPI_F32))
     g = ops.gemm(dy, ad.B, b_mn=True, alpha=ad.scale)
     if ad.GA is not None:
         ops.gemm(g, x, a_mn=True, b_mn=True, out=ad.GA, epi=ops.EPI_F32_ACC)
-    return ops.gemm(dy, w, b_mn=True, a2=g, b2=ad.A)
+    return _tp_reduce(ops.gemm(dy, w, b_mn=True, a2=g, b2=ad.A), tp)
 
 
 def _tp_reduce(t, tp):
@@ -81,8 +99,7 @@ def _dense_mlp_fwd(x2, P, c, save, lora, tp=None):
     h2, rstd2, _ = ops.rmsnorm_fwd(x2, P["post_norm"], c.rms_eps)
     gu, u_gu = _lin(h2, P["gu_w"], lora.get("gu"))
     a = ops.swiglu_fwd(gu)
-    out, u_dn = _lin(a, P["down_w"], lora.get("down"), res=_res(x2, tp))
-    _tp_reduce(out, tp)
+    out, u_dn = _lin_rowpar(a, P["down_w"], lora.get("down"), x2, tp)
     return out, (dict(h2=h2, rstd2=rstd2, gu=gu, a=a, u_gu=u_gu, u_dn=u_dn) if save else None)
 
 
@@ -103,8 +120,7 @@ def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool
     v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
     att, lse = attention_fwd(q, k, v, b.cu_seqlens, b.max_seqlen, True)
     att2 = att.view(T, nq * hd)
-    x2, u_o = _lin(att2, P["o_w"], lora.get("o"), res=_res(x, tp))
-    _tp_reduce(x2, tp)
+    x2, u_o = _lin_rowpar(att2, P["o_w"], lora.get("o"), x, tp)
     if moe is None:
         out, mc = _dense_mlp_fwd(x2, P, cfg, save, lora, tp)
     else:
@@ -128,7 +144,7 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
         da = _lin_bwd(dout, mc["a"], mc["u_dn"], P["down_w"], G.get("down_w"), lora.get("down"))
         dgu = ops.swiglu_bwd(mc["gu"], da)
         del da
-        dh2 = _tp_reduce(_lin_bwd(dgu, mc["h2"], mc["u_gu"], P["gu_w"], G.get("gu_w"), lora.get("gu")), tp)
+        dh2 = _lin_bwd(dgu, mc["h2"], mc["u_gu"], P["gu_w"], G.get("gu_w"), lora.get("gu"), tp)
         del dgu
         dx2 = ops.rmsnorm_bwd(c["x2"], P["post_norm"], mc["rstd2"], dh2, dres=dout, dw=G.get("post_norm"))
         del dh2
@@ -149,7 +165,7 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
                           G.get("q_norm"), G.get("k_norm"), cfg.rms_eps)
     if G.get("qkv_b") is not None:
         G["qkv_b"].add_(dqkv.float().sum(0))
-    dh1 = _tp_reduce(_lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv")), tp)
+    dh1 = _lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv"), tp)
     del dqkv
     dx = ops.rmsnorm_bwd(x, P["in_norm"], c["rstd1"], dh1, dres=dx2, dw=G.get("in_norm"))
     return dx

@@ -98,6 +98,7 @@ class TPContext:
     group: Any
     rank: int
     size: int
+    fabric: Any = None  # parallel.tp_fabric.TPFabric: fused GEMM -> all-reduce over peer memory
 EXPERT_PARAMS = ("exp_gu_w", "exp_down_w")  # sharded by expert under expert parallelism
 
 
@@ -126,6 +127,7 @@ class CausalLM:
         self.cfg = cfg
         self.tp_size, self.tp_rank = tp
         self.tp_group = None  # set by the trainer (NCCL / gloo group of the TP peers)
+        self.tp_fabric = None  # TPFabric of the TP group (attach_tp_fabric)
         self.layer_cfg = tp_local_cfg(cfg, self.tp_size)
         self.flat = flat
         # expert parallelism: this rank's experts [ep_rank*E/ep, (ep_rank+1)*E/ep) live in expert_flat
@@ -176,6 +178,17 @@ class CausalLM:
                     g = layer.G.get(n)
                     if g is not None:
                         dist.all_reduce(g, group=self.tp_group)
+
+    def attach_tp_fabric(self, fabric, capacity: int = 1 << 20):
+        """Row-parallel outputs and column-parallel input gradients summed by
+        the fused GEMM -> all-reduce kernels (parallel.tp_fabric) instead of
+        NCCL; ``fabric`` spans the tensor-parallel group."""
+        from ..parallel.tp_fabric import TPFabric
+
+        if fabric.world != self.tp_size:
+            raise ValueError("the fabric must span the tensor-parallel group")
+        self.tp_fabric = TPFabric(fabric, capacity)
+        return self.tp_fabric
 
     def attach_ep_fabric(self, fabric, capacity_rows: int = 1 << 16):
         """Expert dispatch / combine over peer memory (parallel.ep_fabric) for
@@ -240,7 +253,7 @@ class CausalLM:
             return self._hidden_cpu(input_ids.reshape(-1), batch)
         ids = input_ids.reshape(-1).contiguous()
         x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"))
-        tpc = TPContext(self.tp_group, self.tp_rank, self.tp_size) if self.tp_size > 1 else None
+        tpc = TPContext(self.tp_group, self.tp_rank, self.tp_size, self.tp_fabric) if self.tp_size > 1 else None
         for layer in self.layers:
             layer.batch = batch
             layer.tp = tpc
@@ -333,14 +346,16 @@ class CausalLM:
 def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
                 with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
                 lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None,
-                tp: tuple[int, int] | None = None) -> CausalLM:
+                tp: tuple[int, int] | None = None, ep_fabric=None) -> CausalLM:
     """Build (and random-init) a model.
 
     ``lora``: an object with ``rank``, ``alpha``, ``target_modules``, ``dropout``
     (the ``lora`` config section) -> frozen base + trainable adapters.
     ``load_in_4bit``: NF4-quantise the dense projections after init (QLoRA).
     ``ep``: (ep size, ep rank, expert-dp rank, expert-dp size) for expert
-    parallelism; the expert tensors of this rank go to ``model.expert_flat``.
+    parallelism; the expert tensors of this rank go to ``model.expert_flat``
+    (in peer-visible memory of ``ep_fabric`` when given: policy refresh and
+    the fused dispatch read it from the other ranks).
     """
     device = torch.device(device)
     if dtype is None:
@@ -372,7 +387,8 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                 espec.append(ParamSpec(s_.name, (el,) + tuple(s_.shape[1:]), s_.init, s_.weight_decay, s_.std))
                 rows[s_.name] = (tuple(s_.shape), lo, hi)
         specs = [s_ for s_ in specs if not is_expert_param(s_.name)]
-        expert_flat = FlatParams(espec, device, dtype, ep_dp_rank, ep_dp_world, with_grad, with_optimizer)
+        expert_flat = FlatParams(espec, device, dtype, ep_dp_rank, ep_dp_world, with_grad, with_optimizer,
+                                 alloc=ep_fabric.allocator() if ep_fabric is not None else None)
         if init:
             expert_flat.init_(seed, seed_index=seed_index, row_slices=rows)
     flat = FlatParams([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,

@@ -70,7 +70,20 @@ class IntegratedRunner:
         self.world = t.world
         v = c.inference.vllm
         max_len = v.max_model_len or c.data.seq_len
-        self.engine = Generator(t.model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
+        gen_model = t.model
+        self.policy_sync = None
+        if t.model.expert_flat is not None:
+            # expert-parallel trainer: rollouts run on a full replica refreshed from the shards
+            from ..models.qwen import build_model
+            from ..parallel.policy_sync import ExpertPolicySync
+
+            if getattr(t, "ep_fabric", None) is None:
+                raise NotImplementedError("expert-parallel RL needs CUDA ranks on one node (peer fabric)")
+            gen_model = build_model(t.model.cfg, t.model.device, t.model.flat.compute_dtype, init=False,
+                                    with_grad=False, with_optimizer=False)
+            self.policy_sync = ExpertPolicySync(t.model, gen_model, t.ep_fabric)
+            self.policy_sync.refresh()
+        self.engine = Generator(gen_model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
                                 gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
         self.sender = FileSystemRolloutSender(out, c.transport) if self.world.rank == 0 else None
         # batches past a resumed step are stale
@@ -98,6 +111,8 @@ class IntegratedRunner:
         if ev:
             ev[0].record()
         t0 = time.perf_counter()
+        if self.policy_sync is not None and step > 0:
+            self.policy_sync.refresh()  # the generator replica picks up the last update
         recs = self.orch.materialize(step)
         gen_s = time.perf_counter() - t0
         if ev:
@@ -161,9 +176,14 @@ def main(argv: list[str] | None = None) -> int:
     if cfg.launcher.mode == "integrated":
         from ..parallel.dist import destroy_distributed
 
+        from ..trainer.rl import _close_fabric
+
+        runner = IntegratedRunner(cfg)
         try:
-            return IntegratedRunner(cfg).setup().run()
+            return runner.setup().run()
         finally:
+            if getattr(runner, "trainer", None) is not None:
+                _close_fabric(runner.trainer)
             destroy_distributed()
     from .launcher import run_process_launcher
 

@@ -59,12 +59,24 @@ class RLTrainer:
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if w.device.type == "cuda" else torch.float32
         if model is None:
+            self.ep_fabric = None
+            if dims.ep > 1 and w.device.type == "cuda" and c.fsdp.backend != "gloo":
+                from ..parallel.fabric import Fabric
+
+                self.ep_fabric = Fabric(self.groups.ep_rank, dims.ep, w.device, group=self.groups.ep)
             model = build_model(arch, w.device, dtype, dp_rank=self.dp_rank, dp_world=self.dp_world, seed=c.seed,
+                                ep_fabric=self.ep_fabric,
                                 lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                 ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
                                 if dims.ep > 1 else None,
                                 tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
             model.tp_group = self.groups.tp
+            self.tp_fabric = None
+            if dims.tp > 1 and w.device.type == "cuda" and c.fsdp.backend != "gloo" and c.fsdp.tp_reduce == "fabric":
+                from ..parallel.fabric import Fabric
+
+                self.tp_fabric = Fabric(self.groups.tp_rank, dims.tp, w.device, group=self.groups.tp)
+                model.attach_tp_fabric(self.tp_fabric)
             p = Path(c.model.name)
             if not c.model.random_init and p.is_dir() and any(p.glob("*.safetensors")):
                 from ..models.hf_io import load_hf_weights
@@ -77,6 +89,8 @@ class RLTrainer:
             model.enable_activation_offload()
         if self.groups.ep is not None:
             model.ep_group = self.groups.ep
+            if getattr(self, "ep_fabric", None) is not None and c.fsdp.ep_dispatch == "fabric":
+                model.attach_ep_fabric(self.ep_fabric)
         self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world,
                                        expert_flat=model.expert_flat, ep_dp_group=self.groups.ep_dp,
                                        ep_dp_world=self.groups.ep_dp_size)
@@ -246,6 +260,14 @@ def _lora_meta(cfg, model) -> dict:
             "lora_target_modules": model.lora.target_modules}
 
 
+def _close_fabric(t) -> None:
+    for name in ("ep_fabric", "tp_fabric"):
+        fab = getattr(t, name, None)
+        if fab is not None:
+            fab.close()
+            setattr(t, name, None)
+
+
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     cfg = load_config(RLConfig, argv)
@@ -256,6 +278,7 @@ def main(argv: list[str] | None = None) -> int:
     try:
         return t.run()
     finally:
+        _close_fabric(t)
         destroy_distributed()
 
 

@@ -77,15 +77,29 @@ class SFTTrainer:
             from ..parallel.fabric import maybe_fabric
 
             self.fabric = maybe_fabric(dp_world, dp_rank, dev)
+        self.ep_fabric = None
+        if dev.type == "cuda" and dims.ep > 1 and c.fsdp.backend != "gloo":
+            from ..parallel.fabric import Fabric
+
+            self.ep_fabric = Fabric(self.groups.ep_rank, dims.ep, dev, group=self.groups.ep)
         self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed, fabric=self.fabric,
+                                 ep_fabric=self.ep_fabric,
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                  ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
                                  if dims.ep > 1 else None,
                                  tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
         self.model.tp_group = self.groups.tp
+        self.tp_fabric = None
+        if dims.tp > 1 and dev.type == "cuda" and c.fsdp.backend != "gloo" and c.fsdp.tp_reduce == "fabric":
+            from ..parallel.fabric import Fabric
+
+            self.tp_fabric = Fabric(self.groups.tp_rank, dims.tp, dev, group=self.groups.tp)
+            self.model.attach_tp_fabric(self.tp_fabric)
         if self.groups.ep is not None:
             self.model.ep_group = self.groups.ep
+            if self.ep_fabric is not None and c.fsdp.ep_dispatch == "fabric":
+                self.model.attach_ep_fabric(self.ep_fabric)
         ac = c.model.activation_checkpointing
         self.model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
@@ -277,8 +291,9 @@ def main(argv: list[str] | None = None) -> int:
     try:
         return trainer.train()
     finally:
-        if trainer.fabric is not None:
-            trainer.fabric.close()
+        for fab in (trainer.fabric, trainer.ep_fabric, trainer.tp_fabric):
+            if fab is not None:
+                fab.close()
         destroy_distributed()
 
 
