@@ -52,3 +52,31 @@ def test_attention_matches_reference(cuda_ext, lens, hq, hk):
         err = (got.float() - want).abs().max().item()
         scale = want.abs().max().item()
         assert err <= 3e-2 * scale + 3e-2, (name, err, scale)
+
+
+@pytest.mark.parametrize("lq,lk,hq,hk", [([128, 256], [256, 512], 4, 2), ([300, 64], [428, 448], 8, 2),
+                                         ([128], [128], 2, 2), ([0, 200], [256, 456], 2, 1)])
+def test_attention_separate_keys(cuda_ext, lq, lk, hq, hk):
+    """Separate key sequences (context parallelism): the queries of sequence i
+    are the last lq[i] of its lk[i] keys (offset a multiple of 128); keys that
+    no query sees get zero gradients."""
+    torch.manual_seed(1)
+    Tq, Tk = sum(lq), sum(lk)
+    q = torch.randn(Tq, hq, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(Tk, hk, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(Tk, hk, 128, device="cuda", dtype=torch.bfloat16)
+    cuq = torch.tensor([0] + list(torch.tensor(lq).cumsum(0)), dtype=torch.int32, device="cuda")
+    cuk = torch.tensor([0] + list(torch.tensor(lk).cumsum(0)), dtype=torch.int32, device="cuda")
+    out, lse = attention_fwd(q, k, v, cuq, max(lq), True, None, cuk, max(lk))
+    do = torch.randn(Tq, hq, 128, device="cuda", dtype=torch.bfloat16)
+    dq, dk, dv = attention_bwd(do, q, k, v, out, lse, cuq, max(lq), True, None, cuk, max(lk))
+    torch.cuda.synchronize()
+    assert cuda_ext.read_error(0) == 0
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    ro = ref.attention(qf, kf, vf, cuq.cpu(), True, None, cuk.cpu())
+    ro.backward(do.float())
+    torch.testing.assert_close(out.float(), ro.detach(), rtol=2e-2, atol=2e-2)
+    for got, want, name in ((dq, qf.grad, "dq"), (dk, kf.grad, "dk"), (dv, vf.grad, "dv")):
+        err = (got.float() - want).abs().max().item()
+        scale = want.abs().max().item()
+        assert err <= 3e-2 * scale + 3e-2, (name, err, scale)

@@ -57,4 +57,7 @@ def test_kept_activations_match_recompute(cuda_ext):
         Engine(m, AdamWHyper()).sft_micro_step(b, 1e-3)
         torch.cuda.synchronize()
         grads.append(m.flat.grad.clone())
-    assert torch.equal(grads[0], grads[1]) and torch.equal(grads[0], grads[2])
+    # same kernels on the same activations; only the float-atomic summation
+    # order of the norm-weight / embedding gradients can differ
+    for g in grads[1:]:
+        torch.testing.assert_close(grads[0], g, rtol=1e-4, atol=1e-6)

@@ -67,6 +67,7 @@ struct FwdParams {
   __nv_bfloat16* o;
   float* lse;
   const int* cu;
+  const int* cuk;  // key sequences (nullptr: the query sequences); see AttnArgs::cu_seqlens_k
   int64_t o_row;  // elements between consecutive tokens of o
   int Hq, Hk, T, nseq;
   float scale_log2;
@@ -104,11 +105,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int g = h / (p.Hq / p.Hk);
   const int s0 = p.cu[seq];
   const int L = p.cu[seq + 1] - s0;
+  const int ks0 = p.cuk ? p.cuk[seq] : s0;          // first key row of the sequence
+  const int Lk = p.cuk ? p.cuk[seq + 1] - ks0 : L;
+  const int off = Lk - L;                            // query i sits at key position i + off
   const int n_qt = (L + TILE - 1) / TILE;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest tiles first
   if (qt < 0) return;
   const int q0 = qt * TILE;                       // within the sequence
-  const int kv_end = min(L, q0 + TILE);            // causal: keys < q0 + 128
+  const int kv_end = min(Lk, q0 + off + TILE);     // causal: keys < q0 + off + 128
   const int n_kv = (kv_end + TILE - 1) / TILE;
 
   const int warp = threadIdx.x >> 5;
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         mbar_arrive_expect_tx(&s->kv_full[st], 2 * TILE_BYTES);
-        const int krow = s0 + j * TILE;
+        const int krow = ks0 + j * TILE;
         tma_load_2d(&tmK, &s->kv_full[st], sK[st], g * HD, krow);
         tma_load_2d(&tmK, &s->kv_full[st], sK[st] + SLAB_BYTES, g * HD + 64, krow);
         tma_load_2d(&tmV, &s->kv_full[st], sV[st], g * HD, krow);
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const int k0 = j * TILE;
       if (j == n_kv - 1) {
-        const int lim = min(qi + 1, L) - k0;  // keys [0, lim) valid
+        const int lim = min(qi + off + 1, Lk) - k0;  // keys [0, lim) valid
 #pragma unroll
         for (int e = 0; e < 128; ++e)
           if (e >= lim) sv[e] = -INFINITY;
@@ -354,6 +358,7 @@ struct BwdParams {
   const float* lse;    // [Hq, T]
   const float* delta;  // [Hq, T]
   const int* cu;
+  const int* cuk;      // key sequences (v2 kernels; nullptr: the query sequences)
   __nv_bfloat16* dq;   // [T, Hq, 128]
   __nv_bfloat16* dk;   // [T, Hk, 128]
   __nv_bfloat16* dv;
@@ -839,12 +844,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int g = h / rep;
   const int s0 = p.cu[seq];
   const int L = p.cu[seq + 1] - s0;
-  const int n_kt = (L + TILE - 1) / TILE;
+  const int ks0 = p.cuk ? p.cuk[seq] : s0;
+  const int Lk = p.cuk ? p.cuk[seq + 1] - ks0 : L;
+  const int off = Lk - L;
+  const int n_kt = (Lk + TILE - 1) / TILE;
   const int jt = n_kt - 1 - static_cast<int>(blockIdx.x);  // heaviest (earliest) tiles launch first
   if (jt < 0) return;
   const int k0 = jt * TILE;
-  const int i0 = k0 / QT;                  // first q tile that sees these keys (causal)
-  const int n_it = (L + QT - 1) / QT - i0;
+  const int i0 = max(0, k0 - off) / QT;    // first q tile that sees these keys (causal)
+  const int n_it = max(0, (L + QT - 1) / QT - i0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -875,10 +883,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_expect_tx(&s->a_full, 2 * TILE_BYTES);
-      tma_load_2d(&tmK, &s->a_full, sK, g * HD, s0 + k0);
-      tma_load_2d(&tmK, &s->a_full, sK + SLAB_BYTES, g * HD + 64, s0 + k0);
-      tma_load_2d(&tmV, &s->a_full, sV, g * HD, s0 + k0);
-      tma_load_2d(&tmV, &s->a_full, sV + SLAB_BYTES, g * HD + 64, s0 + k0);
+      tma_load_2d(&tmK, &s->a_full, sK, g * HD, ks0 + k0);
+      tma_load_2d(&tmK, &s->a_full, sK + SLAB_BYTES, g * HD + 64, ks0 + k0);
+      tma_load_2d(&tmV, &s->a_full, sV, g * HD, ks0 + k0);
+      tma_load_2d(&tmV, &s->a_full, sV + SLAB_BYTES, g * HD + 64, ks0 + k0);
       int issued = 0;
       for (int it = 0; it < n_it; ++it) {
         const int st = it & 1;
@@ -975,7 +983,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const int qi = q0 + c;
-        const bool valid = (kj <= qi) && (c < qlim) && (kj < L);
+        const bool valid = (kj <= qi + off) && (c < qlim) && (kj < Lk);
         const float pv = valid ? exp2f(pt[c] - __ldg(lse_row + c) * LOG2E) : 0.f;
         pt[c] = pv;
         dp[c] = pv * (dp[c] - (valid ? __ldg(dlt_row + c) : 0.f));
@@ -1000,12 +1008,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&s->p_full);
     }
+    if (n_it == 0 && kj < Lk) {
+      // keys that no query sees (an empty query sequence): zero gradients
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      if (rep == 1) {
+        uint4* dv4 = reinterpret_cast<uint4*>(p.dv + ((int64_t)(ks0 + kj) * p.Hk + g) * HD);
+        uint4* dk4 = reinterpret_cast<uint4*>(p.dk + ((int64_t)(ks0 + kj) * p.Hk + g) * HD);
+        for (int u = 0; u < 16; ++u) dv4[u] = z, dk4[u] = z;
+      } else {
+        uint4* dv4 = reinterpret_cast<uint4*>(p2.part_dv + ((int64_t)(ks0 + kj) * p.Hq + h) * HD);
+        uint4* dk4 = reinterpret_cast<uint4*>(p2.part_dk + ((int64_t)(ks0 + kj) * p.Hq + h) * HD);
+        for (int u = 0; u < 32; ++u) dv4[u] = z, dk4[u] = z;
+      }
+    }
     if (ok && n_it > 0 && mbar_wait_warp(&s->mma_done, (n_it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
-      const bool valid = kj < L;
+      const bool valid = kj < Lk;
       if (rep == 1) {
-        store_row128(tdV + lane_off, p.dv + ((int64_t)(s0 + kj) * p.Hk + g) * HD, 1.f, valid);
-        store_row128(tdK + lane_off, p.dk + ((int64_t)(s0 + kj) * p.Hk + g) * HD, p.scale, valid);
+        store_row128(tdV + lane_off, p.dv + ((int64_t)(ks0 + kj) * p.Hk + g) * HD, 1.f, valid);
+        store_row128(tdK + lane_off, p.dk + ((int64_t)(ks0 + kj) * p.Hk + g) * HD, p.scale, valid);
       } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -1014,8 +1035,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld_32x32b_x32(tdK + lane_off + c * 32, w);
           tmem_wait_ld();
           if (valid) {
-            float4* dv4 = reinterpret_cast<float4*>(p2.part_dv + ((int64_t)(s0 + kj) * p.Hq + h) * HD + c * 32);
-            float4* dk4 = reinterpret_cast<float4*>(p2.part_dk + ((int64_t)(s0 + kj) * p.Hq + h) * HD + c * 32);
+            float4* dv4 = reinterpret_cast<float4*>(p2.part_dv + ((int64_t)(ks0 + kj) * p.Hq + h) * HD + c * 32);
+            float4* dk4 = reinterpret_cast<float4*>(p2.part_dk + ((int64_t)(ks0 + kj) * p.Hq + h) * HD + c * 32);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               dv4[u] = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]), __uint_as_float(v[4 * u + 2]),
@@ -1109,11 +1130,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int g = h / (p.Hq / p.Hk);
   const int s0 = p.cu[seq];
   const int L = p.cu[seq + 1] - s0;
+  const int ks0 = p.cuk ? p.cuk[seq] : s0;
+  const int Lk = p.cuk ? p.cuk[seq + 1] - ks0 : L;
+  const int off = Lk - L;
   const int n_qt = (L + TILE - 1) / TILE;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
   if (qt < 0) return;
   const int q0 = qt * TILE;
-  const int n_kv = (min(L, q0 + TILE) + KT - 1) / KT;
+  const int n_kv = (min(Lk, q0 + off + TILE) + KT - 1) / KT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -1155,7 +1179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (j >= KV_STAGES && !mbar_wait(&s->kv_empty[st], ((j - KV_STAGES) / KV_STAGES) & 1, abort, p.err, kErrTimeoutProducer)) break;
         uint8_t* kd = sKV + st * 2 * QTILE_BYTES;
         uint8_t* vd = kd + QTILE_BYTES;
-        const int krow = s0 + j * KT;
+        const int krow = ks0 + j * KT;
         mbar_arrive_expect_tx(&s->kv_full[st], 2 * QTILE_BYTES);
         tma_load_2d(&tmK64, &s->kv_full[st], kd, g * HD, krow);
         tma_load_2d(&tmK64, &s->kv_full[st], kd + QSLAB, g * HD + 64, krow);
@@ -1243,7 +1267,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const int kj = kb + c;
-        const bool valid = (kj <= qi) && (kj < L) && vq;
+        const bool valid = (kj <= qi + off) && (kj < Lk) && vq;
         const float pv = valid ? exp2f(pr[c] - lse2) : 0.f;
         pr[c] = pv * (dp[c] - dlt);
       }
@@ -1298,13 +1322,15 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
     attr[dev & 63] = true;
   }
+  const int Tk = a.cu_seqlens_k ? a.Tk : a.T;
   CUtensorMap mq = head_map(a.q, a.q_row, a.Hq, a.T);
-  CUtensorMap mk = head_map(a.k, a.k_row, a.Hk, a.T);
-  CUtensorMap mv = head_map(a.v, a.v_row, a.Hk, a.T);
+  CUtensorMap mk = head_map(a.k, a.k_row, a.Hk, Tk);
+  CUtensorMap mv = head_map(a.v, a.v_row, a.Hk, Tk);
   FwdParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(a.o);
   p.lse = a.lse;
   p.cu = a.cu_seqlens;
+  p.cuk = a.cu_seqlens_k;
   p.o_row = a.o_row;
   p.Hq = a.Hq;
   p.Hk = a.Hk;
@@ -1342,9 +1368,10 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
         reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row, reinterpret_cast<const __nv_bfloat16*>(b.dout),
         b.delta, a.T, a.Hq);
   }
+  const int Tk = a.cu_seqlens_k ? a.Tk : a.T;
   CUtensorMap mq = head_map(a.q, a.q_row, a.Hq, a.T);
-  CUtensorMap mk = head_map(a.k, a.k_row, a.Hk, a.T);
-  CUtensorMap mv = head_map(a.v, a.v_row, a.Hk, a.T);
+  CUtensorMap mk = head_map(a.k, a.k_row, a.Hk, Tk);
+  CUtensorMap mv = head_map(a.v, a.v_row, a.Hk, Tk);
   CUtensorMap mdo = head_map(b.dout, (int64_t)a.Hq * 128, a.Hq, a.T);
   CUtensorMap mq64 = head_map64(a.q, a.q_row, a.Hq, a.T);
   CUtensorMap mdo64 = head_map64(b.dout, (int64_t)a.Hq * 128, a.Hq, a.T);
@@ -1353,6 +1380,7 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   p.lse = a.lse;
   p.delta = b.delta;
   p.cu = a.cu_seqlens;
+  p.cuk = a.cu_seqlens_k;
   p.dq = reinterpret_cast<__nv_bfloat16*>(b.dq);
   p.dk = reinterpret_cast<__nv_bfloat16*>(b.dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(b.dv);
@@ -1365,15 +1393,16 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   p2.part_dk = b.part_dk;
   p2.part_dv = b.part_dv;
   const int nt = (a.max_seqlen + TILE - 1) / TILE;
-  attn_bwd_dkv2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
-  CUtensorMap mk64 = head_map64(a.k, a.k_row, a.Hk, a.T);
-  CUtensorMap mv64 = head_map64(a.v, a.v_row, a.Hk, a.T);
+  const int ntk = ((a.cu_seqlens_k ? a.max_seqlen_k : a.max_seqlen) + TILE - 1) / TILE;
+  attn_bwd_dkv2_kernel<<<dim3(ntk, a.Hq, a.nseq), NUM_THREADS, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
+  CUtensorMap mk64 = head_map64(a.k, a.k_row, a.Hk, Tk);
+  CUtensorMap mv64 = head_map64(a.v, a.v_row, a.Hk, Tk);
   attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p);
   if (rep > 1) {
     const int warps = 8;
-    const int64_t work = (int64_t)a.T * a.Hk;
+    const int64_t work = (int64_t)Tk * a.Hk;
     attn_dkv_reduce_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
-        b.part_dk, b.part_dv, p.dk, p.dv, a.T, a.Hq, a.Hk, a.scale);
+        b.part_dk, b.part_dv, p.dk, p.dv, Tk, a.Hq, a.Hk, a.scale);
   }
 }
 
@@ -1411,10 +1440,12 @@ int attn_bwd_explicit(const AttnBwdArgs& b, int* err, cudaStream_t stream) {
   } catch (const std::exception&) {
     return 4;
   }
+  if (a.cu_seqlens_k) return 6;  // separate key sequences: v2 kernels (attn_bwd) only
   BwdParams p;
   p.lse = a.lse;
   p.delta = b.delta;
   p.cu = a.cu_seqlens;
+  p.cuk = nullptr;
   p.dq = reinterpret_cast<__nv_bfloat16*>(b.dq);
   p.dk = reinterpret_cast<__nv_bfloat16*>(b.dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(b.dv);

@@ -16,6 +16,13 @@ struct AttnArgs {
   const int* cu_seqlens = nullptr;  // device int32 [nseq + 1]
   int nseq = 0, max_seqlen = 0, T = 0, Hq = 0, Hk = 0, head_dim = 128;
   float scale = 0.f;
+  // Optional separate key sequences (context parallelism): k/v are [Tk, Hk,
+  // 128] and sequence i's keys are rows cu_seqlens_k[i] .. cu_seqlens_k[i+1].
+  // Its queries are the LAST Lq positions of those Lk keys (causal mask
+  // aligned bottom-right: query j sees keys <= j + Lk - Lq).  Requires
+  // Lk >= Lq and (Lk - Lq) % 128 == 0 for every sequence.
+  const int* cu_seqlens_k = nullptr;
+  int max_seqlen_k = 0, Tk = 0;
 };
 
 struct AttnBwdArgs {

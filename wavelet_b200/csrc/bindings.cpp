@@ -553,7 +553,8 @@ static int64_t head_row_stride(const at::Tensor& t, const char* name) {
 }
 
 static wb::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
-                              const at::Tensor& cu, int64_t max_seqlen, bool causal, double scale) {
+                              const at::Tensor& cu, int64_t max_seqlen, bool causal, double scale,
+                              const c10::optional<at::Tensor>& cu_k = c10::nullopt, int64_t max_seqlen_k = 0) {
   WB_CHECK(causal, "attention: only causal attention is implemented");
   WB_CHECK(cu.scalar_type() == at::kInt && cu.is_cuda() && cu.is_contiguous(), "attention: cu_seqlens must be int32 CUDA");
   wb::AttnArgs a;
@@ -566,18 +567,28 @@ static wb::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at
   a.T = q.size(0);
   a.Hq = q.size(1);
   a.Hk = k.size(1);
-  WB_CHECK(k.size(0) == a.T && v.size(0) == a.T && v.size(1) == a.Hk, "attention: k/v shape mismatch");
   a.cu_seqlens = cu.data_ptr<int>();
   a.nseq = cu.numel() - 1;
   a.max_seqlen = max_seqlen;
   a.scale = static_cast<float>(scale);
+  if (cu_k) {
+    WB_CHECK(cu_k->scalar_type() == at::kInt && cu_k->is_cuda() && cu_k->is_contiguous() && cu_k->numel() == cu.numel(),
+             "attention: cu_seqlens_k must be int32 CUDA with one entry per cu_seqlens entry");
+    WB_CHECK(v.size(0) == k.size(0) && v.size(1) == a.Hk, "attention: k/v shape mismatch");
+    a.cu_seqlens_k = cu_k->data_ptr<int>();
+    a.max_seqlen_k = max_seqlen_k;
+    a.Tk = k.size(0);
+  } else {
+    WB_CHECK(k.size(0) == a.T && v.size(0) == a.T && v.size(1) == a.Hk, "attention: k/v shape mismatch");
+  }
   return a;
 }
 
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
-              int64_t max_seqlen, bool causal, double scale, at::Tensor& out, at::Tensor& lse) {
+              int64_t max_seqlen, bool causal, double scale, at::Tensor& out, at::Tensor& lse,
+              const c10::optional<at::Tensor>& cu_k, int64_t max_seqlen_k) {
   const c10::cuda::CUDAGuard guard(q.device());
-  wb::AttnArgs a = attn_args(q, k, v, cu, max_seqlen, causal, scale);
+  wb::AttnArgs a = attn_args(q, k, v, cu, max_seqlen, causal, scale, cu_k, max_seqlen_k);
   check_bf16(out, "out");
   WB_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "attention: out must be contiguous [T, Hq, 128]");
   check_f32(lse, "lse");
@@ -591,10 +602,11 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
 
 void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
               const at::Tensor& out, const at::Tensor& lse, const at::Tensor& cu, int64_t max_seqlen, bool causal,
-              double scale, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv) {
+              double scale, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, const c10::optional<at::Tensor>& cu_k,
+              int64_t max_seqlen_k) {
   const c10::cuda::CUDAGuard guard(q.device());
   wb::AttnBwdArgs b;
-  b.f = attn_args(q, k, v, cu, max_seqlen, causal, scale);
+  b.f = attn_args(q, k, v, cu, max_seqlen, causal, scale, cu_k, max_seqlen_k);
   check_bf16(dout, "dout");
   WB_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes(), "attention: dout must be contiguous [T, Hq, 128]");
   WB_CHECK(out.sizes() == q.sizes() && out.stride(2) == 1 && out.stride(1) == 128, "attention: bad out");
@@ -609,9 +621,11 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, 
   at::Tensor delta = at::empty({b.f.Hq, b.f.T}, q.options().dtype(at::kFloat));
   b.delta = delta.data_ptr<float>();
   at::Tensor pdk, pdv;
+  WB_CHECK(dk.sizes() == k.sizes() && dv.sizes() == v.sizes(), "attention: dk/dv must match k/v");
   if (b.f.Hq != b.f.Hk) {
-    pdk = at::empty({b.f.T, b.f.Hq, 128}, q.options().dtype(at::kFloat));
-    pdv = at::empty({b.f.T, b.f.Hq, 128}, q.options().dtype(at::kFloat));
+    const int64_t Tk = k.size(0);
+    pdk = at::empty({Tk, b.f.Hq, 128}, q.options().dtype(at::kFloat));
+    pdv = at::empty({Tk, b.f.Hq, 128}, q.options().dtype(at::kFloat));
     b.part_dk = pdk.data_ptr<float>();
     b.part_dv = pdv.data_ptr<float>();
   }

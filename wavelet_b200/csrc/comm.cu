@@ -124,6 +124,10 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // Each thread owns 8 consecutive floats (two 16-byte loads per rank, all
 // ranks' loads issued before the adds so W*2 requests are in flight).
+constexpr int kMaxSumBlocks = 1024;
+__device__ float g_sum_scratch[2 * kMaxSumBlocks];
+__device__ unsigned g_sum_counter;
+
 template <int W>
 __global__ void __launch_bounds__(512) rs_kernel(PeerPtrs grads, int64_t lo, int64_t n8, float scale, float* out,
                                                  float* stats) {
@@ -157,11 +161,9 @@ __global__ void __launch_bounds__(512) rs_kernel(PeerPtrs grads, int64_t lo, int
     dst[1] = a1;
   }
   ss = block_sum(ss, red);
+  __syncthreads();
   bad = block_sum(bad, red);
-  if (threadIdx.x == 0) {
-    atomicAdd(stats, ss);
-    atomicAdd(stats + 1, bad);
-  }
+  grid_sum2_ordered(ss, bad, g_sum_scratch, &g_sum_counter, stats, red);  // fixed order: reproducible norm
 }
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {

@@ -277,6 +277,47 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Deterministic grid-wide sum of two per-block totals (a, b), added to
+// out[0], out[1].  Every block parks its totals in scratch[2 * block]; the
+// last block to arrive (ticket on *counter) sums the slots in a fixed order
+// (strided per thread, then a shuffle tree) and resets the counter, so the
+// result does not depend on block scheduling.  a and b must be the block's
+// totals in thread 0; scratch holds 2 * gridDim.x floats; red holds 32 floats
+// of shared memory; *counter is 0 between launches.
+__device__ __forceinline__ void grid_sum2_ordered(float a, float b, float* scratch, unsigned* counter, float* out,
+                                                  float* red) {
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    scratch[2 * blockIdx.x] = a;
+    scratch[2 * blockIdx.x + 1] = b;
+    __threadfence();
+    is_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  float s0 = 0.f, s1 = 0.f;
+  for (unsigned i = threadIdx.x; i < gridDim.x; i += blockDim.x) {
+    s0 += __ldcg(scratch + 2 * i);
+    s1 += __ldcg(scratch + 2 * i + 1);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  s0 = warp_sum(s0);
+  s1 = warp_sum(s1);
+  __syncthreads();
+  if (l == 0) red[w] = s0, red[16 + w] = s1;
+  __syncthreads();
+  if (w == 0) {
+    s0 = warp_sum(l < nw ? red[l] : 0.f);
+    s1 = warp_sum(l < nw ? red[16 + l] : 0.f);
+    if (l == 0) {
+      out[0] += s0;
+      out[1] += s1;
+      *counter = 0;
+    }
+  }
+}
+
 }  // namespace wb
 
 // Host side: one device int per GPU that kernels OR their error codes into.

@@ -67,7 +67,14 @@ struct __align__(8) Smem {
   float lut[16];
 };
 
-constexpr size_t smem_bytes() { return 1024 + STAGES * STAGE_BYTES + sizeof(Smem) + 64; }
+// kEpiPeerBF16 stages each epilogue warp's [32 rows x 64 cols] bf16 slice in
+// shared memory (4 KB per warp, after the barrier block) so that peer stores
+// leave as whole 128-byte row segments instead of 16-byte pieces of 32 rows.
+constexpr int PEER_STAGE_BYTES = 4 * 32 * 128;
+constexpr size_t smem_bytes(bool peer = false) {
+  return 1024 + STAGES * STAGE_BYTES + 1024 + (peer ? PEER_STAGE_BYTES : 0);
+}
+static_assert(sizeof(Smem) <= 1024, "barrier block must fit in front of the peer staging area");
 
 struct Params {
   void* C;
@@ -243,6 +250,60 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, int row, int col
           c[j] = w;
         }
       }
+    }
+  }
+}
+
+// kEpiPeerBF16, 64 columns of this warp's 32 rows: pack to bf16, stage in
+// shared memory (16-byte chunks XOR-swizzled by row), read back so that 8
+// lanes hold one row's 128 contiguous bytes, and store every destination's
+// copy as full 128-byte segments.  Partial column blocks use the per-thread
+// path of epilogue_chunk.
+__device__ __forceinline__ void peer_store64(const Params& p, int col0, const uint32_t (&v0)[32],
+                                             const uint32_t (&v1)[32], uint8_t* stg, int lane, int row_base) {
+  const bool full = (col0 + 64 <= p.N) && ((p.ldc & 7) == 0) && ((p.peer_off & 7) == 0);
+  if (!full) {
+    epilogue_chunk<kEpiPeerBF16>(p, row_base + lane, col0, v0, 0);
+    if (col0 + 32 < p.N) epilogue_chunk<kEpiPeerBF16>(p, row_base + lane, col0 + 32, v1, 0);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t* v = (j < 4) ? v0 : v1;
+    const int b = (j & 3) * 8;
+    uint4 w;
+    w.x = pack_bf16(__uint_as_float(v[b + 0]) * p.alpha, __uint_as_float(v[b + 1]) * p.alpha);
+    w.y = pack_bf16(__uint_as_float(v[b + 2]) * p.alpha, __uint_as_float(v[b + 3]) * p.alpha);
+    w.z = pack_bf16(__uint_as_float(v[b + 4]) * p.alpha, __uint_as_float(v[b + 5]) * p.alpha);
+    w.w = pack_bf16(__uint_as_float(v[b + 6]) * p.alpha, __uint_as_float(v[b + 7]) * p.alpha);
+    *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) = w;
+  }
+  __syncwarp();
+  const int ch = lane & 7;
+  uint4 o[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = 4 * it + (lane >> 3);
+    o[it] = *reinterpret_cast<const uint4*>(stg + r * 128 + ((ch ^ (r & 7)) << 4));
+  }
+  __syncwarp();  // the staging slice is rewritten by the next 64 columns
+  const int nd = p.peer_rs_rows > 0 ? 1 : p.peer_world;
+  for (int i = 0; i < nd; ++i) {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int row = row_base + 4 * it + (lane >> 3);
+      if (row >= p.M) continue;
+      int r;
+      int64_t drow = row;
+      if (p.peer_rs_rows > 0) {
+        r = static_cast<int>(row / p.peer_rs_rows);
+        drow = row - (int64_t)r * p.peer_rs_rows;
+      } else {
+        r = p.peer_rank + 1 + i;
+        if (r >= p.peer_world) r -= p.peer_world;
+      }
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.peer[r]) + p.peer_off + drow * p.ldc + col0 + ch * 8;
+      *reinterpret_cast<uint4*>(dst) = o[it];
     }
   }
 }
@@ -518,13 +579,26 @@ __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
       const int tm = ti.tm, tn = ti.tn;
       const int row = tm * BM + q * 32 + lane;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if constexpr (EPI == kEpiPeerBF16) {
+        uint8_t* stg = tiles + STAGES * STAGE_BYTES + 1024 + q * 4096;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        if (tn * BN + c >= p.N) break;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_addr + c, v);
-        tmem_wait_ld();
-        epilogue_chunk<EPI>(p, row, tn * BN + c, v, ti.c_row_off);
+        for (int c = 0; c < BN; c += 64) {
+          if (tn * BN + c >= p.N) break;
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(t_addr + c, v0);
+          tmem_ld_32x32b_x32(t_addr + c + 32, v1);
+          tmem_wait_ld();
+          peer_store64(p, tn * BN + c, v0, v1, stg, lane, tm * BM + q * 32);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          if (tn * BN + c >= p.N) break;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_addr + c, v);
+          tmem_wait_ld();
+          epilogue_chunk<EPI>(p, row, tn * BN + c, v, ti.c_row_off);
+        }
       }
       tc_fence_before();
       mbar_arrive(&s->tmem_empty[acc]);
@@ -546,8 +620,9 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
+  constexpr size_t smem = smem_bytes(EPI == kEpiPeerBF16);
   if (!attr_set[dev & 63]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set[dev & 63] = true;
   }
   // A(m,k): K-major -> rows of K; MN-major -> rows of M.
@@ -608,7 +683,7 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   p.peer_rs_rows = g.peer_rs_rows;
   const int tiles = p.num_m * p.num_n * (GROUP == 2 ? g.groups : 1);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem_bytes(), stream>>>(ta, tb, ta2, tb2, p);
+  kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem, stream>>>(ta, tb, ta2, tb2, p);
 }
 
 }  // namespace gemm

@@ -438,8 +438,14 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
-// Sum of squares of a flat fp32 buffer into out[0] (atomic), non-finite count
-// into out[1].
+// Cross-block scratch of the deterministic grid sums (one launch at a time per
+// device: the optimizer's reductions run in stream order).
+constexpr int kMaxSumBlocks = 1024;
+__device__ float g_sum_scratch[2 * kMaxSumBlocks];
+__device__ unsigned g_sum_counter;
+
+// Sum of squares of a flat fp32 buffer added to out[0] and the non-finite
+// count to out[1], in a fixed order (bit-reproducible).
 __global__ void sumsq_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
   __shared__ float red[32];
   float s = 0.f, bad = 0.f;
@@ -458,10 +464,7 @@ __global__ void sumsq_kernel(const float* __restrict__ x, int64_t n, float* __re
   s = block_sum(s, red);
   __syncthreads();
   bad = block_sum(bad, red);
-  if (threadIdx.x == 0) {
-    atomicAdd(&out[0], s);
-    atomicAdd(&out[1], bad);
-  }
+  grid_sum2_ordered(s, bad, g_sum_scratch, &g_sum_counter, out, red);
 }
 
 // clip factor = min(1, max_norm / (sqrt(sumsq) + 1e-6)); written to out.
@@ -784,6 +787,7 @@ void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t
 
 void sumsq(const float* x, int64_t n, float* out, cudaStream_t st) {
   if (n <= 0) return;
+  static_assert(148 * 4 <= kMaxSumBlocks, "sumsq grid exceeds the scratch");
   sumsq_kernel<<<grid_for((n + 3) / 4, 256, 148 * 4), 256, 0, st>>>(x, n, out);
 }
 

@@ -27,6 +27,8 @@ import torch
 
 from .. import ops
 from ..ops.attention import attention_bwd, attention_fwd
+from ..parallel.context_parallel import attention_bwd as cp_attention_bwd
+from ..parallel.context_parallel import attention_fwd as cp_attention_fwd
 from .config import ArchConfig
 
 
@@ -38,6 +40,7 @@ class BatchCtx:
     cu_seqlens: torch.Tensor  # int32 [n+1]
     max_seqlen: int
     inv_freq: torch.Tensor  # fp32 [head_dim/2]
+    cp: Any = None  # parallel.context_parallel.CPPlan: attention over the CP group's full sequences
 
 
 def _lin(x, w, ad, bias=None, res=None):
@@ -118,7 +121,10 @@ def layer_fwd(x: torch.Tensor, P: dict, cfg: ArchConfig, b: BatchCtx, save: bool
     q = qkv[:, : nq * hd].view(T, nq, hd)
     k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
     v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
-    att, lse = attention_fwd(q, k, v, b.cu_seqlens, b.max_seqlen, True)
+    if b.cp is not None:
+        att, lse = cp_attention_fwd(q, k, v, b.cp)
+    else:
+        att, lse = attention_fwd(q, k, v, b.cu_seqlens, b.max_seqlen, True)
     att2 = att.view(T, nq * hd)
     x2, u_o = _lin_rowpar(att2, P["o_w"], lora.get("o"), x, tp)
     if moe is None:
@@ -156,7 +162,11 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
     q = qkv[:, : nq * hd].view(T, nq, hd)
     k = qkv[:, nq * hd : (nq + nk) * hd].view(T, nk, hd)
     v = qkv[:, (nq + nk) * hd :].view(T, nk, hd)
-    dq, dk, dv = attention_bwd(datt.view(T, nq, hd), q, k, v, c["att"], c["lse"], b.cu_seqlens, b.max_seqlen, True)
+    if b.cp is not None:
+        dq, dk, dv = cp_attention_bwd(datt.view(T, nq, hd), q, k, v, c["att"], c["lse"], b.cp)
+    else:
+        dq, dk, dv = attention_bwd(datt.view(T, nq, hd), q, k, v, c["att"], c["lse"], b.cu_seqlens, b.max_seqlen,
+                                   True)
     del datt
     dqkv = torch.cat([dq.reshape(T, -1), dk.reshape(T, -1), dv.reshape(T, -1)], 1)
     del dq, dk, dv

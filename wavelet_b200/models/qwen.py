@@ -236,18 +236,20 @@ class CausalLM:
         return self.flat.grad_view(self.head_name)
 
     # ----------------------------------------------------------- batches
-    def batch_ctx(self, position_ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> BatchCtx:
+    def batch_ctx(self, position_ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,
+                  cp=None) -> BatchCtx:
         return BatchCtx(
             pos=position_ids.to(device=self.device, dtype=torch.int32).reshape(-1).contiguous(),
             cu_seqlens=cu_seqlens.to(device=self.device, dtype=torch.int32).contiguous(),
             max_seqlen=int(max_seqlen),
             inv_freq=self.inv_freq,
+            cp=cp,
         )
 
     # ----------------------------------------------------------- forward
     def hidden(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
         """Final normalised hidden states [T, H] (autograd-connected)."""
-        if not input_ids.is_cuda and not self.fused_cpu and self.tp_size == 1:
+        if not input_ids.is_cuda and not self.fused_cpu and self.tp_size == 1 and batch.cp is None:
             if self.expert_flat is not None:
                 raise NotImplementedError("the CPU reference path runs without expert parallelism")
             return self._hidden_cpu(input_ids.reshape(-1), batch)

@@ -41,28 +41,33 @@ def swiglu(gu: torch.Tensor) -> torch.Tensor:
     return (F.silu(g.float()) * u.float()).to(gu.dtype)
 
 
-def attention(q, k, v, cu_seqlens: torch.Tensor, causal: bool = True, scale: float | None = None):
+def attention(q, k, v, cu_seqlens: torch.Tensor, causal: bool = True, scale: float | None = None,
+              cu_seqlens_k: torch.Tensor | None = None):
     """Packed variable-length attention.
 
     q: [T, hq, d], k/v: [T, hk, d]; cu_seqlens: int32 [n+1] sequence
-    boundaries.  GQA by head repetition.  Returns [T, hq, d].
+    boundaries.  GQA by head repetition.  Returns [T, hq, d].  With
+    ``cu_seqlens_k`` the keys of sequence i are k[cu_seqlens_k[i]:
+    cu_seqlens_k[i+1]] and its queries are the last positions of that key
+    sequence (causal mask aligned bottom-right).
     """
     T, hq, d = q.shape
     hk = k.shape[1]
     scale = scale if scale is not None else 1.0 / math.sqrt(d)
-    out = torch.empty_like(q)
+    out = torch.zeros_like(q)
     bounds = cu_seqlens.tolist()
+    kb = cu_seqlens_k.tolist() if cu_seqlens_k is not None else bounds
     rep = hq // hk
-    for s, e in zip(bounds[:-1], bounds[1:]):
+    for s, e, ks0, ke in zip(bounds[:-1], bounds[1:], kb[:-1], kb[1:]):
         if e <= s:
             continue
         qs = q[s:e].transpose(0, 1).float()
-        ks = k[s:e].transpose(0, 1).float().repeat_interleave(rep, 0)
-        vs = v[s:e].transpose(0, 1).float().repeat_interleave(rep, 0)
+        ks = k[ks0:ke].transpose(0, 1).float().repeat_interleave(rep, 0)
+        vs = v[ks0:ke].transpose(0, 1).float().repeat_interleave(rep, 0)
         att = (qs @ ks.transpose(-1, -2)) * scale
         if causal:
-            L = e - s
-            mask = torch.ones(L, L, dtype=torch.bool, device=q.device).tril()
+            Lq, Lk = e - s, ke - ks0
+            mask = torch.ones(Lq, Lk, dtype=torch.bool, device=q.device).tril(Lk - Lq)
             att = att.masked_fill(~mask, float("-inf"))
         p = att.softmax(-1)
         out[s:e] = (p @ vs).transpose(0, 1).to(q.dtype)

@@ -138,6 +138,13 @@ class Groups:
         self.dp_size = dims.dp
         self.tp_rank = 0
         self.ep_rank = 0
+        self.cp_rank = 0
+        self.cp_size = dims.cp
+        # dp x cp: the ranks that hold the same parameters (gradients and
+        # optimizer shards reduce over them; the reference's dp_cp mesh)
+        self.dp_cp = None
+        self.dp_cp_rank = 0
+        self.dp_cp_size = dims.dp * dims.cp
         if not dist.is_initialized() or dims.world_size == 1:
             return
         W = dims.world_size
@@ -156,6 +163,29 @@ class Groups:
             g = dist.new_group(ranks) if dims.tp > 1 else None
             if rank in ranks:
                 self.tp = g
+        self.cp_rank = c["cp"]
+        if dims.cp > 1:
+            # context-parallel groups: same data-parallel coordinates and tp
+            seen = set()
+            for r0 in range(W):
+                c0 = dims.coords(r0)
+                key = (c0["dp_replicate"], c0["dp_shard"], c0["tp"])
+                if key in seen:
+                    continue
+                seen.add(key)
+                ranks = [r for r in range(W) if (dims.coords(r)["dp_replicate"], dims.coords(r)["dp_shard"],
+                                                 dims.coords(r)["tp"]) == key]
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    self.cp = g
+            for tp in range(dims.tp):
+                ranks = [r for r in range(W) if dims.coords(r)["tp"] == tp]
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    self.dp_cp = g
+                    self.dp_cp_rank = ranks.index(rank)
+        else:
+            self.dp_cp, self.dp_cp_rank = self.dp, self.dp_rank
         if dims.ep > 1:
             # contiguous blocks of ep ranks among the dp_shard x cp ranks
             for base in range(0, W, dims.ep):

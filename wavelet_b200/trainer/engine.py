@@ -8,6 +8,7 @@ and per-token loss weights.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Any
 
 import torch
 import torch.distributed as dist
@@ -25,6 +26,7 @@ class PackedBatch:
     max_seqlen: int
     targets: torch.Tensor  # int64 [T], -100 = ignore
     loss_mask: torch.Tensor  # float [T]
+    cp: Any = None  # parallel.context_parallel.CPPlan of a context-parallel shard
 
     def to(self, device, non_blocking=True) -> "PackedBatch":
         return PackedBatch(
@@ -34,6 +36,7 @@ class PackedBatch:
             self.max_seqlen,
             self.targets.to(device, non_blocking=non_blocking),
             self.loss_mask.to(device, non_blocking=non_blocking),
+            None if self.cp is None else self.cp.to(device),
         )
 
     @property
@@ -43,7 +46,7 @@ class PackedBatch:
     def pin_memory(self) -> "PackedBatch":
         return PackedBatch(
             self.input_ids.pin_memory(), self.position_ids.pin_memory(), self.cu_seqlens.pin_memory(),
-            self.max_seqlen, self.targets.pin_memory(), self.loss_mask.pin_memory(),
+            self.max_seqlen, self.targets.pin_memory(), self.loss_mask.pin_memory(), self.cp,
         )
 
     def nbytes(self) -> int:
@@ -81,7 +84,7 @@ class Engine:
         Returns the (scaled) loss contribution as a device scalar.
         """
         m = self.model
-        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen)
+        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
         h = m.hidden(b.input_ids, ctx)
         weights = b.loss_mask.float() * token_scale
         loss, dh = lm_head.sft_loss_and_grad(h.detach(), m.head_weight(), b.targets, weights, m.head_grad(), self.chunk)
@@ -94,7 +97,7 @@ class Engine:
     def sft_eval(self, b: PackedBatch) -> tuple[torch.Tensor, float]:
         """Forward-only masked CE sum and loss-token count of one micro-batch."""
         m = self.model
-        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen)
+        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
         h = m.hidden(b.input_ids, ctx)
         valid = (b.targets >= 0).float() * b.loss_mask.float()
         lp, _ = lm_head.logprob_entropy(h.detach(), m.head_weight(), b.targets.clamp_min(0), 1.0,

@@ -54,6 +54,10 @@ class RLTrainer:
         w = self.world
         dims = ParallelDims(dp_replicate=c.fsdp.dp_replicate, dp_shard=c.fsdp.dp_shard, cp=c.fsdp.cp, tp=c.fsdp.tp,
                             ep=c.fsdp.ep, world_size=w.world_size)
+        if dims.cp > 1:
+            # rollout batches are packed varlen sequences with per-sequence
+            # normalisations; context parallelism shards SFT micro-batches
+            raise NotImplementedError("fsdp.cp > 1 is supported by the SFT trainer; RL trains with cp = 1")
         self.groups = Groups(dims, w.rank)
         self.dp_rank, self.dp_world = self.groups.dp_rank, dims.dp
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)

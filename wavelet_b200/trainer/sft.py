@@ -65,10 +65,12 @@ class SFTTrainer:
         w = self.world
         dims = ParallelDims(dp_replicate=c.fsdp.dp_replicate, dp_shard=c.fsdp.dp_shard, cp=c.fsdp.cp, tp=c.fsdp.tp,
                             ep=c.fsdp.ep, world_size=w.world_size)
-        if dims.cp > 1:
-            raise NotImplementedError("context parallel SFT is not wired into the SFT trainer yet")
         self.groups = Groups(dims, w.rank)
         dp_rank, dp_world = self.groups.dp_rank, dims.dp
+        # parameters are replicated over dp x cp: their shards and gradient
+        # reductions use that group (data is split over dp only)
+        self.cp = dims.cp
+        opt_group, opt_rank, opt_world = self.groups.dp_cp, self.groups.dp_cp_rank, self.groups.dp_cp_size
         dev = w.device
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
@@ -82,7 +84,7 @@ class SFTTrainer:
             from ..parallel.fabric import Fabric
 
             self.ep_fabric = Fabric(self.groups.ep_rank, dims.ep, dev, group=self.groups.ep)
-        self.model = build_model(arch, dev, dtype, dp_rank=dp_rank, dp_world=dp_world, seed=c.seed, fabric=self.fabric,
+        self.model = build_model(arch, dev, dtype, dp_rank=opt_rank, dp_world=opt_world, seed=c.seed, fabric=self.fabric,
                                  ep_fabric=self.ep_fabric,
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
@@ -108,10 +110,10 @@ class SFTTrainer:
             from ..models.hf_io import load_hf_weights
 
             load_hf_weights(self.model, Path(c.model.name))
-        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, self.groups.dp, dp_world,
+        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, opt_group, opt_world,
                                        fabric=self.fabric, expert_flat=self.model.expert_flat,
                                        ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size)
-        self.engine = Engine(self.model, self.optimizer.adamw.h, self.groups.dp, dp_world)
+        self.engine = Engine(self.model, self.optimizer.adamw.h, opt_group, opt_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
         from ..data.tokenizer import load_tokenizer
@@ -169,16 +171,25 @@ class SFTTrainer:
         return self
 
     # ------------------------------------------------------------ validation
+    def _shard(self, b):
+        """This rank's context-parallel share of a host micro-batch."""
+        if self.cp == 1:
+            return b
+        from ..parallel.context_parallel import shard_batch
+
+        align = 128 if self.world.device.type == "cuda" else 8
+        return shard_batch(b, self.cp, self.groups.cp_rank, self.groups.cp, align=align)
+
     def validate(self) -> dict[str, float]:
         """Token-mean masked CE over one pass of the validation set (all ranks)."""
         dev = self.world.device
         tot = torch.zeros(2, dtype=torch.float64, device=dev)
         for b in self.val_dataset.eval_batches():
-            loss, n = self.engine.sft_eval(b.to(dev))
+            loss, n = self.engine.sft_eval(self._shard(b).to(dev))
             tot[0] += loss.double()
             tot[1] += n
         if self.world.distributed:
-            torch.distributed.all_reduce(tot, group=self.groups.dp)
+            torch.distributed.all_reduce(tot, group=self.groups.dp_cp)
         loss_v, n_v = tot.tolist()
         return {"val/loss": loss_v / max(n_v, 1.0), "val/tokens": n_v}
 
@@ -186,7 +197,7 @@ class SFTTrainer:
     def train_step(self) -> dict[str, Any]:
         c = self.config
         t0 = time.perf_counter()
-        batches = [self.dataset.next_micro_batch() for _ in range(self.accum)]
+        batches = [self._shard(self.dataset.next_micro_batch()) for _ in range(self.accum)]
         local = float(sum(float(b.loss_mask.sum()) for b in batches))
         total = self.engine.global_token_count(local, self.world.device)
         scale = 1.0 / max(total, 1.0)
@@ -203,14 +214,14 @@ class SFTTrainer:
         self.model.finalize_grads()
         stats = self.optimizer.step(lr)
         if self.world.distributed:
-            torch.distributed.all_reduce(loss, group=self.groups.dp)
+            torch.distributed.all_reduce(loss, group=self.groups.dp_cp)
         loss_v = float(loss.item())
         if not (loss_v == loss_v) or loss_v in (float("inf"), float("-inf")):
             raise FloatingPointError(f"non-finite SFT loss at step {self.step}")
         self.step += 1
         dt = time.perf_counter() - t0
         m = {"loss": loss_v, "optim/grad_norm": stats["grad_norm"], "optim/lr": lr, "train/loss_tokens": total}
-        m.update(self.perf.step_metrics(tokens * (self.world.world_size // max(1, self.config.fsdp.tp)), dt))
+        m.update(self.perf.step_metrics(tokens * (self.world.world_size // max(1, self.config.fsdp.tp * self.cp)), dt))
         m["_tokens"], m["_seconds"] = float(tokens), dt
         return m
 
