@@ -823,7 +823,7 @@ class RLInferenceConfig(ConfigModel):
 
 
 class RLRewardConfig(ConfigModel):
-    mode: Literal["passthrough", "reference_match", "math_format", "reverse_match"] = "passthrough"
+    mode: Literal["passthrough", "reference_match", "math_format", "reverse_match", "environment"] = "passthrough"
     normalize_whitespace: bool = True
     case_sensitive: bool = True
     reasoning_end: str = "<end_working_out>"

@@ -6,7 +6,11 @@ Built-in environments (no network, no external verifier package):
   ``vocab``, ``seed``), reward = fraction of generated tokens matching the
   reversed prompt;
 * ``file:<path>`` — prompt rows from a local JSONL/Parquet file scored by the
-  configured reward (``reference_match`` / ``math_format`` against ``answer``).
+  configured reward (``reference_match`` / ``math_format`` against ``answer``);
+* the native environments of ``wavelet_b200.environments``
+  (``equation_builder``, ``polaris_math_tagged``; ``args`` are their
+  ``load_environment`` arguments), scored by their own reward on the
+  evaluation split.
 
 For every example ``rollouts_per_example`` samples are drawn; the metrics are
 the mean reward, pass@1 and pass@k (unbiased estimator of Chen et al. 2021,
@@ -36,6 +40,12 @@ def pass_at_k(n: int, c: int, k: int) -> float:
     return 1.0 - math.prod(1.0 - k / i for i in range(n - c + 1, n + 1))
 
 
+def _native(env_id: str) -> bool:
+    from .. import environments
+
+    return environments.is_native(env_id)
+
+
 def _env_prompts(cfg, env):
     a = env.args or {}
     if env.id.startswith("file:"):
@@ -46,7 +56,18 @@ def _env_prompts(cfg, env):
     if env.resolved_name in ("reverse", "reverse_match", "synthetic-reverse"):
         vocab = int(a.get("vocab", cfg.data.fake_vocab_size))
         return SyntheticReversePrompts(vocab, int(a.get("prompt_len", cfg.data.fake_prompt_len)), seed=int(a.get("seed", 12345)))
-    raise ValueError(f"unknown eval environment {env.id!r} (built-ins: reverse, file:<path>)")
+    from .. import environments
+
+    if environments.is_native(env.id):
+        from .reward import register_environment
+        from .sources import EnvironmentPromptSource
+
+        e = environments.load_environment(env.id, **{k: v for k, v in a.items() if k not in ("success_threshold",)})
+        register_environment(e)
+        return EnvironmentPromptSource([(e, 1.0)], cfg.model.name, seed=int(a.get("seed", 0)),
+                                       split="eval" if e.eval_examples else "train")
+    raise ValueError(f"unknown eval environment {env.id!r} (built-ins: reverse, file:<path>, "
+                     f"{', '.join(environments.available())})")
 
 
 def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]:
@@ -55,6 +76,8 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
     reward_cfg = cfg.reward
     if env.resolved_name in ("reverse", "reverse_match", "synthetic-reverse"):
         reward_cfg = cfg.reward.model_copy(update={"mode": "reverse_match"})
+    elif _native(env.id):
+        reward_cfg = cfg.reward.model_copy(update={"mode": "environment"})
     ecfg = cfg.model_copy(update={"reward": reward_cfg,
                                   "orchestrator": cfg.orchestrator.model_copy(update={"rollouts_per_example": k})})
     s = env.sampling

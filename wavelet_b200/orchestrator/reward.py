@@ -9,7 +9,11 @@ Modes:
   textually, with a small format bonus;
 * ``reverse_match`` — the synthetic verifiable reward of the GRPO benchmark:
   the fraction of generated tokens equal to the reversed prompt tokens
-  (position-wise), computed on token ids.
+  (position-wise), computed on token ids;
+* ``environment`` — the reward function of the native environment named in
+  the rollout's metadata (``wavelet_b200.environments``).  Rollouts from an
+  environment are scored by it under ``passthrough`` too when they carry no
+  reward of their own.
 
 Post-processing: optional rescale to [0, 1] from [rescale_min, rescale_max],
 then clamp.
@@ -40,12 +44,29 @@ def reverse_match_score(prompt_ids: list[int], completion_ids: list[int]) -> flo
     return hits / len(completion_ids)
 
 
+# environments built with non-default arguments, registered by the prompt
+# source's owner so that scoring uses the same instance (name -> Environment)
+_ENV_OVERRIDE: dict = {}
+
+
+def register_environment(env) -> None:
+    _ENV_OVERRIDE[env.name] = env
+
+
 class RLRewardScorer:
     def __init__(self, cfg):
         self.cfg = cfg
 
     def score(self, r: RLExample) -> float:
         c = self.cfg
+        md = r.metadata or {}
+        if md.get("env") and (c.mode == "environment" or (c.mode == "passthrough" and r.reward is None)):
+            from .. import environments
+
+            env = _ENV_OVERRIDE.get(md["env"]) or environments.load_environment(md["env"])
+            return self._post(float(env.reward(assistant_text(r.completion), md.get("env_row") or {})))
+        if c.mode == "environment":
+            raise ValueError("reward.mode='environment' needs rollouts from a native environment (metadata.env)")
         if c.mode == "passthrough":
             if r.reward is None:
                 raise ValueError("reward.mode='passthrough' requires each rollout row to provide a reward.")

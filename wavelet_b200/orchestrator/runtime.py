@@ -41,11 +41,37 @@ def build_prompt_source(cfg: RLConfig, vocab: int, rank: int = 0):
     """Prompt source for the orchestrator: synthetic reverse-text prompts
     (``data.source: fake``) or pretokenised prompt rows from local files."""
     d = cfg.data
+    envs = native_train_envs(cfg)
+    if envs:
+        from .sources import EnvironmentPromptSource
+
+        return EnvironmentPromptSource(envs, cfg.model.name, seed=d.seed, rank=rank)
     if d.source == "fake":
         return SyntheticReversePrompts(min(vocab, d.fake_vocab_size), d.fake_prompt_len, seed=d.seed * 1000 + rank)
     from .sources import FilePromptSource
 
     return FilePromptSource(cfg, rank=rank)
+
+
+def native_train_envs(cfg: RLConfig) -> list:
+    """(Environment, ratio) of every training environment that is a native
+    one (``orchestrator.envs`` / ``orchestrator.verifier_env_id``)."""
+    from .. import environments
+    from .reward import register_environment
+
+    o = cfg.orchestrator
+    specs = [(e.id, e.args, e.ratio) for e in o.envs]
+    if not specs and o.verifier_env_id:
+        specs = [(o.verifier_env_id, o.verifier_env_args, 1.0)]
+    out = []
+    for env_id, args, ratio in specs:
+        if not environments.is_native(env_id):
+            raise ValueError(f"environment {env_id!r} needs the verifiers package, which is not installed; "
+                             f"native environments: {', '.join(environments.available())}")
+        env = environments.load_environment(env_id, **(args or {}))
+        register_environment(env)
+        out.append((env, float(ratio)))
+    return out
 
 
 class IntegratedRunner:

@@ -110,3 +110,79 @@ class FilePromptSource:
 
     def load_state_dict(self, sd: dict) -> None:
         self.epoch, self.cursor = int(sd["epoch"]), int(sd["cursor"])
+
+
+class EnvironmentPromptSource:
+    """Chat prompts from native environments (``wavelet_b200.environments``),
+    mixed by ``ratio`` (orchestrator.envs): each draw picks the environment
+    whose share of the prompts handed out so far is furthest below its ratio
+    (deterministic weighted round robin), then that environment's next row in
+    a seeded per-epoch shuffle.  The rollout metadata names the environment
+    and carries the row, so the reward scorer can call the environment's
+    reward."""
+
+    def __init__(self, envs: list[tuple[Any, float]], model_name: str, seed: int = 0, rank: int = 0, world: int = 1,
+                 tokenizer=None, split: str = "train"):
+        if not envs:
+            raise ValueError("EnvironmentPromptSource needs at least one environment")
+        self.envs = envs
+        self.model_name = model_name
+        self.tok = tokenizer
+        self.seed, self.rank, self.world = seed, rank, world
+        self.split = split
+        self.drawn = [0] * len(envs)
+        self.cursor = [0] * len(envs)
+        self.epoch = [0] * len(envs)
+
+    def _rows(self, i: int) -> list[dict[str, Any]]:
+        env = self.envs[i][0]
+        return env.examples if self.split == "train" else env.eval_examples
+
+    def _order(self, i: int) -> list[int]:
+        idx = list(range(len(self._rows(i))))
+        random.Random((self.seed * 7919 + self.epoch[i]) * 31 + i).shuffle(idx)
+        return idx[self.rank :: self.world] or idx
+
+    def _tokenizer(self):
+        if self.tok is None:
+            from ..data.tokenizer import load_tokenizer
+
+            self.tok = load_tokenizer(self.model_name)
+        return self.tok
+
+    def _pick(self) -> int:
+        total = sum(self.drawn) + 1
+        wsum = sum(w for _, w in self.envs)
+        deficit = [w / wsum * total - d for (_, w), d in zip(self.envs, self.drawn)]
+        return max(range(len(self.envs)), key=lambda i: (deficit[i], -i))
+
+    def take(self, n: int) -> list[PromptRecord]:
+        out = []
+        for _ in range(n):
+            i = self._pick()
+            order = self._order(i)
+            if self.cursor[i] >= len(order):
+                self.epoch[i] += 1
+                self.cursor[i] = 0
+                order = self._order(i)
+            row = self._rows(i)[order[self.cursor[i]]]
+            self.cursor[i] += 1
+            self.drawn[i] += 1
+            env = self.envs[i][0]
+            prompt = env.chat(row)
+            tok = self._tokenizer()
+            if hasattr(tok, "apply_chat_template"):
+                ids = tok.apply_chat_template(prompt, tokenize=True, add_generation_prompt=True)
+            else:
+                ids = tok.encode("\n".join(m["content"] for m in prompt))
+            target = [{"role": "assistant", "content": str(row["answer"])}] if row.get("answer") is not None else None
+            md = {"env": env.name, "env_row": row, "task": row.get("task", env.name), "source": env.name}
+            out.append(PromptRecord(list(map(int, ids)), prompt, target, md,
+                                    str(row.get("example_id", f"{env.name}-{self.drawn[i]}"))))
+        return out
+
+    def state_dict(self) -> dict:
+        return {"drawn": list(self.drawn), "cursor": list(self.cursor), "epoch": list(self.epoch)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.drawn, self.cursor, self.epoch = list(sd["drawn"]), list(sd["cursor"]), list(sd["epoch"])
