@@ -400,6 +400,28 @@ __device__ __forceinline__ void store_row128(uint32_t taddr, __nv_bfloat16* dst,
   }
 }
 
+// Columns [0, 64) of a TMEM accumulator row (from taddr) -> 64 bf16 at dst.
+__device__ __forceinline__ void store_row64(uint32_t taddr, __nv_bfloat16* dst, float mul, bool valid) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, v);
+    tmem_wait_ld();
+    if (valid) {
+      uint4* d = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 w;
+        w.x = pack_bf16(__uint_as_float(v[8 * u + 0]) * mul, __uint_as_float(v[8 * u + 1]) * mul);
+        w.y = pack_bf16(__uint_as_float(v[8 * u + 2]) * mul, __uint_as_float(v[8 * u + 3]) * mul);
+        w.z = pack_bf16(__uint_as_float(v[8 * u + 4]) * mul, __uint_as_float(v[8 * u + 5]) * mul);
+        w.w = pack_bf16(__uint_as_float(v[8 * u + 6]) * mul, __uint_as_float(v[8 * u + 7]) * mul);
+        d[u] = w;
+      }
+    }
+  }
+}
+
 struct __align__(8) BwdSmem {
   uint64_t a_full;      // loaded-once operands
   uint64_t b_full[2];   // per-iteration operands
@@ -786,6 +808,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   P^T = exp2(S^T*sl2 - lse2[q]),  dS^T = P^T (dP^T - delta[q])
 //   dV += P^T dO, dK += dS^T Q         (M=128 keys, N=128 dims, K=64 queries)
 constexpr int QT = 64;
+// v2 backward kernels: warp 0 TMA, warp 1 MMA, warps 2..9 softmax.  Two
+// softmax warps share each TMEM lane quadrant (warp & 3) and split the 64
+// columns of a tile (half = (warp - 2) / 4 takes columns 32*half..+31), so each
+// SM sub-partition runs two independent exp/ALU streams.
+constexpr int NUM_THREADS_BWD2 = 64 + 256;
+constexpr int BWD2_SOFTMAX_THREADS = 256;
 constexpr int QSLAB = QT * 64 * 2;          // [64 rows x 64 cols] bf16 = 8 KB
 constexpr int QTILE_BYTES = 2 * QSLAB;      // [64 x 128] = 16 KB
 constexpr int PT_BYTES = TILE * QT * 2;     // [128 keys x 64 q] = 16 KB
@@ -823,7 +851,7 @@ constexpr size_t dkv2_smem_bytes() {
   return 1024 + 2 * TILE_BYTES + 4 * QTILE_BYTES + 2 * PT_BYTES + sizeof(Bwd2Smem) + 64;
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS_BWD2, 1)
     attn_bwd_dkv2_kernel(const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO64,
                          Bwd2Params p2) {
@@ -862,7 +890,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&s->b_empty[i], 1);
       mbar_init(&s->s_full[i], 1);
     }
-    mbar_init(&s->p_full, 128);
+    mbar_init(&s->p_full, BWD2_SOFTMAX_THREADS);
     mbar_init(&s->mma_done, 1);
     mbar_init(&s->drain, 1);
     s->abort = 0;
@@ -958,6 +986,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int r = q * 32 + lane;  // key row
     const int kj = k0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int half = (warp - 2) >> 2;
+    const int cb = half * 32;  // this warp's 32 query columns of the tile
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int st = it & 1;
@@ -967,42 +997,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int qlim = L - q0;
       if (!mbar_wait_warp(&s->s_full[st], (it >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      float pt[64], dp[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      float pt[32], dp[32];
+      {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tS[st] + lane_off + c * 32, v);
+        tmem_ld_32x32b_x32(tS[st] + lane_off + cb, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) pt[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
-        tmem_ld_32x32b_x32(tdP[st] + lane_off + c * 32, v);
+        for (int e = 0; e < 32; ++e) pt[e] = __uint_as_float(v[e]) * p.scale_log2;
+        tmem_ld_32x32b_x32(tdP[st] + lane_off + cb, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) dp[c * 32 + e] = __uint_as_float(v[e]);
+        for (int e = 0; e < 32; ++e) dp[e] = __uint_as_float(v[e]);
       }
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int qi = q0 + c;
-        const bool valid = (kj <= qi + off) && (c < qlim) && (kj < Lk);
-        const float pv = valid ? exp2f(pt[c] - __ldg(lse_row + c) * LOG2E) : 0.f;
+      for (int c = 0; c < 32; ++c) {
+        const int qc = cb + c;
+        const int qi = q0 + qc;
+        const bool valid = (kj <= qi + off) && (qc < qlim) && (kj < Lk);
+        const float pv = valid ? exp2f(pt[c] - __ldg(lse_row + qc) * LOG2E) : 0.f;
         pt[c] = pv;
-        dp[c] = pv * (dp[c] - (valid ? __ldg(dlt_row + c) : 0.f));
+        dp[c] = pv * (dp[c] - (valid ? __ldg(dlt_row + qc) : 0.f));
       }
       if (it > 0 && !mbar_wait_warp(&s->mma_done, (it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint4 w;
         w.x = pack_bf16(pt[c * 8 + 0], pt[c * 8 + 1]);
         w.y = pack_bf16(pt[c * 8 + 2], pt[c * 8 + 3]);
         w.z = pack_bf16(pt[c * 8 + 4], pt[c * 8 + 5]);
         w.w = pack_bf16(pt[c * 8 + 6], pt[c * 8 + 7]);
-        st_tile_chunk(sPt, r, c, w);
+        st_tile_chunk(sPt, r, half * 4 + c, w);
         uint4 d;
         d.x = pack_bf16(dp[c * 8 + 0], dp[c * 8 + 1]);
         d.y = pack_bf16(dp[c * 8 + 2], dp[c * 8 + 3]);
         d.z = pack_bf16(dp[c * 8 + 4], dp[c * 8 + 5]);
         d.w = pack_bf16(dp[c * 8 + 6], dp[c * 8 + 7]);
-        st_tile_chunk(sdSt, r, c, d);
+        st_tile_chunk(sdSt, r, half * 4 + c, d);
       }
       fence_proxy_async_shared();
       tc_fence_before();
@@ -1014,22 +1044,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (rep == 1) {
         uint4* dv4 = reinterpret_cast<uint4*>(p.dv + ((int64_t)(ks0 + kj) * p.Hk + g) * HD);
         uint4* dk4 = reinterpret_cast<uint4*>(p.dk + ((int64_t)(ks0 + kj) * p.Hk + g) * HD);
-        for (int u = 0; u < 16; ++u) dv4[u] = z, dk4[u] = z;
+        for (int u = half * 8; u < half * 8 + 8; ++u) dv4[u] = z, dk4[u] = z;
       } else {
         uint4* dv4 = reinterpret_cast<uint4*>(p2.part_dv + ((int64_t)(ks0 + kj) * p.Hq + h) * HD);
         uint4* dk4 = reinterpret_cast<uint4*>(p2.part_dk + ((int64_t)(ks0 + kj) * p.Hq + h) * HD);
-        for (int u = 0; u < 32; ++u) dv4[u] = z, dk4[u] = z;
+        for (int u = half * 16; u < half * 16 + 16; ++u) dv4[u] = z, dk4[u] = z;
       }
     }
     if (ok && n_it > 0 && mbar_wait_warp(&s->mma_done, (n_it - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
       const bool valid = kj < Lk;
       if (rep == 1) {
-        store_row128(tdV + lane_off, p.dv + ((int64_t)(ks0 + kj) * p.Hk + g) * HD, 1.f, valid);
-        store_row128(tdK + lane_off, p.dk + ((int64_t)(ks0 + kj) * p.Hk + g) * HD, p.scale, valid);
+        store_row64(tdV + lane_off + half * 64, p.dv + ((int64_t)(ks0 + kj) * p.Hk + g) * HD + half * 64, 1.f, valid);
+        store_row64(tdK + lane_off + half * 64, p.dk + ((int64_t)(ks0 + kj) * p.Hk + g) * HD + half * 64, p.scale,
+                    valid);
       } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = half * 2; c < half * 2 + 2; ++c) {
           uint32_t v[32], w[32];
           tmem_ld_32x32b_x32(tdV + lane_off + c * 32, v);
           tmem_ld_32x32b_x32(tdK + lane_off + c * 32, w);
@@ -1113,7 +1144,7 @@ struct __align__(8) Dq2Smem {
   int abort;
 };
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS_BWD2, 1)
     attn_bwd_dq2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK64,
                         const __grid_constant__ CUtensorMap tmV64, const __grid_constant__ CUtensorMap tmDO,
                         BwdParams p) {
@@ -1148,7 +1179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&s->s_full[0], 1);
     mbar_init(&s->s_full[1], 1);
-    mbar_init(&s->p_full, 128);
+    mbar_init(&s->p_full, BWD2_SOFTMAX_THREADS);
     mbar_init(&s->ds_done, 1);
     mbar_init(&s->drain, 1);
     s->abort = 0;
@@ -1244,28 +1275,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const bool vq = qi < L;
+    const int half = (warp - 2) >> 2;
+    const int cb = half * 32;  // this warp's 32 key columns of the tile
     const float lse2 = vq ? p.lse[(int64_t)h * p.T + s0 + qi] * LOG2E : INFINITY;
     const float dlt = vq ? p.delta[(int64_t)h * p.T + s0 + qi] : 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!mbar_wait_warp(&s->s_full[j & 1], (j >> 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      float pr[64], dp[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      float pr[32], dp[32];
+      {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tS[j & 1] + lane_off + c * 32, v);
+        tmem_ld_32x32b_x32(tS[j & 1] + lane_off + cb, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) pr[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
-        tmem_ld_32x32b_x32(tdP[j & 1] + lane_off + c * 32, v);
+        for (int e = 0; e < 32; ++e) pr[e] = __uint_as_float(v[e]) * p.scale_log2;
+        tmem_ld_32x32b_x32(tdP[j & 1] + lane_off + cb, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) dp[c * 32 + e] = __uint_as_float(v[e]);
+        for (int e = 0; e < 32; ++e) dp[e] = __uint_as_float(v[e]);
       }
-      const int kb = j * KT;
+      const int kb = j * KT + cb;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < 32; ++c) {
         const int kj = kb + c;
         const bool valid = (kj <= qi + off) && (kj < Lk) && vq;
         const float pv = valid ? exp2f(pr[c] - lse2) : 0.f;
@@ -1273,13 +1305,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (j > 0 && !mbar_wait_warp(&s->ds_done, (j - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) { ok = false; break; }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint4 w;
         w.x = pack_bf16(pr[c * 8 + 0], pr[c * 8 + 1]);
         w.y = pack_bf16(pr[c * 8 + 2], pr[c * 8 + 3]);
         w.z = pack_bf16(pr[c * 8 + 4], pr[c * 8 + 5]);
         w.w = pack_bf16(pr[c * 8 + 6], pr[c * 8 + 7]);
-        st_tile_chunk(sdS, r, c, w);
+        st_tile_chunk(sdS, r, half * 4 + c, w);
       }
       fence_proxy_async_shared();
       tc_fence_before();
@@ -1287,7 +1319,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (ok && n_kv > 0 && mbar_wait_warp(&s->ds_done, (n_kv - 1) & 1, abort, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
-      store_row128(tdQ + lane_off, p.dq + ((int64_t)(s0 + qi) * p.Hq + h) * HD, p.scale, vq);
+      store_row64(tdQ + lane_off + half * 64, p.dq + ((int64_t)(s0 + qi) * p.Hq + h) * HD + half * 64, p.scale, vq);
     }
   }
   tc_fence_before();
@@ -1394,10 +1426,10 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   p2.part_dv = b.part_dv;
   const int nt = (a.max_seqlen + TILE - 1) / TILE;
   const int ntk = ((a.cu_seqlens_k ? a.max_seqlen_k : a.max_seqlen) + TILE - 1) / TILE;
-  attn_bwd_dkv2_kernel<<<dim3(ntk, a.Hq, a.nseq), NUM_THREADS, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
+  attn_bwd_dkv2_kernel<<<dim3(ntk, a.Hq, a.nseq), NUM_THREADS_BWD2, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
   CUtensorMap mk64 = head_map64(a.k, a.k_row, a.Hk, Tk);
   CUtensorMap mv64 = head_map64(a.v, a.v_row, a.Hk, Tk);
-  attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p);
+  attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS_BWD2, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p);
   if (rep > 1) {
     const int warps = 8;
     const int64_t work = (int64_t)Tk * a.Hk;
