@@ -34,6 +34,8 @@
 //     bf16 straight into the 128-byte-swizzled stage layout that TMA would
 //     have produced (fence.proxy.async before arriving on the stage barrier),
 //     so a frozen base weight is read at 0.5 byte per element.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "tma.h"
@@ -100,7 +102,26 @@ struct Params {
   void* peer[8];  // kEpiPeerBF16 receive buffers (GemmArgs::peer)
   int peer_world, peer_rank;
   int64_t peer_off, peer_rs_rows;
+  // split tail (dense mode): tiles >= split_first are cut into split_s K-pieces
+  int split_first, split_s;
 };
+
+// Tail-wave split.  A dense GEMM whose tile count leaves a small last wave
+// (e.g. 448 tiles on 148 SMs: 3 full waves + 4 tiles, so the 4th wave runs 4
+// SMs while 144 idle) cuts each of the `rem` tail tiles into split_s K-ranges.
+// Every piece writes its fp32 partial tile here; per (tile, 32-row quadrant)
+// the last piece to finish (atomic ticket, no waiting) sums the partials in
+// piece order and runs the normal epilogue.  At most 4 pieces per tile: the
+// reduction is one CTA's L2 round trips, so a longer split costs more in the
+// reducer than it saves in the wave.  Sized for rem * split_s <= 256
+// pieces and rem <= 128 tiles (host enforces); one workspace per device, so
+// tail-split GEMMs on one device run in stream order (every launch of this
+// library's GEMMs shares it).  Tickets return to zero after each use.
+constexpr int SPLIT_MAX_PIECES = 256;
+constexpr int SPLIT_MAX_S = 4;  // pieces per tile: the reducer keeps all their loads in flight
+constexpr int SPLIT_MAX_TILES = 128;
+__device__ __align__(256) float g_split_ws[(size_t)SPLIT_MAX_PIECES * 128 * 256];
+__device__ int g_split_ticket[SPLIT_MAX_TILES * 4];
 
 // Tile decode shared by the three warp roles (they must agree exactly).
 struct TileInfo {
@@ -108,6 +129,7 @@ struct TileInfo {
   int kb_begin, num_k;
   int64_t b_off;
   int64_t c_row_off;
+  int split, piece;  // split tail: index among the split tiles and K-piece (split = -1: whole tile)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m, int& n) {
@@ -132,13 +154,34 @@ __device__ __forceinline__ TileInfo tile_info(int t, const Params& p) {
     ti.b_off = 0;
     ti.c_row_off = (int64_t)g * p.M;
   } else {
-    tile_coords(t, p.num_m, p.num_n, ti.tm, ti.tn);
+    ti.split = -1;
+    ti.piece = 0;
+    int tile = t;
     ti.kb_begin = 0;
     ti.num_k = p.num_k;
+    if (GROUP == 0 && p.split_s > 1 && t >= p.split_first) {
+      const int v = t - p.split_first;
+      ti.split = v / p.split_s;
+      ti.piece = v - ti.split * p.split_s;
+      tile = p.split_first + ti.split;
+      ti.kb_begin = ti.piece * p.num_k / p.split_s;
+      ti.num_k = (ti.piece + 1) * p.num_k / p.split_s - ti.kb_begin;
+    }
+    tile_coords(tile, p.num_m, p.num_n, ti.tm, ti.tn);
     ti.b_off = (GROUP == 1) ? (int64_t)p.tile_group[ti.tm] * p.b_group_stride : 0;
     ti.c_row_off = 0;
   }
+  if constexpr (GROUP == 2) ti.split = -1, ti.piece = 0;
   return ti;
+}
+
+template <int GROUP, bool BQ, int EPI>
+constexpr bool kSplitCapable = (GROUP == 0 && !BQ && EPI != kEpiPeerBF16);
+
+// Units of work: tiles, with every split tail tile counted once per K-piece.
+__device__ __forceinline__ int num_units(const Params& p, int groups_mul) {
+  const int tiles = p.num_m * p.num_n * groups_mul;
+  return (p.split_s > 1) ? p.split_first + (tiles - p.split_first) * p.split_s : tiles;
 }
 
 template <int EPI>
@@ -376,7 +419,7 @@ __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.num_m * p.num_n * (GROUP == 2 ? p.groups : 1);
+  const int num_tiles = (GROUP == 0) ? num_units(p, 1) : p.num_m * p.num_n * (GROUP == 2 ? p.groups : 1);
   const int num_k2 = (GROUP == 0) ? p.num_k2 : 0;
 
   if (threadIdx.x == 0) {
@@ -579,6 +622,70 @@ __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
       const int tm = ti.tm, tn = ti.tn;
       const int row = tm * BM + q * 32 + lane;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if (kSplitCapable<GROUP, BQ, EPI> && ti.split >= 0) {
+        // tail piece: fp32 partial out, TMEM back to the MMA warp, then the
+        // last piece of this (tile, quadrant) reduces and runs the epilogue
+        float* part = g_split_ws + ((size_t)(ti.split * p.split_s + ti.piece) * BM + q * 32 + lane) * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          if (tn * BN + c >= p.N) break;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_addr + c, v);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(part + c);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            dst[u] = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                                 __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+        }
+        tc_fence_before();
+        mbar_arrive(&s->tmem_empty[acc]);
+        if (++acc == 2) acc = 0, acc_phase ^= 1;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&g_split_ticket[ti.split * 4 + q], 1) == p.split_s - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          const float* base = g_split_ws + ((size_t)ti.split * p.split_s * BM + q * 32 + lane) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            if (tn * BN + c >= p.N) break;
+            // all pieces' loads in flight before the adds (split_s <= SPLIT_MAX_S)
+            float4 w[SPLIT_MAX_S][8];
+#pragma unroll
+            for (int pc = 0; pc < SPLIT_MAX_S; ++pc) {
+              if (pc < p.split_s) {
+                const float4* src = reinterpret_cast<const float4*>(base + (size_t)pc * BM * BN + c);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) w[pc][u] = __ldcg(src + u);
+              }
+            }
+            float a[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = 0.f;
+#pragma unroll
+            for (int pc = 0; pc < SPLIT_MAX_S; ++pc) {
+              if (pc < p.split_s) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  a[4 * u] += w[pc][u].x;
+                  a[4 * u + 1] += w[pc][u].y;
+                  a[4 * u + 2] += w[pc][u].z;
+                  a[4 * u + 3] += w[pc][u].w;
+                }
+              }
+            }
+            uint32_t v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(a[j]);
+            epilogue_chunk<EPI>(p, row, tn * BN + c, v, 0);
+          }
+          if (lane == 0) g_split_ticket[ti.split * 4 + q] = 0;
+        }
+        continue;
+      }
       if constexpr (EPI == kEpiPeerBF16) {
         uint8_t* stg = tiles + STAGES * STAGE_BYTES + 1024 + q * 4096;
 #pragma unroll 1
@@ -681,8 +788,24 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
   p.peer_rank = g.peer_rank;
   p.peer_off = g.peer_off;
   p.peer_rs_rows = g.peer_rs_rows;
+  p.split_first = 0;
+  p.split_s = 1;
   const int tiles = p.num_m * p.num_n * (GROUP == 2 ? g.groups : 1);
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  static const bool split_off = std::getenv("WAVELET_GEMM_NO_SPLIT") != nullptr;  // A/B switch
+  if (GROUP == 0 && !BQ && EPI != kEpiPeerBF16 && p.num_k2 == 0 && !g.no_split && !split_off && tiles > grid) {
+    const int rem = tiles % grid;
+    int S = rem > 0 ? grid / rem : 1;
+    S = S < SPLIT_MAX_S ? S : SPLIT_MAX_S;
+    // at least 64 k-blocks per piece: measured on B200, shorter pieces lose
+    // more in the partial-tile round trip than the shorter wave saves
+    // (K = 3584: 1126 -> 980 TFLOP/s split; K = 18944: 1199 -> 1308)
+    S = S < p.num_k / 64 ? S : p.num_k / 64;
+    if (S >= 2 && rem <= SPLIT_MAX_TILES && rem * S <= SPLIT_MAX_PIECES) {
+      p.split_first = tiles - rem;
+      p.split_s = S;
+    }
+  }
   kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem, stream>>>(ta, tb, ta2, tb2, p);
 }
 

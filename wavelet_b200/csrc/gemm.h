@@ -73,6 +73,9 @@ struct GemmArgs {
   int peer_rank = 0;
   int64_t peer_off = 0;
   int64_t peer_rs_rows = 0;
+  // Dense mode cuts the tiles of a small last wave into K-pieces reduced in a
+  // per-device workspace (gemm.cu, "tail-wave split"); true keeps whole tiles.
+  bool no_split = false;
 };
 
 void gemm_bf16(const GemmArgs& g, cudaStream_t stream);

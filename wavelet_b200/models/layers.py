@@ -174,7 +174,7 @@ def layer_bwd(dout: torch.Tensor, x: torch.Tensor, c: dict, P: dict, G: dict, cf
     ops.qk_norm_rope_bwd_(dqkv, qkv_pre, nq, nk, b.pos, b.inv_freq, P.get("q_norm"), P.get("k_norm"), c["rstd_qk"],
                           G.get("q_norm"), G.get("k_norm"), cfg.rms_eps)
     if G.get("qkv_b") is not None:
-        G["qkv_b"].add_(dqkv.float().sum(0))
+        G["qkv_b"].add_(dqkv.sum(0, dtype=torch.float32))  # reduce in fp32, no fp32 copy of dqkv
     dh1 = _lin_bwd(dqkv, c["h1"], c["u_qkv"], P["qkv_w"], G.get("qkv_w"), lora.get("qkv"), tp)
     del dqkv
     dx = ops.rmsnorm_bwd(x, P["in_norm"], c["rstd1"], dh1, dres=dx2, dw=G.get("in_norm"))
