@@ -229,9 +229,23 @@ ALIASES = {
 }
 
 
+# a DeepSeek-V4 of every attention type in three layers (CPU tests, smoke runs)
+TINY_DEEPSEEK_V4 = dict(
+    vocab_size=1024, hidden_size=64, num_hidden_layers=3, num_attention_heads=4, head_dim=32, q_lora_rank=32,
+    partial_rotary_factor=0.5,
+    layer_types=["sliding_attention", "compressed_sparse_attention", "heavily_compressed_attention"],
+    compress_rates={"compressed_sparse_attention": 4, "heavily_compressed_attention": 16}, sliding_window=16,
+    o_groups=2, o_lora_rank=16, index_n_heads=2, index_head_dim=32, index_topk=4, moe_intermediate_size=64,
+    n_routed_experts=4, num_experts_per_tok=2, num_hash_layers=1, hc_mult=2, max_position_embeddings=4096)
+
+
 def resolve_arch(name: str, overrides: dict[str, Any] | None = None) -> ArchConfig:
     """Resolve a model name: preset, alias, a local HF dir, or a config.json path."""
     key = ALIASES.get(name, name)
+    if key == "tiny-deepseek-v4":
+        from .deepseek_v4.config import DeepseekV4Config
+
+        return DeepseekV4Config(**{**TINY_DEEPSEEK_V4, **(overrides or {})})
     if key in PRESETS:
         cfg = PRESETS[key]
     else:
@@ -239,7 +253,13 @@ def resolve_arch(name: str, overrides: dict[str, Any] | None = None) -> ArchConf
         if p.is_dir() and (p / "config.json").exists():
             p = p / "config.json"
         if p.is_file():
-            cfg = from_hf_config(json.loads(p.read_text()))
+            d = json.loads(p.read_text())
+            if d.get("model_type") == "deepseek_v4":
+                from .deepseek_v4.config import DeepseekV4Config
+
+                cfg = DeepseekV4Config.from_dict(d)
+                return DeepseekV4Config.from_dict({**cfg.to_dict(), **(overrides or {})}) if overrides else cfg
+            cfg = from_hf_config(d)
         else:
             raise ValueError(
                 f"unknown model {name!r}: not a preset ({', '.join(sorted(PRESETS))}), "

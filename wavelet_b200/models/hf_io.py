@@ -101,6 +101,14 @@ def internal_from_hf(cfg, hf: dict[str, torch.Tensor]) -> dict[str, torch.Tensor
 def load_hf_weights(model, path: Path) -> None:
     from safetensors.torch import load_file
 
+    if hasattr(model, "load_pretrained"):  # eager DeepSeek-V4: native checkpoint directory
+        cfg_file = Path(path) / "config.json"
+        if cfg_file.exists() and json.loads(cfg_file.read_text()).get("wavelet_checkpoint_format") is None:
+            raise ValueError(f"{path} is a published DeepSeek-V4 checkpoint; convert it to a converted native "
+                             "checkpoint first (python -m wavelet_b200.models.deepseek_v4.convert)")
+        model.load_pretrained(path)
+        return
+
     files = sorted(Path(path).glob("*.safetensors"))
     if not files:
         raise FileNotFoundError(f"no .safetensors files in {path}")

@@ -349,7 +349,8 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                 with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
                 lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None,
                 tp: tuple[int, int] | None = None, ep_fabric=None) -> CausalLM:
-    """Build (and random-init) a model.
+    """Build (and random-init) a model (a ``DeepseekV4Config`` builds the
+    eager DeepSeek-V4 model behind the same interface).
 
     ``lora``: an object with ``rank``, ``alpha``, ``target_modules``, ``dropout``
     (the ``lora`` config section) -> frozen base + trainable adapters.
@@ -362,6 +363,15 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     device = torch.device(device)
     if dtype is None:
         dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    from .deepseek_v4.config import DeepseekV4Config
+
+    if isinstance(cfg, DeepseekV4Config):
+        if lora is not None or load_in_4bit or ep or tp or fabric is not None or ep_fabric is not None:
+            raise NotImplementedError("the eager DeepSeek-V4 model trains with data parallelism only "
+                                      "(no LoRA / QLoRA, tensor or expert parallelism, peer fabric)")
+        from .deepseek_v4.trainable import DeepseekV4Trainable
+
+        return DeepseekV4Trainable(cfg, device, dtype, dp_rank, dp_world, seed, init, with_grad, with_optimizer)
     tp_size, tp_rank = tp or (1, 0)
     full_specs = param_specs(cfg)
     specs = param_specs(tp_local_cfg(cfg, tp_size)) if tp_size > 1 else full_specs

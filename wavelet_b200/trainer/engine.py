@@ -89,8 +89,8 @@ class Engine:
         weights = b.loss_mask.float() * token_scale
         loss, dh = lm_head.sft_loss_and_grad(h.detach(), m.head_weight(), b.targets, weights, m.head_grad(), self.chunk)
         h.backward(dh)
-        if not b.input_ids.is_cuda:
-            m.collect_cpu_grads()
+        if not b.input_ids.is_cuda or getattr(m, "eager", False):
+            m.collect_cpu_grads()  # autograd gradients -> the fp32 flat gradient store
         return loss
 
     @torch.no_grad()

@@ -26,8 +26,26 @@ def device_peak_flops(device: torch.device) -> float:
     return 2.25e15
 
 
+def _deepseek_v4_params(cfg) -> int:
+    """DeepSeek-V4: attention projections, compressor projections, the two
+    hyper-connection maps, active + shared experts and the router per layer."""
+    H, nh, D, hc = cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim, cfg.hc_mult
+    attn = H * cfg.q_lora_rank + cfg.q_lora_rank * nh * D + H * D + nh * D * cfg.o_lora_rank \
+        + cfg.o_groups * cfg.o_lora_rank * H
+    hc_maps = 2 * (2 + hc) * hc * hc * H
+    moe = (cfg.num_experts_per_tok + cfg.n_shared_experts) * 3 * H * cfg.moe_intermediate_size \
+        + cfg.n_routed_experts * H
+    total = 0
+    for t in cfg.layer_types:
+        comp = 0 if t == "sliding_attention" else 2 * (2 if t == "compressed_sparse_attention" else 1) * D * H
+        total += attn + comp + hc_maps + moe
+    return total + cfg.vocab_size * H
+
+
 def matmul_params(cfg) -> int:
     """Parameters that take part in matmuls for one token (active experts only)."""
+    if hasattr(cfg, "hc_mult"):
+        return _deepseek_v4_params(cfg)
     H, I = cfg.hidden_size, cfg.intermediate_size
     attn = H * cfg.qkv_dim + cfg.q_dim * H
     total = 0
@@ -42,7 +60,11 @@ def matmul_params(cfg) -> int:
 
 def flops_per_token(cfg, seq_len: int, lora_params: int | None = None) -> float:
     n = matmul_params(cfg)
-    attn = 12 * cfg.num_layers * cfg.q_dim * seq_len
+    if hasattr(cfg, "hc_mult"):  # each query reads its window plus at most index_topk entries
+        keys = min(seq_len, cfg.sliding_window + cfg.index_topk)
+        attn = 12 * cfg.num_hidden_layers * cfg.num_attention_heads * cfg.head_dim * keys
+    else:
+        attn = 12 * cfg.num_layers * cfg.q_dim * seq_len
     if lora_params:
         return 4 * n + 6 * lora_params + attn
     return 6 * n + attn
