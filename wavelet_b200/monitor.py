@@ -281,6 +281,9 @@ class RunMonitor:
         try:
             self._wandb = wandb.init(project=w.project, entity=w.entity, name=w.name, group=w.group, tags=w.tags,
                                      mode=w.mode, config=cfg, dir=str(self.output_dir))
+            from .wandb_overview import maybe_create_overview
+
+            maybe_create_overview(self._wandb, cfg if isinstance(cfg, dict) else None, w)
         except Exception as e:  # offline fallback
             if getattr(w, "offline_fallback", True):
                 self.log_event("wandb_init_failed", payload={"error": str(e)})
