@@ -29,7 +29,6 @@ class ExpertPolicySync:
         self.fab = fabric
         ef = trainer_model.expert_flat
         self.expert_ptrs = fabric.ptrs_of(ef.compute)
-        self.base = ef.compute.data_ptr()
         if trainer_model.ep_size != fabric.world:
             raise ValueError("the fabric must span the expert-parallel group")
 
