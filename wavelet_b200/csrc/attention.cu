@@ -1371,7 +1371,7 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * LOG2E;
   p.err = error_word(dev);
   dim3 grid((a.max_seqlen + TILE - 1) / TILE, a.Hq, a.nseq);
-  attn_fwd_kernel<<<grid, NUM_THREADS, fwd_smem_bytes(), stream>>>(mq, mk, mv, p);
+  attn_fwd_kernel<<<grid, NUM_THREADS, fwd_smem_bytes(), stream>>>(mq, mk, mv, p); note_launch();
 }
 
 }  // namespace wb
@@ -1398,7 +1398,7 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
     const int64_t work = (int64_t)a.T * a.Hq;
     attn_delta_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row, reinterpret_cast<const __nv_bfloat16*>(b.dout),
-        b.delta, a.T, a.Hq);
+        b.delta, a.T, a.Hq); note_launch();
   }
   const int Tk = a.cu_seqlens_k ? a.Tk : a.T;
   CUtensorMap mq = head_map(a.q, a.q_row, a.Hq, a.T);
@@ -1426,15 +1426,15 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
   p2.part_dv = b.part_dv;
   const int nt = (a.max_seqlen + TILE - 1) / TILE;
   const int ntk = ((a.cu_seqlens_k ? a.max_seqlen_k : a.max_seqlen) + TILE - 1) / TILE;
-  attn_bwd_dkv2_kernel<<<dim3(ntk, a.Hq, a.nseq), NUM_THREADS_BWD2, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2);
+  attn_bwd_dkv2_kernel<<<dim3(ntk, a.Hq, a.nseq), NUM_THREADS_BWD2, dkv2_smem_bytes(), stream>>>(mq64, mk, mv, mdo64, p2); note_launch();
   CUtensorMap mk64 = head_map64(a.k, a.k_row, a.Hk, Tk);
   CUtensorMap mv64 = head_map64(a.v, a.v_row, a.Hk, Tk);
-  attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS_BWD2, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p);
+  attn_bwd_dq2_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS_BWD2, dq2_smem_bytes(), stream>>>(mq, mk64, mv64, mdo, p); note_launch();
   if (rep > 1) {
     const int warps = 8;
     const int64_t work = (int64_t)Tk * a.Hk;
     attn_dkv_reduce_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
-        b.part_dk, b.part_dv, p.dk, p.dv, Tk, a.Hq, a.Hk, a.scale);
+        b.part_dk, b.part_dv, p.dk, p.dv, Tk, a.Hq, a.Hk, a.scale); note_launch();
   }
 }
 
@@ -1461,7 +1461,7 @@ int attn_bwd_explicit(const AttnBwdArgs& b, int* err, cudaStream_t stream) {
     const int64_t work = (int64_t)a.T * a.Hq;
     attn_delta_kernel<<<(int)((work + warps - 1) / warps), warps * 32, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row, reinterpret_cast<const __nv_bfloat16*>(b.dout),
-        b.delta, a.T, a.Hq);
+        b.delta, a.T, a.Hq); note_launch();
   }
   CUtensorMap mq, mk, mv, mdo;
   try {
@@ -1488,8 +1488,8 @@ int attn_bwd_explicit(const AttnBwdArgs& b, int* err, cudaStream_t stream) {
   p.scale_log2 = a.scale * LOG2E;
   p.err = err;
   const int nt = (a.max_seqlen + TILE - 1) / TILE;
-  attn_bwd_dkv_kernel<<<dim3(nt, a.Hk, a.nseq), NUM_THREADS, dkv_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
-  attn_bwd_dq_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq_smem_bytes(), stream>>>(mq, mk, mv, mdo, p);
+  attn_bwd_dkv_kernel<<<dim3(nt, a.Hk, a.nseq), NUM_THREADS, dkv_smem_bytes(), stream>>>(mq, mk, mv, mdo, p); note_launch();
+  attn_bwd_dq_kernel<<<dim3(nt, a.Hq, a.nseq), NUM_THREADS, dq_smem_bytes(), stream>>>(mq, mk, mv, mdo, p); note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : 5;
 }
 

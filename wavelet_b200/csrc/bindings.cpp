@@ -14,6 +14,8 @@
 namespace wb {
 int* error_word(int device);
 int read_error_word(int device);
+long long launch_count();
+void note_launches(long long n);
 void clear_error_word(int device);
 }  // namespace wb
 
@@ -407,9 +409,12 @@ void rmsnorm_bwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& rst
   const int rows = x.numel() / H;
   if (dw) check_f32(*dw, "dw");
   const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor part;
+  if (dw) part = at::empty({wb::rmsnorm_dw_splits(rows), H}, x.options().dtype(at::kFloat));
   wb::rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(),
                   dres ? dres->data_ptr() : nullptr, dx.data_ptr(),
-                  dw ? dw->data_ptr<float>() : nullptr, rows, H, cur_stream());
+                  dw ? dw->data_ptr<float>() : nullptr, dw ? part.data_ptr<float>() : nullptr, rows, H,
+                  cur_stream());
 }
 
 void qk_norm_rope_fwd(at::Tensor& qkv, int64_t n_q, int64_t n_k, const at::Tensor& pos,
@@ -761,6 +766,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("slots_sum", &slots_sum);
   m.def("rows_gather_sum", &rows_gather_sum);
   m.def("read_error", &read_error);
+  m.def("launch_count", []() { return wb::launch_count(); },
+        "kernels launched by this library since it was loaded (every launch site counts one)");
+  m.def("note_launches", [](int64_t n) { wb::note_launches(n); },
+        "count n launches made outside the launch sites (kernels replayed from a captured graph)");
   m.def("clear_error", &clear_error);
   m.attr("EPI_BF16") = (int)wb::kEpiBF16;
   m.attr("EPI_F32") = (int)wb::kEpiF32;

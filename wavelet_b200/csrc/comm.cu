@@ -406,13 +406,13 @@ static void check_world(int world) {
 void peer_barrier(const PeerPtrs& pads, int rank, int world, uint32_t epoch, int slot_base, uint64_t budget_ns,
                   int* err, cudaStream_t st) {
   check_world(world);
-  comm::barrier_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, slot_base, budget_ns, err);
+  comm::barrier_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, slot_base, budget_ns, err); note_launch();
 }
 
 void norm_exchange(const PeerPtrs& pads, int rank, int world, uint32_t epoch, const float* stats, float max_norm,
                    float* tot, uint64_t budget_ns, int* err, cudaStream_t st) {
   check_world(world);
-  comm::norm_exchange_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, stats, max_norm, tot, budget_ns, err);
+  comm::norm_exchange_kernel<<<1, 32, 0, st>>>(pads, rank, world, epoch, stats, max_norm, tot, budget_ns, err); note_launch();
 }
 
 #define WB_WORLD_SWITCH(W, ...)                          \
@@ -434,7 +434,7 @@ void rs_sum_sumsq(const PeerPtrs& grads, int world, int64_t lo, int64_t n, float
   if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 512, 148 * 4);
-  WB_WORLD_SWITCH(world, comm::rs_kernel<kW><<<grid, 512, 0, st>>>(grads, lo, n8, scale, out, stats));
+  WB_WORLD_SWITCH(world, comm::rs_kernel<kW><<<grid, 512, 0, st>>>(grads, lo, n8, scale, out, stats)); note_launch();
 }
 
 void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* master, const float* g, float* m, float* v,
@@ -445,7 +445,7 @@ void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* mast
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 256, 148 * 8);
   WB_WORLD_SWITCH(world, comm::adamw_ag_kernel<kW><<<grid, 256, 0, st>>>(compute, lo, master, g, m, v, n8, lr, b1, b2,
-                                                                            eps, wd, bc1, bc2, tot));
+                                                                            eps, wd, bc1, bc2, tot)); note_launch();
 }
 
 void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src, int64_t n, cudaStream_t st) {
@@ -453,14 +453,14 @@ void allgather_bf16(const PeerPtrs& dst, int world, int64_t lo, const void* src,
   if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 256, 148 * 8);
-  WB_WORLD_SWITCH(world, comm::ag_kernel<kW><<<grid, 256, 0, st>>>(dst, lo, static_cast<const uint4*>(src), n8));
+  WB_WORLD_SWITCH(world, comm::ag_kernel<kW><<<grid, 256, 0, st>>>(dst, lo, static_cast<const uint4*>(src), n8)); note_launch();
 }
 
 void gather_from_peers(const PeerPtrs& src, int world, int64_t off, int64_t n, void* dst, cudaStream_t st) {
   if (n <= 0) return;
   if (n % 8 || off % 8) throw std::runtime_error("wavelet_b200 gather_from_peers: n and offset must be multiples of 8");
   comm::gather_from_peers_kernel<<<comm::grid_for(n / 8 * world, 256, 148 * 8), 256, 0, st>>>(
-      src, world, off, n / 8, static_cast<uint4*>(dst));
+      src, world, off, n / 8, static_cast<uint4*>(dst)); note_launch();
 }
 
 void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const void* res, void* out,
@@ -469,7 +469,7 @@ void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const vo
   if (n % 8 || stride % 8) throw std::runtime_error("wavelet_b200 slots_sum: n and slot stride must be multiples of 8");
   comm::slots_sum_kernel<<<comm::grid_for(n / 8, 256, 148 * 8), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(slots), world, stride, n / 8, static_cast<const __nv_bfloat16*>(res),
-      static_cast<__nv_bfloat16*>(out));
+      static_cast<__nv_bfloat16*>(out)); note_launch();
 }
 
 void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,
@@ -477,7 +477,7 @@ void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int*
   if (n <= 0) return;
   if (H % 8 || ldx % 8 || ldd % 8) throw std::runtime_error("wavelet_b200 rows_scatter: H and strides must be multiples of 8");
   comm::rows_scatter_kernel<<<(n + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, src_row, dst_rank,
-                                                         dst_row, scale, dst, ldd, n, H);
+                                                         dst_row, scale, dst, ldd, n, H); note_launch();
 }
 
 void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, const int64_t* src_row, const float* w,
@@ -493,6 +493,7 @@ void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, cons
   else
     comm::rows_gather_sum_kernel<false><<<grid, 256, 0, st>>>(src, lds, src_rank, src_row, w, k,
                                                               static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H);
+  note_launch();
 }
 
 }  // namespace wb

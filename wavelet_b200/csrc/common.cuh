@@ -323,4 +323,8 @@ __device__ __forceinline__ void grid_sum2_ordered(float a, float b, float* scrat
 // Host side: one device int per GPU that kernels OR their error codes into.
 namespace wb {
 int* error_word(int device);
+// Kernels launched by this library since load (every launch site adds one);
+// read through the extension's launch_count() for launch accounting.
+void note_launch();
+long long launch_count();
 }

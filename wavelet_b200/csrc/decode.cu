@@ -583,7 +583,7 @@ void kv_append(const void* k, int64_t k_row, const void* v, int64_t v_row, void*
   const int warps = 8;
   kv_append_kernel<<<(T * Hk + warps - 1) / warps, warps * 32, 0, st>>>(
       (const __nv_bfloat16*)k, k_row, (const __nv_bfloat16*)v, v_row, (__nv_bfloat16*)k_cache,
-      (__nv_bfloat16*)v_cache, slot, T, Hk, block_size);
+      (__nv_bfloat16*)v_cache, slot, T, Hk, block_size); note_launch();
 }
 
 void decode_attention(const DecodeArgs& a, cudaStream_t st) {
@@ -609,17 +609,17 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st) {
     decode_attn3_kernel<<<grid, D2_WARPS * 32, smem, st>>>(
         tk, tv, (const __nv_bfloat16*)a.q, a.q_row, a.block_tables, a.max_blocks, a.ctx_lens, (__nv_bfloat16*)a.out,
         a.out_row, a.part_o, a.part_ml, a.Hq, a.Hk, a.block_size, a.splits, a.scale * 1.4426950408889634f,
-        error_word(dev));
+        error_word(dev)); note_launch();
   } else {
   decode_attn_kernel<<<grid, DEC_THREADS, 0, st>>>(
       (const __nv_bfloat16*)a.q, a.q_row, (const __nv_bfloat16*)a.k_cache, (const __nv_bfloat16*)a.v_cache,
       a.block_tables, a.max_blocks, a.ctx_lens, (__nv_bfloat16*)a.out, a.out_row, a.part_o, a.part_ml, a.Hq, a.Hk,
-      a.block_size, a.splits, a.scale * 1.4426950408889634f);
+      a.block_size, a.splits, a.scale * 1.4426950408889634f); note_launch();
   }
   if (a.splits > 1) {
     const int warps = 8;
     decode_combine_kernel<<<(a.nseq * a.Hq + warps - 1) / warps, warps * 32, 0, st>>>(
-        a.part_o, a.part_ml, (__nv_bfloat16*)a.out, a.out_row, a.nseq, a.Hq, a.splits);
+        a.part_o, a.part_ml, (__nv_bfloat16*)a.out, a.out_row, a.nseq, a.Hq, a.splits); note_launch();
   }
 }
 
@@ -628,7 +628,7 @@ void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv
                    cudaStream_t st, const int64_t* seed_dev) {
   if (rows <= 0) return;
   sample_kernel<<<rows, 1024, 0, st>>>((const __nv_bfloat16*)z, ldz, V, inv_tau, thresh, min_p, seed, row_ids, out_tok,
-                                       out_lp, seed_dev);
+                                       out_lp, seed_dev); note_launch();
 }
 
 // One decode step's bookkeeping on the device (so a step needs no host work):
@@ -669,7 +669,7 @@ void decode_advance(const int64_t* tok, const float* lp, int64_t* ids, int32_t* 
   if (rows <= 0) return;
   if (rows > 1024) throw std::runtime_error("decode_advance: at most 1024 rows");
   decode_advance_kernel<<<1, 1024, 0, st>>>(tok, lp, ids, pos, ctx, slots, bt, max_blocks, block_size, win_tok, win_lp,
-                                            win_ld, step, seed, rows);
+                                            win_ld, step, seed, rows); note_launch();
 }
 
 }  // namespace wb

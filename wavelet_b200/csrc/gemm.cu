@@ -806,7 +806,7 @@ static void launch(const GemmArgs& g, cudaStream_t stream) {
       p.split_s = S;
     }
   }
-  kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem, stream>>>(ta, tb, ta2, tb2, p);
+  kern<<<grid, BQ ? NUM_THREADS_Q : NUM_THREADS, smem, stream>>>(ta, tb, ta2, tb2, p); note_launch();
 }
 
 }  // namespace gemm

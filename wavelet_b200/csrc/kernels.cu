@@ -106,18 +106,15 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
-// dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres);  dw += sum_rows dy*xhat.
-// Each CTA owns a contiguous run of rows and accumulates dw in shared memory.
+// dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres).  One warp per row,
+// each CTA a contiguous run of rows.  dw is a separate column pass
+// (rmsnorm_dw_kernel) so that it is summed in a fixed order.
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w,
                                    const float* __restrict__ rstd,
                                    const __nv_bfloat16* __restrict__ dy,
                                    const __nv_bfloat16* __restrict__ dres,
-                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
-                                   int rows, int H, int rows_per_cta) {
-  extern __shared__ float sdw[];
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
-  __syncthreads();
+                                   __nv_bfloat16* __restrict__ dx, int rows, int H, int rows_per_cta) {
   const int warps = blockDim.x >> 5;
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * rows_per_cta;
@@ -129,6 +126,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
     const uint4* dyr = reinterpret_cast<const uint4*>(dy + (int64_t)row * H);
     const float rs = rstd[row];
     float dot = 0.f;
+#pragma unroll 4
     for (int i = lane; i < nv; i += 32) {
       uint4 a = xr[i], g = dyr[i], ww = wr[i];
       const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
@@ -144,37 +142,65 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
     const float mean = dot / H;
     uint4* dxr = reinterpret_cast<uint4*>(dx + (int64_t)row * H);
     const uint4* drr = dres ? reinterpret_cast<const uint4*>(dres + (int64_t)row * H) : nullptr;
+#pragma unroll 4
     for (int i = lane; i < nv; i += 32) {
       uint4 a = xr[i], g = dyr[i], ww = wr[i];
       const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
       const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
       const uint32_t* pw = reinterpret_cast<const uint32_t*>(&ww);
-      uint4 rres;
-      if (drr) rres = drr[i];
+      uint4 rres = drr ? drr[i] : make_uint4(0, 0, 0, 0);
       const uint32_t* pr = reinterpret_cast<const uint32_t*>(&rres);
       uint4 o;
       uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float xh0 = bf16_lo(pa[j]) * rs, xh1 = bf16_hi(pa[j]) * rs;
-        float g0 = bf16_lo(pg[j]), g1 = bf16_hi(pg[j]);
-        float d0 = rs * (bf16_lo(pw[j]) * g0 - xh0 * mean);
-        float d1 = rs * (bf16_hi(pw[j]) * g1 - xh1 * mean);
-        if (drr) {
-          d0 += bf16_lo(pr[j]);
-          d1 += bf16_hi(pr[j]);
-        }
+        const float xh0 = bf16_lo(pa[j]) * rs, xh1 = bf16_hi(pa[j]) * rs;
+        const float d0 = rs * (bf16_lo(pw[j]) * bf16_lo(pg[j]) - xh0 * mean) + bf16_lo(pr[j]);
+        const float d1 = rs * (bf16_hi(pw[j]) * bf16_hi(pg[j]) - xh1 * mean) + bf16_hi(pr[j]);
         po[j] = pack_bf16(d0, d1);
-        const int c = i * 8 + 2 * j;
-        atomicAdd(&sdw[c], g0 * xh0);
-        atomicAdd(&sdw[c + 1], g1 * xh1);
       }
       dxr[i] = o;
     }
   }
-  __syncthreads();
-  if (dw)
-    for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+// part[s, c] = sum over the rows of split s of dy[r, c] * x[r, c] * rstd[r].
+// Thread = 8 consecutive columns, block = 1024 columns, grid.y = row splits.
+__global__ void rmsnorm_dw_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ rstd,
+                                  const __nv_bfloat16* __restrict__ dy, float* __restrict__ part, int rows, int H,
+                                  int rows_per_split) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;  // chunk of 8 columns
+  if (c8 * 8 >= H) return;
+  const int r0 = blockIdx.y * rows_per_split;
+  const int r1 = min(rows, r0 + rows_per_split);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll 4
+  for (int r = r0; r < r1; ++r) {
+    const uint4 a = reinterpret_cast<const uint4*>(x + (int64_t)r * H)[c8];
+    const uint4 g = reinterpret_cast<const uint4*>(dy + (int64_t)r * H)[c8];
+    const float rs = rstd[r];
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] += bf16_lo(pg[j]) * bf16_lo(pa[j]) * rs;
+      acc[2 * j + 1] += bf16_hi(pg[j]) * bf16_hi(pa[j]) * rs;
+    }
+  }
+  float4* dst = reinterpret_cast<float4*>(part + (int64_t)blockIdx.y * H + c8 * 8);
+  dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+// dw[c] += sum_s part[s, c], splits in order (reproducible).
+__global__ void colsum_add_kernel(const float* __restrict__ part, int splits, int H, float* __restrict__ dw) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  float s = 0.f;
+  for (int k = 0; k < splits; ++k) s += part[(int64_t)k * H + c];
+  dw[c] += s;
 }
 
 // ------------------------------------------------------------ QK-norm + RoPE
@@ -698,19 +724,29 @@ void rmsnorm_fwd(const void* x, const void* res, void* h_out, const void* w, voi
   const int threads = 256, warps = threads / 32;
   rmsnorm_fwd_kernel<<<(rows + warps - 1) / warps, threads, 0, st>>>(
       (const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (__nv_bfloat16*)h_out,
-      (const __nv_bfloat16*)w, (__nv_bfloat16*)y, rstd, rows, H, eps);
+      (const __nv_bfloat16*)w, (__nv_bfloat16*)y, rstd, rows, H, eps); note_launch();
 }
 
+int rmsnorm_dw_splits(int rows) { return rows < 64 ? 1 : (rows < 4096 ? rows / 64 : 64); }
+
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres,
-                 void* dx, float* dw, int rows, int H, cudaStream_t st) {
+                 void* dx, float* dw, float* part, int rows, int H, cudaStream_t st) {
   if (H % 8) throw std::runtime_error("rmsnorm: hidden size must be a multiple of 8");
+  if (rows <= 0) return;
   const int threads = 256;
   const int ctas = 148 * 2;
   const int rows_per_cta = (rows + ctas - 1) / ctas;
   const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
-  rmsnorm_bwd_kernel<<<grid, threads, H * sizeof(float), st>>>(
+  rmsnorm_bwd_kernel<<<grid, threads, 0, st>>>(
       (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dy,
-      (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, rows, H, rows_per_cta);
+      (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, rows, H, rows_per_cta); note_launch();
+  if (dw) {
+    const int splits = rmsnorm_dw_splits(rows);
+    const int per = (rows + splits - 1) / splits;
+    rmsnorm_dw_kernel<<<dim3((H / 8 + 127) / 128, splits), 128, 0, st>>>(
+        (const __nv_bfloat16*)x, rstd, (const __nv_bfloat16*)dy, part, rows, H, per); note_launch();
+    colsum_add_kernel<<<(H + 255) / 256, 256, 0, st>>>(part, splits, H, dw); note_launch();
+  }
 }
 
 void qk_norm_rope_fwd(void* qkv, int64_t row_stride, int n_q, int n_k, const int* pos,
@@ -720,7 +756,7 @@ void qk_norm_rope_fwd(void* qkv, int64_t row_stride, int n_q, int n_k, const int
   const int64_t work = (int64_t)tokens * (n_q + n_k);
   qk_norm_rope_fwd_kernel<<<(int)((work + warps - 1) / warps), threads, 0, st>>>(
       (__nv_bfloat16*)qkv, row_stride, n_q, n_k, pos, inv_freq, (const __nv_bfloat16*)q_w,
-      (const __nv_bfloat16*)k_w, rstd, tokens, eps);
+      (const __nv_bfloat16*)k_w, rstd, tokens, eps); note_launch();
 }
 
 void qk_norm_rope_bwd(void* dqkv, int64_t drow_stride, const void* qkv_pre, int64_t row_stride,
@@ -731,31 +767,31 @@ void qk_norm_rope_bwd(void* dqkv, int64_t drow_stride, const void* qkv_pre, int6
   const int64_t work = (int64_t)tokens * (n_q + n_k);
   qk_norm_rope_bwd_kernel<<<(int)((work + warps - 1) / warps), threads, 0, st>>>(
       (__nv_bfloat16*)dqkv, drow_stride, (const __nv_bfloat16*)qkv_pre, row_stride, n_q, n_k, pos,
-      inv_freq, (const __nv_bfloat16*)q_w, (const __nv_bfloat16*)k_w, rstd, dq_w, dk_w, tokens);
+      inv_freq, (const __nv_bfloat16*)q_w, (const __nv_bfloat16*)k_w, rstd, dq_w, dk_w, tokens); note_launch();
 }
 
 void swiglu_fwd(const void* gu, void* h, int64_t rows, int I, cudaStream_t st) {
   if (I % 8) throw std::runtime_error("swiglu: intermediate size must be a multiple of 8");
   swiglu_fwd_kernel<<<grid_for(rows * (I / 8), 256), 256, 0, st>>>((const __nv_bfloat16*)gu,
-                                                                  (__nv_bfloat16*)h, rows, I);
+                                                                  (__nv_bfloat16*)h, rows, I); note_launch();
 }
 
 void swiglu_bwd(const void* gu, const void* dh, void* dgu, int64_t rows, int I, cudaStream_t st) {
   if (I % 8) throw std::runtime_error("swiglu: intermediate size must be a multiple of 8");
   swiglu_bwd_kernel<<<grid_for(rows * (I / 8), 256), 256, 0, st>>>(
-      (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dh, (__nv_bfloat16*)dgu, rows, I);
+      (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dh, (__nv_bfloat16*)dgu, rows, I); note_launch();
 }
 
 void embedding_fwd(const void* table, const int64_t* ids, void* out, int64_t T, int H, int64_t V,
                    cudaStream_t st) {
   embedding_fwd_kernel<<<grid_for(T * (H / 8), 256), 256, 0, st>>>(
-      (const __nv_bfloat16*)table, ids, (__nv_bfloat16*)out, T, H, V);
+      (const __nv_bfloat16*)table, ids, (__nv_bfloat16*)out, T, H, V); note_launch();
 }
 
 void embedding_bwd(const void* dy, const int64_t* ids, float* dtable, int64_t T, int H, int64_t V,
                    cudaStream_t st) {
   embedding_bwd_kernel<<<grid_for(T * (H / 4), 256), 256, 0, st>>>((const __nv_bfloat16*)dy, ids,
-                                                                  dtable, T, H, V);
+                                                                  dtable, T, H, V); note_launch();
 }
 
 void splitk_reduce(const float* ws, int S, int64_t M, int N, void* out, int64_t ldc, const void* bias, const void* res,
@@ -763,7 +799,7 @@ void splitk_reduce(const float* ws, int S, int64_t M, int N, void* out, int64_t 
   if (M <= 0 || N <= 0) return;
   if (N % 4 || ldc % 4 || (res && ldr % 4)) throw std::runtime_error("splitk_reduce: N and strides must be multiples of 4");
   splitk_reduce_kernel<<<grid_for(M * (N / 4), 256, 148 * 8), 256, 0, st>>>(
-      ws, S, M, N, (__nv_bfloat16*)out, ldc, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)res, ldr, alpha);
+      ws, S, M, N, (__nv_bfloat16*)out, ldc, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)res, ldr, alpha); note_launch();
 }
 
 void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,
@@ -774,7 +810,7 @@ void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t nume
   nf4_dequant_kernel<<<grid_for(nblk, 256, 148 * 8), 256, 0, st>>>(
       (const uint4*)codes, absmax, (uint4*)out, nblk, make_float4(lut[0], lut[1], lut[2], lut[3]),
       make_float4(lut[4], lut[5], lut[6], lut[7]), make_float4(lut[8], lut[9], lut[10], lut[11]),
-      make_float4(lut[12], lut[13], lut[14], lut[15]));
+      make_float4(lut[12], lut[13], lut[14], lut[15])); note_launch();
 }
 
 void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,
@@ -782,17 +818,17 @@ void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t
                 const float* gscale_dev, float gscale_host, cudaStream_t st) {
   if (n <= 0) return;
   adamw_kernel<<<grid_for((n + 3) / 4, 256, 148 * 8), 256, 0, st>>>(
-      p, g, m, v, (__nv_bfloat16*)p16, n, lr, b1, b2, eps, wd, bc1, bc2, gscale_dev, gscale_host);
+      p, g, m, v, (__nv_bfloat16*)p16, n, lr, b1, b2, eps, wd, bc1, bc2, gscale_dev, gscale_host); note_launch();
 }
 
 void sumsq(const float* x, int64_t n, float* out, cudaStream_t st) {
   if (n <= 0) return;
   static_assert(148 * 4 <= kMaxSumBlocks, "sumsq grid exceeds the scratch");
-  sumsq_kernel<<<grid_for((n + 3) / 4, 256, 148 * 4), 256, 0, st>>>(x, n, out);
+  sumsq_kernel<<<grid_for((n + 3) / 4, 256, 148 * 4), 256, 0, st>>>(x, n, out); note_launch();
 }
 
 void clip_factor(const float* sumsq_v, float max_norm, float* out, cudaStream_t st) {
-  clip_factor_kernel<<<1, 1, 0, st>>>(sumsq_v, max_norm, out);
+  clip_factor_kernel<<<1, 1, 0, st>>>(sumsq_v, max_norm, out); note_launch();
 }
 
 void softmax_stats(const void* z, int64_t ldz, int rows, int V, const int64_t* target,
@@ -801,7 +837,7 @@ void softmax_stats(const void* z, int64_t ldz, int rows, int V, const int64_t* t
   if ((ldz % 8) || (reinterpret_cast<uintptr_t>(z) & 15))
     throw std::runtime_error("softmax_stats: rows must be 16-byte aligned");
   softmax_stats_kernel<<<rows, 512, 0, st>>>((const __nv_bfloat16*)z, ldz, V, target, inv_tau,
-                                             lse, lp, ent);
+                                             lse, lp, ent); note_launch();
 }
 
 void softmax_grad(void* z, int64_t ldz, int rows, int V, const int64_t* target, float inv_tau,
@@ -811,7 +847,7 @@ void softmax_grad(void* z, int64_t ldz, int rows, int V, const int64_t* target, 
   if ((ldz % 8) || (reinterpret_cast<uintptr_t>(z) & 15))
     throw std::runtime_error("softmax_grad: rows must be 16-byte aligned");
   softmax_grad_kernel<<<rows, 512, 0, st>>>((__nv_bfloat16*)z, ldz, V, target, inv_tau, lse, ent,
-                                            dlp, dent);
+                                            dlp, dent); note_launch();
 }
 
 }  // namespace wb

@@ -7,8 +7,11 @@ namespace wb {
 
 void rmsnorm_fwd(const void* x, const void* res, void* h_out, const void* w, void* y, float* rstd,
                  int rows, int H, float eps, cudaStream_t st);
+// dw (optional, fp32, +=) is reduced through part: fp32 scratch of
+// rmsnorm_dw_splits(rows) x H elements (reproducible order).
+int rmsnorm_dw_splits(int rows);
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres,
-                 void* dx, float* dw, int rows, int H, cudaStream_t st);
+                 void* dx, float* dw, float* part, int rows, int H, cudaStream_t st);
 void qk_norm_rope_fwd(void* qkv, int64_t row_stride, int n_q, int n_k, const int* pos,
                       const float* inv_freq, const void* q_w, const void* k_w, float* rstd,
                       int tokens, float eps, cudaStream_t st);

@@ -2,6 +2,7 @@
 // small runtime queries used by the Python layer.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <stdexcept>
 
@@ -29,6 +30,14 @@ int* error_word(int device) {
   }
   return words[device];
 }
+
+static std::atomic<long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+void note_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int read_error_word(int device) {
   int v = 0;

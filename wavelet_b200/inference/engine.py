@@ -155,6 +155,7 @@ class Generator:
         self.use_graphs = (cuda_graphs and self.dev.type == "cuda" and not any(self._moe) and not model.quant)
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
         self._graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
+        self._graph_kernels: dict[tuple[int, int], int] = {}
         self._graph_pool = None
 
     # ------------------------------------------------------------ utilities
@@ -501,12 +502,16 @@ class Generator:
             g = torch.cuda.CUDAGraph()
             if self._graph_pool is None:
                 self._graph_pool = torch.cuda.graph_pool_handle()
+            m = ops.ext()
+            n0 = m.launch_count()
             with torch.cuda.graph(g, pool=self._graph_pool):
                 self._step_on(b, splits)
+            self._graph_kernels[key] = m.launch_count() - n0  # library kernels inside the graph
             for k, v in saved.items():
                 b[k].copy_(v)
             self._graphs[key] = g
         g.replay()
+        ops.ext().note_launches(self._graph_kernels.get(key, 0))  # replayed kernels count as launches
 
     @torch.no_grad()
     def _decode_window(self, seqs: list[_Seq], seed: int) -> int:

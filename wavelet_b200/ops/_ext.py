@@ -132,45 +132,24 @@ def available() -> bool:
 
 
 # --------------------------------------------------------------------------
-# Launch accounting: while a ``count_launches()`` block is active, every call
-# into the extension is counted (each binding launches one kernel, except
-# ``adamw_step``/``gemm`` which also launch exactly one).  bench.py reports the
-# count of kernels this repository launched inside its timed region.
-_NON_KERNEL = {"read_error", "clear_error"}
-
-
-class _CountingProxy:
-    def __init__(self, mod: ModuleType):
-        self._mod = mod
-        self.count = 0
-
-    def __getattr__(self, name):
-        attr = getattr(self._mod, name)
-        if callable(attr) and name not in _NON_KERNEL:
-            def wrapped(*a, **k):
-                self.count += 1
-                return attr(*a, **k)
-
-            return wrapped
-        return attr
-
-
+# Launch accounting: the library counts every kernel it launches (a counter
+# bumped at each launch site); ``count_launches()`` reports the kernels this
+# repository launched inside the block.  A graph replay adds the number of
+# library kernels recorded when the graph was captured (``note_launches``).
 class count_launches:
-    """Context manager counting extension kernel launches."""
+    """Context manager: ``count`` = kernels this library launched in the block."""
 
     def __enter__(self):
-        global _module
-        base = load()
-        self._base = base
-        self.proxy = _CountingProxy(base)
-        _module = self.proxy  # type: ignore[assignment]
+        self._m = load()
+        self._start = int(self._m.launch_count())
+        self._end = None
         return self
 
     @property
     def count(self) -> int:
-        return self.proxy.count
+        end = self._end if self._end is not None else int(self._m.launch_count())
+        return end - self._start
 
     def __exit__(self, *exc):
-        global _module
-        _module = self._base
+        self._end = int(self._m.launch_count())
         return False
