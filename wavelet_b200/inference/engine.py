@@ -41,6 +41,7 @@ import numpy as np
 import torch
 
 from .. import ops
+from ..utils import nvtx
 from ..models.layers import _lin
 from ..models.qwen import CausalLM
 from ..ops import reference as ref
@@ -398,7 +399,8 @@ class Generator:
                 active += new
                 gen_tokens += len(new)
             elif active and self._fast_ok(active):
-                n = self._decode_window(active, base_seed * 1000003 + step)
+                with nvtx.range("generate.decode_window"):
+                    n = self._decode_window(active, base_seed * 1000003 + step)
                 gen_tokens += n
                 step += self._last_window - 1
                 n_windows += 1

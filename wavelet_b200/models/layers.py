@@ -26,6 +26,7 @@ from typing import Any
 import torch
 
 from .. import ops
+from ..utils import nvtx
 from ..ops.attention import attention_bwd, attention_fwd
 from ..parallel.context_parallel import attention_bwd as cp_attention_bwd
 from ..parallel.context_parallel import attention_fwd as cp_attention_fwd
@@ -226,7 +227,7 @@ class DecoderLayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, layer):
         keep = not getattr(layer, "recompute", True)
-        with torch.no_grad():
+        with torch.no_grad(), nvtx.range(f"layer{layer.index}.fwd"):
             out, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=keep, moe=layer.moe, lora=layer.lora,
                                    tp=layer.tp)
         ctx.cache = cache  # kept activations: the backward skips the recompute
@@ -249,7 +250,7 @@ class DecoderLayerFn(torch.autograd.Function):
         else:
             (x,) = ctx.saved_tensors
         layer = ctx.layer
-        with torch.no_grad():
+        with torch.no_grad(), nvtx.range(f"layer{layer.index}.bwd"):
             cache, ctx.cache = ctx.cache, None
             if cache is None:
                 _, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=True, moe=layer.moe, lora=layer.lora,

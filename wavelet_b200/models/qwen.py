@@ -117,6 +117,7 @@ class _Layer:
     offload: Any = None  # ActivationOffload when activations live in host memory
     recompute: bool = True  # activation checkpointing of this layer
     tp: Any = None  # TPContext under tensor parallelism
+    index: int = 0  # position in the stack (NVTX range names)
 
 
 class CausalLM:
@@ -151,7 +152,7 @@ class CausalLM:
                 P.update({n[len(pre):]: expert_flat.view(n) for n in en})
                 if expert_flat.grad is not None:
                     G.update({n[len(pre):]: expert_flat.grad_view(n) for n in en})
-            layer = _Layer(self.layer_cfg, P, G)
+            layer = _Layer(self.layer_cfg, P, G, index=i)
             if cfg.layer_is_moe(i):
                 from .moe import MoEBlock
 

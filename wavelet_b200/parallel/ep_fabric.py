@@ -34,6 +34,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils import nvtx
 from .fabric import Fabric
 
 PAD = 128
@@ -129,8 +130,9 @@ class FabricEP:
     def dispatch(self, name: str, src: torch.Tensor, p: FabricPlan, scale: torch.Tensor | None = None) -> torch.Tensor:
         """Rows of ``src`` (one per copy, optionally scaled) into every owner's
         ``name`` buffer; returns this rank's received [R, H] view."""
-        ops.ext().rows_scatter(src, p.src_tok, p.dst_rank, p.dst_row, scale, self.ptrs(name), self.ep, self.H)
-        self.fab.barrier()
+        with nvtx.range(f"ep.dispatch.{name}"):
+            ops.ext().rows_scatter(src, p.src_tok, p.dst_rank, p.dst_row, scale, self.ptrs(name), self.ep, self.H)
+            self.fab.barrier()
         out = self.view(name, p.R)
         if p.pad_rows.numel():
             out.index_fill_(0, p.pad_rows, 0)
@@ -140,9 +142,10 @@ class FabricEP:
                 out: torch.Tensor) -> torch.Tensor:
         """out[t] = res[t] + sum_j w[t, j] * owner_rows[copy (t, j)] (after a barrier
         that orders the owners' writes of ``name``)."""
-        self.fab.barrier()
-        ops.ext().rows_gather_sum(self.ptrs(name), self.ep, self.H, p.dst_rank, p.dst_row,
-                                  None if w is None else w.reshape(-1).float().contiguous(), k, res, out)
+        with nvtx.range(f"ep.combine.{name}"):
+            self.fab.barrier()
+            ops.ext().rows_gather_sum(self.ptrs(name), self.ep, self.H, p.dst_rank, p.dst_row,
+                                      None if w is None else w.reshape(-1).float().contiguous(), k, res, out)
         return out
 
     def gather_copies(self, name: str, p: FabricPlan, T: int, k: int) -> torch.Tensor:

@@ -25,6 +25,7 @@ from __future__ import annotations
 import torch
 
 from .. import ops
+from ..utils import nvtx
 from .fabric import Fabric, SharedBuffer
 
 
@@ -55,10 +56,12 @@ class TPFabric:
         buf = self.bufs[self.flip]
         self.flip ^= 1
         m = ops.ext()
-        m.gemm_peer(a.contiguous(), w, b_mn, N, alpha, a2, b2, buf.ptrs, self.rank, self.rank * self.capacity, N, 0)
-        self.fab.barrier()
-        out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
-        m.slots_sum(buf.tensor, self.world, self.capacity, n, None if res is None else res.contiguous(), out)
+        with nvtx.range("tp.gemm_allreduce"):
+            m.gemm_peer(a.contiguous(), w, b_mn, N, alpha, a2, b2, buf.ptrs, self.rank, self.rank * self.capacity, N,
+                        0)
+            self.fab.barrier()
+            out = torch.empty(M, N, device=a.device, dtype=torch.bfloat16)
+            m.slots_sum(buf.tensor, self.world, self.capacity, n, None if res is None else res.contiguous(), out)
         return out
 
     def check(self) -> None:

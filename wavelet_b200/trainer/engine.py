@@ -16,6 +16,7 @@ import torch.distributed as dist
 from ..models.qwen import CausalLM
 from ..ops import lm_head
 from ..parallel.zero import AdamWHyper, CompositeAdamW, FusedShardedAdamW, ShardedAdamW
+from ..utils import nvtx
 
 
 @dataclass
@@ -87,8 +88,11 @@ class Engine:
         ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
         h = m.hidden(b.input_ids, ctx)
         weights = b.loss_mask.float() * token_scale
-        loss, dh = lm_head.sft_loss_and_grad(h.detach(), m.head_weight(), b.targets, weights, m.head_grad(), self.chunk)
-        h.backward(dh)
+        with nvtx.range("lm_head.loss"):
+            loss, dh = lm_head.sft_loss_and_grad(h.detach(), m.head_weight(), b.targets, weights, m.head_grad(),
+                                                 self.chunk)
+        with nvtx.range("backward"):
+            h.backward(dh)
         if not b.input_ids.is_cuda or getattr(m, "eager", False):
             m.collect_cpu_grads()  # autograd gradients -> the fp32 flat gradient store
         return loss
@@ -105,8 +109,9 @@ class Engine:
         return -(lp * valid).sum(), float(valid.sum())
 
     def optimizer_step(self, lr: float) -> dict[str, float]:
-        self.model.finalize_grads()
-        return self.opt.step(lr)
+        with nvtx.range("optimizer.step"):
+            self.model.finalize_grads()
+            return self.opt.step(lr)
 
     def global_token_count(self, local: float, device) -> float:
         if self.dp_world > 1 and dist.is_initialized():
