@@ -6,7 +6,7 @@ Contract (one JSON line from rank 0):
   torchrun --nproc-per-node N bench.py --gpus N ...        (N>1, one rank per GPU)
   python bench.py --impl reference ...                     (reference arm)
 
-Workload (BASELINE config "Qwen2.5-7B-shaped dense SFT"): 28 layers, hidden
+Workload (the headline "Qwen2.5-7B-shaped dense SFT" configuration): 28 layers, hidden
 3584, 28/4 heads x 128, SwiGLU 18944, vocab 152064 untied, RoPE 1e6, random
 N(0, 0.02) init, bf16 compute / fp32 master + AdamW, sequences of 4096 uniform
 random tokens with the loss masked on a random 10-40% prompt prefix.  Weak
@@ -32,7 +32,7 @@ import sys
 import threading
 import time
 
-BASELINE_TOKS = None  # BASELINE.md publishes no number for this config
+BASELINE_TOKS = None  # the reference publishes no number for this configuration
 
 
 def parse():

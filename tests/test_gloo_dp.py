@@ -1,4 +1,4 @@
-"""BASELINE config #1: tiny decoder SFT on CPU/gloo, world_size=2, sharded
+"""Plumbing configuration: tiny decoder SFT on CPU/gloo, world_size=2, sharded
 data parallel (2 layers, hidden 128, 4/2 heads x 32, SwiGLU 512, vocab 1024,
 RMSNorm, RoPE 1e4, fp32, N(0, 0.02) init, batch 8 x 128 seed-generated tokens
 in [3, 1024), loss on the second half of each sequence, AdamW lr 1e-3, 10

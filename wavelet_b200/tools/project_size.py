@@ -24,7 +24,7 @@ from datetime import datetime, timezone
 from pathlib import Path
 
 SUFFIXES = {".py", ".cu", ".cuh", ".cpp", ".h", ".md", ".yaml", ".yml", ".toml", ".json", ".html", ".js", ".css"}
-SKIP = {".git", "__pycache__", ".pytest_cache", ".venv", "outputs", "_build", "_work", "gpurun_out", "baseline"}
+SKIP = {".git", "__pycache__", ".pytest_cache", ".venv", "outputs", "_build", "_work", "baseline"}
 COMMENT = {".py": "#", ".yaml": "#", ".yml": "#", ".toml": "#", ".cu": "//", ".cuh": "//", ".cpp": "//", ".h": "//",
            ".js": "//", ".css": "/*"}
 BRANCHES = (ast.If, ast.For, ast.While, ast.Try, ast.ExceptHandler, ast.With, ast.BoolOp, ast.IfExp, ast.Assert,
