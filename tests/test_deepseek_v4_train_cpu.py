@@ -70,3 +70,26 @@ def test_sft_cli_trains_deepseek_v4(tmp_path):
     rows = [json.loads(line) for line in (out / "metrics.jsonl").read_text().splitlines()]
     assert [x["step"] for x in rows] == [1, 2, 3, 4]
     assert (out / "checkpoint-4" / "STABLE").exists()
+
+
+def test_trainer_checkpoint_converts_to_native(tmp_path):
+    """checkpoint-N of a DeepSeek-V4 SFT run -> native checkpoint whose
+    logits equal the trained model's."""
+    from wavelet_b200.models.deepseek_v4 import DeepseekV4ForCausalLM
+    from wavelet_b200.tools.convert_checkpoint import convert_checkpoint
+    from wavelet_b200.trainer.ckpt import CheckpointManager
+
+    cfg = resolve_arch("tiny-deepseek-v4")
+    m = build_model(cfg, "cpu", torch.float32, seed=9)
+    eng = Engine(m, AdamWHyper(lr=1e-3))
+    with torch.no_grad():  # routing state lives in buffers, outside the flat stores
+        m.module.model.layers[0].mlp.router.tid2eid.copy_(torch.randint(0, 4, (1024, 2)))
+        m.module.model.layers[1].mlp.router.selection_bias.uniform_(-0.1, 0.1)
+    mgr = CheckpointManager(tmp_path / "ckpts", mode="async")
+    d = mgr.save(1, model=m, optimizer=eng.opt, data_state=None, meta={"arch": cfg.to_dict()}, block=True)
+    mgr.wait()
+    out = convert_checkpoint(d, tmp_path / "native", dtype="float32")
+    back = DeepseekV4ForCausalLM.from_pretrained(out).eval()
+    ids = torch.tensor([[5, 6, 7, 8, 9, 10, 11, 12]])
+    with torch.no_grad():
+        torch.testing.assert_close(back(ids).logits, m.module.eval()(ids).logits, atol=1e-6, rtol=1e-6)

@@ -119,6 +119,16 @@ class DeepseekV4Trainable:
         if on:
             raise NotImplementedError("activation offload is not available for the eager DeepSeek-V4 model")
 
+    def extra_state(self) -> dict[str, torch.Tensor]:
+        """Persistent buffers (routing bias, hash table) for trainer checkpoints."""
+        return {n: b for n, b in self.module.named_buffers() if n.endswith(("selection_bias", "tid2eid"))}
+
+    def load_extra_state(self, tensors: dict[str, torch.Tensor]) -> None:
+        with torch.no_grad():
+            for n, t in tensors.items():
+                b = self.module.get_buffer(n)
+                b.copy_(t.to(b.device, b.dtype))
+
     def load_pretrained(self, path: str | Path) -> None:
         """Load a native checkpoint directory into the stores."""
         from safetensors.torch import load_file

@@ -42,6 +42,8 @@ def convert_checkpoint(ckpt: Path, output_dir: Path | None = None, config_path: 
         raise FileNotFoundError(f"{root} is not a stable checkpoint (no STABLE marker)")
     meta = json.loads((root / "meta.json").read_text())
     out = Path(output_dir) if output_dir else root / "weights"
+    if meta.get("arch", {}).get("model_type") == "deepseek_v4":
+        return _convert_deepseek_v4(root, meta, out, DTYPES[dtype])
     if "arch" in meta:
         arch = ArchConfig.from_dict(meta["arch"]) if hasattr(ArchConfig, "from_dict") else ArchConfig(**meta["arch"])
     elif config_path is not None:
@@ -71,6 +73,37 @@ def convert_checkpoint(ckpt: Path, output_dir: Path | None = None, config_path: 
     from ..models.hf_io import save_hf
 
     save_hf(model, out, dtype=DTYPES[dtype], max_shard_bytes=_parse_size(max_shard_size))
+    return out
+
+
+def _convert_deepseek_v4(root: Path, meta: dict, out: Path, dtype: torch.dtype) -> Path:
+    """DeepSeek-V4 checkpoints hold native tensor names in two stores (the
+    compute-dtype store and the fp32 store of the sensitive tensors); the
+    output is a native checkpoint directory (config.json + model.safetensors)
+    that ``DeepseekV4ForCausalLM.from_pretrained`` loads and
+    ``models.deepseek_v4.convert`` turns into the published layout."""
+    from safetensors.torch import load_file
+
+    from ..models.deepseek_v4 import DeepseekV4Config, DeepseekV4ForCausalLM
+
+    cfg = DeepseekV4Config.from_dict(meta["arch"])
+    state = load_file(str(root / "trainer" / "model.safetensors"))
+    for extra in ("experts-ep0.safetensors", "extra.safetensors"):  # fp32 store; routing buffers
+        if (root / "trainer" / extra).exists():
+            state.update(load_file(str(root / "trainer" / extra)))
+    model = DeepseekV4ForCausalLM(cfg, init=False)
+    missing = set(dict(model.named_parameters())) - set(state)
+    if missing:
+        raise ValueError(f"DeepSeek-V4 checkpoint lacks {sorted(missing)[:5]} ...")
+    with torch.no_grad():
+        params, buffers = dict(model.named_parameters()), dict(model.named_buffers())
+        for k, v in state.items():
+            if k in params:
+                params[k].copy_(v.float())
+            elif k in buffers:
+                buffers[k].copy_(v.to(buffers[k].dtype))
+    model.to_compute_dtype(dtype)
+    model.save_pretrained(out)
     return out
 
 

@@ -5,6 +5,8 @@ every rank finished, so a crash never leaves a checkpoint that looks valid):
 
     meta.json                       step, world size, model arch, flat layout hash
     trainer/model.safetensors       full bf16 compute weights (rank 0)
+    trainer/experts-ep<e>.safetensors  expert store of expert-parallel rank e (MoE)
+    trainer/extra.safetensors       model buffers outside the flat stores (routing tables)
     trainer/optim-rank<r>.pt        fp32 master / exp_avg / exp_avg_sq shard of rank r
     trainer/scheduler.json          optimizer step counter and LR state
     dataloader/rank<r>.json         data cursor of rank r
@@ -86,6 +88,9 @@ class CheckpointManager:
         if ef is not None and getattr(model, "ep_dp_rank", 0) == 0:  # one copy per expert shard
             experts = {n: self._host("e:" + n, ef.view(n)) for n in ef.names()}
         ep_rank = getattr(model, "ep_rank", 0)
+        extra = None  # model state outside the flat stores (e.g. routing tables)
+        if self.rank == 0 and hasattr(model, "extra_state"):
+            extra = {n: self._host("x:" + n, t) for n, t in model.extra_state().items()}
         opt = {k: (self._host("o:" + k, v) if torch.is_tensor(v) else v) for k, v in optimizer.state_dict().items()}
         if torch.cuda.is_available():
             torch.cuda.synchronize()
@@ -102,6 +107,8 @@ class CheckpointManager:
                     (d / "trainer" / "scheduler.json").write_text(json.dumps(scheduler_state or {}, indent=2))
                 if experts is not None:
                     _save_safetensors(experts, d / "trainer" / f"experts-ep{ep_rank}.safetensors")
+                if extra:
+                    _save_safetensors(extra, d / "trainer" / "extra.safetensors")
                 torch.save({**opt, "shard_rank": self.rank, "shard_world": self.world}, d / "trainer" / f"optim-rank{self.rank}.pt")
                 if data_state is not None:
                     (d / "dataloader" / f"rank{self.rank}.json").write_text(json.dumps(data_state))
@@ -157,6 +164,8 @@ class CheckpointManager:
         if ef is not None:
             we = load_file(str(d / "trainer" / f"experts-ep{model.ep_rank}.safetensors"))
             ef.load_state({k: v.to(ef.device) for k, v in we.items()})
+        if hasattr(model, "load_extra_state") and (d / "trainer" / "extra.safetensors").exists():
+            model.load_extra_state(load_file(str(d / "trainer" / "extra.safetensors")))
         if optimizer is not None and not skip_optimizer:
             saved_world = int(meta.get("world_size", 1))
             if saved_world == self.world:
