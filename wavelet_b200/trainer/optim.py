@@ -4,13 +4,20 @@
 local fp32 master shard after the gradient reduce-scatter:
 
 * ``adamw`` / ``adam`` — the fused AdamW kernel (``adam`` = no decay);
-* ``sgd`` — momentum SGD (optionally Nesterov) with decoupled decay;
-* ``sign_sgd`` — sign of the gradient times lr (trainer/optim.py:30);
-* ``muon`` — Newton–Schulz orthogonalised momentum for 2-D weights (5
-  quintic iterations on the Gram of the smaller side), AdamW for the rest
-  (trainer/optim.py:67-188).  Muon needs whole matrices, so with data
-  parallelism the rank that owns a matrix's first element updates it from the
-  all-gathered gradient.
+* ``sgd`` — ``torch.optim.SGD`` semantics: L2 decay added to the gradient,
+  momentum, optionally Nesterov (trainer/optim.py:429-437);
+* ``sign_sgd`` — sign of the gradient times lr, decoupled decay
+  (trainer/optim.py:30);
+* ``muon`` — for every weight of two or more dimensions except embeddings and
+  the LM head: EMA momentum, Newton–Schulz orthogonalisation (5 quintic
+  iterations on the Gram of the smaller side, batched over leading dims),
+  rescaled to the gradient's norm; AdamW for the rest; decoupled decay on
+  both (trainer/optim.py:67-188, 402-428).  Muon needs whole matrices while
+  the flat store is sharded over data-parallel ranks, so the momentum
+  source is all-gathered into the (then unused) replicated gradient buffer
+  and each rank orthogonalises every matrix that overlaps its shard; the
+  per-matrix gradient norms are summed over the shards with one small
+  all-reduce.
 * 8-bit variants are served by the fp32 AdamW (bitsandbytes is not part of
   this framework).
 
@@ -59,18 +66,27 @@ def lr_at(step: int, base_lr: float, total_steps: int, sched) -> float:
 
 def newton_schulz5(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
     """Quintic Newton–Schulz iteration towards the orthogonal polar factor
-    (coefficients a, b, c = 3.4445, -4.7750, 2.0315 from the Muon write-up)."""
+    (coefficients a, b, c = 3.4445, -4.7750, 2.0315 from the Muon write-up),
+    over the last two dims; leading dims (stacked experts) are a batch."""
     a, b, c = 3.4445, -4.7750, 2.0315
     x = g.float()
-    transposed = x.shape[0] > x.shape[1]
+    transposed = x.shape[-2] > x.shape[-1]
     if transposed:
-        x = x.t()
-    x = x / (x.norm() + eps)
+        x = x.transpose(-2, -1)
+    shape = x.shape
+    x = x.reshape(-1, shape[-2], shape[-1])
+    x = x / (x.norm(dim=(1, 2), keepdim=True) + eps)
     for _ in range(steps):
-        A = x @ x.t()
+        A = x @ x.transpose(1, 2)
         B = b * A + c * (A @ A)
         x = a * x + B @ x
-    return x.t() if transposed else x
+    x = x.reshape(shape)
+    return x.transpose(-2, -1) if transposed else x
+
+
+def is_muon_matrix(name: str, shape: tuple[int, ...]) -> bool:
+    n = name.lower()
+    return len(shape) >= 2 and "embed" not in n and "lm_head" not in n
 
 
 class FlatOptimizer:
@@ -138,12 +154,13 @@ class FlatOptimizer:
                 p.mul_(1 - lr * wd)
             p.add_(gs.sign(), alpha=-lr)
         elif self.type == "sgd":
-            if self.momentum_buf is None:
-                self.momentum_buf = torch.zeros_like(p)
-            buf = self.momentum_buf.mul_(self.cfg.momentum).add_(gs)
-            upd = gs.add(buf, alpha=self.cfg.momentum) if self.cfg.nesterov else buf
-            if wd > 0:
-                p.mul_(1 - lr * wd)
+            d = gs.add(p, alpha=wd) if wd > 0 else gs
+            if self.momentum_buf is None:  # first step: the buffer is the gradient
+                self.momentum_buf = d.clone()
+            else:
+                self.momentum_buf.mul_(self.cfg.momentum).add_(d)
+            buf = self.momentum_buf
+            upd = d.add(buf, alpha=self.cfg.momentum) if self.cfg.nesterov else buf
             p.add_(upd, alpha=-lr)
         elif self.type == "muon":
             self._muon(gs, lr)
@@ -158,38 +175,54 @@ class FlatOptimizer:
         return {"grad_norm": norm, "clip_factor": factor}
 
     def _muon(self, gs: torch.Tensor, lr: float) -> None:
-        """Muon on 2-D weight shards that lie entirely inside this rank's shard;
-        AdamW-style update on everything else."""
         flat = self.flat
+        beta, wd = self.cfg.muon_momentum, self.cfg.weight_decay
         if self.momentum_buf is None:
             self.momentum_buf = torch.zeros_like(flat.master)
-        mu = self.cfg.muon_momentum
-        buf = self.momentum_buf.mul_(mu).add_(gs)
+        mom = self.momentum_buf.mul_(beta).add_(gs, alpha=1 - beta)
+        src = gs.add(mom, alpha=beta) if self.cfg.nesterov else mom
         lo = flat.dp_rank * flat.shard_numel
         hi = lo + flat.shard_numel
-        handled = torch.zeros(flat.shard_numel, dtype=torch.bool, device=gs.device)
-        for s in flat.specs:
+        mats = [s for s in flat.specs if is_muon_matrix(s.name, s.shape)]
+        spans = []
+        sq = torch.zeros(len(mats), dtype=torch.float64, device=gs.device)
+        for i, s in enumerate(mats):
             off, n = flat.offsets[s.name]
-            if len(s.shape) != 2 or off < lo or off + n > hi or s.name in ("embed", "lm_head"):
+            a, b = max(off, lo), min(off + n, hi)
+            spans.append((off, n, a, b))
+            if a < b:
+                sq[i] = gs[a - lo : b - lo].double().pow(2).sum()
+        if self.world > 1:
+            dist.all_reduce(sq, group=self.group)
+            full = flat.grad  # replicated gradient buffer: free after the reduce-scatter
+            dist.all_gather_into_tensor(full, src.contiguous(), group=self.group)
+        else:
+            full = src
+        gnorm = sq.sqrt().tolist()
+        handled = torch.zeros(flat.shard_numel, dtype=torch.bool, device=gs.device)
+        for s, (off, n, a, b), gn in zip(mats, spans, gnorm):
+            if a >= b:
                 continue
-            a, b = off - lo, off - lo + n
-            u = (gs[a:b] + mu * buf[a:b]) if self.cfg.nesterov else buf[a:b]
-            o = newton_schulz5(u.view(s.shape))
-            scale = max(1.0, s.shape[0] / s.shape[1]) ** 0.5
-            if self.cfg.weight_decay > 0:
-                flat.master[a:b].mul_(1 - lr * self.cfg.weight_decay)
-            flat.master[a:b].add_(o.reshape(-1), alpha=-lr * scale)
-            handled[a:b] = True
+            upd = newton_schulz5(full[off : off + n].view(s.shape)).reshape(-1)
+            upd = upd[a - off : b - off] * (gn / max(float(upd.norm()), 1e-7))
+            seg = flat.master[a - lo : b - lo]
+            if wd > 0:
+                seg.mul_(1 - lr * wd)
+            seg.add_(upd, alpha=-lr)
+            handled[a - lo : b - lo] = True
         rest = ~handled
         if rest.any():
-            m = flat.exp_avg
-            v = flat.exp_avg_sq
+            m, v = flat.exp_avg, flat.exp_avg_sq
             b1, b2 = self.cfg.betas1, self.cfg.betas2
             t = self.adamw.step_count
-            m[rest] = b1 * m[rest] + (1 - b1) * gs[rest]
-            v[rest] = b2 * v[rest] + (1 - b2) * gs[rest] ** 2
-            den = (v[rest] / (1 - b2**t)).sqrt() + 1e-8
-            flat.master[rest] -= lr * (m[rest] / (1 - b1**t)) / den
+            g = gs[rest]
+            m[rest] = b1 * m[rest] + (1 - b1) * g
+            v[rest] = b2 * v[rest] + (1 - b2) * g * g
+            upd = (m[rest] / (1 - b1**t)) / ((v[rest] / (1 - b2**t)).sqrt() + 1e-8)
+            pr = flat.master[rest]
+            if wd > 0:
+                pr = pr * (1 - lr * wd)
+            flat.master[rest] = pr - lr * upd
 
     def state_dict(self) -> dict:
         sd = dict(self.adamw.state_dict())
