@@ -46,7 +46,7 @@ def write_synthetic_run(out: Path, steps: int = 50, ranks: int = 8, seed: int = 
         _jsonl(out / "metrics.jsonl", [{"step": s, "timestamp": _ts(t0, t), "loss": loss,
                                         "optim/grad_norm": 0.5 + rng.random(), "optim/lr": 1e-5,
                                         "perf/tokens_per_second": 2.0e5 * (0.95 + 0.1 * rng.random()),
-                                        "perf/mfu": 0.4 + 0.02 * rng.random(),
+                                        "perf/mfu": 40.0 + 2.0 * rng.random(),
                                         "node/synthetic/tokens_per_second": 2.0e5}])
         _jsonl(out / "orchestrator_metrics.jsonl", [{"step": s - 1, "timestamp": _ts(t0, t - 5), "reward/mean": reward,
                                                      "rollout/tokens_per_second": 5e4 * (0.9 + 0.2 * rng.random()),
