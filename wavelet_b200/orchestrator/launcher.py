@@ -118,7 +118,8 @@ def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executabl
 
 def run_process_launcher(cfg, argv: list[str]) -> int:
     out = Path(cfg.output_dir)
-    pathing.validate_output_dir(out, clean=cfg.clean_output_dir, resuming=cfg.ckpt is not None and cfg.ckpt.is_resuming)
+    pathing.validate_output_dir(out, clean=cfg.clean_output_dir, resuming=cfg.ckpt is not None and cfg.ckpt.is_resuming,
+                                protected_paths=(cfg.model.name, cfg.model.adapter_path))
     attempt = pathing.create_launch_attempt(out)
     pathing.write_launch_artifacts(attempt, command="rl", argv=argv)
     dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(cfg))

@@ -88,7 +88,8 @@ class IntegratedRunner:
         world_rank = int(os.environ.get("RANK", "0"))
         if world_rank == 0:
             resume = c.ckpt is not None and c.ckpt.is_resuming
-            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume)
+            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume,
+                                        protected_paths=(c.model.name, c.model.adapter_path))
             attempt = pathing.create_launch_attempt(out)
             dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(c))
         self.trainer.setup()

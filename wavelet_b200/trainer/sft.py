@@ -134,7 +134,8 @@ class SFTTrainer:
         if c.ckpt is not None:
             resume = pathing.resolve_resume_dir(c.checkpoint_output_dir, c.ckpt.resume_step, c.ckpt.resume_dir)
         if w.rank == 0:
-            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume is not None)
+            pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume is not None,
+                                        protected_paths=(c.model.name, c.model.adapter_path))
             attempt = pathing.create_launch_attempt(out)
             dump_yaml(attempt.config_dir / "sft.yaml", config_to_plain(c))
         if w.distributed:

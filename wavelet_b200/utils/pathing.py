@@ -15,6 +15,7 @@ from __future__ import annotations
 import os
 import shlex
 import shutil
+from collections.abc import Iterable
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -139,13 +140,36 @@ def resolve_resume_dir(output_dir: Path, resume_step: int | None, resume_dir: Pa
     return p
 
 
-def has_run_state(output_dir: Path) -> bool:
+def existing_run_state_entries(output_dir: Path) -> list[str]:
     root = Path(output_dir)
-    return root.exists() and (any((root / n).exists() for n in RUN_STATE_ENTRIES) or bool(list_checkpoint_steps(root, False)))
+    if not root.exists():
+        return []
+    out = [n for n in RUN_STATE_ENTRIES if (root / n).exists() or (root / n).is_symlink()]
+    return out + sorted(p.name for p in root.glob("checkpoint-*"))
+
+
+def has_run_state(output_dir: Path) -> bool:
+    return bool(existing_run_state_entries(output_dir))
+
+
+def _refuse_unsafe_root(root: Path) -> None:
+    """Directories that are clearly not run directories are never cleaned."""
+    reasons = []
+    if root == Path(root.anchor):
+        reasons.append("the filesystem root")
+    if root == Path.home().absolute():
+        reasons.append("the home directory")
+    cwd = Path.cwd().absolute()
+    if cwd == root or cwd.is_relative_to(root):
+        reasons.append("the current working directory or one of its parents")
+    if reasons:
+        raise ValueError(f"clean_output_dir=true refuses to clean '{root}': it is " + " and ".join(reasons)
+                         + ". Point output_dir at a dedicated run directory.")
 
 
 def clean_output_dir(output_dir: Path) -> None:
-    """Remove run state (never the directory itself or unrelated files)."""
+    """Remove the run state; the directory itself goes too when nothing else
+    (unrelated files) is left in it."""
     root = Path(output_dir)
     if not root.exists():
         return
@@ -158,13 +182,34 @@ def clean_output_dir(output_dir: Path) -> None:
     for p in root.glob("checkpoint-*"):
         if p.is_dir():
             shutil.rmtree(p)
+    if root.is_dir() and not any(root.iterdir()):
+        root.rmdir()
 
 
-def validate_output_dir(output_dir: Path, *, clean: bool, resuming: bool) -> None:
+def validate_output_dir(output_dir: Path, *, clean: bool, resuming: bool,
+                        protected_paths: Iterable[Path | str | None] = ()) -> None:
+    """Refuse to overwrite a previous run unless resuming or cleaning
+    (reference utils/pathing.py:186-259): cleaning and resuming exclude each
+    other, cleaning never touches the filesystem root, the home or working
+    directory, nor an input (model, adapter) that lies inside the run."""
+    if clean and resuming:
+        raise ValueError("clean_output_dir=true cannot be used with checkpoint resume. "
+                         "Choose either a clean run or an explicit resume.")
+    if resuming:
+        return
+    root = Path(output_dir).absolute()
     if clean:
+        _refuse_unsafe_root(root)
+        inside = [str(p) for p in protected_paths
+                  if p is not None and Path(p).exists() and Path(p).absolute().is_relative_to(root)]
+        if inside:
+            raise ValueError("clean_output_dir=true would remove required input path(s): " + ", ".join(inside))
         clean_output_dir(output_dir)
         return
-    if has_run_state(output_dir) and not resuming:
+    entries = existing_run_state_entries(output_dir)
+    if entries:
+        preview = ", ".join(entries[:5]) + (", ..." if len(entries) > 5 else "")
         raise FileExistsError(
-            f"{output_dir} already holds run state; pass --clean-output-dir to start over or resume from a checkpoint"
+            f"{output_dir} already contains run state ({preview}); use a fresh output_dir, set "
+            "clean_output_dir=true, or resume from a checkpoint"
         )
