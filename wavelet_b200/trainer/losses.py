@@ -11,8 +11,13 @@ reduction is a vectorised segment sum, with identical semantics:
 * token normalisation (sum / global token count) or sequence normalisation
   (each sequence's mean, summed, / global sequence count) for the RL part;
   CE and ref-KL are token-normalised;
-* metrics are per-sequence masked means averaged over sequences, plus
-  mean / median / std / min / max across sequences.
+* metrics are per-sequence masked means, over the sequences that have
+  tokens of the metric's component, averaged over those sequences, plus
+  mean / median / std / min / max across them.
+
+A ``custom`` RL loss keeps the reference's contract: it is called once per
+sequence span with 1-D inputs and returns a scalar (or per-token) loss and
+scalar (or ``(values, mask)``) metrics.
 """
 
 from __future__ import annotations
@@ -38,7 +43,8 @@ class LossInputs:
 @dataclass
 class LossOutput:
     loss: Tensor  # per-token loss vector [T] (summed by compute_loss)
-    metrics: dict[str, tuple[Tensor, Tensor]] = field(default_factory=dict)  # name -> (values, mask)
+    # name -> (values, mask) for the vectorised losses; a custom loss may give scalars
+    metrics: dict[str, tuple[Tensor, Tensor] | Tensor] = field(default_factory=dict)
 
 
 def _trust_region(inp: LossInputs, cfg, invalid, masked_high, masked_low, teacher_logprobs) -> LossOutput:
@@ -162,6 +168,7 @@ def setup_rl_loss_fn(cfg) -> LossFn:
                 raise TypeError("Custom RL loss must return LossOutput.")
             return out
 
+        custom.per_span = True  # called once per sequence span (trainer/losses.py:433-490)
         return custom
     return {"ipo": lambda i: ipo_loss(i, cfg), "icepop": lambda i: icepop_loss(i, cfg)}.get(
         cfg.type, lambda i: dppo_loss(i, cfg))
@@ -216,10 +223,17 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
     scales = {k: max(float(v), 1.0) for k, v in counts.items()}
     scales.update({k: max(float(v), 1.0) for k, v in (component_scales or {}).items()})
     total = trainer_logprobs.sum() * 0.0
-    metrics_in: dict[str, tuple[Tensor, Tensor]] = {}
+    seq_metrics: list[tuple[str, Tensor, Tensor, Tensor]] = []  # name, values, mask, active sequences
+    span_metrics: dict[str, list[Tensor]] = {}
+
+    def active_of(mask: Tensor) -> Tensor:
+        return seg_sum(mask.float(), seg, n) > 0
 
     rl_mask = loss_mask if rl_weights is None else loss_mask & (rl_weights != 0)
-    if bool(rl_mask.any()):
+    if bool(rl_mask.any()) and getattr(fn, "per_span", False):
+        total = total + _per_span_rl(fn, trainer_logprobs, inference_logprobs, teacher_logprobs, advantages,
+                                     rl_mask, rl_weights, cu_seqlens, cfg.normalization, span_metrics) / scales["rl"]
+    elif bool(rl_mask.any()):
         out = fn(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, rl_mask, rl_weights))
         per = out.loss
         if cfg.normalization == "sequence":
@@ -228,7 +242,8 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
             total = total + (per_seq / cnt).sum() / scales["rl"]
         else:
             total = total + per.sum() / scales["rl"]
-        metrics_in.update(out.metrics)
+        act = active_of(rl_mask)
+        seq_metrics += [(k, v, m, act) for k, (v, m) in out.metrics.items()]
     for name, w, f in (("ce", ce_weights, ce_loss), ("ref_kl", ref_kl_weights, ref_kl_loss)):
         if w is None:
             continue
@@ -236,12 +251,13 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
         if bool(cm.any()):
             out = f(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, cm, w))
             total = total + out.loss.sum() / scales[name]
-            metrics_in.update(out.metrics)
+            act = active_of(cm)
+            seq_metrics += [(k, v, m, act) for k, (v, m) in out.metrics.items()]
 
     metrics: dict[str, float] = {}
-    active = seg_sum(loss_mask.float(), seg, n) > 0
-    for k, (vals, m) in metrics_in.items():
-        per_seq = _seq_means(vals.detach(), m, seg, n, active)
+    per_seq_values = {k: _seq_means(v.detach(), m, seg, n, act) for k, v, m, act in seq_metrics}
+    per_seq_values.update({k: torch.stack(v) for k, v in span_metrics.items()})
+    for k, per_seq in per_seq_values.items():
         if per_seq.numel() == 0:
             continue
         metrics[k] = float(per_seq.mean())
@@ -251,3 +267,30 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
         metrics[f"{k}/min"] = float(per_seq.min())
         metrics[f"{k}/max"] = float(per_seq.max())
     return total, metrics
+
+
+def _per_span_rl(fn: LossFn, tl: Tensor, il: Tensor, teacher: Tensor | None, adv: Tensor, rl_mask: Tensor,
+                 weights: Tensor | None, cu_seqlens: Tensor, normalization: str,
+                 span_metrics: dict[str, list[Tensor]]) -> Tensor:
+    """Sum of a per-span loss over the sequences with RL tokens (each span's
+    loss divided by its token count under sequence normalisation)."""
+    total = tl.sum() * 0.0
+    bounds = cu_seqlens.tolist()
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        m = rl_mask[a:b]
+        if not bool(m.any()):
+            continue
+        out = fn(LossInputs(tl[a:b], il[a:b], None if teacher is None else teacher[a:b], adv[a:b], m,
+                            None if weights is None else weights[a:b]))
+        loss = out.loss if out.loss.dim() == 0 else out.loss.sum()
+        if normalization == "sequence":
+            loss = loss / m.sum().clamp_min(1)
+        total = total + loss
+        for k, v in out.metrics.items():
+            if isinstance(v, tuple):
+                vals, vm = v
+                den = vm.float().sum()
+                v = (torch.where(vm, vals.float(), torch.zeros_like(vals, dtype=torch.float32)).sum()
+                     / den.clamp_min(1.0))
+            span_metrics.setdefault(k, []).append(v.detach().float().reshape(()))
+    return total
