@@ -124,7 +124,7 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         for r, c in zip(records, comps):
             md = dict(r.metadata or {})
             md.update(prompt_ids=c.prompt_ids, completion_ids=c.token_ids, finish_reason=c.finish_reason,
-                      completion_token_count=len(c.token_ids), prompt_token_count=len(c.prompt_ids),
+                      completion_token_count=len(c.token_ids), prompt_token_count=len(c.prompt_ids), input_token_count=len(c.prompt_ids),
                       is_truncated=c.finish_reason == "length", policy_step=self.policy_step)
             text = self.tokenizer.decode(c.token_ids) if self.tokenizer is not None else ""
             out.append(replace(r, input_ids=c.prompt_ids + c.token_ids,

@@ -18,6 +18,7 @@ orchestrator/algorithms.py:39-258 and advantage.py:15-206:
 
 from __future__ import annotations
 
+import hashlib
 import importlib.util
 import math
 import sys
@@ -58,31 +59,35 @@ def _rewards(records: list[RLExample], name: str) -> list[float]:
     return [float(r.reward) for r in records]
 
 
-def _completion_tokens(r: RLExample) -> float:
-    md = r.metadata or {}
-    v = md.get("completion_token_count")
-    if isinstance(v, (int, float)):
-        return float(v)
-    return float(sum(bool(x) for x in r.loss_mask)) if r.loss_mask is not None else 0.0
-
-
 def _md_num(r: RLExample, key: str, default: float = 0.0) -> float:
-    v = (r.metadata or {}).get(key)
-    return float(v) if isinstance(v, (int, float)) else default
+    v = (r.metadata or {}).get(key, default)
+    return float(v) if isinstance(v, (int, float)) and not isinstance(v, bool) else default
+
+
+def _completion_tokens(r: RLExample) -> float:
+    """Metadata count when positive, else the trainable tokens of the record."""
+    v = _md_num(r, "completion_token_count")
+    if v > 0.0 or r.loss_mask is None:
+        return v
+    return float(sum(bool(x) for x in r.loss_mask))
 
 
 def _input_tokens(r: RLExample) -> float:
-    md = r.metadata or {}
-    if isinstance(md.get("prompt_token_count"), (int, float)):
-        return float(md["prompt_token_count"])
-    if r.input_ids is not None and r.loss_mask is not None:
-        return float(sum(1 for x in r.loss_mask if not x))
-    return 0.0
+    for key in ("input_token_count", "prompt_token_count"):
+        v = _md_num(r, key)
+        if v > 0.0:
+            return v
+    if r.input_ids is None:
+        return 0.0
+    return max(float(len(r.input_ids)) - _completion_tokens(r), 0.0)
 
 
 def _is_truncated(r: RLExample) -> bool:
     md = r.metadata or {}
-    return bool(md.get("is_truncated") or md.get("finish_reason") == "length")
+    if "is_truncated" in md:
+        return bool(md["is_truncated"])
+    ro = md.get("rollout")
+    return isinstance(ro, dict) and bool(ro.get("is_truncated"))
 
 
 def center(values: list[float]) -> list[float]:
@@ -91,16 +96,23 @@ def center(values: list[float]) -> list[float]:
 
 
 def efficiency_shaped(rewards: list[float], costs: list[float]) -> list[float]:
-    """Among equal-reward rollouts prefer cheaper ones: centred reward minus a
-    cost term normalised within the group and scaled by the reward spread."""
-    adv = center(rewards)
-    if not costs or max(costs) == min(costs):
-        return adv
-    cmean = sum(costs) / len(costs)
-    cspan = max(costs) - min(costs)
-    rspan = max(rewards) - min(rewards)
-    scale = 0.5 * (rspan if rspan > 0 else 1.0) * (1.0 if any(r > 0 for r in rewards) else 0.0)
-    return [a - scale * (c - cmean) / cspan for a, c in zip(adv, costs)]
+    """Among the best-reward rollouts, the cheaper ones earn a bonus: each
+    is scaled by 1 + clamp(1 - cost / mean cost of the best, 0, 1); the
+    shaped rewards are then centred (orchestrator/advantage.py:126-149).
+    Groups without a positive reward, or whose best rollouts cost nothing,
+    are only centred."""
+    if len(rewards) != len(costs):
+        raise ValueError("rewards and costs must have the same length")
+    best = max(rewards)
+    if best <= 0:
+        return center(rewards)
+    top = [r >= best for r in rewards]
+    top_costs = [c for c, t in zip(costs, top) if t]
+    mean_cost = sum(top_costs) / len(top_costs)
+    if mean_cost <= 0:
+        return center(rewards)
+    return center([r * (1.0 + min(max(1.0 - c / mean_cost, 0.0), 1.0)) if t else r
+                   for r, c, t in zip(rewards, costs, top)])
 
 
 def group_reward_advantages(rewards: list[float], *, costs: list[float] | None = None, normalize: bool = False,
@@ -165,33 +177,64 @@ class DistillAlgorithm(BaseAlgorithm):
 
 
 # ------------------------------------------------------------------ custom
-_REGISTRY: dict[str, Callable[..., Algorithm]] = {}
+_NAME_ATTR = "_wavelet_b200_algorithm_name"
 
 
 def register_algorithm(name: str):
-    """Decorator for user files: ``@register_algorithm("mine")`` on a factory
-    or class that accepts ``**kwargs`` (custom_algorithms.py:19-130)."""
+    """Decorator for user files: ``@register_algorithm("mine")`` names a class
+    or factory (called with the config's ``kwargs``) within its own file
+    (orchestrator/custom_algorithms.py:19-130 of the reference).  Names are
+    file-local: two files may both define "mine"."""
+    if not name.strip():
+        raise ValueError("Custom algorithm registration name must not be empty.")
+    if name != name.strip():
+        raise ValueError("Custom algorithm registration name must not have surrounding whitespace.")
 
     def deco(obj):
-        _REGISTRY[name] = obj
+        setattr(obj, _NAME_ATTR, name)
         return obj
 
     return deco
 
 
-def load_custom_algorithm(file: Path, name: str, kwargs: dict[str, Any]) -> Algorithm:
-    file = Path(file)
-    mod_name = f"_wavelet_custom_algo_{abs(hash(str(file.resolve())))}"
-    if mod_name not in sys.modules:
-        spec = importlib.util.spec_from_file_location(mod_name, file)
-        if spec is None or spec.loader is None:
-            raise ImportError(f"cannot import custom algorithm file {file}")
-        mod = importlib.util.module_from_spec(spec)
-        sys.modules[mod_name] = mod
+def _load_module(path: Path):
+    mod_name = "_wavelet_b200_custom_algorithm_" + hashlib.sha256(str(path).encode()).hexdigest()[:16]
+    spec = importlib.util.spec_from_file_location(mod_name, path)
+    if spec is None or spec.loader is None:
+        raise ImportError(f"cannot import custom algorithm file {path}")
+    mod = importlib.util.module_from_spec(spec)
+    previous = sys.modules.get(mod_name)
+    sys.modules[mod_name] = mod
+    try:
         spec.loader.exec_module(mod)
-    if name not in _REGISTRY:
-        raise KeyError(f"algorithm {name!r} is not registered by {file} (registered: {sorted(_REGISTRY)})")
-    return _REGISTRY[name](**kwargs)
+    except Exception:
+        if previous is None:
+            sys.modules.pop(mod_name, None)
+        else:
+            sys.modules[mod_name] = previous
+        raise
+    return mod
+
+
+def load_custom_algorithm(file: Path | str, name: str, kwargs: dict[str, Any] | None = None) -> Algorithm:
+    """Import ``file`` (relative paths from the working directory), find the
+    object registered as ``name`` (else the module attribute of that name),
+    call it with ``kwargs`` and check that both hooks exist."""
+    path = Path(file).expanduser().resolve()
+    if not path.is_file():
+        raise ValueError(f"Custom algorithm file does not exist: {path}")
+    mod = _load_module(path)
+    named = [v for v in vars(mod).values() if getattr(v, _NAME_ATTR, None) == name]
+    if len(named) > 1:
+        raise ValueError(f"Custom algorithm name {name!r} is registered more than once in {path}")
+    factory = named[0] if named else getattr(mod, name, None)
+    if not callable(factory):
+        raise TypeError(f"Custom algorithm {name!r} is not callable in {path}")
+    algo = factory(**(kwargs or {}))
+    missing = [h for h in ("score_rollout", "score_group") if not callable(getattr(algo, h, None))]
+    if missing:
+        raise TypeError(f"Custom algorithm {name!r} from {path} is missing callable hooks: {', '.join(missing)}.")
+    return algo
 
 
 # ------------------------------------------------------------------ factory
@@ -220,6 +263,16 @@ def algorithm_scope(cfg) -> str:
     return "group" if cfg.type in ("grpo", "max_rl") else "rollout"
 
 
+def uses_group_advantages(cfg) -> bool:
+    """Whether scoring needs complete rollout groups."""
+    return algorithm_scope(cfg) in ("group", "both")
+
+
+def algorithm_loss_component(cfg) -> str:
+    """The token-loss component an algorithm's records train."""
+    return {"sft": "ce", "opd": "ref_kl", "opsd": "ref_kl"}.get(cfg.type, "rl")
+
+
 def algorithm_epsilon(cfg) -> float:
     return getattr(cfg, "epsilon", 1e-6)
 
@@ -229,6 +282,8 @@ def score_records(algo: Algorithm, records: list[RLExample], scope: str,
     out = list(records)
     if scope in ("rollout", "both"):
         out = [algo.score_rollout(r) for r in out]
+        if not all(isinstance(r, RLExample) for r in out):
+            raise TypeError("score_rollout must return RLExample")
     if scope == "rollout" or not out:
         return out
     if scope == "group" and all(r.advantage is not None for r in out):
@@ -237,9 +292,9 @@ def score_records(algo: Algorithm, records: list[RLExample], scope: str,
     for i, r in enumerate(out):
         groups.setdefault(group_key(r) if group_key else 0, []).append(i)
     for idx in groups.values():
-        res = algo.score_group([out[i] for i in idx])
-        if len(res) != len(idx):
-            raise ValueError("score_group must return one record per input record")
+        res = list(algo.score_group([out[i] for i in idx]))
+        if len(res) != len(idx) or not all(isinstance(r, RLExample) for r in res):
+            raise ValueError("score_group must return one RLExample for every input record")
         for i, r in zip(idx, res):
             out[i] = r
     return out

@@ -97,7 +97,7 @@ class RLOrchestrator:
             md = dict(p.metadata)
             md.update(prompt_ids=p.prompt_ids, completion_ids=c.token_ids, finish_reason=c.finish_reason,
                       is_truncated=c.finish_reason == "length", completion_token_count=len(c.token_ids),
-                      prompt_token_count=len(p.prompt_ids), group=f"{step}:{c.prompt_index}",
+                      prompt_token_count=len(p.prompt_ids), input_token_count=len(p.prompt_ids), group=f"{step}:{c.prompt_index}",
                       sample_index=c.sample_index, example_id=p.example_id)
             recs.append(RLExample(prompt=p.prompt, completion=[], advantage=None, reward=None, input_ids=ids,
                                   loss_mask=mask, target_completion=p.target_completion,
