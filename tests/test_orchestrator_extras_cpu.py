@@ -39,7 +39,7 @@ def test_standard_and_difficulty_samplers_resume():
     again.load_state_dict(sd)
     assert [again.next_index() for _ in range(10)] == [sampler.next_index() for _ in range(10)]
     g = gates["adv"]
-    assert not g.admit([0.0, 0.0]) and g.admit([0.5, -0.5]) and g.metrics()["reject_rate"] == 0.5
+    assert not g.admit([0.0, 0.0]) and g.admit([0.5, -0.5]) and g.metrics()["admission_rate"] == 0.5
 
 
 def test_adaptive_concurrency_and_admission():

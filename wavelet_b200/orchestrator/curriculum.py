@@ -12,6 +12,13 @@ Gates (applied after a whole group is scored):
 * ``AdvRangeGate`` — reject a group whose advantages all lie in
   [reject_min, reject_max] (e.g. all zero: no learning signal).
 All state round-trips through ``state_dict`` / ``load_state_dict``.
+
+``Curriculum`` composes one sampler with named gates: the prompt source asks
+it for the next record index (and its ``record:<i>`` task key), the
+orchestrator reports each scored group back through ``on_result``, which
+feeds the sampler and returns whether every gate admits the group.  Group
+outputs are ``{"reward": r, "advantage": a}`` dicts (``a`` a number or a
+per-token list) or plain numbers.
 """
 
 from __future__ import annotations
@@ -19,6 +26,25 @@ from __future__ import annotations
 import math
 import random
 from typing import Any, Iterable, Mapping
+
+
+def _rewards(outputs) -> list[float]:
+    out = []
+    for o in outputs:
+        r = o.get("reward") if isinstance(o, Mapping) else o
+        if r is not None and math.isfinite(float(r)):
+            out.append(float(r))
+    return out
+
+
+def _advantages(outputs) -> list[float]:
+    out = []
+    for o in outputs:
+        a = o.get("advantage") if isinstance(o, Mapping) else o
+        if a is None:
+            continue
+        out.extend(float(x) for x in (a if isinstance(a, (list, tuple)) else [a]) if x is not None)
+    return out
 
 
 class StandardSampler:
@@ -84,9 +110,16 @@ class DifficultyPoolSampler:
         self.selections += 1
         return self.rng.choices(range(self.n), weights=w, k=1)[0]
 
-    def observe(self, task_key, rewards: Iterable[float]) -> None:
+    @property
+    def task_rewards(self) -> dict[str, float]:
+        return {f"record:{k}": v for k, v in sorted(self.ema.items())}
+
+    def task_pool(self, task_key: str) -> str | None:
+        return self.pool_of(int(str(task_key).rsplit(":", 1)[-1]))
+
+    def observe(self, task_key, rewards: Iterable) -> None:
         idx = int(str(task_key).rsplit(":", 1)[-1])
-        vals = [float(r) for r in rewards if r is not None and math.isfinite(float(r))]
+        vals = _rewards(rewards)
         if not vals:
             return
         m = sum(vals) / len(vals)
@@ -122,8 +155,9 @@ class AdvRangeGate:
         self.admitted = 0
         self.rejected = 0
 
-    def admit(self, advantages: Iterable[float | None]) -> bool:
-        adv = [float(a) for a in advantages if a is not None]
+    def admit(self, outputs: Iterable) -> bool:
+        """False when every advantage of the group lies in [reject_min, reject_max]."""
+        adv = _advantages(outputs)
         ok = not adv or not all(self.cfg.reject_min <= a <= self.cfg.reject_max for a in adv)
         if ok:
             self.admitted += 1
@@ -140,7 +174,7 @@ class AdvRangeGate:
     def metrics(self) -> dict[str, float]:
         tot = self.admitted + self.rejected
         return {"admitted": float(self.admitted), "rejected": float(self.rejected),
-                "reject_rate": self.rejected / tot if tot else 0.0}
+                "admission_rate": self.admitted / tot if tot else 1.0}
 
 
 def build_curriculum(cfg, task_count: int, seed: int = 0, shuffle: bool = True):
@@ -151,3 +185,37 @@ def build_curriculum(cfg, task_count: int, seed: int = 0, shuffle: bool = True):
         sampler = DifficultyPoolSampler(cfg.sampler, task_count)
     gates = {name: AdvRangeGate(g) for name, g in (cfg.gates.items() if cfg is not None else [])}
     return sampler, gates
+
+
+class Curriculum:
+    """Sampler + gates with one checkpointable state (reference
+    orchestrator/curriculum.py: ``Curriculum``)."""
+
+    def __init__(self, cfg, task_count: int, data_seed: int = 0, shuffle: bool = True):
+        self.sampler, self.gates = build_curriculum(cfg, task_count, data_seed, shuffle)
+
+    def next_record_index(self) -> tuple[int, str]:
+        i = self.sampler.next_index()
+        return i, f"record:{i}"
+
+    def on_result(self, task_key: str, outputs: list) -> bool:
+        self.sampler.observe(task_key, outputs)
+        ok = True
+        for g in self.gates.values():  # every gate sees (and counts) the group
+            ok = g.admit(outputs) and ok
+        return ok
+
+    def state_dict(self) -> dict[str, Any]:
+        return {"sampler": self.sampler.state_dict(), "gates": {k: g.state_dict() for k, g in self.gates.items()}}
+
+    def load_state_dict(self, sd: Mapping[str, Any]) -> None:
+        self.sampler.load_state_dict(sd["sampler"])
+        for k, g in self.gates.items():
+            if k in sd.get("gates", {}):
+                g.load_state_dict(sd["gates"][k])
+
+    def metrics(self) -> dict[str, float]:
+        m = {f"sampler/{k}": v for k, v in self.sampler.metrics().items()}
+        for name, g in self.gates.items():
+            m.update({f"gate/{name}/{k}": v for k, v in g.metrics().items()})
+        return m

@@ -131,23 +131,47 @@ class RLOrchestrator:
                 keep += g
         return keep, dropped
 
+    def _curriculum_gate(self, recs: list[RLExample]) -> tuple[list[RLExample], int]:
+        """Report each scored group to the prompt source's curriculum (sampler
+        EMA + gates) and keep the admitted groups."""
+        cur = getattr(self.prompts, "curriculum", None)
+        if cur is None:
+            return recs, 0
+        groups: dict[Any, list[RLExample]] = {}
+        for r in recs:
+            groups.setdefault((r.metadata or {}).get("group"), []).append(r)
+        keep, rejected = [], 0
+        for g in groups.values():
+            key = (g[0].metadata or {}).get("task_key")
+            if key is None:
+                keep += g
+                continue
+            if cur.on_result(key, [{"reward": r.reward, "advantage": r.advantage} for r in g]):
+                keep += g
+            else:
+                rejected += len(g)
+        self.last_stats.update({f"curriculum/{k}": v for k, v in cur.metrics().items()})
+        return keep, rejected
+
     def materialize(self, step: int) -> list[RLExample]:
         o = self.cfg.orchestrator
         n_prompts = o.examples_per_step or 1
         prompts = self.prompts.take(n_prompts)
         recs = self.score(self.custom_rollout(prompts, step) if self.custom_rollout else self.generate_records(prompts, step))
+        recs, gated = self._curriculum_gate(recs)
         kept, dropped = self._filter_zero(recs)
         retries = 0
         while (o.refill_zero_advantage and dropped and retries < o.zero_advantage_max_retries
                and len(kept) < len(recs)):
             need = max(1, dropped // max(1, o.rollouts_per_example or 1))
-            more = self.score(self.generate_records(self.prompts.take(need), step))
+            more, _ = self._curriculum_gate(self.score(self.generate_records(self.prompts.take(need), step)))
             more_kept, dropped = self._filter_zero(more)
             kept += more_kept
             retries += 1
         if not kept:
             kept = recs  # never publish an empty batch; zero-advantage rows contribute no gradient
         rewards = [float(r.reward or 0.0) for r in recs]
+        self.last_stats["rollout/curriculum_rejected"] = float(gated)
         self.last_stats.update({"reward/mean": sum(rewards) / max(1, len(rewards)),
                                 "rollout/zero_advantage_dropped": float(dropped),
                                 "rollout/zero_advantage_retries": float(retries)})

@@ -60,6 +60,13 @@ class FilePromptSource:
         self.model_name = cfg.model.name
         self.epoch = 0
         self.cursor = 0
+        # orchestrator.curriculum: the sampler picks every prompt; gates admit scored groups
+        cur = getattr(getattr(cfg, "orchestrator", None), "curriculum", None)
+        self.curriculum = None
+        if cur is not None:
+            from .curriculum import Curriculum
+
+            self.curriculum = Curriculum(cur, len(self.rows), self.seed, self.shuffle)
 
     def _tokenizer(self):
         if self.tok is None:
@@ -95,6 +102,13 @@ class FilePromptSource:
 
     def take(self, n: int) -> list[PromptRecord]:
         out = []
+        if self.curriculum is not None:
+            for _ in range(n):
+                i, key = self.curriculum.next_record_index()
+                rec = self._record(i)
+                rec.metadata["task_key"] = key
+                out.append(rec)
+            return out
         order = self._order()
         while len(out) < n:
             if self.cursor >= len(order):
@@ -106,10 +120,15 @@ class FilePromptSource:
         return out
 
     def state_dict(self) -> dict:
-        return {"epoch": self.epoch, "cursor": self.cursor}
+        sd = {"epoch": self.epoch, "cursor": self.cursor}
+        if self.curriculum is not None:
+            sd["curriculum"] = self.curriculum.state_dict()
+        return sd
 
     def load_state_dict(self, sd: dict) -> None:
         self.epoch, self.cursor = int(sd["epoch"]), int(sd["cursor"])
+        if self.curriculum is not None and "curriculum" in sd:
+            self.curriculum.load_state_dict(sd["curriculum"])
 
 
 class EnvironmentPromptSource:
