@@ -21,7 +21,8 @@ local fp32 master shard after the gradient reduce-scatter:
 * 8-bit variants are served by the fp32 AdamW (bitsandbytes is not part of
   this framework).
 
-Schedules: constant, linear, cosine, sqrt with warmup (trainer/optim.py:513-832).
+Schedules: constant, linear, cosine, sqrt with warmup, as closed forms of
+the reference's torch scheduler chains (trainer/optim.py:513-832).
 """
 
 from __future__ import annotations
@@ -38,30 +39,62 @@ from ..parallel.zero import AdamWHyper, NonFiniteGradientError, ShardedAdamW
 
 
 def lr_at(step: int, base_lr: float, total_steps: int, sched) -> float:
-    """LR for optimizer step ``step`` (0-based) under a SchedulerConfig."""
-    warm = sched.warmup_steps if sched.warmup_steps is not None else int(round(sched.warmup_ratio * total_steps))
-    min_lr = sched.min_lr
+    """LR of optimizer step ``step`` (0-based): the closed form of the
+    reference's torch scheduler chains (trainer/optim.py:513-832) after
+    ``step`` scheduler steps.
+
+    * floor factor f = min_lr_factor, else min_lr / lr, else 1e-8;
+    * warmup over W steps (warmup_steps, else int(T * warmup_ratio)): the
+      factor rises linearly from f at step 0 to 1 at step W;
+    * constant: 1 after warmup;
+    * linear: hold 1 until the last D steps (D = decay_steps, else
+      int(T * decay_ratio) - W, clamped to [1, T - W]), then fall linearly to
+      f over D - 1 steps;
+    * cosine: cosine from 1 to the floor over min(T - 1 - W, D) steps after
+      warmup, then stay at the floor;
+    * sqrt: hold, then f + (1 - f) * sqrt(1 - t) over the last D of the
+      T - 1 - W post-warmup steps.
+    """
+    T = total_steps
+    if T <= 0:
+        raise ValueError("the LR schedule needs total_steps > 0")
+    W = sched.warmup_steps if sched.warmup_steps is not None else int(T * sched.warmup_ratio)
+    D = sched.decay_steps if sched.decay_steps is not None else max(int(T * sched.decay_ratio) - W, 1)
     if sched.min_lr_factor is not None:
-        min_lr = base_lr * sched.min_lr_factor
-    if warm > 0 and step < warm:
-        return base_lr * (step + 1) / warm
+        f = sched.min_lr_factor
+    else:
+        f = sched.min_lr / base_lr if sched.min_lr > 0.0 else 1e-8
+    k = step
+    if sched.type != "cosine":  # the constant, linear and sqrt chains clamp warmup to the run
+        W = min(W, T)
+    if W > 0 and k < W:
+        return base_lr * (f + (1.0 - f) * k / W)
+    t = k - W  # steps since warmup ended
     if sched.type == "constant":
         return base_lr
-    decay_total = sched.decay_steps if sched.decay_steps is not None else max(1, int(round((total_steps - warm) * sched.decay_ratio)))
-    decay_start = total_steps - decay_total if sched.decay_steps is None else warm
-    decay_start = max(decay_start, warm)
-    if step < decay_start:
-        return base_lr
-    t = min(1.0, (step - decay_start + 1) / max(1, decay_total))
+    eff = max(T - 1, 1)
     if sched.type == "linear":
-        f = 1.0 - t
-    elif sched.type == "cosine":
-        f = 0.5 * (1.0 + math.cos(math.pi * t))
-    elif sched.type == "sqrt":
-        f = 1.0 - math.sqrt(t)
-    else:
-        raise ValueError(f"unknown scheduler {sched.type}")
-    return min_lr + (base_lr - min_lr) * f
+        D = max(min(D, eff), 1)
+        if T - W > 0:
+            D = min(D, T - W)
+        start = min(T - D, eff)
+        if start < W or k < start:
+            return base_lr
+        n = max(D - 1, 1)
+        return base_lr * (1.0 + (f - 1.0) * min(k - start, n) / n)
+    if sched.type == "cosine":
+        span = min(max(eff - W, 1), D)
+        floor = max(sched.min_lr, f * base_lr)
+        t = min(t, span)
+        return floor + (base_lr - floor) * (1.0 + math.cos(math.pi * t / span)) / 2.0
+    if sched.type == "sqrt":
+        post = max(T - W - 1, 1)
+        span = min(max(D, 1), post)
+        d = t - (post - span)
+        if d <= 0:
+            return base_lr
+        return base_lr * (f + (1.0 - f) * math.sqrt(max(1.0 - min(d / span, 1.0), 0.0)))
+    raise ValueError(f"unknown scheduler type {sched.type!r}")
 
 
 def newton_schulz5(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
