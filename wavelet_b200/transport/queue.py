@@ -217,6 +217,8 @@ class FileSystemRolloutReceiver:
         self.queue_dir = resolve_queue_dir(output_dir, cfg)
         self.next_step = start_step
         self.consumer_id = consumer_id or process_identity("rl-trainer")
+        self._floor = start_step  # batches below the resume point are never taken
+        self._received: set[int] = set()
 
     def _batch(self, step: int) -> RolloutBatch | None:
         d = step_dir(self.queue_dir, step)
@@ -229,21 +231,26 @@ class FileSystemRolloutReceiver:
                           self.cfg.idle_timeout_seconds, f"rollout step {self.next_step}")
         append_event(self.output_dir / "events", "rollout_received", queue_step=b.step, consumer_id=self.consumer_id,
                      details={"wait_seconds": waited, "mode": "exact"})
+        self._received.add(b.step)
         self.next_step += 1
         return b
 
     def wait_available(self) -> RolloutBatch:
-        """Block until any unconsumed stable batch >= next_step exists; take the oldest."""
+        """Block until a stable batch this receiver has not taken (and nobody
+        consumed) exists, then take the oldest: a step published late, below
+        ``next_step``, is still picked up; ``next_step`` never moves back."""
         def find():
             for s in stable_steps(self.queue_dir):
-                if s >= self.next_step and not (step_dir(self.queue_dir, s) / CONSUMED).exists():
+                if (s >= self._floor and s not in self._received
+                        and not (step_dir(self.queue_dir, s) / CONSUMED).exists()):
                     return self._batch(s)
             return None
 
         b, waited = _poll(find, self.cfg.poll_interval_seconds, self.cfg.idle_timeout_seconds, "any rollout batch")
         append_event(self.output_dir / "events", "rollout_received", queue_step=b.step, consumer_id=self.consumer_id,
                      details={"wait_seconds": waited, "mode": "available"})
-        self.next_step = b.step + 1
+        self._received.add(b.step)
+        self.next_step = max(self.next_step, b.step + 1)
         return b
 
     def claim(self, b: RolloutBatch, trainer_step: int) -> None:
