@@ -158,3 +158,12 @@ output_dir: {tmp_path / 'out'}
     rows = [json.loads(l) for l in (tmp_path / "out" / "metrics.jsonl").read_text().splitlines()]
     assert [x["step"] for x in rows] == [1, 2, 3]
     assert "reward/mean" in rows[0] and "rollout/tokens_per_second" in rows[0]
+
+
+def test_mixed_sampling_temperatures_pack_apart():
+    exs = [RLExample([], [], 1.0, 1.0, input_ids=list(range(6)), loss_mask=[False] * 3 + [True] * 3,
+                     temperatures=t) for t in (0.7, 1.0, 0.7, 1.0, 1.0)]
+    batches = make_rank_batches(exs, 64, 0, 1)
+    temps = sorted(b.temperature for b in batches if b.num_samples)
+    assert temps == [0.7, 1.0]  # one bin per temperature, no mixing
+    assert sum(b.num_samples for b in batches) == 5

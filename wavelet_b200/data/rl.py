@@ -227,6 +227,13 @@ def make_rank_batches(examples: list[RLExample], seq_len: int, dp_rank: int, dp_
                       default_temperature: float = 1.0) -> list[RLPackedBatch]:
     samples = [sample_from_example(e, default_temperature) for e in examples]
     lengths = [s.input_ids.numel() for s in samples]
-    bins = pack_ffd(lengths, seq_len)
+    # the LM-head kernels take one temperature per micro-batch: rollouts sampled
+    # at different temperatures (per-environment sampling) are packed apart
+    by_temp: dict[float, list[int]] = {}
+    for i, smp in enumerate(samples):
+        by_temp.setdefault(float(smp.temperature), []).append(i)
+    bins = []
+    for idx in by_temp.values():
+        bins += [[idx[j] for j in b] for b in pack_ffd([lengths[i] for i in idx], seq_len)]
     mine = distribute_bins(bins, lengths, dp_world)[dp_rank]
     return [collate([samples[i] for i in b]) for b in mine]
