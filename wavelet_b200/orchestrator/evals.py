@@ -40,6 +40,33 @@ def pass_at_k(n: int, c: int, k: int) -> float:
     return 1.0 - math.prod(1.0 - k / i for i in range(n - c + 1, n + 1))
 
 
+def pass_hat_k(n: int, c: int, k: int) -> float:
+    """pass^k: probability that k draws without replacement all succeed."""
+    return math.comb(c, k) / math.comb(n, k) if k <= n else 0.0
+
+
+def group_metrics(prefix: str, by_example: dict[str, list[float | None]], threshold: float = 1.0) -> dict[str, float]:
+    """avg@n, pass@k and pass^k for k = 1, 2, 4, ... <= n (averaged over
+    examples), reward mean and failed (reward-less) rollouts, as the
+    reference reports them (orchestrator/eval_utils.py)."""
+    groups = list(by_example.values())
+    n = min((len(v) for v in groups), default=0)
+    rewards = [float(x) for v in groups for x in v if x is not None]
+    m = {f"{prefix}/num_examples": float(len(groups)),
+         f"{prefix}/failed_rollouts": float(sum(x is None for v in groups for x in v)),
+         f"{prefix}/reward_mean": sum(rewards) / max(1, len(rewards))}
+    if n == 0:
+        return m
+    m[f"{prefix}/avg@{n}"] = sum(float(x or 0.0) for v in groups for x in v[:n]) / (n * len(groups))
+    k = 1
+    while k <= n:
+        succ = [sum(x is not None and float(x) >= threshold for x in v[:n]) for v in groups]
+        m[f"{prefix}/pass@{k}"] = sum(pass_at_k(n, c, k) for c in succ) / len(groups)
+        m[f"{prefix}/pass^{k}"] = sum(pass_hat_k(n, c, k) for c in succ) / len(groups)
+        k *= 2
+    return m
+
+
 def _native(env_id: str) -> bool:
     from .. import environments
 
@@ -92,14 +119,15 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
     scorer = RLRewardScorer(reward_cfg)
     recs = [replace(r, reward=scorer.score(r)) for r in recs]
     thr = float((env.args or {}).get("success_threshold", 1.0))
-    by_ex: dict[str, list[float]] = {}
+    by_ex: dict[str, list[float | None]] = {}
     for r in recs:
-        by_ex.setdefault(str((r.metadata or {}).get("example_id")), []).append(float(r.reward or 0.0))
-    rewards = [x for v in by_ex.values() for x in v]
-    m = {f"eval/{env.resolved_name}/reward_mean": sum(rewards) / max(1, len(rewards)),
-         f"eval/{env.resolved_name}/pass@1": sum(pass_at_k(len(v), sum(x >= thr for x in v), 1) for v in by_ex.values()) / max(1, len(by_ex)),
-         f"eval/{env.resolved_name}/pass@{k}": sum(pass_at_k(len(v), sum(x >= thr for x in v), k) for v in by_ex.values()) / max(1, len(by_ex)),
-         f"eval/{env.resolved_name}/num_examples": float(len(by_ex))}
+        by_ex.setdefault(str((r.metadata or {}).get("example_id")), []).append(r.reward)
+    m = group_metrics(f"eval/{env.resolved_name}", by_ex, thr)
+    if k > 1 and f"eval/{env.resolved_name}/pass@{k}" not in m:  # a k that is not a power of two
+        n = min(len(v) for v in by_ex.values())
+        m[f"eval/{env.resolved_name}/pass@{k}"] = sum(
+            pass_at_k(n, sum(x is not None and float(x) >= thr for x in v[:n]), min(k, n)) for v in by_ex.values()
+        ) / max(1, len(by_ex))
     d = out_dir / "evals" / env.resolved_name
     d.mkdir(parents=True, exist_ok=True)
     with (d / f"step-{step}.jsonl").open("w") as f:
