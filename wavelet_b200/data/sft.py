@@ -8,7 +8,8 @@ Sources (``data.source``):
   ``fake_input_ids``), no tokenizer needed.
 
 Records are prompt/completion pairs or chat ``messages``; the loss mask is set
-per message role by ``data.loss_mask`` (assistant only by default).  Packing:
+per message role by ``data.loss_mask`` (assistant only by default), and off
+for any message with ``step_loss_mask: 0``.  Packing:
 ``pad`` (one example per row, right padding) or ``cat`` (examples concatenated
 into ``seq_len`` windows with sequence boundaries kept in ``cu_seqlens`` so
 attention never crosses examples).
@@ -127,6 +128,14 @@ def _role_trainable(role: str, lm) -> bool:
     return bool(getattr(lm, role, False)) if role in ("system", "user", "assistant", "tool") else False
 
 
+def _trainable(m: dict[str, Any], lm) -> int:
+    """The role's ``data.loss_mask`` setting, switched off for a message whose
+    ``step_loss_mask`` is 0 (e.g. an intermediate tool-calling turn)."""
+    if not _role_trainable(m["role"], lm):
+        return 0
+    return 0 if m.get("step_loss_mask", 1) in (0, False) else 1
+
+
 def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
     """Tokenise message by message so every token knows its role.
 
@@ -139,10 +148,11 @@ def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
     if hasattr(tok, "render_message"):
         for m in msgs:
             t = tok.encode(tok.render_message(m["role"], str(m.get("content") or "")))
+            head = len(tok.encode(tok.role_header(m["role"])))
             ids += t
-            mask += [1 if _role_trainable(m["role"], cfg.loss_mask) else 0] * len(t)
+            mask += [0] * head + [_trainable(m, cfg.loss_mask)] * (len(t) - head)  # the role tag is never trained
         ids.append(tok.eos_token_id)
-        mask.append(1 if _role_trainable(msgs[-1]["role"], cfg.loss_mask) else 0)
+        mask.append(_trainable(msgs[-1], cfg.loss_mask))
         return Sample(ids, mask)
     prev: list[int] = []
     for i, m in enumerate(msgs):
@@ -158,8 +168,17 @@ def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
             mask = mask[:common]
             prev = prev[:common]
         new = cur[len(prev):]
+        head = 0
+        if m["role"] == "assistant" and _trainable(m, cfg.loss_mask):
+            # the generation prompt (assistant header) belongs to the context, not the completion
+            gen = tok.apply_chat_template(msgs[:i], tokenize=True, add_generation_prompt=True) if i else []
+            if hasattr(gen, "input_ids"):
+                gen = gen["input_ids"]
+            gen = list(gen)
+            if len(gen) >= len(prev) and gen[: len(prev)] == prev and cur[: len(gen)] == gen:
+                head = len(gen) - len(prev)
         ids += new
-        mask += [1 if _role_trainable(m["role"], cfg.loss_mask) else 0] * len(new)
+        mask += [0] * head + [_trainable(m, cfg.loss_mask)] * (len(new) - head)
         prev = cur
     return Sample(ids, mask)
 

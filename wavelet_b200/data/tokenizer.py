@@ -34,8 +34,11 @@ class CharTokenizer:
     def __call__(self, text: str, add_special_tokens: bool = False, **_: Any) -> dict[str, list[int]]:
         return {"input_ids": self.encode(text, add_special_tokens)}
 
+    def role_header(self, role: str) -> str:
+        return self.ROLE_TAGS.get(role, "<|" + role + "|>")
+
     def render_message(self, role: str, content: str) -> str:
-        return f"{self.ROLE_TAGS.get(role, '<|' + role + '|>')}{content}\n"
+        return f"{self.role_header(role)}{content}\n"
 
     def apply_chat_template(self, messages: list[dict[str, Any]], tokenize: bool = False,
                             add_generation_prompt: bool = False, **_: Any):
