@@ -9,6 +9,8 @@ Cases:
   attention         varlen causal attention forward + backward
   gemm              dense tcgen05 GEMM (forward / dgrad / wgrad layouts)
   nf4-gemm          NF4-B GEMM (in-kernel dequantisation, small M)
+  lm-head           chunked LM-head cross-entropy forward + backward (logit
+                    GEMM, softmax stats, in-place dL/dz, dgrad and fp32 wgrad)
   generate          the native generator end to end (prefill + decode)
 """
 
@@ -122,7 +124,25 @@ def generate(a) -> dict:
             "new_tokens": a.new_tokens, "seconds": dt, "tokens/s": n / dt, **gen.stats}
 
 
-CASES = {"decode-attention": decode_attention, "attention": attention, "gemm": gemm, "nf4-gemm": nf4_gemm,
+def lm_head(a) -> dict:
+    """Whole-vocabulary CE of ``--m`` tokens (hidden ``--k``, vocabulary
+    ``--n``): three GEMMs of 2*T*H*V FLOPs plus two row passes over the bf16
+    logit chunk; the [T, V] logits are never held whole."""
+    from ..ops import lm_head as lmh
+
+    T, H, V = a.m, a.k, a.n
+    h = (torch.randn(T, H, device="cuda") * 0.5).bfloat16()
+    W = (torch.randn(V, H, device="cuda") * 0.02).bfloat16()
+    gW = torch.zeros(V, H, device="cuda")
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    wts = torch.full((T,), 1.0 / T, device="cuda")
+    ms = _time(lambda: lmh.sft_loss_and_grad(h, W, tgt, wts, gW, chunk=a.chunk), a.iters)
+    flops = 3 * 2.0 * T * H * V
+    return {"case": "lm-head", "tokens": T, "hidden": H, "vocab": V, "chunk": a.chunk, "ms": ms,
+            "tflops": flops / (ms * 1e9)}
+
+
+CASES = {"lm-head": lm_head, "decode-attention": decode_attention, "attention": attention, "gemm": gemm, "nf4-gemm": nf4_gemm,
          "generate": generate}
 
 
@@ -142,6 +162,7 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--samples", type=int, default=8)
     p.add_argument("--new-tokens", type=int, default=256)
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--chunk", type=int, default=4096, help="lm-head token chunk")
     a = p.parse_args(sys.argv[1:] if argv is None else argv)
     from ..ops import _ext
 
