@@ -52,3 +52,21 @@ def test_hf_style_template_masks_the_generation_prompt():
     s = tokenize_messages([{"role": "user", "content": "hi"}, {"role": "assistant", "content": "ok"}], Templated(),
                           SimpleNamespace(loss_mask=LossMaskConfig()))
     assert [t for t, m in zip(s.input_ids, s.loss_mask) if m] == [ord("o"), ord("k"), 9]
+
+
+def test_cat_packing_resume_keeps_the_pending_sample():
+    from wavelet_b200.configs.config import SFTConfig
+    from wavelet_b200.data.sft import SFTDataset
+
+    cfg = SFTConfig.model_validate({"data": {"source": "fake", "seq_len": 64, "micro_batch_size": 1,
+                                             "pack_function": "cat", "fake_length": "variable",
+                                             "max_examples": 12, "batch_size": 1}}).data
+    a = SFTDataset(cfg, seed=3)
+    for _ in range(3):
+        a.next_micro_batch()
+    sd = a.state_dict()
+    b = SFTDataset(cfg, seed=3)
+    b.load_state_dict(sd)
+    for _ in range(4):
+        x, y = a.next_micro_batch(), b.next_micro_batch()
+        assert x.input_ids.tolist() == y.input_ids.tolist()

@@ -256,6 +256,7 @@ class SFTDataset:
             self.state.cursor += 1
             if (self.state.cursor - 1) % self.dp_world == self.dp_rank:
                 s = self.samples()[i]
+                self._last_index = i
                 self.state.num_samples[s.source] = self.state.num_samples.get(s.source, 0) + 1
                 self.state.num_tokens[s.source] = self.state.num_tokens.get(s.source, 0) + len(s.input_ids)
                 return s
@@ -270,11 +271,18 @@ class SFTDataset:
             budget = S * c.micro_batch_size
             used = 0
             while used < budget:
-                s = self._pending if getattr(self, "_pending", None) else self._next_sample()
-                self._pending = None
+                # a sample that did not fit the previous window opens this one; it is
+                # already past the cursor, so the state carries its index (resume)
+                pend = getattr(self, "_pending_index", None)
+                if pend is not None:
+                    s, idx = self.samples()[pend], pend
+                else:
+                    s = self._next_sample()
+                    idx = self._last_index
+                self._pending_index = None
                 take = min(len(s.input_ids), budget - used)
                 if take < len(s.input_ids) and used > 0:
-                    self._pending = s  # start the next window with it
+                    self._pending_index = idx
                     break
                 seqs.append(torch.tensor(s.input_ids[:take]))
                 masks.append(torch.tensor(s.loss_mask[:take], dtype=torch.float32))
@@ -301,11 +309,12 @@ class SFTDataset:
 
     def state_dict(self) -> dict[str, Any]:
         return {"epoch": self.state.epoch, "cursor": self.state.cursor, "num_samples": dict(self.state.num_samples),
-                "num_tokens": dict(self.state.num_tokens)}
+                "num_tokens": dict(self.state.num_tokens), "pending": getattr(self, "_pending_index", None)}
 
     def load_state_dict(self, sd: dict[str, Any]) -> None:
         self.state = SFTDataState(int(sd["epoch"]), int(sd["cursor"]), dict(sd.get("num_samples", {})),
                                   dict(sd.get("num_tokens", {})))
+        self._pending_index = sd.get("pending")
 
 
 def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor]) -> PackedBatch:
