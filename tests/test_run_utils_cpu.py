@@ -199,3 +199,14 @@ def test_phase_timer_is_inert_without_cuda():
     t.start("forward")
     t.stop("forward")
     assert t.read() == {} or torch.cuda.is_available()
+
+
+def test_emit_perf_line_shape(monkeypatch, capsys):
+    from wavelet_b200.monitor import emit_perf
+
+    monkeypatch.delenv("WAVELET_PERF_LOG", raising=False)
+    emit_perf("example", step=2)
+    assert capsys.readouterr().out == ""
+    monkeypatch.setenv("WAVELET_PERF_LOG", "1")
+    emit_perf("example", step=2, seconds=0.125, mode="async")
+    assert capsys.readouterr().out == "WAVELET_PERF example step=2 seconds=0.125 mode=async\n"

@@ -30,6 +30,20 @@ from typing import Any, Iterable
 SECRET_HINTS = ("api_key", "apikey", "token", "secret", "password", "env_vars")
 
 
+def perf_enabled() -> bool:
+    """``WAVELET_PERF_LOG=1`` turns on ``WAVELET_PERF`` timing lines on stdout."""
+    return os.environ.get("WAVELET_PERF_LOG", "").lower() in {"1", "true", "yes", "on"}
+
+
+def emit_perf(event: str, *, force: bool = False, **fields: object) -> None:
+    """One grep-able line, ``WAVELET_PERF <event> key=value ...`` (floats to
+    3 decimals), the line shape of the reference's monitor.py:263-279."""
+    if not (force or perf_enabled()):
+        return
+    vals = " ".join(f"{k}={v:.3f}" if isinstance(v, float) else f"{k}={v}" for k, v in fields.items())
+    print(f"WAVELET_PERF {event}" + (f" {vals}" if vals else ""), flush=True)
+
+
 def utc_now() -> str:
     return _dt.datetime.now(_dt.timezone.utc).isoformat()
 

@@ -19,6 +19,7 @@ from typing import Any, Callable, Iterator
 import torch
 
 from ..data.rl import RLExample, example_to_payload
+from ..monitor import emit_perf
 from ..transport.queue import FileSystemRolloutSender
 from .algorithms import algorithm_epsilon, algorithm_scope, build_algorithm, score_records
 from .reward import RLRewardScorer
@@ -178,7 +179,9 @@ class RLOrchestrator:
         return kept
 
     def publish(self, step: int, policy_step: int | None = None) -> Any:
+        t0 = time.perf_counter()
         recs = self.materialize(step)
+        emit_perf("rollout_materialized", step=step, seconds=time.perf_counter() - t0, rows=len(recs))
         rows = [example_to_payload(r) for r in recs]
         tokens = sum(len(r.input_ids or []) for r in recs)
         if self.sender is None:

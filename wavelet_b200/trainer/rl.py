@@ -27,7 +27,7 @@ from ..configs.config import RLConfig
 from ..data.rl import RLExample, example_from_payload, make_rank_batches
 from ..models.config import resolve_arch
 from ..models.qwen import build_model
-from ..monitor import RunMonitor, setup_logger
+from ..monitor import RunMonitor, emit_perf, setup_logger
 from ..ops import lm_head
 from ..parallel.dist import Groups, ParallelDims, destroy_distributed, init_distributed
 from ..transport.policy import PolicyExporter
@@ -185,7 +185,9 @@ class RLTrainer:
         metrics.update({"loss": float(lt), "optim/grad_norm": st["grad_norm"], "optim/lr": lr,
                         "train/rl_units": scales["rl"], "train/num_samples": float(len(examples)),
                         "train/tokens": float(tokens)})
-        metrics.update(self.perf.step_metrics(tokens * self.dp_world, time.perf_counter() - t0, c.data.seq_len))
+        dt = time.perf_counter() - t0
+        metrics.update(self.perf.step_metrics(tokens * self.dp_world, dt, c.data.seq_len))
+        emit_perf("trainer_step", step=self.step, seconds=dt, tokens=tokens)
         return metrics
 
     def _logprobs(self, h, tgt, b):
