@@ -133,3 +133,19 @@ def test_muon_two_ranks_match_one():
     for r in range(world):
         for n in ref:
             torch.testing.assert_close(got[r][n], ref[n], rtol=1e-5, atol=1e-6, msg=f"rank {r} {n}")
+
+
+@pytest.mark.parametrize("kind", ["adamw", "sgd", "muon"])
+def test_finite_gradients_with_overflowing_norm_abort_before_update(kind):
+    from wavelet_b200.parallel.zero import NonFiniteGradientError
+
+    flat = FlatParams(SPECS, "cpu", torch.float32)
+    flat.init_(seed=3)
+    flat.sync_master_from_compute()
+    before = flat.master.clone()
+    opt = FlatOptimizer(flat, OptimizerConfig(type=kind, lr=0.1), max_grad_norm=1.0)
+    flat.grad.fill_(1e30)  # every element finite; the squared norm is not
+    with pytest.raises(NonFiniteGradientError):
+        opt.step(0.1)
+    assert torch.equal(flat.master, before)
+    assert opt.step_count == 0

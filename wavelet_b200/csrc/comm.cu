@@ -93,6 +93,7 @@ __global__ void norm_exchange_kernel(PeerPtrs pads, int rank, int world, uint32_
     b += ld_relaxed_sys(mvals + 2 * t + 1);
   }
   if (!ok) b = 1.f;  // a missing peer: treat as non-finite so no rank updates from a partial norm
+  if (!isfinite(s)) b += 1.f;  // finite gradients whose squared norm overflows: skip the step as well
   float factor = 1.f;
   if (max_norm > 0.f) factor = fminf(1.f, max_norm / (sqrtf(s) + 1e-6f));
   tot[0] = s;

@@ -22,6 +22,8 @@ reduce-scatter + ``torch.optim.AdamW`` (fused) + ``clip_grad_norm_`` path
 
 from __future__ import annotations
 
+import math
+
 from dataclasses import dataclass
 
 import torch
@@ -144,6 +146,7 @@ class ShardedAdamW:
         if self.world > 1:
             dist.all_reduce(stats, group=self.group)
         norm_sq, bad = stats.tolist()
+        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
         if check_finite and bad > 0:
             self.flat.zero_grad()
             raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
@@ -264,6 +267,7 @@ class CompositeAdamW:
         if self.distributed:
             dist.all_reduce(total, group=self.norm_group)
         norm_sq, bad = total.tolist()
+        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
         if check_finite and bad > 0:
             for p in self.parts:
                 p.flat.zero_grad()

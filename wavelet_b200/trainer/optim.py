@@ -174,6 +174,7 @@ class FlatOptimizer:
         if self.world > 1:
             dist.all_reduce(a.stats, group=self.group)
         norm_sq, bad = a.stats.tolist()
+        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
         if bad > 0:
             raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
         norm = norm_sq**0.5
