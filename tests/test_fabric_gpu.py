@@ -101,6 +101,24 @@ def test_fused_step_world1_matches_nccl_path(cuda_ext):
     fab.close()
 
 
+def test_fused_step_skips_an_overflowing_norm(cuda_ext):
+    from wavelet_b200.models.config import PRESETS
+    from wavelet_b200.models.qwen import build_model
+    from wavelet_b200.parallel.fabric import Fabric
+    from wavelet_b200.parallel.zero import AdamWHyper, FusedShardedAdamW, NonFiniteGradientError
+
+    fab = Fabric(0, 1, torch.device("cuda", 0))
+    a = build_model(PRESETS["tiny-gpu"], "cuda", torch.bfloat16, seed=3, fabric=fab)
+    opt = FusedShardedAdamW(a.flat, AdamWHyper(lr=1e-3, max_grad_norm=1.0), fab)
+    master, compute = a.flat.master.clone(), a.flat.compute.clone()
+    a.flat.grad.fill_(1e30)  # finite elements, fp32 sum of squares overflows
+    with pytest.raises(NonFiniteGradientError):
+        opt.step()
+    assert torch.equal(a.flat.master, master) and torch.equal(a.flat.compute, compute)
+    assert opt.step_count == 0
+    fab.close()
+
+
 def _two_rank_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import datetime
