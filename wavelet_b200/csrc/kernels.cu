@@ -507,62 +507,81 @@ __global__ void clip_factor_kernel(const float* __restrict__ sumsq, float max_no
 // For each row of z (bf16 logits, temperature tau): lse of z/tau, the target
 // log-prob z_t/tau - lse and the entropy lse - sum p * z/tau.  One CTA per row,
 // single pass with per-thread online (max, sum, weighted-sum) merged at the end.
+// The running values live in the base-2 domain (v = z * log2(e) / tau), so every
+// exponential is one ex2 of a difference; the max of each 8-logit load is taken on
+// packed bf16 pairs (order is kept by the positive scale); two 16-byte loads per
+// thread are in flight.  Results are converted back to natural-log units.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void stats_accum8(const uint4& a, float c, float& m, float& s, float& w) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162 mx = __hmax2(__hmax2(p[0], p[1]), __hmax2(p[2], p[3]));
+  const float lm = fmaxf(__low2float(mx), __high2float(mx)) * c;
+  if (lm > m) {
+    const float sc = ex2_approx(m - lm);  // m = -inf on the first load: sc = 0, s = w = 0
+    s *= sc;
+    w *= sc;
+    m = lm;
+  }
+  const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float v0 = bf16_lo(pa[j]) * c, v1 = bf16_hi(pa[j]) * c;
+    const float e0 = ex2_approx(v0 - m), e1 = ex2_approx(v1 - m);
+    s += e0 + e1;
+    w = fmaf(e0, v0, fmaf(e1, v1, w));
+  }
+}
+
+__device__ __forceinline__ void stats_merge(float& m, float& s, float& w, float m2, float s2, float w2) {
+  const float mm = fmaxf(m, m2);
+  const float a = (m == -INFINITY) ? 0.f : ex2_approx(m - mm);
+  const float b = (m2 == -INFINITY) ? 0.f : ex2_approx(m2 - mm);
+  s = s * a + s2 * b;
+  w = w * a + w2 * b;
+  m = mm;
+}
+
 __global__ void softmax_stats_kernel(const __nv_bfloat16* __restrict__ z, int64_t ldz, int V,
                                      const int64_t* __restrict__ target, float inv_tau,
                                      float* __restrict__ lse_out, float* __restrict__ lp_out,
                                      float* __restrict__ ent_out) {
+  constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
   __shared__ float sm[32], ss[32], sw[32];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* zr = z + row * ldz;
+  const float c = inv_tau * kLog2e;
   float m = -INFINITY, s = 0.f, w = 0.f;
   const int nv = V >> 3;
-  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-    uint4 a = reinterpret_cast<const uint4*>(zr)[i];
-    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
-    float vals[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) vals[2 * j] = bf16_lo(pa[j]) * inv_tau, vals[2 * j + 1] = bf16_hi(pa[j]) * inv_tau;
-    float lm = vals[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, vals[j]);
-    if (lm > m) {
-      const float sc = __expf(m - lm);
-      s *= sc;
-      w *= sc;
-      m = lm;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float e = __expf(vals[j] - m);
-      s += e;
-      w += e * vals[j];
-    }
+  const uint4* zv = reinterpret_cast<const uint4*>(zr);
+  for (int i = threadIdx.x; i < nv; i += 2 * blockDim.x) {
+    const int i2 = i + blockDim.x;
+    const uint4 a = zv[i];
+    uint4 b = a;
+    if (i2 < nv) b = zv[i2];
+    stats_accum8(a, c, m, s, w);
+    if (i2 < nv) stats_accum8(b, c, m, s, w);
   }
   for (int i = (nv << 3) + threadIdx.x; i < V; i += blockDim.x) {
-    const float val = __bfloat162float(zr[i]) * inv_tau;
-    if (val > m) {
-      const float sc = __expf(m - val);
+    const float v = __bfloat162float(zr[i]) * c;
+    if (v > m) {
+      const float sc = ex2_approx(m - v);
       s *= sc;
       w *= sc;
-      m = val;
+      m = v;
     }
-    const float e = __expf(val - m);
+    const float e = ex2_approx(v - m);
     s += e;
-    w += e * val;
+    w = fmaf(e, v, w);
   }
-  // warp merge
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float w2 = __shfl_xor_sync(0xffffffffu, w, o);
-    const float mm = fmaxf(m, m2);
-    const float a = (m == -INFINITY) ? 0.f : __expf(m - mm);
-    const float b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
-    s = s * a + s2 * b;
-    w = w * a + w2 * b;
-    m = mm;
-  }
+  for (int o = 16; o > 0; o >>= 1)
+    stats_merge(m, s, w, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+                __shfl_xor_sync(0xffffffffu, w, o));
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) sm[wid] = m, ss[wid] = s, sw[wid] = w;
   __syncthreads();
@@ -572,21 +591,13 @@ __global__ void softmax_stats_kernel(const __nv_bfloat16* __restrict__ z, int64_
     s = lane < nw ? ss[lane] : 0.f;
     w = lane < nw ? sw[lane] : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      const float w2 = __shfl_xor_sync(0xffffffffu, w, o);
-      const float mm = fmaxf(m, m2);
-      const float a = (m == -INFINITY) ? 0.f : __expf(m - mm);
-      const float b = (m2 == -INFINITY) ? 0.f : __expf(m2 - mm);
-      s = s * a + s2 * b;
-      w = w * a + w2 * b;
-      m = mm;
-    }
+    for (int o = 16; o > 0; o >>= 1)
+      stats_merge(m, s, w, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+                  __shfl_xor_sync(0xffffffffu, w, o));
     if (lane == 0) {
-      const float lse = m + __logf(s);
+      const float lse = m * kLn2 + __logf(s);  // sum_j e^(z_j/tau) = 2^m * s
       lse_out[row] = lse;
-      if (ent_out) ent_out[row] = lse - w / s;
+      if (ent_out) ent_out[row] = lse - (w / s) * kLn2;
       if (lp_out) {
         int64_t t = target ? target[row] : -1;
         lp_out[row] = (t >= 0 && t < V) ? __bfloat162float(zr[t]) * inv_tau - lse : 0.f;

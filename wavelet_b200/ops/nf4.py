@@ -20,6 +20,9 @@ the kernel (csrc/gemm.cu, NF4 B operand).
 
 from __future__ import annotations
 
+import dataclasses
+import itertools
+
 from dataclasses import dataclass
 from functools import lru_cache
 from statistics import NormalDist
@@ -40,6 +43,9 @@ def nf4_table() -> tuple[float, ...]:
     return tuple(v / top for v in vals)
 
 
+_NF4_UIDS = itertools.count()
+
+
 @dataclass
 class NF4Weight:
     codes: torch.Tensor  # uint8 [rows * cols / 2]
@@ -47,6 +53,9 @@ class NF4Weight:
     rows: int
     cols: int
     version: int = 0  # bumped whenever codes/absmax change (invalidates dequant caches)
+    # process-unique serial for cache keys: id() is reused once an object is freed,
+    # so a new weight could otherwise hit a dead weight's cached dequantisation
+    uid: int = dataclasses.field(default_factory=lambda: next(_NF4_UIDS), compare=False)
 
     @property
     def shape(self) -> tuple[int, int]:
@@ -107,7 +116,7 @@ class DequantCache:
         self.pool: list[torch.Tensor] = []
 
     def get(self, q: NF4Weight) -> torch.Tensor:
-        key = (id(q), q.version)
+        key = (q.uid, q.version)
         n = q.rows * q.cols
         for i, (k, t) in enumerate(self.entries):
             if k == key:
