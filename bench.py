@@ -52,23 +52,36 @@ def parse():
                         "grpo-4b: Qwen3-4B-shape GRPO step (native generator + trainer, integrated)")
     p.add_argument("--activation-checkpointing", default="none", choices=["none", "full"],
                    help="none: keep every layer's activations (no recompute); full: recompute each layer in backward")
+    p.add_argument("--tp", type=int, default=None,
+                   help="tensor-parallel degree (default: 2 at 8 GPUs, the headline dp4xtp2 layout; else 1)")
+    p.add_argument("--ref-attn", default="auto",
+                   help="reference arm: model.attn_implementation (the reference's default 'auto' picks FA2 here)")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
                    help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
     return p.parse_args()
 
 
 def reference_arm(args):
-    reason = (
-        "reference build unavailable: its build backend (hatchling) is not installed and there is no "
-        "offline wheel for it, so `pip install --no-index --find-links /opt/wheelhouse` of the reference fails; "
-        "it also pins torch>=2.13 and vllm>=0.28 (image has torch 2.11, vllm 0.22)"
-    )
-    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if os.path.isdir(os.path.join(ref_dir, "wavelet")):
-        reason = "reference installed but the reference arm runner is not implemented"
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
-    return 0
+    """Runs the stock reference trainer from ``baseline/_ref`` (see
+    ``baseline/reference_sft.py``); prints the same JSON line with
+    ``"impl": "reference"``, or an ``unavailable`` line with the real reason."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(here, "baseline"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.workload != "sft":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                f"reference arm for workload {args.workload!r} not run: the reference's RL path needs vLLM>=0.28 "
+                "(image has 0.22) and its QLoRA path needs peft + bitsandbytes (neither installed)")}), flush=True)
+        return 0
+    try:
+        import reference_sft
+    except Exception as exc:  # the real error, not a canned reason
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": f"import failed: {type(exc).__name__}: {exc}"}),
+                  flush=True)
+        return 0
+    return reference_sft.run(args, ClockSampler)
 
 
 class ClockSampler:
@@ -212,6 +225,8 @@ def rl_main(args):
 
 def main():
     args = parse()
+    if args.tp is None:
+        args.tp = 2 if (args.gpus == 8 and args.workload == "sft") else 1
     if args.impl == "reference":
         return reference_arm(args)
     if args.workload == "grpo-4b":
