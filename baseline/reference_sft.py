@@ -267,7 +267,20 @@ def run(args, clock_sampler_cls) -> int:
         dump_yaml(get_config_dir(config.output_dir) / "sft.yaml", config.model_dump(mode="json", exclude_none=True))
     setup_config_logger("sft", config)
     trainer = SFTTrainer(config)
-    trainer.setup()
+    try:
+        trainer.setup()
+    except Exception as exc:  # a blocker inside the stock path: report it, do not mask it
+        import traceback
+
+        tb = traceback.extract_tb(exc.__traceback__)
+        where = f"{tb[-1].filename}:{tb[-1].lineno}" if tb else "?"
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                f"stock SFTTrainer.setup() failed at {where}: {type(exc).__name__}: {exc}")[:600],
+                "config": {"parallelism": f"dp{dp}" + (f"xtp{tp}" if tp > 1 else "")}}), flush=True)
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        return 0
     _reinit_parameters(trainer.model, seed=1234)
     h2d = _batch_bytes(trainer) * trainer.accumulation_steps
     dev = trainer.world.device

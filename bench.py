@@ -53,7 +53,7 @@ def parse():
     p.add_argument("--activation-checkpointing", default="none", choices=["none", "full"],
                    help="none: keep every layer's activations (no recompute); full: recompute each layer in backward")
     p.add_argument("--tp", type=int, default=None,
-                   help="tensor-parallel degree (default: 2 at 8 GPUs, the headline dp4xtp2 layout; else 1)")
+                   help="tensor-parallel degree (default 1: data parallel over every GPU; 2 at 8 GPUs = dp4xtp2)")
     p.add_argument("--ref-attn", default="auto",
                    help="reference arm: model.attn_implementation (the reference's default 'auto' picks FA2 here)")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
@@ -223,10 +223,78 @@ def rl_main(args):
     return 0
 
 
+def optimizer_parity_check(engine, groups, dp, tp, hyper, lr, dev) -> dict:
+    """One optimizer step of the fused peer-memory kernels checked against an
+    NCCL + fp32 PyTorch oracle on the same gradients (run once, untimed).
+
+    Before the fused step: NCCL ``reduce_scatter_tensor`` of the same fp32
+    gradient buffer (the oracle shard), the oracle global norm from it, and
+    copies of a window of this rank's fp32 master / moments.  After it: the
+    fused reduce-scatter output against the oracle shard (whole shard), the
+    fused grad norm against the oracle norm, the fused AdamW master window
+    against a plain fp32 AdamW of the oracle gradient, and the bf16 parameters
+    that every peer stored into this rank's replica (the fused all-gather)
+    against the peers' master windows gathered over NCCL.  Returns the max
+    over ranks of each error."""
+    import torch
+    import torch.distributed as dist
+
+    from wavelet_b200.parallel.zero import FusedShardedAdamW
+
+    opt = engine.opt
+    assert isinstance(opt, FusedShardedAdamW)
+    flat = engine.model.trainable
+    n = flat.shard_numel
+    g_ref = torch.empty(n, device=dev, dtype=torch.float32)
+    dist.reduce_scatter_tensor(g_ref, flat.grad, op=dist.ReduceOp.SUM, group=groups.dp)
+    st = torch.zeros(2, device=dev, dtype=torch.float32)
+    opt.local_sumsq_(g_ref, st)
+    st64 = st.double()
+    dist.all_reduce(st64)  # world: every dp x tp rank
+    norm_ref = float(st64[0]) ** 0.5
+    factor = min(1.0, hyper.max_grad_norm / (norm_ref + 1e-6)) if hyper.max_grad_norm > 0 else 1.0
+    wlen = min(n, 1 << 22)
+    win = slice(n - wlen, n)  # the tail of the shard: matrices (TP-sharded region under TP)
+    p0, m0, v0 = flat.master[win].clone(), flat.exp_avg[win].clone(), flat.exp_avg_sq[win].clone()
+    step = opt.step_count + 1
+    out = opt.step(lr)
+    g_err = (opt.g_shard - g_ref).abs().max() / g_ref.abs().max().clamp_min(1e-30)
+    # fp32 AdamW oracle on the window, fed the fused reduce-scatter output and
+    # clip factor (the reduce-scatter and the norm are checked against NCCL above)
+    b1, b2 = hyper.betas
+    g = opt.g_shard[win] * out["clip_factor"]
+    m1 = b1 * m0 + (1 - b1) * g
+    v1 = b2 * v0 + (1 - b2) * g * g
+    p1 = p0 * (1 - lr * hyper.weight_decay) - (lr / (1 - b1 ** step)) * m1 / (
+        v1.sqrt() / (1 - b2 ** step) ** 0.5 + hyper.eps)
+    p_err = (flat.master[win] - p1).abs().max()
+    # fused all-gather: every peer's window as stored into this rank's bf16 replica
+    mine16 = flat.master[win].to(torch.bfloat16)
+    allw = torch.empty(dp * wlen, device=dev, dtype=torch.bfloat16)
+    dist.all_gather_into_tensor(allw, mine16, group=groups.dp)
+    comp = flat.compute.detach()
+    ag_bad = torch.zeros((), device=dev, dtype=torch.float32)
+    for r in range(dp):
+        lo = r * n + (n - wlen)
+        ag_bad += (comp[lo:lo + wlen] != allw[r * wlen:(r + 1) * wlen]).sum().float()
+    res = torch.stack([g_err.float(), p_err.float(), ag_bad,
+                       torch.tensor(abs(out["grad_norm"] - norm_ref) / max(norm_ref, 1e-30), device=dev)])
+    dist.all_reduce(res, op=dist.ReduceOp.MAX)
+    res = res.tolist()
+    return {"rs_grad_max_rel_err": res[0], "adamw_master_max_abs_err": res[1], "allgather_mismatches": int(res[2]),
+            "grad_norm_rel_err": res[3], "grad_norm": norm_ref, "clip_factor_oracle": factor,
+            "window_elems_per_rank": wlen,
+            "oracle": "NCCL reduce_scatter + NCCL all_reduce(norm) + fp32 torch AdamW + NCCL all_gather",
+            "ok": bool(res[0] <= 1e-5 and res[1] <= 1e-6 and res[2] == 0 and res[3] <= 1e-4)}
+
+
 def main():
     args = parse()
     if args.tp is None:
-        args.tp = 2 if (args.gpus == 8 and args.workload == "sft") else 1
+        # data parallel at every N by default: the reference's tensor-parallel
+        # path (Hugging Face tp_plan) needs `accelerate`, which this image lacks,
+        # so dp is the layout both arms run; --tp 2 runs dp(N/2) x tp2 here
+        args.tp = 1
     if args.impl == "reference":
         return reference_arm(args)
     if args.workload == "grpo-4b":
@@ -239,8 +307,8 @@ def main():
     from wavelet_b200.models.config import resolve_arch
     from wavelet_b200.models.qwen import build_model
     from wavelet_b200.ops import _ext
-    from wavelet_b200.parallel.dist import destroy_distributed, init_distributed
-    from wavelet_b200.parallel.fabric import maybe_fabric
+    from wavelet_b200.parallel.dist import Groups, ParallelDims, destroy_distributed, init_distributed
+    from wavelet_b200.parallel.fabric import Fabric, maybe_fabric
     from wavelet_b200.parallel.zero import AdamWHyper
     from wavelet_b200.data.fake import synthetic_sft_microbatches
     from wavelet_b200.trainer.engine import Engine
@@ -251,37 +319,66 @@ def main():
     assert N == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={N}"
     dev = world.device
     _ext.load()
+    qlora = args.workload == "qlora"
+    tp = args.tp
+    if N % tp:
+        raise SystemExit(f"--tp {tp} must divide --gpus {N}")
+    if qlora and tp > 1:
+        raise SystemExit("the QLoRA workload runs data-parallel only (--tp 1)")
+    dims = ParallelDims(tp=tp, world_size=N)
+    groups = Groups(dims, rank)
+    dp, dp_rank = dims.dp, groups.dp_rank
 
     overrides = {"num_layers": args.layers} if args.layers else None
     cfg = resolve_arch(args.model, overrides)
-    fabric = maybe_fabric(N, rank, dev) if args.comm == "fabric" else None
-    qlora = args.workload == "qlora"
+    fabric = maybe_fabric(dp, dp_rank, dev, group=groups.dp) if args.comm == "fabric" else None
+    norm_fabric = Fabric(rank, N, dev) if (fabric is not None and tp > 1) else None
+    tp_fabric = Fabric(groups.tp_rank, tp, dev, group=groups.tp) if (tp > 1 and args.comm == "fabric") else None
     lora = None
     if qlora:
         from types import SimpleNamespace
 
         lora = SimpleNamespace(rank=16, alpha=32.0, dropout=0.0, target_modules=[
             "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"])
-    model = build_model(cfg, dev, torch.bfloat16, dp_rank=rank, dp_world=N, seed=1234, fabric=fabric,
-                        lora=lora, load_in_4bit=qlora)
+    model = build_model(cfg, dev, torch.bfloat16, dp_rank=dp_rank, dp_world=dp, seed=1234, fabric=fabric,
+                        lora=lora, load_in_4bit=qlora, tp=(tp, groups.tp_rank) if tp > 1 else None)
+    model.tp_group = groups.tp
+    if tp_fabric is not None:
+        model.attach_tp_fabric(tp_fabric)
     hyper = AdamWHyper(lr=2e-4 if qlora else 1e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
                        max_grad_norm=1.0)
     model.set_activation_checkpointing(1 if args.activation_checkpointing == "full" else None)
-    engine = Engine(model, hyper, dp_group=None, dp_world=N, fabric=fabric)
+    engine = Engine(model, hyper, dp_group=groups.dp, dp_world=dp, fabric=fabric, norm_fabric=norm_fabric)
     stepper = SFTStepper(engine, dev)
 
     S = args.seq_len or (2048 if qlora else 4096)
-    mb = args.micro_batches or (max(1, 32 // N) if qlora else 8)
-    host_batches = synthetic_sft_microbatches(mb, S, cfg.vocab_size, seed=100 + rank)
-    host_batches = [b.pin_memory() for b in host_batches]
-    dev_batches = [b.to(dev) for b in host_batches]
+    # micro-batches of one sequence per data-parallel rank and step: the global
+    # batch is 8 sequences per GPU at every layout (64 at 8 GPUs)
+    mb = args.micro_batches or (max(1, 32 // N) if qlora else 8 * tp)
+    # distinct batches every step (TP peers share their data-parallel rank's data)
+    n_dev = args.warmup + args.steps
+    n_host = 0 if args.no_e2e else args.steps
+    sets = [synthetic_sft_microbatches(mb, S, cfg.vocab_size, seed=100003 * i + 101 * dp_rank + 7)
+            for i in range(n_dev + n_host)]
+    dev_sets = [[b.to(dev) for b in st] for st in sets[:n_dev]]
+    host_sets = [[b.pin_memory() for b in st] for st in sets[n_dev:]]
     torch.cuda.synchronize()
+    it = iter(range(n_dev))
 
     def step_device():
-        return stepper.train_step(dev_batches, hyper.lr, device_resident=True)
+        return stepper.train_step(dev_sets[next(it)], hyper.lr, device_resident=True)
 
     for _ in range(args.warmup):
         step_device()
+
+    parity = None
+    if N > 1 and fabric is not None and not qlora:
+        # one extra, untimed step on a warm-up batch: fused collectives vs the NCCL oracle
+        scale = 1.0 / engine.global_token_count(float(dev_sets[0][0].loss_mask.sum()), dev)
+        engine.sft_micro_step(dev_sets[0][0], scale)
+        model.finalize_grads()
+        parity = optimizer_parity_check(engine, groups, dp, tp, hyper, hyper.lr, dev)
+        torch.cuda.synchronize()
 
     sampler = ClockSampler(dev.index if dev.index is not None else 0) if rank == 0 else None
     if sampler:
@@ -306,7 +403,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     launches = counter.count
-    tokens_per_step = N * mb * S
+    tokens_per_step = dp * mb * S
     value = tokens_per_step / (ms / 1000.0)
 
     e2e = None
@@ -318,8 +415,8 @@ def main():
         e_s = torch.cuda.Event(enable_timing=True)
         e_e = torch.cuda.Event(enable_timing=True)
         e_s.record()
-        for _ in range(args.steps):
-            stepper.train_step(host_batches, hyper.lr)
+        for i in range(args.steps):
+            stepper.train_step(host_sets[i], hyper.lr)
         e_e.record()
         torch.cuda.synchronize()
         te = torch.tensor([e_s.elapsed_time(e_e) / args.steps], device=dev, dtype=torch.float64)
@@ -336,6 +433,7 @@ def main():
     from wavelet_b200.trainer.perf import flops_per_token
 
     mfu_flops = flops_per_token(cfg, S, model.lora.num_trainable() if model.lora is not None else None)
+    layout = f"dp{dp}" + (f"xtp{tp}" if tp > 1 else "")
     if rank == 0:
         rec = {
             "metric": ("QLoRA SFT tok/s (Qwen2.5-7B-shape, NF4 base, LoRA r16 all projections)" if qlora
@@ -350,20 +448,22 @@ def main():
             "scaling": "strong" if qlora else "weak",
             "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None,
             "dtype": "bf16",
-            "data": "synthetic (uniform random tokens, random-init weights)",
+            "data": "synthetic (uniform random tokens, a new batch every step, random-init weights)",
             "config": {
                 "model": "Qwen2.5-7B-shape" + (f" ({args.layers} layers: INVALID debug run)" if args.layers else ""),
-                "global_batch": N * mb,
+                "global_batch": dp * mb,
                 "seq_len": S,
                 "micro_batch": 1,
                 "grad_accum": mb,
-                "parallelism": f"dp{N}",
+                "parallelism": layout,
                 **({"base": "NF4 blocksize 64 (fp32 absmax), frozen", "lora": "r=16 alpha=32 on q/k/v/o/gate/up/down"}
                    if qlora else {}),
                 "optimizer": "AdamW (fp32 master, sharded)" + (" on LoRA adapters" if qlora else ""),
                 "activation_checkpointing": args.activation_checkpointing,
                 "optimizer_comm": ("fused peer-memory RS+AdamW+AG kernels" if fabric is not None
-                                   else ("NCCL reduce-scatter/all-gather" if N > 1 else "none (1 GPU)")),
+                                   else ("NCCL reduce-scatter/all-gather" if dp > 1 else "none (1 data-parallel rank)")),
+                **({"tp_comm": "fused GEMM->all-reduce epilogue over peer memory" if tp_fabric is not None
+                    else "NCCL all-reduce"} if tp > 1 else {}),
                 "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",
             },
             "mfu": value * mfu_flops / (N * 2.25e15),
@@ -371,10 +471,12 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
             "e2e": e2e,
+            **({"fused_vs_nccl": parity} if parity is not None else {}),
         }
         print(json.dumps(rec), flush=True)
-    if fabric is not None:
-        fabric.close()
+    for fab in (fabric, norm_fabric, tp_fabric):
+        if fab is not None:
+            fab.close()
     destroy_distributed()
     return 0
 

@@ -17,6 +17,67 @@ def _bufs(fab, n, dtype, k):
     return [fab.alloc(n, dtype) for _ in range(k)]
 
 
+
+def test_weighted_norm_boundary(cuda_ext):
+    """Elements below the boundary enter the squared norm with weight w_lo
+    (tensor-parallel replicated parameters); the reduced values are unchanged."""
+    from wavelet_b200.parallel.fabric import Fabric
+
+    fab = Fabric(0, 1, torch.device("cuda", 0))
+    W, n = 2, 1 << 15
+    grads = _bufs(fab, W * n, torch.float32, W)
+    torch.manual_seed(1)
+    for b in grads:
+        b.tensor.copy_(torch.randn(W * n, device="cuda"))
+    lo, w_end = n, n + 4096
+    out = torch.empty(n, device="cuda")
+    stats = torch.zeros(2, device="cuda")
+    cuda_ext.rs_sum_sumsq([b.ptrs[0] for b in grads], W, lo, n, 1.0, out, stats, w_end, 0.5)
+    ref = sum(b.tensor[lo : lo + n] for b in grads)
+    torch.testing.assert_close(out, ref, rtol=1e-6, atol=1e-6)
+    want = 0.5 * ref[:4096].pow(2).sum() + ref[4096:].pow(2).sum()
+    torch.testing.assert_close(stats[0], want, rtol=1e-4, atol=0)
+    fab.close()
+
+
+def test_fabric_waits_run_out_and_report(cuda_ext):
+    """A bounded device-side wait that no peer ever satisfies ends after its
+    budget: the barrier and the norm exchange set the timeout bit of the error
+    word (the norm exchange also marks the step non-finite, so no rank would
+    update), ``Fabric.check`` raises ``PeerTimeoutError``, and the context stays
+    usable.  The "peer" is a second local pad that nothing writes, so no other
+    process or launch is involved."""
+    import time
+
+    from wavelet_b200.parallel.fabric import ERR_TIMEOUT_PEER, SLOT_BARRIER, SLOT_NORM, Fabric, PeerTimeoutError
+
+    dev = torch.device("cuda", 0)
+    fab = Fabric(0, 1, dev, budget_s=0.05)
+    ghost = fab.alloc(256, torch.int32)  # pad of a "rank 1" that never signals
+    pads = [fab.pads.ptrs[0], ghost.ptrs[0]]
+    cuda_ext.clear_error(0)
+    t0 = time.time()
+    cuda_ext.peer_barrier(pads, 0, 2, 7, SLOT_BARRIER, 0.05)
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 5.0
+    assert cuda_ext.read_error(0) & ERR_TIMEOUT_PEER
+    with pytest.raises(PeerTimeoutError):
+        fab.check()
+    assert cuda_ext.read_error(0) == 0  # check() cleared it
+    stats = torch.tensor([4.0, 0.0], device=dev)
+    tot = torch.zeros(3, device=dev)
+    cuda_ext.norm_exchange(pads, 0, 2, 9, stats, 1.0, tot, 0.05)
+    torch.cuda.synchronize()
+    assert tot[1].item() > 0  # a missing peer reads as a non-finite step: nobody updates
+    assert cuda_ext.read_error(0) & ERR_TIMEOUT_PEER
+    with pytest.raises(PeerTimeoutError):
+        fab.check()
+    # the context is still usable after the timeouts
+    x = torch.arange(1024, device=dev, dtype=torch.float32)
+    assert float(x.sum()) == 1023 * 1024 / 2
+    fab.close()
+
+
 def test_rs_and_adamw_allgather_emulated_ranks(cuda_ext):
     from wavelet_b200.parallel.fabric import Fabric
 
@@ -112,10 +173,16 @@ def test_fused_step_skips_an_overflowing_norm(cuda_ext):
     opt = FusedShardedAdamW(a.flat, AdamWHyper(lr=1e-3, max_grad_norm=1.0), fab)
     master, compute = a.flat.master.clone(), a.flat.compute.clone()
     a.flat.grad.fill_(1e30)  # finite elements, fp32 sum of squares overflows
-    with pytest.raises(NonFiniteGradientError):
+    with pytest.raises(NonFiniteGradientError, match="overflows"):
         opt.step()
     assert torch.equal(a.flat.master, master) and torch.equal(a.flat.compute, compute)
     assert opt.step_count == 0
+    # clipping off: the norm is not used and the finite gradients update
+    opt_nc = FusedShardedAdamW(a.flat, AdamWHyper(lr=1e-3, max_grad_norm=0.0), fab)
+    a.flat.grad.fill_(1e18)  # each square is finite in fp32, their sum is not
+    out = opt_nc.step()
+    assert out["clip_factor"] == 1.0 and opt_nc.step_count == 1
+    assert torch.isfinite(a.flat.master).all() and not torch.equal(a.flat.master, master)
     fab.close()
 
 

@@ -165,3 +165,32 @@ def test_softmax_stats_and_grad(cuda_ext, tau):
     g = z.clone()
     cuda_ext.softmax_grad(g, tgt, 1.0 / tau, lse, ent, dlp, dent)
     torch.testing.assert_close(g.float(), zz.grad, rtol=5e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("tau", [1.0, 0.7])
+@pytest.mark.parametrize("V", [13, 4099, 151939])
+def test_softmax_stats_ragged_vocab(cuda_ext, V, tau):
+    """Vocabularies that are not a multiple of 8 (the scalar tail loop) and
+    rows shorter than one pass of the block (fewer than 512 vectors): rows
+    padded to a 16-byte stride, compared with torch logsumexp / entropy."""
+    torch.manual_seed(V)
+    R = 5
+    ld = (V + 7) // 8 * 8
+    buf = (torch.randn(R, ld, device="cuda") * 3).to(torch.bfloat16)
+    z = buf[:, :V]
+    tgt = torch.tensor([0, V - 1, V // 2, V - 2, 1], device="cuda")
+    lse = torch.empty(R, device="cuda")
+    lp = torch.empty(R, device="cuda")
+    ent = torch.empty(R, device="cuda")
+    cuda_ext.softmax_stats(z, tgt, 1.0 / tau, lse, lp, ent)
+    zf = z.float() / tau
+    logp = torch.log_softmax(zf, -1)
+    torch.testing.assert_close(lse, torch.logsumexp(zf, -1), rtol=1e-4, atol=1e-3)
+    torch.testing.assert_close(lp, logp.gather(1, tgt[:, None])[:, 0], rtol=1e-4, atol=1e-3)
+    torch.testing.assert_close(ent, -(logp.exp() * logp).sum(-1), rtol=1e-3, atol=1e-3)
+    # the padding columns were not read as logits
+    buf2 = buf.clone()
+    buf2[:, V:] = 1e4
+    lse2 = torch.empty(R, device="cuda")
+    cuda_ext.softmax_stats(buf2[:, :V], tgt, 1.0 / tau, lse2, None, None)
+    torch.testing.assert_close(lse2, lse, rtol=0, atol=0)

@@ -145,7 +145,38 @@ def test_finite_gradients_with_overflowing_norm_abort_before_update(kind):
     before = flat.master.clone()
     opt = FlatOptimizer(flat, OptimizerConfig(type=kind, lr=0.1), max_grad_norm=1.0)
     flat.grad.fill_(1e30)  # every element finite; the squared norm is not
-    with pytest.raises(NonFiniteGradientError):
+    with pytest.raises(NonFiniteGradientError, match="overflows"):
         opt.step(0.1)
     assert torch.equal(flat.master, before)
     assert opt.step_count == 0
+
+
+@pytest.mark.parametrize("kind", ["adamw", "sgd"])
+def test_overflowing_norm_steps_when_clipping_is_off(kind):
+    """With max_grad_norm = 0 the norm is not used, so finite gradients whose
+    squared norm overflows still update (the reference checks it only when
+    clipping)."""
+    flat = FlatParams(SPECS, "cpu", torch.float32)
+    flat.init_(seed=3)
+    flat.sync_master_from_compute()
+    before = flat.master.clone()
+    opt = FlatOptimizer(flat, OptimizerConfig(type=kind, lr=0.1), max_grad_norm=0.0)
+    flat.grad.fill_(1e18)  # each square is finite in fp32, their sum is not
+    out = opt.step(0.1)
+    assert out["clip_factor"] == 1.0
+    assert torch.isfinite(flat.master).all()
+    assert not torch.equal(flat.master, before)
+    assert opt.step_count == 1
+
+
+def test_non_finite_element_message_counts_elements():
+    from wavelet_b200.parallel.zero import NonFiniteGradientError
+
+    flat = FlatParams(SPECS, "cpu", torch.float32)
+    flat.init_(seed=3)
+    opt = FlatOptimizer(flat, OptimizerConfig(type="adamw", lr=0.1), max_grad_norm=0.0)
+    flat.grad.zero_()
+    flat.grad[5] = float("nan")
+    flat.grad[9] = float("inf")
+    with pytest.raises(NonFiniteGradientError, match=r"\(2 elements\)"):
+        opt.step(0.1)

@@ -20,6 +20,7 @@
 //
 // Parity: replaces the FA2/FA3/SDPA attention of the reference's HF models
 // (trainer/model.py:315-360) including packed varlen (trainer/rl.py:189-229).
+#include <atomic>
 #include <cuda_bf16.h>
 #include <math.h>
 
@@ -1349,10 +1350,10 @@ void attn_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (a.Hq % a.Hk) throw std::runtime_error("wavelet_b200 attention: Hq must be a multiple of Hk");
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool attr[64] = {false};
-  if (!attr[dev & 63]) {
+  static std::atomic<bool> attr[64];  // per device; cudaFuncSetAttribute is idempotent
+  if (!attr[dev & 63].load(std::memory_order_acquire)) {
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem_bytes());
-    attr[dev & 63] = true;
+    attr[dev & 63].store(true, std::memory_order_release);
   }
   const int Tk = a.cu_seqlens_k ? a.Tk : a.T;
   CUtensorMap mq = head_map(a.q, a.q_row, a.Hq, a.T);
@@ -1387,11 +1388,11 @@ void attn_bwd(const AttnBwdArgs& b, cudaStream_t stream) {
     throw std::runtime_error("wavelet_b200 attention: GQA backward needs fp32 partial buffers");
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool attr[64] = {false};
-  if (!attr[dev & 63]) {
+  static std::atomic<bool> attr[64];  // per device; cudaFuncSetAttribute is idempotent
+  if (!attr[dev & 63].load(std::memory_order_acquire)) {
     cudaFuncSetAttribute(attn_bwd_dkv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dkv2_smem_bytes());
     cudaFuncSetAttribute(attn_bwd_dq2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq2_smem_bytes());
-    attr[dev & 63] = true;
+    attr[dev & 63].store(true, std::memory_order_release);
   }
   {
     const int warps = 8;
@@ -1447,14 +1448,14 @@ int attn_bwd_explicit(const AttnBwdArgs& b, int* err, cudaStream_t stream) {
   if (a.head_dim != 128) return 1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 2;
-  static bool attr[64] = {false};
-  if (!attr[dev & 63]) {
+  static std::atomic<bool> attr[64];  // per device; cudaFuncSetAttribute is idempotent
+  if (!attr[dev & 63].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dkv_smem_bytes()) !=
             cudaSuccess ||
         cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq_smem_bytes()) !=
             cudaSuccess)
       return 3;
-    attr[dev & 63] = true;
+    attr[dev & 63].store(true, std::memory_order_release);
   }
   {
     const int warps = 8;

@@ -8,6 +8,7 @@
 // and cached; kernels only ever receive those resolved addresses.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "attention.h"
@@ -19,27 +20,39 @@ static __device__ __align__(256) float g_noalloc_delta[WB_ATTN_BWD_NOALLOC_MAX_R
 static __device__ __align__(256) int g_noalloc_err[1];
 
 constexpr int kMaxDevices = 64;
-float* g_delta_addr[kMaxDevices] = {nullptr};
-int* g_err_addr[kMaxDevices] = {nullptr};
+// Resolved addresses per device.  Readers on any host thread load them with
+// acquire; the one writer (under the mutex) publishes each with release after
+// cudaGetSymbolAddress succeeded, so a non-null value is always complete.
+std::atomic<float*> g_delta_addr[kMaxDevices];
+std::atomic<int*> g_err_addr[kMaxDevices];
 std::mutex g_setup_mu;
 
 // Resolve the static arrays' device addresses for the current device.
-int setup_current_device(int* dev_out) {
+int setup_current_device(int* dev_out, float** delta, int** err) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return WB_NOALLOC_ESETUP;
   *dev_out = dev;
-  if (g_delta_addr[dev] && g_err_addr[dev]) return WB_NOALLOC_OK;
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_delta_addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_delta) != cudaSuccess || p == nullptr) return WB_NOALLOC_ESETUP;
-    g_delta_addr[dev] = static_cast<float*>(p);
+  float* d = g_delta_addr[dev].load(std::memory_order_acquire);
+  int* e = g_err_addr[dev].load(std::memory_order_acquire);
+  if (!d || !e) {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    d = g_delta_addr[dev].load(std::memory_order_relaxed);
+    if (!d) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_delta) != cudaSuccess || p == nullptr) return WB_NOALLOC_ESETUP;
+      d = static_cast<float*>(p);
+      g_delta_addr[dev].store(d, std::memory_order_release);
+    }
+    e = g_err_addr[dev].load(std::memory_order_relaxed);
+    if (!e) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_err) != cudaSuccess || p == nullptr) return WB_NOALLOC_ESETUP;
+      e = static_cast<int*>(p);
+      g_err_addr[dev].store(e, std::memory_order_release);
+    }
   }
-  if (!g_err_addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_err) != cudaSuccess || p == nullptr) return WB_NOALLOC_ESETUP;
-    g_err_addr[dev] = static_cast<int*>(p);
-  }
+  *delta = d;
+  *err = e;
   return WB_NOALLOC_OK;
 }
 
@@ -53,12 +66,14 @@ extern "C" int wb_attn_bwd_noalloc(const void* q, int64_t q_row, const void* k, 
   if (T < 0 || nseq < 0 || Hq <= 0 || Hk <= 0 || Hq % Hk != 0 || max_seqlen < 0) return WB_NOALLOC_EARG;
   if ((int64_t)Hq * (int64_t)T > (int64_t)WB_ATTN_BWD_NOALLOC_MAX_ROWS) return WB_NOALLOC_ETOO_LARGE;
   int dev = 0;
-  const int rc = setup_current_device(&dev);
+  float* delta = nullptr;
+  int* err = nullptr;
+  const int rc = setup_current_device(&dev, &delta, &err);
   if (rc != WB_NOALLOC_OK) return rc;
   if (T == 0 || nseq == 0) return WB_NOALLOC_OK;
   // The error word must start at zero for this call; Delta is fully
   // overwritten by the pre-pass before it is read, so it needs no clearing.
-  if (cudaMemsetAsync(g_err_addr[dev], 0, sizeof(int), stream) != cudaSuccess) return WB_NOALLOC_ELAUNCH;
+  if (cudaMemsetAsync(err, 0, sizeof(int), stream) != cudaSuccess) return WB_NOALLOC_ELAUNCH;
   wb::AttnBwdArgs b;
   b.f.q = q;
   b.f.k = k;
@@ -81,19 +96,21 @@ extern "C" int wb_attn_bwd_noalloc(const void* q, int64_t q_row, const void* k, 
   b.dq = dq;
   b.dk = dk;
   b.dv = dv;
-  b.delta = g_delta_addr[dev];
-  const int lrc = wb::attn_bwd_explicit(b, g_err_addr[dev], stream);
+  b.delta = delta;
+  const int lrc = wb::attn_bwd_explicit(b, err, stream);
   if (lrc == 1) return WB_NOALLOC_EARG;
   return lrc == 0 ? WB_NOALLOC_OK : WB_NOALLOC_ELAUNCH;
 }
 
 extern "C" int wb_attn_bwd_noalloc_status(int device) {
-  if (device < 0 || device >= kMaxDevices || !g_err_addr[device]) return 0;
+  if (device < 0 || device >= kMaxDevices) return 0;
+  int* err = g_err_addr[device].load(std::memory_order_acquire);
+  if (!err) return 0;
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(device);
   int v = 0;
-  cudaMemcpy(&v, g_err_addr[device], sizeof(int), cudaMemcpyDeviceToHost);
+  cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost);
   cudaSetDevice(prev);
   return v;
 }
@@ -105,7 +122,8 @@ extern "C" const char* wb_attn_bwd_noalloc_strerror(int code) {
     case WB_NOALLOC_ETOO_LARGE:
       return "Hq * T exceeds the static scratch capacity (WB_ATTN_BWD_NOALLOC_MAX_ROWS = 1048576 rows)";
     case WB_NOALLOC_EARG:
-      return "invalid argument (null pointer, negative size, head_dim != 128 or Hq not a multiple of Hk)";
+      return "invalid argument (a null pointer, negative T, nseq or max_seqlen, Hq or Hk not positive, or Hq "
+             "not a multiple of Hk)";
     case WB_NOALLOC_ESETUP:
       return "could not resolve the device address of the static scratch (cudaGetSymbolAddress failed)";
     case WB_NOALLOC_ELAUNCH:

@@ -22,7 +22,7 @@
 // Return codes
 #define WB_NOALLOC_OK 0
 #define WB_NOALLOC_ETOO_LARGE 1      // Hq * T exceeds WB_ATTN_BWD_NOALLOC_MAX_ROWS
-#define WB_NOALLOC_EARG 2            // bad argument (null pointer, head_dim != 128, Hq % Hk != 0, ...)
+#define WB_NOALLOC_EARG 2            // bad argument (null pointer, negative T / nseq / max_seqlen, Hq % Hk != 0)
 #define WB_NOALLOC_ESETUP 3          // cudaGetSymbolAddress of the static scratch failed
 #define WB_NOALLOC_ELAUNCH 4         // a kernel launch or TMA descriptor encode failed
 
@@ -31,7 +31,7 @@ extern "C" {
 #endif
 
 // Causal varlen GQA attention backward (same math and layouts as the
-// library's attn_bwd): q/k/v/o are [T, H, 128] bf16 with the given row
+// library's attn_bwd; the head dimension is fixed at 128): q/k/v/o are [T, H, 128] bf16 with the given row
 // strides (elements between tokens), dout/dq are contiguous [T, Hq, 128],
 // dk/dv contiguous [T, Hk, 128], lse [Hq, T] fp32 from the forward,
 // cu_seqlens device int32 [nseq + 1].  All pointers are device pointers on

@@ -231,12 +231,12 @@ void peer_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t world,
 }
 
 void rs_sum_sumsq(const std::vector<int64_t>& grads, int64_t world, int64_t lo, int64_t n, double scale,
-                  at::Tensor& out, at::Tensor& stats) {
+                  at::Tensor& out, at::Tensor& stats, int64_t w_end, double w_lo) {
   check_f32(out, "out");
   check_f32(stats, "stats");
   WB_CHECK(out.numel() >= n, "rs_sum_sumsq: out too small");
   wb::rs_sum_sumsq(peers_of(grads, (int)world), (int)world, lo, n, (float)scale, out.data_ptr<float>(),
-                   stats.data_ptr<float>(), cur_stream());
+                   stats.data_ptr<float>(), w_end, (float)w_lo, cur_stream());
 }
 
 void norm_exchange(const std::vector<int64_t>& pads, int64_t rank, int64_t world, int64_t epoch,
@@ -756,7 +756,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fabric_close", &fabric_close_);
   m.def("from_ptr", &from_ptr);
   m.def("peer_barrier", &peer_barrier);
-  m.def("rs_sum_sumsq", &rs_sum_sumsq);
+  m.def("rs_sum_sumsq", &rs_sum_sumsq, py::arg("grads"), py::arg("world"), py::arg("lo"), py::arg("n"),
+        py::arg("scale"), py::arg("out"), py::arg("stats"), py::arg("w_end") = 0, py::arg("w_lo") = 1.0);
   m.def("norm_exchange", &norm_exchange);
   m.def("adamw_allgather", &adamw_allgather);
   m.def("allgather_bf16", &allgather_bf16);

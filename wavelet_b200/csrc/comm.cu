@@ -93,7 +93,9 @@ __global__ void norm_exchange_kernel(PeerPtrs pads, int rank, int world, uint32_
     b += ld_relaxed_sys(mvals + 2 * t + 1);
   }
   if (!ok) b = 1.f;  // a missing peer: treat as non-finite so no rank updates from a partial norm
-  if (!isfinite(s)) b += 1.f;  // finite gradients whose squared norm overflows: skip the step as well
+  // finite gradients whose squared norm overflows: no usable clip factor, so
+  // skip the step when clipping is on (with clipping off the step proceeds)
+  if (!isfinite(s) && max_norm > 0.f) b += 1.f;
   float factor = 1.f;
   if (max_norm > 0.f) factor = fminf(1.f, max_norm / (sqrtf(s) + 1e-6f));
   tot[0] = s;
@@ -131,10 +133,14 @@ __device__ unsigned g_sum_counter;
 
 template <int W>
 __global__ void __launch_bounds__(512) rs_kernel(PeerPtrs grads, int64_t lo, int64_t n8, float scale, float* out,
-                                                 float* stats) {
+                                                 float* stats, int64_t w_end, float w_lo) {
   __shared__ float red[32];
   float ss = 0.f, bad = 0.f;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    // elements below w_end (a multiple of 8) enter the squared norm with weight
+    // w_lo: parameters replicated over tensor-parallel ranks are counted once
+    // in the cross-TP norm sum (each of the tp replicas adds 1/tp of them)
+    const float wgt = (lo + 8 * i < w_end) ? w_lo : 1.f;
     float4 x0[W], x1[W];
 #pragma unroll
     for (int r = 0; r < W; ++r) {
@@ -154,7 +160,7 @@ __global__ void __launch_bounds__(512) rs_kernel(PeerPtrs grads, int64_t lo, int
     for (int j = 0; j < 4; ++j) {
       e0[j] *= scale;
       e1[j] *= scale;
-      ss += e0[j] * e0[j] + e1[j] * e1[j];
+      ss += wgt * (e0[j] * e0[j] + e1[j] * e1[j]);
       bad += (isfinite(e0[j]) ? 0.f : 1.f) + (isfinite(e1[j]) ? 0.f : 1.f);
     }
     float4* dst = reinterpret_cast<float4*>(out) + 2 * i;
@@ -430,12 +436,14 @@ void norm_exchange(const PeerPtrs& pads, int rank, int world, uint32_t epoch, co
   }
 
 void rs_sum_sumsq(const PeerPtrs& grads, int world, int64_t lo, int64_t n, float scale, float* out, float* stats,
-                  cudaStream_t st) {
+                  int64_t w_end, float w_lo, cudaStream_t st) {
   if (n <= 0) return;
-  if (n % 8 || lo % 8) throw std::runtime_error("wavelet_b200 fabric: shard must be a multiple of 8 elements");
+  if (n % 8 || lo % 8 || w_end % 8)
+    throw std::runtime_error("wavelet_b200 fabric: shard and norm-weight boundary must be multiples of 8 elements");
   const int64_t n8 = n / 8;
   const int grid = comm::grid_for(n8, 512, 148 * 4);
-  WB_WORLD_SWITCH(world, comm::rs_kernel<kW><<<grid, 512, 0, st>>>(grads, lo, n8, scale, out, stats)); note_launch();
+  WB_WORLD_SWITCH(world, comm::rs_kernel<kW><<<grid, 512, 0, st>>>(grads, lo, n8, scale, out, stats, w_end, w_lo));
+  note_launch();
 }
 
 void adamw_allgather(const PeerPtrs& compute, int world, int64_t lo, float* master, const float* g, float* m, float* v,

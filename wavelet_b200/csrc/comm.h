@@ -45,9 +45,11 @@ void peer_barrier(const PeerPtrs& pads, int rank, int world, uint32_t epoch, int
                   uint64_t budget_ns, int* err, cudaStream_t st);
 
 // out[i] = scale * sum_r grads[r][lo + i] for i < n (fixed rank order), and
-// stats[0] += sum out^2, stats[1] += #non-finite.  n multiple of 8.
+// stats[0] += sum wgt(i) * out^2, stats[1] += #non-finite, where wgt = w_lo for
+// global index lo + i < w_end and 1 above (w_end = 0: plain sum of squares).
+// n, lo and w_end multiples of 8.
 void rs_sum_sumsq(const PeerPtrs& grads, int world, int64_t lo, int64_t n, float scale, float* out,
-                  float* stats, cudaStream_t st);
+                  float* stats, int64_t w_end, float w_lo, cudaStream_t st);
 
 // Exchange (sumsq, nonfinite) with every peer, then write
 // tot = {sumsq, nonfinite, clip factor} (fixed rank order sum).

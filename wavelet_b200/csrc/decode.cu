@@ -8,6 +8,7 @@
 // [num_seqs].
 // These replace vLLM's paged attention / sampler used by the reference's
 // rollout engine (inference/engine.py:776-818).
+#include <atomic>
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
@@ -595,11 +596,11 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st) {
   if (rep <= D2_MAXREP && a.block_size % D2_TOK == 0 && a.cache_rows > 0) {
     int dev = 0;
     cudaGetDevice(&dev);
-    static bool attr[64] = {false};
+    static std::atomic<bool> attr[64];  // per device; cudaFuncSetAttribute is idempotent
     const size_t smem = d2_smem_bytes(D2_MAXREP);
-    if (!attr[dev & 63]) {
+    if (!attr[dev & 63].load(std::memory_order_acquire)) {
       cudaFuncSetAttribute(decode_attn3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr[dev & 63] = true;
+      attr[dev & 63].store(true, std::memory_order_release);
     }
     const uint64_t rows = (uint64_t)a.cache_rows * a.Hk;  // [num_blocks * Hk * block_size, 128]
     CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, rows, HD, 64, D2_TOK,

@@ -34,6 +34,7 @@
 //     bf16 straight into the 128-byte-swizzled stage layout that TMA would
 //     have produced (fence.proxy.async before arriving on the stage barrier),
 //     so a frozen base weight is read at 0.5 byte per element.
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -724,13 +725,13 @@ __global__ void __launch_bounds__(BQ ? NUM_THREADS_Q : NUM_THREADS, 1)
 template <bool A_MN, bool B_MN, int EPI, int GROUP = 0, bool BQ = false>
 static void launch(const GemmArgs& g, cudaStream_t stream) {
   auto kern = gemm_kernel<A_MN, B_MN, EPI, GROUP, BQ>;
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64];  // per device; cudaFuncSetAttribute is idempotent
   int dev = 0;
   cudaGetDevice(&dev);
   constexpr size_t smem = smem_bytes(EPI == kEpiPeerBF16);
-  if (!attr_set[dev & 63]) {
+  if (!attr_set[dev & 63].load(std::memory_order_acquire)) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set[dev & 63] = true;
+    attr_set[dev & 63].store(true, std::memory_order_release);
   }
   // A(m,k): K-major -> rows of K; MN-major -> rows of M.
   CUtensorMap ta = A_MN ? make_tmap_2d(g.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.M, g.K, g.lda,

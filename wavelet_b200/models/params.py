@@ -82,6 +82,35 @@ class FlatParams:
             self.exp_avg_sq = torch.zeros_like(self.master)
         self._views: dict[str, torch.Tensor] = {}
         self._gviews: dict[str, torch.Tensor] = {}
+        # tensor parallelism: the parameters that every TP rank holds whole (and
+        # whose gradients are identical on every TP rank) come first, in
+        # [0, tp_repl_end); the global gradient norm counts them once
+        self.tp_size = 1
+        self.tp_repl_end = 0
+
+    def set_tp_replicated(self, names: Iterable[str], tp_size: int) -> None:
+        """Marks the leading parameters ``names`` as replicated over ``tp_size``
+        tensor-parallel ranks (they must be the first specs of the store)."""
+        names = set(names)
+        lead = 0
+        for s in self.specs:
+            if s.name not in names:
+                break
+            lead += 1
+        if lead != len(names):
+            raise ValueError("TP-replicated parameters must come first in the flat store")
+        end = 0
+        for s in self.specs[:lead]:
+            off, n = self.offsets[s.name]
+            end = max(end, off + (n + ALIGN - 1) // ALIGN * ALIGN)
+        self.tp_size = int(tp_size)
+        self.tp_repl_end = end
+
+    def shard_repl_split(self) -> int:
+        """Number of leading elements of this rank's shard that lie in the
+        TP-replicated region."""
+        lo = self.dp_rank * self.shard_numel
+        return max(0, min(self.tp_repl_end - lo, self.shard_numel))
 
     # ------------------------------------------------------------- views
     def view(self, name: str) -> torch.Tensor:

@@ -382,9 +382,13 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     frozen = lora is not None
     seed_index = {s.name: i for i, s in enumerate(full_specs)}
     tp_rows = {}
+    tp_repl = []
     if tp_size > 1:
         sl = tp_slicers(cfg, tp_size, tp_rank)
         tp_rows = {s.name: sl[s.name.split(".", 1)[-1]] for s in specs if s.name.split(".", 1)[-1] in sl}
+        # replicated parameters first: the gradient norm weighs [0, tp_repl_end) by 1/tp
+        tp_repl = [s for s in specs if s.name not in tp_rows]
+        specs = tp_repl + [s for s in specs if s.name in tp_rows]
     ep_size, ep_rank, ep_dp_rank, ep_dp_world = ep or (1, 0, 0, 1)
     expert_flat = None
     if ep_size > 1:
@@ -407,6 +411,8 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     flat = FlatParams([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,
                       with_grad and not frozen, with_optimizer and not frozen,
                       alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
+    if tp_repl:
+        flat.set_tp_replicated([s.name for s in tp_repl], tp_size)
     quant = {}
     if init:
         flat.init_(seed, seed_index=seed_index, row_slices=tp_rows or None)

@@ -37,6 +37,21 @@ class NonFiniteGradientError(RuntimeError):
     pass
 
 
+def skip_reason(norm_sq: float, bad: float, max_grad_norm: float) -> str | None:
+    """Why an optimizer step must be skipped, or None.
+
+    Non-finite gradient elements always skip the step.  A squared norm that
+    overflows float32 while every element is finite skips it only when
+    clipping is on (its clip factor would be 0); with ``max_grad_norm <= 0``
+    the step proceeds, as in the reference, which looks at the norm only when
+    clipping (trainer/trainer.py:1034-1101, trainer/rl.py:939)."""
+    if bad > 0:
+        return f"non-finite gradients detected ({int(bad)} elements)"
+    if not math.isfinite(norm_sq) and max_grad_norm and max_grad_norm > 0:
+        return "the squared gradient norm overflows float32 (every element is finite); the clip cannot scale it"
+    return None
+
+
 @dataclass
 class AdamWHyper:
     lr: float = 1e-3
@@ -48,11 +63,14 @@ class AdamWHyper:
 
 class ShardedAdamW:
     def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 offload: bool = False, offload_chunk: int = 1 << 26):
+                 offload: bool = False, offload_chunk: int = 1 << 26, norm_world: bool = False):
         self.flat = flat
         self.h = hyper
         self.group = dp_group
         self.world = dp_world
+        # norm_world: the squared norm is summed over every rank of the job
+        # (tensor parallelism: each TP rank holds a different part of the model)
+        self.norm_world = norm_world
         self.step_count = 0
         dev = flat.device
         # optim.cpu_offload: fp32 master / moments live in pinned host memory and
@@ -86,8 +104,29 @@ class ShardedAdamW:
     def prepare(self) -> torch.Tensor:
         self._g = self.reduce_grads()
         self.stats.zero_()
-        ops.sumsq_(self._g, self.stats)
+        self.local_sumsq_(self._g, self.stats)
         return self.stats
+
+    def local_sumsq_(self, g: torch.Tensor, stats: torch.Tensor) -> None:
+        """(sum of squares, non-finite count) of this rank's reduced gradient
+        ``g`` added into ``stats``; TP-replicated elements weigh 1/tp."""
+        flat = self.flat
+        k = flat.shard_repl_split() if self.world > 1 else min(flat.tp_repl_end, g.numel())
+        if flat.tp_size > 1 and k > 0:
+            part = torch.zeros_like(stats)
+            ops.sumsq_(g[:k], part)
+            part[0] /= flat.tp_size
+            stats.add_(part)
+            if k < g.numel():
+                ops.sumsq_(g[k:], stats)
+        else:
+            ops.sumsq_(g, stats)
+
+    def reduce_stats_(self, stats: torch.Tensor) -> None:
+        if self.norm_world and dist.is_initialized():
+            dist.all_reduce(stats)
+        elif self.world > 1:
+            dist.all_reduce(stats, group=self.group)
 
     @torch.no_grad()
     def apply(self, lr: float, factor: float) -> None:
@@ -143,13 +182,12 @@ class ShardedAdamW:
     def step(self, lr: float | None = None, check_finite: bool = True) -> dict[str, float]:
         lr = self.h.lr if lr is None else lr
         stats = self.prepare()
-        if self.world > 1:
-            dist.all_reduce(stats, group=self.group)
+        self.reduce_stats_(stats)
         norm_sq, bad = stats.tolist()
-        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
-        if check_finite and bad > 0:
+        why = skip_reason(norm_sq, bad, self.h.max_grad_norm)
+        if check_finite and why is not None:
             self.flat.zero_grad()
-            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
+            raise NonFiniteGradientError(why)
         norm = norm_sq**0.5
         factor = self.clip_factor(norm)
         self.apply(lr, factor)
@@ -187,9 +225,12 @@ class FusedShardedAdamW(ShardedAdamW):
     non-finite step leaves the parameters unchanged on every rank.
     """
 
-    def __init__(self, flat: FlatParams, hyper: AdamWHyper, fabric):
+    def __init__(self, flat: FlatParams, hyper: AdamWHyper, fabric, norm_fabric=None):
         super().__init__(flat, hyper, dp_group=fabric.group, dp_world=fabric.world)
         self.fabric = fabric
+        # norm_fabric: pads spanning every rank of the job, for the norm exchange
+        # under tensor parallelism (the data-parallel fabric spans one TP slice)
+        self.norm_fabric = norm_fabric if norm_fabric is not None else fabric
         if self.g_shard is None:
             self.g_shard = torch.empty(flat.shard_numel, device=flat.device, dtype=torch.float32)
         self.tot = torch.zeros(3, device=flat.device, dtype=torch.float32)
@@ -205,10 +246,12 @@ class FusedShardedAdamW(ShardedAdamW):
         lo = flat.dp_rank * flat.shard_numel
         fab.barrier()
         self.stats.zero_()
-        m.rs_sum_sumsq(self.grad_ptrs, self.world, lo, flat.shard_numel, 1.0, self.g_shard, self.stats)
-        e = fab.next_epoch(SLOT_NORM)
+        m.rs_sum_sumsq(self.grad_ptrs, self.world, lo, flat.shard_numel, 1.0, self.g_shard, self.stats,
+                       flat.tp_repl_end, 1.0 / flat.tp_size)
+        nf = self.norm_fabric
+        e = nf.next_epoch(SLOT_NORM)
         max_norm = float(self.h.max_grad_norm or 0.0)
-        m.norm_exchange(fab.pads.ptrs, fab.rank, self.world, e, self.stats, max_norm, self.tot, fab.budget_s)
+        m.norm_exchange(nf.pads.ptrs, nf.rank, nf.world, e, self.stats, max_norm, self.tot, nf.budget_s)
         self.step_count += 1
         b1, b2 = self.h.betas
         m.adamw_allgather(self.compute_ptrs, self.world, lo, flat.master, self.g_shard, flat.exp_avg,
@@ -217,10 +260,14 @@ class FusedShardedAdamW(ShardedAdamW):
         flat.zero_grad()
         norm_sq, bad, factor = self.tot.tolist()
         fab.check()
-        if bad > 0:
+        if nf is not fab:
+            nf.check()
+        if bad > 0:  # the kernels skipped the update on every rank
             self.step_count -= 1
+            overflow = 1.0 if (not math.isfinite(norm_sq) and max_norm > 0) else 0.0  # norm_exchange adds it
+            why = skip_reason(norm_sq, bad - overflow, max_norm)
             if check_finite:
-                raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements); step skipped")
+                raise NonFiniteGradientError(f"{why}; step skipped")
         return {"grad_norm": norm_sq**0.5, "clip_factor": factor}
 
     @torch.no_grad()
@@ -267,11 +314,11 @@ class CompositeAdamW:
         if self.distributed:
             dist.all_reduce(total, group=self.norm_group)
         norm_sq, bad = total.tolist()
-        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
-        if check_finite and bad > 0:
+        why = skip_reason(norm_sq, bad, self.h.max_grad_norm)
+        if check_finite and why is not None:
             for p in self.parts:
                 p.flat.zero_grad()
-            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
+            raise NonFiniteGradientError(why)
         norm = norm_sq**0.5
         factor = self.parts[0].clip_factor(norm)
         for p in self.parts:

@@ -56,7 +56,8 @@ class PackedBatch:
 
 class Engine:
     def __init__(self, model: CausalLM, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK, fabric=None, ep_dp_group=None, ep_dp_world: int = 1):
+                 lm_head_chunk: int = lm_head.DEFAULT_CHUNK, fabric=None, ep_dp_group=None, ep_dp_world: int = 1,
+                 norm_fabric=None):
         self.model = model
         # the optimizer owns the trainable store: the full model, or only the
         # LoRA adapters when the base is frozen; with expert parallelism the
@@ -67,9 +68,10 @@ class Engine:
                  ShardedAdamW(model.expert_flat, hyper, ep_dp_group, ep_dp_world)],
                 norm_group=None, distributed=dist.is_initialized() and dp_world > 1)
         elif fabric is not None:
-            self.opt = FusedShardedAdamW(model.trainable, hyper, fabric)
+            self.opt = FusedShardedAdamW(model.trainable, hyper, fabric, norm_fabric)
         else:
-            self.opt = ShardedAdamW(model.trainable, hyper, dp_group, dp_world)
+            self.opt = ShardedAdamW(model.trainable, hyper, dp_group, dp_world,
+                                    norm_world=model.trainable.tp_size > 1)
         self.fabric = fabric
         self.dp_group = dp_group
         self.dp_world = dp_world

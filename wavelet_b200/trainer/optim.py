@@ -35,7 +35,7 @@ import torch.distributed as dist
 
 from .. import ops
 from ..models.params import FlatParams
-from ..parallel.zero import AdamWHyper, NonFiniteGradientError, ShardedAdamW
+from ..parallel.zero import AdamWHyper, NonFiniteGradientError, ShardedAdamW, skip_reason
 
 
 def lr_at(step: int, base_lr: float, total_steps: int, sched) -> float:
@@ -126,7 +126,8 @@ class FlatOptimizer:
     """Common driver: reduce-scatter, norm/clip, per-type update, all-gather."""
 
     def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1, fabric=None,
-                 expert_flat: FlatParams | None = None, ep_dp_group=None, ep_dp_world: int = 1):
+                 expert_flat: FlatParams | None = None, ep_dp_group=None, ep_dp_world: int = 1,
+                 norm_fabric=None):
         self.flat = flat
         self.cfg = cfg
         self.type = cfg.type
@@ -149,10 +150,11 @@ class FlatOptimizer:
         elif fabric is not None and cfg.type in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
             from ..parallel.zero import FusedShardedAdamW
 
-            self.adamw = FusedShardedAdamW(flat, hyper, fabric)  # fused peer-memory RS + AdamW + AG
+            self.adamw = FusedShardedAdamW(flat, hyper, fabric, norm_fabric)  # fused peer-memory RS + AdamW + AG
         else:
             self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world,
-                                      offload=bool(getattr(cfg, "cpu_offload", False)))
+                                      offload=bool(getattr(cfg, "cpu_offload", False)),
+                                      norm_world=flat.tp_size > 1)
         self.momentum_buf = None
 
     @property
@@ -170,13 +172,13 @@ class FlatOptimizer:
         flat = self.flat
         g = a.reduce_grads()
         a.stats.zero_()
-        ops.sumsq_(g, a.stats)
-        if self.world > 1:
-            dist.all_reduce(a.stats, group=self.group)
+        a.local_sumsq_(g, a.stats)
+        a.reduce_stats_(a.stats)
         norm_sq, bad = a.stats.tolist()
-        bad += 0.0 if math.isfinite(norm_sq) else 1.0  # an overflowing norm is no usable clip
-        if bad > 0:
-            raise NonFiniteGradientError(f"non-finite gradients detected ({int(bad)} elements)")
+        why = skip_reason(norm_sq, bad, a.h.max_grad_norm)
+        if why is not None:
+            flat.zero_grad()
+            raise NonFiniteGradientError(why)
         norm = norm_sq**0.5
         factor = min(1.0, a.h.max_grad_norm / (norm + 1e-6)) if a.h.max_grad_norm > 0 else 1.0
         a.step_count += 1

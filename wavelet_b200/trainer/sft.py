@@ -75,10 +75,18 @@ class SFTTrainer:
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
         self.fabric = None
-        if dev.type == "cuda" and dims.dp == w.world_size and dims.ep == 1 and c.fsdp.backend != "gloo":
+        self.norm_fabric = None
+        if dev.type == "cuda" and dims.cp == 1 and dims.ep == 1 and c.fsdp.backend != "gloo":
             from ..parallel.fabric import maybe_fabric
 
-            self.fabric = maybe_fabric(dp_world, dp_rank, dev)
+            # the fused optimizer step runs over the data-parallel group (inside
+            # each tensor-parallel slice); under TP the gradient-norm exchange
+            # spans every rank of the job
+            self.fabric = maybe_fabric(dp_world, dp_rank, dev, group=self.groups.dp)
+            if self.fabric is not None and dims.tp > 1:
+                from ..parallel.fabric import Fabric
+
+                self.norm_fabric = Fabric(w.rank, w.world_size, dev)
         self.ep_fabric = None
         if dev.type == "cuda" and dims.ep > 1 and c.fsdp.backend != "gloo":
             from ..parallel.fabric import Fabric
@@ -112,7 +120,8 @@ class SFTTrainer:
             load_hf_weights(self.model, Path(c.model.name))
         self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, opt_group, opt_world,
                                        fabric=self.fabric, expert_flat=self.model.expert_flat,
-                                       ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size)
+                                       ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size,
+                                       norm_fabric=self.norm_fabric)
         self.engine = Engine(self.model, self.optimizer.adamw.h, opt_group, opt_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
@@ -303,7 +312,7 @@ def main(argv: list[str] | None = None) -> int:
     try:
         return trainer.train()
     finally:
-        for fab in (trainer.fabric, trainer.ep_fabric, trainer.tp_fabric):
+        for fab in (trainer.fabric, trainer.norm_fabric, trainer.ep_fabric, trainer.tp_fabric):
             if fab is not None:
                 fab.close()
         destroy_distributed()
