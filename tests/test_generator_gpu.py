@@ -110,3 +110,39 @@ def test_generator_logprobs_match_training_forward(cuda_ext, graphs):
         ref = lp[start : start + len(o.token_ids)].cpu()
         worst = max(worst, (ref - torch.tensor(o.logprobs)).abs().max().item())
     assert worst < 0.1, worst
+
+
+def test_sample_thresholds_kernel_matches_sort_oracle(cuda_ext):
+    """Device top-k / top-p thresholds: top-k is the exact k-th largest logit;
+    top-p is the logit at which the descending cumulative probability first
+    reaches p (the kept mass reaches p, the mass strictly above does not), on
+    bf16 rows with many tied values and mixed temperatures."""
+    from wavelet_b200.inference.engine import sampling_thresholds_reference
+
+    torch.manual_seed(0)
+    B, V = 9, 151936
+    z = (torch.randn(B, V, device="cuda") * 2.5).to(torch.bfloat16)
+    z[3, :100] = 30.0  # a block of ties at the top
+    top_k = [0, 1, 50, 120, 0, 0, 40, 3, 0]
+    top_p = [1.0, 1.0, 1.0, 0.9, 0.5, 0.95, 0.7, 1.0, 0.999]
+    inv_tau = torch.tensor([1.0, 1.0, 0.5, 1.0, 2.0, 1.0, 1.0 / 0.7, 1.0, 1.0], device="cuda")
+    out = torch.empty(B, device="cuda")
+    cuda_ext.sample_thresholds(z, torch.tensor(top_k, dtype=torch.int32, device="cuda"),
+                               torch.tensor(top_p, device="cuda"), inv_tau, out)
+    ref = sampling_thresholds_reference(z, top_k, top_p, inv_tau)
+    zf = z.float()
+    for i in range(B):
+        if top_k[i] == 0 and top_p[i] >= 1.0:
+            assert out[i].item() == float("-inf")
+            continue
+        if top_p[i] >= 1.0:
+            assert out[i].item() == ref[i].item(), (i, out[i].item(), ref[i].item())
+            continue
+        pr = torch.softmax(zf[i] * inv_tau[i], -1)
+        th = out[i].item()
+        kth = float(torch.topk(zf[i], top_k[i]).values[-1]) if top_k[i] > 0 else float("-inf")
+        pth = th if th > kth else None
+        if pth is not None:  # the nucleus decides: kept mass >= p, mass strictly above < p
+            assert float(pr[zf[i] >= pth].sum()) >= top_p[i] - 1e-4
+            assert float(pr[zf[i] > pth].sum()) < top_p[i] + 1e-4
+        assert abs(th - ref[i].item()) <= 0.0625 * max(1.0, abs(ref[i].item())), (i, th, ref[i].item())

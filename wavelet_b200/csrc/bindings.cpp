@@ -700,6 +700,22 @@ void sample_tokens(const at::Tensor& z, const at::Tensor& inv_tau, const c10::op
                     out_lp.data_ptr<float>(), cur_stream(), seed_dev ? seed_dev->data_ptr<int64_t>() : nullptr);
 }
 
+void sample_thresholds(const at::Tensor& z, const c10::optional<at::Tensor>& top_k,
+                       const c10::optional<at::Tensor>& top_p, const c10::optional<at::Tensor>& inv_tau,
+                       at::Tensor& out) {
+  check_bf16(z, "z");
+  WB_CHECK(z.dim() == 2 && z.stride(1) == 1, "sample_thresholds: z must be [B, V] row-major");
+  check_f32(out, "out");
+  WB_CHECK(out.numel() >= z.size(0), "sample_thresholds: out too small");
+  if (top_k) WB_CHECK(top_k->scalar_type() == at::kInt && top_k->is_contiguous(), "sample_thresholds: top_k int32");
+  if (top_p) check_f32(*top_p, "top_p");
+  if (inv_tau) check_f32(*inv_tau, "inv_tau");
+  const c10::cuda::CUDAGuard guard(z.device());
+  wb::sample_thresholds(z.data_ptr(), z.stride(0), (int)z.size(0), (int)z.size(1),
+                        top_k ? top_k->data_ptr<int32_t>() : nullptr, top_p ? top_p->data_ptr<float>() : nullptr,
+                        inv_tau ? inv_tau->data_ptr<float>() : nullptr, out.data_ptr<float>(), cur_stream());
+}
+
 void decode_advance(const at::Tensor& tok, const at::Tensor& lp, at::Tensor& ids, at::Tensor& pos, at::Tensor& ctx,
                     at::Tensor& slots, const at::Tensor& bt, int64_t block_size, at::Tensor& win_tok,
                     at::Tensor& win_lp, at::Tensor& step, at::Tensor& seed) {
@@ -749,6 +765,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &sample_tokens, py::arg("z"), py::arg("inv_tau"), py::arg("thresh"), py::arg("min_p"),
         py::arg("seed"), py::arg("row_ids"), py::arg("out_tok"), py::arg("out_lp"), py::arg("seed_dev") = py::none());
   m.def("decode_advance", &decode_advance);
+  m.def("sample_thresholds", &sample_thresholds, py::arg("z"), py::arg("top_k"), py::arg("top_p"),
+        py::arg("inv_tau"), py::arg("out"));
   m.def("fabric_malloc", &fabric_malloc_);
   m.def("fabric_free", &fabric_free_);
   m.def("fabric_export", &fabric_export_);

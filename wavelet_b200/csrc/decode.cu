@@ -624,6 +624,166 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st) {
   }
 }
 
+namespace {
+
+// Order-preserving 16-bit key of a bf16 value: larger value -> larger key.
+__device__ __forceinline__ uint32_t bf16_key(uint16_t b) { return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u); }
+__device__ __forceinline__ float key_value(uint32_t k) {
+  const uint16_t b = (k & 0x8000u) ? (uint16_t)(k & 0x7FFFu) : (uint16_t)(~k & 0xFFFFu);
+  return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+constexpr int TH_THREADS = 1024;
+
+// Scan 256 bins from the top (bin 255) down; returns the first bin whose
+// inclusive running total reaches `target`, and the total strictly above it
+// in *above*.  Runs in warp 0 (8 bins per lane), result broadcast via smem.
+template <typename T>
+__device__ int scan_desc(const T* bins, T target, T* above, int* s_bin, T* s_above) {
+  __syncthreads();  // every thread has read the previous scan's result; the bins are complete
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    T part = 0;  // lane l owns bins 255-8l .. 248-8l (descending)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part += bins[255 - 8 * lane - j];
+    T incl = part;  // inclusive prefix over lanes (descending bin order)
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const T excl = incl - part;
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= target);
+    const int first = hit ? __ffs(hit) - 1 : 31;
+    if (lane == first) {
+      T run = excl;
+      int bin = 248 - 8 * lane;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int b = 255 - 8 * lane - j;
+        if (run + bins[b] >= target || j == 7) {
+          bin = b;
+          break;
+        }
+        run += bins[b];
+      }
+      *s_bin = bin;
+      *s_above = run;
+    }
+  }
+  __syncthreads();
+  *above = *s_above;
+  return *s_bin;
+}
+
+// Per row: the sampling threshold in logit units (keep z >= thresh) of the
+// row's top-k (k-th largest logit) and top-p (the logit at which the sorted
+// cumulative probability of softmax(z * inv_tau) first reaches p), the larger
+// of the two; -inf when neither applies.  Radix select over the 16-bit bf16
+// keys: one pass for the max and the softmax denominator, one histogram pass
+// over the high byte (counts and probability mass), one over the low byte
+// inside the selected high-byte bins.  No sort, no host round trip.
+__global__ void __launch_bounds__(TH_THREADS) sample_thresh_kernel(const __nv_bfloat16* __restrict__ z, int64_t ldz,
+                                                                   int V, const int* __restrict__ top_k,
+                                                                   const float* __restrict__ top_p,
+                                                                   const float* __restrict__ inv_tau,
+                                                                   float* __restrict__ out) {
+  __shared__ unsigned cnt_hi[256], cnt_lo[256];
+  __shared__ float mass_hi[256], mass_lo[256];
+  __shared__ float red[32];
+  __shared__ int s_bin;
+  __shared__ unsigned s_above_u;
+  __shared__ float s_above_f;
+  const int row = blockIdx.x;
+  const uint16_t* zr = reinterpret_cast<const uint16_t*>(z + (int64_t)row * ldz);
+  const int k = top_k ? top_k[row] : 0;
+  const float p = top_p ? top_p[row] : 1.f;
+  const float it = inv_tau ? inv_tau[row] : 1.f;
+  const bool use_k = k > 0 && k < V;
+  const bool use_p = p < 1.f && it > 0.f;
+  if (!use_k && !use_p) {
+    if (threadIdx.x == 0) out[row] = -INFINITY;
+    return;
+  }
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) cnt_hi[i] = 0, cnt_lo[i] = 0, mass_hi[i] = 0.f, mass_lo[i] = 0.f;
+  // pass 1: row max (for a stable softmax mass)
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, __bfloat162float(__ushort_as_bfloat16(zr[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  // pass 2: high-byte histograms (count, mass) and the softmax denominator
+  float tot = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const uint16_t b = zr[i];
+    const uint32_t key = bf16_key(b);
+    if (use_k) atomicAdd(&cnt_hi[key >> 8], 1u);
+    if (use_p) {
+      const float e = __expf((__bfloat162float(__ushort_as_bfloat16(b)) - mx) * it);
+      tot += e;
+      atomicAdd(&mass_hi[key >> 8], e);
+    }
+  }
+  if (use_p) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = tot;
+  }
+  __syncthreads();
+  if (use_p && threadIdx.x == 0) {
+    float v = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[w];  // fixed order
+    red[0] = v;
+  }
+  __syncthreads();
+  tot = red[0];
+  int hk = -1, hp = -1;
+  unsigned above_k = 0;
+  float above_p = 0.f;
+  if (use_k) hk = scan_desc<unsigned>(cnt_hi, (unsigned)k, &above_k, &s_bin, &s_above_u);
+  if (use_p) hp = scan_desc<float>(mass_hi, p * tot, &above_p, &s_bin, &s_above_f);
+  // pass 3: low-byte histograms inside the selected high-byte bins
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const uint16_t b = zr[i];
+    const uint32_t key = bf16_key(b);
+    const int hi = (int)(key >> 8);
+    if (hi == hk) atomicAdd(&cnt_lo[key & 255u], 1u);
+    if (hi == hp) atomicAdd(&mass_lo[key & 255u], __expf((__bfloat162float(__ushort_as_bfloat16(b)) - mx) * it));
+  }
+  __syncthreads();
+  float th = -INFINITY;
+  if (use_k) {
+    unsigned a2 = 0;
+    const int lo = scan_desc<unsigned>(cnt_lo, (unsigned)k - above_k, &a2, &s_bin, &s_above_u);
+    th = key_value(((uint32_t)hk << 8) | (uint32_t)lo);
+  }
+  if (use_p) {
+    float a2 = 0.f;
+    const int lo = scan_desc<float>(mass_lo, p * tot - above_p, &a2, &s_bin, &s_above_f);
+    th = fmaxf(th, key_value(((uint32_t)hp << 8) | (uint32_t)lo));
+  }
+  if (threadIdx.x == 0) out[row] = th;
+}
+
+}  // namespace
+
+void sample_thresholds(const void* z, int64_t ldz, int rows, int V, const int* top_k, const float* top_p,
+                       const float* inv_tau, float* out, cudaStream_t st) {
+  if (rows <= 0) return;
+  sample_thresh_kernel<<<rows, TH_THREADS, 0, st>>>((const __nv_bfloat16*)z, ldz, V, top_k, top_p, inv_tau, out);
+  note_launch();
+}
+
 void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv_tau, const float* thresh,
                    float min_p, uint64_t seed, const int64_t* row_ids, int64_t* out_tok, float* out_lp,
                    cudaStream_t st, const int64_t* seed_dev) {

@@ -28,6 +28,11 @@ void decode_attention(const DecodeArgs& a, cudaStream_t st);
 void sample_tokens(const void* z, int64_t ldz, int rows, int V, const float* inv_tau, const float* thresh,
                    float min_p, uint64_t seed, const int64_t* row_ids, int64_t* out_tok, float* out_lp,
                    cudaStream_t st, const int64_t* seed_dev = nullptr);
+// Per-row sampling threshold in logit units for top-k (top_k[i] > 0) and
+// top-p (top_p[i] < 1, softmax of z * inv_tau): keep z >= out[i]; -inf where
+// neither applies.  top_k / top_p / inv_tau may be null (off).
+void sample_thresholds(const void* z, int64_t ldz, int rows, int V, const int* top_k, const float* top_p,
+                       const float* inv_tau, float* out, cudaStream_t st);
 void decode_advance(const int64_t* tok, const float* lp, int64_t* ids, int32_t* pos, int32_t* ctx, int32_t* slots,
                     const int32_t* bt, int max_blocks, int block_size, int64_t* win_tok, float* win_lp, int win_ld,
                     int32_t* step, int64_t* seed, int rows, cudaStream_t st);

@@ -48,6 +48,30 @@ from ..ops import reference as ref
 from ..ops.attention import attention_fwd
 
 
+def sampling_thresholds_reference(z: torch.Tensor, top_k: list[int], top_p: list[float],
+                                  inv_tau: torch.Tensor) -> torch.Tensor:
+    """Per-row sampling threshold in logit units (keep ``z >= thresh``): the
+    k-th largest logit for top-k, and for top-p the logit at which the
+    descending cumulative probability of softmax(z * inv_tau) first reaches p;
+    the larger of the two, -inf where neither applies.  Sort-based float32
+    oracle of the ``sample_thresholds`` kernel (and its CPU path)."""
+    B = z.shape[0]
+    zf = z.float()
+    th = torch.full((B,), float("-inf"), device=z.device)
+    for i in range(B):
+        t = float("-inf")
+        if top_k[i] > 0 and top_k[i] < zf.shape[1]:
+            t = float(torch.topk(zf[i], top_k[i]).values[-1])
+        it = float(inv_tau[i])
+        if top_p[i] < 1.0 and it > 0:
+            srt = torch.sort(zf[i], descending=True).values
+            c = torch.softmax(srt * it, -1).cumsum(-1)
+            k = int((c < top_p[i]).sum()) + 1
+            t = max(t, float(srt[min(k, srt.numel()) - 1]))
+        th[i] = t
+    return th
+
+
 @dataclass
 class SamplingParams:
     temperature: float = 1.0
@@ -295,26 +319,17 @@ class Generator:
         inv_tau = torch.tensor([(1.0 / s.params.temperature) if s.params.temperature > 0 else 0.0 for s in seqs],
                                device=self.dev, dtype=torch.float32)
         thresh = None
-        need_k = [s.params.top_k for s in seqs if s.params.top_k > 0]
-        if need_k:
-            kmax = max(need_k)
-            top = torch.topk(z.float(), kmax, dim=-1).values
-            th = torch.full((B,), float("-inf"), device=self.dev)
-            for i, s in enumerate(seqs):
-                if s.params.top_k > 0:
-                    th[i] = top[i, s.params.top_k - 1]
-            thresh = th
-        top_p_rows = [i for i, s in enumerate(seqs) if s.params.top_p < 1.0]
-        if top_p_rows:
-            # nucleus: threshold = smallest logit inside the top-p mass (sorted once per row)
-            zz = z[top_p_rows].float() * inv_tau[top_p_rows, None].clamp_min(1e-6)
-            srt, _ = torch.sort(zz, dim=-1, descending=True)
-            pr = torch.softmax(srt, -1).cumsum(-1)
-            th_p = torch.full((B,), float("-inf"), device=self.dev)
-            for j, i in enumerate(top_p_rows):
-                k = int((pr[j] < seqs[i].params.top_p).sum().item()) + 1
-                th_p[i] = srt[j, min(k, srt.shape[1]) - 1] / max(1e-6, float(inv_tau[i]))
-            thresh = th_p if thresh is None else torch.maximum(thresh, th_p)
+        need_k = any(s.params.top_k > 0 for s in seqs)
+        need_p = any(s.params.top_p < 1.0 for s in seqs)
+        if (need_k or need_p) and z.is_cuda:
+            # device radix select over the bf16 logits: no sort, no per-row host work
+            thresh = torch.empty(B, device=self.dev, dtype=torch.float32)
+            tk = torch.tensor([s.params.top_k for s in seqs], dtype=torch.int32, device=self.dev) if need_k else None
+            tp = torch.tensor([s.params.top_p for s in seqs], dtype=torch.float32, device=self.dev) if need_p else None
+            ops.ext().sample_thresholds(z, tk, tp, inv_tau, thresh)
+        elif need_k or need_p:
+            thresh = sampling_thresholds_reference(z, [s.params.top_k for s in seqs],
+                                                   [s.params.top_p for s in seqs], inv_tau)
         min_p = max((s.params.min_p for s in seqs), default=0.0)
         tok = torch.empty(B, dtype=torch.long, device=self.dev)
         lp = torch.empty(B, dtype=torch.float32, device=self.dev)
@@ -337,7 +352,14 @@ class Generator:
             if min_p > 0:
                 zt = z.float() * inv_tau[:, None]
                 keep &= zt >= (zt.max(-1, keepdim=True).values + math.log(min_p))
-            masks = [keep[i].nonzero().flatten().tolist() if seqs[i].params.return_sampling_mask else None for i in range(B)]
+            # one device -> host transfer for every row's kept token ids
+            nz = keep.nonzero().cpu()
+            counts = keep.sum(-1).cpu().tolist()
+            cols = nz[:, 1].tolist()
+            masks, off = [], 0
+            for i in range(B):
+                masks.append(cols[off:off + counts[i]] if seqs[i].params.return_sampling_mask else None)
+                off += counts[i]
         return tok, lp, masks
 
     # -------------------------------------------------------------- driver
