@@ -194,3 +194,36 @@ def test_softmax_stats_ragged_vocab(cuda_ext, V, tau):
     lse2 = torch.empty(R, device="cuda")
     cuda_ext.softmax_stats(buf2[:, :V], tgt, 1.0 / tau, lse2, None, None)
     torch.testing.assert_close(lse2, lse, rtol=0, atol=0)
+
+
+def test_adamw8_kernel_matches_cpu_oracle(cuda_ext):
+    """8-bit AdamW kernel against the float32 torch formulation of the same
+    codes: parameters to float rounding, decoded moments within one code step
+    (log2 / exp2 may round a boundary value to the neighbouring code)."""
+    from wavelet_b200 import ops
+
+    torch.manual_seed(0)
+    n = 256 * 37 + 101  # a partial last block
+    p = torch.randn(n) * 0.02
+    m8 = torch.zeros(n, dtype=torch.int8)
+    v8 = torch.zeros(n, dtype=torch.uint8)
+    nb = (n + 255) // 256
+    am, av = torch.zeros(nb), torch.zeros(nb)
+    pd, m8d, v8d, amd, avd = (t.cuda() for t in (p.clone(), m8.clone(), v8.clone(), am.clone(), av.clone()))
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    for step in range(1, 6):
+        g = torch.randn(n) * torch.exp2(torch.randint(-8, 2, (n,)).float())
+        kw = dict(lr=1e-2, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1, step=step, gscale_host=0.5)
+        ops.adamw8_flat_(p, g, m8, v8, am, av, None, **kw)
+        ops.adamw8_flat_(pd, g.cuda(), m8d, v8d, amd, avd, p16, **kw)
+        # re-sync the codes so the next step starts from the same state
+        torch.testing.assert_close(pd.cpu(), p, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(amd.cpu(), am, rtol=1e-5, atol=0)
+        dm = (m8d.cpu().int() - m8.int()).abs()
+        dv = (v8d.cpu().int() - v8.int()).abs()
+        assert int(dm.max()) <= 1 and int(dv.max()) <= 1
+        assert float((dm > 0).float().mean()) < 0.01
+        m8d.copy_(m8.cuda())
+        v8d.copy_(v8.cuda())
+        pd.copy_(p.cuda())
+    torch.testing.assert_close(p16.float().cpu(), p.to(torch.bfloat16).float(), rtol=1e-2, atol=1e-4)

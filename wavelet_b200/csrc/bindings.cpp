@@ -510,6 +510,46 @@ void adamw_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v
                  cur_stream());
 }
 
+void adamw8_step(at::Tensor& p, const at::Tensor& g, at::Tensor& m8, at::Tensor& v8, at::Tensor& am,
+                 at::Tensor& av, const c10::optional<at::Tensor>& p16, double lr, double b1, double b2, double eps,
+                 double wd, int64_t step, const c10::optional<at::Tensor>& gscale_dev, double gscale_host) {
+  check_f32(p, "p");
+  check_f32(g, "g");
+  check_f32(am, "am");
+  check_f32(av, "av");
+  const int64_t n = p.numel();
+  WB_CHECK(p.is_contiguous() && g.is_contiguous() && m8.is_contiguous() && v8.is_contiguous(),
+           "adamw8: buffers must be contiguous");
+  WB_CHECK(m8.scalar_type() == at::kChar && v8.scalar_type() == at::kByte, "adamw8: m8 int8, v8 uint8");
+  WB_CHECK(g.numel() == n && m8.numel() == n && v8.numel() == n, "adamw8: size mismatch");
+  WB_CHECK(am.numel() >= (n + 255) / 256 && av.numel() >= (n + 255) / 256, "adamw8: scale buffers too small");
+  if (p16) {
+    check_bf16(*p16, "p16");
+    WB_CHECK(p16->numel() == n && p16->is_contiguous(), "adamw8: bad p16");
+  }
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  const c10::cuda::CUDAGuard guard(p.device());
+  wb::adamw8_step(p.data_ptr<float>(), g.data_ptr<float>(), m8.data_ptr<int8_t>(), v8.data_ptr<uint8_t>(),
+                  am.data_ptr<float>(), av.data_ptr<float>(), p16 ? p16->data_ptr() : nullptr, n, (float)lr,
+                  (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
+                  gscale_dev ? gscale_dev->data_ptr<float>() : nullptr, (float)gscale_host, cur_stream());
+}
+
+// Managed ("paged") device memory: pages migrate to host memory under device
+// memory pressure and back on access; preferred location is `device`.
+at::Tensor managed_empty(int64_t nbytes, int64_t device) {
+  void* ptr = nullptr;
+  WB_CHECK(cudaMallocManaged(&ptr, (size_t)std::max<int64_t>(nbytes, 1)) == cudaSuccess, "cudaMallocManaged failed");
+  cudaMemLocation loc{};
+  loc.type = cudaMemLocationTypeDevice;
+  loc.id = (int)device;
+  cudaMemAdvise(ptr, (size_t)std::max<int64_t>(nbytes, 1), cudaMemAdviseSetPreferredLocation, loc);
+  cudaMemset(ptr, 0, (size_t)std::max<int64_t>(nbytes, 1));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return at::from_blob(ptr, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+}
+
 void sumsq(const at::Tensor& x, at::Tensor& out) {
   check_f32(x, "x");
   check_f32(out, "out");
@@ -755,6 +795,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &embedding_bwd);
   m.def("adamw_step", &adamw_step);
   m.def("sumsq", &sumsq);
+  m.def("adamw8_step", &adamw8_step);
+  m.def("managed_empty", &managed_empty);
   m.def("clip_factor", &clip_factor);
   m.def("softmax_stats", &softmax_stats);
   m.def("softmax_grad", &softmax_grad);

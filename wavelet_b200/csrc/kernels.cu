@@ -464,6 +464,92 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// ------------------------------------------------------------------ 8-bit AdamW
+// AdamW whose moments live in 8 bits per element with one fp32 scale per
+// block of 256 elements (the memory class of bitsandbytes' 8-bit Adam,
+// reference trainer/optim.py:393-512; the code is this library's own).
+// Codes are logarithmic, relative to the block's absolute maximum a:
+//   m (signed):  c in [-127, 127], |m| = a * 2^((|c| - 127) / 8), c = 0 -> 0
+//   v (>= 0):    c in [0, 255],     v = a * 2^((c - 255) / 16),   c = 0 -> 0
+// i.e. a relative step of 2^(1/8) (9%) for m and 2^(1/16) (4.4%) for v over
+// about 16 octaves below the block maximum.  Each step dequantises, runs the
+// fp32 AdamW update, takes the new block maxima and re-quantises (round to
+// nearest in the log domain).  The fp32 master weights are kept in full.
+constexpr int kQ8Block = 256;
+
+__device__ __forceinline__ float q8m_decode(int8_t c, float a) {
+  if (c == 0) return 0.f;
+  const int mag = c < 0 ? -c : c;
+  const float v = a * exp2f((float)(mag - 127) * 0.125f);
+  return c < 0 ? -v : v;
+}
+__device__ __forceinline__ int8_t q8m_encode(float x, float a) {
+  if (!(a > 0.f) || x == 0.f) return 0;
+  const float r = fabsf(x) / a;
+  float l = 127.f + 8.f * log2f(r);
+  int c = (int)rintf(l);
+  if (c < 1) c = (r >= 0.5f * exp2f(-126.f * 0.125f)) ? 1 : 0;
+  c = min(c, 127);
+  return (int8_t)(x < 0.f ? -c : c);
+}
+__device__ __forceinline__ float q8v_decode(uint8_t c, float a) {
+  return c == 0 ? 0.f : a * exp2f((float)((int)c - 255) * 0.0625f);
+}
+__device__ __forceinline__ uint8_t q8v_encode(float x, float a) {
+  if (!(a > 0.f) || !(x > 0.f)) return 0;
+  const float r = x / a;
+  int c = (int)rintf(255.f + 16.f * log2f(r));
+  if (c < 1) c = (r >= 0.5f * exp2f(-254.f * 0.0625f)) ? 1 : 0;
+  return (uint8_t)min(c, 255);
+}
+
+__global__ void __launch_bounds__(kQ8Block) adamw8_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                                          int8_t* __restrict__ m8, uint8_t* __restrict__ v8,
+                                                          float* __restrict__ am, float* __restrict__ av,
+                                                          __nv_bfloat16* __restrict__ p16, int64_t n, float lr,
+                                                          float b1, float b2, float eps, float wd, float bc1,
+                                                          float bc2, const float* __restrict__ gscale_dev,
+                                                          float gscale_host) {
+  __shared__ float red_m[kQ8Block / 32], red_v[kQ8Block / 32];
+  const float gs = gscale_host * (gscale_dev ? *gscale_dev : 1.f);
+  const float step = lr / bc1;
+  const float rbc2 = rsqrtf(bc2);
+  const int64_t nblk = (n + kQ8Block - 1) / kQ8Block;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int64_t i = blk * kQ8Block + threadIdx.x;
+    const bool ok = i < n;
+    float m = 0.f, v = 0.f;
+    if (ok) {
+      const float gj = g[i] * gs;
+      m = b1 * q8m_decode(m8[i], am[blk]) + (1.f - b1) * gj;
+      v = b2 * q8v_decode(v8[i], av[blk]) + (1.f - b2) * gj * gj;
+      float w = p[i] * (1.f - lr * wd);
+      w -= step * m / (sqrtf(v) * rbc2 + eps);
+      p[i] = w;
+      if (p16) p16[i] = __float2bfloat16(w);
+    }
+    float mx_m = fabsf(m), mx_v = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx_m = fmaxf(mx_m, __shfl_xor_sync(0xffffffffu, mx_m, o));
+      mx_v = fmaxf(mx_v, __shfl_xor_sync(0xffffffffu, mx_v, o));
+    }
+    if (lane == 0) red_m[wid] = mx_m, red_v[wid] = mx_v;
+    __syncthreads();
+    mx_m = red_m[0];
+    mx_v = red_v[0];
+#pragma unroll
+    for (int w = 1; w < kQ8Block / 32; ++w) mx_m = fmaxf(mx_m, red_m[w]), mx_v = fmaxf(mx_v, red_v[w]);
+    __syncthreads();  // red_* is rewritten by the next block's reduction
+    if (ok) {
+      m8[i] = q8m_encode(m, mx_m);
+      v8[i] = q8v_encode(v, mx_v);
+    }
+    if (threadIdx.x == 0) am[blk] = mx_m, av[blk] = mx_v;
+  }
+}
+
 // Cross-block scratch of the deterministic grid sums (one launch at a time per
 // device: the optimizer's reductions run in stream order).
 constexpr int kMaxSumBlocks = 1024;
@@ -830,6 +916,15 @@ void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t
   if (n <= 0) return;
   adamw_kernel<<<grid_for((n + 3) / 4, 256, 148 * 8), 256, 0, st>>>(
       p, g, m, v, (__nv_bfloat16*)p16, n, lr, b1, b2, eps, wd, bc1, bc2, gscale_dev, gscale_host); note_launch();
+}
+
+void adamw8_step(float* p, const float* g, int8_t* m8, uint8_t* v8, float* am, float* av, void* p16, int64_t n,
+                 float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, const float* gscale_dev,
+                 float gscale_host, cudaStream_t st) {
+  if (n <= 0) return;
+  adamw8_kernel<<<grid_for((n + kQ8Block - 1) / kQ8Block, 1, 148 * 8), kQ8Block, 0, st>>>(
+      p, g, m8, v8, am, av, (__nv_bfloat16*)p16, n, lr, b1, b2, eps, wd, bc1, bc2, gscale_dev, gscale_host);
+  note_launch();
 }
 
 void sumsq(const float* x, int64_t n, float* out, cudaStream_t st) {

@@ -29,6 +29,11 @@ void splitk_reduce(const float* ws, int S, int64_t M, int N, void* out, int64_t 
                    int64_t ldr, float alpha, cudaStream_t st);
 void nf4_dequant(const void* codes, const float* absmax, void* out, int64_t numel, const float* lut,
                  cudaStream_t st);
+// AdamW with 8-bit block-scaled moments (256 elements per fp32 scale, log
+// codes; see kernels.cu).  m8 / v8: n codes; am / av: ceil(n / 256) scales.
+void adamw8_step(float* p, const float* g, int8_t* m8, uint8_t* v8, float* am, float* av, void* p16, int64_t n,
+                 float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, const float* gscale_dev,
+                 float gscale_host, cudaStream_t st);
 void adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, float lr,
                 float b1, float b2, float eps, float wd, float bc1, float bc2,
                 const float* gscale_dev, float gscale_host, cudaStream_t st);

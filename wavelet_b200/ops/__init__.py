@@ -368,6 +368,95 @@ def adamw_flat_(p, g, m, v, p16, *, lr, betas, eps, weight_decay, step, gscale=N
     ext().adamw_step(p, g, m, v, p16, lr, betas[0], betas[1], eps, weight_decay, step, gscale, gscale_host)
 
 
+Q8_BLOCK = 256
+
+
+def q8m_decode(c: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    """8-bit signed log code -> value (block scale ``a`` broadcast per 256)."""
+    mag = c.abs().float()
+    v = a * torch.exp2((mag - 127.0) * 0.125)
+    return torch.where(c == 0, torch.zeros_like(v), torch.where(c < 0, -v, v))
+
+
+def q8m_encode(x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    r = x.abs() / a.clamp_min(1e-38)
+    c = torch.round(127.0 + 8.0 * torch.log2(r.clamp_min(1e-38)))
+    small = torch.where(r >= 0.5 * 2.0 ** (-126 * 0.125), 1.0, 0.0)
+    c = torch.where(c < 1, small, c).clamp(max=127)
+    c = torch.where((a > 0) & (x != 0), c, torch.zeros_like(c))
+    return torch.where(x < 0, -c, c).to(torch.int8)
+
+
+def q8v_decode(c: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    v = a * torch.exp2((c.float() - 255.0) * 0.0625)
+    return torch.where(c == 0, torch.zeros_like(v), v)
+
+
+def q8v_encode(x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    r = x / a.clamp_min(1e-38)
+    c = torch.round(255.0 + 16.0 * torch.log2(r.clamp_min(1e-38)))
+    small = torch.where(r >= 0.5 * 2.0 ** (-254 * 0.0625), 1.0, 0.0)
+    c = torch.where(c < 1, small, c).clamp(max=255)
+    c = torch.where((a > 0) & (x > 0), c, torch.zeros_like(c))
+    return c.to(torch.uint8)
+
+
+def q8_dequant_moments(m8, v8, am, av):
+    """fp32 (m, v) of 8-bit block-coded moments (checkpoint re-sharding)."""
+    n = m8.numel()
+    nb = (n + Q8_BLOCK - 1) // Q8_BLOCK
+    idx = torch.arange(n, device=m8.device) // Q8_BLOCK
+    return q8m_decode(m8, am[:nb][idx]), q8v_decode(v8, av[:nb][idx])
+
+
+def q8_quant_moments(m, v):
+    """8-bit codes and block scales of fp32 moments (m, v)."""
+    n = m.numel()
+    nb = (n + Q8_BLOCK - 1) // Q8_BLOCK
+    pad = nb * Q8_BLOCK - n
+    mb = torch.nn.functional.pad(m.float(), (0, pad)).view(nb, Q8_BLOCK)
+    vb = torch.nn.functional.pad(v.float(), (0, pad)).view(nb, Q8_BLOCK)
+    am, av = mb.abs().amax(1), vb.amax(1)
+    return (q8m_encode(mb, am[:, None]).reshape(-1)[:n], q8v_encode(vb, av[:, None]).reshape(-1)[:n], am, av)
+
+
+def adamw8_flat_(p, g, m8, v8, am, av, p16, *, lr, betas, eps, weight_decay, step, gscale=None, gscale_host=1.0):
+    """AdamW with 8-bit block-scaled log-coded moments (csrc/kernels.cu
+    ``adamw8_kernel``); the CPU branch is the same math in float32 torch."""
+    if p.is_cuda:
+        ext().adamw8_step(p, g, m8, v8, am, av, p16, lr, betas[0], betas[1], eps, weight_decay, step, gscale,
+                          gscale_host)
+        return
+    b1, b2 = betas
+    n = p.numel()
+    nb = (n + Q8_BLOCK - 1) // Q8_BLOCK
+    pad = nb * Q8_BLOCK - n
+
+    def blocks(t, fill=0):
+        return torch.nn.functional.pad(t, (0, pad), value=fill).view(nb, Q8_BLOCK)
+
+    gg = blocks(g.float() * gscale_host * (float(gscale) if gscale is not None else 1.0))
+    m = b1 * q8m_decode(blocks(m8), am[:nb, None]) + (1 - b1) * gg
+    v = b2 * q8v_decode(blocks(v8), av[:nb, None]) + (1 - b2) * gg * gg
+    bc1, bc2 = 1 - b1**step, 1 - b2**step
+    pp = blocks(p) * (1 - lr * weight_decay) - (lr / bc1) * m / (v.sqrt() / math.sqrt(bc2) + eps)
+    valid = torch.ones(nb * Q8_BLOCK, dtype=torch.bool)
+    if pad:
+        valid[n:] = False
+    valid = valid.view(nb, Q8_BLOCK)
+    m = torch.where(valid, m, torch.zeros_like(m))
+    v = torch.where(valid, v, torch.zeros_like(v))
+    amax_m = m.abs().amax(1)
+    amax_v = v.amax(1)
+    p.copy_(pp.reshape(-1)[:n])
+    m8.copy_(q8m_encode(m, amax_m[:, None]).reshape(-1)[:n])
+    v8.copy_(q8v_encode(v, amax_v[:, None]).reshape(-1)[:n])
+    am[:nb] = amax_m
+    av[:nb] = amax_v
+    if p16 is not None:
+        p16.copy_(p)
+
+
 def sumsq_(x, out):
     if not x.is_cuda:
         out[0] += x.double().pow(2).sum().float()

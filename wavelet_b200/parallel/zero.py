@@ -215,6 +215,79 @@ class ShardedAdamW:
             dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
 
 
+class ShardedAdamW8bit(ShardedAdamW):
+    """ZeRO step with 8-bit moments: the fp32 master shard is kept, the two
+    AdamW moments are stored as 8-bit block-scaled log codes (one fp32 scale
+    per 256 elements; ``ops.adamw8_flat_``), 2 bytes per element instead of 8.
+    ``paged``: the codes live in CUDA managed memory, which migrates to host
+    memory under device memory pressure (the role of bitsandbytes' paged
+    optimizers, reference trainer/optim.py:393-512)."""
+
+    def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
+                 paged: bool = False, norm_world: bool = False):
+        super().__init__(flat, hyper, dp_group, dp_world, norm_world=norm_world)
+        n = flat.shard_numel
+        nb = (n + ops.Q8_BLOCK - 1) // ops.Q8_BLOCK
+        dev = flat.device
+        self.paged = paged and dev.type == "cuda"
+        if self.paged:
+            m = ops.ext()
+            idx = dev.index if dev.index is not None else torch.cuda.current_device()
+            self.m8 = m.managed_empty(n, idx).view(torch.int8)
+            self.v8 = m.managed_empty(n, idx)
+        else:
+            self.m8 = torch.zeros(n, device=dev, dtype=torch.int8)
+            self.v8 = torch.zeros(n, device=dev, dtype=torch.uint8)
+        self.am = torch.zeros(nb, device=dev, dtype=torch.float32)
+        self.av = torch.zeros(nb, device=dev, dtype=torch.float32)
+        # the fp32 moments of the store are not used: free them
+        flat.exp_avg = None
+        flat.exp_avg_sq = None
+
+    @torch.no_grad()
+    def apply(self, lr: float, factor: float) -> None:
+        flat = self.flat
+        self.step_count += 1
+        compute = flat.compute.detach()
+        p16 = compute[flat.shard_slice]
+        ops.adamw8_flat_(flat.master, self._g, self.m8, self.v8, self.am, self.av,
+                         p16 if flat.compute.dtype == torch.bfloat16 else None,
+                         lr=lr, betas=self.h.betas, eps=self.h.eps, weight_decay=self.h.weight_decay,
+                         step=self.step_count, gscale_host=factor)
+        if compute.dtype != torch.bfloat16:
+            p16.copy_(flat.master)
+        if self.world > 1:
+            src = p16 if compute.is_cuda else p16.clone()
+            dist.all_gather_into_tensor(compute, src, group=self.group)
+        flat.zero_grad()
+        self._g = None
+
+    def state_dict(self) -> dict:
+        return {"step": self.step_count, "master": self.flat.master, "m8": self.m8, "v8": self.v8,
+                "m8_scale": self.am, "v8_scale": self.av}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict) -> None:
+        self.step_count = int(sd["step"])
+        self.flat.master.copy_(sd["master"])
+        if "m8" in sd:
+            self.m8.copy_(sd["m8"])
+            self.v8.copy_(sd["v8"])
+            self.am.copy_(sd["m8_scale"])
+            self.av.copy_(sd["v8_scale"])
+        else:  # fp32 moments (a re-sharded or fp32-AdamW checkpoint): quantise
+            m8, v8, am, av = ops.q8_quant_moments(sd["exp_avg"].to(self.am.device), sd["exp_avg_sq"].to(self.am.device))
+            self.m8.copy_(m8)
+            self.v8.copy_(v8)
+            self.am.copy_(am)
+            self.av.copy_(av)
+        compute = self.flat.compute.detach()
+        p16 = compute[self.flat.shard_slice]
+        p16.copy_(self.flat.master.to(p16.dtype))
+        if self.world > 1:
+            dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
+
+
 class FusedShardedAdamW(ShardedAdamW):
     """ZeRO step as fused peer-memory kernels (one node, world <= 8).
 

@@ -174,6 +174,12 @@ class CheckpointManager:
                 # re-shard: concatenate every saved shard then take ours
                 parts = [torch.load(d / "trainer" / f"optim-rank{r}.pt", map_location="cpu", weights_only=False) for r in range(saved_world)]
                 sd = {"step": parts[0]["step"]}
+                if "m8" in parts[0]:  # 8-bit moments: block scales do not survive re-sharding; go through fp32
+                    from ..ops import q8_dequant_moments
+
+                    for q in parts:
+                        q["exp_avg"], q["exp_avg_sq"] = q8_dequant_moments(q["m8"], q["v8"], q["m8_scale"],
+                                                                           q["v8_scale"])
                 for k in ("master", "exp_avg", "exp_avg_sq"):
                     full = torch.cat([p[k] for p in parts])
                     full = torch.nn.functional.pad(full, (0, max(0, flat.numel - full.numel())))[: flat.numel]

@@ -18,8 +18,10 @@ local fp32 master shard after the gradient reduce-scatter:
   and each rank orthogonalises every matrix that overlaps its shard; the
   per-matrix gradient norms are summed over the shards with one small
   all-reduce.
-* 8-bit variants are served by the fp32 AdamW (bitsandbytes is not part of
-  this framework).
+* ``adamw_8bit`` / ``adam_8bit`` / ``paged_adamw_8bit`` — AdamW with 8-bit
+  block-scaled moments (``parallel.zero.ShardedAdamW8bit``); the paged
+  variant keeps the 8-bit state in CUDA managed memory (the reference uses
+  bitsandbytes for these, trainer/optim.py:393-512).
 
 Schedules: constant, linear, cosine, sqrt with warmup, as closed forms of
 the reference's torch scheduler chains (trainer/optim.py:513-832).
@@ -140,14 +142,21 @@ class FlatOptimizer:
         )
         if expert_flat is not None:
             # expert parallelism: dense + expert stores, one global clip
-            if cfg.type not in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
-                raise NotImplementedError("expert parallelism supports the AdamW family only")
+            if cfg.type not in ("adamw", "adam"):
+                raise NotImplementedError("expert parallelism supports optim.type adamw / adam only")
             from ..parallel.zero import CompositeAdamW
 
             self.adamw = CompositeAdamW([ShardedAdamW(flat, hyper, dp_group, dp_world),
                                          ShardedAdamW(expert_flat, hyper, ep_dp_group, ep_dp_world)],
                                         distributed=dist.is_initialized() and dp_world > 1)
-        elif fabric is not None and cfg.type in ("adamw", "adam", "adamw_8bit", "adam_8bit"):
+        elif cfg.type in ("adamw_8bit", "adam_8bit", "paged_adamw_8bit"):
+            if getattr(cfg, "cpu_offload", False):
+                raise ValueError("optim.cpu_offload does not apply to the 8-bit optimizers")
+            from ..parallel.zero import ShardedAdamW8bit
+
+            self.adamw = ShardedAdamW8bit(flat, hyper, dp_group, dp_world, paged=cfg.type == "paged_adamw_8bit",
+                                          norm_world=flat.tp_size > 1)
+        elif fabric is not None and cfg.type in ("adamw", "adam"):
             from ..parallel.zero import FusedShardedAdamW
 
             self.adamw = FusedShardedAdamW(flat, hyper, fabric, norm_fabric)  # fused peer-memory RS + AdamW + AG
