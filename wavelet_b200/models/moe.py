@@ -119,11 +119,16 @@ class MoEBlock:
         self.aux_loss_scale = 0.0
         self.last_aux = None
         self.last_counts = None
+        self.router_logits_bf16 = False  # model.moe_router_dtype == 'none' (set by apply_model_options)
 
     # ------------------------------------------------------------ shared
     def _route(self, h2, P):
         cfg = self.cfg
         logits = ops.gemm(h2, P["router_w"], epi=ops.EPI_F32)
+        if self.router_logits_bf16:
+            # model.moe_router_dtype 'none': the gate runs in the model dtype, so
+            # its logits are bf16 values (fp32 accumulation, bf16 output)
+            logits = logits.to(torch.bfloat16).float()
         probs = torch.softmax(logits, -1)
         topv, topi = torch.topk(probs, cfg.num_experts_per_tok, dim=-1)
         s = topv.sum(-1, keepdim=True)

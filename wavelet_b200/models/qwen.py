@@ -168,9 +168,36 @@ class CausalLM:
         for i, layer in enumerate(self.layers):
             layer.lora = adapters.layer_views(i)
 
+    def freeze(self, names: list[str]) -> None:
+        """Keep the parameters ``names`` of the dense store fixed: their
+        gradients are zeroed before the optimizer step (so they add nothing to
+        the clip norm) and their values (bf16 and this rank's fp32 master
+        part) are put back after it, so neither the update nor weight decay
+        moves them (the reference sets ``requires_grad=False``,
+        trainer/moe.py:275-300)."""
+        flat = self.flat
+        lo, hi = flat.dp_rank * flat.shard_numel, (flat.dp_rank + 1) * flat.shard_numel
+        self._frozen = []
+        for n in names:
+            off, k = flat.offsets[n]
+            a, b = max(off, lo), min(off + k, hi)
+            master = flat.master[a - lo:b - lo].clone() if (flat.master is not None and a < b) else None
+            self._frozen.append((n, flat.view(n).clone(), (a - lo, b - lo) if a < b else None, master))
+
+    def after_optimizer_step(self) -> None:
+        for n, val, span, master in getattr(self, "_frozen", []):
+            self.flat.view(n).copy_(val)
+            if span is not None and master is not None:
+                self.flat.master[span[0]:span[1]].copy_(master)
+
     def finalize_grads(self) -> None:
         """Cross-TP sums of gradients that each TP rank only partially owns:
-        the QK-norm weights are shared by all heads, which are split."""
+        the QK-norm weights are shared by all heads, which are split.  Frozen
+        parameters get zero gradients."""
+        for n, _, _, _ in getattr(self, "_frozen", []):
+            g = self.flat.grad_view(n)
+            if g is not None:
+                g.zero_()
         if self.tp_size > 1 and self.flat.grad is not None:
             import torch.distributed as dist
 

@@ -113,7 +113,11 @@ class Engine:
     def optimizer_step(self, lr: float) -> dict[str, float]:
         with nvtx.range("optimizer.step"):
             self.model.finalize_grads()
-            return self.opt.step(lr)
+            out = self.opt.step(lr)
+            hook = getattr(self.model, "after_optimizer_step", None)
+            if hook is not None:
+                hook()
+            return out
 
     def global_token_count(self, local: float, device) -> float:
         if self.dp_world > 1 and dist.is_initialized():

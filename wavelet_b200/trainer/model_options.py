@@ -1,0 +1,52 @@
+"""Model-section options that act after the model is built.
+
+* ``model.matmul_precision`` -> ``torch.set_float32_matmul_precision`` (the
+  float32 torch matmuls: CPU paths, Muon's Newton-Schulz, the eager
+  DeepSeek-V4 model), as the reference does at set-up.
+* ``model.moe_router_dtype``: ``none`` keeps the router gate in the model
+  dtype (bf16 logits, as a bf16 ``nn.Linear`` gate produces); ``float32``
+  keeps the fp32 logits of the router GEMM (reference trainer/moe.py:298).
+* ``model.freeze_moe_router``: the router weights are frozen (no gradient,
+  no update, no decay); a model without MoE routers is an error, as in the
+  reference (trainer/moe.py:275-300).
+* ``model.meta_device_init`` and ``fsdp.reshard_after_forward`` ask the
+  reference's FSDP wrapper to build on the meta device and to free gathered
+  weights after forward.  Here parameters are always allocated directly on
+  the device (nothing is built on the host first) and the bf16 weights stay
+  resident by design, so both are satisfied as they are; setting either
+  explicitly logs what happens instead.
+"""
+
+from __future__ import annotations
+
+import logging
+
+import torch
+
+log = logging.getLogger("wavelet")
+
+
+def apply_model_options(model, mcfg, fsdp_cfg=None) -> list[str]:
+    notes: list[str] = []
+    prec = getattr(mcfg, "matmul_precision", None)
+    if prec:
+        torch.set_float32_matmul_precision(prec)
+    layers = getattr(model, "layers", [])
+    routers = [layer.moe for layer in layers if getattr(layer, "moe", None) is not None]
+    for moe in routers:
+        moe.router_logits_bf16 = getattr(mcfg, "moe_router_dtype", "none") == "none"
+    if getattr(mcfg, "freeze_moe_router", False):
+        names = [n for n in model.flat.names() if n.endswith(".router_w")]
+        if not routers or not names:
+            raise ValueError("model.freeze_moe_router=true requires a model with MoE routers (a Qwen3-MoE shape)")
+        model.freeze(names)
+        notes.append(f"model.freeze_moe_router: {len(names)} router weights frozen")
+    if getattr(mcfg, "meta_device_init", False):
+        notes.append("model.meta_device_init: parameters are allocated directly on the device "
+                     "(no host materialisation to defer)")
+    if fsdp_cfg is not None and "reshard_after_forward" in getattr(fsdp_cfg, "model_fields_set", set()):
+        notes.append(f"fsdp.reshard_after_forward={fsdp_cfg.reshard_after_forward}: bf16 weights stay resident "
+                     "on every data-parallel rank (only optimizer state is sharded)")
+    for n in notes:
+        log.info(n)
+    return notes

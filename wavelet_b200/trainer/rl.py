@@ -87,6 +87,9 @@ class RLTrainer:
 
                 load_hf_weights(model, p)
         self.model = model
+        from .model_options import apply_model_options
+
+        apply_model_options(model, c.model, c.fsdp)
         ac = c.model.activation_checkpointing
         model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:

@@ -110,6 +110,9 @@ class SFTTrainer:
             self.model.ep_group = self.groups.ep
             if self.ep_fabric is not None and c.fsdp.ep_dispatch == "fabric":
                 self.model.attach_ep_fabric(self.ep_fabric)
+        from .model_options import apply_model_options
+
+        apply_model_options(self.model, c.model, c.fsdp)
         ac = c.model.activation_checkpointing
         self.model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
