@@ -7,6 +7,7 @@
 
 #include "attention.h"
 #include "comm.h"
+#include "moe.h"
 #include "decode.h"
 #include "gemm.h"
 #include "kernels.h"
@@ -328,19 +329,20 @@ void slots_sum(const at::Tensor& slots, int64_t world, int64_t stride, int64_t n
 }
 
 void rows_scatter(const at::Tensor& x, const at::Tensor& src_row, const at::Tensor& dst_rank, const at::Tensor& dst_row,
-                  const c10::optional<at::Tensor>& scale, const std::vector<int64_t>& dst, int64_t world, int64_t ldd) {
+                  const c10::optional<at::Tensor>& scale, const std::vector<int64_t>& dst, int64_t world, int64_t ldd,
+                  int64_t limit_rows) {
   check_bf16(x, "x");
   WB_CHECK(src_row.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong && dst_rank.scalar_type() == at::kInt,
            "rows_scatter: index dtypes");
   if (scale) check_f32(*scale, "scale");
   wb::rows_scatter(x.data_ptr(), ld_of(x, "x"), src_row.data_ptr<int64_t>(), dst_rank.data_ptr<int>(),
                    dst_row.data_ptr<int64_t>(), scale ? scale->data_ptr<float>() : nullptr, peers_of(dst, (int)world),
-                   ldd, (int)src_row.numel(), (int)x.size(1), cur_stream());
+                   ldd, (int)src_row.numel(), (int)x.size(1), limit_rows, cur_stream());
 }
 
 void rows_gather_sum(const std::vector<int64_t>& src, int64_t world, int64_t lds, const at::Tensor& src_rank,
                      const at::Tensor& src_row, const c10::optional<at::Tensor>& w, int64_t k,
-                     const c10::optional<at::Tensor>& res, at::Tensor& out) {
+                     const c10::optional<at::Tensor>& res, at::Tensor& out, int64_t limit_rows) {
   WB_CHECK(src_row.scalar_type() == at::kLong && src_rank.scalar_type() == at::kInt, "rows_gather_sum: index dtypes");
   if (w) check_f32(*w, "w");
   const bool f32 = out.scalar_type() == at::kFloat;
@@ -349,7 +351,7 @@ void rows_gather_sum(const std::vector<int64_t>& src, int64_t world, int64_t lds
   wb::rows_gather_sum(peers_of(src, (int)world), lds, src_rank.data_ptr<int>(), src_row.data_ptr<int64_t>(),
                       w ? w->data_ptr<float>() : nullptr, (int)k, res ? res->data_ptr() : nullptr,
                       res ? ld_of(*res, "res") : 0, out.data_ptr(), ld_of(out, "out"), f32, (int)out.size(0),
-                      (int)out.size(1), cur_stream());
+                      (int)out.size(1), limit_rows, cur_stream());
 }
 
 void allgather_bf16(const std::vector<int64_t>& dst, int64_t world, int64_t lo, const at::Tensor& src) {
@@ -771,6 +773,86 @@ void decode_advance(const at::Tensor& tok, const at::Tensor& lp, at::Tensor& ids
                      step.data_ptr<int32_t>(), seed.data_ptr<int64_t>(), (int)tok.size(0), cur_stream());
 }
 
+static void check_i32(const at::Tensor& t, const char* name) {
+  WB_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), std::string(name) + " must be int32 CUDA");
+}
+static void check_i64(const at::Tensor& t, const char* name) {
+  WB_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.is_contiguous(), std::string(name) + " must be int64 CUDA");
+}
+
+void moe_route(const at::Tensor& logits, int64_t k, bool norm_topk, bool bf16_logits, at::Tensor& probs,
+               at::Tensor& topi, at::Tensor& topv, at::Tensor& w, at::Tensor& ssum, at::Tensor& counts) {
+  check_f32(logits, "logits");
+  WB_CHECK(logits.dim() == 2 && logits.is_contiguous(), "moe_route: logits [T, E] contiguous");
+  const int64_t T = logits.size(0), E = logits.size(1);
+  check_f32(probs, "probs");
+  check_f32(topv, "topv");
+  check_f32(w, "w");
+  check_f32(ssum, "ssum");
+  check_i64(topi, "topi");
+  check_i32(counts, "counts");
+  WB_CHECK(probs.numel() == T * E && topi.numel() == T * k && topv.numel() == T * k && w.numel() == T * k &&
+               ssum.numel() == T && counts.numel() >= E, "moe_route: output sizes");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  wb::moe_route(logits.data_ptr<float>(), (int)T, (int)E, (int)k, norm_topk, bf16_logits, probs.data_ptr<float>(),
+                topi.data_ptr<int64_t>(), topv.data_ptr<float>(), w.data_ptr<float>(), ssum.data_ptr<float>(),
+                counts.data_ptr<int32_t>(), cur_stream());
+}
+
+void moe_layout(const at::Tensor& allc, int64_t ep, int64_t me, int64_t pad, int64_t cap_rows, at::Tensor& base,
+                at::Tensor& tile_group, at::Tensor& k_start, at::Tensor& k_len, at::Tensor& n_recv, at::Tensor& rows,
+                at::Tensor& overflow) {
+  check_i32(allc, "allc");
+  check_i64(base, "base");
+  check_i32(tile_group, "tile_group");
+  check_i32(k_start, "k_start");
+  check_i32(k_len, "k_len");
+  check_i32(n_recv, "n_recv");
+  check_i32(rows, "rows");
+  check_i32(overflow, "overflow");
+  const int64_t E = base.numel();
+  WB_CHECK(allc.numel() >= ep * E && ep > 0 && E % ep == 0 && me >= 0 && me < ep, "moe_layout: bad counts table");
+  WB_CHECK(k_start.numel() >= E / ep && k_len.numel() >= E / ep && n_recv.numel() >= E / ep, "moe_layout: sizes");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const c10::cuda::CUDAGuard guard(allc.device());
+  wb::moe_layout(allc.data_ptr<int32_t>(), (int)ep, (int)me, (int)E, (int)pad, cap_rows, (int)tile_group.numel(),
+                 base.data_ptr<int64_t>(), tile_group.data_ptr<int32_t>(), k_start.data_ptr<int32_t>(),
+                 k_len.data_ptr<int32_t>(), n_recv.data_ptr<int32_t>(), rows.data_ptr<int32_t>(),
+                 overflow.data_ptr<int32_t>(), wb::error_word(allc.get_device()), cur_stream());
+}
+
+void moe_copy_rows(const at::Tensor& topi, int64_t E, int64_t El, const at::Tensor& base, at::Tensor& dst_row,
+                   at::Tensor& dst_rank) {
+  check_i64(topi, "topi");
+  check_i64(base, "base");
+  check_i64(dst_row, "dst_row");
+  check_i32(dst_rank, "dst_rank");
+  WB_CHECK(dst_row.numel() == topi.numel() && dst_rank.numel() == topi.numel() && base.numel() >= E,
+           "moe_copy_rows: sizes");
+  const c10::cuda::CUDAGuard guard(topi.device());
+  wb::moe_copy_rows(topi.data_ptr<int64_t>(), (int)topi.numel(), (int)E, (int)El, base.data_ptr<int64_t>(),
+                    dst_row.data_ptr<int64_t>(), dst_rank.data_ptr<int32_t>(), cur_stream());
+}
+
+void moe_zero_pad(at::Tensor& x, const at::Tensor& k_start, const at::Tensor& k_len, const at::Tensor& n_recv,
+                  const c10::optional<at::Tensor>& overflow) {
+  check_bf16(x, "x");
+  WB_CHECK(x.dim() == 2 && x.stride(1) == 1, "moe_zero_pad: x [R, H] row-major");
+  check_i32(k_start, "k_start");
+  const c10::cuda::CUDAGuard guard(x.device());
+  wb::moe_zero_pad(x.data_ptr(), x.stride(0), (int)x.size(1), (int)k_start.numel(), k_start.data_ptr<int32_t>(),
+                   k_len.data_ptr<int32_t>(), n_recv.data_ptr<int32_t>(),
+                   overflow ? overflow->data_ptr<int32_t>() : nullptr, cur_stream());
+}
+
+void moe_put_counts(const std::vector<int64_t>& dst, int64_t world, int64_t me, const at::Tensor& cnt) {
+  check_i32(cnt, "cnt");
+  const c10::cuda::CUDAGuard guard(cnt.device());
+  wb::moe_put_counts(peers_of(dst, (int)world), (int)world, (int)me, (int)cnt.numel(), cnt.data_ptr<int32_t>(),
+                     cur_stream());
+}
+
 int64_t read_error(int64_t device) { return wb::read_error_word((int)device); }
 void clear_error(int64_t device) { wb::clear_error_word((int)device); }
 
@@ -821,12 +903,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_exchange", &norm_exchange);
   m.def("adamw_allgather", &adamw_allgather);
   m.def("allgather_bf16", &allgather_bf16);
-  m.def("rows_scatter", &rows_scatter);
+  m.def("rows_scatter", &rows_scatter, py::arg("x"), py::arg("src_row"), py::arg("dst_rank"), py::arg("dst_row"),
+        py::arg("scale"), py::arg("dst"), py::arg("world"), py::arg("ldd"), py::arg("limit_rows") = -1);
   m.def("gather_from_peers", &gather_from_peers);
   m.def("gemm_peer", &gemm_peer);
   m.def("slots_sum", &slots_sum);
-  m.def("rows_gather_sum", &rows_gather_sum);
+  m.def("rows_gather_sum", &rows_gather_sum, py::arg("src"), py::arg("world"), py::arg("lds"), py::arg("src_rank"),
+        py::arg("src_row"), py::arg("w"), py::arg("k"), py::arg("res"), py::arg("out"), py::arg("limit_rows") = -1);
   m.def("read_error", &read_error);
+  m.def("moe_route", &moe_route);
+  m.def("moe_layout", &moe_layout);
+  m.def("moe_copy_rows", &moe_copy_rows);
+  m.def("moe_zero_pad", &moe_zero_pad);
+  m.def("moe_put_counts", &moe_put_counts);
   m.def("launch_count", []() { return wb::launch_count(); },
         "kernels launched by this library since it was loaded (every launch site counts one)");
   m.def("note_launches", [](int64_t n) { wb::note_launches(n); },

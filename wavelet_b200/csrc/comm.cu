@@ -246,10 +246,13 @@ __global__ void __launch_bounds__(256) rows_scatter_kernel(const __nv_bfloat16* 
                                                            const int* __restrict__ dst_rank,
                                                            const int64_t* __restrict__ dst_row,
                                                            const float* __restrict__ scale, PeerPtrs dst, int64_t ldd,
-                                                           int n, int H) {
+                                                           int n, int H, int64_t limit_rows) {
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= n) return;
+  // a row outside the destination buffer (an over-capacity layout, which the
+  // layout kernel has already reported) is dropped, never written
+  if (limit_rows >= 0 && (dst_row[w] < 0 || dst_row[w] >= limit_rows)) return;
   const uint4* src = reinterpret_cast<const uint4*>(x + src_row[w] * ldx);
   uint4* out = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst.p[dst_rank[w]]) + dst_row[w] * ldd);
   const float sc = scale ? scale[w] : 1.f;
@@ -276,7 +279,8 @@ __global__ void __launch_bounds__(256) rows_gather_sum_kernel(PeerPtrs src, int6
                                                               const int64_t* __restrict__ src_row,
                                                               const float* __restrict__ wt, int k,
                                                               const __nv_bfloat16* __restrict__ res, int64_t ldr,
-                                                              void* __restrict__ out, int64_t ldo, int T, int H) {
+                                                              void* __restrict__ out, int64_t ldo, int T, int H,
+                                                              int64_t limit_rows) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -297,6 +301,7 @@ __global__ void __launch_bounds__(256) rows_gather_sum_kernel(PeerPtrs src, int6
     }
     for (int s = 0; s < k; ++s) {
       const int64_t i = (int64_t)t * k + s;
+      if (limit_rows >= 0 && (src_row[i] < 0 || src_row[i] >= limit_rows)) continue;  // never read out of bounds
       const float wv = wt ? wt[i] : 1.f;
       const uint4 v = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src.p[src_rank[i]]) +
                                                      src_row[i] * lds)[c];
@@ -482,26 +487,29 @@ void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const vo
 }
 
 void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,
-                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, cudaStream_t st) {
+                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, int64_t limit_rows,
+                  cudaStream_t st) {
   if (n <= 0) return;
   if (H % 8 || ldx % 8 || ldd % 8) throw std::runtime_error("wavelet_b200 rows_scatter: H and strides must be multiples of 8");
   comm::rows_scatter_kernel<<<(n + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, src_row, dst_rank,
-                                                         dst_row, scale, dst, ldd, n, H); note_launch();
+                                                         dst_row, scale, dst, ldd, n, H, limit_rows); note_launch();
 }
 
 void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, const int64_t* src_row, const float* w,
                      int k, const void* res, int64_t ldr, void* out, int64_t ldo, bool f32_out, int T, int H,
-                     cudaStream_t st) {
+                     int64_t limit_rows, cudaStream_t st) {
   if (T <= 0) return;
   if (H % 8 || lds % 8 || ldo % 8 || (res && ldr % 8))
     throw std::runtime_error("wavelet_b200 rows_gather_sum: H and strides must be multiples of 8");
   const int grid = (T + 7) / 8;
   if (f32_out)
     comm::rows_gather_sum_kernel<true><<<grid, 256, 0, st>>>(src, lds, src_rank, src_row, w, k,
-                                                             static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H);
+                                                             static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H,
+                                                             limit_rows);
   else
     comm::rows_gather_sum_kernel<false><<<grid, 256, 0, st>>>(src, lds, src_rank, src_row, w, k,
-                                                              static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H);
+                                                              static_cast<const __nv_bfloat16*>(res), ldr, out, ldo, T, H,
+                                                             limit_rows);
   note_launch();
 }
 

@@ -78,10 +78,13 @@ void slots_sum(const void* slots, int world, int64_t stride, int64_t n, const vo
 
 // Expert-parallel row exchange over peer memory (comm.cu): dispatch rows to
 // their expert's rank / combine the k expert outputs of every token.
+// limit_rows >= 0: rows at or past it (or negative) are skipped (not written /
+// not read): an over-capacity layout never touches memory past the buffers.
 void rows_scatter(const void* x, int64_t ldx, const int64_t* src_row, const int* dst_rank, const int64_t* dst_row,
-                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, cudaStream_t st);
+                  const float* scale, const PeerPtrs& dst, int64_t ldd, int n, int H, int64_t limit_rows,
+                  cudaStream_t st);
 void rows_gather_sum(const PeerPtrs& src, int64_t lds, const int* src_rank, const int64_t* src_row, const float* w,
                      int k, const void* res, int64_t ldr, void* out, int64_t ldo, bool f32_out, int T, int H,
-                     cudaStream_t st);
+                     int64_t limit_rows, cudaStream_t st);
 
 }  // namespace wb

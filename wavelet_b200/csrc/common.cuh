@@ -23,6 +23,7 @@ enum : int {
   kErrTimeoutDrain = 1 << 3,
   kErrTimeoutPeer = 1 << 4,
   kErrBadShape = 1 << 5,
+  kErrEpOverflow = 1 << 6,  // an expert-parallel layout exceeded the buffer capacity (transfers skipped)
 };
 
 // 2 s: orders of magnitude above any legitimate wait inside one kernel.

@@ -169,7 +169,16 @@ __device__ __forceinline__ TileInfo tile_info(int t, const Params& p) {
       ti.num_k = (ti.piece + 1) * p.num_k / p.split_s - ti.kb_begin;
     }
     tile_coords(tile, p.num_m, p.num_n, ti.tm, ti.tn);
-    ti.b_off = (GROUP == 1) ? (int64_t)p.tile_group[ti.tm] * p.b_group_stride : 0;
+    ti.b_off = 0;
+    if constexpr (GROUP == 1) {
+      // a tile past the used rows of a device-built layout has group -1: no
+      // k-blocks, so the producer, MMA and epilogue all skip it
+      const int g = p.tile_group[ti.tm];
+      if (g < 0)
+        ti.num_k = 0;
+      else
+        ti.b_off = (int64_t)g * p.b_group_stride;
+    }
     ti.c_row_off = 0;
   }
   if constexpr (GROUP == 2) ti.split = -1, ti.piece = 0;

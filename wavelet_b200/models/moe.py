@@ -101,6 +101,63 @@ class Routing:
         self.E = E
 
 
+class DeviceRouting:
+    """The ``Routing`` layout built on the device (``moe_layout`` /
+    ``moe_copy_rows`` kernels): no host round trip, so a layer needs no
+    synchronisation and can be captured in a CUDA graph.  The row buffers are
+    sized for the worst case (every copy plus a full padding tile per expert);
+    tiles past the used rows carry group -1 and the grouped GEMMs skip them."""
+
+    def __init__(self, topi: torch.Tensor, counts: torch.Tensor, E: int, pad: int = PAD):
+        T, k = topi.shape
+        dev = topi.device
+        m = ops.ext()
+        self.E = E
+        self.R = max(pad, (T * k + E * (pad - 1) + pad - 1) // pad * pad)
+        self.counts = counts
+        self.base = torch.empty(E, dtype=torch.int64, device=dev)
+        self.tile_group = torch.empty(self.R // pad, dtype=torch.int32, device=dev)
+        self.k_start = torch.empty(E, dtype=torch.int32, device=dev)
+        self.k_len = torch.empty(E, dtype=torch.int32, device=dev)
+        self.n_recv = torch.empty(E, dtype=torch.int32, device=dev)
+        self.rows = torch.empty(1, dtype=torch.int32, device=dev)
+        self.overflow = torch.empty(1, dtype=torch.int32, device=dev)
+        m.moe_layout(counts, 1, 0, pad, self.R, self.base, self.tile_group, self.k_start, self.k_len, self.n_recv,
+                     self.rows, self.overflow)
+        self.pos = torch.empty(T * k, dtype=torch.int64, device=dev)
+        self.dst_rank = torch.empty(T * k, dtype=torch.int32, device=dev)
+        m.moe_copy_rows(topi.reshape(-1).contiguous(), E, E, self.base, self.pos, self.dst_rank)
+        self.tok = torch.arange(T, device=dev).repeat_interleave(k)
+
+    def scatter_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """[R, H] buffer with row pos[i] = x[tok[i]] and zero padding rows."""
+        xs = torch.empty(self.R, x.shape[1], device=x.device, dtype=x.dtype)
+        xs.index_copy_(0, self.pos, x.index_select(0, self.tok))
+        ops.ext().moe_zero_pad(xs, self.k_start, self.k_len, self.n_recv, self.overflow)
+        return xs
+
+    def scatter_copies(self, rows: torch.Tensor) -> torch.Tensor:
+        """[R, H] buffer with row pos[i] = rows[i] ((token, slot) order) and zero padding."""
+        out = torch.empty(self.R, rows.shape[1], device=rows.device, dtype=rows.dtype)
+        out.index_copy_(0, self.pos, rows)
+        ops.ext().moe_zero_pad(out, self.k_start, self.k_len, self.n_recv, self.overflow)
+        return out
+
+
+def moe_metrics(model) -> dict[str, float]:
+    """moe/max_vio (mean over layers of (max expert load - mean) / mean),
+    its max over layers, and moe/routing_confidence (mean selected top-k
+    probability mass) of the last forward (reference trainer/moe.py:387-436);
+    one host transfer for all layers."""
+    stats = [layer.moe.last_stats for layer in getattr(model, "layers", [])
+             if getattr(layer, "moe", None) is not None and layer.moe.last_stats is not None]
+    if not stats:
+        return {}
+    st = torch.stack(stats).float().cpu()
+    return {"moe/max_vio": float(st[:, 0].mean()), "moe/max_vio/max": float(st[:, 0].max()),
+            "moe/routing_confidence": float(st[:, 1].mean())}
+
+
 class MoEBlock:
     """Sparse MLP of one decoder layer (GPU path and the CPU fallbacks of the
     same ops).  With ``ep_size > 1`` this rank holds experts
@@ -117,30 +174,61 @@ class MoEBlock:
         self.ep_rank = ep_rank
         self.E_loc = cfg.num_experts // ep_size
         self.aux_loss_scale = 0.0
-        self.last_aux = None
         self.last_counts = None
+        self.last_stats = None  # device [max_vio, routing confidence] of the last forward
         self.router_logits_bf16 = False  # model.moe_router_dtype == 'none' (set by apply_model_options)
 
     # ------------------------------------------------------------ shared
     def _route(self, h2, P):
+        """Router logits GEMM, then softmax / top-k / weights / per-expert
+        counts in one device kernel (``moe_route``).  With
+        model.moe_router_dtype 'none' the logits are rounded to bf16 first (a
+        gate in the model dtype); 'float32' keeps the fp32 GEMM output."""
         cfg = self.cfg
         logits = ops.gemm(h2, P["router_w"], epi=ops.EPI_F32)
-        if self.router_logits_bf16:
-            # model.moe_router_dtype 'none': the gate runs in the model dtype, so
-            # its logits are bf16 values (fp32 accumulation, bf16 output)
-            logits = logits.to(torch.bfloat16).float()
-        probs = torch.softmax(logits, -1)
-        topv, topi = torch.topk(probs, cfg.num_experts_per_tok, dim=-1)
-        s = topv.sum(-1, keepdim=True)
-        w = topv / s if cfg.norm_topk_prob else topv
+        k, E = cfg.num_experts_per_tok, cfg.num_experts
+        T = logits.shape[0]
+        if logits.is_cuda:
+            dev = logits.device
+            probs = torch.empty(T, E, device=dev, dtype=torch.float32)
+            topi = torch.empty(T, k, device=dev, dtype=torch.int64)
+            topv = torch.empty(T, k, device=dev, dtype=torch.float32)
+            w = torch.empty(T, k, device=dev, dtype=torch.float32)
+            s = torch.empty(T, 1, device=dev, dtype=torch.float32)
+            counts = torch.zeros(E, device=dev, dtype=torch.int32)
+            ops.ext().moe_route(logits.contiguous(), k, bool(cfg.norm_topk_prob), bool(self.router_logits_bf16),
+                                probs, topi, topv, w, s, counts)
+        else:
+            if self.router_logits_bf16:
+                logits = logits.to(torch.bfloat16).float()
+            probs = torch.softmax(logits, -1)
+            topv, topi = torch.topk(probs, k, dim=-1)
+            s = topv.sum(-1, keepdim=True)
+            w = topv / s if cfg.norm_topk_prob else topv
+            counts = torch.bincount(topi.reshape(-1), minlength=E).to(torch.int32)
+        self._counts = counts
         return probs, topv, topi, s, w
 
-    def _experts(self, x, P, rt: Routing):
+    def _note_stats(self, counts: torch.Tensor, s: torch.Tensor) -> None:
+        c = counts.float()
+        mean = c.mean().clamp_min(1e-9)
+        self.last_counts = counts
+        self.last_stats = torch.stack([(c.max() - mean) / mean, s.float().mean()])
+
+    def _local_routing(self, topi):
+        if topi.is_cuda:
+            return DeviceRouting(topi, self._counts, self.cfg.num_experts)
+        return Routing(topi, self.cfg.num_experts)
+
+    def _experts(self, x, P, rt):
         """Expert FFNs of this rank over the rows ``x[rt.tok]`` laid out by ``rt``."""
         cfg = self.cfg
         E, H, Ie = self.E_loc, cfg.hidden_size, cfg.moe_intermediate_size
-        xs = torch.zeros(rt.R, H, device=x.device, dtype=x.dtype)
-        xs.index_copy_(0, rt.pos, x.index_select(0, rt.tok))
+        if isinstance(rt, DeviceRouting):
+            xs = rt.scatter_rows(x)
+        else:
+            xs = torch.zeros(rt.R, H, device=x.device, dtype=x.dtype)
+            xs.index_copy_(0, rt.pos, x.index_select(0, rt.tok))
         gu = torch.empty(rt.R, 2 * Ie, device=x.device, dtype=x.dtype)
         ops.gemm_grouped(xs, False, P["exp_gu_w"].view(E * 2 * Ie, H), False, gu, 1, rt.R, 2 * Ie, H, rt.tile_group,
                          2 * Ie, E * 2 * Ie, None, None, E, ops.EPI_BF16, 1.0)
@@ -222,15 +310,14 @@ class MoEBlock:
             counts = plan["counts"]
         else:
             plan = None
-            rt = Routing(topi, cfg.num_experts)
+            rt = self._local_routing(topi)
             xs, gu, a, y = self._experts(h2, P, rt)
             y_copy = y.index_select(0, rt.pos)
             counts = rt.counts
         contrib = y_copy.float() * w.reshape(-1, 1)
         out = (x2.float() + contrib.view(T, k, -1).sum(1)).to(x2.dtype)
         f = counts.float() / (T * k)
-        self.last_aux = float(cfg.num_experts * (f * probs.mean(0)).sum())
-        self.last_counts = counts
+        self._note_stats(counts, s)
         cache = None
         if save:
             cache = dict(h2=h2, rstd2=rstd2, probs=probs, topv=topv, topi=topi, s=s, w=w, rt=rt, xs=xs, gu=gu, a=a,
@@ -253,14 +340,13 @@ class MoEBlock:
         cfg = self.cfg
         T, k = x2.shape[0], cfg.num_experts_per_tok
         fe = self.ep_fabric
-        fp = fe.plan(topi)
+        fp = fe.plan(topi, self._counts)
         xs = fe.dispatch("xs", h2, fp)  # rows land directly in the owner's padded expert layout
         gu, a = self._fabric_experts(xs, P, fp, fe.view("y", fp.R))
         out = torch.empty_like(x2)
         fe.combine("y", fp, k, w, x2, out)  # out = x2 + sum_k w_k y_k, read from the owners
         f = fp.counts.float() / (T * k)
-        self.last_aux = float(cfg.num_experts * (f * probs.mean(0)).sum())
-        self.last_counts = fp.counts
+        self._note_stats(fp.counts, s)
         cache = None
         if save:
             y_copy = fe.gather_copies("y", fp, T, k)
@@ -294,6 +380,8 @@ class MoEBlock:
             self._a2a(dy_recv, dy_copy[plan["order"]], plan["recv"], plan["send"])
             dy = torch.zeros(rt.R, H, device=dout.device, dtype=dout.dtype)
             dy.index_copy_(0, rt.pos, dy_recv)
+        elif isinstance(rt, DeviceRouting):
+            dy = rt.scatter_copies(dy_copy)
         else:
             dy = torch.zeros(rt.R, H, device=dout.device, dtype=dout.dtype)
             dy.index_copy_(0, rt.pos, dy_copy)
@@ -340,7 +428,7 @@ class MoEBlock:
         probs, topv, topi, s, w = self._route(h2, P)
         if self.ep_fabric is not None and self.ep_size > 1:
             fe = self.ep_fabric
-            fp = fe.plan(topi)
+            fp = fe.plan(topi, self._counts)
             xs = fe.dispatch("xs", h2, fp)
             self._fabric_experts(xs, P, fp, fe.view("y", fp.R))
             out = torch.empty_like(x)
@@ -351,7 +439,7 @@ class MoEBlock:
             _, _, _, y = self._experts(x_recv, P, rt)
             y_copy = self._combine(y.index_select(0, rt.pos), plan, T, k)
         else:
-            rt = Routing(topi, cfg.num_experts)
+            rt = self._local_routing(topi)
             _, _, _, y = self._experts(h2, P, rt)
             y_copy = y.index_select(0, rt.pos)
         contrib = y_copy.float() * w.reshape(-1, 1)

@@ -185,6 +185,11 @@ class CausalLM:
             self._frozen.append((n, flat.view(n).clone(), (a - lo, b - lo) if a < b else None, master))
 
     def after_optimizer_step(self) -> None:
+        for layer in self.layers:  # an over-capacity expert layout invalidates the step: report it
+            fe = getattr(layer.moe, "ep_fabric", None) if layer.moe is not None else None
+            if fe is not None:
+                fe.check()
+                break
         for n, val, span, master in getattr(self, "_frozen", []):
             self.flat.view(n).copy_(val)
             if span is not None and master is not None:
@@ -218,12 +223,16 @@ class CausalLM:
         self.tp_fabric = TPFabric(fabric, capacity)
         return self.tp_fabric
 
-    def attach_ep_fabric(self, fabric, capacity_rows: int = 1 << 16):
+    def attach_ep_fabric(self, fabric, capacity_rows: int = 1 << 16, max_tokens: int = 0,
+                         capacity_factor: float = 2.0):
         """Expert dispatch / combine over peer memory (parallel.ep_fabric) for
-        every MoE layer; ``fabric`` spans the expert-parallel group."""
+        every MoE layer; ``fabric`` spans the expert-parallel group.  The row
+        buffers hold ``capacity_factor`` x the copies of ``max_tokens`` tokens
+        per micro-batch (plus padding), at least ``capacity_rows``."""
         from ..parallel.ep_fabric import FabricEP
 
-        fe = FabricEP(fabric, self.ep_group, self.cfg.num_experts, self.cfg.hidden_size, capacity_rows)
+        fe = FabricEP(fabric, self.ep_group, self.cfg.num_experts, self.cfg.hidden_size, capacity_rows,
+                      k=self.cfg.num_experts_per_tok, max_tokens=max_tokens, capacity_factor=capacity_factor)
         for layer in self.layers:
             if layer.moe is not None:
                 layer.moe.ep_fabric = fe

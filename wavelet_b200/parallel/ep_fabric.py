@@ -8,22 +8,27 @@ gradients), each laid out exactly as the grouped GEMM wants it: rows grouped
 by local expert, each expert segment padded to 128 rows, and inside a
 segment the rows of source rank 0, then 1, ...
 
-Forward of one MoE layer (all ranks in lockstep):
-  1. counts: every rank all-gathers its per-expert copy counts (tiny), so all
-     ranks know every destination's layout and the row of every copy;
+Forward of one MoE layer (all ranks in lockstep, no host synchronisation):
+  1. counts: every rank stores its per-expert copy counts into every peer's
+     count table (``moe_put_counts``) -> barrier; each rank then builds, on
+     the device, every destination's layout and the row of each of its copies
+     (``moe_layout`` / ``moe_copy_rows``), identically on all ranks;
   2. dispatch (``rows_scatter``): each rank stores its token rows straight
      into the destination rank's ``xs`` row over NVLink -> barrier;
-  3. padding rows zeroed locally; grouped tcgen05 expert GEMMs on ``xs``,
-     writing ``y`` -> barrier;
+  3. padding rows zeroed locally; grouped tcgen05 expert GEMMs on ``xs`` (tiles
+     past the used rows are skipped), writing ``y`` -> barrier;
   4. combine (``rows_gather_sum``): each token loads its k expert outputs from
      the owning ranks and forms x2 + sum_k w_k y_k in one pass.
 Backward mirrors it: ``dy`` rows (dout scaled by the routing weight) are
 dispatched, the expert backward runs locally, and ``dxs`` rows are gathered
 back and summed per token.  Each direction costs the bytes of the NCCL path
 but no staging copies, and the gather, weighting and residual add ride on
-the transfers.  Buffers hold ``capacity`` rows and grow (on every rank at
-once: the decision is made on the all-gathered counts) when a layout does not
-fit.
+the transfers.  Buffers hold ``capacity`` rows, fixed at construction
+(``capacity_factor`` x the copies of ``max_tokens`` tokens, plus a padding
+tile per local expert); a layout that would not fit any rank's buffer is
+detected on the device, every transfer of that layer is skipped (nothing is
+written or read past a buffer) and ``check()`` raises: raise
+``fsdp.ep_capacity_factor``.
 """
 
 from __future__ import annotations
@@ -38,23 +43,30 @@ from ..utils import nvtx
 from .fabric import Fabric
 
 PAD = 128
+ERR_EP_OVERFLOW = 1 << 6  # csrc/common.cuh kErrEpOverflow
 
 
 @dataclass
 class FabricPlan:
-    R: int  # rows of this rank's padded layout
-    tile_group: torch.Tensor
-    k_start: torch.Tensor
-    k_len: torch.Tensor
-    pad_rows: torch.Tensor  # rows of the layout that receive no copy (zeroed)
+    R: int  # rows of this rank's layout buffers (the capacity)
+    tile_group: torch.Tensor  # int32 [R / 128]: local expert of each tile, -1 past the used rows
+    k_start: torch.Tensor  # int32 [El]: segment start of each local expert
+    k_len: torch.Tensor  # int32 [El]: padded segment length
+    n_recv: torch.Tensor  # int32 [El]: received copies per local expert
+    overflow: torch.Tensor  # int32 [1]: 1 when some rank's layout exceeded the capacity
     dst_rank: torch.Tensor  # int32 [T*k] rank owning each copy's expert ((token, slot) order)
     dst_row: torch.Tensor  # int64 [T*k] row of the copy in that rank's layout
     src_tok: torch.Tensor  # int64 [T*k] token of each copy
-    counts: torch.Tensor  # this rank's per-expert copy counts
+    counts: torch.Tensor  # int32 [E]: this rank's per-expert copy counts
+
+
+class EPCapacityError(RuntimeError):
+    pass
 
 
 class FabricEP:
-    def __init__(self, fabric: Fabric, group, E: int, H: int, capacity: int, dtype=torch.bfloat16):
+    def __init__(self, fabric: Fabric, group, E: int, H: int, capacity: int, dtype=torch.bfloat16, k: int = 8,
+                 max_tokens: int = 0, capacity_factor: float = 2.0):
         self.fab = fabric
         self.group = group
         self.ep = fabric.world
@@ -62,8 +74,11 @@ class FabricEP:
         self.E = E
         self.El = E // self.ep
         self.H = H
-        self.capacity = capacity
-        self.bufs = {n: fabric.alloc(capacity * H, dtype) for n in ("xs", "y", "dy", "dxs")}
+        if max_tokens > 0:
+            capacity = max(capacity, int(capacity_factor * max_tokens * k) + self.El * PAD)
+        self.capacity = (capacity + PAD - 1) // PAD * PAD
+        self.bufs = {n: fabric.alloc(self.capacity * H, dtype) for n in ("xs", "y", "dy", "dxs")}
+        self.cnt = fabric.alloc(self.ep * E, torch.int32)  # every rank's per-expert counts
 
     def view(self, name: str, rows: int) -> torch.Tensor:
         return self.bufs[name].tensor[: rows * self.H].view(rows, self.H)
@@ -72,70 +87,43 @@ class FabricEP:
         return self.bufs[name].ptrs
 
     # ------------------------------------------------------------------ plan
-    def plan(self, topi: torch.Tensor) -> FabricPlan:
+    def plan(self, topi: torch.Tensor, counts: torch.Tensor | None = None) -> FabricPlan:
         T, k = topi.shape
         dev = topi.device
-        e = topi.reshape(-1)
-        cnt = torch.bincount(e, minlength=self.E).to(torch.int32)
-        allc = torch.empty(self.ep * self.E, dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(allc, cnt, group=self.group)
-        C = allc.view(self.ep, self.E).tolist()  # host sync: the layouts size the grouped GEMMs
-        El = self.El
-        seg_start = [[0] * El for _ in range(self.ep)]
-        Rs = []
-        for d in range(self.ep):
-            acc = 0
-            for el in range(El):
-                seg_start[d][el] = acc
-                n = sum(C[s][d * El + el] for s in range(self.ep))
-                acc += (n + PAD - 1) // PAD * PAD
-            Rs.append(max(acc, PAD))
-        if max(Rs) > self.capacity:
-            # every rank sees the same counts, so all grow together (collective handle exchange)
-            self.capacity = int(max(Rs) * 1.25)
-            self.bufs = {n: self.fab.alloc(self.capacity * self.H, torch.bfloat16) for n in ("xs", "y", "dy", "dxs")}
-        base = []
-        for ge in range(self.E):
-            d, el = divmod(ge, El)
-            base.append(seg_start[d][el] + sum(C[s][ge] for s in range(self.rank)))
-        base_t = torch.tensor(base, dtype=torch.int64, device=dev)
-        order = torch.argsort(e, stable=True)
-        cum = torch.zeros(self.E + 1, dtype=torch.int64, device=dev)
-        cum[1:] = cnt.to(torch.int64).cumsum(0)
-        rank_in = torch.empty_like(order)
-        rank_in[order] = torch.arange(e.numel(), device=dev) - cum[e[order]]
-        dst_row = base_t[e] + rank_in
-        dst_rank = (e // El).to(torch.int32)
-        # this rank's receive layout
-        me = self.rank
-        tiles, kl, pads = [], [], []
-        for el in range(El):
-            n = sum(C[s][me * El + el] for s in range(self.ep))
-            padded = (n + PAD - 1) // PAD * PAD
-            tiles += [el] * (padded // PAD)
-            kl.append(padded)
-            pads += range(seg_start[me][el] + n, seg_start[me][el] + padded)
-        if not tiles:
-            tiles = [0]
-        R = Rs[me]
-        return FabricPlan(
-            R=R, tile_group=torch.tensor(tiles, dtype=torch.int32, device=dev),
-            k_start=torch.tensor(seg_start[me], dtype=torch.int32, device=dev),
-            k_len=torch.tensor(kl, dtype=torch.int32, device=dev),
-            pad_rows=torch.tensor(pads, dtype=torch.int64, device=dev),
-            dst_rank=dst_rank, dst_row=dst_row,
-            src_tok=torch.arange(T, device=dev).repeat_interleave(k), counts=cnt)
+        m = ops.ext()
+        e = topi.reshape(-1).contiguous()
+        if counts is None:
+            counts = torch.bincount(e, minlength=self.E).to(torch.int32)
+        with nvtx.range("ep.plan"):
+            m.moe_put_counts(self.cnt.ptrs, self.ep, self.rank, counts)
+            self.fab.barrier()
+            El = self.El
+            base = torch.empty(self.E, dtype=torch.int64, device=dev)
+            tile_group = torch.empty(self.capacity // PAD, dtype=torch.int32, device=dev)
+            k_start = torch.empty(El, dtype=torch.int32, device=dev)
+            k_len = torch.empty(El, dtype=torch.int32, device=dev)
+            n_recv = torch.empty(El, dtype=torch.int32, device=dev)
+            rows = torch.empty(1, dtype=torch.int32, device=dev)
+            overflow = torch.empty(1, dtype=torch.int32, device=dev)
+            m.moe_layout(self.cnt.tensor, self.ep, self.rank, PAD, self.capacity, base, tile_group, k_start, k_len,
+                         n_recv, rows, overflow)
+            dst_row = torch.empty(T * k, dtype=torch.int64, device=dev)
+            dst_rank = torch.empty(T * k, dtype=torch.int32, device=dev)
+            m.moe_copy_rows(e, self.E, El, base, dst_row, dst_rank)
+        return FabricPlan(R=self.capacity, tile_group=tile_group, k_start=k_start, k_len=k_len, n_recv=n_recv,
+                          overflow=overflow, dst_rank=dst_rank, dst_row=dst_row,
+                          src_tok=torch.arange(T, device=dev).repeat_interleave(k), counts=counts)
 
     # --------------------------------------------------------------- transfers
     def dispatch(self, name: str, src: torch.Tensor, p: FabricPlan, scale: torch.Tensor | None = None) -> torch.Tensor:
         """Rows of ``src`` (one per copy, optionally scaled) into every owner's
         ``name`` buffer; returns this rank's received [R, H] view."""
         with nvtx.range(f"ep.dispatch.{name}"):
-            ops.ext().rows_scatter(src, p.src_tok, p.dst_rank, p.dst_row, scale, self.ptrs(name), self.ep, self.H)
+            ops.ext().rows_scatter(src, p.src_tok, p.dst_rank, p.dst_row, scale, self.ptrs(name), self.ep, self.H,
+                                   self.capacity)
             self.fab.barrier()
         out = self.view(name, p.R)
-        if p.pad_rows.numel():
-            out.index_fill_(0, p.pad_rows, 0)
+        ops.ext().moe_zero_pad(out, p.k_start, p.k_len, p.n_recv, p.overflow)
         return out
 
     def combine(self, name: str, p: FabricPlan, k: int, w: torch.Tensor | None, res: torch.Tensor | None,
@@ -145,14 +133,27 @@ class FabricEP:
         with nvtx.range(f"ep.combine.{name}"):
             self.fab.barrier()
             ops.ext().rows_gather_sum(self.ptrs(name), self.ep, self.H, p.dst_rank, p.dst_row,
-                                      None if w is None else w.reshape(-1).float().contiguous(), k, res, out)
+                                      None if w is None else w.reshape(-1).float().contiguous(), k, res, out,
+                                      self.capacity)
         return out
 
     def gather_copies(self, name: str, p: FabricPlan, T: int, k: int) -> torch.Tensor:
         """The [T*k, H] rows of this rank's copies (no sum)."""
         out = torch.empty(T * k, self.H, device=p.dst_row.device, dtype=torch.bfloat16)
-        ops.ext().rows_gather_sum(self.ptrs(name), self.ep, self.H, p.dst_rank, p.dst_row, None, 1, None, out)
+        ops.ext().rows_gather_sum(self.ptrs(name), self.ep, self.H, p.dst_rank, p.dst_row, None, 1, None, out,
+                                  self.capacity)
         return out
+
+    def check(self) -> None:
+        """Raise when a layer's layout exceeded the buffer capacity (its
+        transfers were skipped, so that step's results are invalid)."""
+        dev = self.fab.device.index if self.fab.device.index is not None else torch.cuda.current_device()
+        m = ops.ext()
+        err = m.read_error(dev)
+        if err & ERR_EP_OVERFLOW:
+            m.clear_error(dev)
+            raise EPCapacityError(f"rank {self.rank}: an expert-parallel layout exceeded the {self.capacity}-row "
+                                  "buffers; raise fsdp.ep_capacity_factor")
 
     def close(self) -> None:
         pass  # buffers belong to the fabric (freed by Fabric.close)

@@ -97,7 +97,8 @@ class RLTrainer:
         if self.groups.ep is not None:
             model.ep_group = self.groups.ep
             if getattr(self, "ep_fabric", None) is not None and c.fsdp.ep_dispatch == "fabric":
-                model.attach_ep_fabric(self.ep_fabric)
+                model.attach_ep_fabric(self.ep_fabric, max_tokens=c.data.seq_len,
+                                       capacity_factor=c.fsdp.ep_capacity_factor)
         self.optimizer = FlatOptimizer(model.trainable, c.optim, c.max_grad_norm, self.groups.dp, self.dp_world,
                                        expert_flat=model.expert_flat, ep_dp_group=self.groups.ep_dp,
                                        ep_dp_world=self.groups.ep_dp_size)

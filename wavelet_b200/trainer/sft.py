@@ -109,7 +109,8 @@ class SFTTrainer:
         if self.groups.ep is not None:
             self.model.ep_group = self.groups.ep
             if self.ep_fabric is not None and c.fsdp.ep_dispatch == "fabric":
-                self.model.attach_ep_fabric(self.ep_fabric)
+                self.model.attach_ep_fabric(self.ep_fabric, max_tokens=c.data.seq_len * c.data.micro_batch_size,
+                                            capacity_factor=c.fsdp.ep_capacity_factor)
         from .model_options import apply_model_options
 
         apply_model_options(self.model, c.model, c.fsdp)
