@@ -47,9 +47,10 @@ def parse():
                    help="micro-batches of 1 sequence per GPU per step (default 8 for sft; 32/N for qlora)")
     p.add_argument("--layers", type=int, default=None, help="(debug only) override layer count; invalidates the number")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", default="sft", choices=["sft", "qlora", "grpo-4b"],
+    p.add_argument("--workload", default="sft", choices=["sft", "qlora", "grpo-4b", "grpo-30b-a3b"],
                    help="sft: dense full fine-tune (headline); qlora: NF4 base + LoRA r16 on all projections; "
-                        "grpo-4b: Qwen3-4B-shape GRPO step (native generator + trainer, integrated)")
+                        "grpo-4b: Qwen3-4B-shape GRPO step (native generator + trainer, integrated); "
+                        "grpo-30b-a3b: Qwen3-30B-A3B-shape MoE GRPO step, expert parallel over all GPUs")
     p.add_argument("--activation-checkpointing", default="none", choices=["none", "full"],
                    help="none: keep every layer's activations (no recompute); full: recompute each layer in backward")
     p.add_argument("--tp", type=int, default=None,
@@ -136,13 +137,23 @@ class ClockSampler:
         return {"sm_mhz": med, "sm_max_mhz": max(maxes) if maxes else None, "reasons": sorted(reasons), "samples": len(sms)}
 
 
+RL_WORKLOADS = {
+    # workload: (example config, model label, prompts per step, samples, prompt len, new tokens)
+    "grpo-4b": ("examples/grpo_4b/rl.yaml", "Qwen3-4B-shape", 64, 8, 256, 1024),
+    "grpo-30b-a3b": ("examples/grpo_30b_a3b/rl.yaml", "Qwen3-30B-A3B-shape (128 experts, top-8)", 32, 8, 512, 2048),
+}
+
+
 def rl_main(args):
-    """GRPO step on the Qwen3-4B shape through the integrated RL runner
-    (``wavelet rl`` with launcher.mode=integrated): every rank generates
-    64/N prompts x 8 samples (256-token prompts, 1024 new tokens), scores and
-    publishes them, then trains on the packed batch.  Reports rollout tokens/s
-    (generated tokens over device-timed generation, summed over ranks) and
-    the device-timed step time (max over ranks)."""
+    """GRPO step through the integrated RL runner (``wavelet rl`` with
+    launcher.mode=integrated): every rank generates its share of the prompts x
+    8 samples, scores and publishes them, then trains on the packed batch.
+    grpo-4b: Qwen3-4B shape, data parallel; grpo-30b-a3b: Qwen3-30B-A3B shape
+    with expert parallelism over all N ranks (expert dispatch / combine over
+    peer memory) and a full generator replica per rank refreshed from the
+    expert shards after every step.  Reports rollout tokens/s (generated
+    tokens over device-timed generation, summed over ranks) and the
+    device-timed step time (max over ranks)."""
     import tempfile
 
     import torch
@@ -156,10 +167,17 @@ def rl_main(args):
     from wavelet_b200.utils.config import load_yaml
 
     root = os.path.dirname(os.path.abspath(__file__))
-    d = load_yaml(os.path.join(root, "examples", "grpo_4b", "rl.yaml"))
+    cfg_path, label, prompts, samples, plen, new_tok = RL_WORKLOADS[args.workload]
+    d = load_yaml(os.path.join(root, cfg_path))
     N = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    d["orchestrator"]["examples_per_step"] = max(1, 64 // N)
+    d["orchestrator"]["examples_per_step"] = max(1, prompts // N)
+    if args.workload == "grpo-30b-a3b":
+        d.setdefault("fsdp", {})["ep"] = N
+        if N == 1:
+            d["fsdp"]["enabled"] = False
+    if args.layers:
+        d["model"]["arch_overrides"] = {"num_layers": args.layers}
     d["output_dir"] = os.path.join(tempfile.gettempdir(), f"wavelet_b200_bench_rl_{os.environ.get('MASTER_PORT', 'x')}")
     d["clean_output_dir"] = True
     d["max_steps"] = args.warmup + args.steps
@@ -201,14 +219,19 @@ def rl_main(args):
     K = args.steps
     value = gen_tok / (gen_ms / 1000.0)
     if rank == 0:
+        par = (f"integrated ep{N} (experts sharded over every rank; dense weights data parallel; "
+               "each rank generates on a full replica)" if args.workload == "grpo-30b-a3b"
+               else f"integrated dp{N} (each rank generates and trains)")
         rec = {
-            "metric": "RL rollout tok/s (Qwen3-4B-shape GRPO, native generator)",
+            "metric": f"RL rollout tok/s ({label} GRPO, native generator)",
             "value": value, "unit": "tokens/s", "n_gpus": N, "steps": K, "warmup": args.warmup,
             "ms_per_step": step_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (uniform random 256-token prompts, reversed-prompt reward, random-init weights)",
-            "config": {"model": "Qwen3-4B-shape", "prompts_per_step": 64, "samples_per_prompt": 8,
-                       "prompt_len": 256, "max_new_tokens": 1024, "temperature": 1.0,
-                       "parallelism": f"integrated dp{N} (each rank generates and trains)",
+            "dtype": "bf16",
+            "data": f"synthetic (uniform random {plen}-token prompts, reversed-prompt reward, random-init weights)",
+            "config": {"model": label + (f" ({args.layers} layers: INVALID debug run)" if args.layers else ""),
+                       "prompts_per_step": prompts, "samples_per_prompt": samples,
+                       "prompt_len": plen, "max_new_tokens": new_tok, "temperature": 1.0,
+                       "parallelism": par,
                        "l2": "inputs larger than L2 (8 GB of weights, tens of GB of KV per step)"},
             "rl_step_ms": step_ms / K, "generate_ms_per_step": gen_ms / K,
             "train_tokens_per_step": train_tok / K, "generated_tokens_per_step": gen_tok / K,
@@ -297,7 +320,7 @@ def main():
         args.tp = 1
     if args.impl == "reference":
         return reference_arm(args)
-    if args.workload == "grpo-4b":
+    if args.workload in RL_WORKLOADS:
         return rl_main(args)
 
     import torch
