@@ -56,6 +56,9 @@ def wait_healthy(urls: list[str], timeout: float, poll: float = 1.0) -> None:
 
 
 class HTTPPolicyInferenceEngine(PolicyInferenceEngine):
+    concurrent_generate = True  # the servers batch concurrent requests
+    concurrent_policy_load = True  # a weight load pauses the servers' generation itself
+
     def __init__(self, config):
         super().__init__(config)
         self.urls = endpoints(config)

@@ -23,6 +23,11 @@ from ..data.rl import RLExample
 
 
 class PolicyInferenceEngine(ABC):
+    # whether the engine serves several generation calls at once (HTTP servers
+    # batch them) and can swap policy weights while generating
+    concurrent_generate = False
+    concurrent_policy_load = False
+
     def __init__(self, config):
         self.config = config
         self.policy_step: int | None = None

@@ -154,6 +154,16 @@ class RLOrchestrator:
         self.last_stats.update({f"curriculum/{k}": v for k, v in cur.metrics().items()})
         return keep, rejected
 
+    def for_step(self, prompts) -> "RLOrchestrator":
+        """A view of this orchestrator with its own prompt source and stats,
+        for one step generated concurrently with others (the algorithm,
+        scorer and engine are shared)."""
+        view = type(self).__new__(type(self))
+        view.__dict__.update(self.__dict__)
+        view.prompts = prompts
+        view.last_stats = {}
+        return view
+
     def materialize(self, step: int) -> list[RLExample]:
         o = self.cfg.orchestrator
         n_prompts = o.examples_per_step or 1

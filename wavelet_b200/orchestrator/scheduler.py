@@ -1,31 +1,24 @@
 """``wavelet rl-inference``: the rollout role in process mode.
 
-For every optimizer step s (from the resume cursor on):
-
-1. wait until a policy snapshot >= ``required_policy_step(s)`` is STABLE
-   (``max_async_level`` lets generation run ahead of training);
-2. load it into the inference engine (HTTP servers or in-process);
-3. materialise the step's rollouts (generate, score, advantages, zero-
-   advantage filtering) and publish them to the rollout queue.
-
-On resume, queue batches at or beyond the resume step are discarded
-(orchestrator/scheduler.py:1912-1996 of the reference).  Orchestrator
-metrics are appended to ``orchestrator_metrics.jsonl``.
+Steps are generated ahead of the trainer with bounded prefetch and published
+in order by ``orchestrator.async_scheduler.AsyncRolloutScheduler`` (policy
+loads as snapshots appear, retries, evals, colocate_sleep, resume of the
+prompt and curriculum state).  On resume, queue batches at or beyond the
+resume step are discarded (orchestrator/scheduler.py:1912-1996 of the
+reference).  Orchestrator metrics are appended to ``orchestrator_metrics.jsonl``.
 """
 
 from __future__ import annotations
 
 import logging
 import sys
-import time
 from pathlib import Path
 
 from ..configs.config import RLConfig
-from ..monitor import append_jsonl, setup_logger, utc_now
-from ..transport.queue import FileSystemPolicyReceiver, FileSystemRolloutSender, prune_from, stable_steps
+from ..monitor import setup_logger
+from ..transport.queue import FileSystemPolicyReceiver, FileSystemRolloutSender
 from ..utils.config import load_config
 from .rollouts import RLOrchestrator
-from .schedule import required_policy_step, target_steps
 
 log = logging.getLogger("wavelet")
 
@@ -51,31 +44,18 @@ class RolloutScheduler:
 
     def resume_step(self) -> int:
         """First step to produce: one past the trainer's last consumed batch."""
-        done = [s for s in stable_steps(self.sender.queue_dir)]
-        consumed = [s for s in done if (self.sender.queue_dir / f"step-{s:06d}" / "consumed.json").exists()]
-        start = (max(consumed) + 1) if consumed else 0
-        prune_from(self.sender.queue_dir, start)
-        return start
+        return self.pipeline().resume_step()
+
+    def pipeline(self):
+        from .async_scheduler import AsyncRolloutScheduler
+
+        if getattr(self, "_pipeline", None) is None:
+            self._pipeline = AsyncRolloutScheduler(self.cfg, self.orch, self.engine, self.sender, self.policies)
+        return self._pipeline
 
     def run(self) -> int:
-        total = target_steps(self.cfg)
-        step = self.resume_step()
-        loaded = None
-        while step < total:
-            need = required_policy_step(step, self.cfg)
-            snap = self.policies.wait_for_step(need)
-            if loaded != snap.step:
-                self.engine.load_policy(snap.step_dir, step=snap.step)
-                loaded = snap.step
-            t0 = time.perf_counter()
-            self.orch.publish(step, policy_step=loaded)
-            m = dict(self.orch.last_stats)
-            m.update({"step": step, "policy_step": loaded, "policy_lag": step - loaded,
-                      "time/publish_seconds": time.perf_counter() - t0, "timestamp": utc_now()})
-            append_jsonl(self.out / "orchestrator_metrics.jsonl", m)
-            log.info("published rollouts for step %d (policy %d, reward %.4f)", step, loaded, m.get("reward/mean", 0.0))
-            step += 1
-        return 0
+        """Bounded-prefetch, in-order rollout publishing (``AsyncRolloutScheduler``)."""
+        return self.pipeline().run()
 
 
 class _GeneratorAdapter:

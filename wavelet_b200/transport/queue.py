@@ -126,6 +126,7 @@ class RolloutManifest:
     environment_next_record_cursors: dict[str, int] | None = None
     environment_selection_cursor: int | None = None
     curriculum_state: dict[str, dict[str, Any]] | None = None
+    prompt_source_state: dict[str, Any] | None = None  # prompt source right after this step's draw (resume)
 
 
 @dataclass
