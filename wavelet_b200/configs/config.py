@@ -281,10 +281,10 @@ class FSDPConfig(ConfigModel):
     # how expert-parallel token copies move on one CUDA node: fused row kernels
     # over peer memory ("fabric") or variable-split NCCL all-to-alls ("nccl")
     ep_dispatch: Literal["fabric", "nccl"] = "fabric"
-    # expert-parallel row buffers (fabric dispatch): this many times the
-    # (token, expert) copies of one micro-batch, plus padding; a layer whose
-    # routing needs more on some rank is reported as an error
-    ep_capacity_factor: float = Field(default=2.0, ge=1.0)
+    # expert-parallel row buffers (fabric dispatch): unset = room for the worst
+    # routing; a number = that many times the average (token, expert) copies
+    # per rank (less memory; a layer whose routing needs more is an error)
+    ep_capacity_factor: float | None = Field(default=None, ge=1.0)
     # how tensor-parallel partial sums are reduced on one CUDA node: GEMMs whose
     # epilogue stores into the peers' buffers ("fabric") or NCCL all-reduce
     tp_reduce: Literal["fabric", "nccl"] = "fabric"

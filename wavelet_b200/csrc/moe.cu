@@ -11,8 +11,10 @@
 //                 start / padded length / row count, and the expert of every
 //                 128-row tile (-1 past the end, so the grouped GEMM skips it).
 //                 A layout that does not fit the capacity of any rank sets
-//                 the overflow flag (kErrEpOverflow) and every transfer of
-//                 that layer is skipped: nothing is written out of bounds.
+//                 the overflow flag (kErrEpOverflow); the layout is then
+//                 empty (no tiles, zero-length segments) and every transfer
+//                 of that layer is skipped: nothing is written out of bounds
+//                 and nothing reads rows that were not written.
 //   moe_copy_rows stable row of every (token, slot) copy in its owner's layout
 //                 (copies of one expert keep (token, slot) order), and the
 //                 owner rank.
@@ -139,9 +141,11 @@ __global__ void moe_layout_kernel(const int* __restrict__ allc, int ep, int me, 
   __syncthreads();
   if (ge < E && ge / El == me) {
     const int el = ge - me * El;
-    k_start[el] = start[ge];
-    k_len[el] = padded[ge];
-    n_recv[el] = n;
+    // an over-capacity layout is empty: no tile, no segment, no row, so no
+    // kernel reads a row that nothing wrote
+    k_start[el] = s_over ? 0 : start[ge];
+    k_len[el] = s_over ? 0 : padded[ge];
+    n_recv[el] = s_over ? 0 : n;
     if (!s_over) {
       const int t0 = start[ge] / pad, t1 = (start[ge] + padded[ge]) / pad;
       for (int t = t0; t < t1 && t < cap_tiles; ++t) tile_group[t] = el;
@@ -150,7 +154,7 @@ __global__ void moe_layout_kernel(const int* __restrict__ allc, int ep, int me, 
   if (threadIdx.x == 0) {
     int rows = 0;
     for (int el = 0; el < El; ++el) rows += padded[me * El + el];
-    rows_out[0] = rows;
+    rows_out[0] = s_over ? 0 : rows;
     overflow[0] = s_over;
     if (s_over && err) atomicOr(err, kErrEpOverflow);
   }

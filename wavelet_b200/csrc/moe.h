@@ -19,7 +19,8 @@ void moe_route(const float* logits, int T, int E, int k, bool norm_topk, bool bf
 // owner's padded layout; this rank's layout: k_start / k_len (padded) /
 // n_recv per local expert, tile_group[t] = local expert of 128-row tile t or
 // -1, rows[0] = rows used.  overflow[0] = 1 (and kErrEpOverflow in err) when
-// any rank's layout exceeds cap_rows; the layout is then empty.
+// any rank's layout exceeds cap_rows; the layout is then empty (every tile -1,
+// k_start / k_len / n_recv 0, rows 0).
 void moe_layout(const int* allc, int ep, int me, int E, int pad, int64_t cap_rows, int cap_tiles, int64_t* base,
                 int* tile_group, int* k_start, int* k_len, int* n_recv, int* rows, int* overflow, int* err,
                 cudaStream_t st);

@@ -184,12 +184,16 @@ class CausalLM:
             master = flat.master[a - lo:b - lo].clone() if (flat.master is not None and a < b) else None
             self._frozen.append((n, flat.view(n).clone(), (a - lo, b - lo) if a < b else None, master))
 
-    def after_optimizer_step(self) -> None:
-        for layer in self.layers:  # an over-capacity expert layout invalidates the step: report it
+    def _check_ep_layouts(self) -> None:
+        """An over-capacity expert layout invalidates the micro-batches of this
+        step: report it (EPCapacityError) before the optimizer uses them."""
+        for layer in self.layers:
             fe = getattr(layer.moe, "ep_fabric", None) if layer.moe is not None else None
             if fe is not None:
                 fe.check()
-                break
+                return
+
+    def after_optimizer_step(self) -> None:
         for n, val, span, master in getattr(self, "_frozen", []):
             self.flat.view(n).copy_(val)
             if span is not None and master is not None:
@@ -199,6 +203,7 @@ class CausalLM:
         """Cross-TP sums of gradients that each TP rank only partially owns:
         the QK-norm weights are shared by all heads, which are split.  Frozen
         parameters get zero gradients."""
+        self._check_ep_layouts()
         for n, _, _, _ in getattr(self, "_frozen", []):
             g = self.flat.grad_view(n)
             if g is not None:
@@ -224,11 +229,11 @@ class CausalLM:
         return self.tp_fabric
 
     def attach_ep_fabric(self, fabric, capacity_rows: int = 1 << 16, max_tokens: int = 0,
-                         capacity_factor: float = 2.0):
+                         capacity_factor: float | None = None):
         """Expert dispatch / combine over peer memory (parallel.ep_fabric) for
         every MoE layer; ``fabric`` spans the expert-parallel group.  The row
-        buffers hold ``capacity_factor`` x the copies of ``max_tokens`` tokens
-        per micro-batch (plus padding), at least ``capacity_rows``."""
+        buffers fit the worst routing of ``max_tokens`` tokens per micro-batch
+        (or ``capacity_factor`` x the average copies), at least ``capacity_rows``."""
         from ..parallel.ep_fabric import FabricEP
 
         fe = FabricEP(fabric, self.ep_group, self.cfg.num_experts, self.cfg.hidden_size, capacity_rows,

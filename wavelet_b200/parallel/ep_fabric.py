@@ -23,12 +23,14 @@ Backward mirrors it: ``dy`` rows (dout scaled by the routing weight) are
 dispatched, the expert backward runs locally, and ``dxs`` rows are gathered
 back and summed per token.  Each direction costs the bytes of the NCCL path
 but no staging copies, and the gather, weighting and residual add ride on
-the transfers.  Buffers hold ``capacity`` rows, fixed at construction
-(``capacity_factor`` x the copies of ``max_tokens`` tokens, plus a padding
-tile per local expert); a layout that would not fit any rank's buffer is
-detected on the device, every transfer of that layer is skipped (nothing is
-written or read past a buffer) and ``check()`` raises: raise
-``fsdp.ep_capacity_factor``.
+the transfers.  Buffers hold ``capacity`` rows, fixed at construction: by
+default the worst case (every rank sends each of its ``max_tokens`` tokens to
+min(k, experts per rank) experts of one rank), or ``capacity_factor`` x the
+average copies per rank to save memory, plus a padding tile per local expert.
+A layout that would not fit is detected on the device: that layer's layout
+is empty and its transfers are skipped (nothing is written or read past a
+buffer, nothing unwritten is read), and ``check()`` raises before the
+optimizer step: raise ``fsdp.ep_capacity_factor`` or leave it unset.
 """
 
 from __future__ import annotations
@@ -66,7 +68,7 @@ class EPCapacityError(RuntimeError):
 
 class FabricEP:
     def __init__(self, fabric: Fabric, group, E: int, H: int, capacity: int, dtype=torch.bfloat16, k: int = 8,
-                 max_tokens: int = 0, capacity_factor: float = 2.0):
+                 max_tokens: int = 0, capacity_factor: float | None = None):
         self.fab = fabric
         self.group = group
         self.ep = fabric.world
@@ -75,7 +77,12 @@ class FabricEP:
         self.El = E // self.ep
         self.H = H
         if max_tokens > 0:
-            capacity = max(capacity, int(capacity_factor * max_tokens * k) + self.El * PAD)
+            # worst case per destination: every token sends one copy to each of
+            # up to min(k, El) of its experts, from every rank
+            worst = self.ep * max_tokens * min(k, self.El)
+            rows = worst if capacity_factor is None or capacity_factor <= 0 else \
+                min(worst, int(capacity_factor * max_tokens * k))
+            capacity = max(capacity, rows + self.El * PAD)
         self.capacity = (capacity + PAD - 1) // PAD * PAD
         self.bufs = {n: fabric.alloc(self.capacity * H, dtype) for n in ("xs", "y", "dy", "dxs")}
         self.cnt = fabric.alloc(self.ep * E, torch.int32)  # every rank's per-expert counts
