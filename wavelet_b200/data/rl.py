@@ -69,6 +69,7 @@ class RLSample:
     ref_kl_weights: torch.Tensor | None
     sampling_mask: list[list[int]] | None  # per target position (only masked ones used)
     reward: float = 0.0
+    has_inference: torch.Tensor | None = None  # [L] bool: target positions with a recorded inference log-prob
 
 
 def _per_token(v, n: int, default: float | None) -> torch.Tensor | None:
@@ -121,7 +122,8 @@ def sample_from_example(e: RLExample, default_temperature: float = 1.0) -> RLSam
         sm = [[] for _ in range(L)]
         for k, i in enumerate(idx.tolist()):
             sm[i] = list(e.sampling_mask[k])
-    return RLSample(ids, pos_mask, ilp, tlp, adv, float(temp), ce, rk, sm, float(e.reward or 0.0))
+    has_inf = pos_mask.clone() if e.inference_logprobs is not None else torch.zeros(L, dtype=torch.bool)
+    return RLSample(ids, pos_mask, ilp, tlp, adv, float(temp), ce, rk, sm, float(e.reward or 0.0), has_inf)
 
 
 # -------------------------------------------------------------------- packing
@@ -181,12 +183,25 @@ class RLPackedBatch:
     sampling_mask: list[list[int]] | None
     num_samples: int
     rewards: list[float] = field(default_factory=list)
+    has_inference: torch.Tensor | None = None  # bool [T]
 
     def to(self, device) -> "RLPackedBatch":
         mv = lambda t: None if t is None else t.to(device, non_blocking=True)  # noqa: E731
         return RLPackedBatch(self.base.to(device), mv(self.inference_logprobs), mv(self.teacher_logprobs),
                              mv(self.advantages), mv(self.loss_mask), self.temperature, mv(self.ce_weights),
-                             mv(self.ref_kl_weights), self.sampling_mask, self.num_samples, self.rewards)
+                             mv(self.ref_kl_weights), self.sampling_mask, self.num_samples, self.rewards,
+                             mv(self.has_inference))
+
+    def missing_inference(self) -> torch.Tensor:
+        """Target positions whose RL or reference-KL term needs an inference
+        log-prob that the record did not carry (host tensors)."""
+        need = self.loss_mask.clone()
+        if self.ce_weights is not None:  # cross-entropy-only tokens use no inference log-prob
+            need &= ~((self.ce_weights != 0) & (self.advantages == 0))
+        if self.ref_kl_weights is not None:
+            need |= self.loss_mask & (self.ref_kl_weights != 0)
+        has = self.has_inference if self.has_inference is not None else torch.ones_like(need)
+        return need & ~has
 
 
 def collate(samples: list[RLSample], pad_token: int = 0) -> RLPackedBatch:
@@ -196,7 +211,8 @@ def collate(samples: list[RLSample], pad_token: int = 0) -> RLPackedBatch:
         z = torch.zeros(1)
         base = PackedBatch(ids, torch.zeros(1, dtype=torch.int32), torch.tensor([0, 1], dtype=torch.int32), 1,
                            torch.full((1,), -100), z.clone())
-        return RLPackedBatch(base, z.clone(), None, z.clone(), torch.zeros(1, dtype=torch.bool), 1.0, None, None, None, 0)
+        return RLPackedBatch(base, z.clone(), None, z.clone(), torch.zeros(1, dtype=torch.bool), 1.0, None, None, None, 0,
+                             [], torch.zeros(1, dtype=torch.bool))
     temps = {s.temperature for s in samples}
     if len(temps) > 1:
         raise ValueError("one packed micro-batch must use a single sampling temperature")
@@ -218,9 +234,10 @@ def collate(samples: list[RLSample], pad_token: int = 0) -> RLPackedBatch:
         for s in samples:
             sm += s.sampling_mask if s.sampling_mask is not None else [[] for _ in range(s.input_ids.numel())]
     base = PackedBatch(ids, pos, cu, max(lens), torch.cat(tg), mask.float())
+    has = torch.cat([s.has_inference if s.has_inference is not None else s.loss_mask for s in samples])
     return RLPackedBatch(base, cat("inference_logprobs"), cat("teacher_logprobs"), cat("advantages"), mask,
                          samples[0].temperature, cat("ce_weights"), cat("ref_kl_weights"), sm, len(samples),
-                         [s.reward for s in samples])
+                         [s.reward for s in samples], has)
 
 
 def make_rank_batches(examples: list[RLExample], seq_len: int, dp_rank: int, dp_world: int,

@@ -168,6 +168,31 @@ class CausalLM:
         for i, layer in enumerate(self.layers):
             layer.lora = adapters.layer_views(i)
 
+    def adapters_disabled(self):
+        """Context manager: forward passes see the frozen base model only (the
+        LoRA adapters are detached from every layer and restored on exit) —
+        the reference policy of LoRA training."""
+        import contextlib
+
+        @contextlib.contextmanager
+        def _off():
+            saved = [layer.lora for layer in self.layers]
+            lora = self.lora
+            rg = self.flat.compute.requires_grad  # the CPU path turns it on for a model without adapters
+            for layer in self.layers:
+                layer.lora = None
+            self.lora = None
+            try:
+                yield
+            finally:
+                self.lora = lora
+                for layer, l in zip(self.layers, saved):
+                    layer.lora = l
+                if self.flat.compute.requires_grad != rg:
+                    self.flat.compute.requires_grad_(rg)
+
+        return _off()
+
     def freeze(self, names: list[str]) -> None:
         """Keep the parameters ``names`` of the dense store fixed: their
         gradients are zeroed before the optimizer step (so they add nothing to

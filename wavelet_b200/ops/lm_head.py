@@ -133,3 +133,27 @@ def logprob_entropy(h, W, targets, temperature: float = 1.0, gW=None, chunk: int
     if anchor is None:
         anchor = torch.empty(0, device=h.device, requires_grad=True)
     return ChunkedLogprobFn.apply(h, anchor, W, gW, targets, temperature, chunk, want_entropy)
+
+
+class _HeadLogitsCPU(torch.autograd.Function):
+    """CPU logits ``h W^T`` whose weight gradient is added into the flat
+    gradient view ``gW`` (the parameter views of the flat store do not take
+    part in autograd), so the LM head trains on every CPU path of the model,
+    the fused-kernel fallbacks (tensor / context parallel) included."""
+
+    @staticmethod
+    def forward(ctx, h, W, gW):
+        ctx.save_for_backward(h, W)
+        ctx.gW = gW
+        return h @ W.t()
+
+    @staticmethod
+    def backward(ctx, dz):
+        h, W = ctx.saved_tensors
+        if ctx.gW is not None:
+            ctx.gW.add_((dz.t() @ h).to(ctx.gW.dtype))
+        return dz @ W, None, None
+
+
+def cpu_head_logits(h: torch.Tensor, W: torch.Tensor, gW: torch.Tensor | None) -> torch.Tensor:
+    return _HeadLogitsCPU.apply(h, W.detach(), gW)

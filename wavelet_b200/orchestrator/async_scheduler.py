@@ -16,6 +16,10 @@ own formulation of the same behaviour:
   ``max_async_level + max_off_policy_steps`` steps behind.
 * **In-order publish.**  Finished steps are published to the durable queue in
   step order, each with the policy step that generated it.
+* **Chunks.**  With ``orchestrator.rollout_chunk_examples`` an optimizer step's
+  prompts are split into chunks of that many examples, each its own queue step
+  (queue step q = chunk q % C of optimizer step q // C), so the trainer can
+  start on the first chunk while later ones are generated.
 * **Policy loads.**  The newest STABLE snapshot is loaded as soon as it
   appears: in the background while steps are in flight when the engine can
   swap weights under load (``engine.concurrent_policy_load``: the HTTP servers
@@ -63,7 +67,7 @@ from typing import Callable
 from ..data.rl import example_to_payload
 from ..monitor import append_jsonl, emit_perf, utc_now
 from ..transport.queue import FileSystemPolicyReceiver, FileSystemRolloutSender, prune_from, stable_steps, step_dir
-from .schedule import required_policy_step, target_steps
+from .schedule import chunks_per_step, required_policy_step, target_steps
 
 log = logging.getLogger("wavelet")
 
@@ -233,6 +237,7 @@ class AsyncRolloutScheduler:
         self.done: dict[int, tuple[_Step, list, dict]] = {}
         self.load_future: Future | None = None
         self.asleep = False
+        self.C = chunks_per_step(cfg)  # queue steps (chunks) per optimizer step
         self.stats = {"rollout/retries": 0.0, "rollout/stale_discarded": 0.0}
         names = [e.resolved_name for e in cfg.eval.env] if cfg.eval is not None else []
         self.last_eval = eval_steps_done(self.out / "eval_metrics.jsonl", names)
@@ -330,9 +335,16 @@ class AsyncRolloutScheduler:
         recs = view.materialize(st.step)
         return recs, dict(view.last_stats)
 
+    def _unit_examples(self, unit: int) -> int:
+        o = self.cfg.orchestrator
+        n = o.examples_per_step or 1
+        if self.C == 1:
+            return n
+        ce = o.rollout_chunk_examples
+        return max(1, min(ce, n - (unit % self.C) * ce))
+
     def _submit(self, pool: ThreadPoolExecutor, step: int, attempt: int = 0) -> None:
-        n = self.cfg.orchestrator.examples_per_step or 1
-        prompts = self.prompts.take(n)
+        prompts = self.prompts.take(self._unit_examples(step))
         st = _Step(step, self.loaded, self.prompts.state_dict(), attempt)
         self._wake()
         fut = pool.submit(self._materialize, st, prompts)
@@ -353,7 +365,7 @@ class AsyncRolloutScheduler:
                     self._submit(pool, st.step, st.attempt + 1)
                     continue
                 raise
-            if st.policy is not None and st.policy < required_policy_step(st.step, self.cfg):
+            if st.policy is not None and st.policy < required_policy_step(st.step // self.C, self.cfg):
                 self.stats["rollout/stale_discarded"] += 1
                 self._submit(pool, st.step, st.attempt)
                 continue
@@ -364,14 +376,15 @@ class AsyncRolloutScheduler:
             st, recs, stats = self.done.pop(next_pub)
             rows = [example_to_payload(r) for r in recs]
             cur = self.prompts.curriculum
-            self.sender.publish(rows, step=st.step, training_records=rows, optimizer_step=st.step,
+            self.sender.publish(rows, step=st.step, training_records=rows, optimizer_step=st.step // self.C,
+                                chunk_index=(st.step % self.C) if self.C > 1 else None,
                                 policy_step=st.policy, tokens=sum(len(r.input_ids or []) for r in recs),
                                 reward_mean=stats.get("reward/mean"), prompt_source_state=st.prompt_state,
                                 curriculum_state=cur.state_dict() if cur is not None else None)
             m = dict(stats)
             m.update(self.stats)
-            m.update({"step": st.step, "policy_step": st.policy,
-                      "policy_lag": None if st.policy is None else st.step - st.policy,
+            m.update({"step": st.step, "optimizer_step": st.step // self.C, "policy_step": st.policy,
+                      "policy_lag": None if st.policy is None else st.step // self.C - st.policy,
                       "time/step_seconds": time.perf_counter() - st.t_submit, "timestamp": utc_now()})
             append_jsonl(self.out / "orchestrator_metrics.jsonl", m)
             log.info("published rollouts for step %d (policy %s, reward %.4f)", st.step, st.policy,
@@ -383,10 +396,11 @@ class AsyncRolloutScheduler:
 
     # ------------------------------------------------------------ run
     def run(self, target: int | None = None, start: int | None = None) -> int:
-        total = target_steps(self.cfg) if target is None else target
+        """Publish queue steps up to ``target`` optimizer steps (x chunks)."""
+        total = (target_steps(self.cfg) if target is None else target) * self.C
         step = self.resume_step() if start is None else start
         next_pub = step
-        prefetch = max(1, min(int(self.cfg.orchestrator.max_async_level), max(total - step, 1)))
+        prefetch = max(1, min(max(1, int(self.cfg.orchestrator.max_async_level)) * self.C, max(total - step, 1)))
         if not self.concurrent_generate:
             prefetch = 1  # one generator on one GPU: steps run back to back (still ahead of the trainer)
         poll = self.cfg.policy_transfer.poll_interval_seconds
@@ -394,7 +408,7 @@ class AsyncRolloutScheduler:
             while next_pub < total:
                 self._finish_load()
                 self._maybe_start_load(pool)
-                need = required_policy_step(step, self.cfg) if step < total else None
+                need = required_policy_step(step // self.C, self.cfg) if step < total else None
                 ready = need is not None and self.loaded is not None and self.loaded >= need
                 if need is not None and not ready and not self.pending and self.load_future is None:
                     self._after_load(self._load(need))  # nothing in flight: block for the required snapshot
@@ -413,7 +427,7 @@ class AsyncRolloutScheduler:
                 else:
                     time.sleep(poll)
             self._finish_load(block=True)
-        self._final_evals(total)
+        self._final_evals(total // self.C)
         return 0
 
     def _final_evals(self, total: int) -> None:

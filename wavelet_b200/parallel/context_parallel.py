@@ -109,6 +109,26 @@ def shard_batch(b, cp: int, rank: int, group, align: int = 128):
     return local
 
 
+def shard_index(cu_seqlens: torch.Tensor, cp: int, rank: int, align: int = 128):
+    """Token map of this rank's context-parallel share (the layout of
+    ``shard_batch``): for every local token its source row in the packed
+    batch, whether it is a real token (not chunk padding) and its sequence.
+    Any per-token tensor ``t`` of the batch maps to the local layout as
+    ``torch.where(real, t[src], fill)``."""
+    bounds = cu_seqlens.tolist()
+    lens = [e - s_ for s_, e in zip(bounds[:-1], bounds[1:])]
+    unit = 2 * cp * align
+    C = [max(1, -(-L // unit)) * unit // (2 * cp) for L in lens]
+    src, real, seq = [], [], []
+    for c in (rank, 2 * cp - 1 - rank):
+        for s_, L in enumerate(lens):
+            p = torch.arange(c * C[s_], (c + 1) * C[s_])
+            src.append((bounds[s_] + p).clamp_max(bounds[s_] + max(L, 1) - 1))
+            real.append(p < L)
+            seq.append(torch.full((C[s_],), s_, dtype=torch.long))
+    return torch.cat(src), torch.cat(real), torch.cat(seq)
+
+
 def cu_q_local(C: list[int]) -> torch.Tensor:
     """Sequence boundaries of the local tokens (every chunk is its own
     sequence for the per-token kernels; attention uses the plan)."""

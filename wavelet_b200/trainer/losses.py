@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import importlib
 from dataclasses import dataclass, field
-from typing import Callable
+from typing import Any, Callable
 
 import torch
 from torch import Tensor
@@ -207,21 +207,44 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
                  advantages: Tensor, loss_mask: Tensor, cfg, *, cu_seqlens: Tensor,
                  rl_weights: Tensor | None = None, ce_weights: Tensor | None = None,
                  ref_kl_weights: Tensor | None = None, component_scales: dict[str, float] | None = None,
-                 rl_loss_fn: LossFn | None = None) -> tuple[Tensor, dict[str, float]]:
+                 rl_loss_fn: LossFn | None = None, present: dict[str, bool] | None = None, sync: bool = True,
+                 seg: Tensor | None = None, n_seq: int | None = None,
+                 seq_counts: Tensor | None = None) -> tuple[Tensor, dict[str, Any]]:
     """Scalar loss (already divided by the component scales) and metrics.
 
     ``component_scales`` are the global normalisers (token / sequence counts
     summed over data-parallel ranks and micro-batches); when absent the local
     counts are used (trainer/losses.py:520-591).
+
+    Host-synchronisation-free use (the trainer's micro-batch loop): pass every
+    component scale, ``present`` (whether the batch has any RL / CE / ref-KL
+    token, known on the host before the copy) and ``sync=False``: the metrics
+    are then 0-d device tensors, converted once per step by the caller.
+
+    Context parallelism: ``seg`` / ``n_seq`` give each local token's sequence
+    (local tokens of one sequence need not be contiguous) and ``seq_counts`` the
+    sequence's RL-token count over all ranks (the sequence normaliser).
     """
     T = trainer_logprobs.shape[0]
-    seg = segment_ids(cu_seqlens, T)
-    n = cu_seqlens.numel() - 1
+    if seg is None:
+        seg = segment_ids(cu_seqlens, T)
+        n = cu_seqlens.numel() - 1
+    else:
+        n = int(n_seq)
     loss_mask = loss_mask.bool()
     fn = rl_loss_fn or setup_rl_loss_fn(cfg)
-    counts = component_unit_counts(loss_mask, seg, n, rl_weights, ce_weights, ref_kl_weights, cfg.normalization)
-    scales = {k: max(float(v), 1.0) for k, v in counts.items()}
-    scales.update({k: max(float(v), 1.0) for k, v in (component_scales or {}).items()})
+    given = dict(component_scales or {})
+    if all(k in given for k in ("rl", "ce", "ref_kl")):
+        scales = {k: max(float(v), 1.0) for k, v in given.items()}
+    else:
+        counts = component_unit_counts(loss_mask, seg, n, rl_weights, ce_weights, ref_kl_weights, cfg.normalization)
+        scales = {k: max(float(v), 1.0) for k, v in counts.items()}
+        scales.update({k: max(float(v), 1.0) for k, v in given.items()})
+
+    def has(name: str, mask: Tensor) -> bool:
+        if present is not None and name in present:
+            return bool(present[name])
+        return bool(mask.any())
     total = trainer_logprobs.sum() * 0.0
     seq_metrics: list[tuple[str, Tensor, Tensor, Tensor]] = []  # name, values, mask, active sequences
     span_metrics: dict[str, list[Tensor]] = {}
@@ -230,15 +253,18 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
         return seg_sum(mask.float(), seg, n) > 0
 
     rl_mask = loss_mask if rl_weights is None else loss_mask & (rl_weights != 0)
-    if bool(rl_mask.any()) and getattr(fn, "per_span", False):
+    rl_present = has("rl", rl_mask)
+    if rl_present and getattr(fn, "per_span", False):
+        if seq_counts is not None:
+            raise NotImplementedError("per-span custom RL losses need whole sequences (no context parallelism)")
         total = total + _per_span_rl(fn, trainer_logprobs, inference_logprobs, teacher_logprobs, advantages,
                                      rl_mask, rl_weights, cu_seqlens, cfg.normalization, span_metrics) / scales["rl"]
-    elif bool(rl_mask.any()):
+    elif rl_present:
         out = fn(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, rl_mask, rl_weights))
         per = out.loss
         if cfg.normalization == "sequence":
             per_seq = seg_sum(per, seg, n)
-            cnt = seg_sum(rl_mask.float(), seg, n).clamp_min(1.0)
+            cnt = (seq_counts.float() if seq_counts is not None else seg_sum(rl_mask.float(), seg, n)).clamp_min(1.0)
             total = total + (per_seq / cnt).sum() / scales["rl"]
         else:
             total = total + per.sum() / scales["rl"]
@@ -248,25 +274,38 @@ def compute_loss(trainer_logprobs: Tensor, inference_logprobs: Tensor, teacher_l
         if w is None:
             continue
         cm = loss_mask & (w != 0)
-        if bool(cm.any()):
+        if has(name, cm):
             out = f(LossInputs(trainer_logprobs, inference_logprobs, teacher_logprobs, advantages, cm, w))
             total = total + out.loss.sum() / scales[name]
             act = active_of(cm)
             seq_metrics += [(k, v, m, act) for k, (v, m) in out.metrics.items()]
 
-    metrics: dict[str, float] = {}
+    dev_metrics: dict[str, Tensor] = {}
     per_seq_values = {k: _seq_means(v.detach(), m, seg, n, act) for k, v, m, act in seq_metrics}
     per_seq_values.update({k: torch.stack(v) for k, v in span_metrics.items()})
     for k, per_seq in per_seq_values.items():
         if per_seq.numel() == 0:
             continue
-        metrics[k] = float(per_seq.mean())
-        metrics[f"{k}/mean"] = float(per_seq.mean())
-        metrics[f"{k}/median"] = float(per_seq.median())
-        metrics[f"{k}/std"] = float(per_seq.std(unbiased=False)) if per_seq.numel() > 1 else 0.0
-        metrics[f"{k}/min"] = float(per_seq.min())
-        metrics[f"{k}/max"] = float(per_seq.max())
-    return total, metrics
+        per_seq = per_seq.float()
+        mean = per_seq.mean()
+        dev_metrics[k] = mean
+        dev_metrics[f"{k}/mean"] = mean
+        dev_metrics[f"{k}/median"] = per_seq.median()
+        dev_metrics[f"{k}/std"] = per_seq.std(unbiased=False) if per_seq.numel() > 1 else torch.zeros_like(mean)
+        dev_metrics[f"{k}/min"] = per_seq.min()
+        dev_metrics[f"{k}/max"] = per_seq.max()
+    if not sync:
+        return total, dev_metrics
+    return total, tensors_to_floats(dev_metrics)
+
+
+def tensors_to_floats(d: dict[str, Tensor]) -> dict[str, float]:
+    """0-d tensors -> floats with one device-to-host transfer."""
+    if not d:
+        return {}
+    keys = list(d)
+    vals = torch.stack([d[k].detach().float().reshape(()) for k in keys]).cpu().tolist()
+    return dict(zip(keys, vals))
 
 
 def _per_span_rl(fn: LossFn, tl: Tensor, il: Tensor, teacher: Tensor | None, adv: Tensor, rl_mask: Tensor,
