@@ -8,12 +8,17 @@ Subcommands (reference debug.py:50-1800):
   and reward settings, and the B200 kernel constraints of the model
   (head_dim 128, NF4 column multiples, extension present).  Exit 1 on any
   error-level check.
-* ``inference {inspect,health,smoke}`` — engine/server configuration, HTTP
-  health of every replica, or a few probe generations with a summary.
-* ``orchestrator {inspect,sample}`` — queue and policy-directory state, or
-  one materialised (not published) rollout batch.
-* ``trainer {inspect,tokens}`` — validate a published rollout batch (row
-  schema, token/mask/logprob alignment, advantages) or dump per-token rows.
+* ``inference {inspect,health,smoke,benchmark,continuous-batch|batch}`` —
+  engine/server configuration, HTTP health of every replica, a few probe
+  generations, timed generation rounds, or many concurrent completion
+  requests against the servers (latency percentiles, throughput, errors).
+* ``orchestrator {inspect,sample,benchmark,materialize}`` — queue and policy
+  state, the prompts a step would draw, one step's rollouts with per-phase
+  timings, or the same published as a queue step.
+* ``trainer {inspect,tokens,parity}`` — validate a rollout batch (row schema,
+  token/mask/logprob alignment, advantages), dump per-token rows, or compare
+  inference and trainer log-probs of its trainable tokens (a stored column,
+  or ``--compute`` with the configured model).
 
 All reports print as text, or as JSON with ``--json``.
 """
@@ -186,14 +191,108 @@ def http_health(cfg: RLConfig) -> list[dict[str, Any]]:
     return out
 
 
+def _engine_and_orchestrator(cfg: RLConfig, engine=None):
+    from .inference.policy import create_policy_inference_engine
+    from .orchestrator.rollouts import RLOrchestrator
+    from .orchestrator.runtime import build_prompt_source
+    from .orchestrator.scheduler import _GeneratorAdapter
+
+    if engine is None:
+        engine = create_policy_inference_engine(cfg)
+        engine.setup()
+    return engine, RLOrchestrator(cfg, _GeneratorAdapter(engine), None, build_prompt_source(cfg, 1 << 30))
+
+
+def _percentile(xs: list[float], q: float) -> float | None:
+    if not xs:
+        return None
+    ys = sorted(xs)
+    return ys[min(len(ys) - 1, max(0, int(round(q * (len(ys) - 1)))))]
+
+
+def inference_benchmark(cfg: RLConfig, *, count: int, warmup: int, repeats: int, engine=None) -> dict[str, Any]:
+    """Timed generations of ``count`` prompts (``repeats`` timed rounds after
+    ``warmup`` untimed ones) through the configured engine."""
+    import time
+
+    engine, orch = _engine_and_orchestrator(cfg, engine)
+    prompts = orch.prompts.take(count)
+    for _ in range(warmup):
+        orch.generate_records(prompts, 0)
+    rounds = []
+    for i in range(repeats):
+        t0 = time.perf_counter()
+        recs = orch.generate_records(prompts, i)
+        dt = time.perf_counter() - t0
+        ntok = sum(len((r.metadata or {}).get("completion_ids") or []) for r in recs)
+        rounds.append({"seconds": dt, "completions": len(recs), "completion_tokens": ntok,
+                       "tokens_per_second": ntok / max(dt, 1e-9)})
+    tps = [r["tokens_per_second"] for r in rounds]
+    return {"prompts": count, "warmup": warmup, "repeats": repeats, "rounds": rounds,
+            "tokens_per_second": {"mean": sum(tps) / len(tps), "min": min(tps), "max": max(tps)}}
+
+
+def continuous_batch_probe(cfg: RLConfig, *, count: int, concurrency: int, max_completion_tokens: int,
+                           stagger_ms: float = 0.0, post=None) -> dict[str, Any]:
+    """``count`` completion requests kept ``concurrency`` in flight against the
+    HTTP inference replicas (round robin, optionally staggered): latency
+    percentiles, throughput and errors of the servers' continuous batching."""
+    import time
+    from concurrent.futures import ThreadPoolExecutor
+
+    from .inference.client import endpoints, http_json
+
+    urls = endpoints(cfg)
+    post = post or (lambda url, payload: http_json(url + "/v1/completions", payload,
+                                                    timeout=cfg.inference.http.request_timeout_seconds))
+    prompt_len = max(1, cfg.data.fake_prompt_len or 8)
+    t_start = time.perf_counter()
+
+    def one(i: int) -> dict[str, Any]:
+        delay = t_start + i * stagger_ms / 1000.0 - time.perf_counter()
+        if delay > 0:
+            time.sleep(delay)
+        url = urls[i % len(urls)]
+        t0 = time.perf_counter()
+        try:
+            r = post(url, {"prompt_token_ids": [[3 + (i + j) % 50 for j in range(prompt_len)]],
+                           "max_tokens": max_completion_tokens, "n": 1,
+                           "temperature": cfg.inference.sampling.temperature})
+            toks = sum(len(c.get("token_ids") or []) for c in r.get("choices", []))
+            return {"index": i, "url": url, "seconds": time.perf_counter() - t0, "tokens": toks, "error": None}
+        except Exception as e:  # reported per request
+            return {"index": i, "url": url, "seconds": time.perf_counter() - t0, "tokens": 0, "error": str(e)}
+
+    with ThreadPoolExecutor(max_workers=concurrency) as pool:
+        reqs = list(pool.map(one, range(count)))
+    wall = time.perf_counter() - t_start
+    lat = [r["seconds"] for r in reqs if r["error"] is None]
+    toks = sum(r["tokens"] for r in reqs)
+    return {"metrics": {"requests": count, "concurrency": concurrency, "errors": sum(r["error"] is not None for r in reqs),
+                        "wall_seconds": wall, "tokens": toks, "tokens_per_second": toks / max(wall, 1e-9),
+                        "latency_p50": _percentile(lat, 0.5), "latency_p95": _percentile(lat, 0.95),
+                        "latency_max": max(lat) if lat else None},
+            "sample": reqs[:5], "errors": [r for r in reqs if r["error"] is not None][:5]}
+
+
 def _inference_main(argv: list[str]) -> int:
     from .utils.config import load_config
 
-    p = argparse.ArgumentParser(prog="wavelet debug inference")
-    p.add_argument("action", choices=("inspect", "health", "smoke"))
+    p = argparse.ArgumentParser(prog="wavelet debug inference",
+                                description="Inspect and probe RL inference without trainer / orchestrator.")
+    p.add_argument("action", choices=("inspect", "health", "smoke", "benchmark", "continuous-batch", "batch"))
     p.add_argument("--json", action="store_true")
-    p.add_argument("--prompts", type=int, default=2)
+    p.add_argument("--prompts", "--count", dest="count", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=0)
+    p.add_argument("--repeats", type=int, default=1)
+    p.add_argument("--concurrency", type=int, default=8)
+    p.add_argument("--stagger-ms", type=float, default=0.0)
+    p.add_argument("--max-completion-tokens", type=int, default=128)
     a, rest = p.parse_known_args(argv)
+    for name, lo in (("count", 1), ("warmup", 0), ("repeats", 1), ("concurrency", 1), ("stagger_ms", 0),
+                     ("max_completion_tokens", 1)):
+        if getattr(a, name) < lo:
+            raise SystemExit(f"--{name.replace('_', '-')} must be >= {lo}")
     cfg = load_config(RLConfig, rest)
     if a.action == "inspect":
         _print({"mode": cfg.inference.mode, "sampling": cfg.inference.sampling.model_dump(),
@@ -203,47 +302,89 @@ def _inference_main(argv: list[str]) -> int:
         rows = http_health(cfg)
         _print({"health": rows}, a.json)
         return 0 if all(r["ok"] for r in rows) else 1
-    from .inference.policy import create_policy_inference_engine
-    from .orchestrator.rollouts import RLOrchestrator
-    from .orchestrator.runtime import build_prompt_source
-    from .orchestrator.scheduler import _GeneratorAdapter
-
-    eng = create_policy_inference_engine(cfg)
-    eng.setup()
-    orch = RLOrchestrator(cfg, _GeneratorAdapter(eng), None, build_prompt_source(cfg, 1 << 30))
-    recs = orch.generate_records(orch.prompts.take(a.prompts), 0)
+    if a.action in ("continuous-batch", "batch"):
+        rep = continuous_batch_probe(cfg, count=a.count, concurrency=a.concurrency,
+                                     max_completion_tokens=a.max_completion_tokens, stagger_ms=a.stagger_ms)
+        _print(rep, a.json)
+        return 0 if rep["metrics"]["errors"] == 0 else 1
+    if a.action == "benchmark":
+        _print(inference_benchmark(cfg, count=a.count, warmup=a.warmup, repeats=a.repeats), a.json)
+        return 0
+    eng, orch = _engine_and_orchestrator(cfg)
+    recs = orch.generate_records(orch.prompts.take(a.count), 0)
     _print({"records": len(recs), "stats": orch.last_stats,
             "completion_tokens": [len((r.metadata or {}).get("completion_ids") or []) for r in recs]}, a.json)
     return 0
 
 
 # -------------------------------------------------------------- orchestrator
+def probe_orchestrator(cfg: RLConfig, *, step: int = 0, engine=None, write: bool = False) -> dict[str, Any]:
+    """One step's rollouts end to end (prompt draw, generation, rewards,
+    advantages, zero-advantage filter) with per-phase timings; ``write``
+    publishes them as queue step ``step`` (the ``materialize`` action)."""
+    import time
+
+    from .data.rl import example_to_payload
+    from .transport.queue import FileSystemRolloutSender
+
+    timings: dict[str, float] = {}
+    t0 = time.perf_counter()
+    engine, orch = _engine_and_orchestrator(cfg, engine)
+    timings["setup"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    recs = orch.materialize(step)
+    timings["materialize"] = time.perf_counter() - t0
+    out = None
+    if write:
+        t0 = time.perf_counter()
+        rows = [example_to_payload(r) for r in recs]
+        batch = FileSystemRolloutSender(Path(cfg.output_dir), cfg.transport).publish(
+            rows, step=step, training_records=rows, optimizer_step=step,
+            tokens=sum(len(r.input_ids or []) for r in recs), reward_mean=orch.last_stats.get("reward/mean"))
+        out = str(batch.path)
+        timings["write"] = time.perf_counter() - t0
+    timings["total"] = sum(timings.values())
+    return {"step": step, "records_trainable": len(recs), "examples_per_step": cfg.orchestrator.examples_per_step,
+            "rollouts_per_example": cfg.orchestrator.rollouts_per_example, "timings": timings,
+            "metrics": orch.last_stats, "output_path": out,
+            "sample": [{"reward": r.reward, "advantage": r.advantage, "tokens": len(r.input_ids or [])}
+                       for r in recs[:8]]}
+
+
 def _orchestrator_main(argv: list[str]) -> int:
     from .transport.queue import resolve_policy_dir, resolve_queue_dir, scan_queue, stable_steps
     from .utils.config import load_config
 
-    p = argparse.ArgumentParser(prog="wavelet debug orchestrator")
-    p.add_argument("action", choices=("inspect", "sample"))
+    p = argparse.ArgumentParser(prog="wavelet debug orchestrator",
+                                description="Inspect and benchmark RL orchestration without trainer.")
+    p.add_argument("action", choices=("inspect", "sample", "benchmark", "materialize"))
+    p.add_argument("--step", type=int, default=0)
+    p.add_argument("--examples", type=int, default=None)
+    p.add_argument("--rollouts", type=int, default=None)
     p.add_argument("--json", action="store_true")
     a, rest = p.parse_known_args(argv)
+    if a.examples is not None and a.examples < 1:
+        raise SystemExit("--examples must be >= 1")
+    if a.rollouts is not None and a.rollouts < 1:
+        raise SystemExit("--rollouts must be >= 1")
     cfg = load_config(RLConfig, rest)
+    upd = {k: v for k, v in (("examples_per_step", a.examples), ("rollouts_per_example", a.rollouts)) if v}
+    if upd:
+        cfg = cfg.model_copy(update={"orchestrator": cfg.orchestrator.model_copy(update=upd)})
     out = Path(cfg.output_dir)
     if a.action == "inspect":
         _print({"queue": scan_queue(resolve_queue_dir(out, cfg.transport)),
                 "policies": stable_steps(resolve_policy_dir(out, cfg.policy_transfer))}, a.json)
         return 0
-    from .inference.policy import create_policy_inference_engine
-    from .orchestrator.rollouts import RLOrchestrator
-    from .orchestrator.runtime import build_prompt_source
-    from .orchestrator.scheduler import _GeneratorAdapter
+    if a.action == "sample":
+        from .orchestrator.runtime import build_prompt_source
 
-    eng = create_policy_inference_engine(cfg)
-    eng.setup()
-    orch = RLOrchestrator(cfg, _GeneratorAdapter(eng), None, build_prompt_source(cfg, 1 << 30))
-    recs = orch.materialize(0)
-    _print({"records": len(recs), "stats": orch.last_stats,
-            "sample": [{"reward": r.reward, "advantage": r.advantage, "tokens": len(r.input_ids or [])}
-                       for r in recs[:8]]}, a.json)
+        src = build_prompt_source(cfg, 1 << 30)
+        prompts = src.take(cfg.orchestrator.examples_per_step or 1)
+        _print({"step": a.step, "prompts": [{"example_id": p_.example_id, "tokens": len(p_.prompt_ids),
+                                             "metadata": p_.metadata} for p_ in prompts]}, a.json)
+        return 0
+    _print(probe_orchestrator(cfg, step=a.step, write=a.action == "materialize"), a.json)
     return 0
 
 
@@ -256,6 +397,16 @@ def _records_file(path: Path) -> Path:
         return path
     side = sorted(path.glob(f"*{TRAIN_SUFFIX}"))
     return side[0] if side else path / "rollouts.jsonl"
+
+
+def _resolve_batch(cfg: RLConfig | None, batch: Path | None, queue_step: int | None) -> Path:
+    if batch is not None:
+        return _records_file(batch)
+    if cfg is None or queue_step is None:
+        raise SystemExit("give a rollout batch path, or --queue-step with a config")
+    from .transport.queue import resolve_queue_dir, step_dir
+
+    return _records_file(step_dir(resolve_queue_dir(Path(cfg.output_dir), cfg.transport), queue_step))
 
 
 def inspect_rollout_batch(path: Path) -> dict[str, Any]:
@@ -284,28 +435,153 @@ def inspect_rollout_batch(path: Path) -> dict[str, Any]:
     return {"rows": len(rows), "tokens": tokens, "issues": issues, "ok": not issues}
 
 
-def _trainer_main(argv: list[str]) -> int:
-    p = argparse.ArgumentParser(prog="wavelet debug trainer")
-    p.add_argument("action", choices=("inspect", "tokens"))
-    p.add_argument("batch", type=Path, help="rollout step directory (or its training-records file)")
-    p.add_argument("--json", action="store_true")
-    p.add_argument("--limit", type=int, default=2)
-    a = p.parse_args(argv)
-    if a.action == "inspect":
-        rep = inspect_rollout_batch(a.batch)
-        _print(rep, a.json)
-        return 0 if rep["ok"] else 1
-    from .data.rl import example_from_payload
+def trainer_logprobs_of_rows(cfg: RLConfig, rows: list[dict[str, Any]], model=None) -> list[list[float]]:
+    """Trainer log-probs (one per trainable token) of rollout rows under the
+    configured model at the sampling temperature: the trainer's own LM-head
+    path, no gradient."""
+    import torch
+
+    from .data.rl import example_from_payload, make_rank_batches
+    from .models.config import resolve_arch
+    from .models.qwen import build_model
+    from .ops import lm_head
+
+    if model is None:
+        model = build_model(resolve_arch(cfg.model.name, cfg.model.arch_overrides or None),
+                            "cuda" if torch.cuda.is_available() else "cpu", None, seed=cfg.seed, with_grad=False,
+                            with_optimizer=False)
+        p = Path(cfg.model.name)
+        if not cfg.model.random_init and p.is_dir() and any(p.glob("*.safetensors")):
+            from .models.hf_io import load_hf_weights
+
+            load_hf_weights(model, p)
+    temp = cfg.inference.sampling.temperature or cfg.inference.default_temperature
+    out = []
+    with torch.no_grad():
+        for row in rows:
+            ex = example_from_payload(row)
+            (b,) = make_rank_batches([ex], max(cfg.data.seq_len, len(ex.input_ids or [])), 0, 1, temp)
+            b = b.to(model.device)
+            ctx = model.batch_ctx(b.base.position_ids, b.base.cu_seqlens, b.base.max_seqlen)
+            h = model.hidden(b.base.input_ids, ctx)
+            tgt = b.base.targets.clamp_min(0)
+            if h.is_cuda:
+                lp, _ = lm_head.logprob_entropy(h, model.head_weight(), tgt, b.temperature, want_entropy=False)
+            else:
+                lp, _ = lm_head.ref.logprob_entropy(model.logits(h), tgt, b.temperature)
+            out.append(lp[b.loss_mask].float().cpu().tolist())
+    return out
+
+
+def runtime_parity_report(path: Path, *, trainer_column: str = "trainer_logprobs", threshold: float = 1e-3,
+                          max_rows: int | None = None, computed: list[list[float]] | None = None) -> dict[str, Any]:
+    """Inference vs trainer log-probs of the trainable tokens of a rollout
+    batch: max / mean absolute difference, rows without either side, and
+    alignment errors; passed when every compared token is within
+    ``threshold``.  The trainer side is the ``trainer_column`` of the rows or,
+    with ``computed``, log-probs the trainer computed for them."""
     from .transport.queue import read_training_records
 
-    rows = [example_from_payload(r) for r in read_training_records(_records_file(a.batch))][: a.limit]
-    out = []
-    for r in rows:
-        lp = r.inference_logprobs or []
-        out.append([{"pos": i, "token": t, "trainable": bool(m), "logprob": lp[i] if i < len(lp) else None}
-                    for i, (t, m) in enumerate(zip(r.input_ids or [], r.loss_mask or []))])
-    _print({"rows": out}, True)
-    return 0
+    rows = read_training_records(path)
+    if max_rows is not None:
+        rows = rows[:max_rows]
+    errors, miss_inf, miss_tr = [], 0, 0
+    n_tok, max_d, sum_d = 0, 0.0, 0.0
+    for i, row in enumerate(rows):
+        k = sum(bool(m) for m in row.get("loss_mask") or [])
+        inf = row.get("inference_logprobs")
+        tr = computed[i] if computed is not None else row.get(trainer_column)
+        if inf is None:
+            miss_inf += 1
+            continue
+        if tr is None:
+            miss_tr += 1
+            continue
+        if len(inf) != k:
+            errors.append({"row": i, "field": "inference_logprobs", "message": "logprob count must match trainable token count"})
+            continue
+        if len(tr) != k:
+            errors.append({"row": i, "field": trainer_column, "message": "trainer logprob count must match trainable token count"})
+            continue
+        for x, y in zip(inf, tr):
+            d = abs(float(x) - float(y))
+            max_d = max(max_d, d)
+            sum_d += d
+            n_tok += 1
+    skip = None
+    if n_tok == 0 and not errors:
+        skip = ("no rows" if not rows else "no inference log-probs" if miss_inf == len(rows)
+                else "no trainer log-probs" if miss_tr else "no trainable tokens")
+    return {"path": str(path), "threshold": threshold, "rows_checked": len(rows), "token_count": n_tok,
+            "max_abs_diff": max_d if n_tok else None, "mean_abs_diff": sum_d / n_tok if n_tok else None,
+            "passed": bool(n_tok and max_d <= threshold and not errors), "skipped": n_tok == 0 and not errors,
+            "skip_reason": skip, "coverage": {"rows_missing_inference_logprobs": miss_inf,
+                                              "rows_missing_trainer_logprobs": miss_tr},
+            "errors": errors}
+
+
+def _trainer_main(argv: list[str]) -> int:
+    from .utils.config import load_config
+
+    p = argparse.ArgumentParser(prog="wavelet debug trainer",
+                                description="Inspect trainer inputs and replay artifacts without training.")
+    p.add_argument("action", choices=("inspect", "tokens", "parity"))
+    p.add_argument("batch", type=Path, nargs="?", default=None,
+                   help="rollout step directory (or its training-records file)")
+    p.add_argument("--queue-step", type=int, default=None)
+    p.add_argument("--json", action="store_true")
+    p.add_argument("--limit", "--max-rows", dest="limit", type=int, default=None)
+    p.add_argument("--trainer-logprobs-column", default="trainer_logprobs")
+    p.add_argument("--threshold", type=float, default=1e-3)
+    p.add_argument("--compute", action="store_true",
+                   help="parity: compute the trainer log-probs with the configured model instead of reading a column")
+    p.add_argument("--write-report", type=Path, default=None)
+    p.add_argument("--write-tokens", type=Path, default=None)
+    a, rest = p.parse_known_args(argv)
+    if a.limit is not None and a.limit < 1:
+        raise SystemExit("--max-rows must be >= 1")
+    if a.threshold < 0:
+        raise SystemExit("--threshold must be >= 0")
+    cfg = load_config(RLConfig, rest) if (rest or a.compute or a.queue_step is not None) else None
+    path = _resolve_batch(cfg, a.batch, a.queue_step)
+    if a.action == "inspect":
+        rep = inspect_rollout_batch(path)
+        code = 0 if rep["ok"] else 1
+    elif a.action == "parity":
+        computed = None
+        if a.compute:
+            from .transport.queue import read_training_records
+
+            rows = read_training_records(path)[: a.limit] if a.limit else read_training_records(path)
+            computed = trainer_logprobs_of_rows(cfg, rows)
+        rep = runtime_parity_report(path, trainer_column=a.trainer_logprobs_column, threshold=a.threshold,
+                                    max_rows=a.limit, computed=computed)
+        code = 0 if (rep["passed"] or rep["skipped"]) else 1
+    else:
+        from .data.rl import example_from_payload
+        from .transport.queue import read_training_records
+
+        rows = [example_from_payload(r) for r in read_training_records(path)][: a.limit or 2]
+        rep = {"rows": []}
+        for r in rows:
+            lp = r.inference_logprobs or []
+            k = 0
+            toks = []
+            for i, (t, m) in enumerate(zip(r.input_ids or [], r.loss_mask or [])):
+                toks.append({"pos": i, "token": t, "trainable": bool(m),
+                             "logprob": (lp[k] if m and k < len(lp) else None)})
+                k += bool(m)
+            rep["rows"].append(toks)
+        if a.write_tokens is not None:
+            a.write_tokens.parent.mkdir(parents=True, exist_ok=True)
+            a.write_tokens.write_text("\n".join(json.dumps(x) for x in rep["rows"]) + "\n")
+            rep = {"rows": len(rep["rows"]), "written": str(a.write_tokens)}
+        code = 0
+    if a.write_report is not None:
+        a.write_report.parent.mkdir(parents=True, exist_ok=True)
+        a.write_report.write_text(json.dumps(rep, indent=2, sort_keys=True, default=str))
+    _print(rep, a.json or a.action == "tokens")
+    return code
 
 
 COMMANDS = {"preflight": (_preflight_main, "Validate cheap RL launch prerequisites"),
