@@ -62,19 +62,66 @@ def test_trace_conversion(tmp_path):
 
 def test_slurm_render_and_nodelist(tmp_path):
     from wavelet_b200.configs.config import RLConfig
-    from wavelet_b200.deployment.slurm import expand_nodelist, render_sbatch, worker_commands
+    from wavelet_b200.deployment.slurm import expand_nodelist, plan_roles, render_sbatch
+    from wavelet_b200.utils.config import load_yaml
 
     assert expand_nodelist("gpu[01-03,07],login1") == ["gpu01", "gpu02", "gpu03", "gpu07", "login1"]
     cfg = RLConfig.model_validate({"output_dir": str(tmp_path), "slurm": {"partition": "p", "time_limit": "1:00:00"},
-                                   "deployment": {"type": "multi_node", "num_train_nodes": 1,
-                                                  "num_inference_nodes": 1, "gpus_per_node": 8},
-                                   "launcher": {"mode": "process"}})
+                                   "deployment": {"type": "multi_node", "num_train_nodes": 2,
+                                                  "num_inference_nodes": 1, "gpus_per_node": 8,
+                                                  "inference_replicas_per_node": 2},
+                                   "launcher": {"mode": "process"}, "max_steps": 3})
     script = render_sbatch(cfg, "rl", ["@", "x.yaml"])
-    assert "#SBATCH --nodes=2" in script and "#SBATCH --partition=p" in script and "slurm-worker rl" in script
-    t = worker_commands(cfg, "rl", ["@", "x.yaml"], 0, ["n0", "n1"])
-    assert "--nproc-per-node=8" in t[0] and "rl-inference" in t[1]
-    i = worker_commands(cfg, "rl", ["@", "x.yaml"], 1, ["n0", "n1"])
-    assert "inference-server" in i[0]
+    assert "#SBATCH --nodes=3" in script and "#SBATCH --partition=p" in script and "slurm-worker rl" in script
+    roles = plan_roles(cfg, "rl", ["n0", "n1", "n2"], tmp_path)
+    names = [r.name for r in roles]
+    assert names == ["inference_server_0", "inference_server_1", "trainer", "rl_inference"]
+    s0, s1, tr, ri = roles
+    assert s0.service and s0.endpoint == "http://n2:8000" and s1.endpoint == "http://n2:8001"
+    assert "--nodelist=n2" in s0.argv and "--gpus-per-task=4" in s0.argv
+    assert "--nodelist=n0,n1" in tr.argv and "--nnodes=2" in tr.argv and "--nproc-per-node=8" in tr.argv
+    assert "--rdzv-endpoint=n0:29500" in tr.argv and "rl-trainer" in tr.argv
+    assert ri.env["CUDA_VISIBLE_DEVICES"] == "" and "srun" not in ri.argv
+    ic = load_yaml(tmp_path / "rl_inference.yaml")
+    assert ic["inference"]["http"]["hosts"] == ["n2", "n2"] and ic["inference"]["http"]["ports"] == [8000, 8001]
+    assert "slurm" not in ic and ic["deployment"]["type"] == "single_node"
+    sc = load_yaml(tmp_path / "inference_server_1.yaml")
+    assert sc["inference"]["http"]["host"] == "0.0.0.0" and sc["inference"]["http"]["port"] == 8001
+    with pytest.raises(RuntimeError, match="needs 3"):
+        plan_roles(cfg, "rl", ["n0", "n1"], tmp_path)
+
+
+def test_slurm_controller_lifecycle(tmp_path):
+    """Servers first, health wait, then jobs; a failing job tears everything
+    down; a server dying before health fails fast; success terminates the
+    servers."""
+    import sys as _sys
+    import time as _time
+
+    from wavelet_b200.deployment.slurm import RoleLaunch, run_roles
+
+    py = _sys.executable
+    server = RoleLaunch("server", [py, "-c", "import time; time.sleep(60)"], service=True, endpoint="http://x:1")
+    ok_job = RoleLaunch("trainer", [py, "-c", "import time; time.sleep(0.3)"])
+    ok_job2 = RoleLaunch("rl_inference", [py, "-c", "pass"])
+    bad_job = RoleLaunch("trainer", [py, "-c", "import sys; sys.exit(3)"])
+    calls = []
+
+    def healthy(urls, t):
+        calls.append(list(urls))
+
+    t0 = _time.monotonic()
+    assert run_roles([server, ok_job, ok_job2], tmp_path / "a", health=healthy, poll=0.05) == 0
+    assert calls == [["http://x:1"]] and _time.monotonic() - t0 < 20
+    assert run_roles([server, bad_job, ok_job2], tmp_path / "b", health=healthy, poll=0.05) == 1
+    dying = RoleLaunch("server", [py, "-c", "import sys; sys.exit(2)"], service=True, endpoint="http://x:1")
+
+    def never(urls, t):
+        _time.sleep(0.1)
+        raise TimeoutError
+
+    assert run_roles([dying, ok_job], tmp_path / "c", health=never, startup_timeout=30, poll=0.05) == 1
+    assert (tmp_path / "a" / "trainer.log").exists()
 
 
 @pytest.mark.integration

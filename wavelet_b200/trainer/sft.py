@@ -146,7 +146,9 @@ class SFTTrainer:
         resume = None
         if c.ckpt is not None:
             resume = pathing.resolve_resume_dir(c.checkpoint_output_dir, c.ckpt.resume_step, c.ckpt.resume_dir)
-        if w.rank == 0:
+        # a SLURM job controller validated the output directory and created the
+        # launch attempt before starting this role (WAVELET_SLURM_OUTPUT_PREPARED)
+        if w.rank == 0 and os.environ.get("WAVELET_SLURM_OUTPUT_PREPARED") != "1":
             pathing.validate_output_dir(out, clean=c.clean_output_dir, resuming=resume is not None,
                                         protected_paths=(c.model.name, c.model.adapter_path))
             attempt = pathing.create_launch_attempt(out)
