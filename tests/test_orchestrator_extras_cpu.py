@@ -117,3 +117,52 @@ def test_live_episode_and_state_server(tmp_path):
     assert c.get("/api/state").json()["step"] == 4
     assert c.get("/api/events", params={"after": 0}).json()["events"][0]["event"] == "batch_published"
     assert c.get("/api/events", params={"after": 1}).json()["events"] == []
+
+
+def test_ray_role_backend_with_a_stand_in_ray(tmp_path, monkeypatch):
+    """launcher.backend=ray: roles run as Ray tasks behind the same poll /
+    terminate surface (a minimal stand-in for the ray module runs the tasks
+    on threads)."""
+    import sys
+    import threading
+    import types
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.orchestrator.launcher import RoleRunner, RoleSpec, wait_for_roles
+
+    calls = {"init": None, "cancel": [], "shutdown": 0}
+
+    class Ref:
+        def __init__(self, fn, args):
+            self.result = None
+            self.t = threading.Thread(target=lambda: setattr(self, "result", fn(*args)), daemon=True)
+            self.t.start()
+
+    fake = types.ModuleType("ray")
+    fake.remote = lambda fn: types.SimpleNamespace(remote=lambda *a: Ref(fn, a))
+    fake.init = lambda **kw: calls.__setitem__("init", kw)
+
+    def wait(refs, timeout=None):
+        for r in refs:
+            r.t.join(timeout)
+        return [r for r in refs if not r.t.is_alive()], [r for r in refs if r.t.is_alive()]
+
+    fake.wait = wait
+    fake.get = lambda r: r.result
+    fake.cancel = lambda r, force=False: calls["cancel"].append(force)
+    fake.shutdown = lambda: calls.__setitem__("shutdown", calls["shutdown"] + 1)
+    monkeypatch.setitem(sys.modules, "ray", fake)
+    cfg = RLConfig.model_validate({"launcher": {"mode": "process", "backend": "ray", "ray_address": "auto"},
+                                   "output_dir": str(tmp_path / "o")})
+    runner = RoleRunner(cfg, tmp_path / "logs")
+    assert calls["init"]["address"] == "auto"
+    py = sys.executable
+    ok = runner.start(RoleSpec("rl-trainer", [py, "-c", "print('hi')"]))
+    bad = runner.start(RoleSpec("rl-inference", [py, "-c", "import sys; sys.exit(4)"]))
+    svc = runner.start(RoleSpec("inference-server-0", [py, "-c", "import time; time.sleep(1.5)"], service=True))
+    assert wait_for_roles([ok, bad], [svc], poll=0.05) == 1
+    assert ok.poll() == 0 and bad.poll() == 4
+    assert False in calls["cancel"]  # the server task was asked to stop
+    assert "hi" in (tmp_path / "logs" / "rl-trainer.log").read_text()
+    runner.close()
+    assert calls["shutdown"] == 1

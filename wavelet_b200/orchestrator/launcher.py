@@ -62,6 +62,86 @@ class RoleProcess:
                 pass
 
 
+def _run_role_subprocess(argv: list[str], env: dict[str, str], log_path: str, cwd: str) -> int:
+    """Body of a Ray task: run one role as a child process group with its log
+    file; a cancelled task (KeyboardInterrupt inside the worker) stops the
+    whole group before returning."""
+    Path(log_path).parent.mkdir(parents=True, exist_ok=True)
+    with open(log_path, "ab") as log:
+        p = subprocess.Popen(argv, env={**os.environ, **env}, stdout=log, stderr=subprocess.STDOUT, cwd=cwd,
+                             start_new_session=True)
+        try:
+            return p.wait()
+        except KeyboardInterrupt:
+            try:
+                os.killpg(p.pid, signal.SIGTERM)
+                p.wait(timeout=10)
+            except Exception:
+                try:
+                    os.killpg(p.pid, signal.SIGKILL)
+                except ProcessLookupError:
+                    pass
+            return 130
+
+
+class RayRoleProcess:
+    """A role running as a Ray task (``launcher.backend: ray``): the same
+    ``poll`` / ``terminate`` surface as ``RoleProcess``, so the supervisor and
+    its failure handling are shared (reference orchestrator/launcher.py:200-262)."""
+
+    def __init__(self, spec: RoleSpec, log_dir: Path, ray_module, remote_fn):
+        self.spec = spec
+        self.ray = ray_module
+        self.log_path = log_dir / f"{spec.name}.log"
+        self.ref = remote_fn.remote(spec.argv, dict(spec.env), str(self.log_path), str(Path.cwd()))
+        self._code = None
+
+    def poll(self):
+        if self._code is not None:
+            return self._code
+        ready, _ = self.ray.wait([self.ref], timeout=0)
+        if not ready:
+            return None
+        self._code = int(self.ray.get(self.ref))
+        return self._code
+
+    def terminate(self, grace: float = 10.0):
+        if self.poll() is not None:
+            return
+        self.ray.cancel(self.ref, force=False)  # interrupts the task, which stops its process group
+        ready, _ = self.ray.wait([self.ref], timeout=grace)
+        if not ready:
+            self.ray.cancel(self.ref, force=True)
+
+
+class RoleRunner:
+    """Starts roles locally (``launcher.backend: local``) or as Ray tasks."""
+
+    def __init__(self, cfg, log_dir: Path):
+        self.log_dir = log_dir
+        self.backend = getattr(cfg.launcher, "backend", "local")
+        self.ray = None
+        if self.backend == "ray":
+            try:
+                import ray
+            except ImportError as exc:
+                raise ImportError("launcher.backend='ray' requires the ray package; install it or use "
+                                  "launcher.backend='local'") from exc
+            self.ray = ray
+            self.remote = ray.remote(_run_role_subprocess)
+            ray.init(address=cfg.launcher.ray_address, runtime_env=cfg.launcher.ray_runtime_env,
+                     ignore_reinit_error=True)
+
+    def start(self, spec: RoleSpec):
+        if self.ray is not None:
+            return RayRoleProcess(spec, self.log_dir, self.ray, self.remote)
+        return RoleProcess(spec, self.log_dir)
+
+    def close(self) -> None:
+        if self.ray is not None:
+            self.ray.shutdown()
+
+
 def wait_for_roles(jobs: list[RoleProcess], services: list[RoleProcess], poll: float = 1.0) -> int:
     """Return 0 when every job exits 0; tear everything down on the first failure."""
     try:
@@ -124,7 +204,8 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
     pathing.write_launch_artifacts(attempt, command="rl", argv=argv)
     dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(cfg))
     services, jobs = build_roles(cfg, attempt)
-    running_services = [RoleProcess(s, attempt.log_dir) for s in services]
+    runner = RoleRunner(cfg, attempt.log_dir)
+    running_services = [runner.start(s) for s in services]
     if running_services:
         from ..inference.client import endpoints, wait_healthy
 
@@ -134,7 +215,7 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
             for s in running_services:
                 s.terminate()
             raise
-    running_jobs = [RoleProcess(j, attempt.log_dir) for j in jobs]
+    running_jobs = [runner.start(j) for j in jobs]
 
     def _sigterm(*_):
         raise KeyboardInterrupt
@@ -146,3 +227,5 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
         for r in running_jobs + running_services:
             r.terminate()
         return 130
+    finally:
+        runner.close()
