@@ -177,3 +177,29 @@ def test_debug_preflight_and_trainer_inspect(tmp_path, capsys):
     (d / "rollouts.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
     rep = inspect_rollout_batch(d)
     assert rep["rows"] == 2 and not rep["ok"] and rep["issues"][0]["row"] == 1
+
+
+def test_dashboard_page_routes_all_answer(tmp_path):
+    """Every API route the single-page dashboard calls answers for a run, and
+    series carry timestamps for the elapsed-time axis."""
+    import re as _re
+
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.dashboard.server import RunRegistry, build_app, default_static_dir
+    from wavelet_b200.dashboard.synth import write_synthetic_run
+
+    write_synthetic_run(tmp_path / "runB", steps=12, ranks=2)
+    c = TestClient(build_app(RunRegistry([tmp_path]), default_static_dir()))
+    page = c.get("/").text
+    used = set(_re.findall(r"\$\{API\}/runs/\$\{encodeURIComponent\(S\.run\)\}/([a-z/]+)", page))
+    assert {"summary", "metrics/keys", "rollouts", "rollouts/rows", "evals", "episodes", "nodes", "logs", "config",
+            "timeline"} <= used | {"rollouts/rows"}
+    for route in sorted(used):
+        params = {"step": 3} if route == "rollouts/rows" else {}
+        if route.endswith("/"):
+            continue
+        assert c.get(f"/api/runs/runB/{route}", params=params).status_code == 200, route
+    s = c.get("/api/runs/runB/series", params={"keys": "loss", "points": 50}).json()
+    assert len(s["times"]) == len(s["steps"]) and s["times"][0]
+    assert c.get("/api/current").json()["run"] == "runB"

@@ -92,7 +92,8 @@ class MetricTable:
             idx = idx[-limit:]
         if points and len(idx) > points:
             idx = _minmax_indices(idx, [np.asarray(self.cols[k]) for k in keys], points)
-        out = {"steps": [None if math.isnan(x) else x for x in steps[idx].tolist()], "series": {}}
+        out = {"steps": [None if math.isnan(x) else x for x in steps[idx].tolist()],
+               "times": [self.times[i] for i in idx.tolist()], "series": {}}
         for k in keys:
             v = np.asarray(self.cols[k])[idx]
             out["series"][k] = [None if math.isnan(x) else x for x in v.tolist()]
