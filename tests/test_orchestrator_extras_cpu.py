@@ -2,6 +2,7 @@
 metrics parsing, agent-trajectory merging, live episodes and the state server."""
 
 import json
+from pathlib import Path
 import threading
 import time
 
@@ -98,18 +99,60 @@ def test_agent_trajectory_merge_and_branch():
 
 
 def test_live_episode_and_state_server(tmp_path):
+    import asyncio
+    import subprocess
+    import sys as _sys
+
     from fastapi.testclient import TestClient
 
-    from wavelet_b200.orchestrator.live import LiveEpisode, episode_abandoned
+    from wavelet_b200.orchestrator import live
+    from wavelet_b200.orchestrator.live import (LiveEpisode, current_episode, episode_abandoned,
+                                                install_environment_hooks, list_episodes, read_episode)
     from wavelet_b200.orchestrator.state_server import OrchestratorRunState, build_state_app
 
-    with LiveEpisode(tmp_path, task="reverse", step=3) as ep:
-        ep.turn(prompt_tokens=10, output_tokens=5)
-    evs = [json.loads(l) for l in (tmp_path / "traces" / "live.jsonl").read_text().splitlines()]
-    assert [e["event"] for e in evs] == ["episode_started", "episode_turn", "episode_finished"]
-    assert not episode_abandoned(evs, ep.id)
-    dead = [{**evs[0], "rollout_id": "x", "pid": 2**22 + 12345}]
-    assert episode_abandoned(dead, "x")
+    with LiveEpisode(tmp_path, "reverse", step=3, example_id="e1") as ep:
+        assert current_episode() is ep
+        ep.event("generation", prompt_tokens=10, output_tokens=5, text="x" * (live.MAX_TEXT + 10))
+    doc = read_episode(tmp_path, ep.id)
+    assert doc["status"] == "completed" and [e["phase"] for e in doc["events"]] == ["episode_started", "generation"]
+    assert doc["events"][1]["text"].endswith("10 more]")
+    assert current_episode() is None
+    with pytest.raises(ValueError):
+        with LiveEpisode(tmp_path, "reverse") as bad:
+            raise ValueError("boom")
+    assert read_episode(tmp_path, bad.id)["status"] == "error" and "boom" in read_episode(tmp_path, bad.id)["error"]
+
+    async def arun():
+        async with LiveEpisode(tmp_path, "async-env") as a:
+            await a.aevent("turn", n=1)
+        return a.id
+
+    aid = asyncio.run(arun())
+    assert read_episode(tmp_path, aid)["status"] == "completed"
+    # an episode whose writer died reads as abandoned (a child process that exits)
+    code = ("import sys; sys.path.insert(0, %r); from wavelet_b200.orchestrator.live import LiveEpisode; "
+            "e = LiveEpisode(%r, 'dead'); e.event('episode_started'); print(e.id)") % (str(Path(__file__).resolve().parents[1]), str(tmp_path))
+    dead_id = subprocess.run([_sys.executable, "-c", code], capture_output=True, text=True).stdout.strip()
+    metas = {m["id"]: m for m in list_episodes(tmp_path)}
+    assert metas[dead_id]["abandoned"] and episode_abandoned(metas[dead_id])
+    assert not metas[ep.id]["abandoned"]
+    # bounded documents and pruning of finished episodes
+    with LiveEpisode(tmp_path, "big") as big:
+        for i in range(live.MAX_EVENTS + 20):
+            big.event("e", i=i)
+    assert len(read_episode(tmp_path, big.id)["events"]) <= live.MAX_EVENTS
+    assert live.prune_finished(tmp_path / "traces" / "live", keep=1) >= 3
+    assert len([m for m in list_episodes(tmp_path) if m["status"] != "running" or m["abandoned"]]) == 1
+
+    class Env:
+        def score(self, x):
+            return 2.0 * x
+
+    env = install_environment_hooks(Env())
+    with LiveEpisode(tmp_path, "hooked") as hk:
+        assert env.score(1.5) == 3.0
+    assert [e["phase"] for e in read_episode(tmp_path, hk.id)["events"]][-2:] == ["score_started", "score_finished"]
+    assert env.score(1.0) == 2.0  # outside an episode: untouched
     st = OrchestratorRunState(tmp_path)
     st.update(status="running", step=4)
     st.event("batch_published", step=4)

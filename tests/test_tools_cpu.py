@@ -203,3 +203,35 @@ def test_dashboard_page_routes_all_answer(tmp_path):
     s = c.get("/api/runs/runB/series", params={"keys": "loss", "points": 50}).json()
     assert len(s["times"]) == len(s["steps"]) and s["times"][0]
     assert c.get("/api/current").json()["run"] == "runB"
+
+
+def test_orchestrator_live_episodes_reach_the_dashboard(tmp_path):
+    """With orchestrator.live_traces on, each prompt group being generated has
+    a live episode document; the dashboard lists and serves them."""
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.dashboard.server import RunRegistry, build_app, default_static_dir
+    from wavelet_b200.dashboard.synth import write_synthetic_run
+    from wavelet_b200.orchestrator.rollouts import PromptRecord, RLOrchestrator
+
+    run = tmp_path / "runL"
+    write_synthetic_run(run, steps=3, ranks=1)
+    cfg = RLConfig.model_validate({"output_dir": str(run),
+                                   "orchestrator": {"examples_per_step": 2, "rollouts_per_example": 2}})
+
+    orch = RLOrchestrator(cfg, engine=None, sender=None, prompts=None)
+    prompts = [PromptRecord([1, 2, 3], example_id="p0"), PromptRecord([4, 5], example_id="p1")]
+    eps = orch._live_episodes(prompts, 7)
+    assert len(eps) == 2
+    for ep in eps:
+        ep.finish("completed")
+    c = TestClient(build_app(RunRegistry([tmp_path]), default_static_dir()))
+    listed = c.get("/api/runs/runL/live").json()["episodes"]
+    assert {e["example_id"] for e in listed} == {"p0", "p1"} and all(e["step"] == 7 for e in listed)
+    doc = c.get(f"/api/runs/runL/live/{listed[0]['id']}").json()
+    assert doc["events"][0]["phase"] == "episode_started"
+    assert c.get("/api/runs/runL/live/nothere").status_code == 404
+    off = RLOrchestrator(RLConfig.model_validate({"output_dir": str(run), "orchestrator": {"live_traces": False}}),
+                         engine=None, sender=None, prompts=None)
+    assert off._live_episodes(prompts, 8) == []

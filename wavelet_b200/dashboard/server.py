@@ -230,6 +230,21 @@ def build_app(registry: RunRegistry, static_dir: Path | None = None):
         steps = [b["step"] for b in r.rollouts() if b["stable"]]
         return r.rollout_rows(steps[-1], 0, limit) if steps else {"rows": [], "total": 0}
 
+    @app.get(API + "/runs/{rid}/live")
+    def live_list(rid: str, limit: int = Query(200, ge=1, le=2000)):
+        from ..orchestrator.live import list_episodes
+
+        return {"episodes": list_episodes(reader(rid).path, limit)}
+
+    @app.get(API + "/runs/{rid}/live/{eid}")
+    def live_one(rid: str, eid: str):
+        from ..orchestrator.live import read_episode
+
+        doc = read_episode(reader(rid).path, eid)
+        if doc is None:
+            raise HTTPException(404, eid)
+        return doc
+
     @app.get(API + "/runs/{rid}/queue")
     def queue(rid: str):
         return reader(rid).queue()

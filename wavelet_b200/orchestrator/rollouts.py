@@ -83,13 +83,41 @@ class RLOrchestrator:
             return_sampling_mask=self.cfg.sampling_mask_required(),
         )
 
+    def _live_episodes(self, prompts: list[PromptRecord], step: int) -> list:
+        """One live trace document per prompt group while it is generated
+        (orchestrator.live_traces; read by the dashboard's live view)."""
+        o = getattr(self.cfg, "orchestrator", None)
+        out_dir = getattr(self.cfg, "output_dir", None)
+        if o is None or not getattr(o, "live_traces", False) or out_dir is None:
+            return []
+        from .live import LiveEpisode
+
+        eps = []
+        for p in prompts:
+            ep = LiveEpisode(out_dir, str(p.metadata.get("task") or p.metadata.get("env") or "prompts"), "train",
+                             step=step, example_id=p.example_id)
+            ep.event("episode_started", prompt_tokens=len(p.prompt_ids))
+            eps.append(ep)
+        return eps
+
     def generate_records(self, prompts: list[PromptRecord], step: int) -> list[RLExample]:
         params = self._sampling()
         if params.seed is not None:
             params.seed = params.seed + step
+        eps = self._live_episodes(prompts, step)
         t0 = time.perf_counter()
-        comps = self.engine.generate([p.prompt_ids for p in prompts], params)
+        try:
+            comps = self.engine.generate([p.prompt_ids for p in prompts], params)
+        except BaseException as e:
+            for ep in eps:
+                ep.finish("error", error=e)
+            raise
         gen_s = time.perf_counter() - t0
+        for i, ep in enumerate(eps):
+            mine = [c for c in comps if c.prompt_index == i]
+            ep.event("generation_finished", samples=len(mine), completion_tokens=[len(c.token_ids) for c in mine],
+                     finish_reasons=[c.finish_reason for c in mine], seconds=gen_s)
+            ep.finish("completed")
         recs = []
         for c in comps:
             p = prompts[c.prompt_index]
