@@ -638,6 +638,12 @@ class RLPolicyTransferConfig(ConfigModel):
     nccl_inference_world_size: int = Field(default=1, ge=1)
     nccl_rank_offset: int = Field(default=1, ge=1)
     nccl_dtype: Literal["model", "bfloat16", "float32"] = "bfloat16"
+    # device transfer between processes of one node: push over peer memory
+    # into `peer_slots` receive buffers per generator (2: the trainer never
+    # waits; 1: half the generator memory, a load may copy twice); off or
+    # across nodes: the NCCL broadcast
+    peer: bool = True
+    peer_slots: int = Field(default=2, ge=1, le=2)
 
 
 class RLSamplingConfig(_LegacySampling):

@@ -8,6 +8,7 @@
 #include "attention.h"
 #include "comm.h"
 #include "moe.h"
+#include "policy.h"
 #include "decode.h"
 #include "gemm.h"
 #include "kernels.h"
@@ -270,6 +271,57 @@ void gather_from_peers(const std::vector<int64_t>& src, int64_t world, int64_t o
   check_bf16(dst, "dst");
   WB_CHECK(dst.is_contiguous() && dst.numel() >= n * world, "gather_from_peers: dst too small");
   wb::gather_from_peers(peers_of(src, (int)world), (int)world, off, n, dst.data_ptr(), cur_stream());
+}
+
+// Policy push: seg is a host int64 table [nseg, 6] (src_off, dst_off, rows,
+// row_len, src_stride, dst_stride); every block is checked against the source
+// tensor and dst_numel here, before anything is launched.  Returns the vector
+// width used (8 / 4 when every term is aligned to it, else 1).
+int64_t policy_push(const at::Tensor& src, const std::vector<int64_t>& dst, int64_t dst_numel, bool dst_bf16,
+                    const at::Tensor& seg) {
+  check_cuda(src, "src");
+  WB_CHECK(src.is_contiguous() && (src.scalar_type() == at::kBFloat16 || src.scalar_type() == at::kFloat),
+           "policy_push: src must be a contiguous bf16 / fp32 tensor");
+  WB_CHECK(!seg.is_cuda() && seg.scalar_type() == at::kLong && seg.dim() == 2 && seg.size(1) == 6 && seg.is_contiguous(),
+           "policy_push: seg must be a contiguous host int64 [nseg, 6] table");
+  const int nd = (int)dst.size();
+  WB_CHECK(nd >= 1 && nd <= wb::kMaxPeers, "policy_push: 1..8 destinations");
+  const bool src_bf16 = src.scalar_type() == at::kBFloat16;
+  const int64_t n = seg.size(0);
+  if (n == 0) return 0;
+  const int64_t* g = seg.data_ptr<int64_t>();
+  const int want = (src_bf16 || dst_bf16) ? 8 : 4;  // 16-byte loads and stores on both sides
+  bool aligned = reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0;
+  for (int64_t p : dst) aligned = aligned && p % 16 == 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t* r = g + 6 * i;
+    WB_CHECK(r[0] >= 0 && r[1] >= 0 && r[2] >= 1 && r[3] >= 1 && r[4] >= r[3] && r[5] >= r[3],
+             "policy_push: segment " + std::to_string(i) + " has a bad shape");
+    WB_CHECK(r[0] + (r[2] - 1) * r[4] + r[3] <= src.numel(), "policy_push: segment " + std::to_string(i) + " reads past src");
+    WB_CHECK(r[1] + (r[2] - 1) * r[5] + r[3] <= dst_numel, "policy_push: segment " + std::to_string(i) + " writes past dst");
+    for (int k = 0; k < 6; ++k)
+      if (k != 2 && r[k] % want) aligned = false;
+  }
+  const int vec = aligned ? want : 1;
+  auto prefix = at::empty({n}, at::TensorOptions().dtype(at::kLong));
+  int64_t* pf = prefix.data_ptr<int64_t>();
+  int64_t total = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    pf[i] = total;
+    total += g[6 * i + 2] * (g[6 * i + 3] / vec);
+  }
+  auto dev = src.device();
+  auto seg_d = seg.to(dev);
+  auto pre_d = prefix.to(dev);
+  wb::policy_push(src.data_ptr(), src_bf16 ? 1 : 0, peers_of(dst, nd), nd, dst_bf16 ? 1 : 0, seg_d.data_ptr<int64_t>(),
+                  pre_d.data_ptr<int64_t>(), (int)n, total, vec, cur_stream());
+  return vec;
+}
+
+void policy_signal(const std::vector<int64_t>& pads, int64_t word, int64_t value) {
+  WB_CHECK(word >= 0 && word < wb::kPadWords, "policy_signal: word out of the pad");
+  wb::policy_signal(peers_of(pads, (int)pads.size()), (int)pads.size(), (int)word, static_cast<uint32_t>(value),
+                    cur_stream());
 }
 
 // Fused GEMM -> all-reduce / reduce-scatter, GEMM half: the tcgen05 GEMM of
@@ -916,6 +968,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_copy_rows", &moe_copy_rows);
   m.def("moe_zero_pad", &moe_zero_pad);
   m.def("moe_put_counts", &moe_put_counts);
+  m.def("policy_push", &policy_push, py::arg("src"), py::arg("dst"), py::arg("dst_numel"), py::arg("dst_bf16"),
+        py::arg("seg"));
+  m.def("policy_signal", &policy_signal);
   m.def("launch_count", []() { return wb::launch_count(); },
         "kernels launched by this library since it was loaded (every launch site counts one)");
   m.def("note_launches", [](int64_t n) { wb::note_launches(n); },

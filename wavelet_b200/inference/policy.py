@@ -84,6 +84,17 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         self.tokenizer = tokenizer
         self.generator = None
         self.paused = False
+        self.device_receiver = None  # transport.policy.DevicePolicyReceiver of a separate generator process
+
+    def attach_device_receiver(self, index: int = 0):
+        """Receive device policy updates (``policy_transfer.type: nccl``) in
+        this generator process: announces the peer receive slots now so the
+        trainer can find them."""
+        from ..transport.policy import DevicePolicyReceiver
+
+        self.device_receiver = DevicePolicyReceiver(self.model, self.config.output_dir, self.config.policy_transfer,
+                                                    index)
+        return self.device_receiver
 
     def setup(self) -> None:
         import torch
@@ -106,8 +117,14 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         from ..transport.policy import load_policy_into
 
         if policy_dir is not None and Path(policy_dir).exists() and (Path(policy_dir) / "policy.json").exists():
-            load_policy_into(self.model, Path(policy_dir))
+            meta = load_policy_into(self.model, Path(policy_dir), self.device_receiver, step)
+            step = int(meta.get("loaded_step", step))  # a peer update may already hold a newer step
         self.policy_step = step
+
+    def close(self) -> None:
+        if self.device_receiver is not None:
+            self.device_receiver.close()
+            self.device_receiver = None
 
     def sampling(self, overrides: dict[str, Any] | None = None):
         from .engine import SamplingParams

@@ -76,8 +76,13 @@ def build_app(config: RLConfig, engine=None):
     if engine is None:
         engine = NativePolicyInferenceEngine(config, tokenizer=tok)
         engine.setup()
+        if config.policy_transfer.type == "nccl":
+            import os
+
+            engine.attach_device_receiver(int(os.environ.get("WAVELET_INFERENCE_REPLICA", "0")))
     gate = GenerationGate()
     app = FastAPI(title="wavelet inference server")
+    app.state.engine = engine
     state: dict[str, Any] = {"started_at": time.time(), "requests": 0, "generated_tokens": 0, "sleeping": False}
     lock = threading.Lock()
 
@@ -147,9 +152,21 @@ def build_app(config: RLConfig, engine=None):
         return {"status": "loaded", "policy_step": step}
 
     @app.post("/init_broadcaster")
-    def init_broadcaster(payload: dict[str, Any]):
-        state["broadcaster"] = payload
-        return {"status": "ok", "protocol": "flat_v1"}
+    def init_broadcaster(payload: dict[str, Any] | None = None):
+        """Device transfer setup: the receive slots of this generator (peer
+        path) or the NCCL group coordinates of the fallback."""
+        rec = getattr(engine, "device_receiver", None)
+        if rec is None and config.policy_transfer.type == "nccl" and hasattr(engine, "attach_device_receiver"):
+            rec = engine.attach_device_receiver(int((payload or {}).get("index", 0)))
+        if rec is None:
+            return {"status": "off"}
+        pt = config.policy_transfer
+        out = {"status": "ok", "protocols": ["peer_v1", "flat_v1"] if rec.peer is not None else ["flat_v1"],
+               "nccl": {"host": pt.nccl_host, "port": pt.nccl_port, "rank": pt.nccl_rank_offset + rec.index,
+                        "world_size": 1 + pt.nccl_inference_world_size}}
+        if rec.peer is not None:
+            out["peer"] = {"receiver": str(rec.peer.path), "slots": rec.peer.slots, "epochs": rec.peer.epochs()}
+        return out
 
     @app.post("/annotate")
     def annotate(payload: dict[str, Any]):
@@ -224,7 +241,10 @@ def main(argv: list[str] | None = None) -> int:
     import uvicorn
 
     app = build_app(cfg)
-    uvicorn.run(app, host=cfg.inference.http.host, port=cfg.inference.http.port, log_level="warning")
+    try:
+        uvicorn.run(app, host=cfg.inference.http.host, port=cfg.inference.http.port, log_level="warning")
+    finally:
+        app.state.engine.close()  # releases the device policy receive slots
     return 0
 
 

@@ -26,7 +26,7 @@ CSRC = _PKG / "csrc"
 BUILD_DIR = _PKG / "_build"
 NAME = "wb_C"
 
-SOURCES = ["bindings.cpp", "runtime.cu", "gemm.cu", "kernels.cu", "attention.cu", "attention_noalloc.cu", "decode.cu", "comm.cu", "moe.cu"]
+SOURCES = ["bindings.cpp", "runtime.cu", "gemm.cu", "kernels.cu", "attention.cu", "attention_noalloc.cu", "decode.cu", "comm.cu", "moe.cu", "policy.cu"]
 
 CUDA_FLAGS = [
     "-gencode=arch=compute_100a,code=sm_100a",

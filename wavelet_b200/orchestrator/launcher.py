@@ -165,6 +165,22 @@ def wait_for_roles(jobs: list[RoleProcess], services: list[RoleProcess], poll: f
 def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executable) -> tuple[list[RoleSpec], list[RoleSpec]]:
     pl = plan(cfg)
     base = config_to_plain(cfg)
+    device_transfer = cfg.policy_transfer.type == "nccl" and cfg.inference.mode == "vllm_http"
+    if device_transfer:
+        # one generator process per replica receives the device policy updates
+        base["policy_transfer"] = {**base["policy_transfer"], "nccl_inference_world_size": len(pl.ports)}
+    every = list(dict.fromkeys(pl.trainer_devices + [d for g in pl.inference_devices for d in g]))
+
+    def visible(own: list[str]) -> dict[str, str]:
+        """The role's own GPUs first (its cuda:0..); with device policy
+        transfer every other GPU of the placement stays visible too, because
+        a CUDA IPC handle only opens in a process that sees the GPU holding
+        the memory."""
+        if not own:
+            return {}
+        devs = own + [d for d in every if d not in own] if device_transfer and cfg.policy_transfer.peer else own
+        return {"CUDA_VISIBLE_DEVICES": ",".join(devs)}
+
     services: list[RoleSpec] = []
     if cfg.inference.mode == "vllm_http":
         for r, (devs, port) in enumerate(zip(pl.inference_devices, pl.ports)):
@@ -173,7 +189,7 @@ def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executabl
             path = attempt.config_dir / f"inference_server_{r}.yaml"
             dump_yaml(path, c)
             services.append(RoleSpec(f"inference-server-{r}", [python, "-m", "wavelet_b200", "inference-server", "@", str(path)],
-                                     {"CUDA_VISIBLE_DEVICES": ",".join(devs)} if devs else {}, service=True))
+                                     {**visible(devs), "WAVELET_INFERENCE_REPLICA": str(r)}, service=True))
     trainer_cfg = attempt.config_dir / "rl_trainer.yaml"
     dump_yaml(trainer_cfg, base)
     n = len(pl.trainer_devices) or cfg.launcher.trainer_num_processes
@@ -181,7 +197,7 @@ def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executabl
     trainer_argv = ([python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
                      "--master-addr=127.0.0.1", f"--master-port={port}", "-m", "wavelet_b200", "rl-trainer", "@", str(trainer_cfg)]
                     if n > 1 else [python, "-m", "wavelet_b200", "rl-trainer", "@", str(trainer_cfg)])
-    env_t = {"CUDA_VISIBLE_DEVICES": ",".join(pl.trainer_devices)} if pl.trainer_devices else {}
+    env_t = visible(pl.trainer_devices)
     env_t.update(cfg.launcher.env_vars.for_role("trainer"))
     inf_cfg = dict(base)
     inf_cfg["inference"] = {**base["inference"], "http": {**base["inference"]["http"], "ports": pl.ports,

@@ -124,7 +124,8 @@ class RLTrainer:
 
         # with streamed chunks, queue step q holds chunk q % C of optimizer step q // C
         self.receiver = FileSystemRolloutReceiver(out, c.transport, start_step=self.step * chunks_per_step(c))
-        self.exporter = PolicyExporter(out, c.policy_transfer, rank=w.rank)
+        self.exporter = PolicyExporter(out, c.policy_transfer, rank=w.rank, world=w.world_size,
+                                       barrier=dist.barrier if w.world_size > 1 and dist.is_initialized() else None)
         self.perf = PerfTracker(arch, w.device)
         self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
         return self
@@ -442,6 +443,7 @@ class RLTrainer:
         finally:
             if self.ckpt is not None:
                 self.ckpt.wait()
+            self.exporter.close()
             self.monitor.finish(status=status, step=self.step)
 
 
