@@ -194,3 +194,37 @@ def test_nccl_fallback_broadcast_between_processes(tmp_path):
     a, b = torch.load(f"{res}.0"), torch.load(f"{res}.1")
     assert a["mode"] == "nccl" and b["step"] == 5
     torch.testing.assert_close(b["w"], a["w"], rtol=0, atol=0)
+
+
+def test_launcher_keeps_every_gpu_visible_for_device_transfer(tmp_path):
+    """Device transfer between processes: each role sees its own GPUs first
+    and every other GPU of the placement (an IPC handle opens only where the
+    owning GPU is visible); every generator knows its replica index and the
+    trainer expects one receiver per replica."""
+    import yaml
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.orchestrator.launcher import build_roles
+    from wavelet_b200.utils.pathing import LaunchAttempt
+
+    def roles(transfer):
+        cfg = RLConfig.model_validate({
+            "output_dir": str(tmp_path / "o"), "policy_transfer": {"type": transfer},
+            "inference": {"mode": "vllm_http"},
+            "launcher": {"mode": "process", "trainer_num_processes": 2, "inference_num_replicas": 2,
+                         "trainer_cuda_visible_devices": "0,1", "inference_cuda_visible_devices": "2,3"}})
+        att = LaunchAttempt(tmp_path / "a", tmp_path / "a" / "cfg", tmp_path / "a" / "logs")
+        att.config_dir.mkdir(parents=True, exist_ok=True)
+        return build_roles(cfg, att)
+
+    services, main = roles("nccl")
+    envs = {r.name: r.env for r in services + main}
+    assert envs["inference-server-0"]["CUDA_VISIBLE_DEVICES"] == "2,0,1,3"
+    assert envs["inference-server-1"]["CUDA_VISIBLE_DEVICES"] == "3,0,1,2"
+    assert envs["inference-server-1"]["WAVELET_INFERENCE_REPLICA"] == "1"
+    tr = [r for r in main if r.name == "rl-trainer"][0]
+    assert tr.env["CUDA_VISIBLE_DEVICES"] == "0,1,2,3"
+    conf = yaml.safe_load((tmp_path / "a" / "cfg" / "rl_trainer.yaml").read_text())
+    assert conf["policy_transfer"]["nccl_inference_world_size"] == 2
+    services, main = roles("filesystem")
+    assert {r.name: r.env for r in services}["inference-server-1"]["CUDA_VISIBLE_DEVICES"] == "3"
