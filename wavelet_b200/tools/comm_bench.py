@@ -19,6 +19,11 @@ Cases:
            + combine over peer memory vs NCCL all-to-all (transfers only)
   refresh  expert policy refresh: pull-gather of every rank's expert shard
            into the full tensor vs NCCL all-gather
+  policy   split-placement policy transfer (--model shape): the first half of
+           the ranks are trainer replicas, the second half generators; the
+           peer push of every trainer rank's share into every generator's
+           receive slot vs an NCCL broadcast of the flat buffer from trainer
+           rank 0 (the reference's transport), plus the generator's slot load
 """
 
 from __future__ import annotations
@@ -184,7 +189,78 @@ def refresh(a, fab, rank, world) -> list[dict]:
              "speedup_vs_nccl": nccl_ms / fused_ms, "roofline_ms": roof, "frac_of_roofline": roof / fused_ms}]
 
 
-CASES = {"tp-ar": tp_ar, "optim": optim, "ep": ep, "refresh": refresh}
+def policy(a, fab, rank, world) -> list[dict]:
+    import tempfile
+
+    from ..models.config import resolve_arch
+    from ..models.qwen import build_model
+    from ..transport.peer_policy import PeerPolicyReceiver, PeerPolicySender, used_numel
+
+    if world < 2 or world % 2:
+        raise ValueError("the policy case needs an even world size (trainers + generators)")
+    T = world // 2
+    trainer = rank < T
+    tgroup = dist.new_group(list(range(T)))
+    bgroup = dist.new_group([0] + list(range(T, world)))  # NCCL baseline: trainer rank 0 + generators
+    m = build_model(resolve_arch(a.model), torch.device("cuda", torch.cuda.current_device()), torch.bfloat16,
+                    seed=0 if trainer else 1, with_grad=False, with_optimizer=False)
+    n = used_numel(m.flat)
+    root = [tempfile.mkdtemp(prefix="wb_policy_bench_") if rank == 0 else None]
+    dist.broadcast_object_list(root, src=0)
+    rec = None if trainer else PeerPolicyReceiver(m, root[0], rank - T, slots=2)
+    dist.barrier()
+    snd = (PeerPolicySender(m, root[0], rank=rank, world=T, expect=world - T, timeout_s=60,
+                            barrier=lambda: dist.barrier(group=tgroup)) if trainer else None)
+    kern, proto = [], []
+    for step in range(3 + a.iters):
+        dist.barrier()
+        if trainer:
+            info = snd.push(step)
+            if step >= 3:
+                kern.append(info["kernel_ms"])
+                proto.append(1e3 * info["push_seconds"])
+    dist.barrier()
+    load_ms = 0.0
+    if not trainer:
+        rec.load(2 + a.iters, timeout_s=60)
+    # every generator now holds trainer rank 0's weights: compare per-parameter sums
+    sums = torch.stack([m.flat.view(nm).float().sum() for nm in m.flat.names()])
+    every = [torch.empty_like(sums) for _ in range(world)]
+    dist.all_gather(every, sums)
+    match = all(torch.equal(every[0], every[g]) for g in range(T, world))
+    if not trainer:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.iters):
+            m.flat.compute.copy_(rec.bufs[0])
+        e1.record()
+        torch.cuda.synchronize()
+        load_ms = e0.elapsed_time(e1) / a.iters
+    stats = torch.tensor([sum(kern) / len(kern) if kern else 0.0, sum(proto) / len(proto) if proto else 0.0,
+                          load_ms], device="cuda")
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    buf = m.flat.compute[:n]
+
+    def bcast():
+        if rank == 0 or not trainer:
+            dist.broadcast(buf, src=0, group=bgroup)
+
+    nccl_ms = _time(bcast, a.iters)
+    if snd is not None:
+        snd.close()
+    dist.barrier()
+    if rec is not None:
+        rec.close()
+    G = world - T
+    nbytes = n * 2
+    roof = _roof(nvl=nbytes * max(G / T, 1.0))  # a generator's ingress, or a trainer rank's egress
+    return [{"case": "policy", "model": a.model, "bytes": nbytes, "trainers": T, "generators": G,
+             "push_kernel_ms": float(stats[0]), "push_protocol_ms": float(stats[1]), "nccl_broadcast_ms": nccl_ms,
+             "generator_load_ms": float(stats[2]), "weights_match": match, "roofline_ms": roof, "frac_of_roofline": roof / float(stats[0]),
+             "speedup_vs_nccl": nccl_ms / float(stats[0])}]
+
+
+CASES = {"tp-ar": tp_ar, "optim": optim, "ep": ep, "refresh": refresh, "policy": policy}
 
 
 def main(argv: list[str] | None = None) -> int:
@@ -193,6 +269,7 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--params", type=int, default=1 << 30)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--model", default="qwen3-4b", help="architecture of the policy case")
     a = ap.parse_args(argv)
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", rank))

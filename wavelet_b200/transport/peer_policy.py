@@ -382,12 +382,16 @@ class PeerPolicySender:
             self._signal(k, 0)  # the slot is about to change: no generator starts copying it
         self.barrier()
         src = self._sources()
-        for name, segs in self.segs.items():
-            if self.dev.type == "cuda":
-                from .. import ops
+        cuda = self.dev.type == "cuda"
+        if cuda:
+            from .. import ops
 
+            m = ops.ext()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            ev[0].record()
+        for name, segs in self.segs.items():
+            if cuda:
                 table = torch.tensor(segs, dtype=torch.int64).reshape(-1, 6)
-                m = ops.ext()
                 for i in range(0, len(self.dests), 8):
                     group = self.dests[i:i + 8]
                     m.policy_push(src[name], [d.slots[k] for d in group], self.dst_numel,
@@ -395,14 +399,18 @@ class PeerPolicySender:
             else:
                 for d in self.dests:
                     apply_segments(src[name], segs, d.slots[k])
-        if self.dev.type == "cuda":
+        kernel_ms = 0.0
+        if cuda:
+            ev[1].record()
             torch.cuda.synchronize(self.dev)
+            kernel_ms = ev[0].elapsed_time(ev[1])
         self.barrier()
         if self.rank == 0:
             self._signal(k, e)
         self.push_seconds = time.perf_counter() - t0
         return {"protocol": PROTOCOL, "slot": k, "epoch": e, "receivers": len(self.dests),
-                "bytes_per_receiver_this_rank": self.bytes, "push_seconds": self.push_seconds}
+                "bytes_per_receiver_this_rank": self.bytes, "kernel_ms": kernel_ms,
+                "push_seconds": self.push_seconds}
 
     def close(self) -> None:
         if self.dev.type == "cuda":
