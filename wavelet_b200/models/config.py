@@ -239,13 +239,33 @@ TINY_DEEPSEEK_V4 = dict(
     n_routed_experts=4, num_experts_per_tok=2, num_hash_layers=1, hc_mult=2, max_position_embeddings=4096)
 
 
+# Small transformers configs of architectures without a native decoder (the
+# generic Hugging Face path, models/hf_generic.py).
+GENERIC_PRESETS: dict[str, dict[str, Any]] = {
+    "tiny-llama": dict(model_type="llama", vocab_size=1024, hidden_size=128, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2, intermediate_size=256,
+                       max_position_embeddings=4096, rms_norm_eps=1e-6, rope_theta=10000.0,
+                       tie_word_embeddings=False),
+    "tiny-mistral": dict(model_type="mistral", vocab_size=1024, hidden_size=128, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=2, intermediate_size=256,
+                         max_position_embeddings=4096, rms_norm_eps=1e-6, rope_theta=10000.0,
+                         tie_word_embeddings=True, sliding_window=None),
+}
+
+
 def resolve_arch(name: str, overrides: dict[str, Any] | None = None) -> ArchConfig:
-    """Resolve a model name: preset, alias, a local HF dir, or a config.json path."""
+    """Resolve a model name: preset, alias, a local HF dir, or a config.json
+    path.  A config.json of an architecture without a native decoder gives an
+    ``HFGenericConfig`` (trained through the transformers module)."""
     key = ALIASES.get(name, name)
     if key == "tiny-deepseek-v4":
         from .deepseek_v4.config import DeepseekV4Config
 
         return DeepseekV4Config(**{**TINY_DEEPSEEK_V4, **(overrides or {})})
+    if key in GENERIC_PRESETS:
+        from .hf_generic import HFGenericConfig
+
+        return HFGenericConfig({**GENERIC_PRESETS[key], **(overrides or {})})
     if key in PRESETS:
         cfg = PRESETS[key]
     else:
@@ -259,6 +279,10 @@ def resolve_arch(name: str, overrides: dict[str, Any] | None = None) -> ArchConf
 
                 cfg = DeepseekV4Config.from_dict(d)
                 return DeepseekV4Config.from_dict({**cfg.to_dict(), **(overrides or {})}) if overrides else cfg
+            if d.get("model_type", "qwen3") not in ("qwen2", "qwen3", "qwen3_moe") and "model_type" in d:
+                from .hf_generic import HFGenericConfig
+
+                return HFGenericConfig({**d, **(overrides or {})}, source=str(p.parent))
             cfg = from_hf_config(d)
         else:
             raise ValueError(

@@ -30,6 +30,8 @@ import torch
 
 
 def hf_state_dict(model) -> dict[str, torch.Tensor]:
+    if hasattr(model, "hf_state_dict"):  # a transformers module: its own names
+        return model.hf_state_dict()
     cfg = model.cfg
     f = model.flat
     q, kv = cfg.q_dim, cfg.kv_dim
@@ -101,6 +103,9 @@ def internal_from_hf(cfg, hf: dict[str, torch.Tensor]) -> dict[str, torch.Tensor
 def load_hf_weights(model, path: Path) -> None:
     from safetensors.torch import load_file
 
+    if getattr(model.cfg, "generic_hf", False):  # a transformers module: its own checkpoint names
+        model.load_pretrained(path)
+        return
     if hasattr(model, "load_pretrained"):  # eager DeepSeek-V4: native checkpoint directory
         cfg_file = Path(path) / "config.json"
         if cfg_file.exists() and json.loads(cfg_file.read_text()).get("wavelet_checkpoint_format") is None:

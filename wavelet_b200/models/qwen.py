@@ -432,6 +432,13 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
         dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     from .deepseek_v4.config import DeepseekV4Config
 
+    if getattr(cfg, "generic_hf", False):
+        if lora is not None or load_in_4bit or ep or tp or fabric is not None or ep_fabric is not None:
+            raise NotImplementedError("Hugging Face models without a native decoder train with data parallelism "
+                                      "only (no LoRA / QLoRA, tensor or expert parallelism, peer fabric)")
+        from .hf_generic import HFCausalLMTrainable
+
+        return HFCausalLMTrainable(cfg, device, dtype, dp_rank, dp_world, seed, init, with_grad, with_optimizer)
     if isinstance(cfg, DeepseekV4Config):
         if lora is not None or load_in_4bit or ep or tp or fabric is not None or ep_fabric is not None:
             raise NotImplementedError("the eager DeepSeek-V4 model trains with data parallelism only "

@@ -259,7 +259,7 @@ class RLTrainer:
                                      rl_loss_fn=self.loss_fn, present=present, sync=False,
                                      seg=seg, n_seq=n_seq, seq_counts=seq_counts)
             loss.backward()
-            if not h.is_cuda:
+            if not h.is_cuda or getattr(m, "eager", False):
                 m.collect_cpu_grads()
             loss_total += loss.detach().float()
             if any_tok:
