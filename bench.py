@@ -59,6 +59,9 @@ def parse():
                    help="reference arm: model.attn_implementation (the reference's default 'auto' picks FA2 here)")
     p.add_argument("--comm", default="fabric", choices=["fabric", "nccl"],
                    help="optimizer-step collectives: fused peer-memory kernels (fabric) or NCCL")
+    p.add_argument("--shard-params", action="store_true",
+                   help="ZeRO-3: bf16 weights sharded over the data-parallel ranks, gathered layer by layer "
+                        "(fsdp.shard_params); the optimizer collectives then run per layer over NCCL")
     return p.parse_args()
 
 
@@ -354,7 +357,10 @@ def main():
 
     overrides = {"num_layers": args.layers} if args.layers else None
     cfg = resolve_arch(args.model, overrides)
-    fabric = maybe_fabric(dp, dp_rank, dev, group=groups.dp) if args.comm == "fabric" else None
+    zero3 = args.shard_params
+    if zero3 and (qlora or tp > 1):
+        raise SystemExit("--shard-params runs the dense workload data-parallel only")
+    fabric = maybe_fabric(dp, dp_rank, dev, group=groups.dp) if (args.comm == "fabric" and not zero3) else None
     norm_fabric = Fabric(rank, N, dev) if (fabric is not None and tp > 1) else None
     tp_fabric = Fabric(groups.tp_rank, tp, dev, group=groups.tp) if (tp > 1 and args.comm == "fabric") else None
     lora = None
@@ -364,7 +370,12 @@ def main():
         lora = SimpleNamespace(rank=16, alpha=32.0, dropout=0.0, target_modules=[
             "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"])
     model = build_model(cfg, dev, torch.bfloat16, dp_rank=dp_rank, dp_world=dp, seed=1234, fabric=fabric,
-                        lora=lora, load_in_4bit=qlora, tp=(tp, groups.tp_rank) if tp > 1 else None)
+                        lora=lora, load_in_4bit=qlora, tp=(tp, groups.tp_rank) if tp > 1 else None,
+                        shard_params=zero3)
+    if zero3:
+        from wavelet_b200.parallel.zero3 import ParamGatherer
+
+        ParamGatherer(model, group=groups.dp if dp > 1 else None)
     model.tp_group = groups.tp
     if tp_fabric is not None:
         model.attach_tp_fabric(tp_fabric)
@@ -456,7 +467,7 @@ def main():
     from wavelet_b200.trainer.perf import flops_per_token
 
     mfu_flops = flops_per_token(cfg, S, model.lora.num_trainable() if model.lora is not None else None)
-    layout = f"dp{dp}" + (f"xtp{tp}" if tp > 1 else "")
+    layout = f"dp{dp}" + (f"xtp{tp}" if tp > 1 else "") + ("-zero3" if zero3 else "")
     if rank == 0:
         rec = {
             "metric": ("QLoRA SFT tok/s (Qwen2.5-7B-shape, NF4 base, LoRA r16 all projections)" if qlora
@@ -484,7 +495,9 @@ def main():
                 "optimizer": "AdamW (fp32 master, sharded)" + (" on LoRA adapters" if qlora else ""),
                 "activation_checkpointing": args.activation_checkpointing,
                 "optimizer_comm": ("fused peer-memory RS+AdamW+AG kernels" if fabric is not None
-                                   else ("NCCL reduce-scatter/all-gather" if dp > 1 else "none (1 data-parallel rank)")),
+                                   else ("per-layer NCCL weight gathers and gradient reductions (ZeRO-3)" if zero3
+                                         else ("NCCL reduce-scatter/all-gather" if dp > 1
+                                               else "none (1 data-parallel rank)"))),
                 **({"tp_comm": "fused GEMM->all-reduce epilogue over peer memory" if tp_fabric is not None
                     else "NCCL all-reduce"} if tp > 1 else {}),
                 "l2": "inputs larger than L2 (15 GB of weights read per micro-step)",

@@ -1,0 +1,52 @@
+"""`wavelet sft` with sharded parameters (fsdp.shard_params, ZeRO-3) on 2
+gloo CPU ranks against the same data-parallel run with replicated weights:
+per-step losses agree, and a checkpoint is written from the shards."""
+
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _cfg(tmp: Path, name: str, shard: bool) -> Path:
+    out = tmp / name
+    text = (ROOT / "examples" / "tiny_cpu" / "sft.yaml").read_text().replace("outputs/tiny_cpu_sft", str(out))
+    text = text.replace("max_steps: 10", "max_steps: 3")
+    text = text.replace("fsdp:\n  backend: gloo\n", f"fsdp:\n  backend: gloo\n  shard_params: {str(shard).lower()}\n")
+    text += "ckpt:\n  mode: async\n  interval: 3\n"
+    p = tmp / f"{name}.yaml"
+    p.write_text(text)
+    return p
+
+
+def _run(cfg: Path) -> None:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = {**os.environ, "WAVELET_FORCE_CPU": "1"}
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "wavelet_b200", "sft", "@",
+                        str(cfg)], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+
+
+def _losses(out: Path) -> list[float]:
+    return [json.loads(line)["loss"] for line in (out / "metrics.jsonl").read_text().splitlines()]
+
+
+@pytest.mark.integration
+def test_zero3_sft_matches_replicated_weights(tmp_path):
+    _run(_cfg(tmp_path, "rep", False))
+    _run(_cfg(tmp_path, "z3", True))
+    a, b = _losses(tmp_path / "rep"), _losses(tmp_path / "z3")
+    assert len(a) == len(b) == 3
+    for x, y in zip(a, b):
+        assert abs(x - y) <= 1e-4 * abs(x), (a, b)
+    assert (tmp_path / "z3" / "checkpoint-3" / "trainer" / "model.safetensors").exists()

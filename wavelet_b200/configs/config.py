@@ -278,6 +278,11 @@ class FSDPConfig(ConfigModel):
     ep: int = Field(default=1, ge=1)
     cpu_offload: bool = False
     reshard_after_forward: bool = True
+    # ZeRO-3: the bf16 weights are sharded over the data-parallel (x context)
+    # group too and gathered one decoder layer at a time, again in backward
+    # (FSDP2 with reshard_after_forward); off: every rank keeps the full bf16
+    # weights and only the fp32 optimizer state is sharded
+    shard_params: bool = False
     # how expert-parallel token copies move on one CUDA node: fused row kernels
     # over peer memory ("fabric") or variable-split NCCL all-to-alls ("nccl")
     ep_dispatch: Literal["fabric", "nccl"] = "fabric"

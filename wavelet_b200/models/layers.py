@@ -227,6 +227,9 @@ class DecoderLayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, anchor, layer):
         keep = not getattr(layer, "recompute", True)
+        z = getattr(layer, "zero3", None)
+        if z is not None:
+            z.stage_forward(layer.index)  # ZeRO-3: gather this layer's weights
         with torch.no_grad(), nvtx.range(f"layer{layer.index}.fwd"):
             out, cache = layer_fwd(x, layer.P, layer.cfg, layer.batch, save=keep, moe=layer.moe, lora=layer.lora,
                                    tp=layer.tp)
@@ -250,6 +253,9 @@ class DecoderLayerFn(torch.autograd.Function):
         else:
             (x,) = ctx.saved_tensors
         layer = ctx.layer
+        z = getattr(layer, "zero3", None)
+        if z is not None:
+            z.stage_backward(layer.index)  # weights again, gradients into a zeroed staging slot
         with torch.no_grad(), nvtx.range(f"layer{layer.index}.bwd"):
             cache, ctx.cache = ctx.cache, None
             if cache is None:
@@ -257,6 +263,8 @@ class DecoderLayerFn(torch.autograd.Function):
                                      tp=layer.tp)
             dx = layer_bwd(dout, x, cache, layer.P, layer.G, layer.cfg, layer.batch, moe=layer.moe, lora=layer.lora,
                            tp=layer.tp)
+        if z is not None:
+            z.end_backward_layer(layer.index)
         return dx, None, None
 
 
@@ -264,9 +272,10 @@ class EmbeddingFn(torch.autograd.Function):
     """Row gather whose backward scatter-adds straight into the fp32 grad."""
 
     @staticmethod
-    def forward(ctx, ids, anchor, table, gtable):
+    def forward(ctx, ids, anchor, table, gtable, zero3=None):
         ctx.save_for_backward(ids)
         ctx.gtable = gtable
+        ctx.zero3 = zero3
         return ops.embedding_fwd(table, ids)
 
     @staticmethod
@@ -274,7 +283,9 @@ class EmbeddingFn(torch.autograd.Function):
         (ids,) = ctx.saved_tensors
         if ctx.gtable is not None:
             ops.embedding_bwd_(dy, ids, ctx.gtable)
-        return None, None, None, None
+        if ctx.zero3 is not None:  # the last node of the backward: reduce the remaining gradients
+            ctx.zero3.finish_backward()
+        return None, None, None, None, None
 
 
 class FinalNormFn(torch.autograd.Function):

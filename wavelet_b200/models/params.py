@@ -39,6 +39,10 @@ class ParamSpec:
 
 
 class FlatParams:
+    # ZeRO-3 stores (ShardedFlatParams) hold only this rank's shard of
+    # ``compute`` and ``grad``; full parameters exist while a unit is staged
+    sharded_compute = False
+
     def __init__(
         self,
         specs: Iterable[ParamSpec],
@@ -66,12 +70,13 @@ class FlatParams:
         self.shard_numel = self.numel // dp_world
         # ``alloc(numel, dtype)`` places the replicated buffers in peer-visible
         # memory (parallel.fabric) for the fused collective kernels.
+        local = self.shard_numel if self.sharded_compute else self.numel
         if alloc is not None:
-            self.compute = alloc(self.numel, compute_dtype)
-            self.grad = alloc(self.numel, torch.float32) if with_grad else None
+            self.compute = alloc(local, compute_dtype)
+            self.grad = alloc(local, torch.float32) if with_grad else None
         else:
-            self.compute = torch.zeros(self.numel, device=self.device, dtype=compute_dtype)
-            self.grad = torch.zeros(self.numel, device=self.device, dtype=torch.float32) if with_grad else None
+            self.compute = torch.zeros(local, device=self.device, dtype=compute_dtype)
+            self.grad = torch.zeros(local, device=self.device, dtype=torch.float32) if with_grad else None
         self.master = None
         self.exp_avg = None
         self.exp_avg_sq = None
@@ -140,6 +145,12 @@ class FlatParams:
 
     @property
     def shard_slice(self) -> slice:
+        """This rank's optimizer shard as a slice of ``compute`` / ``grad``."""
+        return slice(self.dp_rank * self.shard_numel, (self.dp_rank + 1) * self.shard_numel)
+
+    @property
+    def global_shard_slice(self) -> slice:
+        """This rank's optimizer shard in the full flat layout."""
         return slice(self.dp_rank * self.shard_numel, (self.dp_rank + 1) * self.shard_numel)
 
     # ------------------------------------------------------------- init
@@ -213,3 +224,111 @@ class FlatParams:
     def iter_params(self, fn: Callable[[str, torch.Tensor], None]) -> None:
         for s in self.specs:
             fn(s.name, self.view(s.name))
+
+
+class ShardedFlatParams(FlatParams):
+    """ZeRO-3 flat store: the full layout (offsets) of ``FlatParams``, but each
+    data-parallel rank keeps only its shard [r * shard, (r + 1) * shard) of
+    the bf16 ``compute`` buffer and of the fp32 ``grad`` buffer (the reduced
+    gradients of the elements it owns), next to the fp32 optimizer shard.
+    A parameter's full tensor exists only while its unit (a decoder layer, or
+    the embedding / final norm / head edges) is staged by a
+    ``parallel.zero3.ParamGatherer``: ``view`` / ``grad_view`` then return
+    views of the staging buffers (the reference's FSDP2 with
+    reshard_after_forward, trainer/model.py:1136-1195)."""
+
+    sharded_compute = True
+
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        self.lo = self.dp_rank * self.shard_numel
+        self.hi = self.lo + self.shard_numel
+        self._staged: dict[str, torch.Tensor] = {}
+        self._gstaged: dict[str, torch.Tensor] = {}
+        self.gatherer = None  # set by ParamGatherer
+
+    @property
+    def shard_slice(self) -> slice:
+        return slice(0, self.shard_numel)
+
+    def local_range(self, off: int, n: int) -> tuple[int, int, int, int] | None:
+        """(lo, hi) of [off, off + n) held here, in local and in tensor
+        coordinates: (local_lo, local_hi, tensor_lo, tensor_hi)."""
+        a, b = max(off, self.lo), min(off + n, self.hi)
+        if a >= b:
+            return None
+        return a - self.lo, b - self.lo, a - off, b - off
+
+    def view(self, name: str) -> torch.Tensor:
+        v = self._staged.get(name)
+        if v is None:
+            raise RuntimeError(f"{name} is sharded (ZeRO-3): its unit is not gathered")
+        return v
+
+    def grad_view(self, name: str) -> torch.Tensor | None:
+        if self.grad is None:
+            return None
+        v = self._gstaged.get(name)
+        if v is None:
+            raise RuntimeError(f"the gradient of {name} is sharded (ZeRO-3): its unit is not staged for backward")
+        return v
+
+    def init_(self, seed: int = 0, std_override: float | None = None, seed_index: dict | None = None,
+              row_slices: dict | None = None) -> None:
+        """The same weights as ``FlatParams.init_`` (one generator seed per
+        tensor), of which this rank keeps the part in its shard."""
+        if row_slices:
+            raise NotImplementedError("sharded parameters do not combine with tensor or expert parallelism")
+        g = torch.Generator(device=self.device)
+        for i, s in enumerate(self.specs):
+            off, n = self.offsets[s.name]
+            r = self.local_range(off, n)
+            if r is None:
+                continue
+            ll, lh, tl, th = r
+            dst = self.compute[ll:lh]
+            if s.init == "ones":
+                dst.fill_(1.0)
+            elif s.init == "zeros":
+                dst.zero_()
+            else:
+                g.manual_seed(seed * 1_000_003 + (seed_index[s.name] if seed_index else i))
+                std = std_override if std_override is not None else s.std
+                tmp = torch.empty(n, device=self.device, dtype=torch.float32)
+                tmp.normal_(0.0, std, generator=g)
+                dst.copy_(tmp[tl:th])
+                del tmp
+        self.sync_master_from_compute()
+
+    def load_state(self, tensors: dict[str, torch.Tensor], strict: bool = True) -> list[str]:
+        missing = []
+        for s in self.specs:
+            t = tensors.get(s.name)
+            if t is None:
+                missing.append(s.name)
+                continue
+            off, n = self.offsets[s.name]
+            r = self.local_range(off, n)
+            if r is not None:
+                ll, lh, tl, th = r
+                self.compute[ll:lh].copy_(t.reshape(-1)[tl:th].to(self.compute_dtype))
+        if strict and missing:
+            raise KeyError(f"missing parameters: {missing[:8]}{'...' if len(missing) > 8 else ''}")
+        self.sync_master_from_compute()
+        return missing
+
+    def build_decay_mask(self) -> torch.Tensor:
+        mask = torch.zeros(self.shard_numel, device=self.device, dtype=torch.float32)
+        for s in self.specs:
+            if s.weight_decay:
+                r = self.local_range(*self.offsets[s.name])
+                if r is not None:
+                    mask[r[0]:r[1]] = 1.0
+        self.decay_mask = mask
+        return mask
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        raise RuntimeError("a ZeRO-3 store has no full tensors; gather them (ParamGatherer.full_state)")
+
+    def iter_params(self, fn: Callable[[str, torch.Tensor], None]) -> None:
+        raise RuntimeError("a ZeRO-3 store has no full tensors; gather them (ParamGatherer.full_state)")

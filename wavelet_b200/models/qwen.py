@@ -23,7 +23,7 @@ from .. import ops
 from ..ops import reference as ref
 from .config import ArchConfig
 from .layers import BatchCtx, DecoderLayerFn, EmbeddingFn, FinalNormFn
-from .params import FlatParams, ParamSpec
+from .params import FlatParams, ParamSpec, ShardedFlatParams
 
 
 def param_specs(cfg: ArchConfig) -> list[ParamSpec]:
@@ -144,9 +144,11 @@ class CausalLM:
         for i in range(cfg.num_layers):
             pre = f"l{i}."
             names = [n for n in flat.names() if n.startswith(pre)]
-            P = {n[len(pre):]: flat.view(n) for n in names}
+            # a ZeRO-3 store binds P / G when the layer's unit is gathered
+            P = {n[len(pre):]: flat.view(n) for n in names} if not flat.sharded_compute else {}
             P.update({n[len(pre):]: q for n, q in self.quant.items() if n.startswith(pre)})
-            G = {n[len(pre):]: flat.grad_view(n) for n in names} if flat.grad is not None else {}
+            G = {n[len(pre):]: flat.grad_view(n) for n in names} if (flat.grad is not None and
+                                                                     not flat.sharded_compute) else {}
             if expert_flat is not None:
                 en = [n for n in expert_flat.names() if n.startswith(pre)]
                 P.update({n[len(pre):]: expert_flat.view(n) for n in en})
@@ -160,6 +162,7 @@ class CausalLM:
             self.layers.append(layer)
         self.anchor = torch.empty(0, device=self.device, requires_grad=True)
         self.ep_group = None
+        self.zero3 = None  # parallel.zero3.ParamGatherer of a ZeRO-3 store
 
     # ----------------------------------------------------------- adapters
     def attach_lora(self, adapters) -> None:
@@ -207,7 +210,11 @@ class CausalLM:
             off, k = flat.offsets[n]
             a, b = max(off, lo), min(off + k, hi)
             master = flat.master[a - lo:b - lo].clone() if (flat.master is not None and a < b) else None
-            self._frozen.append((n, flat.view(n).clone(), (a - lo, b - lo) if a < b else None, master))
+            if flat.sharded_compute:  # ZeRO-3: this rank keeps (and restores) only its part
+                val = flat.compute[a - lo:b - lo].clone() if a < b else None
+            else:
+                val = flat.view(n).clone()
+            self._frozen.append((n, val, (a - lo, b - lo) if a < b else None, master))
 
     def _check_ep_layouts(self) -> None:
         """An over-capacity expert layout invalidates the micro-batches of this
@@ -220,7 +227,11 @@ class CausalLM:
 
     def after_optimizer_step(self) -> None:
         for n, val, span, master in getattr(self, "_frozen", []):
-            self.flat.view(n).copy_(val)
+            if self.flat.sharded_compute:
+                if span is not None:
+                    self.flat.compute[span[0]:span[1]].copy_(val)
+            else:
+                self.flat.view(n).copy_(val)
             if span is not None and master is not None:
                 self.flat.master[span[0]:span[1]].copy_(master)
 
@@ -229,7 +240,11 @@ class CausalLM:
         the QK-norm weights are shared by all heads, which are split.  Frozen
         parameters get zero gradients."""
         self._check_ep_layouts()
-        for n, _, _, _ in getattr(self, "_frozen", []):
+        for n, _, span, _ in getattr(self, "_frozen", []):
+            if self.flat.sharded_compute:  # ZeRO-3: the reduced gradients of this rank's part
+                if span is not None and self.flat.grad is not None:
+                    self.flat.grad[span[0]:span[1]].zero_()
+                continue
             g = self.flat.grad_view(n)
             if g is not None:
                 g.zero_()
@@ -321,7 +336,9 @@ class CausalLM:
                 raise NotImplementedError("the CPU reference path runs without expert parallelism")
             return self._hidden_cpu(input_ids.reshape(-1), batch)
         ids = input_ids.reshape(-1).contiguous()
-        x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"))
+        if self.zero3 is not None:
+            self.zero3.begin_forward()
+        x = EmbeddingFn.apply(ids, self.anchor, self.weight("embed"), self.grad("embed"), self.zero3)
         tpc = TPContext(self.tp_group, self.tp_rank, self.tp_size, self.tp_fabric) if self.tp_size > 1 else None
         for layer in self.layers:
             layer.batch = batch
@@ -415,7 +432,7 @@ class CausalLM:
 def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed=0, init=True,
                 with_grad=True, with_optimizer=True, fabric=None, lora=None, load_in_4bit: bool = False,
                 lora_seed: int = 0, ep: tuple[int, int, int, int] | None = None,
-                tp: tuple[int, int] | None = None, ep_fabric=None) -> CausalLM:
+                tp: tuple[int, int] | None = None, ep_fabric=None, shard_params: bool = False) -> CausalLM:
     """Build (and random-init) a model (a ``DeepseekV4Config`` builds the
     eager DeepSeek-V4 model behind the same interface).
 
@@ -426,6 +443,9 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
     parallelism; the expert tensors of this rank go to ``model.expert_flat``
     (in peer-visible memory of ``ep_fabric`` when given: policy refresh and
     the fused dispatch read it from the other ranks).
+    ``shard_params``: ZeRO-3 — the bf16 weights are sharded over the
+    ``dp_world`` ranks too (``ShardedFlatParams``); attach a
+    ``parallel.zero3.ParamGatherer`` before running the model.
     """
     device = torch.device(device)
     if dtype is None:
@@ -447,6 +467,9 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
 
         return DeepseekV4Trainable(cfg, device, dtype, dp_rank, dp_world, seed, init, with_grad, with_optimizer)
     tp_size, tp_rank = tp or (1, 0)
+    if shard_params and (lora is not None or load_in_4bit or tp_size > 1 or (ep or (1,))[0] > 1 or fabric is not None):
+        raise NotImplementedError("sharded parameters (ZeRO-3) train dense or MoE models with data (and context) "
+                                  "parallelism: no LoRA / NF4, tensor or expert parallelism, or fused peer optimizer")
     full_specs = param_specs(cfg)
     specs = param_specs(tp_local_cfg(cfg, tp_size)) if tp_size > 1 else full_specs
     if tp_size > 1 and (lora is not None or load_in_4bit or (ep or (1,))[0] > 1):
@@ -481,9 +504,10 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
                                  alloc=ep_fabric.allocator() if ep_fabric is not None else None)
         if init:
             expert_flat.init_(seed, seed_index=seed_index, row_slices=rows)
-    flat = FlatParams([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,
-                      with_grad and not frozen, with_optimizer and not frozen,
-                      alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
+    store = ShardedFlatParams if shard_params else FlatParams
+    flat = store([s for s in specs if s.name not in qnames], device, dtype, dp_rank, dp_world,
+                 with_grad and not frozen, with_optimizer and not frozen,
+                 alloc=fabric.allocator() if (fabric is not None and not frozen) else None)
     if tp_repl:
         flat.set_tp_replicated([s.name for s in tp_repl], tp_size)
     quant = {}
@@ -504,6 +528,8 @@ def build_model(cfg: ArchConfig, device, dtype=None, dp_rank=0, dp_world=1, seed
             del tmp
     model = CausalLM(cfg, flat, quant, expert_flat, (ep_size, ep_rank), tp=(tp_size, tp_rank))
     model.ep_dp_rank = ep_dp_rank
+    if shard_params:
+        model.fused_cpu = True  # the per-layer gathers hook the kernel-path layer functions (CPU fallbacks too)
     if frozen:
         from .lora import LoRAAdapters
 

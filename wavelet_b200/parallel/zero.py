@@ -86,12 +86,15 @@ class ShardedAdamW:
             self._stage = [torch.empty(min(offload_chunk, flat.shard_numel), device=dev, dtype=torch.float32)
                            for _ in range(3)]
         self.g_shard = (
-            torch.empty(flat.shard_numel, device=dev, dtype=torch.float32) if dp_world > 1 else None
+            torch.empty(flat.shard_numel, device=dev, dtype=torch.float32)
+            if dp_world > 1 and not flat.sharded_compute else None
         )
         self.stats = torch.zeros(2, device=dev, dtype=torch.float32)
         self.clip = torch.ones(2, device=dev, dtype=torch.float32)
 
     def reduce_grads(self) -> torch.Tensor:
+        if self.flat.sharded_compute:  # ZeRO-3: each unit's gradients were reduced into the shard in backward
+            return self.flat.grad
         if self.world > 1:
             dist.reduce_scatter_tensor(self.g_shard, self.flat.grad, op=dist.ReduceOp.SUM, group=self.group)
             return self.g_shard
@@ -145,7 +148,7 @@ class ShardedAdamW:
             )
         if compute.dtype != torch.bfloat16:
             p16.copy_(flat.master)
-        if self.world > 1:
+        if self.world > 1 and not flat.sharded_compute:  # ZeRO-3 gathers lazily, unit by unit
             src = p16 if compute.is_cuda else p16.clone()
             dist.all_gather_into_tensor(compute, src, group=self.group)
         flat.zero_grad()
@@ -211,7 +214,7 @@ class ShardedAdamW:
         compute = self.flat.compute.detach()
         p16 = compute[self.flat.shard_slice]
         p16.copy_(self.flat.master.to(p16.dtype))
-        if self.world > 1:
+        if self.world > 1 and not self.flat.sharded_compute:
             dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
 
 
@@ -256,7 +259,7 @@ class ShardedAdamW8bit(ShardedAdamW):
                          step=self.step_count, gscale_host=factor)
         if compute.dtype != torch.bfloat16:
             p16.copy_(flat.master)
-        if self.world > 1:
+        if self.world > 1 and not flat.sharded_compute:  # ZeRO-3 gathers lazily, unit by unit
             src = p16 if compute.is_cuda else p16.clone()
             dist.all_gather_into_tensor(compute, src, group=self.group)
         flat.zero_grad()
@@ -284,7 +287,7 @@ class ShardedAdamW8bit(ShardedAdamW):
         compute = self.flat.compute.detach()
         p16 = compute[self.flat.shard_slice]
         p16.copy_(self.flat.master.to(p16.dtype))
-        if self.world > 1:
+        if self.world > 1 and not self.flat.sharded_compute:
             dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
 
 

@@ -81,7 +81,9 @@ class CheckpointManager:
         weights = None
         tp_size = getattr(model, "tp_size", 1)
         wname = "model.safetensors" if tp_size == 1 else f"model-tp{model.tp_rank}.safetensors"
-        if (self.rank == 0) if tp_size == 1 else (flat.dp_rank == 0):  # one copy of every TP shard
+        if getattr(flat, "sharded_compute", False):  # ZeRO-3: gathered unit by unit (every rank takes part)
+            weights = flat.gatherer.full_state(lambda n, t: self._host("w:" + n, t))
+        elif (self.rank == 0) if tp_size == 1 else (flat.dp_rank == 0):  # one copy of every TP shard
             weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
         experts = None
         ef = getattr(model, "expert_flat", None)
@@ -183,11 +185,11 @@ class CheckpointManager:
                 for k in ("master", "exp_avg", "exp_avg_sq"):
                     full = torch.cat([p[k] for p in parts])
                     full = torch.nn.functional.pad(full, (0, max(0, flat.numel - full.numel())))[: flat.numel]
-                    sd[k] = full[flat.shard_slice].to(flat.device)
+                    sd[k] = full[flat.global_shard_slice].to(flat.device)
                 if "momentum" in parts[0]:
                     full = torch.cat([p["momentum"] for p in parts])
                     full = torch.nn.functional.pad(full, (0, max(0, flat.numel - full.numel())))[: flat.numel]
-                    sd["momentum"] = full[flat.shard_slice].to(flat.device)
+                    sd["momentum"] = full[flat.global_shard_slice].to(flat.device)
             optimizer.load_state_dict(sd)
         data_state = None
         p = d / "dataloader" / f"rank{self.rank}.json"

@@ -9,12 +9,14 @@
 * ``model.freeze_moe_router``: the router weights are frozen (no gradient,
   no update, no decay); a model without MoE routers is an error, as in the
   reference (trainer/moe.py:275-300).
-* ``model.meta_device_init`` and ``fsdp.reshard_after_forward`` ask the
-  reference's FSDP wrapper to build on the meta device and to free gathered
-  weights after forward.  Here parameters are always allocated directly on
-  the device (nothing is built on the host first) and the bf16 weights stay
-  resident by design, so both are satisfied as they are; setting either
-  explicitly logs what happens instead.
+* ``model.meta_device_init`` asks the reference's FSDP wrapper to build on
+  the meta device: here parameters are always allocated directly on the
+  device (each rank only its shard with ``fsdp.shard_params``), so it is
+  satisfied as it is; setting it logs that.
+* ``fsdp.reshard_after_forward``: with ``fsdp.shard_params`` (ZeRO-3) the
+  gathered weights of a layer are released after its forward and gathered
+  again for its backward, which is the reference's ``true``; without
+  sharded parameters the bf16 weights stay resident on every rank.
 """
 
 from __future__ import annotations
@@ -45,8 +47,13 @@ def apply_model_options(model, mcfg, fsdp_cfg=None) -> list[str]:
         notes.append("model.meta_device_init: parameters are allocated directly on the device "
                      "(no host materialisation to defer)")
     if fsdp_cfg is not None and "reshard_after_forward" in getattr(fsdp_cfg, "model_fields_set", set()):
-        notes.append(f"fsdp.reshard_after_forward={fsdp_cfg.reshard_after_forward}: bf16 weights stay resident "
-                     "on every data-parallel rank (only optimizer state is sharded)")
+        if getattr(fsdp_cfg, "shard_params", False):
+            notes.append("fsdp.reshard_after_forward: sharded parameters are gathered per layer, released after "
+                         "the forward and gathered again in the backward")
+        else:
+            notes.append(f"fsdp.reshard_after_forward={fsdp_cfg.reshard_after_forward}: bf16 weights stay "
+                         "resident on every data-parallel rank (only optimizer state is sharded; "
+                         "fsdp.shard_params shards them)")
     for n in notes:
         log.info(n)
     return notes

@@ -214,7 +214,7 @@ class FlatOptimizer:
         compute = flat.compute.detach()
         p16 = compute[flat.shard_slice]
         p16.copy_(p.to(p16.dtype))
-        if self.world > 1:
+        if self.world > 1 and not flat.sharded_compute:  # ZeRO-3 gathers lazily, unit by unit
             dist.all_gather_into_tensor(compute, p16.clone(), group=self.group)
         flat.zero_grad()
         return {"grad_norm": norm, "clip_factor": factor}

@@ -76,7 +76,8 @@ class SFTTrainer:
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
         self.fabric = None
         self.norm_fabric = None
-        if dev.type == "cuda" and dims.cp == 1 and dims.ep == 1 and c.fsdp.backend != "gloo":
+        shard = c.fsdp.shard_params
+        if dev.type == "cuda" and dims.cp == 1 and dims.ep == 1 and c.fsdp.backend != "gloo" and not shard:
             from ..parallel.fabric import maybe_fabric
 
             # the fused optimizer step runs over the data-parallel group (inside
@@ -98,7 +99,12 @@ class SFTTrainer:
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                  ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
                                  if dims.ep > 1 else None,
-                                 tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
+                                 tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None,
+                                 shard_params=shard)
+        if shard:
+            from ..parallel.zero3 import ParamGatherer
+
+            ParamGatherer(self.model, group=opt_group if opt_world > 1 else None)
         self.model.tp_group = self.groups.tp
         self.tp_fabric = None
         if dims.tp > 1 and dev.type == "cuda" and c.fsdp.backend != "gloo" and c.fsdp.tp_reduce == "fabric":
