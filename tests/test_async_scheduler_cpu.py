@@ -294,3 +294,37 @@ def test_resume_restores_prompt_and_curriculum_state(tmp_path):
     assert stable_steps(q) == [0, 1, 2, 3]
     rows = read_training_records(step_dir(q, 2) / "rollouts.jsonl.train.msgpack")
     assert [r["input_ids"][0] for r in rows] == [4, 5]  # step 2 redrawn from the restored cursor
+
+
+def test_pipeline_status_and_live_state(tmp_path, caplog):
+    """The periodic status line (pipeline_status_interval_seconds) and the
+    live run state: every published batch becomes an event, the status
+    snapshot reaches the state's sink."""
+    import logging
+
+    from wavelet_b200.orchestrator.state_server import OrchestratorRunState
+    from wavelet_b200.orchestrator.status import StatusReporter, pipeline_line
+
+    cfg = _cfg(tmp_path, orchestrator={"max_async_level": 1, "pipeline_status_interval_seconds": 0.02},
+               max_steps=3)
+    out = cfg.output_dir
+    for s in range(4):
+        _policy(out, s)
+    sch = _sched(cfg, FakeOrch(Counter(), delay=0.05), FakeEngine())
+    state = OrchestratorRunState(out)
+    snaps = []
+    sch.run_state = state
+    sch.status_sink = snaps.append
+    with caplog.at_level(logging.INFO, logger="wavelet"):
+        assert sch.run() == 0
+    ev = [e for e in state.events() if e["event"] == "batch_published"]
+    assert [e["step"] for e in ev] == [0, 1, 2] and state.snapshot()["step"] == 2
+    assert snaps and {"published", "target", "inflight", "ready", "loading", "policy_step"} <= set(snaps[-1])
+    assert snaps[-1]["target"] == 3
+    assert any("pipeline: policy" in r.getMessage() for r in caplog.records)
+    line = pipeline_line({"policy_step": None, "published": 1, "target": 4, "submitted": 2, "inflight": 1,
+                          "ready": 0, "loading": True})
+    assert "policy none" in line and "published 1/4" in line and "policy load running" in line
+    r = StatusReporter(lambda: {"policy_step": 3, "published": 0, "target": 1, "submitted": 0, "inflight": 0,
+                                "ready": 0, "loading": False}, 10.0, sink=lambda s: 1 / 0)
+    assert r.emit()["policy_step"] == 3  # a failing sink does not raise

@@ -229,6 +229,10 @@ class AsyncRolloutScheduler:
         base = prompts if prompts is not None else orchestrator.prompts
         self.prompts = base if isinstance(base, LockedPrompts) else LockedPrompts(base)
         self.evaluate = evaluate
+        # live state (state_server.OrchestratorRunState) and the periodic
+        # status snapshots; both optional
+        self.run_state = None
+        self.status_sink = None
         self.wait_memory = wait_memory or (lambda: wait_for_trainer_memory(cfg))
         self.concurrent_generate = bool(getattr(engine, "concurrent_generate", False))
         self.concurrent_load = bool(getattr(engine, "concurrent_policy_load", False))
@@ -389,6 +393,11 @@ class AsyncRolloutScheduler:
             append_jsonl(self.out / "orchestrator_metrics.jsonl", m)
             log.info("published rollouts for step %d (policy %s, reward %.4f)", st.step, st.policy,
                      m.get("reward/mean", 0.0))
+            if self.run_state is not None:
+                self.run_state.update(status="running", step=st.step, policy_step=st.policy,
+                                      metrics={k: v for k, v in m.items() if isinstance(v, (int, float))})
+                self.run_state.event("batch_published", step=st.step, policy_step=st.policy,
+                                     samples=len(recs), reward_mean=m.get("reward/mean"))
             next_pub += 1
             if not self.pending:
                 self._sleep()
@@ -404,8 +413,14 @@ class AsyncRolloutScheduler:
         if not self.concurrent_generate:
             prefetch = 1  # one generator on one GPU: steps run back to back (still ahead of the trainer)
         poll = self.cfg.policy_transfer.poll_interval_seconds
-        with ThreadPoolExecutor(max_workers=prefetch + 1, thread_name_prefix="wavelet-rollouts") as pool:
+        self._progress = {"target": total, "submitted": step, "published": next_pub}
+        from .status import StatusReporter
+
+        status = StatusReporter(self.pipeline_status, self.cfg.orchestrator.pipeline_status_interval_seconds,
+                                sink=self.status_sink)
+        with status, ThreadPoolExecutor(max_workers=prefetch + 1, thread_name_prefix="wavelet-rollouts") as pool:
             while next_pub < total:
+                self._progress.update(submitted=step, published=next_pub)
                 self._finish_load()
                 self._maybe_start_load(pool)
                 need = required_policy_step(step // self.C, self.cfg) if step < total else None
@@ -429,6 +444,13 @@ class AsyncRolloutScheduler:
             self._finish_load(block=True)
         self._final_evals(total // self.C)
         return 0
+
+    def pipeline_status(self) -> dict:
+        """Snapshot for the periodic status line (read from another thread)."""
+        p = getattr(self, "_progress", {"target": 0, "submitted": 0, "published": 0})
+        return {"policy_step": self.loaded, "published": p["published"], "target": p["target"],
+                "submitted": p["submitted"], "inflight": len(self.pending), "ready": len(self.done),
+                "loading": self.load_future is not None}
 
     def _final_evals(self, total: int) -> None:
         """Evaluate the last policy the trainer exports at or before the final

@@ -54,8 +54,26 @@ class RolloutScheduler:
         return self._pipeline
 
     def run(self) -> int:
-        """Bounded-prefetch, in-order rollout publishing (``AsyncRolloutScheduler``)."""
-        return self.pipeline().run()
+        """Bounded-prefetch, in-order rollout publishing (``AsyncRolloutScheduler``),
+        with the live state (``orchestrator.state_server``: HTTP) and the
+        periodic pipeline status line."""
+        from .state_server import OrchestratorRunState, maybe_state_server
+
+        pipe = self.pipeline()
+        state = OrchestratorRunState(self.out)
+        pipe.run_state = state
+        pipe.status_sink = lambda snap: state.update(pipeline=snap, queue_depth=snap["ready"] + snap["inflight"])
+        handle = maybe_state_server(self.cfg, state)
+        try:
+            rc = pipe.run()
+            state.update(status="completed")
+            return rc
+        except BaseException:
+            state.update(status="failed")
+            raise
+        finally:
+            if handle is not None:
+                handle.close()
 
 
 class _GeneratorAdapter:
