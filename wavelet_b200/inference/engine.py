@@ -42,7 +42,7 @@ import torch
 
 from .. import ops
 from ..utils import nvtx
-from ..models.layers import _lin
+from ..models.layers import _lin, _lin_rowpar
 from ..models.qwen import CausalLM
 from ..ops import reference as ref
 from ..ops.attention import attention_fwd
@@ -151,11 +151,19 @@ class Generator:
         self.m = model
         cfg = model.cfg
         self.cfg = cfg
+        # tensor parallelism (Megatron split of a TP-trained model): this rank
+        # runs its heads and FFN columns, row-parallel outputs are summed over
+        # the TP group; the LM head and norms are replicated, so every rank
+        # samples the same tokens from identical logits and a shared seed
+        self.tp = getattr(model, "tp_size", 1)
+        self.lc = getattr(model, "layer_cfg", cfg)  # this rank's head counts
+        if self.tp > 1 and any(layer.moe is not None for layer in model.layers):
+            raise NotImplementedError("tensor-parallel generation of MoE models is not supported")
         self.dev = model.device
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
         self.max_model_len = max_model_len
-        per_block = 2 * cfg.num_layers * block_size * cfg.num_kv_heads * cfg.head_dim * 2
+        per_block = 2 * cfg.num_layers * block_size * self.lc.num_kv_heads * cfg.head_dim * 2
         if kv_cache_bytes is None:
             if self.dev.type == "cuda":
                 free, total = torch.cuda.mem_get_info(self.dev)
@@ -166,7 +174,7 @@ class Generator:
         self.num_blocks = max(4, kv_cache_bytes // per_block)
         # head-major pages: one head's tokens of a block are contiguous (decode
         # attention streams 8 KB runs per head instead of 256-byte pieces)
-        shape = (self.num_blocks, cfg.num_kv_heads, block_size, cfg.head_dim)
+        shape = (self.num_blocks, self.lc.num_kv_heads, block_size, cfg.head_dim)
         dt = model.flat.compute_dtype
         self.k_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
         self.v_cache = [torch.empty(shape, device=self.dev, dtype=dt) for _ in range(cfg.num_layers)]
@@ -177,7 +185,9 @@ class Generator:
         self.stats: dict[str, float] = {}
         self._moe = [layer.moe for layer in model.layers]
         self.window = window
-        self.use_graphs = (cuda_graphs and self.dev.type == "cuda" and not any(self._moe) and not model.quant)
+        # graphs replay fixed launches: TP collectives (host-side epochs, NCCL) stay eager
+        self.use_graphs = (cuda_graphs and self.dev.type == "cuda" and not any(self._moe) and not model.quant
+                           and self.tp == 1)
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
         self._graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
         self._graph_kernels: dict[tuple[int, int], int] = {}
@@ -217,8 +227,13 @@ class Generator:
     # -------------------------------------------------------------- forward
     def _layers_forward(self, x, pos, slots, attn_fn):
         cfg = self.cfg
-        nq, nk, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        nq, nk, hd = self.lc.num_heads, self.lc.num_kv_heads, cfg.head_dim
         T = x.shape[0]
+        tpc = None
+        if self.tp > 1:
+            from ..models.qwen import TPContext
+
+            tpc = TPContext(self.m.tp_group, self.m.tp_rank, self.tp, self.m.tp_fabric)
         for li, layer in enumerate(self.m.layers):
             P = layer.P
             lora = layer.lora or {}
@@ -236,14 +251,14 @@ class Generator:
                 self.k_cache[li][blk, :, off] = k
                 self.v_cache[li][blk, :, off] = v
             att = attn_fn(li, q, k, v)
-            x, _ = _lin(att.reshape(T, nq * hd), P["o_w"], lora.get("o"), res=x)
+            x, _ = _lin_rowpar(att.reshape(T, nq * hd), P["o_w"], lora.get("o"), x, tpc)
             if layer.moe is not None:
                 h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
                 x = layer.moe.infer(h2, x, P)
             else:
                 h2, _, _ = ops.rmsnorm_fwd(x, P["post_norm"], cfg.rms_eps)
                 a = ops.swiglu_fwd(_lin(h2, P["gu_w"], lora.get("gu"))[0])
-                x, _ = _lin(a, P["down_w"], lora.get("down"), res=x)
+                x, _ = _lin_rowpar(a, P["down_w"], lora.get("down"), x, tpc)
         hf, _, _ = ops.rmsnorm_fwd(x, self.m.weight("norm"), cfg.rms_eps)
         return hf
 
@@ -299,7 +314,7 @@ class Generator:
     def _decode_attn_ref(self, li, q, bt, ctx, scale):
         """Dense attention over the gathered paged KV (CPU path and oracle)."""
         B, Hq, D = q.shape
-        Hk = self.cfg.num_kv_heads
+        Hk = self.lc.num_kv_heads
         out = torch.empty_like(q)
         for i in range(B):
             L = int(ctx[i])
@@ -337,12 +352,15 @@ class Generator:
             row_ids = torch.tensor([s.row_id for s in seqs], dtype=torch.long, device=self.dev)
             ops.ext().sample_tokens(z, inv_tau, thresh, float(min_p), int(step_seed), row_ids, tok, lp)
         else:
-            zt = z.float() * inv_tau[:, None]
+            # temperature 0 (inv_tau 0) is greedy at scale 1, as in the sampling kernel
+            greedy = inv_tau <= 0
+            zt = z.float() * torch.where(greedy, torch.ones_like(inv_tau), inv_tau)[:, None]
             if thresh is not None:
                 zt = zt.masked_fill(z.float() < thresh[:, None], float("-inf"))
             g = torch.Generator().manual_seed(int(step_seed))
             probs = torch.softmax(zt, -1)
             tok = torch.multinomial(probs, 1, generator=g)[:, 0]
+            tok = torch.where(greedy, zt.argmax(-1), tok)
             lp = torch.log_softmax(zt, -1).gather(1, tok[:, None])[:, 0]
         masks = None
         if any(s.params.truncated and s.params.return_sampling_mask for s in seqs):
@@ -367,6 +385,12 @@ class Generator:
         """Generate ``params.n`` completions for every prompt."""
         t0 = time.perf_counter()
         base_seed = params.seed if params.seed is not None else int(time.time_ns() & 0x7FFFFFFF)
+        if self.tp > 1:  # one seed for the TP group: identical logits then sample identical tokens
+            import torch.distributed as dist
+
+            t = torch.tensor([base_seed], dtype=torch.long, device=self.dev)
+            dist.broadcast(t, src=dist.get_global_rank(self.m.tp_group, 0), group=self.m.tp_group)
+            base_seed = int(t.item())
         pending: list[tuple[int, list[int]]] = list(enumerate(prompts))
         active: list[_Seq] = []
         finished: list[_Seq] = []
@@ -455,7 +479,7 @@ class Generator:
         """Split the context only when (sequences x kv heads) CTAs cannot fill
         the GPU (~3 resident per SM); each split keeps >= 2 stages of 32 tokens.
         Powers of two keep the number of captured graphs small."""
-        ctas = B * self.cfg.num_kv_heads
+        ctas = B * self.lc.num_kv_heads
         want = max(1, -(-3 * 148 // max(1, ctas)))
         cap = max(1, max_ctx // 64)
         sp = max(1, min(16, want, cap))

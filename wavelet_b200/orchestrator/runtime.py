@@ -123,8 +123,11 @@ class IntegratedRunner:
     def _gather(self, rows: list[dict]) -> list[dict]:
         if not dist.is_initialized() or self.world.world_size == 1:
             return rows
+        # tensor-parallel peers generate the same rows (one prompt shard per
+        # data-parallel rank, identical sampling): only TP rank 0 contributes
+        mine = rows if getattr(self.trainer.model, "tp_rank", 0) == 0 else []
         allr: list[Any] = [None] * self.world.world_size
-        dist.all_gather_object(allr, rows)
+        dist.all_gather_object(allr, mine)
         return [r for part in allr for r in part]
 
     def run_step(self) -> dict[str, Any]:
