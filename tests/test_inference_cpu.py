@@ -71,13 +71,13 @@ def test_scheduler_publishes_with_policy_lag(tmp_path, cpu_env, monkeypatch):
     cfg = _cfg(tmp_path, orchestrator={"examples_per_step": 2, "rollouts_per_example": 2, "max_async_level": 1,
                                        "filter_zero_advantage": False})
     out = tmp_path / "out"
-    # a policy snapshot for step 0 (device-kind marker is enough for the in-process engine)
-    pd = step_dir(out / "policies", 0)
-    pd.mkdir(parents=True)
-    (pd / "policy.json").write_text(json.dumps({"step": 0, "kind": "device"}))
-    (pd / STABLE).touch()
     eng = NativePolicyInferenceEngine(cfg)
     eng.setup()
+    # the policy snapshot of step 0: the generator's own weights, exported through the filesystem
+    from wavelet_b200.transport.policy import PolicyExporter
+
+    PolicyExporter(out, cfg.policy_transfer).export(eng.model, 0)
+    assert (step_dir(out / "policies", 0) / STABLE).exists()
     sch = RolloutScheduler(cfg, engine=eng)
     assert sch.run() == 0
     steps = stable_steps(out / "rollouts")
