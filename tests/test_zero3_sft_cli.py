@@ -50,3 +50,35 @@ def test_zero3_sft_matches_replicated_weights(tmp_path):
     for x, y in zip(a, b):
         assert abs(x - y) <= 1e-4 * abs(x), (a, b)
     assert (tmp_path / "z3" / "checkpoint-3" / "trainer" / "model.safetensors").exists()
+
+
+def _run4(cfg: Path) -> None:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = {**os.environ, "WAVELET_FORCE_CPU": "1"}
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "4",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "wavelet_b200", "sft", "@",
+                        str(cfg)], cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-3000:]
+
+
+@pytest.mark.integration
+def test_hybrid_sharding_matches_replicated_weights(tmp_path):
+    """HSDP: 4 ranks = 2 replicas x 2 shards (fsdp.dp_replicate 2 with
+    sharded parameters): the losses of 4-way data parallelism with
+    replicated weights."""
+    def four(p):  # the global batch divisible by 4 ranks x micro-batch
+        p.write_text(p.read_text().replace("micro_batch_size: 4", "micro_batch_size: 2"))
+        return p
+
+    _run4(four(_cfg(tmp_path, "rep4", False)))
+    p = four(_cfg(tmp_path, "hsdp", True))
+    p.write_text(p.read_text().replace("  shard_params: true\n", "  shard_params: true\n  dp_replicate: 2\n"))
+    _run4(p)
+    a, b = _losses(tmp_path / "rep4"), _losses(tmp_path / "hsdp")
+    assert len(a) == len(b) == 3
+    for x, y in zip(a, b):
+        assert abs(x - y) <= 1e-4 * abs(x), (a, b)
+    assert (tmp_path / "hsdp" / "checkpoint-3" / "trainer" / "model.safetensors").exists()

@@ -145,6 +145,15 @@ class Groups:
         self.dp_cp = None
         self.dp_cp_rank = 0
         self.dp_cp_size = dims.dp * dims.cp
+        # hybrid sharding (HSDP, sharded parameters with dp_replicate > 1):
+        # one copy of the sharded model per replica over dp_shard x cp
+        # ("shard"), gradients all-reduced across the replicas ("replicate")
+        self.shard = None
+        self.shard_rank = 0
+        self.shard_size = dims.dp_shard * dims.cp
+        self.replicate = None
+        self.replicate_rank = 0
+        self.replicate_size = dims.dp_replicate
         if not dist.is_initialized() or dims.world_size == 1:
             return
         W = dims.world_size
@@ -186,6 +195,26 @@ class Groups:
                     self.dp_cp_rank = ranks.index(rank)
         else:
             self.dp_cp, self.dp_cp_rank = self.dp, self.dp_rank
+        if dims.dp_replicate > 1:
+            seen_s, seen_r = set(), set()
+            for r0 in range(W):
+                c0 = dims.coords(r0)
+                ks, kr = (c0["dp_replicate"], c0["tp"]), (c0["dp_shard"], c0["cp"], c0["tp"])
+                if ks not in seen_s:
+                    seen_s.add(ks)
+                    ranks = [r for r in range(W) if (dims.coords(r)["dp_replicate"], dims.coords(r)["tp"]) == ks]
+                    g = dist.new_group(ranks) if len(ranks) > 1 else None
+                    if rank in ranks:
+                        self.shard, self.shard_rank = g, ranks.index(rank)
+                if kr not in seen_r:
+                    seen_r.add(kr)
+                    ranks = [r for r in range(W) if (dims.coords(r)["dp_shard"], dims.coords(r)["cp"],
+                                                     dims.coords(r)["tp"]) == kr]
+                    g = dist.new_group(ranks)
+                    if rank in ranks:
+                        self.replicate, self.replicate_rank = g, ranks.index(rank)
+        else:
+            self.shard, self.shard_rank = self.dp_cp, self.dp_cp_rank
         if dims.ep > 1:
             # contiguous blocks of ep ranks among the dp_shard x cp ranks
             for base in range(0, W, dims.ep):

@@ -63,11 +63,15 @@ class AdamWHyper:
 
 class ShardedAdamW:
     def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 offload: bool = False, offload_chunk: int = 1 << 26, norm_world: bool = False):
+                 offload: bool = False, offload_chunk: int = 1 << 26, norm_world: bool = False,
+                 replicate_group=None):
         self.flat = flat
         self.h = hyper
         self.group = dp_group
         self.world = dp_world
+        # hybrid sharding: the sharded store is replicated over this group,
+        # whose members all-reduce their reduced gradient shards
+        self.replicate_group = replicate_group
         # norm_world: the squared norm is summed over every rank of the job
         # (tensor parallelism: each TP rank holds a different part of the model)
         self.norm_world = norm_world
@@ -94,6 +98,8 @@ class ShardedAdamW:
 
     def reduce_grads(self) -> torch.Tensor:
         if self.flat.sharded_compute:  # ZeRO-3: each unit's gradients were reduced into the shard in backward
+            if self.replicate_group is not None:
+                dist.all_reduce(self.flat.grad, group=self.replicate_group)
             return self.flat.grad
         if self.world > 1:
             dist.reduce_scatter_tensor(self.g_shard, self.flat.grad, op=dist.ReduceOp.SUM, group=self.group)
@@ -227,8 +233,8 @@ class ShardedAdamW8bit(ShardedAdamW):
     optimizers, reference trainer/optim.py:393-512)."""
 
     def __init__(self, flat: FlatParams, hyper: AdamWHyper, dp_group=None, dp_world: int = 1,
-                 paged: bool = False, norm_world: bool = False):
-        super().__init__(flat, hyper, dp_group, dp_world, norm_world=norm_world)
+                 paged: bool = False, norm_world: bool = False, replicate_group=None):
+        super().__init__(flat, hyper, dp_group, dp_world, norm_world=norm_world, replicate_group=replicate_group)
         n = flat.shard_numel
         nb = (n + ops.Q8_BLOCK - 1) // ops.Q8_BLOCK
         dev = flat.device

@@ -83,6 +83,8 @@ class CheckpointManager:
         wname = "model.safetensors" if tp_size == 1 else f"model-tp{model.tp_rank}.safetensors"
         if getattr(flat, "sharded_compute", False):  # ZeRO-3: gathered unit by unit (every rank takes part)
             weights = flat.gatherer.full_state(lambda n, t: self._host("w:" + n, t))
+            if self.rank != 0:  # hybrid sharding: every replica gathers its own copy; global rank 0 writes
+                weights = None
         elif (self.rank == 0) if tp_size == 1 else (flat.dp_rank == 0):  # one copy of every TP shard
             weights = {n: self._host("w:" + n, flat.view(n)) for n in flat.names()}
         experts = None

@@ -129,7 +129,7 @@ class FlatOptimizer:
 
     def __init__(self, flat: FlatParams, cfg, max_grad_norm: float, dp_group=None, dp_world: int = 1, fabric=None,
                  expert_flat: FlatParams | None = None, ep_dp_group=None, ep_dp_world: int = 1,
-                 norm_fabric=None):
+                 norm_fabric=None, replicate_group=None):
         self.flat = flat
         self.cfg = cfg
         self.type = cfg.type
@@ -155,7 +155,7 @@ class FlatOptimizer:
             from ..parallel.zero import ShardedAdamW8bit
 
             self.adamw = ShardedAdamW8bit(flat, hyper, dp_group, dp_world, paged=cfg.type == "paged_adamw_8bit",
-                                          norm_world=flat.tp_size > 1)
+                                          norm_world=flat.tp_size > 1, replicate_group=replicate_group)
         elif fabric is not None and cfg.type in ("adamw", "adam"):
             from ..parallel.zero import FusedShardedAdamW
 
@@ -163,7 +163,7 @@ class FlatOptimizer:
         else:
             self.adamw = ShardedAdamW(flat, hyper, dp_group, dp_world,
                                       offload=bool(getattr(cfg, "cpu_offload", False)),
-                                      norm_world=flat.tp_size > 1)
+                                      norm_world=flat.tp_size > 1, replicate_group=replicate_group)
         self.momentum_buf = None
 
     @property

@@ -71,6 +71,11 @@ class SFTTrainer:
         # reductions use that group (data is split over dp only)
         self.cp = dims.cp
         opt_group, opt_rank, opt_world = self.groups.dp_cp, self.groups.dp_cp_rank, self.groups.dp_cp_size
+        # hybrid sharding: sharded parameters and optimizer state over one
+        # replica (dp_shard x cp), gradients all-reduced across dp_replicate
+        hsdp = c.fsdp.shard_params and dims.dp_replicate > 1
+        shard_group, shard_rank, shard_world = ((self.groups.shard, self.groups.shard_rank, self.groups.shard_size)
+                                                if hsdp else (opt_group, opt_rank, opt_world))
         dev = w.device
         arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
         dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
@@ -93,7 +98,8 @@ class SFTTrainer:
             from ..parallel.fabric import Fabric
 
             self.ep_fabric = Fabric(self.groups.ep_rank, dims.ep, dev, group=self.groups.ep)
-        self.model = build_model(arch, dev, dtype, dp_rank=opt_rank, dp_world=opt_world, seed=c.seed, fabric=self.fabric,
+        self.model = build_model(arch, dev, dtype, dp_rank=shard_rank, dp_world=shard_world, seed=c.seed,
+                                 fabric=self.fabric,
                                  ep_fabric=self.ep_fabric,
                                  init=c.model.random_init or not _has_weights(c.model.name), lora=c.lora,
                                  load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
@@ -104,7 +110,7 @@ class SFTTrainer:
         if shard:
             from ..parallel.zero3 import ParamGatherer
 
-            ParamGatherer(self.model, group=opt_group if opt_world > 1 else None)
+            ParamGatherer(self.model, group=shard_group if shard_world > 1 else None)
         self.model.tp_group = self.groups.tp
         self.tp_fabric = None
         if dims.tp > 1 and dev.type == "cuda" and c.fsdp.backend != "gloo" and c.fsdp.tp_reduce == "fabric":
@@ -128,10 +134,11 @@ class SFTTrainer:
             from ..models.hf_io import load_hf_weights
 
             load_hf_weights(self.model, Path(c.model.name))
-        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, opt_group, opt_world,
+        self.optimizer = FlatOptimizer(self.model.trainable, c.optim, c.max_grad_norm, shard_group, shard_world,
                                        fabric=self.fabric, expert_flat=self.model.expert_flat,
                                        ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size,
-                                       norm_fabric=self.norm_fabric)
+                                       norm_fabric=self.norm_fabric,
+                                       replicate_group=self.groups.replicate if hsdp else None)
         self.engine = Engine(self.model, self.optimizer.adamw.h, opt_group, opt_world)
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
