@@ -49,6 +49,9 @@ class RLTrainer:
 
     def setup(self, world=None, model=None) -> "RLTrainer":
         c = self.config
+        if c.fsdp.shard_params:
+            raise NotImplementedError("fsdp.shard_params (ZeRO-3) is available for SFT; the RL trainer keeps the "
+                                      "bf16 weights resident (the generator and the policy export read them whole)")
         torch.manual_seed(c.seed)
         self.world = world or init_distributed(c.fsdp.backend, timeout_s=c.dist_timeout_seconds)
         w = self.world
