@@ -123,3 +123,71 @@ def test_sft_cli_trains_a_generic_preset(tmp_path):
     rows = [json.loads(line) for line in (out / "metrics.jsonl").read_text().splitlines()]
     assert [x["step"] for x in rows] == [1, 2, 3]
     assert (out / "checkpoint-3" / "STABLE").exists()
+
+
+def test_hf_generator_greedy_stops_and_masks():
+    """Rollouts for a generic model: greedy continuation equals step-by-step
+    argmax of the module's own logits (left padding does not leak), stop
+    tokens end a row after min_tokens, truncated sampling returns the kept
+    token ids, and a seed makes sampling reproducible."""
+    from wavelet_b200.inference.engine import SamplingParams
+    from wavelet_b200.inference.hf_generator import HFGenerator, make_generator
+
+    cfg = resolve_arch("tiny-llama")
+    m = build_model(cfg, "cpu", torch.float32, seed=2)
+    g = make_generator(m, max_num_seqs=4, max_model_len=64)
+    assert isinstance(g, HFGenerator)
+    prompts = [[5, 9, 13], [7, 3, 8, 11, 2, 4], [6]]
+    out = g.generate(prompts, SamplingParams(temperature=0.0, max_tokens=6))
+    for c in out:
+        ids = list(c.prompt_ids)
+        for t in c.token_ids:
+            with torch.no_grad():
+                want = int(m.module(input_ids=torch.tensor([ids]), use_cache=False).logits[0, -1].argmax())
+            assert t == want
+            ids.append(t)
+        assert c.finish_reason == "length" and len(c.logprobs) == 6
+    first = out[0].token_ids[1]
+    stopped = g.generate([prompts[0]], SamplingParams(temperature=0.0, max_tokens=6, stop_token_ids=[first]))[0]
+    assert stopped.token_ids == out[0].token_ids[:2] and stopped.finish_reason == "stop"
+    held = g.generate([prompts[0]], SamplingParams(temperature=0.0, max_tokens=6, stop_token_ids=[first],
+                                                   min_tokens=4))[0]
+    assert len(held.token_ids) > 2
+    p = SamplingParams(temperature=1.0, top_k=5, max_tokens=5, n=3, seed=11, return_sampling_mask=True)
+    a, b = g.generate(prompts, p), g.generate(prompts, p)
+    assert [c.token_ids for c in a] == [c.token_ids for c in b]
+    assert all(len(mk) == 5 and t in mk for c in a for mk, t in zip(c.sampling_mask, c.token_ids))
+    assert [(c.prompt_index, c.sample_index) for c in a] == [(i, j) for i in range(3) for j in range(3)]
+
+
+def test_integrated_rl_trains_a_generic_model(tmp_path):
+    root = Path(__file__).resolve().parents[1]
+    cfg = tmp_path / "rl.yaml"
+    cfg.write_text(f"""model:
+  name: tiny-llama
+  random_init: true
+data:
+  source: fake
+  seq_len: 96
+  fake_vocab_size: 64
+  fake_prompt_len: 8
+algo:
+  type: grpo
+reward:
+  mode: reverse_match
+orchestrator:
+  examples_per_step: 2
+  rollouts_per_example: 4
+inference:
+  sampling:
+    max_completion_tokens: 8
+lora: null
+max_steps: 2
+output_dir: {tmp_path / 'out'}
+""")
+    env = {**os.environ, "WAVELET_FORCE_CPU": "1"}
+    r = subprocess.run([sys.executable, "-m", "wavelet_b200", "rl", "@", str(cfg)], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    rows = [json.loads(line) for line in (tmp_path / "out" / "metrics.jsonl").read_text().splitlines()]
+    assert [x["step"] for x in rows] == [1, 2] and "reward/mean" in rows[0]

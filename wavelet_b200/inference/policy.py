@@ -101,7 +101,7 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
 
         from ..models.config import resolve_arch
         from ..models.qwen import build_model
-        from .engine import Generator
+        from .hf_generator import make_generator
 
         c = self.config
         if self.model is None:
@@ -109,9 +109,9 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
             arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
             self.model = build_model(arch, dev, seed=c.seed, with_grad=False, with_optimizer=False)
         v = c.inference.vllm
-        self.generator = Generator(self.model, max_num_seqs=v.max_num_seqs,
-                                   max_model_len=v.max_model_len or c.data.seq_len,
-                                   gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
+        self.generator = make_generator(self.model, max_num_seqs=v.max_num_seqs,
+                                        max_model_len=v.max_model_len or c.data.seq_len,
+                                        gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
 
     def load_policy(self, policy_dir: Path, *, step: int) -> None:
         from ..transport.policy import load_policy_into

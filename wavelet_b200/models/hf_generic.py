@@ -12,10 +12,11 @@ store so the sharded AdamW, checkpoints, the chunked LM-head loss and the
 policy exporters apply unchanged.  Autograd gradients are added into the
 store's fp32 gradient buffer after each backward (``collect_cpu_grads``).
 
-Not supported with this adapter: tensor, expert and context parallelism,
-LoRA / QLoRA, the native generator (rollouts come from an inference server),
-and heads the fused loss cannot express (an LM-head bias, logit soft-capping
-or scaling).
+Rollouts for these models come from ``inference.hf_generator`` (the
+module's own KV cache, the native generator's sampling semantics).  Not
+supported with this adapter: tensor, expert and context parallelism, LoRA /
+QLoRA, and heads the fused loss cannot express (an LM-head bias, logit
+soft-capping or scaling).
 """
 
 from __future__ import annotations

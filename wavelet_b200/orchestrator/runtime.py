@@ -79,7 +79,6 @@ class IntegratedRunner:
         self.cfg = cfg
 
     def setup(self) -> "IntegratedRunner":
-        from ..inference.engine import Generator
         from ..trainer.rl import RLTrainer
 
         c = self.cfg
@@ -110,8 +109,10 @@ class IntegratedRunner:
                                     with_grad=False, with_optimizer=False)
             self.policy_sync = ExpertPolicySync(t.model, gen_model, t.ep_fabric)
             self.policy_sync.refresh()
-        self.engine = Generator(gen_model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
-                                gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
+        from ..inference.hf_generator import make_generator
+
+        self.engine = make_generator(gen_model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
+                                     gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
         self.sender = FileSystemRolloutSender(out, c.transport) if self.world.rank == 0 else None
         # batches past a resumed step are stale
         if self.world.rank == 0 and t.step > 0:
