@@ -8,8 +8,10 @@ in all of them; vision tensors are concatenated along their first dimension
 (patches of all images in batch order, as vision towers consume them), and
 ``mm_token_type_ids`` (one id per input token) is right-padded with zeros to
 ``max_len`` and stacked.  Unknown field names are rejected so that a processor
-change cannot silently drop inputs.  The trainer's decoder models are
-text-only; these fields are carried for models with a vision tower.
+change cannot silently drop inputs.  ``pack_multimodal_row`` does the same for
+one packed row of documents (vision tensors concatenated in document order,
+the number of images of every document alongside), which the vision-language
+models of ``models.hf_generic`` consume.
 """
 
 from __future__ import annotations
@@ -47,4 +49,36 @@ def collate_multimodal_fields(samples: list[dict[str, Any]], max_len: int) -> di
                 out[name] = torch.cat(ts, 0)
             except RuntimeError as e:
                 raise ValueError(f"Multimodal field {name!r} has incompatible shapes") from e
+    return out
+
+
+def as_mm_tensors(kw: dict[str, Any] | None) -> dict[str, torch.Tensor] | None:
+    """Processor fields of one sample as tensors (JSON rows carry lists)."""
+    if not kw:
+        return None
+    bad = sorted(set(kw) - PROCESSOR_FIELDS)
+    if bad:
+        raise ValueError(f"Unsupported processor fields: {bad}")
+    out = {}
+    for k, v in kw.items():
+        t = torch.as_tensor(v)
+        out[k] = t.long() if k.endswith(("_thw", "_sizes")) or k in TOKEN_FIELDS else t.float() if t.is_floating_point() else t
+    return out
+
+
+def pack_multimodal_row(per_doc: list[dict[str, torch.Tensor] | None]) -> dict[str, Any] | None:
+    """The processor fields of a packed row of documents: vision tensors
+    concatenated along their first dimension in document order,
+    ``doc_images`` = images (grid rows) per document."""
+    if not any(per_doc):
+        return None
+    names = sorted(set().union(*[set(d) for d in per_doc if d]))
+    out: dict[str, Any] = {}
+    for n in names:
+        if n in TOKEN_FIELDS:
+            raise ValueError(f"{n} is not supported in packed rows")
+        parts = [d[n] for d in per_doc if d and n in d]
+        out[n] = torch.cat(parts, 0)
+    grid = "image_grid_thw"
+    out["doc_images"] = [int(d[grid].shape[0]) if d and grid in d else 0 for d in per_doc]
     return out

@@ -36,6 +36,7 @@ class Sample:
     input_ids: list[int]
     loss_mask: list[int]
     source: str = "local"
+    mm: dict | None = None  # processor fields of the sample's images (pre-tokenized multimodal rows)
 
 
 # ------------------------------------------------------------------- sources
@@ -183,6 +184,30 @@ def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
     return Sample(ids, mask)
 
 
+def _pretokenized(r: dict[str, Any]) -> Sample:
+    """A row that is already token ids (``input_ids``, optional ``loss_mask``
+    or ``labels`` with -100 for context) and optional ``mm_kwargs`` (the
+    processor's image fields, image placeholder tokens already expanded)."""
+    from .multimodal import as_mm_tensors
+
+    ids = [int(t) for t in r["input_ids"]]
+    if r.get("loss_mask") is not None:
+        mask = [int(bool(x)) for x in r["loss_mask"]]
+    elif r.get("labels") is not None:
+        mask = [int(x != -100) for x in r["labels"]]
+    else:
+        mask = [1] * len(ids)
+    if len(mask) != len(ids):
+        raise ValueError("a pre-tokenized row needs one loss-mask entry per token")
+    return Sample(ids, mask, mm=as_mm_tensors(r.get("mm_kwargs")))
+
+
+def _check_fits(s: Sample, n: int) -> None:
+    if s.mm and len(s.input_ids) > n:
+        raise ValueError(f"a sample with image inputs has {len(s.input_ids)} tokens, more than the {n} of a row: "
+                         "cutting it would split its image tokens from their pixels")
+
+
 # ----------------------------------------------------------------- datasets
 @dataclass
 class SFTDataState:
@@ -227,11 +252,14 @@ class SFTDataset:
             if self.cfg.source == "fake":
                 self._samples = self._fake_samples()
             else:
-                if self.tok is None:
-                    raise ValueError("a tokenizer is required for non-fake SFT data")
                 self._samples = []
                 for r in load_records(self.cfg):
-                    s = tokenize_messages(normalize_messages(r, self.cfg), self.tok, self.cfg)
+                    if "input_ids" in r:
+                        s = _pretokenized(r)  # e.g. processor output of a vision-language sample
+                    else:
+                        if self.tok is None:
+                            raise ValueError("a tokenizer is required for non-fake SFT data")
+                        s = tokenize_messages(normalize_messages(r, self.cfg), self.tok, self.cfg)
                     s.source = r.get("__source", "local")
                     if s.input_ids:
                         self._samples.append(s)
@@ -266,7 +294,7 @@ class SFTDataset:
         c = self.cfg
         S = c.seq_len
         mode = getattr(c, "pack_function", "pad")
-        seqs, masks = [], []
+        seqs, masks, mms = [], [], []
         if mode == "cat":
             budget = S * c.micro_batch_size
             used = 0
@@ -284,15 +312,19 @@ class SFTDataset:
                 if take < len(s.input_ids) and used > 0:
                     self._pending_index = idx
                     break
+                _check_fits(s, take)
                 seqs.append(torch.tensor(s.input_ids[:take]))
                 masks.append(torch.tensor(s.loss_mask[:take], dtype=torch.float32))
+                mms.append(s.mm)
                 used += take
         else:
             for _ in range(c.micro_batch_size):
                 s = self._next_sample()
+                _check_fits(s, S)
                 seqs.append(torch.tensor(s.input_ids[:S]))
                 masks.append(torch.tensor(s.loss_mask[:S], dtype=torch.float32))
-        return pack(seqs, masks)
+                mms.append(s.mm)
+        return pack(seqs, masks, mms)
 
     def eval_batches(self, max_batches: int | None = None):
         """One ordered pass over this rank's share of the samples (validation)."""
@@ -303,8 +335,11 @@ class SFTDataset:
             if max_batches is not None and n >= max_batches:
                 return
             grp = mine[i : i + c.micro_batch_size]
+            for s in grp:
+                _check_fits(s, c.seq_len)
             yield pack([torch.tensor(s.input_ids[: c.seq_len]) for s in grp],
-                       [torch.tensor(s.loss_mask[: c.seq_len], dtype=torch.float32) for s in grp])
+                       [torch.tensor(s.loss_mask[: c.seq_len], dtype=torch.float32) for s in grp],
+                       [s.mm for s in grp])
             n += 1
 
     def state_dict(self) -> dict[str, Any]:
@@ -317,9 +352,10 @@ class SFTDataset:
         self._pending_index = sd.get("pending")
 
 
-def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor]) -> PackedBatch:
+def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor], mms: list | None = None) -> PackedBatch:
     """Concatenate sequences; target of position t is token t+1 of the same
-    sequence (last position of each sequence is ignored)."""
+    sequence (last position of each sequence is ignored).  ``mms``: the
+    documents' image fields (``data.multimodal.pack_multimodal_row``)."""
     ids = torch.cat(seqs).long()
     lens = [len(s) for s in seqs]
     cu = torch.zeros(len(seqs) + 1, dtype=torch.int32)
@@ -337,4 +373,9 @@ def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor]) -> PackedBatch:
     tgt = torch.cat(tg)
     mask = torch.cat(mk)
     tgt = torch.where(mask > 0, tgt, torch.full_like(tgt, -100))
-    return PackedBatch(ids, pos, cu, max(lens), tgt, mask)
+    mm = None
+    if mms is not None:
+        from .multimodal import pack_multimodal_row
+
+        mm = pack_multimodal_row(list(mms))
+    return PackedBatch(ids, pos, cu, max(lens), tgt, mask, mm=mm)

@@ -250,6 +250,15 @@ GENERIC_PRESETS: dict[str, dict[str, Any]] = {
                          num_attention_heads=4, num_key_value_heads=2, intermediate_size=256,
                          max_position_embeddings=4096, rms_norm_eps=1e-6, rope_theta=10000.0,
                          tie_word_embeddings=True, sliding_window=None),
+    # a vision-language model (Qwen2.5-VL layout): 14-pixel patches, 2x2 merge
+    "tiny-qwen2.5-vl": dict(
+        model_type="qwen2_5_vl", image_token_id=1000, video_token_id=1001, vision_start_token_id=1002,
+        vision_end_token_id=1003, tie_word_embeddings=False,
+        text_config=dict(vocab_size=1024, hidden_size=128, num_hidden_layers=2, num_attention_heads=4,
+                         num_key_value_heads=2, intermediate_size=256, max_position_embeddings=4096,
+                         rope_scaling={"type": "mrope", "mrope_section": [4, 6, 6]}),
+        vision_config=dict(depth=2, hidden_size=64, intermediate_size=128, num_heads=4, out_hidden_size=128,
+                           patch_size=14, spatial_merge_size=2, temporal_patch_size=2, in_channels=3)),
 }
 
 

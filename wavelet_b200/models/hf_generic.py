@@ -46,7 +46,10 @@ class HFGenericConfig:
             raise ValueError(f"{d['model_type']} has a native decoder; use it")
         self.d = dict(d)
         self.source = source  # local directory with the weights, when loaded from one
-        g = self.d.get
+        # vision-language models nest the decoder's shape under text_config
+        self.is_vlm = isinstance(self.d.get("vision_config"), dict)
+        text = self.d.get("text_config") if isinstance(self.d.get("text_config"), dict) else {}
+        g = (lambda k, default=None: text.get(k, self.d.get(k, default))) if text else self.d.get
         self.vocab_size = int(g("vocab_size"))
         self.hidden_size = int(g("hidden_size") or g("n_embd") or g("d_model"))
         self.num_layers = int(g("num_hidden_layers") or g("n_layer") or g("num_layers"))
@@ -89,6 +92,13 @@ class HFGenericConfig:
         d = {k: v for k, v in self.d.items() if k not in ("architectures", "transformers_version", "torch_dtype")}
         return AutoConfig.for_model(**d)
 
+    def image_tokens(self, grid_thw) -> int:
+        """Placeholder tokens of one image of patch grid (t, h, w) after the
+        vision tower's spatial merge."""
+        merge = int((self.d.get("vision_config") or {}).get("spatial_merge_size", 1))
+        t, h, w = (int(x) for x in grid_thw)
+        return t * h * w // (merge * merge)
+
 
 def load_generic_config(path: Path) -> HFGenericConfig:
     p = Path(path)
@@ -113,15 +123,15 @@ class HFCausalLMTrainable:
 
     def __init__(self, cfg: HFGenericConfig, device, dtype=None, dp_rank: int = 0, dp_world: int = 1, seed: int = 0,
                  init: bool = True, with_grad: bool = True, with_optimizer: bool = True):
-        from transformers import AutoModelForCausalLM
+        from transformers import AutoModelForCausalLM, AutoModelForImageTextToText
 
         self.cfg = cfg
         self.device = torch.device(device)
         dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
         torch.manual_seed(seed)
+        auto = AutoModelForImageTextToText if cfg.is_vlm else AutoModelForCausalLM
         with torch.device(self.device):
-            module = AutoModelForCausalLM.from_config(cfg.transformers_config(),
-                                                      attn_implementation=_attn_impl(self.device))
+            module = auto.from_config(cfg.transformers_config(), attn_implementation=_attn_impl(self.device))
         self.module = module.to(dtype)
         self.module.train()
         out = self.module.get_output_embeddings()
@@ -178,11 +188,43 @@ class HFCausalLMTrainable:
     def hidden(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
         """Final hidden states [T, H] of one packed row: per-document
         position ids make transformers mask across document boundaries."""
+        if self.cfg.is_vlm:
+            return self._hidden_vlm(input_ids, batch)
         ids = input_ids.reshape(1, -1).to(self.device)
         pos = batch.pos.reshape(1, -1).to(torch.int64)
         out = self.module.base_model(input_ids=ids, position_ids=pos, use_cache=False)
         h = out.last_hidden_state if hasattr(out, "last_hidden_state") else out[0]
         return h.reshape(ids.shape[1], -1)
+
+    def _hidden_vlm(self, input_ids: torch.Tensor, batch: BatchCtx) -> torch.Tensor:
+        """Vision-language models compute their own (multimodal rotary)
+        positions from a document's tokens and image grids, so each document
+        of the row runs on its own with its images (``doc_images`` of them,
+        in order: pixel rows = t * h * w patches per image)."""
+        ids = input_ids.reshape(-1).to(self.device)
+        cu = batch.cu_seqlens.tolist()
+        mm = batch.mm or {}
+        pix, grid = mm.get("pixel_values"), mm.get("image_grid_thw")
+        per_doc = mm.get("doc_images") or [0] * (len(cu) - 1)
+        img_tok = self.cfg.d.get("image_token_id")
+        outs, gi, pi = [], 0, 0
+        for d in range(len(cu) - 1):
+            doc = ids[cu[d]:cu[d + 1]]
+            kw = {}
+            k = int(per_doc[d])
+            if k:
+                g = grid[gi:gi + k]
+                n = int(g.prod(-1).sum())
+                want = sum(self.cfg.image_tokens(row) for row in g.tolist())
+                if img_tok is not None and int((doc == img_tok).sum()) != want:
+                    raise ValueError(f"document {d} has {int((doc == img_tok).sum())} image tokens for images "
+                                     f"that need {want}")
+                kw = {"pixel_values": pix[pi:pi + n].to(self.module.dtype), "image_grid_thw": g}
+                gi, pi = gi + k, pi + n
+            out = self.module.base_model(input_ids=doc[None], use_cache=False, **kw)
+            h = out.last_hidden_state if hasattr(out, "last_hidden_state") else out[0]
+            outs.append(h[0])
+        return torch.cat(outs, 0)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         return h @ self.head_weight().t()

@@ -42,6 +42,7 @@ class BatchCtx:
     max_seqlen: int
     inv_freq: torch.Tensor  # fp32 [head_dim/2]
     cp: Any = None  # parallel.context_parallel.CPPlan: attention over the CP group's full sequences
+    mm: Any = None  # processor fields of the row's images (vision-language models)
 
 
 def _lin(x, w, ad, bias=None, res=None):

@@ -28,8 +28,14 @@ class PackedBatch:
     targets: torch.Tensor  # int64 [T], -100 = ignore
     loss_mask: torch.Tensor  # float [T]
     cp: Any = None  # parallel.context_parallel.CPPlan of a context-parallel shard
+    # processor fields of the row's images (pixel_values, image_grid_thw, ...)
+    # and ``doc_images``: images per document, in document order
+    mm: dict | None = None
 
     def to(self, device, non_blocking=True) -> "PackedBatch":
+        mm = None
+        if self.mm is not None:
+            mm = {k: (v.to(device, non_blocking=non_blocking) if torch.is_tensor(v) else v) for k, v in self.mm.items()}
         return PackedBatch(
             self.input_ids.to(device, non_blocking=non_blocking),
             self.position_ids.to(device, non_blocking=non_blocking),
@@ -38,6 +44,7 @@ class PackedBatch:
             self.targets.to(device, non_blocking=non_blocking),
             self.loss_mask.to(device, non_blocking=non_blocking),
             None if self.cp is None else self.cp.to(device),
+            mm,
         )
 
     @property
@@ -45,13 +52,16 @@ class PackedBatch:
         return int(self.input_ids.numel())
 
     def pin_memory(self) -> "PackedBatch":
+        mm = None if self.mm is None else {k: (v.pin_memory() if torch.is_tensor(v) else v) for k, v in self.mm.items()}
         return PackedBatch(
             self.input_ids.pin_memory(), self.position_ids.pin_memory(), self.cu_seqlens.pin_memory(),
-            self.max_seqlen, self.targets.pin_memory(), self.loss_mask.pin_memory(), self.cp,
+            self.max_seqlen, self.targets.pin_memory(), self.loss_mask.pin_memory(), self.cp, mm,
         )
 
     def nbytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self.input_ids, self.position_ids, self.cu_seqlens, self.targets, self.loss_mask))
+        ts = [self.input_ids, self.position_ids, self.cu_seqlens, self.targets, self.loss_mask]
+        ts += [v for v in (self.mm or {}).values() if torch.is_tensor(v)]
+        return sum(t.numel() * t.element_size() for t in ts)
 
 
 class Engine:
@@ -77,6 +87,15 @@ class Engine:
         self.dp_world = dp_world
         self.chunk = lm_head_chunk
 
+    def _ctx(self, b: PackedBatch):
+        m = self.model
+        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
+        if b.mm is not None:
+            if not getattr(m.cfg, "is_vlm", False):
+                raise ValueError("the batch carries image inputs but the model has no vision tower")
+            ctx.mm = b.mm
+        return ctx
+
     # --------------------------------------------------------------- SFT
     def sft_micro_step(self, b: PackedBatch, token_scale: float) -> torch.Tensor:
         """Forward + backward of the token-normalised CE on one micro-batch.
@@ -87,7 +106,7 @@ class Engine:
         Returns the (scaled) loss contribution as a device scalar.
         """
         m = self.model
-        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
+        ctx = self._ctx(b)
         h = m.hidden(b.input_ids, ctx)
         weights = b.loss_mask.float() * token_scale
         with nvtx.range("lm_head.loss"):
@@ -103,7 +122,7 @@ class Engine:
     def sft_eval(self, b: PackedBatch) -> tuple[torch.Tensor, float]:
         """Forward-only masked CE sum and loss-token count of one micro-batch."""
         m = self.model
-        ctx = m.batch_ctx(b.position_ids, b.cu_seqlens, b.max_seqlen, cp=b.cp)
+        ctx = self._ctx(b)
         h = m.hidden(b.input_ids, ctx)
         valid = (b.targets >= 0).float() * b.loss_mask.float()
         lp, _ = lm_head.logprob_entropy(h.detach(), m.head_weight(), b.targets.clamp_min(0), 1.0,
