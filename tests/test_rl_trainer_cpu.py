@@ -207,7 +207,3 @@ def test_chunked_publisher_queue_layout(tmp_path):
     mans = [sch.sender.stable_batch(s).manifest for s in range(6)]
     assert [(mm.optimizer_step, mm.chunk_index) for mm in mans] == [(0, 0), (0, 1), (0, 2), (1, 0), (1, 1), (1, 2)]
 
-
-def test_sharded_parameters_are_refused_for_rl(tmp_path):
-    with pytest.raises(NotImplementedError, match="shard_params"):
-        _trainer(tmp_path, fsdp={"shard_params": True})

@@ -91,3 +91,59 @@ def test_zero3_matches_replicated_weights(tmp_path, preset):
         assert b["master_equal"]
         for k in b["full"]:
             torch.testing.assert_close(b["reloaded"][k], b["full"][k], rtol=0, atol=0, msg=k)
+
+
+def _export_worker(rank, world, init_file, out_dir, res):
+    os.environ["WAVELET_FORCE_CPU"] = "1"
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    from pathlib import Path
+
+    from wavelet_b200.configs.config import RLPolicyTransferConfig
+    from wavelet_b200.models.config import PRESETS
+    from wavelet_b200.models.qwen import build_model
+    from wavelet_b200.parallel.zero3 import ParamGatherer, ShardedPolicySync
+    from wavelet_b200.transport.peer_policy import apply_segments, push_segments
+    from wavelet_b200.transport.policy import PolicyExporter
+
+    cfg = PRESETS["tiny"]
+    m = build_model(cfg, "cpu", torch.float32, dp_rank=rank, dp_world=world, seed=8, shard_params=True)
+    ParamGatherer(m, group=dist.group.WORLD)
+    # filesystem policy export of the shards: every rank gathers, rank 0 writes
+    d = PolicyExporter(Path(out_dir), RLPolicyTransferConfig(), rank=rank, world=world).export(m, 3)
+    # a full generator replica refreshed from the shards
+    gen = build_model(cfg, "cpu", torch.float32, seed=99, with_grad=False, with_optimizer=False)
+    ShardedPolicySync(m, gen).refresh()
+    # the peer push of a ZeRO-3 rank: exactly its shard
+    dst = torch.zeros_like(gen.flat.compute)
+    for k, segs in push_segments(m, dict(gen.flat.offsets)).items():
+        apply_segments(m.flat.compute, segs, dst)
+    torch.save({"dir": str(d) if d else None, "gen": {n: gen.flat.view(n).clone() for n in gen.flat.names()},
+                "pushed": dst}, f"{res}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+    os._exit(0)
+
+
+def test_zero3_policy_export_replica_refresh_and_shard_push(tmp_path):
+    from wavelet_b200.models.config import PRESETS
+    from wavelet_b200.models.hf_io import load_hf_weights
+    from wavelet_b200.models.qwen import build_model
+
+    with tempfile.TemporaryDirectory() as d:
+        res = os.path.join(d, "res")
+        mp.spawn(_export_worker, args=(2, os.path.join(d, "init"), str(tmp_path / "run"), res), nprocs=2, join=True)
+        r = [torch.load(f"{res}.{k}") for k in range(2)]
+    ref = build_model(PRESETS["tiny"], "cpu", torch.float32, seed=8)  # the same init, replicated
+    for k in range(2):
+        for n in ref.flat.names():
+            torch.testing.assert_close(r[k]["gen"][n], ref.flat.view(n), rtol=0, atol=0, msg=n)
+    # the two ranks' pushes together make every parameter
+    both = r[0]["pushed"] + r[1]["pushed"]
+    for n, (off, k) in ref.flat.offsets.items():
+        torch.testing.assert_close(both[off:off + k], ref.flat.compute[off:off + k], rtol=0, atol=0, msg=n)
+    loaded = build_model(PRESETS["tiny"], "cpu", torch.float32, seed=77)
+    load_hf_weights(loaded, os.path.join(r[0]["dir"], "model"))
+    for n in ref.flat.names():  # the export is bf16
+        want = ref.flat.view(n).to(torch.bfloat16).float()
+        torch.testing.assert_close(loaded.flat.view(n), want, rtol=0, atol=0, msg=n)
+    assert r[1]["dir"] is None

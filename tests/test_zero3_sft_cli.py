@@ -82,3 +82,46 @@ def test_hybrid_sharding_matches_replicated_weights(tmp_path):
     for x, y in zip(a, b):
         assert abs(x - y) <= 1e-4 * abs(x), (a, b)
     assert (tmp_path / "hsdp" / "checkpoint-3" / "trainer" / "model.safetensors").exists()
+
+
+@pytest.mark.integration
+def test_integrated_rl_with_sharded_parameters(tmp_path):
+    """`wavelet rl` on 2 gloo ranks with fsdp.shard_params: the sharded
+    trainer trains and its full generator replica is refreshed every step."""
+    cfg = tmp_path / "rl.yaml"
+    cfg.write_text(f"""model:
+  name: tiny
+  random_init: true
+data:
+  source: fake
+  seq_len: 128
+  fake_vocab_size: 64
+  fake_prompt_len: 8
+algo:
+  type: grpo
+reward:
+  mode: reverse_match
+orchestrator:
+  examples_per_step: 4
+  rollouts_per_example: 4
+inference:
+  sampling:
+    max_completion_tokens: 8
+fsdp:
+  backend: gloo
+  shard_params: true
+lora: null
+max_steps: 2
+output_dir: {tmp_path / 'out'}
+""")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = {**os.environ, "WAVELET_FORCE_CPU": "1"}
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "wavelet_b200", "rl", "@",
+                        str(cfg)], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    rows = [json.loads(line) for line in (tmp_path / "out" / "metrics.jsonl").read_text().splitlines()]
+    assert [x["step"] for x in rows] == [1, 2]

@@ -414,6 +414,8 @@ class CausalLM:
         W = self.head_weight()
         if h.is_cuda:
             return ops.gemm(h.contiguous(), W)
+        if self.flat.sharded_compute:  # the staged head (ZeRO-3)
+            return h @ W.t()
         off, k = self.flat.offsets[self.head_name]
         Wv = self.flat.compute[off : off + k].view(W.shape)
         return h @ Wv.t()

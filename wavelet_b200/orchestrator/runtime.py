@@ -109,6 +109,16 @@ class IntegratedRunner:
                                     with_grad=False, with_optimizer=False)
             self.policy_sync = ExpertPolicySync(t.model, gen_model, t.ep_fabric)
             self.policy_sync.refresh()
+        elif t.model.flat.sharded_compute:
+            # sharded (ZeRO-3) trainer: rollouts run on a full bf16 replica
+            # refreshed from the shards after every optimizer step
+            from ..models.qwen import build_model
+            from ..parallel.zero3 import ShardedPolicySync
+
+            gen_model = build_model(t.model.cfg, t.model.device, t.model.flat.compute_dtype, init=False,
+                                    with_grad=False, with_optimizer=False)
+            self.policy_sync = ShardedPolicySync(t.model, gen_model)
+            self.policy_sync.refresh()
         from ..inference.hf_generator import make_generator
 
         self.engine = make_generator(gen_model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,

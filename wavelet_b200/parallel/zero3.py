@@ -239,6 +239,24 @@ class ParamGatherer:
 
     # ------------------------------------------------------------- full state
     @torch.no_grad()
+    def gather_into(self, dst_flat) -> None:
+        """Collective: every rank writes the full weights into ``dst_flat``
+        (a replicated store of the same layout, e.g. a generator replica):
+        one broadcast per owner segment straight into the destination."""
+        flat = self.flat
+        dst = dst_flat.compute
+        if dst_flat.offsets != flat.offsets:
+            raise ValueError("the destination store has another layout")
+        for u in [self.edge] + self.layers:
+            for lo, hi, _ in u.ranges:
+                for r, a, b in self._owners(lo, hi):
+                    out = dst[a:b]
+                    if r == self.rank:
+                        out.copy_(flat.compute[a - flat.lo: b - flat.lo])
+                    if self.world > 1:
+                        dist.broadcast(out, src=self.ranks[r], group=self.group)
+
+    @torch.no_grad()
     def full_state(self, keep) -> dict[str, torch.Tensor] | None:
         """Collective: every parameter's full tensor passed through ``keep(name,
         tensor)`` on data-parallel rank 0 (a host copy for a checkpoint); the
@@ -255,3 +273,19 @@ class ParamGatherer:
                     out[n] = keep(n, buf[b0:b0 + k].view(shape))
         self.holds = [None, None]
         return out
+
+
+class ShardedPolicySync:
+    """Generator replica of a ZeRO-3 trainer: a full bf16 store of the same
+    layout refreshed from the shards after each optimizer step (every rank
+    takes part; the reference's rollout engine gets FSDP-gathered weights the
+    same way)."""
+
+    def __init__(self, trainer_model, gen_model):
+        self.t = trainer_model
+        self.g = gen_model
+        if trainer_model.zero3 is None:
+            raise ValueError("the trainer model has no ParamGatherer")
+
+    def refresh(self) -> None:
+        self.t.zero3.gather_into(self.g.flat)

@@ -49,9 +49,6 @@ class RLTrainer:
 
     def setup(self, world=None, model=None) -> "RLTrainer":
         c = self.config
-        if c.fsdp.shard_params:
-            raise NotImplementedError("fsdp.shard_params (ZeRO-3) is available for SFT; the RL trainer keeps the "
-                                      "bf16 weights resident (the generator and the policy export read them whole)")
         torch.manual_seed(c.seed)
         self.world = world or init_distributed(c.fsdp.backend, timeout_s=c.dist_timeout_seconds)
         w = self.world
@@ -77,7 +74,12 @@ class RLTrainer:
                                 lora=c.lora, load_in_4bit=c.model.load_in_4bit, lora_seed=c.seed,
                                 ep=(dims.ep, self.groups.ep_rank, self.groups.ep_dp_rank, self.groups.ep_dp_size)
                                 if dims.ep > 1 else None,
-                                tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None)
+                                tp=(dims.tp, self.groups.tp_rank) if dims.tp > 1 else None,
+                                shard_params=c.fsdp.shard_params)
+            if c.fsdp.shard_params:
+                from ..parallel.zero3 import ParamGatherer
+
+                ParamGatherer(model, group=opt_group if opt_world > 1 else None)
             model.tp_group = self.groups.tp
             self.tp_fabric = None
             if dims.tp > 1 and w.device.type == "cuda" and c.fsdp.backend != "gloo" and c.fsdp.tp_reduce == "fabric":

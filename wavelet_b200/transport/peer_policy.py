@@ -113,6 +113,21 @@ def push_segments(model, gen_offsets: dict[str, tuple[int, int]], rank: int = 0,
         raise NotImplementedError("device policy transfer moves full-model weights; LoRA / NF4 trainers use the "
                                   "filesystem transfer (the adapter is small)")
     cfg = model.cfg
+    if getattr(model.flat, "sharded_compute", False):
+        # ZeRO-3: each rank pushes exactly the elements of its shard
+        flat = model.flat
+        segs = []
+        for name, (goff, gn) in gen_offsets.items():
+            if name not in flat.offsets:
+                raise KeyError(f"generator parameter {name} is not held by the trainer")
+            off, n = flat.offsets[name]
+            if n != gn:
+                raise ValueError(f"{name}: trainer has {n} elements, the generator {gn}")
+            r = flat.local_range(off, n)
+            if r is not None:
+                ll, lh, tl, th = r
+                segs.append(_contig(ll, goff + tl, lh - ll))
+        return {"flat": segs} if segs else {}
     tp, tr = getattr(model, "tp_size", 1), getattr(model, "tp_rank", 0)
     split = set(tp_slicers(cfg, tp, tr)) if tp > 1 else set()
     ef = getattr(model, "expert_flat", None)

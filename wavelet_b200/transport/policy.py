@@ -54,6 +54,8 @@ class PolicyExporter:
     def export(self, model, step: int) -> Path | None:
         if self.cfg.type == "nccl":
             return self._export_device(model, step)
+        if getattr(model.flat, "sharded_compute", False) and not (self.lora is not None and self.cfg.lightweight_lora):
+            model = _gathered_view(model)  # every rank takes part in the gathers; rank 0 writes
         if self.rank != 0:
             return None
         d = step_dir(self.policy_dir, step)
@@ -175,6 +177,35 @@ class PolicyExporter:
         steps = stable_steps(self.policy_dir)
         for s in steps[: -self.cfg.keep_last] if len(steps) > self.cfg.keep_last else []:
             shutil.rmtree(step_dir(self.policy_dir, s), ignore_errors=True)
+
+
+class _FullStore:
+    """Read-only flat-store stand-in over gathered full tensors."""
+
+    def __init__(self, tensors: dict, offsets: dict):
+        self._t = tensors
+        self.offsets = offsets
+
+    def view(self, name: str):
+        return self._t[name]
+
+    def names(self):
+        return list(self._t)
+
+
+class _GatheredModel:
+    def __init__(self, model, tensors: dict):
+        self.cfg = model.cfg
+        self.flat = _FullStore(tensors, model.flat.offsets)
+        self.quant = {}
+        self.lora = None
+
+
+def _gathered_view(model):
+    """Collective: the full weights of a ZeRO-3 model as host tensors on
+    data-parallel rank 0 (a stand-in model the exporters read), None elsewhere."""
+    full = model.zero3.full_state(lambda n, t: t.detach().to("cpu", copy=True))
+    return _GatheredModel(model, full) if full is not None else model
 
 
 class DevicePolicyReceiver:
