@@ -101,18 +101,27 @@ def test_placement_split():
 
 
 @pytest.mark.integration
-def test_process_mode_end_to_end(tmp_path):
+@pytest.mark.parametrize("transfer", ["filesystem", "nccl"])
+def test_process_mode_end_to_end(tmp_path, transfer):
     """launcher.mode=process on CPU: inference server + rl-trainer + rl-inference
-    processes cooperating through HTTP and the filesystem queues."""
+    processes cooperating through HTTP and the filesystem queues.  With
+    policy_transfer.type nccl the weights move as device updates (on the CPU
+    the peer slots cannot cross processes, so the trainer broadcasts over its
+    own gloo group and the rollout role loads every update in order)."""
     import socket
     import subprocess
     import sys
     from pathlib import Path
 
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
+    def free():
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        p = s.getsockname()[1]
+        s.close()
+        return p
+
+    port = free()
+    extra = f"  type: nccl\n  nccl_port: {free()}\n  nccl_timeout_seconds: 120\n" if transfer == "nccl" else ""
     cfg = tmp_path / "rl.yaml"
     cfg.write_text(f"""model:
   name: tiny
@@ -141,7 +150,7 @@ transport:
 policy_transfer:
   poll_interval_seconds: 0.2
   idle_timeout_seconds: 120
-launcher:
+{extra}launcher:
   mode: process
   poll_interval_seconds: 0.5
 lora: null
@@ -159,3 +168,6 @@ output_dir: {tmp_path / 'out'}
     rows = [json.loads(l) for l in (tmp_path / "out" / "metrics.jsonl").read_text().splitlines()]
     assert [x["step"] for x in rows] == [1, 2]
     assert (tmp_path / "out" / "orchestrator_metrics.jsonl").exists()
+    if transfer == "nccl":
+        info = json.loads((tmp_path / "out" / "policies" / "step-000002" / "update_info.json").read_text())
+        assert info["protocol"] == "flat_v1"

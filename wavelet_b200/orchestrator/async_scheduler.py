@@ -291,13 +291,32 @@ class AsyncRolloutScheduler:
         self._after_load(f.result())
         return True
 
+    def _broadcast_updates(self) -> bool:
+        """Device policy updates over the NCCL broadcast (``flat_v1``) are
+        collectives with the trainer: every exported step must be loaded, in
+        order (a peer-memory update or a filesystem snapshot may be skipped)."""
+        if self.cfg.policy_transfer.type != "nccl":
+            return False
+        latest = self.policies.latest()
+        if latest is None:
+            return False
+        try:
+            info = json.loads((latest.step_dir / "update_info.json").read_text())
+        except (OSError, ValueError):
+            return False
+        return info.get("protocol") == "flat_v1"
+
     def _maybe_start_load(self, pool: ThreadPoolExecutor) -> None:
-        """Load the newest snapshot when it is newer than the loaded one."""
+        """Load the newest snapshot when it is newer than the loaded one (the
+        next one in order for broadcast updates)."""
         if self.load_future is not None:
             return
         newest = self._newest_policy()
         if newest is None or (self.loaded is not None and newest <= self.loaded):
             return
+        if self._broadcast_updates():
+            newer = [s for s in stable_steps(self.policies.policy_dir) if self.loaded is None or s > self.loaded]
+            newest = newer[0] if newer else newest
         if self.pending and not self.concurrent_load:
             return  # the engine cannot swap weights under load: wait for a drain
         if self.pending:
@@ -442,8 +461,19 @@ class AsyncRolloutScheduler:
                 else:
                     time.sleep(poll)
             self._finish_load(block=True)
+        if self._broadcast_updates():
+            self._drain_broadcasts(total // self.C)
         self._final_evals(total // self.C)
         return 0
+
+    def _drain_broadcasts(self, total: int) -> None:
+        """Take part in the trainer's remaining broadcast updates (it exports
+        every ``export_every_steps`` up to the last step and waits for us)."""
+        every = max(1, int(getattr(self.cfg.policy_transfer, "export_every_steps", 1) or 1))
+        final = total - total % every
+        while self.loaded is None or self.loaded < final:
+            nxt = 0 if self.loaded is None else self.loaded + every - self.loaded % every
+            self._after_load(self._load(min(nxt, final)))
 
     def pipeline_status(self) -> dict:
         """Snapshot for the periodic status line (read from another thread)."""
