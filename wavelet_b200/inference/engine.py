@@ -35,7 +35,6 @@ from __future__ import annotations
 import math
 import time
 from dataclasses import dataclass, field
-from typing import Any
 
 import numpy as np
 import torch

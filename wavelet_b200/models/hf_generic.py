@@ -21,7 +21,6 @@ soft-capping or scaling).
 
 from __future__ import annotations
 
-import json
 from pathlib import Path
 from typing import Any
 
@@ -98,13 +97,6 @@ class HFGenericConfig:
         merge = int((self.d.get("vision_config") or {}).get("spatial_merge_size", 1))
         t, h, w = (int(x) for x in grid_thw)
         return t * h * w // (merge * merge)
-
-
-def load_generic_config(path: Path) -> HFGenericConfig:
-    p = Path(path)
-    src = p if p.is_dir() else p.parent
-    p = p / "config.json" if p.is_dir() else p
-    return HFGenericConfig(json.loads(p.read_text()), source=str(src))
 
 
 def _attn_impl(device: torch.device) -> str:

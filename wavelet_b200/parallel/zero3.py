@@ -83,7 +83,6 @@ class ParamGatherer:
         model.zero3 = self
         for i, layer in enumerate(model.layers):
             layer.zero3 = self
-        self.gathered_bytes = 0  # per process, for the perf counters
 
     def _unit(self, names: list[str], layer: int | None) -> _Unit:
         u = _Unit(names, layer=layer)
@@ -123,7 +122,6 @@ class ParamGatherer:
                     w = dist.broadcast(dst, src=self.ranks[r], group=self.group, async_op=async_op)
                     if async_op:
                         works.append(w)
-        self.gathered_bytes += u.size * buf.element_size()
         return works
 
     def _bind(self, u: _Unit, buf: torch.Tensor, grads: torch.Tensor | None) -> None:
