@@ -12,6 +12,14 @@ Cases:
   lm-head           chunked LM-head cross-entropy forward + backward (logit
                     GEMM, softmax stats, in-place dL/dz, dgrad and fp32 wgrad)
   generate          the native generator end to end (prefill + decode)
+  router            MoE router (softmax, top-k, renormalised weights, expert
+                    counts) against the same in torch
+  sampling          top-k / top-p thresholds + Gumbel sampling of a decode
+                    batch against torch topk / sort / multinomial
+  adamw8            8-bit-moment AdamW and fp32 AdamW flat kernels against
+                    torch's fused AdamW over the same elements
+  policy-push       reshard + cast push of a policy (local destination)
+                    against torch copies of the same segments
 """
 
 from __future__ import annotations
@@ -142,8 +150,132 @@ def lm_head(a) -> dict:
             "tflops": flops / (ms * 1e9)}
 
 
+def router(a) -> dict:
+    """``--m`` tokens routed over ``--n`` experts, top ``--k``."""
+    from .. import ops
+
+    T, E, k = a.m, a.n, a.k
+    logits = torch.randn(T, E, device="cuda")
+    probs = torch.empty(T, E, device="cuda")
+    topi = torch.empty(T, k, device="cuda", dtype=torch.int64)
+    topv = torch.empty(T, k, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    ssum = torch.empty(T, device="cuda")
+    counts = torch.zeros(E, device="cuda", dtype=torch.int32)
+
+    def ours():
+        counts.zero_()
+        ops.ext().moe_route(logits, k, True, True, probs, topi, topv, w, ssum, counts)
+
+    def torch_ref():
+        p = torch.softmax(logits.bfloat16().float(), -1)
+        v, i = torch.topk(p, k, -1)
+        s_ = v.sum(-1, keepdim=True)
+        return v / s_, i, torch.bincount(i.reshape(-1), minlength=E)
+
+    ms, ms_t = _time(ours, a.iters), _time(torch_ref, a.iters)
+    _, i_t, c_t = torch_ref()
+    ours()
+    same = bool(torch.equal(counts.long(), c_t)) and bool(torch.equal(topi, i_t))
+    return {"case": "router", "tokens": T, "experts": E, "top_k": k, "us": ms * 1e3, "torch_us": ms_t * 1e3,
+            "speedup_vs_torch": ms_t / ms, "same_as_torch": same}
+
+
+def sampling(a) -> dict:
+    """A decode step's sampling: ``--batch`` rows of ``--n`` logits, top-k
+    ``--k`` and top-p 0.9 at temperature 1."""
+    from .. import ops
+    from ..inference.engine import sampling_thresholds_reference
+
+    B, V, K = a.batch, a.n, a.k
+    z = (torch.randn(B, V, device="cuda") * 3).bfloat16()
+    inv = torch.ones(B, device="cuda")
+    tk = torch.full((B,), K, device="cuda", dtype=torch.int32)
+    tp = torch.full((B,), 0.9, device="cuda")
+    th = torch.empty(B, device="cuda")
+    tok = torch.empty(B, device="cuda", dtype=torch.long)
+    lp = torch.empty(B, device="cuda")
+    rows = torch.arange(B, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(0)
+
+    def ours():
+        ops.ext().sample_thresholds(z, tk, tp, inv, th)
+        ops.ext().sample_tokens(z, inv, th, 0.0, 7, rows, tok, lp, None)
+
+    def torch_ref():  # thresholds with topk / sort, then masked softmax + multinomial
+        zf = z.float()
+        kth = torch.topk(zf, K, -1).values[:, -1:]
+        srt = torch.sort(zf, -1, descending=True).values
+        cum = torch.softmax(srt, -1).cumsum(-1)
+        idx = (cum < 0.9).sum(-1, keepdim=True).clamp_max(V - 1)
+        pth = srt.gather(1, idx)
+        keep = zf >= torch.maximum(kth, pth)
+        p = torch.softmax(zf.masked_fill(~keep, float("-inf")), -1)
+        t = torch.multinomial(p, 1, generator=gen)
+        return t, torch.log(p.gather(1, t))
+
+    ms, ms_t = _time(ours, a.iters), _time(torch_ref, a.iters)
+    ours()
+    ref = sampling_thresholds_reference(z[:4], [K] * 4, [0.9] * 4, inv[:4])
+    return {"case": "sampling", "rows": B, "vocab": V, "top_k": K, "top_p": 0.9, "us": ms * 1e3,
+            "torch_us": ms_t * 1e3, "speedup_vs_torch": ms_t / ms,
+            "thresholds_match_reference": bool(torch.equal(th[:4], ref.to(th.device)))}
+
+
+def adamw8(a) -> dict:
+    """``--m`` x 2^20 parameters: fp32 master + bf16 shadow, two moments."""
+    from .. import ops
+
+    n = a.m << 20
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda") * 1e-3
+    p16 = p.bfloat16()
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    nb = (n + ops.Q8_BLOCK - 1) // ops.Q8_BLOCK
+    m8, v8 = torch.zeros(n, device="cuda", dtype=torch.int8), torch.zeros(n, device="cuda", dtype=torch.int8)
+    am, av = torch.zeros(nb, device="cuda"), torch.zeros(nb, device="cuda")
+    kw = dict(lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, step=3)
+    ms8 = _time(lambda: ops.adamw8_flat_(p, g, m8, v8, am, av, p16, **kw), a.iters)
+    ms32 = _time(lambda: ops.adamw_flat_(p, g, m, v, p16, **kw), a.iters)
+    tp = torch.nn.Parameter(p.clone())
+    tp.grad = g.clone()
+    opt = torch.optim.AdamW([tp], lr=1e-4, weight_decay=0.01, fused=True)
+    ms_t = _time(opt.step, a.iters)
+    # bytes moved: p (rw fp32), g (r fp32), p16 (w), moments (rw) — 8-bit codes + block scales vs fp32
+    b8 = n * (4 * 2 + 4 + 2 + 1 * 4) + nb * 4 * 4
+    b32 = n * (4 * 2 + 4 + 2 + 4 * 4)
+    return {"case": "adamw8", "params": n, "adamw8_ms": ms8, "adamw_fp32_ms": ms32, "torch_fused_adamw_ms": ms_t,
+            "adamw8_GB/s": b8 / ms8 / 1e6, "adamw_fp32_GB/s": b32 / ms32 / 1e6,
+            "state_bytes_per_param": {"adamw8": 4 + 2 + 2 * 4 / ops.Q8_BLOCK, "fp32": 12}}
+
+
+def policy_push(a) -> dict:
+    """Push a ``--model`` policy from one flat store into another of the same
+    layout on this GPU (each parameter a segment), bf16 -> bf16."""
+    from .. import ops
+    from ..models.config import resolve_arch
+    from ..models.qwen import build_model
+    from ..transport.peer_policy import push_segments
+
+    m = build_model(resolve_arch(a.model), "cuda", torch.bfloat16, seed=0, with_grad=False, with_optimizer=False)
+    dst = torch.empty_like(m.flat.compute)
+    segs = push_segments(m, dict(m.flat.offsets))["flat"]
+    table = torch.tensor(segs, dtype=torch.int64)
+    ms = _time(lambda: ops.ext().policy_push(m.flat.compute, [dst.data_ptr()], dst.numel(), True, table), a.iters)
+    views = [(m.flat.compute[s[0]:s[0] + s[3]], dst[s[1]:s[1] + s[3]]) for s in segs]
+
+    def torch_ref():
+        for src, d in views:
+            d.copy_(src)
+
+    ms_t = _time(torch_ref, a.iters)
+    nbytes = sum(s[2] * s[3] for s in segs) * 2
+    return {"case": "policy-push", "model": a.model, "bytes": nbytes, "segments": len(segs), "ms": ms,
+            "GB/s (read+write)": 2 * nbytes / ms / 1e6, "torch_copies_ms": ms_t, "speedup_vs_torch": ms_t / ms}
+
+
 CASES = {"lm-head": lm_head, "decode-attention": decode_attention, "attention": attention, "gemm": gemm, "nf4-gemm": nf4_gemm,
-         "generate": generate}
+         "generate": generate, "router": router, "sampling": sampling, "adamw8": adamw8, "policy-push": policy_push}
 
 
 def main(argv: list[str] | None = None) -> int:
