@@ -114,12 +114,18 @@ __global__ void __launch_bounds__(256) policy_push_kernel(const TS* __restrict__
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
     const int s = find_segment(prefix, nseg, v);
     const int64_t* g = seg + 6 * (int64_t)s;
-    const int64_t row_v = __ldg(g + 3) / V;
     const int64_t j = v - __ldg(prefix + s);
-    const int64_t r = j / row_v;
-    const int64_t c = (j - r * row_v) * V;
-    const int64_t so = __ldg(g + 0) + r * __ldg(g + 4) + c;
-    const int64_t dof = __ldg(g + 1) + r * __ldg(g + 5) + c;
+    int64_t so, dof;
+    if (__ldg(g + 2) == 1) {  // one contiguous run (most parameters): no division
+      so = __ldg(g + 0) + j * V;
+      dof = __ldg(g + 1) + j * V;
+    } else {
+      const int64_t row_v = __ldg(g + 3) / V;
+      const int64_t r = j / row_v;
+      const int64_t c = (j - r * row_v) * V;
+      so = __ldg(g + 0) + r * __ldg(g + 4) + c;
+      dof = __ldg(g + 1) + r * __ldg(g + 5) + c;
+    }
     if constexpr (V == 1) {
       const TD x = cast1<TS, TD>(src[so]);
       WB_EACH_DST(static_cast<TD*>(dst.p[k])[dof] = x)
