@@ -121,7 +121,18 @@ def load_hf_weights(model, path: Path) -> None:
     for fp in files:
         hf.update(load_file(str(fp)))
     tensors = internal_from_hf(model.cfg, hf)
+    tp = getattr(model, "tp_size", 1)
+    if tp > 1:  # this rank's Megatron part of every split parameter
+        from .qwen import tp_slicers
+
+        sl = tp_slicers(model.cfg, tp, model.tp_rank)
+        tensors = {n: (sl[n.split(".", 1)[-1]][1](t) if n.split(".", 1)[-1] in sl else t) for n, t in tensors.items()}
     model.flat.load_state(tensors)
+    ef = getattr(model, "expert_flat", None)
+    if ef is not None:  # expert parallelism: this rank's block of experts
+        el = model.cfg.num_experts // model.ep_size
+        lo = model.ep_rank * el
+        ef.load_state({n: tensors[n][lo:lo + el] for n in ef.names()})
     if getattr(model, "quant", None):
         from ..ops.nf4 import quantize
 
