@@ -1,0 +1,96 @@
+"""Settings from the reference's schema either act or are named: inert keys
+set away from their default are listed with the reason; keys this framework
+implements take effect (do_sample, max_prompt_tokens, num_generations,
+enforce_eager / cuda_graphs, the LM-head chunk, skip_scheduler, the state
+server's event bound, the tokenizer's chat template); unsupported values are
+refused (repetition_penalty, lora.modules_to_save, generator TP)."""
+
+import pytest
+
+from wavelet_b200.configs.config import RLConfig, SFTConfig
+from wavelet_b200.configs.inert import inert_settings
+
+
+def test_inert_keys_are_named_with_reasons():
+    cfg = RLConfig.model_validate({"inference": {"vllm": {"quantization": "fp8", "enable_fp32_lm_head": False,
+                                                          "gpu_memory_utilization": 0.5}},
+                                   "model": {"compile": True}, "policy_transfer": {"nccl_dtype": "float32"}})
+    msgs = inert_settings(cfg)
+    keys = {m.split("=")[0] for m in msgs}
+    assert keys == {"inference.vllm.quantization", "inference.vllm.enable_fp32_lm_head", "model.compile",
+                    "policy_transfer.nccl_dtype"}
+    assert all("has no effect here" in m for m in msgs)
+    assert inert_settings(RLConfig()) == [] and inert_settings(SFTConfig()) == []
+    # set to its default value: not a change, not named
+    assert inert_settings(RLConfig.model_validate({"model": {"compile": False}})) == []
+    sft = SFTConfig.model_validate({"data": {"num_workers": 4}, "loss_impl": "liger"})
+    assert {m.split("=")[0] for m in inert_settings(sft)} == {"data.num_workers", "loss_impl"}
+
+
+def test_unsupported_values_are_refused():
+    with pytest.raises(ValueError, match="repetition_penalty"):
+        RLConfig.model_validate({"inference": {"sampling": {"repetition_penalty": 1.1}}})
+    with pytest.raises(ValueError, match="modules_to_save"):
+        SFTConfig.model_validate({"lora": {"modules_to_save": ["embed_tokens"]}})
+
+
+def test_sampling_keys_act(tmp_path, monkeypatch):
+    import torch
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    from wavelet_b200.inference.policy import NativePolicyInferenceEngine
+    from wavelet_b200.orchestrator.rollouts import PromptRecord, RLOrchestrator
+
+    cfg = RLConfig.model_validate({"model": {"name": "tiny", "random_init": True},
+                                   "inference": {"sampling": {"do_sample": False, "num_generations": 3,
+                                                              "max_prompt_tokens": 4, "temperature": 0.7}},
+                                   "orchestrator": {"rollouts_per_example": 2}, "output_dir": str(tmp_path)})
+    eng = NativePolicyInferenceEngine(cfg)
+    p = eng.sampling()
+    assert p.temperature == 0.0 and p.n == 3
+    orch = RLOrchestrator(cfg, engine=None, sender=None, prompts=None)
+    assert orch._sampling().temperature == 0.0
+
+    seen = []
+
+    class Eng:
+        def generate(self, prompts, params):
+            seen.extend(prompts)
+            raise RuntimeError("stop")
+
+    orch.engine = Eng()
+    with pytest.raises(RuntimeError, match="stop"):
+        orch.generate_records([PromptRecord(list(range(10)), example_id="a")], 0)
+    assert seen == [[6, 7, 8, 9]]  # the last max_prompt_tokens tokens
+    with pytest.raises(NotImplementedError, match="tensor_parallel_size"):
+        NativePolicyInferenceEngine(RLConfig.model_validate({"inference": {"vllm": {"tensor_parallel_size": 2}}})).setup()
+
+
+def test_generator_graphs_lm_head_chunk_and_state_events():
+    from types import SimpleNamespace
+
+    from wavelet_b200.inference.hf_generator import make_generator
+    from wavelet_b200.models.config import PRESETS
+    from wavelet_b200.models.qwen import build_model
+    from wavelet_b200.ops.lm_head import DEFAULT_CHUNK
+    from wavelet_b200.orchestrator.state_server import OrchestratorRunState
+    from wavelet_b200.trainer.model_options import lm_head_chunk
+
+    import torch
+
+    g = make_generator(build_model(PRESETS["tiny"], "cpu", torch.float32, seed=0), max_num_seqs=4,
+                       max_model_len=64, cuda_graphs=False)
+    assert g.use_graphs is False
+    assert lm_head_chunk(SimpleNamespace(fused_lm_head_token_chunk_size=1024)) == 1024
+    assert lm_head_chunk(SimpleNamespace(fused_lm_head_token_chunk_size="disabled")) == DEFAULT_CHUNK
+    st = OrchestratorRunState("/tmp", max_events=100)
+    for i in range(150):
+        st.event("e", i=i)
+    assert len(st.events()) == 100
+
+
+def test_chat_template_overrides_the_tokenizer(tmp_path):
+    from wavelet_b200.data.tokenizer import load_tokenizer
+
+    with pytest.raises(ValueError, match="chat_template"):
+        load_tokenizer("tiny", chat_template="{{ messages }}")

@@ -127,3 +127,25 @@ monitor:
     assert r.returncode == 0, r.stderr[-3000:]
     rows = [json.loads(line) for line in (out / "metrics.jsonl").read_text().splitlines()]
     assert [x["step"] for x in rows] == [1, 2]
+
+
+def test_frozen_vision_encoder_stays_put():
+    """model.vlm.freeze_vision_encoder: the vision tower keeps its weights
+    through optimizer steps (weight decay included) while the decoder moves."""
+    from types import SimpleNamespace
+
+    from wavelet_b200.trainer.model_options import apply_model_options
+
+    m = build_model(resolve_arch("tiny-qwen2.5-vl"), "cpu", torch.float32, seed=5)
+    mcfg = SimpleNamespace(vlm=SimpleNamespace(freeze_vision_encoder=True, vision_encoder_attr="model.visual"))
+    notes = apply_model_options(m, mcfg)
+    assert any("vision-tower parameters frozen" in n for n in notes)
+    before = {n: m.flat.view(n).clone() for n in m.flat.names()}
+    eng = Engine(m, AdamWHyper(lr=3e-3, weight_decay=0.1))
+    b = _batch([_row(7, 1), _row(8, 1)])
+    for _ in range(2):
+        eng.sft_micro_step(b, 1.0 / float(b.loss_mask.sum()))
+        eng.optimizer_step(3e-3)
+    vis = [n for n in m.flat.names() if n.startswith("model.visual.")]
+    assert vis and all(torch.equal(m.flat.view(n), before[n]) for n in vis)
+    assert not torch.equal(m.flat.view("lm_head.weight"), before["lm_head.weight"])

@@ -54,6 +54,13 @@ class LoRAConfig(ConfigModel):
     target_modules: list[str] = Field(default_factory=lambda: list(DEFAULT_LORA_TARGET_MODULES))
     modules_to_save: list[str] = Field(default_factory=list)
 
+    @model_validator(mode="after")
+    def _no_modules_to_save(self):
+        if self.modules_to_save:
+            raise ValueError("lora.modules_to_save is not supported: the adapters train LoRA factors only "
+                             "(train the full model for modules that must be updated)")
+        return self
+
 
 class ActivationCheckpointingConfig(ConfigModel):
     mode: Literal["full", "selective"] = "full"
@@ -665,6 +672,13 @@ class RLSamplingConfig(_LegacySampling):
     seed: int | None = None
     extra_body: dict[str, Any] = Field(default_factory=dict)
 
+    @model_validator(mode="after")
+    def _native_sampler(self):
+        if self.repetition_penalty != 1.0:
+            raise ValueError("inference.sampling.repetition_penalty is not supported by the native sampler "
+                             "(it would change the sampled distribution the RL losses correct for); use 1.0")
+        return self
+
 
 class RLEvalSamplingConfig(_LegacySampling):
     temperature: float | None = Field(default=None, ge=0.0)
@@ -677,6 +691,12 @@ class RLEvalSamplingConfig(_LegacySampling):
     reasoning_effort: Literal["minimal", "low", "medium", "high"] | None = None
     seed: int | None = None
     extra_body: dict[str, Any] = Field(default_factory=dict)
+
+    @model_validator(mode="after")
+    def _native_sampler(self):
+        if self.repetition_penalty not in (None, 1.0):
+            raise ValueError("eval sampling repetition_penalty is not supported by the native sampler; use 1.0")
+        return self
 
     def to_sampling_args(self) -> dict[str, Any]:
         args: dict[str, Any] = {"logprobs": True}

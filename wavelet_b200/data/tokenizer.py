@@ -48,7 +48,10 @@ class CharTokenizer:
         return self.encode(text) if tokenize else text
 
 
-def load_tokenizer(name_or_path: str | Path, trust_remote_code: bool = False):
+def load_tokenizer(name_or_path: str | Path, trust_remote_code: bool = False, chat_template: str | None = None):
+    """The tokenizer of a local model directory (or the char tokenizer of the
+    synthetic presets).  ``chat_template``: a Jinja template, or the path of a
+    file holding one, that replaces the directory's template."""
     p = Path(str(name_or_path))
     if p.is_dir() and ((p / "tokenizer.json").exists() or (p / "tokenizer_config.json").exists()):
         from transformers import AutoTokenizer
@@ -56,5 +59,16 @@ def load_tokenizer(name_or_path: str | Path, trust_remote_code: bool = False):
         tok = AutoTokenizer.from_pretrained(str(p), trust_remote_code=trust_remote_code, local_files_only=True)
         if tok.pad_token_id is None:
             tok.pad_token = tok.eos_token
+        if chat_template:
+            t = Path(chat_template)
+            tok.chat_template = t.read_text() if t.is_file() else chat_template
         return tok
+    if chat_template:
+        raise ValueError(f"model.chat_template needs a Hugging Face tokenizer; {name_or_path} has none")
     return CharTokenizer()
+
+
+def tokenizer_for(model_cfg):
+    """``load_tokenizer`` with the model section's template and remote-code settings."""
+    return load_tokenizer(model_cfg.name, trust_remote_code=bool(getattr(model_cfg, "trust_remote_code", False)),
+                          chat_template=getattr(model_cfg, "chat_template", None))

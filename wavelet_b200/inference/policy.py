@@ -104,6 +104,10 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         from .hf_generator import make_generator
 
         c = self.config
+        if c.inference.vllm.tensor_parallel_size > 1:
+            raise NotImplementedError("inference.vllm.tensor_parallel_size > 1: a generator process serves one GPU "
+                                      "(scale out with launcher.inference_num_replicas; tensor-parallel generation "
+                                      "runs inside a tensor-parallel trainer in integrated runs)")
         if self.model is None:
             dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
             arch = resolve_arch(c.model.name, c.model.arch_overrides or None)
@@ -111,7 +115,8 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         v = c.inference.vllm
         self.generator = make_generator(self.model, max_num_seqs=v.max_num_seqs,
                                         max_model_len=v.max_model_len or c.data.seq_len,
-                                        gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
+                                        gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size,
+                                        cuda_graphs=v.cuda_graphs and not v.enforce_eager)
 
     def load_policy(self, policy_dir: Path, *, step: int) -> None:
         from ..transport.policy import load_policy_into
@@ -130,8 +135,9 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         from .engine import SamplingParams
 
         s = self.config.inference.sampling
-        p = SamplingParams(temperature=s.temperature, top_p=s.top_p, top_k=s.top_k, min_p=s.min_p,
-                           max_tokens=s.max_completion_tokens or 256, min_tokens=s.min_tokens, n=1, seed=s.seed,
+        p = SamplingParams(temperature=s.temperature if s.do_sample else 0.0, top_p=s.top_p, top_k=s.top_k,
+                           min_p=s.min_p, max_tokens=s.max_completion_tokens or 256, min_tokens=s.min_tokens,
+                           n=s.num_generations, seed=s.seed,
                            return_sampling_mask=self.config.sampling_mask_required())
         for k, v in (overrides or {}).items():
             if hasattr(p, k) and v is not None:
@@ -139,8 +145,11 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         return p
 
     def annotate(self, records: list[RLExample]) -> list[RLExample]:
-        prompts = [record_prompt_ids(r, self.tokenizer) for r in records]
+        keep = self.config.inference.sampling.max_prompt_tokens
+        prompts = [record_prompt_ids(r, self.tokenizer)[-keep:] if keep else record_prompt_ids(r, self.tokenizer)
+                   for r in records]
         params = self.sampling()
+        params.n = 1  # one completion per record
         comps = self.generator.generate(prompts, params)
         out = []
         for r, c in zip(records, comps):

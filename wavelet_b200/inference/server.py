@@ -69,10 +69,10 @@ class GenerationGate:
 def build_app(config: RLConfig, engine=None):
     from fastapi import FastAPI, HTTPException
 
-    from ..data.tokenizer import load_tokenizer
+    from ..data.tokenizer import tokenizer_for
     from .policy import NativePolicyInferenceEngine
 
-    tok = load_tokenizer(config.model.name)
+    tok = tokenizer_for(config.model)
     if engine is None:
         engine = NativePolicyInferenceEngine(config, tokenizer=tok)
         engine.setup()

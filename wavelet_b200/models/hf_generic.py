@@ -237,7 +237,36 @@ class HFCausalLMTrainable:
                 p.grad = None
 
     def finalize_grads(self) -> None:
-        pass
+        for name, _, _, _ in getattr(self, "_frozen", []):
+            g = self.flat.grad_view(name)
+            if g is not None:
+                g.zero_()  # frozen parameters add nothing to the clip norm
+
+    def freeze_prefix(self, prefix: str) -> int:
+        """Freeze every parameter under the submodule ``prefix`` (e.g. the
+        vision tower, ``model.visual``): it gets no gradient, and its values
+        (bf16 and this rank's fp32 master part) are put back after every
+        optimizer step, so weight decay does not move it either.  Returns how
+        many parameters."""
+        flat = self.flat
+        lo, hi = flat.dp_rank * flat.shard_numel, (flat.dp_rank + 1) * flat.shard_numel
+        self._frozen = getattr(self, "_frozen", [])
+        for name, names in self._owners.items():
+            if any(x == prefix or x.startswith(prefix + ".") for x in names):
+                self.module.get_parameter(name).requires_grad_(False)
+                off, k = flat.offsets[name]
+                a, b = max(off, lo), min(off + k, hi)
+                master = flat.master[a - lo:b - lo].clone() if (flat.master is not None and a < b) else None
+                self._frozen.append((name, flat.view(name).clone(), (a - lo, b - lo) if a < b else None, master))
+        if not self._frozen:
+            raise ValueError(f"no parameters under {prefix!r} to freeze")
+        return len(self._frozen)
+
+    def after_optimizer_step(self) -> None:
+        for name, val, span, master in getattr(self, "_frozen", []):
+            self.flat.view(name).copy_(val)
+            if span is not None and master is not None:
+                self.flat.master[span[0]:span[1]].copy_(master)
 
     def set_activation_checkpointing(self, every: int | None) -> None:
         if every is None:

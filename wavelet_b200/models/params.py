@@ -34,6 +34,8 @@ class ParamSpec:
     name: str
     shape: tuple[int, ...]
     init: str = "normal"  # normal | ones | zeros
+    # informational: AdamW decays every parameter alike, as the reference's
+    # single parameter group does (trainer/optim.py builds one group)
     weight_decay: bool = True
     std: float = 0.02
 
@@ -80,7 +82,6 @@ class FlatParams:
         self.master = None
         self.exp_avg = None
         self.exp_avg_sq = None
-        self.decay_mask = None
         if with_optimizer:
             self.master = torch.zeros(self.shard_numel, device=self.device, dtype=torch.float32)
             self.exp_avg = torch.zeros_like(self.master)
@@ -204,16 +205,6 @@ class FlatParams:
         self.sync_master_from_compute()
         return missing
 
-    def build_decay_mask(self) -> torch.Tensor:
-        """fp32 shard mask: 1 where weight decay applies."""
-        full = torch.zeros(self.numel, device=self.device, dtype=torch.float32)
-        for s in self.specs:
-            if s.weight_decay:
-                off, n = self.offsets[s.name]
-                full[off : off + n] = 1.0
-        self.decay_mask = full[self.shard_slice].clone()
-        return self.decay_mask
-
     def zero_grad(self) -> None:
         if self.grad is not None:
             self.grad.zero_()
@@ -316,16 +307,6 @@ class ShardedFlatParams(FlatParams):
             raise KeyError(f"missing parameters: {missing[:8]}{'...' if len(missing) > 8 else ''}")
         self.sync_master_from_compute()
         return missing
-
-    def build_decay_mask(self) -> torch.Tensor:
-        mask = torch.zeros(self.shard_numel, device=self.device, dtype=torch.float32)
-        for s in self.specs:
-            if s.weight_decay:
-                r = self.local_range(*self.offsets[s.name])
-                if r is not None:
-                    mask[r[0]:r[1]] = 1.0
-        self.decay_mask = mask
-        return mask
 
     def state_dict(self) -> dict[str, torch.Tensor]:
         raise RuntimeError("a ZeRO-3 store has no full tensors; gather them (ParamGatherer.full_state)")

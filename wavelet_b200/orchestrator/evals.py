@@ -92,7 +92,7 @@ def _env_prompts(cfg, env):
         e = environments.load_environment(env.id, **{k: v for k, v in a.items() if k not in ("success_threshold",)})
         register_environment(e)
         return EnvironmentPromptSource([(e, 1.0)], cfg.model.name, seed=int(a.get("seed", 0)),
-                                       split="eval" if e.eval_examples else "train")
+                                       split="eval" if e.eval_examples else "train", model_cfg=cfg.model)
     raise ValueError(f"unknown eval environment {env.id!r} (built-ins: reverse, file:<path>, "
                      f"{', '.join(environments.available())})")
 

@@ -77,7 +77,7 @@ class RLOrchestrator:
 
         s = self.cfg.inference.sampling
         return SamplingParams(
-            temperature=s.temperature, top_p=s.top_p, top_k=s.top_k, min_p=s.min_p,
+            temperature=s.temperature if s.do_sample else 0.0, top_p=s.top_p, top_k=s.top_k, min_p=s.min_p,
             max_tokens=s.max_completion_tokens or 256, min_tokens=s.min_tokens,
             n=self.cfg.orchestrator.rollouts_per_example or 1, seed=s.seed,
             return_sampling_mask=self.cfg.sampling_mask_required(),
@@ -106,8 +106,9 @@ class RLOrchestrator:
             params.seed = params.seed + step
         eps = self._live_episodes(prompts, step)
         t0 = time.perf_counter()
-        try:
-            comps = self.engine.generate([p.prompt_ids for p in prompts], params)
+        keep = self.cfg.inference.sampling.max_prompt_tokens
+        try:  # over-long prompts keep their last max_prompt_tokens tokens (as the reference fits them)
+            comps = self.engine.generate([p.prompt_ids[-keep:] if keep else p.prompt_ids for p in prompts], params)
         except BaseException as e:
             for ep in eps:
                 ep.finish("error", error=e)

@@ -45,7 +45,7 @@ def build_prompt_source(cfg: RLConfig, vocab: int, rank: int = 0):
     if envs:
         from .sources import EnvironmentPromptSource
 
-        return EnvironmentPromptSource(envs, cfg.model.name, seed=d.seed, rank=rank)
+        return EnvironmentPromptSource(envs, cfg.model.name, seed=d.seed, rank=rank, model_cfg=cfg.model)
     if d.source == "fake":
         return SyntheticReversePrompts(min(vocab, d.fake_vocab_size), d.fake_prompt_len, seed=d.seed * 1000 + rank)
     from .sources import FilePromptSource
@@ -122,7 +122,8 @@ class IntegratedRunner:
         from ..inference.hf_generator import make_generator
 
         self.engine = make_generator(gen_model, max_num_seqs=v.max_num_seqs, max_model_len=max_len,
-                                     gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size)
+                                     gpu_memory_utilization=v.gpu_memory_utilization, block_size=v.kv_block_size,
+                                     cuda_graphs=v.cuda_graphs and not v.enforce_eager)
         self.sender = FileSystemRolloutSender(out, c.transport) if self.world.rank == 0 else None
         # batches past a resumed step are stale
         if self.world.rank == 0 and t.step > 0:

@@ -60,7 +60,7 @@ class RolloutScheduler:
         from .state_server import OrchestratorRunState, maybe_state_server
 
         pipe = self.pipeline()
-        state = OrchestratorRunState(self.out)
+        state = OrchestratorRunState(self.out, max_events=self.cfg.orchestrator.state_server.max_events)
         pipe.run_state = state
         pipe.status_sink = lambda snap: state.update(pipeline=snap, queue_depth=snap["ready"] + snap["inflight"])
         handle = maybe_state_server(self.cfg, state)
@@ -110,6 +110,9 @@ def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     cfg = load_config(RLConfig, argv)
     setup_logger("rl-inference", cfg.output_dir, cfg.log.level, cfg.log.json_console, cfg.log.json_file)
+    from ..configs.inert import warn_inert
+
+    warn_inert(cfg)  # settings of the reference's schema that do nothing here, named
     return RolloutScheduler(cfg).run()
 
 

@@ -58,6 +58,7 @@ class FilePromptSource:
         self.rank, self.world = rank, world
         self.tok = tokenizer
         self.model_name = cfg.model.name
+        self.model_cfg = cfg.model
         self.epoch = 0
         self.cursor = 0
         # orchestrator.curriculum: the sampler picks every prompt; gates admit scored groups
@@ -70,9 +71,9 @@ class FilePromptSource:
 
     def _tokenizer(self):
         if self.tok is None:
-            from ..data.tokenizer import load_tokenizer
+            from ..data.tokenizer import tokenizer_for
 
-            self.tok = load_tokenizer(self.model_name)
+            self.tok = tokenizer_for(self.model_cfg)
         return self.tok
 
     def _order(self) -> list[int]:
@@ -141,11 +142,12 @@ class EnvironmentPromptSource:
     reward."""
 
     def __init__(self, envs: list[tuple[Any, float]], model_name: str, seed: int = 0, rank: int = 0, world: int = 1,
-                 tokenizer=None, split: str = "train"):
+                 tokenizer=None, split: str = "train", model_cfg=None):
         if not envs:
             raise ValueError("EnvironmentPromptSource needs at least one environment")
         self.envs = envs
         self.model_name = model_name
+        self.model_cfg = model_cfg  # the model section: chat template / remote-code settings of the tokenizer
         self.tok = tokenizer
         self.seed, self.rank, self.world = seed, rank, world
         self.split = split
@@ -164,9 +166,9 @@ class EnvironmentPromptSource:
 
     def _tokenizer(self):
         if self.tok is None:
-            from ..data.tokenizer import load_tokenizer
+            from ..data.tokenizer import load_tokenizer, tokenizer_for
 
-            self.tok = load_tokenizer(self.model_name)
+            self.tok = tokenizer_for(self.model_cfg) if self.model_cfg is not None else load_tokenizer(self.model_name)
         return self.tok
 
     def _pick(self) -> int:

@@ -28,7 +28,17 @@ import torch
 log = logging.getLogger("wavelet")
 
 
-def apply_model_options(model, mcfg, fsdp_cfg=None) -> list[str]:
+def lm_head_chunk(mcfg) -> int:
+    """Tokens per LM-head chunk: ``model.fused_lm_head_token_chunk_size``
+    when it is a number; the loss is always chunked, so ``auto`` and
+    ``disabled`` (the reference's unfused head) use the default chunk."""
+    from ..ops.lm_head import DEFAULT_CHUNK
+
+    v = getattr(mcfg, "fused_lm_head_token_chunk_size", None)
+    return int(v) if isinstance(v, int) and not isinstance(v, bool) and v > 0 else DEFAULT_CHUNK
+
+
+def apply_model_options(model, mcfg, fsdp_cfg=None, trainer_cfg=None) -> list[str]:
     notes: list[str] = []
     prec = getattr(mcfg, "matmul_precision", None)
     if prec:
@@ -43,6 +53,14 @@ def apply_model_options(model, mcfg, fsdp_cfg=None) -> list[str]:
             raise ValueError("model.freeze_moe_router=true requires a model with MoE routers (a Qwen3-MoE shape)")
         model.freeze(names)
         notes.append(f"model.freeze_moe_router: {len(names)} router weights frozen")
+    if trainer_cfg is not None and getattr(trainer_cfg, "activation_offloading", None) is not None \
+            and hasattr(model, "enable_activation_offload"):
+        model.enable_activation_offload()  # layer inputs kept in pinned host memory until the backward
+        notes.append("activation_offloading: layer inputs offloaded to host memory")
+    vlm = getattr(mcfg, "vlm", None)
+    if vlm is not None and getattr(vlm, "freeze_vision_encoder", False) and hasattr(model, "freeze_prefix"):
+        n = model.freeze_prefix(vlm.vision_encoder_attr)
+        notes.append(f"model.vlm.freeze_vision_encoder: {n} vision-tower parameters frozen")
     if getattr(mcfg, "meta_device_init", False):
         notes.append("model.meta_device_init: parameters are allocated directly on the device "
                      "(no host materialisation to defer)")

@@ -93,9 +93,11 @@ class RLTrainer:
 
                 load_hf_weights(model, p)
         self.model = model
-        from .model_options import apply_model_options
+        from .model_options import apply_model_options, lm_head_chunk
 
-        apply_model_options(model, c.model, c.fsdp)
+        self.lm_head_chunk = lm_head_chunk(c.model)
+
+        apply_model_options(model, c.model, c.fsdp, c)
         ac = c.model.activation_checkpointing
         model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
@@ -112,6 +114,9 @@ class RLTrainer:
         out = Path(c.output_dir)
         self.output_dir = out
         setup_logger("rl-trainer", out, c.log.level, c.log.json_console, c.log.json_file)
+        from ..configs.inert import warn_inert
+
+        warn_inert(c)  # settings of the reference's schema that do nothing here, named
         self.monitor = RunMonitor.from_config(out, c.monitor, checkpoint_dir=c.checkpoint_output_dir)
         self.ckpt = None
         if c.ckpt is not None and c.ckpt.mode != "disabled":
@@ -125,6 +130,8 @@ class RLTrainer:
             st = mgr.load(resume, model=model, optimizer=self.optimizer, skip_optimizer=c.ckpt.skip_optimizer)
             if not c.ckpt.skip_progress:
                 self.step = int(st["meta"]["step"])
+            if c.ckpt.skip_scheduler:  # the learning-rate schedule restarts at the resumed step
+                self.sched_offset = self.step
         from ..orchestrator.schedule import chunks_per_step
 
         # with streamed chunks, queue step q holds chunk q % C of optimizer step q // C
@@ -225,7 +232,8 @@ class RLTrainer:
             h = m.hidden(b.base.input_ids, ctx)
             tgt = b.base.targets.clamp_min(0)
             if h.is_cuda:
-                lp, _ = lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, want_entropy=False)
+                lp, _ = lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, want_entropy=False,
+                                                chunk=self.lm_head_chunk)
             else:
                 lp, _ = lm_head.ref.logprob_entropy(m.logits(h), tgt, b.temperature)
         miss = b.missing_inference()
@@ -287,7 +295,7 @@ class RLTrainer:
             for f in (m.trainable, m.expert_flat):
                 if f is not None and f.grad is not None:
                     f.grad.mul_(grad_scale)
-        lr = lr_at(self.step, c.optim.lr, max(1, c.max_steps or 1), c.scheduler)
+        lr = lr_at(self.step - getattr(self, "sched_offset", 0), c.optim.lr, max(1, c.max_steps or 1), c.scheduler)
         m.finalize_grads()
         st = self.optimizer.step(lr)
         after = getattr(m, "after_optimizer_step", None)
@@ -359,7 +367,8 @@ class RLTrainer:
         if b.sampling_mask is not None and any(b.sampling_mask):
             return self._support_logprobs(h, tgt, b)
         if h.is_cuda:
-            return lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, gW=m.head_grad(), anchor=m.anchor)
+            return lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, gW=m.head_grad(), anchor=m.anchor,
+                                           chunk=self.lm_head_chunk)
         z = lm_head.cpu_head_logits(h, m.head_weight(), m.head_grad())
         return lm_head.ref.logprob_entropy(z, tgt, b.temperature)
 
@@ -368,7 +377,8 @@ class RLTrainer:
         (trainer/losses.py:30-69): lp = z_t/T - logsumexp_{j in S}(z_j/T)."""
         m = self.model
         if h.is_cuda:
-            lp_full, ent = lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, gW=m.head_grad(), anchor=m.anchor)
+            lp_full, ent = lm_head.logprob_entropy(h, m.head_weight(), tgt, b.temperature, gW=m.head_grad(),
+                                                   anchor=m.anchor, chunk=self.lm_head_chunk)
         else:
             z = lm_head.cpu_head_logits(h, m.head_weight(), m.head_grad())
             lp_full, ent = lm_head.ref.logprob_entropy(z, tgt, b.temperature)

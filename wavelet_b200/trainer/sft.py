@@ -125,7 +125,7 @@ class SFTTrainer:
                                             capacity_factor=c.fsdp.ep_capacity_factor)
         from .model_options import apply_model_options
 
-        apply_model_options(self.model, c.model, c.fsdp)
+        apply_model_options(self.model, c.model, c.fsdp, c)
         ac = c.model.activation_checkpointing
         self.model.set_activation_checkpointing(ac.freq if ac is not None else None)
         if c.model.smart_gc:
@@ -139,12 +139,14 @@ class SFTTrainer:
                                        ep_dp_group=self.groups.ep_dp, ep_dp_world=self.groups.ep_dp_size,
                                        norm_fabric=self.norm_fabric,
                                        replicate_group=self.groups.replicate if hsdp else None)
-        self.engine = Engine(self.model, self.optimizer.adamw.h, opt_group, opt_world)
+        from .model_options import lm_head_chunk
+
+        self.engine = Engine(self.model, self.optimizer.adamw.h, opt_group, opt_world, lm_head_chunk=lm_head_chunk(c.model))
         self.engine.opt = self.optimizer  # type: ignore[assignment]
         from ..data.sft import SFTDataset
-        from ..data.tokenizer import load_tokenizer
+        from ..data.tokenizer import tokenizer_for
 
-        tok = None if c.data.source == "fake" else load_tokenizer(c.model.name)
+        tok = None if c.data.source == "fake" else tokenizer_for(c.model)
         self.dataset = SFTDataset(c.data, tok, dp_rank, dp_world, seed=c.seed)
         self.val_dataset = SFTDataset(c.val.data, tok, dp_rank, dp_world, seed=c.seed) if c.val is not None else None
         gm = c.data.micro_batch_size * dp_world
@@ -169,6 +171,9 @@ class SFTTrainer:
         if w.distributed:
             torch.distributed.barrier()
         setup_logger("sft", out, c.log.level, c.log.json_console, c.log.json_file)
+        from ..configs.inert import warn_inert
+
+        warn_inert(c)  # settings of the reference's schema that do nothing here, named
         self.monitor = RunMonitor.from_config(out, c.monitor, checkpoint_dir=c.checkpoint_output_dir)
         self.ckpt = None
         if c.ckpt is not None and c.ckpt.mode != "disabled":
@@ -179,6 +184,8 @@ class SFTTrainer:
             st = mgr.load(resume, model=self.model, optimizer=self.optimizer, skip_optimizer=c.ckpt.skip_optimizer)
             if not c.ckpt.skip_progress:
                 self.step = int(st["meta"]["step"])
+            if c.ckpt.skip_scheduler:  # the learning-rate schedule restarts at the resumed step
+                self.sched_offset = self.step
             if st["data_state"] is not None and not c.ckpt.skip_dataloader:
                 self.dataset.load_state_dict(st["data_state"])
         self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
@@ -239,7 +246,7 @@ class SFTTrainer:
             b = b.to(dev)
             tokens += b.num_tokens
             loss += self.engine.sft_micro_step(b, scale)
-        lr = lr_at(self.step, c.optim.lr, self.total_steps, c.scheduler)
+        lr = lr_at(self.step - getattr(self, "sched_offset", 0), c.optim.lr, self.total_steps, c.scheduler)
         self.model.finalize_grads()
         stats = self.optimizer.step(lr)
         if self.world.distributed:
