@@ -62,7 +62,7 @@ def test_sampling_keys_act(tmp_path, monkeypatch):
     with pytest.raises(RuntimeError, match="stop"):
         orch.generate_records([PromptRecord(list(range(10)), example_id="a")], 0)
     assert seen == [[6, 7, 8, 9]]  # the last max_prompt_tokens tokens
-    with pytest.raises(NotImplementedError, match="tensor_parallel_size"):
+    with pytest.raises(NotImplementedError, match="torchrun group"):
         NativePolicyInferenceEngine(RLConfig.model_validate({"inference": {"vllm": {"tensor_parallel_size": 2}}})).setup()
 
 

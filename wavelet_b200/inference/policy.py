@@ -104,10 +104,9 @@ class NativePolicyInferenceEngine(PolicyInferenceEngine):
         from .hf_generator import make_generator
 
         c = self.config
-        if c.inference.vllm.tensor_parallel_size > 1:
-            raise NotImplementedError("inference.vllm.tensor_parallel_size > 1: a generator process serves one GPU "
-                                      "(scale out with launcher.inference_num_replicas; tensor-parallel generation "
-                                      "runs inside a tensor-parallel trainer in integrated runs)")
+        if c.inference.vllm.tensor_parallel_size > 1 and self.model is None:
+            raise NotImplementedError("inference.vllm.tensor_parallel_size > 1 runs as a torchrun group of "
+                                      "inference-server processes (inference.tp_server), not in one process")
         if self.model is None:
             dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
             arch = resolve_arch(c.model.name, c.model.arch_overrides or None)

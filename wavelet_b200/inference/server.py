@@ -238,6 +238,10 @@ def build_app(config: RLConfig, engine=None):
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     cfg = load_config(RLConfig, argv)
+    if cfg.inference.vllm.tensor_parallel_size > 1:  # one replica over a torchrun group of processes
+        from .tp_server import run_tp_server
+
+        return run_tp_server(cfg)
     import uvicorn
 
     app = build_app(cfg)

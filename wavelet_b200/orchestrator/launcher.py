@@ -182,13 +182,21 @@ def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executabl
         return {"CUDA_VISIBLE_DEVICES": ",".join(devs)}
 
     services: list[RoleSpec] = []
+    tp = cfg.inference.vllm.tensor_parallel_size
     if cfg.inference.mode == "vllm_http":
         for r, (devs, port) in enumerate(zip(pl.inference_devices, pl.ports)):
             c = dict(base)
             c["inference"] = {**base["inference"], "http": {**base["inference"]["http"], "port": port, "ports": None}}
             path = attempt.config_dir / f"inference_server_{r}.yaml"
             dump_yaml(path, c)
-            services.append(RoleSpec(f"inference-server-{r}", [python, "-m", "wavelet_b200", "inference-server", "@", str(path)],
+            argv = [python, "-m", "wavelet_b200", "inference-server", "@", str(path)]
+            if tp > 1:  # one replica = a torchrun group of tp processes (inference.tp_server)
+                if devs and len(devs) != tp:
+                    raise ValueError(f"inference replica {r} has {len(devs)} GPUs for tensor_parallel_size {tp}")
+                argv = [python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
+                        "--master-addr=127.0.0.1", f"--master-port={cfg.deployment.trainer_master_port + 101 + r}",
+                        "-m", "wavelet_b200", "inference-server", "@", str(path)]
+            services.append(RoleSpec(f"inference-server-{r}", argv,
                                      {**visible(devs), "WAVELET_INFERENCE_REPLICA": str(r)}, service=True))
     trainer_cfg = attempt.config_dir / "rl_trainer.yaml"
     dump_yaml(trainer_cfg, base)
