@@ -94,3 +94,30 @@ def test_chat_template_overrides_the_tokenizer(tmp_path):
 
     with pytest.raises(ValueError, match="chat_template"):
         load_tokenizer("tiny", chat_template="{{ messages }}")
+
+
+def test_rollout_columns_round_trip_under_renames():
+    from wavelet_b200.configs.config import RLDataConfig
+    from wavelet_b200.data.rl import RLExample, example_from_payload, example_to_payload
+
+    e = RLExample(prompt=[], completion=[], advantage=0.5, reward=1.0, input_ids=[1, 2, 3],
+                  loss_mask=[False, True, True], inference_logprobs=[-0.1, -0.2], temperatures=0.7)
+    plain = example_to_payload(e, RLDataConfig())
+    assert "advantage" in plain and "temperatures" in plain  # default names: the on-disk format is unchanged
+    data = RLDataConfig.model_validate({"advantage_column": "adv", "inference_logprobs_column": "lp"})
+    row = example_to_payload(e, data)
+    assert "adv" in row and "lp" in row and "advantage" not in row
+    back = example_from_payload(row, data)
+    assert back.advantage == 0.5 and back.inference_logprobs == [-0.1, -0.2]
+    # an external file written with custom column names
+    ext = {"input_ids": [1, 2], "loss_mask": [False, True], "adv": -1.0, "reward": 0.0, "prompt": [], "completion": []}
+    assert example_from_payload(ext, data).advantage == -1.0
+
+
+def test_token_batches_and_rollout_selection_are_refused():
+    with pytest.raises(ValueError, match="token_batch_size"):
+        RLConfig.model_validate({"orchestrator": {"examples_per_step": None, "token_batch_size": 4096}})
+    with pytest.raises(ValueError, match="batch_selection"):
+        RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "refill_zero_advantage": False}})
+    msgs = inert_settings(RLConfig.model_validate({"orchestrator": {"oversampling_factor": 2.0}}))
+    assert msgs and msgs[0].startswith("orchestrator.oversampling_factor")

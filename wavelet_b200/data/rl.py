@@ -46,13 +46,45 @@ class RLExample:
     mm_kwargs: dict[str, Any] | None = None
 
 
-def example_from_payload(p: dict[str, Any]) -> RLExample:
+# record field -> data-config attribute naming its column in rollout files
+_COLUMNS = {"advantage": "advantage_column", "reward": "reward_column",
+            "inference_logprobs": "inference_logprobs_column", "teacher_logprobs": "teacher_logprobs_column",
+            "sampling_mask": "sampling_mask_column", "temperatures": "temperature_column",
+            "ce_weight": "ce_weight_column", "ref_kl_weight": "ref_kl_weight_column", "metadata": "metadata_column"}
+
+
+def _renames(data_cfg) -> dict[str, str]:
+    """Field -> column for the columns ``data_cfg`` renames away from the
+    schema defaults (the default names are the fields' own)."""
+    if data_cfg is None:
+        return {}
+    fields = type(data_cfg).model_fields
+    out = {}
+    for field, attr in _COLUMNS.items():
+        if attr in fields and getattr(data_cfg, attr) != fields[attr].default:
+            out[field] = getattr(data_cfg, attr)
+    return out
+
+
+def example_from_payload(p: dict[str, Any], data_cfg=None) -> RLExample:
+    """A rollout record from its JSON row; ``data_cfg`` (the ``data``
+    section) maps renamed columns (``data.advantage_column`` ...) back."""
+    ren = _renames(data_cfg)
+    if ren:
+        p = dict(p)
+        for field, col in ren.items():
+            if col in p:
+                p[field] = p.pop(col)
     known = set(RLExample.__dataclass_fields__)
     return RLExample(**{k: v for k, v in p.items() if k in known})
 
 
-def example_to_payload(e: RLExample) -> dict[str, Any]:
-    return asdict(e)
+def example_to_payload(e: RLExample, data_cfg=None) -> dict[str, Any]:
+    d = asdict(e)
+    for field, col in _renames(data_cfg).items():
+        if field in d:
+            d[col] = d.pop(field)
+    return d
 
 
 @dataclass

@@ -397,7 +397,7 @@ class AsyncRolloutScheduler:
     def _publish_ready(self, next_pub: int) -> int:
         while next_pub in self.done:
             st, recs, stats = self.done.pop(next_pub)
-            rows = [example_to_payload(r) for r in recs]
+            rows = [example_to_payload(r, self.cfg.data) for r in recs]
             cur = self.prompts.curriculum
             self.sender.publish(rows, step=st.step, training_records=rows, optimizer_step=st.step // self.C,
                                 chunk_index=(st.step % self.C) if self.C > 1 else None,

@@ -221,7 +221,7 @@ class RLOrchestrator:
         t0 = time.perf_counter()
         recs = self.materialize(step)
         emit_perf("rollout_materialized", step=step, seconds=time.perf_counter() - t0, rows=len(recs))
-        rows = [example_to_payload(r) for r in recs]
+        rows = [example_to_payload(r, self.cfg.data) for r in recs]
         tokens = sum(len(r.input_ids or []) for r in recs)
         if self.sender is None:
             return recs

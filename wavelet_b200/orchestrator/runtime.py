@@ -159,7 +159,7 @@ class IntegratedRunner:
         gen_s = time.perf_counter() - t0
         if ev:
             ev[1].record()
-        rows = self._gather([example_to_payload(r) for r in recs])
+        rows = self._gather([example_to_payload(r, self.cfg.data) for r in recs])
         if self.sender is not None:
             self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=step,
                                 tokens=sum(len(r.get("input_ids") or []) for r in rows))
@@ -170,7 +170,7 @@ class IntegratedRunner:
             t.receiver.claim(batch, step)
         from ..transport.queue import read_training_records
 
-        records = [example_from_payload(r) for r in read_training_records(batch.training_path)]
+        records = [example_from_payload(r, self.cfg.data) for r in read_training_records(batch.training_path)]
         t1 = time.perf_counter()
         m = t.train_on_examples(records)
         train_s = time.perf_counter() - t1

@@ -418,7 +418,7 @@ class RLTrainer:
             if self.world.rank == 0:
                 self.receiver.claim(batch, step)
             claimed.append(batch)
-            yield [example_from_payload(r) for r in read_training_records(batch.training_path)]
+            yield [example_from_payload(r, self.config.data) for r in read_training_records(batch.training_path)]
 
     def run(self) -> int:
         from ..orchestrator.schedule import chunks_per_step
@@ -440,7 +440,7 @@ class RLTrainer:
                     if self.world.rank == 0:
                         self.receiver.claim(batch, before)
                     claimed = [batch]
-                    records = [example_from_payload(r) for r in read_training_records(batch.training_path)]
+                    records = [example_from_payload(r, c.data) for r in read_training_records(batch.training_path)]
                     metrics = self.train_on_examples(records)
                 if self.world.rank == 0:
                     for bt in claimed:
