@@ -210,6 +210,9 @@ class RLOrchestrator:
             retries += 1
         if not kept:
             kept = recs  # never publish an empty batch; zero-advantage rows contribute no gradient
+        from .teacher import attach_teacher_logprobs, scorer_for
+
+        kept = attach_teacher_logprobs(kept, self.cfg, scorer_for(self.cfg, self.engine))  # OPD / OPSD
         rewards = [float(r.reward or 0.0) for r in recs]
         self.last_stats["rollout/curriculum_rejected"] = float(gated)
         self.last_stats.update({"reward/mean": sum(rewards) / max(1, len(rewards)),
