@@ -89,7 +89,7 @@ def test_zero3_matches_replicated_weights(tmp_path, preset):
             torch.testing.assert_close(b["full"][k], a["full"][k], rtol=1e-5, atol=2e-5, msg=k)
         else:  # a flipped routing decision moves single elements by ~lr: compare in aggregate
             rel = float((b["full"][k] - a["full"][k]).norm() / a["full"][k].norm().clamp_min(1e-12))
-            assert rel < 1e-3, (k, rel)
+            assert rel < 1e-2, (k, rel)  # a gross error (a missing or doubled gradient) is O(1)
     if "reloaded" in b:
         assert b["master_equal"]
         for k in b["full"]:
