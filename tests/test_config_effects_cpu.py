@@ -121,3 +121,71 @@ def test_token_batches_and_rollout_selection_are_refused():
         RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "refill_zero_advantage": False}})
     msgs = inert_settings(RLConfig.model_validate({"orchestrator": {"oversampling_factor": 2.0}}))
     assert msgs and msgs[0].startswith("orchestrator.oversampling_factor")
+
+
+def test_sample_rows_ratio_cap_and_decoding():
+    from types import SimpleNamespace
+
+    from wavelet_b200.data.rl import RLExample
+    from wavelet_b200.data.tokenizer import CharTokenizer
+    from wavelet_b200.trainer.rl import sample_rows
+
+    recs = [RLExample(prompt=[], completion=[], advantage=0.1 * i, reward=float(i), input_ids=[70, 71, 72 + i],
+                      loss_mask=[False, False, True], metadata={"example_id": f"e{i}"}) for i in range(20)]
+    sc = SimpleNamespace(sample_ratio=0.25, max_samples=3)
+    rows = sample_rows(recs, sc, seed=1, step=4)
+    assert len(rows) == 3 and rows == sample_rows(recs, sc, seed=1, step=4)
+    assert rows[0]["prompt_ids"] == [70, 71] and rows[0]["completion_tokens"] == 1
+    assert len(sample_rows(recs, SimpleNamespace(sample_ratio=0.25, max_samples=None), 1, 4)) == 5
+    assert sample_rows(recs, SimpleNamespace(sample_ratio=0.0, max_samples=None), 1, 4) == []
+    dec = sample_rows(recs[:1], SimpleNamespace(sample_ratio=None, max_samples=None), 1, 4, CharTokenizer())
+    assert isinstance(dec[0]["completion"], str) and dec[0]["example_id"] == "e0"
+
+
+def test_per_environment_sampling_group_size_and_algorithm(tmp_path):
+    """orchestrator.envs[] entries: group_size and sampling apply to that
+    environment's prompts only; an entry's algorithm scores its records;
+    data_path reaches the loader; a per-environment curriculum is refused."""
+    import json as _json
+
+    from wavelet_b200.inference.engine import Completion
+    from wavelet_b200.orchestrator.rollouts import PromptRecord, RLOrchestrator
+
+    rows = tmp_path / "eq.jsonl"
+    rows.write_text("".join(_json.dumps({"question": f"q{i}", "answer": str(i)}) + "\n" for i in range(4)))
+    from wavelet_b200.configs.config import VERIFIER_ROLLOUT_FUNCTION
+
+    vf = {"custom_rollout_function": VERIFIER_ROLLOUT_FUNCTION}
+    with pytest.raises(ValueError, match="curriculum"):
+        RLConfig.model_validate({"launcher": {"mode": "process"}, "orchestrator": {
+            **vf, "max_async_level": 1, "envs": [{"id": "equation_builder", "curriculum": {}}]}})
+    cfg = RLConfig.model_validate({"launcher": {"mode": "process"},
+                                   "orchestrator": {**vf, "rollouts_per_example": 2, "max_async_level": 1, "envs": [
+                                       {"id": "equation_builder", "group_size": 3, "sampling": {"temperature": 0.3},
+                                        "algo": {"type": "reward"}}]}})
+    orch = RLOrchestrator(cfg, engine=None, sender=None, prompts=None)
+    name = next(iter(orch.env_cfg))
+    calls = []
+
+    class Eng:
+        def generate(self, prompts, params):
+            calls.append((len(prompts), params.n, params.temperature))
+            return [Completion(i, j, p, [1, 2], [-0.1, -0.2], "length") for i, p in enumerate(prompts)
+                    for j in range(params.n)]
+
+    orch.engine = Eng()
+    ps = [PromptRecord([5, 6], metadata={"env": name}), PromptRecord([7], metadata={"env": "other"}),
+          PromptRecord([8, 9], metadata={"env": name})]
+    recs = orch.generate_records(ps, 0)
+    assert sorted(calls) == sorted([(2, 3, 0.3), (1, 2, 1.0)])
+    assert sum(1 for r in recs if r.metadata["env"] == name) == 6 and all(
+        r.temperatures == 0.3 for r in recs if r.metadata["env"] == name)
+    from dataclasses import replace
+
+    scored = orch.score([replace(r, reward=0.5) for r in recs])
+    assert len(scored) == len(recs)
+    from types import SimpleNamespace
+
+    from wavelet_b200.orchestrator.runtime import env_args
+
+    assert env_args(SimpleNamespace(args={"k": 1}, data_path=rows)) == {"k": 1, "path": str(rows)}

@@ -1158,6 +1158,9 @@ class RLOrchestratorConfig(ConfigModel):
             raise ValueError("orchestrator.verifier_env_args cannot be combined with orchestrator.envs.")
         if self.envs and self.curriculum is not None:
             raise ValueError("orchestrator.curriculum cannot be combined with orchestrator.envs.")
+        if any(e.curriculum is not None for e in self.envs):
+            raise ValueError("per-environment curriculum (orchestrator.envs[].curriculum) is not supported; "
+                             "environments mix by their ratio")
         names = [e.resolved_name for e in self.envs]
         dup = sorted({n for n in names if names.count(n) > 1})
         if dup:

@@ -38,14 +38,16 @@ def http_json(url: str, payload: dict | None = None, timeout: float = 30.0) -> d
         return json.loads(body) if body else {}
 
 
-def wait_healthy(urls: list[str], timeout: float, poll: float = 1.0) -> None:
+def wait_healthy(urls: list[str], timeout: float, poll: float = 1.0, probe_timeout: float = 5.0) -> None:
+    """Poll every server's /health until all answer; each probe waits at most
+    ``probe_timeout`` (inference.http.liveness_timeout_seconds)."""
     t0 = time.monotonic()
     pending = list(urls)
     while pending:
         still = []
         for u in pending:
             try:
-                http_json(u + "/health", timeout=min(5.0, timeout))
+                http_json(u + "/health", timeout=min(probe_timeout, timeout))
             except (urllib.error.URLError, OSError, ValueError):
                 still.append(u)
         pending = still
@@ -66,7 +68,7 @@ class HTTPPolicyInferenceEngine(PolicyInferenceEngine):
 
     def setup(self) -> None:
         h = self.config.inference.http
-        wait_healthy(self.urls, h.startup_timeout_seconds)
+        wait_healthy(self.urls, h.startup_timeout_seconds, probe_timeout=h.liveness_timeout_seconds)
         for u in self.urls:
             http_json(u + "/v1/models", timeout=h.request_timeout_seconds)
 

@@ -293,8 +293,12 @@ class RunMonitor:
             self.log_event("wandb_unavailable", payload={"reason": "wandb is not installed; local files only"})
             return
         try:
+            settings = None
+            if hasattr(wandb, "Settings"):  # monitor.wandb.init_timeout_seconds bounds the start-up handshake
+                settings = wandb.Settings(init_timeout=float(getattr(w, "init_timeout_seconds", 30.0)))
             self._wandb = wandb.init(project=w.project, entity=w.entity, name=w.name, group=w.group, tags=w.tags,
-                                     mode=w.mode, config=cfg, dir=str(self.output_dir))
+                                     mode=w.mode, config=cfg, dir=str(self.output_dir),
+                                     **({"settings": settings} if settings is not None else {}))
             from .wandb_overview import maybe_create_overview
 
             maybe_create_overview(self._wandb, cfg if isinstance(cfg, dict) else None, w)

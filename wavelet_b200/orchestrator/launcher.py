@@ -234,7 +234,8 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
         from ..inference.client import endpoints, wait_healthy
 
         try:
-            wait_healthy(endpoints(cfg), cfg.inference.http.startup_timeout_seconds)
+            wait_healthy(endpoints(cfg), cfg.inference.http.startup_timeout_seconds,
+                         probe_timeout=cfg.inference.http.liveness_timeout_seconds)
         except TimeoutError:
             for s in running_services:
                 s.terminate()

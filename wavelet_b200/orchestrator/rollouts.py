@@ -71,6 +71,14 @@ class RLOrchestrator:
         self.scorer = RLRewardScorer(cfg.reward)
         self.custom_rollout = custom_rollout
         self.last_stats: dict[str, float] = {}
+        # orchestrator.envs[] entries with their own sampling / group size / algorithm
+        self.env_cfg: dict[str, Any] = {}
+        if getattr(getattr(cfg, "orchestrator", None), "envs", None):
+            from .runtime import env_overrides
+
+            self.env_cfg = env_overrides(cfg)
+        self.env_algo = {n: (build_algorithm(e.algo), algorithm_scope(e.algo), algorithm_epsilon(e.algo))
+                         for n, e in self.env_cfg.items() if e.algo is not None}
 
     def _sampling(self):
         from ..inference.engine import SamplingParams
@@ -100,15 +108,54 @@ class RLOrchestrator:
             eps.append(ep)
         return eps
 
+    def _env_params(self, env: str | None, base):
+        """Sampling of one environment's prompts: the global settings with the
+        entry's own ``sampling`` fields and ``group_size`` on top."""
+        e = self.env_cfg.get(env) if env is not None else None
+        if e is None:
+            return base
+        from dataclasses import replace as _replace
+
+        p = _replace(base)
+        if e.sampling is not None:
+            s = e.sampling
+            for k in s.model_fields_set:
+                if k == "max_completion_tokens":
+                    p.max_tokens = s.max_completion_tokens or p.max_tokens
+                elif k == "do_sample":
+                    continue
+                elif hasattr(p, k):
+                    setattr(p, k, getattr(s, k))
+            if not s.do_sample:
+                p.temperature = 0.0
+        if e.group_size is not None:
+            p.n = e.group_size
+        return p
+
     def generate_records(self, prompts: list[PromptRecord], step: int) -> list[RLExample]:
-        params = self._sampling()
-        if params.seed is not None:
-            params.seed = params.seed + step
+        base = self._sampling()
+        if base.seed is not None:
+            base.seed = base.seed + step
         eps = self._live_episodes(prompts, step)
         t0 = time.perf_counter()
         keep = self.cfg.inference.sampling.max_prompt_tokens
+        # prompts of environments with their own sampling run as their own batch
+        batches: dict[Any, tuple[Any, list[int]]] = {}
+        for i, p in enumerate(prompts):
+            env = p.metadata.get("env")
+            key = env if env in self.env_cfg else None
+            if key not in batches:
+                batches[key] = (self._env_params(key, base), [])
+            batches[key][1].append(i)
+        comps, temps = [], {}
         try:  # over-long prompts keep their last max_prompt_tokens tokens (as the reference fits them)
-            comps = self.engine.generate([p.prompt_ids[-keep:] if keep else p.prompt_ids for p in prompts], params)
+            for params, idx in batches.values():
+                got = self.engine.generate([prompts[i].prompt_ids[-keep:] if keep else prompts[i].prompt_ids
+                                            for i in idx], params)
+                for c in got:
+                    c.prompt_index = idx[c.prompt_index]
+                    temps[c.prompt_index] = params.temperature
+                comps += got
         except BaseException as e:
             for ep in eps:
                 ep.finish("error", error=e)
@@ -131,7 +178,7 @@ class RLOrchestrator:
                       sample_index=c.sample_index, example_id=p.example_id)
             recs.append(RLExample(prompt=p.prompt, completion=[], advantage=None, reward=None, input_ids=ids,
                                   loss_mask=mask, target_completion=p.target_completion,
-                                  inference_logprobs=c.logprobs, temperatures=params.temperature,
+                                  inference_logprobs=c.logprobs, temperatures=temps[c.prompt_index],
                                   sampling_mask=c.sampling_mask, metadata=md, source="orchestrator"))
         st = getattr(self.engine, "stats", {}) or {}
         ntok = sum(len(c.token_ids) for c in comps)
@@ -145,7 +192,20 @@ class RLOrchestrator:
         from dataclasses import replace
 
         recs = [replace(r, reward=self.scorer.score(r)) for r in recs]
-        return score_records(self.algo, recs, self.scope, group_key=lambda r: (r.metadata or {}).get("group"))
+        group = lambda r: (r.metadata or {}).get("group")  # noqa: E731
+        if not self.env_algo:
+            return score_records(self.algo, recs, self.scope, group_key=group)
+        # environments with their own algorithm score their records with it
+        by_env: dict[Any, list[int]] = {}
+        for i, r in enumerate(recs):
+            env = (r.metadata or {}).get("env")
+            by_env.setdefault(env if env in self.env_algo else None, []).append(i)
+        out: list[RLExample | None] = [None] * len(recs)
+        for env, idx in by_env.items():
+            algo, scope, _ = self.env_algo[env] if env is not None else (self.algo, self.scope, self.eps)
+            for i, r in zip(idx, score_records(algo, [recs[i] for i in idx], scope, group_key=group)):
+                out[i] = r
+        return out
 
     def _filter_zero(self, recs: list[RLExample]) -> tuple[list[RLExample], int]:
         if not self.cfg.orchestrator.filter_zero_advantage or self.scope == "rollout":

@@ -60,7 +60,7 @@ def native_train_envs(cfg: RLConfig) -> list:
     from .reward import register_environment
 
     o = cfg.orchestrator
-    specs = [(e.id, e.args, e.ratio) for e in o.envs]
+    specs = [(e.id, env_args(e), e.ratio) for e in o.envs]
     if not specs and o.verifier_env_id:
         specs = [(o.verifier_env_id, o.verifier_env_args, 1.0)]
     out = []
@@ -71,6 +71,27 @@ def native_train_envs(cfg: RLConfig) -> list:
         env = environments.load_environment(env_id, **(args or {}))
         register_environment(env)
         out.append((env, float(ratio)))
+    return out
+
+
+def env_args(e) -> dict:
+    """An environment entry's loader arguments; ``data_path`` becomes the
+    loader's ``path`` (the native environments read their rows from it)."""
+    args = dict(e.args or {})
+    if getattr(e, "data_path", None) is not None:
+        args.setdefault("path", str(e.data_path))
+    return args
+
+
+def env_overrides(cfg) -> dict:
+    """Environment name -> its ``orchestrator.envs`` entry (per-environment
+    sampling, group size and algorithm)."""
+    from .. import environments
+
+    out = {}
+    for e in cfg.orchestrator.envs:
+        if environments.is_native(e.id):
+            out[environments.load_environment(e.id, **env_args(e)).name] = e
     return out
 
 

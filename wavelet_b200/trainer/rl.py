@@ -420,6 +420,19 @@ class RLTrainer:
             claimed.append(batch)
             yield [example_from_payload(r, self.config.data) for r in read_training_records(batch.training_path)]
 
+    def _log_samples(self, claimed: list) -> None:
+        """``monitor.samples``: a sample of this step's rollouts into samples.jsonl."""
+        sc = self.config.monitor.samples
+        if not sc.enabled or self.step % sc.interval != 0:
+            return
+        recs = [example_from_payload(r, self.config.data) for b in claimed
+                for r in read_training_records(b.training_path)]
+        if getattr(self, "_sample_tok", None) is None:
+            from ..data.tokenizer import tokenizer_for
+
+            self._sample_tok = tokenizer_for(self.config.model)
+        self.monitor.log_samples(sample_rows(recs, sc, self.config.seed, self.step, self._sample_tok), self.step)
+
     def run(self) -> int:
         from ..orchestrator.schedule import chunks_per_step
 
@@ -446,6 +459,8 @@ class RLTrainer:
                     for bt in claimed:
                         self.receiver.consumed(bt, before, self.step)
                 self.monitor.log(metrics, self.step)
+                if self.world.rank == 0:
+                    self._log_samples(claimed)
                 log.info("rl step %d loss %.4f grad_norm %.3f", self.step, metrics["loss"], metrics["optim/grad_norm"])
                 if self.step % c.policy_transfer.export_every_steps == 0:
                     self.exporter.export(self.model, self.step)
@@ -460,6 +475,40 @@ class RLTrainer:
                 self.ckpt.wait()
             self.exporter.close()
             self.monitor.finish(status=status, step=self.step)
+
+
+def sample_rows(records: list[RLExample], sample_cfg, seed: int, step: int, tokenizer=None) -> list[dict]:
+    """The rollouts of one step to keep in ``samples.jsonl``
+    (``monitor.samples``): ``sample_ratio`` of them (at least one), at most
+    ``max_samples``, drawn with a seed of the run and step; each row carries
+    the prompt and completion (decoded when a tokenizer is given), reward,
+    advantage and token counts."""
+    import random
+
+    if not records or (sample_cfg.sample_ratio is not None and sample_cfg.sample_ratio <= 0):
+        return []
+    n = len(records)
+    if sample_cfg.sample_ratio is not None:
+        n = max(1, int(len(records) * sample_cfg.sample_ratio))
+    if sample_cfg.max_samples is not None:
+        n = min(n, sample_cfg.max_samples)
+    picked = records if n >= len(records) else random.Random(seed + step).sample(records, n)
+    rows = []
+    for r in picked:
+        ids, mask = list(r.input_ids or []), list(r.loss_mask or [])
+        first = next((i for i, m in enumerate(mask) if m), len(ids))
+        prompt, completion = ids[:first], ids[first:]
+        md = r.metadata or {}
+        row = {"example_id": md.get("example_id", md.get("group")), "reward": r.reward,
+               "advantage": r.advantage if isinstance(r.advantage, (int, float)) else None,
+               "prompt_tokens": len(prompt), "completion_tokens": len(completion)}
+        if tokenizer is not None:
+            row["prompt"] = tokenizer.decode(prompt)
+            row["completion"] = tokenizer.decode(completion)
+        else:
+            row["prompt_ids"], row["completion_ids"] = prompt, completion
+        rows.append(row)
+    return rows
 
 
 def _lora_meta(cfg, model) -> dict:
