@@ -41,8 +41,6 @@ INERT: dict[str, str] = {
     "inference.vllm.data_parallel_size_local": _GENERATOR,
     "inference.vllm.data_parallel_rpc_port": _GENERATOR,
     "inference.vllm.fully_sharded_loras": _GENERATOR,
-    "inference.vllm.tool_call_parser": _GENERATOR,
-    "inference.vllm.reasoning_parser": _GENERATOR,
     "inference.vllm.enable_fp32_lm_head": "the generator samples from bf16 logits of an fp32-accumulated GEMM",
     "inference.vllm.enable_fp32_router_logits": "router logits follow model.moe_router_dtype",
     "inference.vllm.use_generation_logprobs": "generation log-probs always come from the sampling kernel",

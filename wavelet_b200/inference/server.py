@@ -11,6 +11,9 @@ and native_server.py:92-215):
     POST /score                  teacher-forced log-probs of given token sequences
     POST /v1/completions         {"prompt_token_ids" | "prompt", sampling...}
     POST /v1/chat/completions[/tokens], /chat/completions/tokens
+                                 reasoning / tool calls split by the configured
+                                 parsers (inference/parsers.py), max_tokens
+                                 fitted to the context
     POST /tokenize, /v1/tokenize
 
 Generation requests are serialised by a gate that ``/pause`` closes while a
@@ -29,6 +32,9 @@ from typing import Any
 from ..configs.config import RLConfig
 from ..data.rl import example_from_payload, example_to_payload
 from ..utils.config import load_config
+from .parsers import ChatOutputParser
+
+CONTEXT_FIT_SAFETY_TOKENS = 16  # tokens kept free when a request's max_tokens is fitted to the context
 
 
 class GenerationGate:
@@ -205,15 +211,55 @@ def build_app(config: RLConfig, engine=None):
                              "logprobs": {"token_logprobs": c.logprobs}, "text": tok.decode(c.token_ids),
                              "finish_reason": c.finish_reason} for i, c in enumerate(comps)]}
 
+    vcfg = config.inference.vllm
+    out_parser = ChatOutputParser.for_model(config.model.name, vcfg.reasoning_parser, vcfg.tool_call_parser)
+
+    def _max_model_len() -> int:
+        g = getattr(engine, "generator", None)
+        return int(getattr(g, "max_model_len", None) or vcfg.max_model_len or config.data.seq_len)
+
     def _chat(payload: dict[str, Any]):
-        ids = tok.apply_chat_template(payload["messages"], tokenize=True, add_generation_prompt=True)
-        ids = list(ids["input_ids"] if isinstance(ids, dict) else ids)
-        comps = _complete([ids], payload)
+        """OpenAI chat completion.  ``tokens`` (the ``/chat/completions/tokens``
+        routes) is the rendered prompt; otherwise ``messages`` is rendered with
+        the chat template, with ``tools`` and ``chat_template_kwargs``.  The
+        completion is split into reasoning, content and tool calls by the
+        configured parsers, and a request whose prompt plus ``max_tokens``
+        overruns the context gets its ``max_tokens`` fitted
+        (ref inference/server.py:186-220, 482-520)."""
+        kwargs = dict(payload.get("chat_template_kwargs") or {})
+        tools = payload.get("tools") or None
+        if payload.get("tokens") is not None:
+            ids = [int(t) for t in payload["tokens"]]
+        else:
+            extra = {"tools": tools} if tools else {}
+            ids = tok.apply_chat_template(payload["messages"], tokenize=True, add_generation_prompt=True,
+                                          **extra, **kwargs)
+            ids = list(ids["input_ids"] if isinstance(ids, dict) else ids)
+        limit = _max_model_len()
+        if len(ids) >= limit:
+            raise HTTPException(status_code=400, detail=f"This model's maximum context length is {limit} tokens. "
+                                                        f"However, your request has {len(ids)} input tokens.")
+        req = dict(payload)
+        asked = payload.get("max_completion_tokens") or payload.get("max_tokens") \
+            or config.inference.sampling.max_completion_tokens or 256
+        room = max(limit - len(ids) - CONTEXT_FIT_SAFETY_TOKENS, 1)
+        req["max_completion_tokens"] = min(int(asked), room)
+        comps = _complete([ids], req)
+        choices = []
+        for i, c in enumerate(comps):
+            parsed = out_parser.parse(tok.decode(c.token_ids), tools=tools,
+                                      tool_choice=payload.get("tool_choice", "auto"),
+                                      include_reasoning=bool(payload.get("include_reasoning", True)),
+                                      chat_template_kwargs=kwargs)
+            finish = "tool_calls" if parsed.tool_calls and c.finish_reason == "stop" else c.finish_reason
+            choices.append({"index": i, "message": parsed.message(), "token_ids": c.token_ids,
+                            "logprobs": {"content": [{"token_id": t, "logprob": lp}
+                                                     for t, lp in zip(c.token_ids, c.logprobs)]},
+                            "finish_reason": finish})
+        n_out = sum(len(c.token_ids) for c in comps)
         return {"object": "chat.completion", "model": config.model.name, "prompt_token_ids": ids,
-                "choices": [{"index": i, "message": {"role": "assistant", "content": tok.decode(c.token_ids)},
-                             "token_ids": c.token_ids,
-                             "logprobs": {"content": [{"token_id": t, "logprob": lp} for t, lp in zip(c.token_ids, c.logprobs)]},
-                             "finish_reason": c.finish_reason} for i, c in enumerate(comps)]}
+                "choices": choices,
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}}
 
     app.post("/v1/chat/completions")(_chat)
     app.post("/v1/chat/completions/tokens")(_chat)
