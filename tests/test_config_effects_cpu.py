@@ -114,11 +114,15 @@ def test_rollout_columns_round_trip_under_renames():
     assert example_from_payload(ext, data).advantage == -1.0
 
 
-def test_token_batches_and_rollout_selection_are_refused():
+def test_token_batches_are_refused_rollout_selection_is_checked():
     with pytest.raises(ValueError, match="token_batch_size"):
         RLConfig.model_validate({"orchestrator": {"examples_per_step": None, "token_batch_size": 4096}})
-    with pytest.raises(ValueError, match="batch_selection"):
+    with pytest.raises(ValueError, match="requires examples_per_step"):
         RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "refill_zero_advantage": False}})
+    with pytest.raises(ValueError, match="refill_zero_advantage=false"):
+        RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "examples_per_step": 2}})
+    RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "examples_per_step": 2,
+                                              "refill_zero_advantage": False}})
     msgs = inert_settings(RLConfig.model_validate({"orchestrator": {"oversampling_factor": 2.0}}))
     assert msgs and msgs[0].startswith("orchestrator.oversampling_factor")
 

@@ -16,7 +16,9 @@ from typing import Annotated, Any, Literal
 
 from pydantic import AliasChoices, BaseModel, ConfigDict, Field, SecretStr, model_validator
 
-VERIFIER_ROLLOUT_FUNCTION = "wavelet.orchestrator.verifiers:generate_and_score"
+VERIFIER_ROLLOUT_FUNCTION = "wavelet.orchestrator.verifiers:generate_rollouts"
+# every value of orchestrator.custom_rollout_function that selects verifiers-package rollouts
+VERIFIER_ROLLOUT_FUNCTIONS = (VERIFIER_ROLLOUT_FUNCTION, "wavelet.orchestrator.verifiers:generate_and_score", "verifiers")
 
 
 class ConfigModel(BaseModel):
@@ -1136,7 +1138,7 @@ class RLOrchestratorConfig(ConfigModel):
 
     @property
     def uses_verifiers(self) -> bool:
-        return self.custom_rollout_function == VERIFIER_ROLLOUT_FUNCTION
+        return self.custom_rollout_function in VERIFIER_ROLLOUT_FUNCTIONS
 
     @model_validator(mode="after")
     def _checks(self):
@@ -1149,9 +1151,6 @@ class RLOrchestratorConfig(ConfigModel):
         if self.token_batch_size is not None:
             raise ValueError("orchestrator.token_batch_size (batches sized by tokens) is not supported: the rollout "
                              "role fills optimizer steps by prompt groups (orchestrator.examples_per_step)")
-        if self.batch_selection == "rollouts":
-            raise ValueError("orchestrator.batch_selection='rollouts' is not supported: batches are whole prompt "
-                             "groups ('groups')")
         if self.envs and self.verifier_env_id is not None:
             raise ValueError("Set orchestrator.envs or legacy orchestrator.verifier_env_id, not both.")
         if self.envs and self.verifier_env_args:

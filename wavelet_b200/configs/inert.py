@@ -50,17 +50,10 @@ INERT: dict[str, str] = {
     "inference.vllm.openai_batch_max_size": "the server batches the requests it has",
     "inference.vllm.extra_args": "there is no vLLM engine to pass them to",
     "inference.sampling.extra_body": "there is no OpenAI-compatible engine behind the sampler",
-    "orchestrator.verifier_model": "verifiers-package environments are not loaded",
-    "orchestrator.verifier_base_url": "verifiers-package environments are not loaded",
-    "orchestrator.verifier_api_key_var": "verifiers-package environments are not loaded",
-    "orchestrator.verifier_client_type": "verifiers-package environments are not loaded",
-    "orchestrator.verifier_timeout_seconds": "verifiers-package environments are not loaded",
-    "orchestrator.verifier_max_total_completion_tokens": "verifiers-package environments are not loaded",
     "orchestrator.oversampling_factor": "each step generates exactly its prompt groups",
     "orchestrator.max_inflight_rollouts": "a step's prompt groups are generated as one batch",
     "orchestrator.max_pending_rollout_chunks": "in-flight steps are bounded by max_async_level",
     "orchestrator.materialize_path": "`debug orchestrator materialize` takes its output path as an argument",
-    "eval.max_inflight_rollouts": "an eval environment is generated as one batch",
     "eval.background": "evals run in the rollout role after the policy load that triggers them",
     "eval.cancel_on_new_policy": "evals run to completion on the policy that triggered them",
     "eval.keep_last_rollout_sets": "eval results are appended to eval_metrics.jsonl",

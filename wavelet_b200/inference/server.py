@@ -253,7 +253,7 @@ def build_app(config: RLConfig, engine=None):
                                       chat_template_kwargs=kwargs)
             finish = "tool_calls" if parsed.tool_calls and c.finish_reason == "stop" else c.finish_reason
             choices.append({"index": i, "message": parsed.message(), "token_ids": c.token_ids,
-                            "logprobs": {"content": [{"token_id": t, "logprob": lp}
+                            "logprobs": {"content": [{"token": f"token_id:{t}", "token_id": t, "logprob": lp}
                                                      for t, lp in zip(c.token_ids, c.logprobs)]},
                             "finish_reason": finish})
         n_out = sum(len(c.token_ids) for c in comps)

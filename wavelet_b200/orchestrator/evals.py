@@ -94,10 +94,21 @@ def _env_prompts(cfg, env):
         return EnvironmentPromptSource([(e, 1.0)], cfg.model.name, seed=int(a.get("seed", 0)),
                                        split="eval" if e.eval_examples else "train", model_cfg=cfg.model)
     raise ValueError(f"unknown eval environment {env.id!r} (built-ins: reverse, file:<path>, "
-                     f"{', '.join(environments.available())})")
+                     f"{', '.join(environments.available())}; other ids need the verifiers package, "
+                     f"which is not installed)")
+
+
+def _builtin(env) -> bool:
+    return env.id.startswith("file:") or env.resolved_name in ("reverse", "reverse_match", "synthetic-reverse") \
+        or _native(env.id)
 
 
 def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]:
+    if not _builtin(env):
+        from .verifier_envs import evaluate, verifiers_available
+
+        if verifiers_available():  # a verifiers-package environment rolls out against the inference servers
+            return evaluate(cfg, env, step=step, out_dir=out_dir, engine=engine)
     n_ex = env.num_examples if env.num_examples > 0 else 32
     k = env.rollouts_per_example
     reward_cfg = cfg.reward

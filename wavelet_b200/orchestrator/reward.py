@@ -71,6 +71,8 @@ class RLRewardScorer:
     def score(self, r: RLExample) -> float:
         c = self.cfg
         md = r.metadata or {}
+        if md.get("reward_source") in ("verifier", "custom") and r.reward is not None:
+            return float(r.reward)  # scored by its verifiers-package environment / the user rollout function
         if md.get("env") and (c.mode == "environment" or (c.mode == "passthrough" and r.reward is None)):
             from .. import environments
 

@@ -79,6 +79,19 @@ class RLOrchestrator:
             self.env_cfg = env_overrides(cfg)
         self.env_algo = {n: (build_algorithm(e.algo), algorithm_scope(e.algo), algorithm_epsilon(e.algo))
                          for n, e in self.env_cfg.items() if e.algo is not None}
+        # prompts of verifiers-package environments are rolled out by the environments themselves
+        vf_envs = {e.name: e for e, _ in getattr(prompts, "envs", [])
+                   if getattr(e, "metadata", {}).get("kind") == "verifiers"}
+        if vf_envs and self.custom_rollout is None:
+            from .verifier_envs import VerifierRollouts
+
+            self.custom_rollout = VerifierRollouts(cfg, vf_envs, engine, fallback=self.generate_records)
+        # a user rollout function ("module.path:function") replaces generation and scoring
+        fn_path = getattr(getattr(cfg, "orchestrator", None), "custom_rollout_function", None)
+        if fn_path and self.custom_rollout is None and not cfg.orchestrator.uses_verifiers:
+            from .custom_rollout import CustomRollout
+
+            self.custom_rollout = CustomRollout(self, fn_path, engine)
 
     def _sampling(self):
         from ..inference.engine import SamplingParams
@@ -210,6 +223,11 @@ class RLOrchestrator:
     def _filter_zero(self, recs: list[RLExample]) -> tuple[list[RLExample], int]:
         if not self.cfg.orchestrator.filter_zero_advantage or self.scope == "rollout":
             return recs, 0
+        if self.cfg.orchestrator.batch_selection == "rollouts":
+            # rollouts count one by one: a zero-advantage rollout is left out on its own (its reward is
+            # still in the step's metrics) unless a CE / ref-KL weight still trains it
+            keep = [r for r in recs if abs(float(r.advantage or 0.0)) > 0.0 or _aux_weighted(r)]
+            return keep, len(recs) - len(keep)
         groups: dict[Any, list[RLExample]] = {}
         for r in recs:
             groups.setdefault((r.metadata or {}).get("group"), []).append(r)
@@ -253,23 +271,32 @@ class RLOrchestrator:
         view.last_stats = {}
         return view
 
+    def _rollout(self, prompts: list[PromptRecord], step: int) -> list[RLExample]:
+        if self.custom_rollout is None:
+            return self.generate_records(prompts, step)
+        recs = self.custom_rollout(prompts, step)
+        self.last_stats.update(getattr(self.custom_rollout, "last_stats", None) or {})
+        return recs
+
     def materialize(self, step: int) -> list[RLExample]:
         o = self.cfg.orchestrator
         n_prompts = o.examples_per_step or 1
         prompts = self.prompts.take(n_prompts)
-        recs = self.score(self.custom_rollout(prompts, step) if self.custom_rollout else self.generate_records(prompts, step))
+        recs = self.score(self._rollout(prompts, step))
         recs, gated = self._curriculum_gate(recs)
         kept, dropped = self._filter_zero(recs)
         retries = 0
         while (o.refill_zero_advantage and dropped and retries < o.zero_advantage_max_retries
                and len(kept) < len(recs)):
             need = max(1, dropped // max(1, o.rollouts_per_example or 1))
-            more, _ = self._curriculum_gate(self.score(self.generate_records(self.prompts.take(need), step)))
+            more, _ = self._curriculum_gate(self.score(self._rollout(self.prompts.take(need), step)))
             more_kept, dropped = self._filter_zero(more)
             kept += more_kept
             retries += 1
         if not kept:
             kept = recs  # never publish an empty batch; zero-advantage rows contribute no gradient
+        if o.batch_selection == "rollouts":
+            kept = _trim_rollouts(kept, n_prompts * (o.rollouts_per_example or 1))
         from .teacher import attach_teacher_logprobs, scorer_for
 
         kept = attach_teacher_logprobs(kept, self.cfg, scorer_for(self.cfg, self.engine))  # OPD / OPSD
@@ -290,3 +317,26 @@ class RLOrchestrator:
             return recs
         return self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=policy_step,
                                    tokens=tokens, reward_mean=self.last_stats.get("reward/mean"))
+
+
+def _aux_weighted(r: RLExample) -> bool:
+    """True when a CE or reference-KL weight still trains the record."""
+    for w in (r.ce_weight, r.ref_kl_weight):
+        if isinstance(w, list) and any(x != 0.0 for x in w):
+            return True
+        if w is not None and not isinstance(w, list) and w != 0.0:
+            return True
+    return False
+
+
+def _trim_rollouts(recs: list[RLExample], target: int) -> list[RLExample]:
+    """The first ``target`` rollouts (every row of a multi-row rollout stays
+    with it; ``metadata.rollout_count`` is 0 on a rollout's later rows)."""
+    out, n = [], 0
+    for r in recs:
+        c = int((r.metadata or {}).get("rollout_count", 1))
+        if c and n >= target:
+            break
+        out.append(r)
+        n += c
+    return out

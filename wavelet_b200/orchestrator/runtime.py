@@ -41,7 +41,7 @@ def build_prompt_source(cfg: RLConfig, vocab: int, rank: int = 0):
     """Prompt source for the orchestrator: synthetic reverse-text prompts
     (``data.source: fake``) or pretokenised prompt rows from local files."""
     d = cfg.data
-    envs = native_train_envs(cfg)
+    envs = train_envs(cfg)
     if envs:
         from .sources import EnvironmentPromptSource
 
@@ -53,9 +53,11 @@ def build_prompt_source(cfg: RLConfig, vocab: int, rank: int = 0):
     return FilePromptSource(cfg, rank=rank)
 
 
-def native_train_envs(cfg: RLConfig) -> list:
-    """(Environment, ratio) of every training environment that is a native
-    one (``orchestrator.envs`` / ``orchestrator.verifier_env_id``)."""
+def train_envs(cfg: RLConfig) -> list:
+    """(environment, ratio) of every training environment
+    (``orchestrator.envs`` / ``orchestrator.verifier_env_id``): native ones
+    from ``wavelet_b200.environments``, any other id from the ``verifiers``
+    package (``orchestrator.verifier_envs``)."""
     from .. import environments
     from .reward import register_environment
 
@@ -63,15 +65,25 @@ def native_train_envs(cfg: RLConfig) -> list:
     specs = [(e.id, env_args(e), e.ratio) for e in o.envs]
     if not specs and o.verifier_env_id:
         specs = [(o.verifier_env_id, o.verifier_env_args, 1.0)]
-    out = []
-    for env_id, args, ratio in specs:
-        if not environments.is_native(env_id):
-            raise ValueError(f"environment {env_id!r} needs the verifiers package, which is not installed; "
-                             f"native environments: {', '.join(environments.available())}")
-        env = environments.load_environment(env_id, **(args or {}))
-        register_environment(env)
-        out.append((env, float(ratio)))
+    out: list = [None] * len(specs)
+    foreign = [i for i, (env_id, _, _) in enumerate(specs) if not environments.is_native(env_id)]
+    if foreign:
+        from .verifier_envs import verifier_train_envs, verifiers_available
+
+        if not verifiers_available():
+            raise ValueError(f"environment {specs[foreign[0]][0]!r} needs the verifiers package, which is not "
+                             f"installed; native environments: {', '.join(environments.available())}")
+        for i, pair in zip(foreign, verifier_train_envs(cfg, [specs[i] for i in foreign])):
+            out[i] = pair
+    for i, (env_id, args, ratio) in enumerate(specs):
+        if out[i] is None:
+            env = environments.load_environment(env_id, **(args or {}))
+            register_environment(env)
+            out[i] = (env, float(ratio))
     return out
+
+
+native_train_envs = train_envs  # the name earlier callers import
 
 
 def env_args(e) -> dict:
@@ -92,6 +104,8 @@ def env_overrides(cfg) -> dict:
     for e in cfg.orchestrator.envs:
         if environments.is_native(e.id):
             out[environments.load_environment(e.id, **env_args(e)).name] = e
+        else:  # a verifiers-package environment goes by its entry's name
+            out[e.resolved_name] = e
     return out
 
 
@@ -150,6 +164,9 @@ class IntegratedRunner:
         if self.world.rank == 0 and t.step > 0:
             prune_from(self.sender.queue_dir, t.step)
         prompts = build_prompt_source(c, t.model.cfg.vocab_size, rank=t.dp_rank)
+        if any(getattr(e, "metadata", {}).get("kind") == "verifiers" for e, _ in getattr(prompts, "envs", [])):
+            raise ValueError("verifiers-package environments call the inference servers over HTTP; "
+                             "run them with launcher.mode: process")
         self.orch = RLOrchestrator(c, self.engine, None, prompts, monitor=t.monitor)
         return self
 

@@ -19,9 +19,10 @@ from typing import Any
 
 from .rollouts import PromptRecord
 
-# Names of rollout functions a config may select (orchestrator.custom_rollout_function)
+# orchestrator.custom_rollout_function: unset = the native generator, one of
+# VERIFIER_ROLLOUT_FUNCTIONS = verifiers-package environments, any other
+# "module.path:function" = a user rollout function (orchestrator.custom_rollout)
 NATIVE_ROLLOUT_FUNCTION = "native"
-VERIFIER_ROLLOUT_FUNCTION = "verifiers"
 
 
 def _read_rows(path: Path) -> list[dict[str, Any]]:
