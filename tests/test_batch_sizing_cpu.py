@@ -1,0 +1,68 @@
+"""Token-sized rollout steps (orchestrator.token_batch_size): groups are drawn
+in rounds sized from the running tokens-per-group estimate until the kept rows
+hold the target (ref orchestrator/scheduler.py:553-560)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import pytest
+
+from wavelet_b200.configs.config import RLConfig
+
+
+@dataclass
+class _Comp:
+    prompt_index: int
+    sample_index: int
+    token_ids: list
+    logprobs: list
+    finish_reason: str = "stop"
+    sampling_mask: list | None = None
+
+
+class _Engine:
+    def __init__(self, comp_len=5):
+        self.comp_len = comp_len
+        self.calls = []
+
+    def generate(self, prompts, params):
+        self.calls.append(len(prompts))
+        return [_Comp(i, k, [3] * self.comp_len, [-0.5] * self.comp_len)
+                for i in range(len(prompts)) for k in range(params.n)]
+
+
+def _cfg(tmp_path, **orch):
+    return RLConfig.model_validate({
+        "model": {"name": "tiny", "random_init": True},
+        "data": {"source": "fake", "seq_len": 64, "fake_vocab_size": 64, "fake_prompt_len": 6},
+        "orchestrator": {"examples_per_step": None, "rollouts_per_example": 2, "filter_zero_advantage": False,
+                         **orch},
+        "reward": {"mode": "reverse_match"}, "algo": {"type": "grpo"},
+        "lora": None, "output_dir": str(tmp_path / "out")})
+
+
+def test_token_batches_fill_to_the_target(tmp_path):
+    from wavelet_b200.orchestrator.rollouts import RLOrchestrator
+    from wavelet_b200.orchestrator.runtime import build_prompt_source
+
+    cfg = _cfg(tmp_path, token_batch_size=100)
+    eng = _Engine()
+    orch = RLOrchestrator(cfg, eng, None, build_prompt_source(cfg, 64))
+    recs = orch.materialize(0)
+    # one group first (2 rollouts x 11 tokens = 22), then ceil(78 / 22) = 4 more groups
+    assert eng.calls == [1, 4]
+    assert sum(len(r.input_ids) for r in recs) == 110 and len(recs) == 10
+    assert orch.last_stats["rollout/token_batch_tokens"] == 110.0
+    assert orch.last_stats["rollout/token_batch_rounds"] == 2.0
+    # the next step starts from the estimate: one round of ceil(100 / 22) = 5 groups
+    orch.materialize(1)
+    assert eng.calls[-1] == 5
+
+
+def test_token_batch_rules():
+    with pytest.raises(ValueError, match="only one of"):
+        RLConfig.model_validate({"orchestrator": {"examples_per_step": 2, "token_batch_size": 64}})
+    with pytest.raises(ValueError, match="rollout_chunk_examples cannot be combined"):
+        RLConfig.model_validate({"orchestrator": {"examples_per_step": None, "token_batch_size": 64,
+                                                  "rollout_chunk_examples": 1}})

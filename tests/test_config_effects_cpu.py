@@ -114,9 +114,7 @@ def test_rollout_columns_round_trip_under_renames():
     assert example_from_payload(ext, data).advantage == -1.0
 
 
-def test_token_batches_are_refused_rollout_selection_is_checked():
-    with pytest.raises(ValueError, match="token_batch_size"):
-        RLConfig.model_validate({"orchestrator": {"examples_per_step": None, "token_batch_size": 4096}})
+def test_rollout_selection_is_checked():
     with pytest.raises(ValueError, match="requires examples_per_step"):
         RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "refill_zero_advantage": False}})
     with pytest.raises(ValueError, match="refill_zero_advantage=false"):

@@ -1148,9 +1148,12 @@ class RLOrchestratorConfig(ConfigModel):
             raise ValueError("batch_selection='rollouts' requires refill_zero_advantage=false.")
         if self.examples_per_step is not None and self.token_batch_size is not None:
             raise ValueError("Set only one of orchestrator.examples_per_step and orchestrator.token_batch_size.")
-        if self.token_batch_size is not None:
-            raise ValueError("orchestrator.token_batch_size (batches sized by tokens) is not supported: the rollout "
-                             "role fills optimizer steps by prompt groups (orchestrator.examples_per_step)")
+        if self.token_batch_size is not None and self.rollout_chunk_examples is not None:
+            raise ValueError("orchestrator.rollout_chunk_examples cannot be combined with orchestrator.token_batch_size; "
+                             "token batches are one dynamic chunk per optimizer step.")
+        if self.token_batch_size is not None and self.batch_selection == "rollouts":
+            raise ValueError("orchestrator.token_batch_size counts the tokens of whole groups; "
+                             "use batch_selection='groups'.")
         if self.envs and self.verifier_env_id is not None:
             raise ValueError("Set orchestrator.envs or legacy orchestrator.verifier_env_id, not both.")
         if self.envs and self.verifier_env_args:

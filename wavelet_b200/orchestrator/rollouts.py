@@ -6,11 +6,15 @@ reference) selects the step's prompts, asks the inference engine for
 log-probs + optional sampling masks), scores rewards, assigns advantages with
 the configured algorithm, drops zero-advantage groups (optionally refilling
 them up to ``zero_advantage_max_retries``), and publishes the batch to the
-filesystem queue as ``RLExample`` training records.
+filesystem queue as ``RLExample`` training records.  A step holds
+``examples_per_step`` prompt groups, or groups drawn until their rows hold
+``token_batch_size`` tokens; with ``batch_selection: rollouts`` rollouts
+count one by one instead of whole groups.
 """
 
 from __future__ import annotations
 
+import math
 import random
 import time
 from dataclasses import dataclass, field
@@ -79,6 +83,9 @@ class RLOrchestrator:
             self.env_cfg = env_overrides(cfg)
         self.env_algo = {n: (build_algorithm(e.algo), algorithm_scope(e.algo), algorithm_epsilon(e.algo))
                          for n, e in self.env_cfg.items() if e.algo is not None}
+        # tokens per prompt group seen so far (token-sized steps); views of this
+        # orchestrator share the one dict
+        self._token_estimate = {"tokens": 0, "groups": 0}
         # prompts of verifiers-package environments are rolled out by the environments themselves
         vf_envs = {e.name: e for e, _ in getattr(prompts, "envs", [])
                    if getattr(e, "metadata", {}).get("kind") == "verifiers"}
@@ -278,8 +285,51 @@ class RLOrchestrator:
         self.last_stats.update(getattr(self.custom_rollout, "last_stats", None) or {})
         return recs
 
+    def _materialize_tokens(self, step: int) -> list[RLExample]:
+        """A step sized by tokens (``orchestrator.token_batch_size``): prompt
+        groups are drawn in rounds, each sized from the running tokens-per-group
+        estimate (shared across steps), until the kept rows hold at least the
+        target; the last round may overshoot by less than its groups' tokens
+        (ref orchestrator/scheduler.py:553-560, 700-760)."""
+        o = self.cfg.orchestrator
+        target = int(o.token_batch_size)
+        est = self._token_estimate
+        kept: list[RLExample] = []
+        scored: list[RLExample] = []
+        tokens = dropped = gated = rounds = 0
+        while tokens < target and rounds < 64:
+            per_group = est["tokens"] / est["groups"] if est["groups"] else 0.0
+            need = max(1, math.ceil((target - tokens) / per_group)) if per_group > 0 else 1
+            recs = self.score(self._rollout(self.prompts.take(need), step))
+            recs, g = self._curriculum_gate(recs)
+            k, d = self._filter_zero(recs)
+            scored += recs
+            kept += k
+            gated += g
+            dropped += d
+            n_tok = sum(len(r.input_ids or []) for r in recs)
+            n_groups = len({(r.metadata or {}).get("group") for r in recs})
+            est["tokens"] += n_tok
+            est["groups"] += n_groups
+            tokens += sum(len(r.input_ids or []) for r in k)
+            rounds += 1
+        if not kept:
+            kept = scored
+        from .teacher import attach_teacher_logprobs, scorer_for
+
+        kept = attach_teacher_logprobs(kept, self.cfg, scorer_for(self.cfg, self.engine))
+        rewards = [float(r.reward or 0.0) for r in scored]
+        self.last_stats.update({"reward/mean": sum(rewards) / max(1, len(rewards)),
+                                "rollout/curriculum_rejected": float(gated),
+                                "rollout/zero_advantage_dropped": float(dropped),
+                                "rollout/token_batch_tokens": float(tokens),
+                                "rollout/token_batch_rounds": float(rounds)})
+        return kept
+
     def materialize(self, step: int) -> list[RLExample]:
         o = self.cfg.orchestrator
+        if getattr(o, "token_batch_size", None):
+            return self._materialize_tokens(step)
         n_prompts = o.examples_per_step or 1
         prompts = self.prompts.take(n_prompts)
         recs = self.score(self._rollout(prompts, step))
