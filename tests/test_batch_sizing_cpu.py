@@ -66,3 +66,28 @@ def test_token_batch_rules():
     with pytest.raises(ValueError, match="rollout_chunk_examples cannot be combined"):
         RLConfig.model_validate({"orchestrator": {"examples_per_step": None, "token_batch_size": 64,
                                                   "rollout_chunk_examples": 1}})
+
+
+def test_oversampling_keeps_the_first_usable_groups(tmp_path):
+    from wavelet_b200.orchestrator.rollouts import RLOrchestrator
+    from wavelet_b200.orchestrator.runtime import build_prompt_source
+
+    cfg = _cfg(tmp_path, examples_per_step=2, oversampling_factor=2.0)
+    eng = _Engine()
+    orch = RLOrchestrator(cfg, eng, None, build_prompt_source(cfg, 64))
+    recs = orch.materialize(0)
+    assert eng.calls == [4]  # ceil(2 x 2.0) groups generated
+    assert len({r.metadata["group"] for r in recs}) == 2 and len(recs) == 4
+
+
+def test_eval_rollout_sets_are_pruned(tmp_path):
+    from wavelet_b200.orchestrator.evals import prune_eval_sets
+
+    d = tmp_path / "evals" / "env"
+    d.mkdir(parents=True)
+    for s in (0, 5, 10, 20):
+        (d / f"step-{s}.jsonl").write_text("{}\n")
+    (d / "notes.txt").write_text("x")
+    removed = prune_eval_sets(d, 2)
+    assert sorted(p.name for p in removed) == ["step-0.jsonl", "step-5.jsonl"]
+    assert sorted(p.name for p in d.iterdir()) == ["notes.txt", "step-10.jsonl", "step-20.jsonl"]

@@ -121,8 +121,8 @@ def test_rollout_selection_is_checked():
         RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "examples_per_step": 2}})
     RLConfig.model_validate({"orchestrator": {"batch_selection": "rollouts", "examples_per_step": 2,
                                               "refill_zero_advantage": False}})
-    msgs = inert_settings(RLConfig.model_validate({"orchestrator": {"oversampling_factor": 2.0}}))
-    assert msgs and msgs[0].startswith("orchestrator.oversampling_factor")
+    msgs = inert_settings(RLConfig.model_validate({"orchestrator": {"max_pending_rollout_chunks": 2}}))
+    assert msgs and msgs[0].startswith("orchestrator.max_pending_rollout_chunks")
 
 
 def test_sample_rows_ratio_cap_and_decoding():

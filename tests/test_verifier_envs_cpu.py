@@ -265,3 +265,28 @@ def test_evaluation_metrics_and_files(tmp_path, fake_vf):
     rows = [json.loads(line) for line in (tmp_path / "out" / "evals" / "fe" / "step-5.jsonl").read_text().splitlines()]
     assert len(rows) == 6 and sum("error" in r for r in rows) == 2
     assert json.loads((tmp_path / "out" / "eval_metrics.jsonl").read_text().splitlines()[-1])["step"] == 5
+
+
+def test_inflight_rollouts_are_capped(tmp_path, fake_vf):
+    import asyncio
+
+    from wavelet_b200.orchestrator import verifier_envs
+
+    state = {"now": 0, "peak": 0}
+    orig = FakeEnv.run_rollout
+
+    async def slow(self, *a, **k):
+        state["now"] += 1
+        state["peak"] = max(state["peak"], state["now"])
+        await asyncio.sleep(0.01)
+        state["now"] -= 1
+        return await orig(self, *a, **k)
+
+    FakeEnv.run_rollout = slow
+    try:
+        cfg = _cfg(tmp_path, [{"id": "fake-env", "args": {"n": 2}}], max_inflight_rollouts=5)
+        recs = _orchestrator(cfg).materialize(0)
+    finally:
+        FakeEnv.run_rollout = orig
+    assert len(recs) == 8 and state["peak"] == 5
+    assert verifier_envs is not None

@@ -49,14 +49,12 @@ INERT: dict[str, str] = {
     "inference.vllm.openai_batch_max_wait_seconds": "the server batches the requests it has",
     "inference.vllm.openai_batch_max_size": "the server batches the requests it has",
     "inference.vllm.extra_args": "there is no vLLM engine to pass them to",
-    "inference.sampling.extra_body": "there is no OpenAI-compatible engine behind the sampler",
-    "orchestrator.oversampling_factor": "each step generates exactly its prompt groups",
-    "orchestrator.max_inflight_rollouts": "a step's prompt groups are generated as one batch",
+    "inference.sampling.extra_body": "the native sampler has no extra request fields (verifiers-package "
+                                     "rollouts pass them to the server)",
     "orchestrator.max_pending_rollout_chunks": "in-flight steps are bounded by max_async_level",
     "orchestrator.materialize_path": "`debug orchestrator materialize` takes its output path as an argument",
     "eval.background": "evals run in the rollout role after the policy load that triggers them",
     "eval.cancel_on_new_policy": "evals run to completion on the policy that triggered them",
-    "eval.keep_last_rollout_sets": "eval results are appended to eval_metrics.jsonl",
     "eval.model_revision": "evals use the policy snapshots of this run",
 }
 

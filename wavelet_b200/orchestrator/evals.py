@@ -67,6 +67,23 @@ def group_metrics(prefix: str, by_example: dict[str, list[float | None]], thresh
     return m
 
 
+def prune_eval_sets(env_dir: Path, keep: int | None) -> list[Path]:
+    """Keep the newest ``keep`` rollout files (``step-<n>.jsonl``) of one
+    environment's eval directory (``eval.keep_last_rollout_sets``)."""
+    if keep is None or not env_dir.is_dir():
+        return []
+    sets = []
+    for f in env_dir.glob("step-*.jsonl"):
+        try:
+            sets.append((int(f.stem.split("-", 1)[1]), f))
+        except ValueError:
+            continue
+    removed = [f for _, f in sorted(sets)[:-keep]] if keep > 0 else [f for _, f in sets]
+    for f in removed:
+        f.unlink()
+    return removed
+
+
 def _native(env_id: str) -> bool:
     from .. import environments
 
@@ -146,6 +163,7 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
             md = r.metadata or {}
             f.write(json.dumps({"example_id": md.get("example_id"), "reward": r.reward,
                                 "completion_ids": md.get("completion_ids")}) + "\n")
+    prune_eval_sets(d, getattr(cfg.eval, "keep_last_rollout_sets", None))
     return m
 
 

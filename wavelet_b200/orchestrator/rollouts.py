@@ -331,7 +331,8 @@ class RLOrchestrator:
         if getattr(o, "token_batch_size", None):
             return self._materialize_tokens(step)
         n_prompts = o.examples_per_step or 1
-        prompts = self.prompts.take(n_prompts)
+        # oversampling_factor: draw more groups than the step needs, keep the first usable ones
+        prompts = self.prompts.take(max(n_prompts, math.ceil(n_prompts * float(getattr(o, "oversampling_factor", 1.0)))))
         recs = self.score(self._rollout(prompts, step))
         recs, gated = self._curriculum_gate(recs)
         kept, dropped = self._filter_zero(recs)
@@ -347,6 +348,8 @@ class RLOrchestrator:
             kept = recs  # never publish an empty batch; zero-advantage rows contribute no gradient
         if o.batch_selection == "rollouts":
             kept = _trim_rollouts(kept, n_prompts * (o.rollouts_per_example or 1))
+        elif len(prompts) > n_prompts:
+            kept = _trim_groups(kept, n_prompts)
         from .teacher import attach_teacher_logprobs, scorer_for
 
         kept = attach_teacher_logprobs(kept, self.cfg, scorer_for(self.cfg, self.engine))  # OPD / OPSD
@@ -389,4 +392,18 @@ def _trim_rollouts(recs: list[RLExample], target: int) -> list[RLExample]:
             break
         out.append(r)
         n += c
+    return out
+
+
+def _trim_groups(recs: list[RLExample], n_groups: int) -> list[RLExample]:
+    """The records of the first ``n_groups`` prompt groups, in order."""
+    seen: set = set()
+    out = []
+    for r in recs:
+        g = (r.metadata or {}).get("group")
+        if g not in seen:
+            if len(seen) >= n_groups:
+                continue
+            seen.add(g)
+        out.append(r)
     return out

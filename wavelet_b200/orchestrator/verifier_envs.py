@@ -313,24 +313,41 @@ def output_records(output: dict[str, Any], *, group: str, env_name: str, step: i
     return recs
 
 
+class _Unlimited:
+    async def __aenter__(self):
+        return self
+
+    async def __aexit__(self, *exc):
+        return False
+
+
 async def run_group(vf, env, example: dict[str, Any], *, client: Any, model: str, sampling: dict[str, Any],
-                    rollout_count: int, max_retries: int, failures: FailureStats | None = None) -> list[dict[str, Any]]:
-    """The outputs of one prompt's group that can be trained on."""
+                    rollout_count: int, max_retries: int, failures: FailureStats | None = None,
+                    limit: asyncio.Semaphore | None = None) -> list[dict[str, Any]]:
+    """The outputs of one prompt's group that can be trained on.  ``limit``
+    bounds the rollouts in flight across groups (a jointly scored group holds
+    it once for the whole group)."""
+    gate = limit if limit is not None else _Unlimited()
+
+    async def one():
+        async with gate:
+            return await env.run_rollout(vf.RolloutInput(**example), client=client, model=model,
+                                         sampling_args=sampling, max_retries=max_retries,
+                                         state_columns=STATE_COLUMNS)
+
     if getattr(env, "requires_group_scoring", False):
         fn = getattr(env, "run_group", None)
         if not callable(fn):
             raise ValueError("the verifier environment scores groups but has no run_group()")
-        results = list(await fn([vf.RolloutInput(**example) for _ in range(rollout_count)], client=client,
-                                model=model, sampling_args=sampling, max_retries=max_retries,
-                                state_columns=STATE_COLUMNS))
+        async with gate:
+            results = list(await fn([vf.RolloutInput(**example) for _ in range(rollout_count)], client=client,
+                                    model=model, sampling_args=sampling, max_retries=max_retries,
+                                    state_columns=STATE_COLUMNS))
         if failures is not None:
             for _ in range(max(0, rollout_count - len(results))):
                 failures.record("MissingRollout")
     else:
-        results = await asyncio.gather(*(env.run_rollout(vf.RolloutInput(**example), client=client, model=model,
-                                                         sampling_args=sampling, max_retries=max_retries,
-                                                         state_columns=STATE_COLUMNS)
-                                         for _ in range(rollout_count)), return_exceptions=True)
+        results = await asyncio.gather(*(one() for _ in range(rollout_count)), return_exceptions=True)
     return successful_outputs(list(results), failures)
 
 
@@ -443,6 +460,8 @@ class VerifierRollouts:
         return [r.advantage for r in scored]
 
     async def _run(self, prompts, step: int) -> list[RLExample]:
+        cap = self.cfg.orchestrator.max_inflight_rollouts
+        limit = asyncio.Semaphore(int(cap)) if cap else None
         jobs, keys = [], []
         for i, p in enumerate(prompts):
             name = p.metadata.get("env")
@@ -452,7 +471,7 @@ class VerifierRollouts:
                                   model=self.model, sampling=self._sampling(name, step),
                                   rollout_count=self._group_size(name),
                                   max_retries=int(self.cfg.orchestrator.verifier_max_retries),
-                                  failures=self.failures))
+                                  failures=self.failures, limit=limit))
             keys.append((i, name))
         results = await asyncio.gather(*jobs, return_exceptions=True)
         recs: list[RLExample] = []
@@ -604,4 +623,7 @@ def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = Non
     with (d / f"step-{step}.jsonl").open("w", encoding="utf-8") as f:
         for o in outs:
             f.write(json.dumps(o, default=_json_default) + "\n")
+    from .evals import prune_eval_sets
+
+    prune_eval_sets(d, getattr(cfg.eval, "keep_last_rollout_sets", None))
     return m
