@@ -290,3 +290,54 @@ def test_inflight_rollouts_are_capped(tmp_path, fake_vf):
         FakeEnv.run_rollout = orig
     assert len(recs) == 8 and state["peak"] == 5
     assert verifier_envs is not None
+
+
+def test_adaptive_concurrency_sheds_under_load(tmp_path, fake_vf, monkeypatch):
+    import asyncio
+
+    from wavelet_b200.orchestrator.concurrency import EngineLoad
+    from wavelet_b200.orchestrator.inference_metrics import EngineMetricsScraper
+
+    seen = []
+    monkeypatch.setattr(EngineMetricsScraper, "scrape",
+                        lambda self, root, timeout=5.0: seen.append(root) or EngineLoad(kv_cache_usage=0.95))
+    orig = FakeEnv.run_rollout
+
+    async def slow(self, *a, **k):
+        await asyncio.sleep(0.03)
+        return await orig(self, *a, **k)
+
+    monkeypatch.setattr(FakeEnv, "run_rollout", slow)
+    cfg = _cfg(tmp_path, [{"id": "fake-env", "args": {"n": 2}}], tasks_per_minute=6000,
+               concurrency={"initial_inflight": 8, "poll_interval_seconds": 0.005})
+    orch = _orchestrator(cfg)
+    recs = orch.materialize(0)
+    assert len(recs) == 8
+    assert orch.last_stats["concurrency/shed"] >= 1 and orch.last_stats["concurrency/limit"] < 8
+    assert set(seen) <= {"http://127.0.0.1:8101", "http://127.0.0.1:8102"} and seen
+    adm = orch.custom_rollout._adm
+    assert adm.rate == 100.0 and adm.burst == 6000.0 and adm.inflight == 0
+
+
+def test_native_server_metrics_are_scraped():
+    from wavelet_b200.orchestrator.inference_metrics import EngineMetricsScraper
+
+    load = EngineMetricsScraper().from_prometheus(
+        "wavelet:kv_cache_usage_perc 0.5\nwavelet:num_requests_running 1\nwavelet:num_requests_waiting 3\n")
+    assert load.kv_cache_usage == 0.5 and load.running == 1 and load.waiting == 3
+
+
+def test_concurrency_rules(tmp_path):
+    with pytest.raises(ValueError, match="at least rollouts_per_example=4"):
+        _cfg(tmp_path, [{"id": "fake-env"}], concurrency={"initial_inflight": 2})
+    with pytest.raises(ValueError, match="cannot exceed the explicit"):
+        _cfg(tmp_path, [{"id": "fake-env"}], max_inflight_rollouts=8, concurrency={"max_inflight": 16})
+    with pytest.raises(ValueError, match="requires the Verifiers rollout source"):
+        RLConfig.model_validate({"orchestrator": {"concurrency": {}}})
+    from wavelet_b200.orchestrator.concurrency import AdmissionController
+
+    adm = AdmissionController(2)
+    assert adm.acquire(3, timeout=0)  # larger than the cap: admitted alone
+    assert not adm.acquire(1, timeout=0)
+    adm.release(3)
+    assert adm.acquire(1, timeout=0)

@@ -1322,12 +1322,33 @@ class RLConfig(TrainerConfig):
             raise ValueError("algo.type='sft' requires a top-level teacher block.")
         if self.teacher is not None and not has_sft:
             raise ValueError("The top-level teacher block is only used by algo.type='sft'.")
+        if self.orchestrator.concurrency is not None:
+            self._check_concurrency()
         if self.orchestrator.envs:
             if not self.orchestrator.uses_verifiers:
                 raise ValueError("orchestrator.envs requires the Verifiers rollout source.")
             if not self._async_process():
                 raise ValueError("orchestrator.envs requires launcher.mode='process' and orchestrator.max_async_level>=1.")
         return self
+
+    def _check_concurrency(self) -> None:
+        o = self.orchestrator
+        if not o.uses_verifiers:
+            raise ValueError("orchestrator.concurrency currently requires the Verifiers rollout source.")
+        if not self._async_process():
+            raise ValueError("orchestrator.concurrency requires launcher.mode='process' and "
+                             "orchestrator.max_async_level>=1.")
+        group = max([o.rollouts_per_example or 1] + [e.group_size or o.rollouts_per_example or 1 for e in o.envs])
+        limits = {"initial_inflight": o.concurrency.initial_inflight, "max_inflight": o.concurrency.max_inflight}
+        small = [k for k, v in limits.items() if v is not None and v < group]
+        if small:
+            raise ValueError(f"orchestrator.concurrency limits must be at least rollouts_per_example={group}: "
+                             f"{', '.join(small)}.")
+        ceiling = o.max_inflight_rollouts
+        big = [k for k, v in limits.items() if ceiling is not None and v is not None and v > ceiling]
+        if big:
+            raise ValueError(f"orchestrator.concurrency limits cannot exceed the explicit "
+                             f"orchestrator.max_inflight_rollouts={ceiling}: {', '.join(big)}.")
 
     def _async_process(self) -> bool:
         return self.launcher.mode == "process" and self.orchestrator.max_async_level >= 1

@@ -71,6 +71,10 @@ class GenerationGate:
     def paused(self) -> bool:
         return self._paused
 
+    @property
+    def active(self) -> int:
+        return self._active
+
 
 def build_app(config: RLConfig, engine=None):
     from fastapi import FastAPI, HTTPException
@@ -115,9 +119,11 @@ def build_app(config: RLConfig, engine=None):
     def metrics():
         g = engine.generator
         usage = g.kv_usage() if g is not None else 0.0
+        active = gate.active  # requests inside the gate: one generates at a time, the rest wait for it
         lines = [
             f"wavelet:kv_cache_usage_perc {usage}",
-            f"wavelet:num_requests_running 0",
+            f"wavelet:num_requests_running {min(active, 1)}",
+            f"wavelet:num_requests_waiting {max(active - 1, 0)}",
             f"wavelet:generation_tokens_total {state['generated_tokens']}",
             f"wavelet:requests_total {state['requests']}",
         ]

@@ -127,7 +127,9 @@ class AdmissionController:
         with self._cv:
             while True:
                 self._refill()
-                if self.inflight + cost <= self.limit and (self.rate is None or self.tokens >= 1.0):
+                # a request larger than the cap (a jointly scored group) runs when nothing else does
+                fits = self.inflight + cost <= self.limit or self.inflight == 0
+                if fits and (self.rate is None or self.tokens >= 1.0):
                     self.inflight += cost
                     if self.rate is not None:
                         self.tokens -= 1.0

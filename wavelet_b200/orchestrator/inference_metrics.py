@@ -4,8 +4,9 @@ orchestrator/inference_metrics.py:40-136).
 Reads either a Prometheus text exposition (``/metrics``; vLLM-style names
 ``vllm:gpu_cache_usage_perc`` / ``vllm:kv_cache_usage_perc``,
 ``vllm:num_requests_running``, ``vllm:num_requests_waiting``,
-``vllm:num_preemptions_total``, ``vllm:generation_tokens_total``) or this
-framework's native ``/debug/state`` JSON, into an ``EngineLoad``.
+``vllm:num_preemptions_total``, ``vllm:generation_tokens_total``, or the
+native server's ``wavelet:`` equivalents) or the native ``/debug/state``
+JSON, into an ``EngineLoad``.
 """
 
 from __future__ import annotations
@@ -18,11 +19,11 @@ from .concurrency import EngineLoad
 
 _LINE = re.compile(r'^([a-zA-Z_:][a-zA-Z0-9_:]*)(\{[^}]*\})?\s+([-+0-9.eEinfNa]+)')
 _NAMES = {
-    "kv": ("vllm:kv_cache_usage_perc", "vllm:gpu_cache_usage_perc"),
-    "running": ("vllm:num_requests_running",),
-    "waiting": ("vllm:num_requests_waiting",),
+    "kv": ("vllm:kv_cache_usage_perc", "vllm:gpu_cache_usage_perc", "wavelet:kv_cache_usage_perc"),
+    "running": ("vllm:num_requests_running", "wavelet:num_requests_running"),
+    "waiting": ("vllm:num_requests_waiting", "wavelet:num_requests_waiting"),
     "preemptions": ("vllm:num_preemptions_total", "vllm:num_preemptions"),
-    "gen_tokens": ("vllm:generation_tokens_total",),
+    "gen_tokens": ("vllm:generation_tokens_total", "wavelet:generation_tokens_total"),
 }
 
 

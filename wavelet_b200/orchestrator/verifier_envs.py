@@ -15,7 +15,9 @@ is the bridge between those environments and the orchestrator:
   training and evaluation rows, chat prompt), so ``EnvironmentPromptSource``
   mixes verifier and native environments by ratio with resumable cursors.
 * ``VerifierRollouts``: the orchestrator's rollout function for verifier
-  prompts.  Each prompt's group runs as ``rollouts_per_example`` (or the
+  prompts, with admission control (in-flight cap ``max_inflight_rollouts``,
+  start rate ``tasks_per_minute``, and the adaptive cap of
+  ``orchestrator.concurrency`` fed by the servers' load metrics).  Each prompt's group runs as ``rollouts_per_example`` (or the
   entry's ``group_size``) concurrent ``env.run_rollout`` calls, or one
   ``env.run_group`` for environments that score groups jointly; failed
   rollouts are dropped and counted by kind, a provider's rate-limit error
@@ -313,24 +315,33 @@ def output_records(output: dict[str, Any], *, group: str, env_name: str, step: i
     return recs
 
 
-class _Unlimited:
+class _Admit:
+    """``async with``: one admission of ``cost`` rollouts (no-op without a controller)."""
+
+    def __init__(self, controller, cost: int):
+        self.controller, self.cost = controller, cost
+
     async def __aenter__(self):
+        if self.controller is not None:
+            await self.controller.aacquire(self.cost)
         return self
 
     async def __aexit__(self, *exc):
+        if self.controller is not None:
+            self.controller.release(self.cost)
         return False
 
 
 async def run_group(vf, env, example: dict[str, Any], *, client: Any, model: str, sampling: dict[str, Any],
                     rollout_count: int, max_retries: int, failures: FailureStats | None = None,
-                    limit: asyncio.Semaphore | None = None) -> list[dict[str, Any]]:
-    """The outputs of one prompt's group that can be trained on.  ``limit``
-    bounds the rollouts in flight across groups (a jointly scored group holds
-    it once for the whole group)."""
-    gate = limit if limit is not None else _Unlimited()
+                    admission=None) -> list[dict[str, Any]]:
+    """The outputs of one prompt's group that can be trained on.
+    ``admission`` (``concurrency.AdmissionController``) bounds the rollouts in
+    flight and their start rate across groups; a jointly scored group is
+    admitted as a whole."""
 
     async def one():
-        async with gate:
+        async with _Admit(admission, 1):
             return await env.run_rollout(vf.RolloutInput(**example), client=client, model=model,
                                          sampling_args=sampling, max_retries=max_retries,
                                          state_columns=STATE_COLUMNS)
@@ -339,7 +350,7 @@ async def run_group(vf, env, example: dict[str, Any], *, client: Any, model: str
         fn = getattr(env, "run_group", None)
         if not callable(fn):
             raise ValueError("the verifier environment scores groups but has no run_group()")
-        async with gate:
+        async with _Admit(admission, rollout_count):
             results = list(await fn([vf.RolloutInput(**example) for _ in range(rollout_count)], client=client,
                                     model=model, sampling_args=sampling, max_retries=max_retries,
                                     state_columns=STATE_COLUMNS))
@@ -428,6 +439,8 @@ class VerifierRollouts:
         self.fallback = fallback
         self.failures = FailureStats()
         self.entries = {getattr(e, "resolved_name", e.id): e for e in cfg.orchestrator.envs}
+        self._adm = None
+        self._adaptive = None
         self._algos = {}
         for name in envs:
             e = self.entries.get(name)
@@ -459,9 +472,62 @@ class VerifierRollouts:
         scored = score_records(algo, proto, scope, group_key=lambda r: 0)
         return [r.advantage for r in scored]
 
+    def _admission(self):
+        """In-flight cap (``max_inflight_rollouts``, resized by the adaptive
+        controller when ``orchestrator.concurrency`` is set) and start rate
+        (``tasks_per_minute``) of the rollouts; None when neither is set."""
+        from .concurrency import AdaptiveConcurrency, AdmissionController
+
+        o = self.cfg.orchestrator
+        if o.max_inflight_rollouts is None and o.tasks_per_minute is None and o.concurrency is None:
+            return None
+        if self._adm is None:
+            if o.concurrency is not None:
+                self._adaptive = AdaptiveConcurrency(o.concurrency, default_initial=o.max_inflight_rollouts or 64)
+            limit = self._adaptive.cap if self._adaptive is not None else (o.max_inflight_rollouts or 1 << 30)
+            if self._adaptive is not None and o.max_inflight_rollouts:
+                limit = min(limit, o.max_inflight_rollouts)
+            tpm = o.tasks_per_minute
+            self._adm = AdmissionController(limit, rate=tpm / 60.0 if tpm else None, burst=tpm)
+        return self._adm
+
+    async def _poll_load(self, adm) -> None:
+        """Feed server load samples to the adaptive controller every poll interval."""
+        from .inference_metrics import EngineMetricsScraper
+
+        c = self.cfg.orchestrator.concurrency
+        scraper = EngineMetricsScraper()
+        roots = [u[: -len("/v1")] if u.endswith("/v1") else u for u in base_urls(self.cfg)]
+        while True:
+            await asyncio.sleep(c.poll_interval_seconds)
+            loads = []
+            for root in roots:
+                try:
+                    loads.append(await asyncio.to_thread(scraper.scrape, root, c.request_timeout_seconds))
+                except Exception as exc:  # noqa: BLE001 - a missed sample is skipped
+                    log.debug("load sample from %s failed: %s", root, exc)
+            if not loads:
+                continue
+            from .concurrency import EngineLoad
+
+            agg = EngineLoad(kv_cache_usage=max(x.kv_cache_usage for x in loads),
+                             running=sum(x.running for x in loads), waiting=sum(x.waiting for x in loads),
+                             preemptions_delta=sum(x.preemptions_delta for x in loads))
+            cap = self._adaptive.observe(agg, adm.inflight)
+            mx = self.cfg.orchestrator.max_inflight_rollouts
+            adm.set_limit(min(cap, mx) if mx else cap)
+
     async def _run(self, prompts, step: int) -> list[RLExample]:
-        cap = self.cfg.orchestrator.max_inflight_rollouts
-        limit = asyncio.Semaphore(int(cap)) if cap else None
+        adm = self._admission()
+        poller = asyncio.create_task(self._poll_load(adm)) if adm is not None and self._adaptive is not None else None
+        try:
+            return await self._run_groups(prompts, step, adm)
+        finally:
+            if poller is not None:
+                poller.cancel()
+                await asyncio.gather(poller, return_exceptions=True)
+
+    async def _run_groups(self, prompts, step: int, adm) -> list[RLExample]:
         jobs, keys = [], []
         for i, p in enumerate(prompts):
             name = p.metadata.get("env")
@@ -471,7 +537,7 @@ class VerifierRollouts:
                                   model=self.model, sampling=self._sampling(name, step),
                                   rollout_count=self._group_size(name),
                                   max_retries=int(self.cfg.orchestrator.verifier_max_retries),
-                                  failures=self.failures, limit=limit))
+                                  failures=self.failures, admission=adm))
             keys.append((i, name))
         results = await asyncio.gather(*jobs, return_exceptions=True)
         recs: list[RLExample] = []
@@ -503,6 +569,8 @@ class VerifierRollouts:
         self.last_stats = self.failures.consume()
         rewards = [float(r.reward) for r in recs if (r.metadata or {}).get("rollout_count")]
         self.last_stats["verifier/rollouts"] = float(len(rewards))
+        if self._adaptive is not None:
+            self.last_stats.update(self._adaptive.metrics())
         if rewards:
             self.last_stats["verifier/reward_mean"] = sum(rewards) / len(rewards)
         return recs
