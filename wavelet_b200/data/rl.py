@@ -50,7 +50,8 @@ class RLExample:
 _COLUMNS = {"advantage": "advantage_column", "reward": "reward_column",
             "inference_logprobs": "inference_logprobs_column", "teacher_logprobs": "teacher_logprobs_column",
             "sampling_mask": "sampling_mask_column", "temperatures": "temperature_column",
-            "ce_weight": "ce_weight_column", "ref_kl_weight": "ref_kl_weight_column", "metadata": "metadata_column"}
+            "ce_weight": "ce_weight_column", "ref_kl_weight": "ref_kl_weight_column", "metadata": "metadata_column",
+            "tools": "tools_column", "chat_template_kwargs": "chat_template_kwargs_column"}
 
 
 def _renames(data_cfg) -> dict[str, str]:

@@ -122,7 +122,51 @@ def normalize_messages(row: dict[str, Any], cfg) -> list[dict[str, Any]]:
                 m["content"] = f"<think>\n{th}\n</think>\n\n{m.get('content') or ''}"
     if cfg.system_prompt and not (msgs and msgs[0].get("role") == "system"):
         msgs = [{"role": "system", "content": cfg.system_prompt}] + msgs
-    return msgs
+    return _decode_tool_calls(msgs)
+
+
+def _decode_tool_calls(msgs: list[dict[str, Any]]) -> list[dict[str, Any]]:
+    """Tool-call ``arguments`` stored as JSON text become objects (chat
+    templates render objects); text that is not JSON stays as it is."""
+    out = []
+    for m in msgs:
+        calls = m.get("tool_calls")
+        if not isinstance(calls, list):
+            out.append(m)
+            continue
+        fixed = []
+        for c in calls:
+            fn = c.get("function") if isinstance(c, dict) else None
+            if isinstance(fn, dict) and isinstance(fn.get("arguments"), str):
+                try:
+                    c = {**c, "function": {**fn, "arguments": json.loads(fn["arguments"])}}
+                except json.JSONDecodeError:
+                    pass
+            fixed.append(c)
+        out.append({**m, "tool_calls": fixed})
+    return out
+
+
+def template_kwargs(row: dict[str, Any], cfg) -> dict[str, Any]:
+    """Chat-template arguments of a row: its tool schemas (``data.tools_column``)
+    and extra template arguments such as ``enable_thinking``
+    (``data.chat_template_kwargs_column``)."""
+    out: dict[str, Any] = {}
+    tools = row.get(getattr(cfg, "tools_column", "tools"))
+    if isinstance(tools, str):
+        tools = json.loads(tools)
+    if tools is not None:
+        if not isinstance(tools, list):
+            raise ValueError("tools must be a list when provided.")
+        out["tools"] = tools
+    extra = row.get(getattr(cfg, "chat_template_kwargs_column", "chat_template_kwargs"))
+    if isinstance(extra, str):
+        extra = json.loads(extra)
+    if extra is not None:
+        if not isinstance(extra, dict):
+            raise ValueError("chat_template_kwargs must be an object when provided.")
+        out.update(extra)
+    return out
 
 
 def _role_trainable(role: str, lm) -> bool:
@@ -137,13 +181,15 @@ def _trainable(m: dict[str, Any], lm) -> int:
     return 0 if m.get("step_loss_mask", 1) in (0, False) else 1
 
 
-def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
+def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg, kwargs: dict[str, Any] | None = None) -> Sample:
     """Tokenise message by message so every token knows its role.
 
     With a template-capable tokenizer the rendered prefix of messages[:i+1]
     is diffed against messages[:i] (exact under incremental templates); the
-    char tokenizer renders each message independently.
+    char tokenizer renders each message independently.  ``kwargs`` (tools,
+    ``enable_thinking``, ...) go to every template call.
     """
+    kw = dict(kwargs or {})
     ids: list[int] = []
     mask: list[int] = []
     if hasattr(tok, "render_message"):
@@ -157,7 +203,7 @@ def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
         return Sample(ids, mask)
     prev: list[int] = []
     for i, m in enumerate(msgs):
-        cur = tok.apply_chat_template(msgs[: i + 1], tokenize=True, add_generation_prompt=False)
+        cur = tok.apply_chat_template(msgs[: i + 1], tokenize=True, add_generation_prompt=False, **kw)
         if hasattr(cur, "input_ids"):
             cur = cur["input_ids"]
         cur = list(cur)
@@ -172,7 +218,7 @@ def tokenize_messages(msgs: list[dict[str, Any]], tok, cfg) -> Sample:
         head = 0
         if m["role"] == "assistant" and _trainable(m, cfg.loss_mask):
             # the generation prompt (assistant header) belongs to the context, not the completion
-            gen = tok.apply_chat_template(msgs[:i], tokenize=True, add_generation_prompt=True) if i else []
+            gen = tok.apply_chat_template(msgs[:i], tokenize=True, add_generation_prompt=True, **kw) if i else []
             if hasattr(gen, "input_ids"):
                 gen = gen["input_ids"]
             gen = list(gen)
@@ -259,7 +305,8 @@ class SFTDataset:
                     else:
                         if self.tok is None:
                             raise ValueError("a tokenizer is required for non-fake SFT data")
-                        s = tokenize_messages(normalize_messages(r, self.cfg), self.tok, self.cfg)
+                        s = tokenize_messages(normalize_messages(r, self.cfg), self.tok, self.cfg,
+                                              template_kwargs(r, self.cfg))
                     s.source = r.get("__source", "local")
                     if s.input_ids:
                         self._samples.append(s)

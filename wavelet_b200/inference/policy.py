@@ -71,7 +71,10 @@ def record_prompt_ids(r: RLExample, tokenizer=None) -> list[int]:
         return list(r.input_ids)
     if tokenizer is None:
         raise ValueError("record has no prompt token ids and no tokenizer is available")
-    ids = tokenizer.apply_chat_template(r.prompt, tokenize=True, add_generation_prompt=True)
+    kw = dict(r.chat_template_kwargs or {})
+    if r.tools:
+        kw["tools"] = r.tools
+    ids = tokenizer.apply_chat_template(r.prompt, tokenize=True, add_generation_prompt=True, **kw)
     return list(ids["input_ids"] if isinstance(ids, dict) else ids)
 
 

@@ -47,6 +47,7 @@ class FilePromptSource:
     def __init__(self, cfg, rank: int = 0, world: int = 1, tokenizer=None):
         d = cfg.data
         paths = d.path if isinstance(d.path, list) else [d.path]
+        self.data_cfg = d
         self.rows: list[dict[str, Any]] = []
         for p in paths:
             for r in _read_rows(Path(p)):
@@ -90,7 +91,12 @@ class FilePromptSource:
         if ids is None:
             tok = self._tokenizer()
             if hasattr(tok, "apply_chat_template") and prompt:
-                ids = tok.apply_chat_template(prompt, tokenize=True, add_generation_prompt=True)
+                from ..data.sft import template_kwargs
+
+                # the row's tool schemas and template arguments (data.tools_column / chat_template_kwargs_column)
+                ids = tok.apply_chat_template(prompt, tokenize=True, add_generation_prompt=True,
+                                              **template_kwargs(r, self.data_cfg))
+                ids = ids["input_ids"] if isinstance(ids, dict) else ids
             else:
                 ids = tok.encode(" ".join(m.get("content", "") for m in prompt))
         target = r.get("target_completion")
