@@ -85,6 +85,9 @@ class FakeOrch:
         self.lock = threading.Lock()
         self.seen = {}
 
+    def write_materialized(self, rows, step):
+        return None
+
     def for_step(self, src):
         orch = self
 

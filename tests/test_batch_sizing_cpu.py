@@ -91,3 +91,28 @@ def test_eval_rollout_sets_are_pruned(tmp_path):
     removed = prune_eval_sets(d, 2)
     assert sorted(p.name for p in removed) == ["step-0.jsonl", "step-5.jsonl"]
     assert sorted(p.name for p in d.iterdir()) == ["notes.txt", "step-10.jsonl", "step-20.jsonl"]
+
+
+def test_publish_reuses_a_stable_batch_and_writes_the_materialized_file(tmp_path):
+    import json
+
+    from wavelet_b200.orchestrator.rollouts import RLOrchestrator
+    from wavelet_b200.orchestrator.runtime import build_prompt_source
+    from wavelet_b200.transport.queue import FileSystemRolloutSender
+
+    mpath = tmp_path / "m" / "rollouts.jsonl"
+    cfg = _cfg(tmp_path, examples_per_step=2, materialize_path=str(mpath), overwrite=False)
+    eng = _Engine()
+    sender = FileSystemRolloutSender(tmp_path / "out", cfg.transport)
+    orch = RLOrchestrator(cfg, eng, sender, build_prompt_source(cfg, 64))
+    b = orch.publish(0, policy_step=0)
+    assert eng.calls == [2] and len(mpath.read_text().splitlines()) == 4
+    assert json.loads(mpath.read_text().splitlines()[0])["input_ids"]
+    # the same step again: the stable batch is reused, nothing is generated
+    again = orch.publish(0, policy_step=0)
+    assert again.path == b.path and eng.calls == [2]
+    events = (tmp_path / "out" / "events").rglob("*.jsonl")
+    assert any("rollout_reused" in p.read_text() for p in events)
+    # a new step would overwrite the materialized file: refused with overwrite off
+    with pytest.raises(FileExistsError, match="overwrite is disabled"):
+        orch.publish(1, policy_step=1)

@@ -52,7 +52,11 @@ INERT: dict[str, str] = {
     "inference.sampling.extra_body": "the native sampler has no extra request fields (verifiers-package "
                                      "rollouts pass them to the server)",
     "orchestrator.max_pending_rollout_chunks": "in-flight steps are bounded by max_async_level",
-    "orchestrator.materialize_path": "`debug orchestrator materialize` takes its output path as an argument",
+    "data.pack_sequences": "RL rows are always packed as variable-length sequences that never attend across each "
+                           "other, which trains the same loss as unpacked rows",
+    "data.pad_to_multiple_of": "packed rows are variable-length; the kernels need no padding",
+    "model.attn_implementation": "attention is the native variable-length tcgen05 kernel",
+    "fsdp.impl": "parameters are sharded by the flat ZeRO store (fsdp.shard_params), not torch FSDP",
     "eval.background": "evals run in the rollout role after the policy load that triggers them",
     "eval.cancel_on_new_policy": "evals run to completion on the policy that triggered them",
     "eval.model_revision": "evals use the policy snapshots of this run",

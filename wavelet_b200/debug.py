@@ -338,6 +338,7 @@ def probe_orchestrator(cfg: RLConfig, *, step: int = 0, engine=None, write: bool
     if write:
         t0 = time.perf_counter()
         rows = [example_to_payload(r) for r in recs]
+        orch.write_materialized(rows, step)  # orchestrator.materialize_path, when set
         batch = FileSystemRolloutSender(Path(cfg.output_dir), cfg.transport).publish(
             rows, step=step, training_records=rows, optimizer_step=step,
             tokens=sum(len(r.input_ids or []) for r in recs), reward_mean=orch.last_stats.get("reward/mean"))

@@ -360,12 +360,58 @@ class RLOrchestrator:
                                 "rollout/zero_advantage_retries": float(retries)})
         return kept
 
+    def reusable_batch(self, step: int) -> Any:
+        """The stable queue batch of ``step`` when the trainer would still
+        accept it (its policy is within the allowed lag), so a restarted
+        producer does not generate it again (ref orchestrator/rollouts.py:306-334)."""
+        if self.sender is None:
+            return None
+        batch = self.sender.stable_batch(step)
+        if batch is None:
+            return None
+        from .schedule import required_policy_step
+
+        man = batch.manifest
+        ps = man.policy_step if man is not None else None
+        if ps is not None and not required_policy_step(step, self.cfg) <= ps <= step:
+            raise ValueError(f"rollout queue step {step} is stable but was generated with policy {ps}, outside the "
+                             f"allowed range [{required_policy_step(step, self.cfg)}, {step}]; remove it or "
+                             f"start from a fresh output directory")
+        from ..transport.queue import append_event
+
+        append_event(self.sender.output_dir / "events", "rollout_reused", queue_step=step, optimizer_step=step,
+                     details={"path": str(batch.path)})
+        return batch
+
+    def write_materialized(self, rows: list[dict], step: int) -> Any:
+        """``orchestrator.materialize_path``: the step's rows also as one JSONL
+        file (an existing file is an error when ``orchestrator.overwrite`` is off)."""
+        from pathlib import Path
+
+        path = getattr(self.cfg.orchestrator, "materialize_path", None)
+        if path is None:
+            return None
+        path = Path(path)
+        if path.exists() and not self.cfg.orchestrator.overwrite:
+            raise FileExistsError(f"Rollout file '{path}' already exists and overwrite is disabled.")
+        path.parent.mkdir(parents=True, exist_ok=True)
+        import json
+
+        with path.open("w", encoding="utf-8") as f:
+            for r in rows:
+                f.write(json.dumps(r, separators=(",", ":"), default=str) + "\n")
+        return path
+
     def publish(self, step: int, policy_step: int | None = None) -> Any:
+        existing = self.reusable_batch(step)
+        if existing is not None:
+            return existing
         t0 = time.perf_counter()
         recs = self.materialize(step)
         emit_perf("rollout_materialized", step=step, seconds=time.perf_counter() - t0, rows=len(recs))
         rows = [example_to_payload(r, self.cfg.data) for r in recs]
         tokens = sum(len(r.input_ids or []) for r in recs)
+        self.write_materialized(rows, step)
         if self.sender is None:
             return recs
         return self.sender.publish(rows, step=step, training_records=rows, optimizer_step=step, policy_step=policy_step,
