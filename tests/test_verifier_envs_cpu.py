@@ -341,3 +341,50 @@ def test_concurrency_rules(tmp_path):
     assert not adm.acquire(1, timeout=0)
     adm.release(3)
     assert adm.acquire(1, timeout=0)
+
+
+def test_evaluation_resumes_from_its_journal(tmp_path, fake_vf):
+    from wavelet_b200.configs.config import RLEvalEnvConfig
+    from wavelet_b200.orchestrator.verifier_envs import evaluate
+
+    from wavelet_b200.configs.config import RLEvalConfig
+
+    cfg = _cfg(tmp_path, [{"id": "fake-env"}])
+    cfg = cfg.model_copy(update={"eval": RLEvalConfig(resume=True)})
+    ev = RLEvalEnvConfig(id="fake-env", name="fe", args={"n": 3, "fail_ids": [2]}, rollouts_per_example=2,
+                         num_examples=3, sampling={"seed": 11})
+    out = tmp_path / "out"
+    m1 = evaluate(cfg, ev, step=4, out_dir=out)
+    env = fake_vf.made["fake-env"]
+    assert len(env.calls) == 6 and m1["eval/fe/failed_rollouts"] == 2.0
+    # the rerun reuses the four committed results and retries only the two failed episodes
+    env.calls.clear()
+    m2 = evaluate(cfg, ev, step=4, out_dir=out)
+    assert len(env.calls) == 2 and {int(c["input"]["example_id"]) for c in env.calls} == {2}
+    assert m2["eval/fe/pass@1"] == m1["eval/fe/pass@1"] and m2["eval/fe/time"] >= m1["eval/fe/time"]
+    journal = out / "evals" / "fe" / "journal-step-4"
+    assert len(list(journal.glob("episode-*.json"))) == 6 and (journal / "manifest.json").exists()
+    # live traces: one document per evaluated episode
+    assert len(list((out / "traces" / "live").glob("*.json"))) >= 6
+    # different settings against the same journal, or a journal without eval.resume: refused
+    ev2 = ev.model_copy(update={"sampling": ev.sampling.model_copy(update={"seed": 12})})
+    with pytest.raises(ValueError, match="settings differ"):
+        evaluate(cfg, ev2, step=4, out_dir=out)
+    cfg_nr = cfg.model_copy(update={"eval": cfg.eval.model_copy(update={"resume": False})})
+    with pytest.raises(FileExistsError, match="eval.resume"):
+        evaluate(cfg_nr, ev, step=4, out_dir=out)
+
+
+def test_native_eval_resume_skips_a_finished_evaluation(tmp_path, monkeypatch):
+    from wavelet_b200.configs.config import RLEvalEnvConfig
+    from wavelet_b200.orchestrator import evals
+
+    cfg = RLConfig.model_validate(
+        {"eval": {"resume": True}, "output_dir": str(tmp_path / "o")})
+    calls = []
+    monkeypatch.setattr(evals, "_run_native_eval",
+                        lambda c, e, env, step, out: calls.append(step) or {"eval/reverse/reward_mean": 0.25})
+    env = RLEvalEnvConfig(id="reverse")
+    assert evals.run_eval_env(cfg, None, env, 3, tmp_path / "o") == {"eval/reverse/reward_mean": 0.25}
+    assert evals.run_eval_env(cfg, None, env, 3, tmp_path / "o") == {"eval/reverse/reward_mean": 0.25}
+    assert calls == [3]

@@ -59,7 +59,6 @@ INERT: dict[str, str] = {
     "fsdp.impl": "parameters are sharded by the flat ZeRO store (fsdp.shard_params), not torch FSDP",
     "eval.background": "evals run in the rollout role after the policy load that triggers them",
     "eval.cancel_on_new_policy": "evals run to completion on the policy that triggered them",
-    "eval.model_revision": "evals use the policy snapshots of this run",
 }
 
 

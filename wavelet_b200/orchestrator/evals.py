@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import json
 import math
+import shutil
 from dataclasses import replace
 from pathlib import Path
 from types import SimpleNamespace
@@ -81,6 +82,9 @@ def prune_eval_sets(env_dir: Path, keep: int | None) -> list[Path]:
     removed = [f for _, f in sorted(sets)[:-keep]] if keep > 0 else [f for _, f in sets]
     for f in removed:
         f.unlink()
+        j = env_dir / f"journal-{f.stem}"  # the evaluation journal of that step
+        if j.is_dir():
+            shutil.rmtree(j)
     return removed
 
 
@@ -126,6 +130,25 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
 
         if verifiers_available():  # a verifiers-package environment rolls out against the inference servers
             return evaluate(cfg, env, step=step, out_dir=out_dir, engine=engine)
+    if cfg.eval is None or not cfg.eval.resume:
+        return _run_native_eval(cfg, engine, env, step, out_dir)
+    # eval.resume: a finished evaluation of this step with the same settings is not run again
+    from .eval_journal import EvalJournal, signature
+
+    sig = signature(env_id=env.id, env_args=env.args, samples=env.rollouts_per_example, num_examples=env.num_examples,
+                    sampling=env.sampling.model_dump(mode="json"), reward=cfg.reward.model_dump(mode="json"),
+                    model_config=cfg.model.model_dump(mode="json"), policy_step=step)
+    with EvalJournal(Path(out_dir) / "evals" / env.resolved_name / f"journal-step-{step}", sig=sig,
+                     resume=True) as journal:
+        done = journal.completed("metrics")
+        if done is not None:
+            return {k: float(v) for k, v in done.items() if k != "reward"}
+        m = _run_native_eval(cfg, engine, env, step, out_dir)
+        journal.record("metrics", {**m, "reward": m.get(f"eval/{env.resolved_name}/reward_mean", 0.0)})
+    return m
+
+
+def _run_native_eval(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]:
     n_ex = env.num_examples if env.num_examples > 0 else 32
     k = env.rollouts_per_example
     reward_cfg = cfg.reward
@@ -134,7 +157,9 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
     elif _native(env.id):
         reward_cfg = cfg.reward.model_copy(update={"mode": "environment"})
     ecfg = cfg.model_copy(update={"reward": reward_cfg,
-                                  "orchestrator": cfg.orchestrator.model_copy(update={"rollouts_per_example": k})})
+                                  "orchestrator": cfg.orchestrator.model_copy(update={
+                                      "rollouts_per_example": k,
+                                      "live_traces": bool(cfg.eval.live_traces if cfg.eval is not None else True)})})
     s = env.sampling
     if s.max_completion_tokens or s.temperature is not None:
         samp = cfg.inference.sampling.model_copy(update={
@@ -163,7 +188,7 @@ def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]
             md = r.metadata or {}
             f.write(json.dumps({"example_id": md.get("example_id"), "reward": r.reward,
                                 "completion_ids": md.get("completion_ids")}) + "\n")
-    prune_eval_sets(d, getattr(cfg.eval, "keep_last_rollout_sets", None))
+    prune_eval_sets(d, cfg.eval.keep_last_rollout_sets if cfg.eval is not None else None)
     return m
 
 

@@ -612,8 +612,16 @@ def _json_default(v: Any) -> Any:
 
 
 async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int, max_retries: int,
-                         max_inflight: int | None) -> list[dict[str, Any]]:
+                         max_inflight: int | None, journal=None, live: dict[str, Any] | None = None
+                         ) -> list[dict[str, Any]]:
+    """Every (example, sample) rollout; results already committed in
+    ``journal`` are reused, new ones are committed as they finish; ``live``
+    (LiveEpisode arguments) traces each rollout for the dashboard."""
+    from .eval_journal import episode_keys
+    from .live import LiveEpisode
+
     total = len(examples) * k
+    keys = episode_keys(examples, k)
     results: list[dict[str, Any] | None] = [None] * total
     nxt = 0
 
@@ -623,18 +631,33 @@ async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int,
             idx = nxt
             nxt += 1
             ei, ri = divmod(idx, k)
+            done = journal.completed(keys[idx]) if journal is not None else None
+            if done is not None:
+                results[idx] = done
+                continue
             s = dict(sampling)
             if s.get("seed") is not None and ri:
                 s["seed"] = int(s["seed"]) + ri  # distinct samples for avg@k / pass@k
+            ep = LiveEpisode(**live, example_id=keys[idx]) if live is not None else None
             try:
+                if ep is not None:
+                    await ep.__aenter__()
                 val = await env.run_rollout(vf.RolloutInput(**examples[ei]), client=clients[ei % len(clients)],
                                             model=model, sampling_args=s, max_retries=max_retries,
                                             state_columns=STATE_COLUMNS)
             except asyncio.CancelledError:
+                if ep is not None:
+                    await ep.__aexit__(asyncio.CancelledError, asyncio.CancelledError(), None)
                 raise
             except Exception as exc:  # noqa: BLE001 - an environment failure is a failed sample
                 val = exc
-            results[idx] = _eval_output(val, examples[ei], ei)
+            out = _eval_output(val, examples[ei], ei)
+            if ep is not None:
+                err = out.get("error")
+                if err is not None:
+                    ep.finish("error", error=err)
+                await ep.__aexit__(None, None, None)
+            results[idx] = journal.record(keys[idx], out) if journal is not None else out
 
     n_workers = max(1, min(total, max_inflight or total))
     tasks = [asyncio.create_task(worker()) for _ in range(n_workers)]
@@ -649,9 +672,8 @@ async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int,
 
 
 def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = None) -> dict[str, float]:
-    """Evaluate the served policy on one verifier environment entry of ``eval.env``."""
-    import time
-
+    """Evaluate the served policy on one verifier environment entry of
+    ``eval.env`` (resumable through its journal when ``eval.resume`` is on)."""
     from .evals import group_metrics
 
     vf = load_verifiers("evals")
@@ -667,18 +689,34 @@ def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = Non
         r.setdefault("example_id", i)
     sargs = env_cfg.sampling.to_sampling_args()  # only what the entry sets; the server's defaults otherwise
     sargs["extra_body"] = {**sargs.get("extra_body", {}), "cache_salt": f"eval-{step}"}
-    t0 = time.perf_counter()
-    outs = asyncio.run(_eval_rollouts(vf, env, examples, clients=client_configs(vf, cfg, client_type="openai_chat_completions"),
-                                      model=model_name(cfg, engine), sampling=sargs, k=env_cfg.rollouts_per_example,
-                                      max_retries=int(getattr(env_cfg, "max_retries", 0) or 0),
-                                      max_inflight=getattr(cfg.eval, "max_inflight_rollouts", None)))
+    from .eval_journal import EvalJournal, signature
+
+    from ..configs.config import RLEvalConfig
+
+    ev = cfg.eval if cfg.eval is not None else RLEvalConfig()
     name = env_cfg.resolved_name
+    model = model_name(cfg, engine)
+    sig = signature(env_id=env_cfg.id, env_args=env_cfg.args, env_kwargs=env_kwargs(cfg), model=model,
+                    sampling=sargs, samples=env_cfg.rollouts_per_example, num_examples=env_cfg.num_examples,
+                    model_config=cfg.model.model_dump(mode="json"), model_revision=ev.model_revision,
+                    policy_step=step, endpoints=base_urls(cfg))
+    live = ({"run_dir": Path(out_dir), "env": name, "kind": "eval", "step": step, "policy_step": step}
+            if ev.live_traces else None)
+    with EvalJournal(Path(out_dir) / "evals" / name / f"journal-step-{step}", sig=sig,
+                     resume=bool(ev.resume)) as journal:
+        outs = asyncio.run(_eval_rollouts(vf, env, examples,
+                                          clients=client_configs(vf, cfg, client_type="openai_chat_completions"),
+                                          model=model, sampling=sargs, k=env_cfg.rollouts_per_example,
+                                          max_retries=int(getattr(env_cfg, "max_retries", 0) or 0),
+                                          max_inflight=ev.max_inflight_rollouts,
+                                          journal=journal, live=live))
+    elapsed = journal.elapsed_seconds
     by_ex: dict[str, list[float | None]] = {}
     for o in outs:
         by_ex.setdefault(str(o["example_id"]), []).append(float(o["reward"]) if "reward" in o else None)
     thr = float((env_cfg.args or {}).get("success_threshold", 1.0))
     m = group_metrics(f"eval/{name}", by_ex, thr)
-    m[f"eval/{name}/time"] = time.perf_counter() - t0
+    m[f"eval/{name}/time"] = elapsed  # summed over resumed attempts
     lens = [sum(len(((st or {}).get("tokens") or {}).get("completion_ids") or []) for st in (o.get("trajectory") or []))
             for o in outs if o.get("error") is None]
     if lens:
@@ -693,5 +731,5 @@ def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = Non
             f.write(json.dumps(o, default=_json_default) + "\n")
     from .evals import prune_eval_sets
 
-    prune_eval_sets(d, getattr(cfg.eval, "keep_last_rollout_sets", None))
+    prune_eval_sets(d, ev.keep_last_rollout_sets)
     return m
