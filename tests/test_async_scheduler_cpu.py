@@ -331,3 +331,64 @@ def test_pipeline_status_and_live_state(tmp_path, caplog):
     r = StatusReporter(lambda: {"policy_step": 3, "published": 0, "target": 1, "submitted": 0, "inflight": 0,
                                 "ready": 0, "loading": False}, 10.0, sink=lambda s: 1 / 0)
     assert r.emit()["policy_step"] == 3  # a failing sink does not raise
+
+
+def _background_run(tmp_path, cancel_on_new_policy):
+    cfg = _cfg(tmp_path, max_steps=4, orchestrator={"max_async_level": 1},
+               eval={"env": [{"id": "reverse", "interval": 1}], "background": True,
+                     "cancel_on_new_policy": cancel_on_new_policy, "final_eval": False,
+                     "eval_base_model": True})
+    out = cfg.output_dir
+    orch = FakeOrch(Counter(), delay=0.01)
+    started, finished, cancelled, loads_during = [], [], [], []
+    eng = FakeEngine(concurrent=True)
+    running = threading.Event()
+
+    def evaluate(env, step, cancel=None):
+        started.append(step)
+        running.set()
+        for _ in range(40):  # a long evaluation: 0.4 s
+            if cancel is not None and cancel.is_set():
+                cancelled.append(step)
+                running.clear()
+                return None
+            time.sleep(0.01)
+        finished.append(step)
+        running.clear()
+        return {"eval/reverse/reward_mean": 0.0}
+
+    orig_load = eng.load_policy
+
+    def load_policy(d, *, step):
+        loads_during.append(running.is_set())
+        orig_load(d, step=step)
+
+    eng.load_policy = load_policy
+
+    def trainer():
+        for s in range(0, 4):
+            while s > 0 and s - 1 not in stable_steps(out / "rollouts"):
+                time.sleep(0.002)
+            _policy(out, s)
+
+    t = threading.Thread(target=trainer, daemon=True)
+    t.start()
+    t0 = time.perf_counter()
+    _sched(cfg, orch, eng, evaluate=evaluate).run()
+    t.join(timeout=10)
+    return started, finished, cancelled, loads_during, time.perf_counter() - t0
+
+
+def test_background_evals_are_cancelled_by_a_new_policy(tmp_path):
+    started, finished, cancelled, loads_during, _ = _background_run(tmp_path, True)
+    assert started and cancelled  # evaluations of superseded policies stopped part-way
+    assert not any(loads_during)  # never a weight swap under a running evaluation
+    m = [json.loads(l) for l in (tmp_path / "out" / "eval_metrics.jsonl").read_text().splitlines()] \
+        if (tmp_path / "out" / "eval_metrics.jsonl").exists() else []
+    assert sorted(r["step"] for r in m) == sorted(finished)  # only finished evaluations report metrics
+
+
+def test_background_evals_can_delay_the_policy_load(tmp_path):
+    started, finished, cancelled, loads_during, _ = _background_run(tmp_path, False)
+    assert not cancelled and sorted(finished) == sorted(started)
+    assert not any(loads_during)

@@ -57,8 +57,6 @@ INERT: dict[str, str] = {
     "data.pad_to_multiple_of": "packed rows are variable-length; the kernels need no padding",
     "model.attn_implementation": "attention is the native variable-length tcgen05 kernel",
     "fsdp.impl": "parameters are sharded by the flat ZeRO store (fsdp.shard_params), not torch FSDP",
-    "eval.background": "evals run in the rollout role after the policy load that triggers them",
-    "eval.cancel_on_new_policy": "evals run to completion on the policy that triggered them",
 }
 
 

@@ -32,7 +32,10 @@ own formulation of the same behaviour:
   ``orchestrator.verifier_max_retries`` times (``rollout/retries``) before the
   run fails.
 * **Evals.**  After each policy load, every eval environment whose interval
-  divides the policy step (and that has not seen this policy) is evaluated;
+  divides the policy step (and that has not seen this policy) is evaluated,
+  inline or, with ``eval.background``, on a thread beside the rollouts (the
+  next policy load cancels it, or waits for it with
+  ``eval.cancel_on_new_policy: false``);
   the base model (policy 0) too when ``eval.eval_base_model``.  At the end the
   final policy is loaded if needed and the environments not yet evaluated at
   it run (``eval.final_eval``).  Results go to ``eval_metrics.jsonl``; a resumed
@@ -236,6 +239,10 @@ class AsyncRolloutScheduler:
         self.wait_memory = wait_memory or (lambda: wait_for_trainer_memory(cfg))
         self.concurrent_generate = bool(getattr(engine, "concurrent_generate", False))
         self.concurrent_load = bool(getattr(engine, "concurrent_policy_load", False))
+        # background evaluation (eval.background): one at a time on its own thread
+        self.eval_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="wavelet-evals")
+        self.eval_future: Future | None = None
+        self.eval_cancel: threading.Event | None = None
         self.loaded: int | None = None
         self.pending: dict[Future, _Step] = {}
         self.done: dict[int, tuple[_Step, list, dict]] = {}
@@ -273,6 +280,9 @@ class AsyncRolloutScheduler:
 
     def _load(self, step: int) -> int:
         snap = self.policies.wait_for_step(step)
+        if self.eval_future is not None:  # the old policy's background evaluation ends before its weights change
+            ev = self.cfg.eval
+            self._join_eval(cancel=ev is None or ev.cancel_on_new_policy)
         self._wake()
         t0 = time.perf_counter()
         self.engine.load_policy(snap.step_dir, step=snap.step)
@@ -317,6 +327,13 @@ class AsyncRolloutScheduler:
         if self._broadcast_updates():
             newer = [s for s in stable_steps(self.policies.policy_dir) if self.loaded is None or s > self.loaded]
             newest = newer[0] if newer else newest
+        if self._eval_running():
+            ev = self.cfg.eval
+            if ev is not None and not ev.cancel_on_new_policy:
+                return  # eval.cancel_on_new_policy: false -> the load waits for the evaluation
+            self._join_eval(cancel=True)  # the evaluation of the old policy stops before its weights change
+        elif self.eval_future is not None:
+            self._join_eval()  # finished: collect it (and its errors)
         if self.pending and not self.concurrent_load:
             return  # the engine cannot swap weights under load: wait for a drain
         if self.pending:
@@ -337,20 +354,53 @@ class AsyncRolloutScheduler:
             self.asleep = False
 
     # ------------------------------------------------------------ evals
-    def _run_evals(self, envs: list, policy_step: int) -> None:
+    def _run_evals(self, envs: list, policy_step: int, *, inline: bool = False) -> None:
+        """Evaluate ``envs`` on the loaded policy.  With ``eval.background``
+        (and an engine that serves concurrent calls) they run on their own
+        thread while rollouts continue; the next policy load then cancels
+        them (``eval.cancel_on_new_policy``, the default) or waits for them."""
         if not envs:
             return
         self._wake()
+        ev = self.cfg.eval
+        if not inline and ev is not None and ev.background and self.concurrent_generate:
+            self._join_eval()  # one background evaluation at a time
+            self.eval_cancel = threading.Event()
+            self.eval_future = self.eval_pool.submit(self._eval_envs, envs, policy_step, self.eval_cancel)
+            return
+        self._eval_envs(envs, policy_step, None)
+
+    def _eval_envs(self, envs: list, policy_step: int, cancel: threading.Event | None) -> None:
         for env in envs:
+            if cancel is not None and cancel.is_set():
+                self.stats["eval/cancelled"] = self.stats.get("eval/cancelled", 0.0) + 1
+                continue
             if self.evaluate is not None:
-                m = self.evaluate(env, policy_step)
+                m = self.evaluate(env, policy_step, cancel) if cancel is not None else self.evaluate(env, policy_step)
             else:
                 from .evals import run_eval_env
 
-                m = run_eval_env(self.cfg, self.orch.engine, env, policy_step, self.out)
+                m = run_eval_env(self.cfg, self.orch.engine, env, policy_step, self.out, cancel=cancel)
+            if m is None:  # cancelled part-way: no metrics for this policy
+                self.stats["eval/cancelled"] = self.stats.get("eval/cancelled", 0.0) + 1
+                continue
             append_jsonl(self.out / "eval_metrics.jsonl",
                          {"step": policy_step, "progress/policy_step": policy_step, "timestamp": utc_now(), **m})
             self.last_eval[env.resolved_name] = policy_step
+
+    def _eval_running(self) -> bool:
+        return self.eval_future is not None and not self.eval_future.done()
+
+    def _join_eval(self, cancel: bool = False) -> None:
+        """Wait for the background evaluation (asking it to stop first when
+        ``cancel``); its errors surface here."""
+        f = self.eval_future
+        if f is None:
+            return
+        if cancel and self.eval_cancel is not None:
+            self.eval_cancel.set()
+        self.eval_future = None
+        f.result()
 
     # ------------------------------------------------------------ steps
     def _materialize(self, st: _Step, prompts: list) -> tuple[list, dict]:
@@ -464,7 +514,9 @@ class AsyncRolloutScheduler:
             self._finish_load(block=True)
         if self._broadcast_updates():
             self._drain_broadcasts(total // self.C)
+        self._join_eval()  # a background evaluation of the last loaded policy finishes
         self._final_evals(total // self.C)
+        self.eval_pool.shutdown(wait=True)
         return 0
 
     def _drain_broadcasts(self, total: int) -> None:
@@ -496,5 +548,5 @@ class AsyncRolloutScheduler:
             return
         if self.loaded is None or self.loaded < final:
             self.loaded = self._load(final)
-        self._run_evals(envs, self.loaded)
+        self._run_evals(envs, self.loaded, inline=True)
         self._sleep()

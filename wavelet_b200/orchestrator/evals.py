@@ -124,12 +124,16 @@ def _builtin(env) -> bool:
         or _native(env.id)
 
 
-def run_eval_env(cfg, engine, env, step: int, out_dir: Path) -> dict[str, float]:
+def run_eval_env(cfg, engine, env, step: int, out_dir: Path, cancel=None) -> dict[str, float] | None:
+    """Metrics of one eval environment at ``step``; None when ``cancel`` (a
+    ``threading.Event``) was set before the evaluation finished."""
+    if cancel is not None and cancel.is_set():
+        return None
     if not _builtin(env):
         from .verifier_envs import evaluate, verifiers_available
 
         if verifiers_available():  # a verifiers-package environment rolls out against the inference servers
-            return evaluate(cfg, env, step=step, out_dir=out_dir, engine=engine)
+            return evaluate(cfg, env, step=step, out_dir=out_dir, engine=engine, cancel=cancel)
     if cfg.eval is None or not cfg.eval.resume:
         return _run_native_eval(cfg, engine, env, step, out_dir)
     # eval.resume: a finished evaluation of this step with the same settings is not run again

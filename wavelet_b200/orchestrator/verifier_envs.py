@@ -612,8 +612,8 @@ def _json_default(v: Any) -> Any:
 
 
 async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int, max_retries: int,
-                         max_inflight: int | None, journal=None, live: dict[str, Any] | None = None
-                         ) -> list[dict[str, Any]]:
+                         max_inflight: int | None, journal=None, live: dict[str, Any] | None = None,
+                         cancel=None) -> list[dict[str, Any]]:
     """Every (example, sample) rollout; results already committed in
     ``journal`` are reused, new ones are committed as they finish; ``live``
     (LiveEpisode arguments) traces each rollout for the dashboard."""
@@ -628,6 +628,8 @@ async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int,
     async def worker():
         nonlocal nxt
         while nxt < total:
+            if cancel is not None and cancel.is_set():
+                return  # no new rollouts once the evaluation is cancelled
             idx = nxt
             nxt += 1
             ei, ri = divmod(idx, k)
@@ -671,7 +673,8 @@ async def _eval_rollouts(vf, env, examples, *, clients, model, sampling, k: int,
     return [r for r in results if r is not None]
 
 
-def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = None) -> dict[str, float]:
+def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = None,
+             cancel=None) -> dict[str, float] | None:
     """Evaluate the served policy on one verifier environment entry of
     ``eval.env`` (resumable through its journal when ``eval.resume`` is on)."""
     from .evals import group_metrics
@@ -709,7 +712,9 @@ def evaluate(cfg, env_cfg, *, step: int, out_dir: Path, engine: Any | None = Non
                                           model=model, sampling=sargs, k=env_cfg.rollouts_per_example,
                                           max_retries=int(getattr(env_cfg, "max_retries", 0) or 0),
                                           max_inflight=ev.max_inflight_rollouts,
-                                          journal=journal, live=live))
+                                          journal=journal, live=live, cancel=cancel))
+    if cancel is not None and cancel.is_set():
+        return None  # stopped part-way; committed episodes stay in the journal
     elapsed = journal.elapsed_seconds
     by_ex: dict[str, list[float | None]] = {}
     for o in outs:
