@@ -6,7 +6,6 @@ from __future__ import annotations
 
 import gc
 import os
-from pathlib import Path
 
 import pytest
 

@@ -11,6 +11,8 @@ RunMonitor, monitor.py:281-700, so its dashboard and tools read our runs):
     <output_dir>/samples.jsonl      bounded sample history
     <output_dir>/logs/<role>[.rank-N].jsonl   structured logs
 
+    <output_dir>/wandb_run_id.txt   the W&B run id (resumed runs continue it)
+
 Only the global rank 0 writes.  W&B is used when importable and enabled;
 otherwise the run continues with local files (offline fallback).
 """
@@ -199,7 +201,7 @@ class RunMonitor:
                 "config": safe,
             }
             _write_json_atomic(self.run_metadata_file, meta)
-        self._init_wandb(safe)
+        self._init_wandb(safe, resumed_from)
         self.log_event("run_resumed" if resumed_from else "run_started", payload={"resumed_from": resumed_from})
         self._heartbeat("running", None)
 
@@ -283,7 +285,20 @@ class RunMonitor:
         self.output_dir.mkdir(parents=True, exist_ok=True)
         _write_json_atomic(self.heartbeat_file, payload)
 
-    def _init_wandb(self, cfg: Any) -> None:
+    def _init_wandb(self, cfg: Any, resumed_from: str | None = None) -> None:
+        """Start the W&B run (ref monitor.py:555-640).
+
+        * A resumed run continues the W&B run whose id ``wandb_run_id.txt``
+          holds (``resume="allow"``); every run writes its id there.
+        * Shared mode (``WANDB_SHARED_MODE=1`` and ``WANDB_RUN_ID`` from the
+          process launcher, online runs only): every role of one RL run logs
+          into the same W&B run, labelled by ``WANDB_SHARED_LABEL``; the primary
+          (``WANDB_SHARED_PRIMARY``, default the orchestrator) owns the run
+          and the launcher finishes it after every role has exited.
+        * An online start that fails falls back to an offline W&B run in the
+          run directory (``monitor.wandb.offline_fallback``); without the
+          package the run keeps its local files only.
+        """
         w = self.wandb_cfg
         if w is None or not getattr(w, "enabled", False) or getattr(w, "mode", "disabled") == "disabled":
             return
@@ -292,22 +307,118 @@ class RunMonitor:
         except ImportError:
             self.log_event("wandb_unavailable", payload={"reason": "wandb is not installed; local files only"})
             return
+        timeout = float(getattr(w, "init_timeout_seconds", 30.0))
+        settings_cls = getattr(wandb, "Settings", None)
+        shared = shared_wandb_settings(wandb, configured_mode=w.mode, init_timeout_seconds=timeout)
+        prev = self._read_wandb_run_id() if shared is None and resumed_from is not None else None
+        kwargs: dict[str, Any] = {"project": w.project or "wavelet", "entity": w.entity, "name": w.name,
+                                  "group": w.group, "tags": w.tags, "config": cfg, "dir": str(self.output_dir),
+                                  "id": prev, "resume": "allow" if prev is not None else None}
+        if shared is not None:
+            kwargs.update(shared)
+        elif callable(settings_cls):
+            kwargs["settings"] = settings_cls(init_timeout=timeout)
+        online_overview = w.mode == "online"
         try:
-            settings = None
-            if hasattr(wandb, "Settings"):  # monitor.wandb.init_timeout_seconds bounds the start-up handshake
-                settings = wandb.Settings(init_timeout=float(getattr(w, "init_timeout_seconds", 30.0)))
-            self._wandb = wandb.init(project=w.project, entity=w.entity, name=w.name, group=w.group, tags=w.tags,
-                                     mode=w.mode, config=cfg, dir=str(self.output_dir),
-                                     **({"settings": settings} if settings is not None else {}))
+            self._wandb = wandb.init(**kwargs) if shared is not None else wandb.init(mode=w.mode, **kwargs)
+        except Exception as e:
+            if w.mode != "online" or not getattr(w, "offline_fallback", True):
+                raise
+            self.log_event("wandb_init_failed", payload={"error": str(e), "fallback": "offline"})
+            fb = {**kwargs, "id": None, "resume": None}
+            if callable(settings_cls):
+                fb["settings"] = settings_cls(init_timeout=timeout)
+            try:
+                self._wandb = wandb.init(mode="offline", **fb)
+            except Exception as e2:  # no W&B at all: local files only
+                self.log_event("wandb_init_failed", payload={"error": str(e2), "fallback": "local files"})
+                self._wandb = None
+                return
+            online_overview = False
+        define = getattr(self._wandb, "define_metric", None)
+        if callable(define):  # every metric is plotted against the optimizer step
+            define("step")
+            define("*", step_metric="step")
+        run_id = os.environ.get("WANDB_RUN_ID") if shared is not None else getattr(self._wandb, "id", None)
+        self._write_wandb_run_id(run_id)
+        if online_overview:
             from .wandb_overview import maybe_create_overview
 
             maybe_create_overview(self._wandb, cfg if isinstance(cfg, dict) else None, w)
-        except Exception as e:  # offline fallback
-            if getattr(w, "offline_fallback", True):
-                self.log_event("wandb_init_failed", payload={"error": str(e)})
-                self._wandb = None
-            else:
-                raise
+
+    @property
+    def wandb_run_id_file(self) -> Path:
+        return self.output_dir / "wandb_run_id.txt"
+
+    def _read_wandb_run_id(self) -> str | None:
+        try:
+            rid = self.wandb_run_id_file.read_text(encoding="utf-8").strip()
+        except OSError:
+            return None
+        return rid or None
+
+    def _write_wandb_run_id(self, run_id: object) -> None:
+        if isinstance(run_id, str) and run_id:
+            self.output_dir.mkdir(parents=True, exist_ok=True)
+            self.wandb_run_id_file.write_text(run_id, encoding="utf-8")
+
+
+def shared_wandb_settings(wandb: Any, *, configured_mode: str, init_timeout_seconds: float) -> dict[str, Any] | None:
+    """``wandb.init`` arguments that join the launcher's shared run, or None
+    when this process is not part of one."""
+    if (os.environ.get("WANDB_SHARED_MODE") != "1" or configured_mode != "online"
+            or os.environ.get("WANDB_MODE") in {"disabled", "offline"}):
+        return None
+    run_id = os.environ.get("WANDB_RUN_ID", "").strip()
+    if not run_id:
+        raise ValueError("WANDB_SHARED_MODE=1 requires WANDB_RUN_ID")
+    settings_cls = getattr(wandb, "Settings", None)
+    if not callable(settings_cls):
+        raise TypeError("the installed W&B SDK has no Settings for shared runs")
+    label = os.environ.get("WANDB_SHARED_LABEL")
+    primary = os.environ.get("WANDB_SHARED_PRIMARY", "orchestrator")
+    finisher = os.environ.get("WANDB_SHARED_FINISHER", primary)
+    return {"id": run_id, "resume": "allow",
+            "settings": settings_cls(mode="shared", init_timeout=init_timeout_seconds, x_label=label,
+                                     x_primary=label == primary, x_update_finish_state=label == finisher)}
+
+
+def shared_wandb_environment(cfg: Any) -> dict[str, str]:
+    """Environment that makes every role of a process-mode RL run log into
+    one W&B run (online runs only): a fresh run id, or the persisted one when
+    the run resumes from a checkpoint (ref orchestrator/runtime.py:559-585)."""
+    import secrets
+
+    w = cfg.monitor.wandb
+    if not w.enabled or w.mode != "online" or os.environ.get("WANDB_MODE") in {"disabled", "offline"}:
+        return {}
+    out = Path(cfg.output_dir)
+    id_file = out / "wandb_run_id.txt"
+    run_id = os.environ.get("WANDB_RUN_ID", "").strip()
+    ck = getattr(cfg, "ckpt", None)
+    if not run_id and ck is not None and ck.is_resuming and id_file.exists():
+        run_id = id_file.read_text(encoding="utf-8").strip()
+    run_id = run_id or secrets.token_hex(4)
+    out.mkdir(parents=True, exist_ok=True)
+    id_file.write_text(run_id, encoding="utf-8")
+    return {"WANDB_SHARED_MODE": "1", "WANDB_RUN_ID": run_id}
+
+
+def finish_shared_wandb_run(cfg: Any, shared_env: dict[str, str], *, exit_code: int) -> None:
+    """Close the shared run once the launcher has joined every role."""
+    if not shared_env:
+        return
+    try:
+        import wandb  # type: ignore
+
+        run = wandb.init(id=shared_env["WANDB_RUN_ID"], project=cfg.monitor.wandb.project or "wavelet",
+                         entity=cfg.monitor.wandb.entity, dir=str(cfg.output_dir),
+                         settings=wandb.Settings(mode="shared", x_label="launcher", x_primary=False,
+                                                 x_update_finish_state=True,
+                                                 init_timeout=cfg.monitor.wandb.init_timeout_seconds))
+        run.finish(exit_code=exit_code)
+    except Exception as e:  # noqa: BLE001 - the roles' data is already uploaded
+        logging.getLogger("wavelet").warning("could not finish the shared W&B run: %s", e)
 
 
 def _usage(prefix: str, path: Path) -> dict[str, Any]:

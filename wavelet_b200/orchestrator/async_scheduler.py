@@ -236,6 +236,7 @@ class AsyncRolloutScheduler:
         # status snapshots; both optional
         self.run_state = None
         self.status_sink = None
+        self.metrics_sink: Callable | None = None  # each published step's metrics (W&B)
         self.wait_memory = wait_memory or (lambda: wait_for_trainer_memory(cfg))
         self.concurrent_generate = bool(getattr(engine, "concurrent_generate", False))
         self.concurrent_load = bool(getattr(engine, "concurrent_policy_load", False))
@@ -461,6 +462,8 @@ class AsyncRolloutScheduler:
                       "policy_lag": None if st.policy is None else st.step // self.C - st.policy,
                       "time/step_seconds": time.perf_counter() - st.t_submit, "timestamp": utc_now()})
             append_jsonl(self.out / "orchestrator_metrics.jsonl", m)
+            if self.metrics_sink is not None:
+                self.metrics_sink(m)
             log.info("published rollouts for step %d (policy %s, reward %.4f)", st.step, st.policy,
                      m.get("reward/mean", 0.0))
             if self.run_state is not None:

@@ -162,7 +162,8 @@ def wait_for_roles(jobs: list[RoleProcess], services: list[RoleProcess], poll: f
             s.terminate()
 
 
-def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executable) -> tuple[list[RoleSpec], list[RoleSpec]]:
+def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executable,
+                shared_wandb: dict[str, str] | None = None) -> tuple[list[RoleSpec], list[RoleSpec]]:
     pl = plan(cfg)
     base = config_to_plain(cfg)
     device_transfer = cfg.policy_transfer.type == "nccl" and cfg.inference.mode == "vllm_http"
@@ -217,6 +218,9 @@ def build_roles(cfg, attempt: pathing.LaunchAttempt, python: str = sys.executabl
             RoleSpec("rl-inference", [python, "-m", "wavelet_b200", "rl-inference", "@", str(inf_path)], env_i)]
     for s in services:
         s.env.update(cfg.launcher.env_vars.for_role("inference"))
+    if shared_wandb:  # every role logs into one W&B run, labelled by its role
+        env_t.update(shared_wandb, WANDB_SHARED_LABEL="trainer")
+        env_i.update(shared_wandb, WANDB_SHARED_LABEL="orchestrator")
     return services, jobs
 
 
@@ -227,7 +231,10 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
     attempt = pathing.create_launch_attempt(out)
     pathing.write_launch_artifacts(attempt, command="rl", argv=argv)
     dump_yaml(attempt.config_dir / "rl.yaml", config_to_plain(cfg))
-    services, jobs = build_roles(cfg, attempt)
+    from ..monitor import finish_shared_wandb_run, shared_wandb_environment
+
+    shared = shared_wandb_environment(cfg)
+    services, jobs = build_roles(cfg, attempt, shared_wandb=shared)
     runner = RoleRunner(cfg, attempt.log_dir)
     running_services = [runner.start(s) for s in services]
     if running_services:
@@ -246,11 +253,15 @@ def run_process_launcher(cfg, argv: list[str]) -> int:
         raise KeyboardInterrupt
 
     signal.signal(signal.SIGTERM, _sigterm)
+    rc = 1
     try:
-        return wait_for_roles(running_jobs, running_services, cfg.launcher.poll_interval_seconds)
+        rc = wait_for_roles(running_jobs, running_services, cfg.launcher.poll_interval_seconds)
+        return rc
     except KeyboardInterrupt:
         for r in running_jobs + running_services:
             r.terminate()
-        return 130
+        rc = 130
+        return rc
     finally:
         runner.close()
+        finish_shared_wandb_run(cfg, shared, exit_code=rc)

@@ -64,9 +64,15 @@ class RolloutScheduler:
         pipe.run_state = state
         pipe.status_sink = lambda snap: state.update(pipeline=snap, queue_depth=snap["ready"] + snap["inflight"])
         handle = maybe_state_server(self.cfg, state)
+        wb = self._wandb_monitor()
+        if wb is not None:  # orchestrator metrics also go to W&B (the shared run of the roles when launched together)
+            pipe.metrics_sink = lambda m: wb.log({k: v for k, v in m.items() if k not in ("step", "timestamp")},
+                                                 m.get("optimizer_step", m.get("step")))
+        status = "failed"
         try:
             rc = pipe.run()
             state.update(status="completed")
+            status = "completed"
             return rc
         except BaseException:
             state.update(status="failed")
@@ -74,6 +80,23 @@ class RolloutScheduler:
         finally:
             if handle is not None:
                 handle.close()
+            if wb is not None:
+                wb.finish(status=status, step=None)
+
+    def _wandb_monitor(self):
+        """A W&B-only monitor of the rollout role (``monitor.wandb``); the
+        local metric files stay the trainer's and ``orchestrator_metrics.jsonl``."""
+        w = self.cfg.monitor.wandb
+        if not self.cfg.monitor.enabled or not w.enabled or w.mode == "disabled":
+            return None
+        from ..monitor import RunMonitor
+        from ..utils.config import config_to_plain
+
+        mon = RunMonitor(self.out, write_events=False, write_metrics_jsonl=False, write_metrics_csv=False,
+                         write_run_metadata=False, write_heartbeat=False, log_cuda_memory=False,
+                         log_disk_usage=False, wandb=w)
+        mon.start_run(run_config=config_to_plain(self.cfg))
+        return mon if mon._wandb is not None else None
 
 
 class _GeneratorAdapter:
