@@ -1,0 +1,127 @@
+"""Dashboard: external tracker history (W&B through a stand-in API, Trackio
+from its SQLite store), evaluation rows with filters and sorting, and episode
+snapshots by id (ref dashboard/external.py, artifacts.py:330-370, live.py)."""
+
+from __future__ import annotations
+
+import json
+import sqlite3
+
+import pytest
+
+
+def _run(tmp_path, wandb=None):
+    run = tmp_path / "run"
+    (run / "configs" / "latest" / "resolved").mkdir(parents=True)
+    cfg = {"monitor": {"wandb": {"enabled": True, "mode": "online", "project": "proj", "entity": "me",
+                                 "name": "nice", **(wandb or {})}}}
+    (run / "configs" / "latest" / "resolved" / "rl.yaml").write_text(json.dumps(cfg))
+    (run / "metrics.jsonl").write_text(json.dumps({"step": 1, "loss": 2.0}) + "\n")
+    return run
+
+
+class _Api:
+    def __init__(self):
+        self.paths = []
+
+    def run(self, path):
+        self.paths.append(path)
+
+        class R:
+            def scan_history(self):
+                return [{"_step": 1, "_timestamp": 10.0, "_runtime": 3, "train/loss": 2.5},
+                        {"_step": 2, "_timestamp": 11.0, "train/loss": 2.0, "lr": 1e-4}]
+
+        return R()
+
+
+def test_wandb_history_source(tmp_path):
+    from wavelet_b200.dashboard.external import ExternalSources
+
+    run = _run(tmp_path)
+    api = _Api()
+    ext = ExternalSources(run, {"monitor": {"wandb": {"enabled": True, "project": "proj", "entity": "me"}}},
+                          wandb_api=api, trackio_dir=tmp_path / "none")
+    assert ext.sources["wandb"].status()["status"] == "unavailable"  # no run id persisted yet
+    (run / "wandb_run_id.txt").write_text("abc")
+    ext = ExternalSources(run, {"monitor": {"wandb": {"enabled": True, "project": "proj", "entity": "me"}}},
+                          wandb_api=api, trackio_dir=tmp_path / "none")
+    src = ext.sources["wandb"]
+    src.refresh_now()
+    assert api.paths == ["me/proj/abc"]
+    assert src.status()["status"] == "ready" and src.status()["rows"] == 2
+    s = src.table().series(["train/loss"])
+    assert s["steps"] == [1.0, 2.0] and s["series"]["train/loss"] == [2.5, 2.0]
+    assert "_runtime" not in src.table().keys()
+    assert ext.status()[1]["status"] == "unavailable"  # trackio: no database
+
+
+def _trackio_db(root, project, run, rows):
+    root.mkdir(parents=True, exist_ok=True)
+    con = sqlite3.connect(root / f"{project}.db")
+    con.execute("CREATE TABLE metrics (id INTEGER PRIMARY KEY, run_name TEXT, step INTEGER, timestamp TEXT, "
+                "metrics TEXT)")
+    for step, m in rows:
+        con.execute("INSERT INTO metrics (run_name, step, timestamp, metrics) VALUES (?, ?, ?, ?)",
+                    (run, step, f"t{step}", json.dumps(m)))
+    con.commit()
+    con.close()
+
+
+def test_trackio_history_source(tmp_path):
+    from wavelet_b200.dashboard.external import trackio_source
+
+    run = _run(tmp_path)
+    root = tmp_path / "trackio"
+    _trackio_db(root, "proj", "nice", [(0, {"reward": 0.1}), (1, {"reward": 0.4})])
+    src = trackio_source(run, {"monitor": {"wandb": {"project": "proj", "name": "nice"}}}, root)
+    src.refresh_now()
+    assert src.status()["status"] == "ready"
+    assert src.table().series(["reward"])["series"]["reward"] == [0.1, 0.4]
+    # the sidecar names another run: not present
+    (run / "trackio_run.json").write_text(json.dumps({"project": "proj", "run": "other"}))
+    assert trackio_source(run, {}, root).status()["status"] == "unavailable"
+
+
+def test_dashboard_routes_for_external_evals_and_episodes(tmp_path, monkeypatch):
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.dashboard.server import RunRegistry, build_app
+    from wavelet_b200.orchestrator.live import LiveEpisode
+
+    monkeypatch.setenv("TRACKIO_DIR", str(tmp_path / "trackio"))
+    _trackio_db(tmp_path / "trackio", "proj", "nice", [(0, {"reward": 0.1}), (3, {"reward": 0.4})])
+    run = _run(tmp_path)
+    ev = run / "evals" / "env1"
+    ev.mkdir(parents=True)
+    rows = [{"example_id": 0, "reward": 1.0, "completion_ids": [1, 2, 3]},
+            {"example_id": 1, "reward": 0.0, "completion_ids": [1]},
+            {"example_id": 1, "error": "boom", "completion": []},
+            {"example_id": 2, "reward": 0.5, "is_truncated": True,
+             "trajectory": [{"tokens": {"completion_ids": [4, 5]}}, {"tokens": {"completion_ids": [6]}}]}]
+    (ev / "step-5.jsonl").write_text("".join(json.dumps(r) + "\n" for r in rows))
+    with LiveEpisode(run, "env1", "eval", step=5, example_id="k") as ep:
+        ep.event("generation_finished", samples=1)
+    c = TestClient(build_app(RunRegistry(runs=[run])))
+    st = {x["source"]: x for x in c.get("/api/runs/run/external").json()}
+    assert st["trackio"]["status"] in ("loading", "ready") and st["wandb"]["status"] == "unavailable"
+    import time  # the reader fetches the tracker history in the background; wait for it
+
+    for _ in range(100):
+        if c.get("/api/runs/run/external").json()[1]["status"] == "ready":
+            break
+        time.sleep(0.02)
+    assert "trackio" in c.get("/api/runs/run/metrics/keys").json()
+    s = c.get("/api/runs/run/series", params={"source": "trackio", "keys": "reward"}).json()
+    assert s["steps"] == [0.0, 3.0]
+    r = c.get("/api/runs/run/evals/5/env1/rows", params={"sort": "reward", "order": "desc"}).json()
+    assert r["total"] == 4 and [x["example_id"] for x in r["rows"]] == ["0", "2", "1", "1"]
+    assert r["stats"]["errors"] == 1 and r["stats"]["truncated"] == 1 and r["stats"]["reward"]["count"] == 3
+    assert r["rows"][1]["completion_len"] == 3  # summed over the trajectory's model calls
+    r = c.get("/api/runs/run/evals/5/env1/rows", params={"has_error": "false", "min_reward": 0.4}).json()
+    assert r["filtered"] == 2
+    assert c.get("/api/runs/run/evals/9/env1/rows").json()["available"] is False
+    assert c.get("/api/runs/run/evals/5/..%2F..%2Fx/rows").status_code in (200, 404)
+    doc = c.get(f"/api/runs/run/episodes/{ep.id}").json()
+    assert doc["id"] == ep.id and doc["status"] == "completed"
+    assert c.get("/api/runs/run/episodes/nope-not-an-id").status_code == 404

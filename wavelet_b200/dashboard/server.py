@@ -2,10 +2,13 @@
 (reference dashboard/server.py:24-379).  Nothing under a run is modified.
 
 Routes (prefix ``/api``): ``health``, ``runs``, ``current`` and per run
-``summary``, ``config``, ``metrics/keys``, ``series``, ``nodes``, ``evals``,
-``rollouts``, ``rollouts/rows``, ``queue``, ``timeline``, ``events``,
-``samples``, ``logs``, ``logs/{name}``, ``episodes``.  ``/`` serves the
-static UI (``dashboard/static``).
+``summary``, ``config``, ``metrics/keys``, ``series`` (sources ``trainer``,
+``orchestrator``, ``eval`` and the external trackers ``wandb`` / ``trackio``),
+``external``, ``nodes``, ``evals``, ``evals/{step}/{env}/rows`` (filtered,
+sorted, paged), ``rollouts``, ``rollouts/rows``, ``queue``, ``timeline``,
+``events``, ``samples``, ``logs``, ``logs/{name}``, ``episodes``,
+``episodes/{id}``, ``live``, ``live/{id}``.  ``/`` serves the static UI
+(``dashboard/static``).
 """
 
 from __future__ import annotations
@@ -25,10 +28,79 @@ def is_run_dir(p: Path) -> bool:
                                                           "orchestrator_metrics.jsonl", "configs"))
 
 
+def _num(v: Any) -> float | None:
+    return float(v) if isinstance(v, (int, float)) and not isinstance(v, bool) else None
+
+
+def eval_row(i: int, r: dict[str, Any]) -> dict[str, Any]:
+    """An evaluation rollout as a table row (native and verifiers-package rows)."""
+    traj = r.get("trajectory") or []
+    n = sum(len(((st or {}).get("tokens") or {}).get("completion_ids") or []) for st in traj) if traj \
+        else len(r.get("completion_ids") or [])
+    return {"row_index": i, "example_id": None if r.get("example_id") is None else str(r.get("example_id")),
+            "reward": _num(r.get("reward")), "error": r.get("error"), "is_truncated": bool(r.get("is_truncated")),
+            "completion_len": n, "row": r}
+
+
+def filter_rows(rows: list[dict[str, Any]], *, example_id: str | None = None, min_reward: float | None = None,
+                max_reward: float | None = None, truncated: bool | None = None,
+                has_error: bool | None = None) -> list[dict[str, Any]]:
+    out = []
+    for r in rows:
+        rw = r.get("reward")
+        if example_id is not None and r.get("example_id") != example_id:
+            continue
+        if min_reward is not None and (rw is None or rw < min_reward):
+            continue
+        if max_reward is not None and (rw is None or rw > max_reward):
+            continue
+        if truncated is not None and bool(r.get("is_truncated")) != truncated:
+            continue
+        if has_error is not None and (r.get("error") is not None) != has_error:
+            continue
+        out.append(r)
+    return out
+
+
+def summarize(values: list[float]) -> dict[str, Any]:
+    if not values:
+        return {"count": 0}
+    v = sorted(values)
+    return {"count": len(v), "mean": sum(v) / len(v), "min": v[0], "max": v[-1], "median": v[len(v) // 2]}
+
+
+EVAL_SORT_KEYS = ("row_index", "reward", "completion_len", "example_id")
+
+
 class RunReader:
     def __init__(self, path: Path):
         self.path = Path(path)
         self.tables: dict[str, MetricTable] = {}
+        self._external = None
+
+    def resolved_config(self) -> dict[str, Any]:
+        """The run's resolved config (the first role file of the latest launch)."""
+        import yaml
+
+        d = self.path / "configs" / "latest" / "resolved"
+        for name in ("rl.yaml", "sft.yaml", "rl_trainer.yaml", "rl_inference.yaml"):
+            p = d / name
+            if p.is_file():
+                try:
+                    return yaml.safe_load(p.read_text()) or {}
+                except yaml.YAMLError:
+                    return {}
+        return {}
+
+    def external(self):
+        from .external import ExternalSources
+
+        if self._external is None:
+            self._external = ExternalSources(self.path, self.resolved_config())
+        return self._external
+
+    def external_status(self) -> list[dict[str, Any]]:
+        return self.external().status()
 
     @property
     def run_id(self) -> str:
@@ -42,8 +114,12 @@ class RunReader:
             return None
 
     def table(self, source: str) -> MetricTable:
+        from .external import SOURCES as EXTERNAL
+
+        if source in EXTERNAL:
+            return self.external().table(source)
         if source not in SOURCES:
-            raise KeyError(f"unknown source {source!r} (one of {sorted(SOURCES)})")
+            raise KeyError(f"unknown source {source!r} (one of {sorted(SOURCES) + list(EXTERNAL)})")
         t = self.tables.get(source)
         if t is None:
             t = self.tables[source] = MetricTable(self.path / SOURCES[source])
@@ -69,7 +145,10 @@ class RunReader:
         return out
 
     def metric_keys(self) -> dict[str, list[str]]:
-        return {s: self.table(s).keys() for s in SOURCES}
+        out = {s: self.table(s).keys() for s in SOURCES}
+        for s in self.external().ready():  # trackers a run also logs to, once fetched
+            out[s] = self.table(s).keys()
+        return out
 
     def series(self, source, keys, **kw) -> dict[str, Any]:
         return self.table(source).series(keys, **kw)
@@ -86,6 +165,25 @@ class RunReader:
             for env in sorted(p for p in d.iterdir() if p.is_dir()):
                 envs[env.name] = sorted(int(p.stem.split("-")[1]) for p in env.glob("step-*.jsonl"))
         return {"metrics": read_jsonl(self.path / "eval_metrics.jsonl"), "envs": envs}
+
+    def eval_rows(self, step: int, env: str, *, sort: str = "row_index", descending: bool = False,
+                  offset: int = 0, limit: int = 50, **filters) -> dict[str, Any]:
+        """One evaluation's rollouts, filtered, sorted and paged, with reward statistics."""
+        d = (self.path / "evals").resolve()
+        p = (d / env / f"step-{step}.jsonl").resolve()
+        if p.parent.parent != d or not p.is_file():
+            return {"available": False, "reason": f"no eval rollouts for step {step} env {env}"}
+        rows = [eval_row(i, r) for i, r in enumerate(read_jsonl(p))]
+        kept = filter_rows(rows, **filters)
+        key = sort if sort in EVAL_SORT_KEYS else "row_index"
+        have = sorted((r for r in kept if r.get(key) is not None), key=lambda r: r[key], reverse=descending)
+        kept = have + [r for r in kept if r.get(key) is None]  # rows without the key last, either order
+        rewards = [r["reward"] for r in rows if r["reward"] is not None]
+        return {"available": True, "step": step, "env": env, "total": len(rows), "filtered": len(kept),
+                "stats": {"reward": summarize(rewards),
+                          "errors": sum(r["error"] is not None for r in rows),
+                          "truncated": sum(r["is_truncated"] for r in rows)},
+                "rows": kept[offset : offset + limit]}
 
     def _queue_dir(self) -> Path:
         return self.path / "rollouts"
@@ -215,6 +313,28 @@ def build_app(registry: RunRegistry, static_dir: Path | None = None):
     @app.get(API + "/runs/{rid}/evals")
     def evals(rid: str):
         return reader(rid).evals()
+
+    @app.get(API + "/runs/{rid}/evals/{step}/{env}/rows")
+    def eval_rows(rid: str, step: int, env: str, sort: str = "row_index", order: str = "asc",
+                  offset: int = Query(0, ge=0), limit: int = Query(50, ge=1, le=500), example_id: str | None = None,
+                  min_reward: float | None = None, max_reward: float | None = None, truncated: bool | None = None,
+                  has_error: bool | None = None):
+        return reader(rid).eval_rows(step, env, sort=sort, descending=order == "desc", offset=offset, limit=limit,
+                                     example_id=example_id, min_reward=min_reward, max_reward=max_reward,
+                                     truncated=truncated, has_error=has_error)
+
+    @app.get(API + "/runs/{rid}/external")
+    def external(rid: str):
+        return reader(rid).external_status()
+
+    @app.get(API + "/runs/{rid}/episodes/{eid}")
+    def episode(rid: str, eid: str):
+        from ..orchestrator.live import read_episode
+
+        doc = read_episode(reader(rid).path, eid)
+        if doc is None:
+            raise HTTPException(404, "episode snapshot unavailable")
+        return doc
 
     @app.get(API + "/runs/{rid}/rollouts")
     def rollouts(rid: str):
