@@ -125,3 +125,37 @@ def test_dashboard_routes_for_external_evals_and_episodes(tmp_path, monkeypatch)
     doc = c.get(f"/api/runs/run/episodes/{ep.id}").json()
     assert doc["id"] == ep.id and doc["status"] == "completed"
     assert c.get("/api/runs/run/episodes/nope-not-an-id").status_code == 404
+
+
+def test_rollout_rows_view_filters_and_sorts(tmp_path):
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.dashboard.server import RunRegistry, build_app
+
+    run = _run(tmp_path)
+    d = run / "rollouts" / "step-000002"
+    d.mkdir(parents=True)
+    recs = [{"reward": 1.0, "advantage": 0.5, "input_ids": [1, 2, 3, 4], "loss_mask": [False, False, True, True],
+             "inference_logprobs": [-0.5, -1.5], "completion": [{"role": "assistant", "content": "the answer"}],
+             "metadata": {"group": "2:0", "env": "math", "example_id": 7, "policy_step": 1}},
+            {"reward": 0.0, "advantage": -0.5, "input_ids": [1, 2, 3], "loss_mask": [False, False, True],
+             "inference_logprobs": [-0.1], "completion": [{"role": "assistant", "content": "nope"}],
+             "metadata": {"group": "2:0", "env": "math", "example_id": 7, "is_truncated": True}},
+            {"reward": 0.5, "advantage": 0.0, "input_ids": [1, 2], "loss_mask": [False, True],
+             "metadata": {"group": "2:1", "env": "code", "example_id": 8}}]
+    (d / "rollouts.jsonl").write_text("".join(json.dumps(r) + "\n" for r in recs))
+    c = TestClient(build_app(RunRegistry(runs=[run])))
+    base = "/api/runs/run/rollouts/rows"
+    raw = c.get(base, params={"step": 2}).json()
+    assert raw["total"] == 3 and raw["rows"][0]["metadata"]["env"] == "math"  # records as stored
+    v = c.get(base, params={"step": 2, "view": True, "sort": "reward", "order": "desc"}).json()
+    assert [r["reward"] for r in v["rows"]] == [1.0, 0.5, 0.0]
+    top = v["rows"][0]
+    assert top["completion_token_count"] == 2 and top["input_token_count"] == 4
+    assert top["logprob_mean"] == -1.0 and top["logprob_min"] == -1.5 and "row" not in top
+    assert v["stats"]["truncated"] == 1 and v["stats"]["reward"]["count"] == 3
+    assert c.get(base, params={"step": 2, "view": True, "env": "code"}).json()["filtered"] == 1
+    assert c.get(base, params={"step": 2, "view": True, "advantage_sign": "negative"}).json()["rows"][0]["reward"] == 0.0
+    assert c.get(base, params={"step": 2, "view": True, "search": "ANSWER"}).json()["filtered"] == 1
+    full = c.get(base, params={"step": 2, "view": True, "full": True, "group_key": "2:1"}).json()
+    assert full["rows"][0]["row"]["metadata"]["example_id"] == 8

@@ -42,13 +42,51 @@ def eval_row(i: int, r: dict[str, Any]) -> dict[str, Any]:
             "completion_len": n, "row": r}
 
 
+ROLLOUT_SORT_KEYS = ("row_index", "reward", "advantage", "completion_token_count", "input_token_count",
+                     "logprob_mean", "logprob_min", "group_key", "env", "example_id", "policy_step", "turn_count")
+
+
+def rollout_row(i: int, r: dict[str, Any], full: bool = False) -> dict[str, Any]:
+    """A rollout record as a compact table row (the record itself with ``full``)."""
+    md = r.get("metadata") or {}
+    lps = [x for x in (r.get("inference_logprobs") or []) if isinstance(x, (int, float))]
+    mask = r.get("loss_mask") or []
+    adv = r.get("advantage")
+    text = " ".join(str(m.get("content") or "") for m in (r.get("completion") or []) if isinstance(m, dict))
+    out = {"row_index": i, "reward": _num(r.get("reward")), "advantage": _num(adv) if not isinstance(adv, list)
+           else (sum(adv) / len(adv) if adv else None),
+           "completion_token_count": md.get("completion_token_count", sum(bool(x) for x in mask)),
+           "input_token_count": len(r.get("input_ids") or []),
+           "logprob_mean": sum(lps) / len(lps) if lps else None, "logprob_min": min(lps) if lps else None,
+           "group_key": None if md.get("group") is None else str(md.get("group")),
+           "env": md.get("env") or r.get("source"), "example_id": None if md.get("example_id") is None
+           else str(md.get("example_id")), "policy_step": md.get("policy_step"),
+           "is_truncated": bool(md.get("is_truncated")), "turn_count": md.get("turn_count"),
+           "stop_condition": md.get("stop_condition") or md.get("finish_reason"), "text": text[:3000]}
+    if full:
+        out["row"] = r
+    return out
+
+
 def filter_rows(rows: list[dict[str, Any]], *, example_id: str | None = None, min_reward: float | None = None,
                 max_reward: float | None = None, truncated: bool | None = None,
-                has_error: bool | None = None) -> list[dict[str, Any]]:
+                has_error: bool | None = None, env: str | None = None, group_key: str | None = None,
+                advantage_sign: str | None = None, search: str | None = None) -> list[dict[str, Any]]:
     out = []
     for r in rows:
         rw = r.get("reward")
         if example_id is not None and r.get("example_id") != example_id:
+            continue
+        if env is not None and r.get("env") != env:
+            continue
+        if group_key is not None and r.get("group_key") != group_key:
+            continue
+        if advantage_sign is not None:
+            a = r.get("advantage")
+            sign = "zero" if not a else ("positive" if a > 0 else "negative")
+            if sign != advantage_sign:
+                continue
+        if search and search.lower() not in str(r.get("text", "")).lower():
             continue
         if min_reward is not None and (rw is None or rw < min_reward):
             continue
@@ -202,9 +240,23 @@ class RunReader:
                         "manifest": man})
         return out
 
-    def rollout_rows(self, step: int, offset: int = 0, limit: int = 50) -> dict[str, Any]:
+    def rollout_rows(self, step: int, offset: int = 0, limit: int = 50, *, view: bool = False, sort: str = "row_index",
+                     descending: bool = False, full: bool = False, **filters) -> dict[str, Any]:
+        """A queue step's rollout records; ``view`` returns compact rows that
+        can be filtered and sorted (with reward / advantage statistics)."""
         rows = read_jsonl(self._queue_dir() / f"step-{step:06d}" / "rollouts.jsonl")
-        return {"step": step, "total": len(rows), "rows": rows[offset : offset + limit]}
+        if not view:
+            return {"step": step, "total": len(rows), "rows": rows[offset : offset + limit]}
+        vs = [rollout_row(i, r, full) for i, r in enumerate(rows)]
+        kept = filter_rows(vs, **filters)
+        key = sort if sort in ROLLOUT_SORT_KEYS else "row_index"
+        have = sorted((r for r in kept if r.get(key) is not None), key=lambda r: r[key], reverse=descending)
+        kept = have + [r for r in kept if r.get(key) is None]
+        return {"step": step, "total": len(vs), "filtered": len(kept),
+                "stats": {"reward": summarize([r["reward"] for r in vs if r["reward"] is not None]),
+                          "advantage": summarize([r["advantage"] for r in vs if r["advantage"] is not None]),
+                          "truncated": sum(r["is_truncated"] for r in vs)},
+                "rows": kept[offset : offset + limit]}
 
     def queue(self) -> dict[str, Any]:
         r = self.rollouts()
@@ -341,8 +393,17 @@ def build_app(registry: RunRegistry, static_dir: Path | None = None):
         return {"batches": reader(rid).rollouts()}
 
     @app.get(API + "/runs/{rid}/rollouts/rows")
-    def rollout_rows(rid: str, step: int, offset: int = Query(0, ge=0), limit: int = Query(50, ge=1, le=1000)):
-        return reader(rid).rollout_rows(step, offset, limit)
+    def rollout_rows(rid: str, step: int, offset: int = Query(0, ge=0), limit: int = Query(50, ge=1, le=1000),
+                     view: bool = False, sort: str = "row_index", order: str = "asc", full: bool = False,
+                     env: str | None = None, group_key: str | None = None, example_id: str | None = None,
+                     min_reward: float | None = None, max_reward: float | None = None, truncated: bool | None = None,
+                     advantage_sign: str | None = None, search: str | None = None):
+        if not view:
+            return reader(rid).rollout_rows(step, offset, limit)
+        return reader(rid).rollout_rows(step, offset, limit, view=True, sort=sort, descending=order == "desc",
+                                        full=full, env=env, group_key=group_key, example_id=example_id,
+                                        min_reward=min_reward, max_reward=max_reward, truncated=truncated,
+                                        advantage_sign=advantage_sign, search=search)
 
     @app.get(API + "/runs/{rid}/episodes")
     def episodes(rid: str, limit: int = Query(50, ge=1, le=1000)):
