@@ -456,7 +456,12 @@ class AsyncRolloutScheduler:
                                 policy_step=st.policy, tokens=sum(len(r.input_ids or []) for r in recs),
                                 reward_mean=stats.get("reward/mean"), prompt_source_state=st.prompt_state,
                                 curriculum_state=cur.state_dict() if cur is not None else None)
-            m = dict(stats)
+            from .rollout_metrics import rollout_metrics
+
+            m = rollout_metrics(rows, step=st.step, group_size=int(self.cfg.orchestrator.rollouts_per_example or 1),
+                                policy_step=st.policy, queue_step=st.step, optimizer_step=st.step // self.C,
+                                stats=stats)
+            m.update(stats)
             m.update(self.stats)
             m.update({"step": st.step, "optimizer_step": st.step // self.C, "policy_step": st.policy,
                       "policy_lag": None if st.policy is None else st.step // self.C - st.policy,

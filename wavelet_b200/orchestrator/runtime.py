@@ -215,6 +215,12 @@ class IntegratedRunner:
         if self.world.rank == 0:
             t.receiver.consumed(batch, step, t.step)
         m.update(self.orch.last_stats)
+        if self.world.rank == 0:  # the batch's rollout metrics (progress, solve rates, stop conditions, ...)
+            from .rollout_metrics import rollout_metrics
+
+            for k, v in rollout_metrics(rows, step=step, group_size=int(self.cfg.orchestrator.rollouts_per_example or 1),
+                                        policy_step=step, stats=self.orch.last_stats).items():
+                m.setdefault(k, v)
         m["time/generate_seconds"] = gen_s
         m["time/train_seconds"] = train_s
         m["time/step_seconds"] = time.perf_counter() - t0
