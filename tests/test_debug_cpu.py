@@ -85,3 +85,28 @@ def test_orchestrator_benchmark_materialize_and_trainer_parity(tmp_path, cpu, ca
     first = json.loads(out.read_text().splitlines()[0])
     assert sum(t["trainable"] for t in first) == sum(rows[0]["loss_mask"])
     capsys.readouterr()
+
+
+def test_preflight_lists_commands_paths_and_environments(tmp_path, monkeypatch):
+    import sys
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.debug import build_preflight_report
+
+    monkeypatch.setitem(sys.modules, "verifiers", None)  # the package is absent
+    cfg = RLConfig.model_validate({
+        "launcher": {"mode": "process", "env_vars": {"common": {"HF_TOKEN": "secret"}}},
+        "output_dir": str(tmp_path / "o"), "model": {"name": "tiny", "random_init": True}, "lora": None,
+        "data": {"source": "fake"},
+        "orchestrator": {"verifier_env_id": "someone/hub-env"},
+        "eval": {"env": [{"id": "equation_builder"}, {"id": "reverse"}]}})
+    r = build_preflight_report(cfg)
+    roles = [c["role"] for c in r["commands"]]
+    assert roles == ["inference-server-0", "rl-trainer", "rl-inference"]
+    assert all(c["env"].get("HF_TOKEN") in (None, "<redacted>") for c in r["commands"])
+    assert r["paths"]["rollouts"].endswith("rollouts") and r["paths"]["policies"].endswith("policies")
+    checks = {c["name"]: c for c in r["checks"]}
+    assert checks["env:equation_builder"]["status"] == "ok"
+    assert checks["env:someone/hub-env"]["status"] == "error" and not r["ok"]
+    assert "env:reverse" not in checks
+    assert r["summary"]["policy_freshness"]["effective_max_policy_lag"] == 0

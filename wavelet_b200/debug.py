@@ -153,16 +153,88 @@ def _model_checks(cfg: RLConfig) -> list[Check]:
     return out
 
 
+def _environment_checks(cfg: RLConfig) -> list[Check]:
+    """Every training / eval environment id resolves: a native one, or one
+    the installed ``verifiers`` package would load."""
+    from . import environments
+    from .orchestrator.verifier_envs import verifiers_available
+
+    o = cfg.orchestrator
+    ids = [e.id for e in o.envs] or ([o.verifier_env_id] if o.verifier_env_id else [])
+    ids += [e.id for e in (cfg.eval.env if cfg.eval is not None else [])
+            if not e.id.startswith("file:") and e.resolved_name not in ("reverse", "reverse_match", "synthetic-reverse")]
+    out = []
+    have_vf = None
+    for env_id in ids:
+        if environments.is_native(env_id):
+            out.append(Check(f"env:{env_id}", "ok", "native environment"))
+            continue
+        have_vf = verifiers_available() if have_vf is None else have_vf
+        out.append(Check(f"env:{env_id}", "ok" if have_vf else "error",
+                         "verifiers-package environment" if have_vf else "needs the verifiers package (not installed)"))
+    return out
+
+
+def _resolved_commands(cfg: RLConfig) -> list[dict[str, Any]]:
+    """The processes a launch would start, with their GPUs and extra environment
+    (role configs are rendered into a scratch directory, nothing is started)."""
+    import tempfile
+
+    if cfg.launcher.mode == "integrated":
+        return [{"role": "rl", "argv": ["wavelet", "rl", "(integrated)"], "env": {}, "service": False}]
+    from .orchestrator.launcher import build_roles
+    from .utils import pathing
+
+    with tempfile.TemporaryDirectory() as tmp:
+        services, jobs = build_roles(cfg, pathing.create_launch_attempt(Path(tmp)))
+    out = []
+    for r in [*services, *jobs]:
+        env = {k: ("<redacted>" if k in cfg.launcher.env_vars.for_role("common") or "KEY" in k or "TOKEN" in k else v)
+               for k, v in r.env.items()}
+        out.append({"role": r.name, "argv": [a if not a.startswith(tmp) else "<config>" for a in r.argv],
+                    "env": env, "service": r.service})
+    return out
+
+
+def _paths(cfg: RLConfig) -> dict[str, str]:
+    from .transport.queue import resolve_policy_dir, resolve_queue_dir
+
+    od = Path(cfg.output_dir)
+    return {"output_dir": str(od), "rollouts": str(resolve_queue_dir(od, cfg.transport)),
+            "policies": str(resolve_policy_dir(od, cfg.policy_transfer)),
+            "checkpoints": str(cfg.checkpoint_output_dir or od), "logs": str(od / "logs"),
+            "evals": str(od / "evals")}
+
+
 def build_preflight_report(cfg: RLConfig) -> dict[str, Any]:
-    from .orchestrator.schedule import max_policy_lag, target_steps
+    from .orchestrator.schedule import max_policy_lag, retained_policy_snapshots, target_steps
 
     checks = [*_path_checks(cfg), *_placement_checks(cfg), *_port_checks(cfg), *_schedule_checks(cfg),
-              *_algorithm_checks(cfg), *_model_checks(cfg)]
+              *_algorithm_checks(cfg), *_model_checks(cfg), *_environment_checks(cfg)]
+    commands: list[dict[str, Any]] = []
+    try:
+        commands = _resolved_commands(cfg)
+    except (ValueError, OSError) as e:
+        checks.append(Check("resolved_commands", "error", str(e)))
+    o = cfg.orchestrator
     return {
         "ok": not any(c.status == "error" for c in checks),
         "summary": {"model": cfg.model.name, "output_dir": str(cfg.output_dir), "launcher_mode": cfg.launcher.mode,
+                    "inference_mode": cfg.inference.mode, "inference_backend": cfg.inference.vllm.server_backend,
                     "policy_transfer": cfg.policy_transfer.type, "target_steps": target_steps(cfg),
-                    "max_policy_lag": max_policy_lag(cfg), "lora": cfg.lora is not None},
+                    "max_policy_lag": max_policy_lag(cfg), "lora": cfg.lora is not None,
+                    "policy_freshness": {"max_async_level": o.max_async_level,
+                                         "max_off_policy_steps": o.max_off_policy_steps,
+                                         "effective_max_policy_lag": max_policy_lag(cfg),
+                                         "retained_policy_snapshots": retained_policy_snapshots(cfg)},
+                    "algo": cfg.algo.model_dump(mode="json", exclude_none=True),
+                    "training_envs": [e.model_dump(mode="json", exclude_none=True) for e in o.envs],
+                    "curriculum": None if o.curriculum is None else o.curriculum.model_dump(mode="json",
+                                                                                           exclude_none=True),
+                    "low_precision": {"load_in_4bit": bool(cfg.model.load_in_4bit),
+                                      "optimizer": cfg.optim.type if hasattr(cfg, "optim") else None}},
+        "paths": _paths(cfg),
+        "commands": commands,
         "checks": [asdict(c) for c in checks],
     }
 
