@@ -180,8 +180,8 @@ def test_group_size_and_group_scoring(tmp_path, fake_vf):
 
     verifier_envs._ENV_CACHE.clear()
     orch = _orchestrator(_cfg(tmp_path, [{"id": "group-env", "args": {"n": 2}, "group_size": 3}]))
-    orch.custom_rollout([p for p in orch.prompts.take(2)], 0)
-    assert orch.custom_rollout.last_stats["verifier/failures/IncompleteGroup"] == 2.0
+    recs, stats = orch.custom_rollout([p for p in orch.prompts.take(2)], 0)
+    assert stats["verifier/failures/IncompleteGroup"] == 2.0 and recs == []
 
 
 def test_rollout_selection_trims_and_drops_single_rollouts(tmp_path, fake_vf):

@@ -46,9 +46,8 @@ class CustomRollout:
         self.path = path
         self.fn = load_rollout_function(path)
         self.engine = engine
-        self.last_stats: dict[str, float] = {}
 
-    def __call__(self, prompts, step: int) -> list[RLExample]:
+    def __call__(self, prompts, step: int) -> tuple[list[RLExample], dict[str, float]]:
         records = [RLExample(prompt=list(p.prompt), completion=[], advantage=None, reward=None,
                              target_completion=p.target_completion,
                              metadata={**p.metadata, "group": f"{step}:{i}", "example_id": p.example_id,
@@ -66,5 +65,4 @@ class CustomRollout:
             md.setdefault("group", "prompt:" + json.dumps(r.prompt, sort_keys=True, default=str))
             md["reward_source"] = "custom"
             res.append(replace(r, metadata=md))
-        self.last_stats = {"rollout/custom_records": float(len(res))}
-        return res
+        return res, {"rollout/custom_records": float(len(res))}

@@ -279,11 +279,18 @@ class RLOrchestrator:
         return view
 
     def _rollout(self, prompts: list[PromptRecord], step: int) -> list[RLExample]:
+        """Records of ``prompts``: the native generator, or the rollout function
+        (verifiers-package environments, a user function); a function may
+        return ``(records, statistics)``."""
         if self.custom_rollout is None:
             return self.generate_records(prompts, step)
-        recs = self.custom_rollout(prompts, step)
-        self.last_stats.update(getattr(self.custom_rollout, "last_stats", None) or {})
-        return recs
+        kw = {"fallback": self.generate_records} if getattr(self.custom_rollout, "takes_fallback", False) else {}
+        out = self.custom_rollout(prompts, step, **kw)
+        if isinstance(out, tuple):
+            recs, stats = out
+            self.last_stats.update(stats or {})
+            return recs
+        return out
 
     def _materialize_tokens(self, step: int) -> list[RLExample]:
         """A step sized by tokens (``orchestrator.token_batch_size``): prompt

@@ -437,7 +437,6 @@ class VerifierRollouts:
         self.clients = client_configs(self.vf, cfg)
         self.model = model_name(cfg, engine)
         self.fallback = fallback
-        self.failures = FailureStats()
         self.entries = {getattr(e, "resolved_name", e.id): e for e in cfg.orchestrator.envs}
         self._adm = None
         self._adaptive = None
@@ -517,17 +516,17 @@ class VerifierRollouts:
             mx = self.cfg.orchestrator.max_inflight_rollouts
             adm.set_limit(min(cap, mx) if mx else cap)
 
-    async def _run(self, prompts, step: int) -> list[RLExample]:
+    async def _run(self, prompts, step: int, failures: FailureStats) -> list[RLExample]:
         adm = self._admission()
         poller = asyncio.create_task(self._poll_load(adm)) if adm is not None and self._adaptive is not None else None
         try:
-            return await self._run_groups(prompts, step, adm)
+            return await self._run_groups(prompts, step, adm, failures)
         finally:
             if poller is not None:
                 poller.cancel()
                 await asyncio.gather(poller, return_exceptions=True)
 
-    async def _run_groups(self, prompts, step: int, adm) -> list[RLExample]:
+    async def _run_groups(self, prompts, step: int, adm, failures: FailureStats) -> list[RLExample]:
         jobs, keys = [], []
         for i, p in enumerate(prompts):
             name = p.metadata.get("env")
@@ -537,43 +536,50 @@ class VerifierRollouts:
                                   model=self.model, sampling=self._sampling(name, step),
                                   rollout_count=self._group_size(name),
                                   max_retries=int(self.cfg.orchestrator.verifier_max_retries),
-                                  failures=self.failures, admission=adm))
+                                  failures=failures, admission=adm))
             keys.append((i, name))
         results = await asyncio.gather(*jobs, return_exceptions=True)
         recs: list[RLExample] = []
         for (i, name), res in zip(keys, results):
             if isinstance(res, BaseException):
                 raise_if_rate_limited(res)
-                self.failures.record(res)
+                failures.record(res)
                 log.warning("verifier rollout group failed: %r", res)
                 continue
             if len(res) < self._group_size(name) and self.cfg.orchestrator.batch_selection != "rollouts":
                 # batches count whole groups: a group that lost rollouts is not trained on
                 # (orchestrator.batch_selection: rollouts keeps the survivors)
                 if res:
-                    self.failures.record("IncompleteGroup")
+                    failures.record("IncompleteGroup")
                 continue
             group = f"{step}:{i}"
             for out, adv in zip(res, self._advantages(name, res, group)):
                 recs += output_records(out, group=group, env_name=name, step=step, advantage=adv)
         return recs
 
-    def __call__(self, prompts, step: int) -> list[RLExample]:
+    takes_fallback = True  # RLOrchestrator passes its own native generation for mixed batches
+
+    def __call__(self, prompts, step: int, fallback=None) -> tuple[list[RLExample], dict[str, float]]:
+        """(records, statistics) of one step; every call keeps its own
+        failure counts, so steps generated concurrently do not mix them."""
+        failures = FailureStats()
         mine = [p for p in prompts if p.metadata.get("env") in self.envs]
         others = [p for p in prompts if p.metadata.get("env") not in self.envs]
-        recs = asyncio.run(self._run(mine, step)) if mine else []
+        recs = asyncio.run(self._run(mine, step, failures)) if mine else []
         if others:
-            if self.fallback is None:
+            fb = fallback or self.fallback
+            if fb is None:
                 raise ValueError("prompts of native environments reached the verifier rollout function")
-            recs += self.fallback(others, step)
-        self.last_stats = self.failures.consume()
+            recs += fb(others, step)
+        stats = failures.consume()
         rewards = [float(r.reward) for r in recs if (r.metadata or {}).get("rollout_count")]
-        self.last_stats["verifier/rollouts"] = float(len(rewards))
+        stats["verifier/rollouts"] = float(len(rewards))
         if self._adaptive is not None:
-            self.last_stats.update(self._adaptive.metrics())
+            stats.update(self._adaptive.metrics())
         if rewards:
-            self.last_stats["verifier/reward_mean"] = sum(rewards) / len(rewards)
-        return recs
+            stats["verifier/reward_mean"] = sum(rewards) / len(rewards)
+        self.last_stats = stats
+        return recs, stats
 
 
 # ----------------------------------------------------------------------------------------------------------------
