@@ -194,3 +194,38 @@ def test_chat_route_parses_and_fits_context(tmp_path):
     # a prompt that fills the context is refused with the context-length message
     r = c.post("/chat/completions/tokens", json={"messages": [], "tokens": list(range(3, 67))})
     assert r.status_code == 400 and "maximum context length is 64" in r.json()["detail"]
+
+
+def test_streamed_chat_and_completion_responses(tmp_path):
+    import json as _json
+
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.data.tokenizer import CharTokenizer
+    from wavelet_b200.inference.server import build_app
+
+    cfg = RLConfig.model_validate({
+        "model": {"name": "tiny", "random_init": True},
+        "data": {"source": "fake", "seq_len": 128, "fake_vocab_size": 64, "fake_prompt_len": 6},
+        "inference": {"vllm": {"server_backend": "offline", "reasoning_parser": "deepseek_r1",
+                               "tool_call_parser": "hermes"}},
+        "lora": None, "output_dir": str(tmp_path / "out")})
+    tok = CharTokenizer()
+    eng = _StubEngine(tok, '<think>r</think>hi<tool_call>{"name": "get_weather", "arguments": {}}</tool_call>')
+    c = TestClient(build_app(cfg, engine=eng))
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}], "tools": WEATHER,
+                                             "stream": True})
+    assert r.headers["content-type"].startswith("text/event-stream")
+    events = [line[6:] for line in r.text.splitlines() if line.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    chunks = [_json.loads(e) for e in events[:-1]]
+    deltas = [ch["choices"][0]["delta"] for ch in chunks if ch["choices"]]
+    assert deltas[0] == {"role": "assistant"} and {"reasoning_content": "r"} in deltas
+    assert {"content": "hi"} in [{k: v for k, v in d.items() if k == "content"} for d in deltas if "content" in d]
+    assert any("tool_calls" in d and d["tool_calls"][0]["function"]["name"] == "get_weather" for d in deltas)
+    assert [ch["choices"][0]["finish_reason"] for ch in chunks if ch["choices"]][-1] == "tool_calls"
+    assert chunks[-1]["usage"]["completion_tokens"] > 0 and all(ch["object"] == "chat.completion.chunk" for ch in chunks)
+    r = c.post("/v1/completions", json={"prompt_token_ids": [1, 2], "stream": True})
+    events = [line[6:] for line in r.text.splitlines() if line.startswith("data: ")]
+    assert events[-1] == "[DONE]" and _json.loads(events[0])["choices"][0]["token_ids"]

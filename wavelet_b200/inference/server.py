@@ -22,9 +22,11 @@ policy is being loaded.
 
 from __future__ import annotations
 
+import json
 import sys
 import threading
 import time
+import uuid
 from contextlib import contextmanager
 from pathlib import Path
 from typing import Any
@@ -212,10 +214,13 @@ def build_app(config: RLConfig, engine=None):
             p = payload["prompt"]
             prompts = [tok.encode(x) for x in ([p] if isinstance(p, str) else p)]
         comps = _complete(prompts, payload)
-        return {"object": "text_completion", "model": config.model.name, "policy_step": engine.policy_step,
+        body = {"object": "text_completion", "model": config.model.name, "policy_step": engine.policy_step,
                 "choices": [{"index": i, "prompt_index": c.prompt_index, "token_ids": c.token_ids,
                              "logprobs": {"token_logprobs": c.logprobs}, "text": tok.decode(c.token_ids),
                              "finish_reason": c.finish_reason} for i, c in enumerate(comps)]}
+        if payload.get("stream"):  # one chunk per choice, then the end marker
+            return _sse({**body, "choices": [ch]} for ch in body["choices"])
+        return body
 
     vcfg = config.inference.vllm
     out_parser = ChatOutputParser.for_model(config.model.name, vcfg.reasoning_parser, vcfg.tool_call_parser)
@@ -263,9 +268,44 @@ def build_app(config: RLConfig, engine=None):
                                                      for t, lp in zip(c.token_ids, c.logprobs)]},
                             "finish_reason": finish})
         n_out = sum(len(c.token_ids) for c in comps)
-        return {"object": "chat.completion", "model": config.model.name, "prompt_token_ids": ids,
+        body = {"object": "chat.completion", "model": config.model.name, "prompt_token_ids": ids,
                 "choices": choices,
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}}
+        if payload.get("stream"):
+            return _sse(_chat_chunks(body))
+        return body
+
+    def _chat_chunks(body: dict[str, Any]):
+        """``chat.completion.chunk`` events of a finished completion: the role,
+        the reasoning, the content, the tool calls, then the finish reason
+        (the generator returns whole completions, so the stream follows it)."""
+        rid = "chatcmpl-" + uuid.uuid4().hex[:24]
+        base = {"id": rid, "object": "chat.completion.chunk", "created": int(time.time()), "model": body["model"]}
+        for ch in body["choices"]:
+            i, msg = ch["index"], ch["message"]
+            yield {**base, "choices": [{"index": i, "delta": {"role": "assistant"}, "finish_reason": None}]}
+            if msg.get("reasoning_content"):
+                yield {**base, "choices": [{"index": i, "delta": {"reasoning_content": msg["reasoning_content"]},
+                                            "finish_reason": None}]}
+            if msg.get("content"):
+                yield {**base, "choices": [{"index": i, "delta": {"content": msg["content"]}, "finish_reason": None,
+                                            "logprobs": ch["logprobs"]}]}
+            for k, tc in enumerate(msg.get("tool_calls") or []):
+                yield {**base, "choices": [{"index": i, "delta": {"tool_calls": [{"index": k, **tc}]},
+                                            "finish_reason": None}]}
+            yield {**base, "choices": [{"index": i, "delta": {}, "finish_reason": ch["finish_reason"],
+                                        "token_ids": ch["token_ids"]}]}
+        yield {**base, "choices": [], "usage": body["usage"], "prompt_token_ids": body["prompt_token_ids"]}
+
+    def _sse(events):
+        from fastapi.responses import StreamingResponse
+
+        def gen():
+            for e in events:
+                yield "data: " + json.dumps(e) + "\n\n"
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(gen(), media_type="text/event-stream")
 
     app.post("/v1/chat/completions")(_chat)
     app.post("/v1/chat/completions/tokens")(_chat)
