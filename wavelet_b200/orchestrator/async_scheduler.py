@@ -450,7 +450,9 @@ class AsyncRolloutScheduler:
             st, recs, stats = self.done.pop(next_pub)
             rows = [example_to_payload(r, self.cfg.data) for r in recs]
             cur = self.prompts.curriculum
-            self.orch.write_materialized(rows, st.step)  # orchestrator.materialize_path, when set
+            write = getattr(self.orch, "write_materialized", None)  # orchestrator.materialize_path, when set
+            if write is not None:
+                write(rows, st.step)
             self.sender.publish(rows, step=st.step, training_records=rows, optimizer_step=st.step // self.C,
                                 chunk_index=(st.step % self.C) if self.C > 1 else None,
                                 policy_step=st.policy, tokens=sum(len(r.input_ids or []) for r in recs),
