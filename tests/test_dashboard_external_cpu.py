@@ -7,7 +7,6 @@ from __future__ import annotations
 import json
 import sqlite3
 
-import pytest
 
 
 def _run(tmp_path, wandb=None):
