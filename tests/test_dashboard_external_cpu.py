@@ -8,7 +8,6 @@ import json
 import sqlite3
 
 
-
 def _run(tmp_path, wandb=None):
     run = tmp_path / "run"
     (run / "configs" / "latest" / "resolved").mkdir(parents=True)
