@@ -198,9 +198,12 @@ def build_app(config: RLConfig, engine=None):
         return {"logprobs": lps}
 
     def _complete(prompts: list[list[int]], payload: dict[str, Any]) -> list[Any]:
+        # OpenAI fields and the vLLM-style extras clients send in extra_body (top_k, min_p, min_tokens,
+        # stop_token_ids), merged into the request body by the OpenAI client
         ov = {"temperature": payload.get("temperature"), "top_p": payload.get("top_p"),
               "top_k": payload.get("top_k"), "min_p": payload.get("min_p"),
               "max_tokens": payload.get("max_completion_tokens") or payload.get("max_tokens"),
+              "min_tokens": payload.get("min_tokens"), "stop_token_ids": payload.get("stop_token_ids"),
               "n": payload.get("n"), "seed": payload.get("seed")}
         with gate.generation(), lock:
             return engine.generate_ids(prompts, ov)
