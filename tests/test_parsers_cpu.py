@@ -229,3 +229,40 @@ def test_streamed_chat_and_completion_responses(tmp_path):
     r = c.post("/v1/completions", json={"prompt_token_ids": [1, 2], "stream": True})
     events = [line[6:] for line in r.text.splitlines() if line.startswith("data: ")]
     assert events[-1] == "[DONE]" and _json.loads(events[0])["choices"][0]["token_ids"]
+
+
+def test_stop_strings_cut_the_completion():
+    from wavelet_b200.data.tokenizer import CharTokenizer
+    from wavelet_b200.inference.server import apply_stop_strings
+
+    tok = CharTokenizer()
+    ids = tok.encode("answer: 42\nEND and more")
+    lps = [-0.1 * i for i in range(len(ids))]
+    out_ids, out_lps, text, hit = apply_stop_strings(tok, ids, lps, ["\nEND", "zzz"])
+    assert hit and text == "answer: 42" and tok.decode(out_ids) == "answer: 42\nEND"
+    assert out_lps == lps[: len(out_ids)]
+    assert apply_stop_strings(tok, ids, lps, "nothing")[3] is False
+    # the earliest of several stop strings wins
+    assert apply_stop_strings(tok, ids, lps, ["more", ":"])[2] == "answer"
+
+
+def test_chat_route_applies_stop_strings(tmp_path):
+    from fastapi.testclient import TestClient
+
+    from wavelet_b200.configs.config import RLConfig
+    from wavelet_b200.data.tokenizer import CharTokenizer
+    from wavelet_b200.inference.server import build_app
+
+    cfg = RLConfig.model_validate({"model": {"name": "tiny", "random_init": True},
+                                   "data": {"source": "fake", "seq_len": 128, "fake_vocab_size": 64,
+                                            "fake_prompt_len": 6},
+                                   "inference": {"vllm": {"server_backend": "offline", "reasoning_parser": None,
+                                                          "tool_call_parser": None}},
+                                   "lora": None, "output_dir": str(tmp_path / "out")})
+    tok = CharTokenizer()
+    c = TestClient(build_app(cfg, engine=_StubEngine(tok, "yes. STOP ignored tail")))
+    ch = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "q"}],
+                                              "stop": [" STOP"]}).json()
+    assert ch["choices"][0]["message"]["content"] == "yes." and ch["choices"][0]["finish_reason"] == "stop"
+    assert tok.decode(ch["choices"][0]["token_ids"]) == "yes. STOP"
+    assert ch["usage"]["completion_tokens"] == len(ch["choices"][0]["token_ids"])

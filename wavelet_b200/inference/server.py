@@ -29,6 +29,7 @@ import time
 import uuid
 from contextlib import contextmanager
 from pathlib import Path
+from types import SimpleNamespace
 from typing import Any
 
 from ..configs.config import RLConfig
@@ -37,6 +38,28 @@ from ..utils.config import load_config
 from .parsers import ChatOutputParser
 
 CONTEXT_FIT_SAFETY_TOKENS = 16  # tokens kept free when a request's max_tokens is fitted to the context
+
+
+def apply_stop_strings(tok, ids: list[int], logprobs: list[float], stops) -> tuple[list[int], list[float], str, bool]:
+    """A completion cut at the first OpenAI ``stop`` string: the tokens up to
+    the one that completes it (their log-probs kept), the text before it, and
+    whether a stop string was found.  The generator samples whole completions,
+    so the cut is made afterwards; tokens sampled before the stop point do not
+    depend on the ones after it."""
+    text = tok.decode(ids)
+    stops = [stops] if isinstance(stops, str) else [x for x in (stops or []) if x]
+    hits = [(text.find(x), x) for x in stops if x in text]
+    if not hits:
+        return ids, logprobs, text, False
+    pos, stop = min(hits)
+    lo, hi = 1, len(ids)  # smallest prefix whose text contains the stop string
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if stop in tok.decode(ids[:mid]):
+            hi = mid
+        else:
+            lo = mid + 1
+    return ids[:lo], logprobs[:lo], text[:pos], True
 
 
 class GenerationGate:
@@ -217,6 +240,13 @@ def build_app(config: RLConfig, engine=None):
             p = payload["prompt"]
             prompts = [tok.encode(x) for x in ([p] if isinstance(p, str) else p)]
         comps = _complete(prompts, payload)
+        if payload.get("stop"):
+            cut = []
+            for c in comps:
+                ids_c, lps_c, _, hit = apply_stop_strings(tok, c.token_ids, c.logprobs, payload["stop"])
+                cut.append(SimpleNamespace(token_ids=ids_c, logprobs=lps_c, prompt_index=c.prompt_index,
+                                           finish_reason="stop" if hit else c.finish_reason))
+            comps = cut
         body = {"object": "text_completion", "model": config.model.name, "policy_step": engine.policy_step,
                 "choices": [{"index": i, "prompt_index": c.prompt_index, "token_ids": c.token_ids,
                              "logprobs": {"token_logprobs": c.logprobs}, "text": tok.decode(c.token_ids),
@@ -261,7 +291,13 @@ def build_app(config: RLConfig, engine=None):
         comps = _complete([ids], req)
         choices = []
         for i, c in enumerate(comps):
-            parsed = out_parser.parse(tok.decode(c.token_ids), tools=tools,
+            if payload.get("stop"):
+                ids_c, lps_c, text, hit = apply_stop_strings(tok, c.token_ids, c.logprobs, payload["stop"])
+                c = SimpleNamespace(token_ids=ids_c, logprobs=lps_c, finish_reason="stop" if hit else c.finish_reason,
+                                    prompt_index=getattr(c, "prompt_index", 0))
+            else:
+                text = tok.decode(c.token_ids)
+            parsed = out_parser.parse(text, tools=tools,
                                       tool_choice=payload.get("tool_choice", "auto"),
                                       include_reasoning=bool(payload.get("include_reasoning", True)),
                                       chat_template_kwargs=kwargs)
@@ -270,7 +306,7 @@ def build_app(config: RLConfig, engine=None):
                             "logprobs": {"content": [{"token": f"token_id:{t}", "token_id": t, "logprob": lp}
                                                      for t, lp in zip(c.token_ids, c.logprobs)]},
                             "finish_reason": finish})
-        n_out = sum(len(c.token_ids) for c in comps)
+        n_out = sum(len(ch["token_ids"]) for ch in choices)
         body = {"object": "chat.completion", "model": config.model.name, "prompt_token_ids": ids,
                 "choices": choices,
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out, "total_tokens": len(ids) + n_out}}
