@@ -366,6 +366,43 @@ def build_app(config: RLConfig, engine=None):
     return app
 
 
+class InProcessServer:
+    """The OpenAI routes of ``build_app`` served from a thread of this
+    process (integrated RL with verifiers-package environments: the
+    environments call the generator that shares the trainer's process)."""
+
+    def __init__(self, config: RLConfig, engine, host: str = "127.0.0.1", port: int = 0):
+        import socket
+
+        import uvicorn
+
+        if port == 0:
+            with socket.socket() as sk:
+                sk.bind((host, 0))
+                port = sk.getsockname()[1]
+        self.host, self.port = host, port
+        self.app = build_app(config, engine=engine)
+        self._server = uvicorn.Server(uvicorn.Config(self.app, host=host, port=port, log_level="warning"))
+        self._thread = threading.Thread(target=self._server.run, name="wavelet-openai", daemon=True)
+
+    @property
+    def base_url(self) -> str:
+        return f"http://{self.host}:{self.port}/v1"
+
+    def start(self, timeout: float = 30.0) -> "InProcessServer":
+        self._thread.start()
+        t0 = time.time()
+        while not self._server.started:
+            if not self._thread.is_alive() or time.time() - t0 > timeout:
+                raise RuntimeError(f"the in-process OpenAI server did not start on {self.host}:{self.port}")
+            time.sleep(0.01)
+        return self
+
+    def close(self) -> None:
+        self._server.should_exit = True
+        self._thread.join(timeout=10)
+
+
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     cfg = load_config(RLConfig, argv)

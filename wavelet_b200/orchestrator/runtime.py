@@ -164,11 +164,35 @@ class IntegratedRunner:
         if self.world.rank == 0 and t.step > 0:
             prune_from(self.sender.queue_dir, t.step)
         prompts = build_prompt_source(c, t.model.cfg.vocab_size, rank=t.dp_rank)
+        self.openai = None
         if any(getattr(e, "metadata", {}).get("kind") == "verifiers" for e, _ in getattr(prompts, "envs", [])):
-            raise ValueError("verifiers-package environments call the inference servers over HTTP; "
-                             "run them with launcher.mode: process")
+            # verifiers-package environments call an OpenAI server: serve this process's generator
+            # from a thread (the environments' requests run while the trainer waits for the step)
+            c = self._serve_generator(c, gen_model)
         self.orch = RLOrchestrator(c, self.engine, None, prompts, monitor=t.monitor)
         return self
+
+    def _serve_generator(self, c: RLConfig, gen_model) -> RLConfig:
+        from ..data.tokenizer import tokenizer_for
+        from ..inference.policy import NativePolicyInferenceEngine
+        from ..inference.server import InProcessServer
+
+        if self.world.world_size > 1:
+            raise NotImplementedError("verifiers-package environments in integrated mode run on one process; "
+                                      "use launcher.mode: process for more GPUs")
+        eng = NativePolicyInferenceEngine(c, model=gen_model, tokenizer=tokenizer_for(c.model))
+        eng.generator = self.engine
+        eng.policy_step = 0
+        self.openai_engine = eng
+        self.openai = InProcessServer(c, eng, host="127.0.0.1", port=0).start()
+        self.cfg = c.model_copy(update={"orchestrator": c.orchestrator.model_copy(
+            update={"verifier_base_url": self.openai.base_url})})
+        return self.cfg
+
+    def close(self) -> None:
+        if getattr(self, "openai", None) is not None:
+            self.openai.close()
+            self.openai = None
 
     def _gather(self, rows: list[dict]) -> list[dict]:
         if not dist.is_initialized() or self.world.world_size == 1:
@@ -191,6 +215,8 @@ class IntegratedRunner:
         if ev:
             ev[0].record()
         t0 = time.perf_counter()
+        if getattr(self, "openai_engine", None) is not None:
+            self.openai_engine.policy_step = step  # reported by the in-process OpenAI server
         if self.policy_sync is not None and step > 0:
             self.policy_sync.refresh()  # the generator replica picks up the last update
         recs = self.orch.materialize(step)
@@ -251,6 +277,7 @@ class IntegratedRunner:
             if t.ckpt is not None:
                 t.ckpt.wait()
             t.monitor.finish(status=status, step=t.step)
+            self.close()
 
 
 def main(argv: list[str] | None = None) -> int:

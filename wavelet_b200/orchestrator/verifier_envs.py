@@ -31,6 +31,10 @@ is the bridge between those environments and the orchestrator:
   ``evals/<env>/step-<n>.jsonl`` and the metrics appended to
   ``eval_metrics.jsonl``.
 
+In process mode the environments call the inference servers; in integrated
+mode the runner serves its own generator on an in-process OpenAI server
+(``inference.server.InProcessServer``) and points the clients at it.
+
 The package is optional: nothing here imports it until an environment that
 is not a native one is requested, and then a missing package is an error
 that names it.
