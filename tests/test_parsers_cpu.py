@@ -266,3 +266,54 @@ def test_chat_route_applies_stop_strings(tmp_path):
     assert ch["choices"][0]["message"]["content"] == "yes." and ch["choices"][0]["finish_reason"] == "stop"
     assert tok.decode(ch["choices"][0]["token_ids"]) == "yes. STOP"
     assert ch["usage"]["completion_tokens"] == len(ch["choices"][0]["token_ids"])
+
+
+def test_concurrent_requests_share_generator_batches():
+    import threading as _th
+    import time as _time
+
+    from wavelet_b200.inference.engine import Completion
+    from wavelet_b200.inference.server import RequestBatcher
+
+    calls = []
+
+    def run(prompts, settings):
+        calls.append((len(prompts), settings["temperature"]))
+        _time.sleep(0.05)
+        return [Completion(i, k, p, [p[0], k], [-0.1, -0.2], "stop") for i, p in enumerate(prompts)
+                for k in range(settings.get("n") or 1)]
+
+    # min_size 6: the worker waits (up to max_wait_seconds) until the six requests are queued
+    b = RequestBatcher(run, wait_seconds=0.0, max_wait_seconds=5.0, min_size=6, max_size=None)
+    out = {}
+
+    def client(i, temp):
+        out[i] = b.submit([[100 + i], [200 + i]], {"temperature": temp, "n": 2})
+
+    ths = [_th.Thread(target=client, args=(i, 1.0 if i < 4 else 0.5)) for i in range(6)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    # two generator calls: one per sampling setting, each holding every request with it
+    assert sorted(calls) == [(4, 0.5), (8, 1.0)]
+    for i in range(6):
+        assert [(c.prompt_index, c.sample_index, c.token_ids[0]) for c in out[i]] == \
+            [(0, 0, 100 + i), (0, 1, 100 + i), (1, 0, 200 + i), (1, 1, 200 + i)]
+    # max_size bounds the requests per batch; an error reaches every waiter of its batch
+    calls.clear()
+    b2 = RequestBatcher(run, wait_seconds=0.05, max_size=2)
+    ths = [_th.Thread(target=client, args=(i, 1.0)) for i in range(4)]
+    b = b2
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    assert all(n <= 4 for n, _ in calls)
+
+    def boom(prompts, settings):
+        raise RuntimeError("generator failed")
+
+    b3 = RequestBatcher(boom, wait_seconds=0.0)
+    with pytest.raises(RuntimeError, match="generator failed"):
+        b3.submit([[1]], {"temperature": 1.0})

@@ -44,10 +44,6 @@ INERT: dict[str, str] = {
     "inference.vllm.enable_fp32_lm_head": "the generator samples from bf16 logits of an fp32-accumulated GEMM",
     "inference.vllm.enable_fp32_router_logits": "router logits follow model.moe_router_dtype",
     "inference.vllm.use_generation_logprobs": "generation log-probs always come from the sampling kernel",
-    "inference.vllm.openai_batch_wait_seconds": "the server batches the requests it has",
-    "inference.vllm.openai_batch_min_size": "the server batches the requests it has",
-    "inference.vllm.openai_batch_max_wait_seconds": "the server batches the requests it has",
-    "inference.vllm.openai_batch_max_size": "the server batches the requests it has",
     "inference.vllm.extra_args": "there is no vLLM engine to pass them to",
     "inference.sampling.extra_body": "the native sampler has no extra request fields (verifiers-package "
                                      "rollouts pass them to the server)",

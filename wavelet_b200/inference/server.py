@@ -16,8 +16,9 @@ and native_server.py:92-215):
                                  fitted to the context
     POST /tokenize, /v1/tokenize
 
-Generation requests are serialised by a gate that ``/pause`` closes while a
-policy is being loaded.
+Concurrent generation requests are collected into shared generator batches
+(``RequestBatcher``, ``inference.vllm.openai_batch_*``); a gate that
+``/pause`` closes holds new requests while a policy is being loaded.
 """
 
 from __future__ import annotations
@@ -60,6 +61,82 @@ def apply_stop_strings(tok, ids: list[int], logprobs: list[float], stops) -> tup
         else:
             lo = mid + 1
     return ids[:lo], logprobs[:lo], text[:pos], True
+
+
+class RequestBatcher:
+    """Concurrent generation requests run as one generator batch
+    (``inference.vllm.openai_batch_*``; ref inference/engine.py:958-1000).
+
+    The worker takes the first waiting request, waits ``wait_seconds`` for
+    others, keeps waiting up to ``max_wait_seconds`` while fewer than
+    ``min_size`` are queued, takes at most ``max_size`` requests, and runs the
+    requests with equal sampling settings as one ``run(prompts, settings)``
+    call; every request gets its own completions back (``prompt_index``
+    relative to its own prompts).  An error fails every request of the
+    batch."""
+
+    def __init__(self, run, *, wait_seconds: float = 0.01, min_size: int = 1, max_wait_seconds: float = 0.01,
+                 max_size: int | None = None):
+        self.run = run
+        self.wait, self.min_size = wait_seconds, min_size
+        self.max_wait = max(wait_seconds, max_wait_seconds)
+        self.max_size = max_size
+        self._queue: list[dict[str, Any]] = []
+        self._cv = threading.Condition()
+        self._thread = threading.Thread(target=self._loop, name="wavelet-batcher", daemon=True)
+        self._thread.start()
+        self.batches = 0  # generator calls made (for tests and metrics)
+
+    def submit(self, prompts: list[list[int]], settings: dict[str, Any]) -> list[Any]:
+        req = {"prompts": prompts, "settings": settings, "done": threading.Event(), "result": None, "error": None}
+        with self._cv:
+            self._queue.append(req)
+            self._cv.notify_all()
+        req["done"].wait()
+        if req["error"] is not None:
+            raise req["error"]
+        return req["result"]
+
+    def _take(self) -> list[dict[str, Any]]:
+        t0 = time.perf_counter()
+        if self.wait > 0:
+            self._cv.wait(timeout=self.wait)
+        while len(self._queue) < self.min_size:
+            left = t0 + self.max_wait - time.perf_counter()
+            if left <= 0:
+                break
+            self._cv.wait(timeout=left)
+        n = len(self._queue) if self.max_size is None else min(self.max_size, len(self._queue))
+        batch, self._queue = self._queue[:n], self._queue[n:]
+        return batch
+
+    def _loop(self) -> None:
+        from dataclasses import replace
+
+        while True:
+            with self._cv:
+                while not self._queue:
+                    self._cv.wait()
+                batch = self._take()
+            groups: dict[str, list[dict[str, Any]]] = {}
+            for r in batch:
+                groups.setdefault(json.dumps(r["settings"], sort_keys=True, default=str), []).append(r)
+            for reqs in groups.values():
+                try:
+                    prompts, offsets = [], []
+                    for r in reqs:
+                        offsets.append(len(prompts))
+                        prompts += r["prompts"]
+                    comps = self.run(prompts, reqs[0]["settings"])
+                    self.batches += 1
+                    for r, o in zip(reqs, offsets):
+                        mine = [c for c in comps if o <= c.prompt_index < o + len(r["prompts"])]
+                        r["result"] = [replace(c, prompt_index=c.prompt_index - o) for c in mine]
+                except BaseException as exc:  # noqa: BLE001 - every waiter learns of it
+                    for r in reqs:
+                        r["error"] = exc
+                for r in reqs:
+                    r["done"].set()
 
 
 class GenerationGate:
@@ -116,6 +193,15 @@ def build_app(config: RLConfig, engine=None):
 
             engine.attach_device_receiver(int(os.environ.get("WAVELET_INFERENCE_REPLICA", "0")))
     gate = GenerationGate()
+    vb = config.inference.vllm
+
+    def _run_batch(prompts, ov):
+        with lock:
+            return engine.generate_ids(prompts, ov)
+
+    # concurrent completion requests share generator batches
+    batcher = RequestBatcher(_run_batch, wait_seconds=vb.openai_batch_wait_seconds, min_size=vb.openai_batch_min_size,
+                             max_wait_seconds=vb.openai_batch_max_wait_seconds, max_size=vb.openai_batch_max_size)
     app = FastAPI(title="wavelet inference server")
     app.state.engine = engine
     state: dict[str, Any] = {"started_at": time.time(), "requests": 0, "generated_tokens": 0, "sleeping": False}
@@ -228,8 +314,8 @@ def build_app(config: RLConfig, engine=None):
               "max_tokens": payload.get("max_completion_tokens") or payload.get("max_tokens"),
               "min_tokens": payload.get("min_tokens"), "stop_token_ids": payload.get("stop_token_ids"),
               "n": payload.get("n"), "seed": payload.get("seed")}
-        with gate.generation(), lock:
-            return engine.generate_ids(prompts, ov)
+        with gate.generation():
+            return batcher.submit(prompts, ov)
 
     @app.post("/v1/completions")
     def completions(payload: dict[str, Any]):
@@ -363,6 +449,7 @@ def build_app(config: RLConfig, engine=None):
     app.post("/v1/tokenize")(_tokenize)
     app.state.engine = engine
     app.state.gate = gate
+    app.state.batcher = batcher
     return app
 
 
