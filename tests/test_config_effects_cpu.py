@@ -24,7 +24,9 @@ def test_inert_keys_are_named_with_reasons():
     # set to its default value: not a change, not named
     assert inert_settings(RLConfig.model_validate({"model": {"compile": False}})) == []
     sft = SFTConfig.model_validate({"data": {"num_workers": 4}, "loss_impl": "liger"})
-    assert {m.split("=")[0] for m in inert_settings(sft)} == {"data.num_workers", "loss_impl"}
+    assert {m.split("=")[0] for m in inert_settings(sft)} == {"loss_impl"}  # num_workers prefetches in SFT
+    rl = RLConfig.model_validate({"data": {"num_workers": 1}})
+    assert {m.split("=")[0] for m in inert_settings(rl)} == {"data.num_workers"}
 
 
 def test_unsupported_values_are_refused():
@@ -191,3 +193,25 @@ def test_per_environment_sampling_group_size_and_algorithm(tmp_path):
     from wavelet_b200.orchestrator.runtime import env_args
 
     assert env_args(SimpleNamespace(args={"k": 1}, data_path=rows)) == {"k": 1, "path": str(rows)}
+
+
+def test_sft_prefetching_dataset_keeps_the_consumed_state():
+    from wavelet_b200.data.sft import PrefetchingDataset, SFTDataset
+
+    cfg = SFTConfig.model_validate({"data": {"source": "fake", "seq_len": 64, "fake_vocab_size": 50,
+                                             "num_workers": 2}}).data
+    plain = SFTDataset(cfg, None, seed=3)
+    want = [plain.next_micro_batch().input_ids.tolist() for _ in range(4)]
+    ds = SFTDataset(cfg, None, seed=3)
+    pre = PrefetchingDataset(ds, 4)
+    got = [pre.next_micro_batch().input_ids.tolist() for _ in range(2)]
+    assert got == want[:2]
+    import time
+
+    time.sleep(0.2)  # the producer runs ahead ...
+    st = pre.state_dict()  # ... but the state is the one after the second batch the trainer took
+    fresh = SFTDataset(cfg, None, seed=3)
+    fresh.load_state_dict(st)
+    assert fresh.next_micro_batch().input_ids.tolist() == want[2]
+    assert len(pre.samples()) == len(plain.samples())  # the wrapped dataset's other methods
+    pre.close()

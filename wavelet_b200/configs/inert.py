@@ -30,8 +30,8 @@ INERT: dict[str, str] = {
     "model.compile": "layers run fixed sm_100a kernel sequences; torch.compile is not used",
     "model.compile_fullgraph": "layers run fixed sm_100a kernel sequences; torch.compile is not used",
     "lora.optimization_dtype": "LoRA adapters always keep fp32 master weights and moments",
-    "data.num_workers": "batches are built in the trainer process",
     "optim.implementation": "AdamW is the fused flat kernel",
+    "data.num_workers": "rollout rows are pretokenized and read in the trainer process",
     "loss_impl": "the loss is the chunked LM-head kernel",
     "slurm.shared_fs": "role configs and logs are written under the run directory in every case",
     "policy_transfer.nccl_dtype": "device updates carry the generator's compute dtype",
@@ -56,6 +56,10 @@ INERT: dict[str, str] = {
 }
 
 
+# keys that take effect in SFT and are inert only in RL configs
+RL_ONLY = frozenset({"data.num_workers"})
+
+
 def _lookup(cfg: Any, path: str) -> tuple[Any, str] | None:
     obj = cfg
     parts = path.split(".")
@@ -71,7 +75,10 @@ def _lookup(cfg: Any, path: str) -> tuple[Any, str] | None:
 def inert_settings(cfg: Any) -> list[str]:
     """One message per inert key that ``cfg`` sets to a non-default value."""
     out = []
+    rl = hasattr(cfg, "orchestrator")
     for path, why in INERT.items():
+        if path in RL_ONLY and not rl:
+            continue  # acts in SFT (data.num_workers: batches prefetched on a thread)
         hit = _lookup(cfg, path)
         if hit is None:
             continue

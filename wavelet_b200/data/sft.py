@@ -426,3 +426,56 @@ def pack(seqs: list[torch.Tensor], masks: list[torch.Tensor], mms: list | None =
 
         mm = pack_multimodal_row(list(mms))
     return PackedBatch(ids, pos, cu, max(lens), tgt, mask, mm=mm)
+
+
+class PrefetchingDataset:
+    """``data.num_workers`` > 0: a background thread builds micro-batches
+    ``depth`` ahead of the trainer (tokenised samples are packed and pinned
+    while the GPU works).  ``state_dict`` is the state right after the last
+    batch the trainer took, so a checkpoint never skips prefetched batches.
+    Wrap a dataset after its state was restored."""
+
+    def __init__(self, dataset, depth: int):
+        import queue
+        import threading
+
+        self.dataset = dataset
+        self._state = dataset.state_dict()
+        self._q: "queue.Queue" = queue.Queue(maxsize=max(1, depth))
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._produce, name="wavelet-sft-prefetch", daemon=True)
+        self._thread.start()
+
+    def _produce(self) -> None:
+        import queue
+
+        while not self._stop.is_set():
+            try:
+                item = (self.dataset.next_micro_batch(), self.dataset.state_dict(), None)
+            except BaseException as exc:  # noqa: BLE001 - raised in the trainer on its next take
+                item = (None, None, exc)
+            while not self._stop.is_set():
+                try:
+                    self._q.put(item, timeout=0.1)
+                    break
+                except queue.Full:
+                    continue
+            if item[2] is not None:
+                return
+
+    def next_micro_batch(self) -> PackedBatch:
+        batch, state, exc = self._q.get()
+        if exc is not None:
+            raise exc
+        self._state = state
+        return batch
+
+    def state_dict(self) -> dict[str, Any]:
+        return self._state
+
+    def close(self) -> None:
+        self._stop.set()
+        self._thread.join(timeout=5)
+
+    def __getattr__(self, name: str):  # samples(), eval_batches(), ... of the wrapped dataset
+        return getattr(self.dataset, name)

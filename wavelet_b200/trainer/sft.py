@@ -188,6 +188,10 @@ class SFTTrainer:
                 self.sched_offset = self.step
             if st["data_state"] is not None and not c.ckpt.skip_dataloader:
                 self.dataset.load_state_dict(st["data_state"])
+        if getattr(c.data, "num_workers", 0) and c.data.num_workers > 0:  # batches built ahead on a thread
+            from ..data.sft import PrefetchingDataset
+
+            self.dataset = PrefetchingDataset(self.dataset, 2 * c.data.num_workers)
         self.monitor.start_run(run_config=config_to_plain(c), world=w, resumed_from=str(resume) if resume else None)
         lora_params = self.model.lora.num_trainable() if self.model.lora is not None else None
         self.perf = PerfTracker(arch, w.device, lora_rank=c.lora.rank if c.lora else None, lora_params=lora_params)
