@@ -80,7 +80,7 @@ def test_orchestrator_samples_from_and_reports_to_the_curriculum(tmp_path):
     rows = tmp_path / "prompts.jsonl"
     rows.write_text("".join(json.dumps({"prompt_ids": [1, 2, i + 3], "answer": str(i)}) + "\n" for i in range(4)))
     cfg = RLConfig.model_validate({
-        "data": {"path": str(rows)},
+        "data": {"path": str(rows)}, "output_dir": str(tmp_path / "out"),
         "orchestrator": {"examples_per_step": 2, "rollouts_per_example": 2,
                          "curriculum": {"sampler": {"type": "difficulty_pool", "seed": 1},
                                         "gates": {"zero_signal": {"type": "advantage_range"}}}}})
